@@ -1,0 +1,413 @@
+#!/usr/bin/env python
+"""Benchmark of the exact flat scan + top-k (MetalANNS search hot path).
+
+Workload: n = 1,000,000 x d = 384 fp32 rows, i.i.d.
+N(0,1) then L2-normalised, cosine, top-10, synthetic (numpy default_rng(0):
+database first, then the queries from the same generator).  One step = one
+batch of --nq queries searched exactly.  With --gpus N > 1 (launched by
+torch.distributed.run) the rows are sharded contiguously over the ranks, each
+rank scans its shard, the per-shard top-k blocks are all-gathered over NCCL
+and merged on the device by (distance, id).
+
+`value` is device-timed with inputs resident in HBM; `e2e` goes through the
+public C ABI with pinned host buffers (query upload and result download inside
+the timed region).  `--impl reference` times the reference CPU exact path
+(ParallelFlatScan restated in oracle/, inner loop = the reference's own dots.c
+when it was built) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC_NAMES = {"cosine": 0, "l2": 1, "ip": 2}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--n", type=int, default=1_000_000)
+    ap.add_argument("--dim", type=int, default=384)
+    ap.add_argument("--nq", type=int, default=1)
+    ap.add_argument("--k", type=int, default=10)
+    ap.add_argument("--metric", default="cosine", choices=list(METRIC_NAMES))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    return ap.parse_args()
+
+
+def make_data(n, dim, nq, seed=0):
+    rng = np.random.default_rng(seed)
+    v = rng.standard_normal((n, dim), dtype=np.float32)
+    v /= np.linalg.norm(v, axis=1, keepdims=True)
+    q = rng.standard_normal((nq, dim), dtype=np.float32)
+    q /= np.linalg.norm(q, axis=1, keepdims=True)
+    return v, q
+
+
+def p50(xs):
+    s = sorted(xs)
+    return s[max(0, math.ceil(0.5 * len(s)) - 1)]  # nearest rank (LatencyDistribution.swift:154-160)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.dev = device_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def committed_traffic(workload):
+    """Per-launch DRAM bytes of the scan kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        d = json.load(f)
+    return d.get(workload)
+
+
+def cpu_reference_qps(v, q, k, metric, seconds, max_queries=None):
+    """ParallelFlatScan (the reference CPU exact path) on the host cores."""
+    import oracle as O
+    cores = os.cpu_count() or 1
+    used = min(cores, 32, max(1, v.shape[0] // 2048))  # ParallelFlatScan.sliceCount
+    norms = O.row_norms(v) if metric in (0, 1) else None
+    use_ref = O.ref_lib() is not None
+    O.parallel_flat_scan(v, q[0], k, metric, cores, norms=norms, use_reference_dots=use_ref)
+    t0 = time.perf_counter()
+    done = 0
+    while True:
+        O.parallel_flat_scan(v, q[done % len(q)], k, metric, cores, norms=norms,
+                             use_reference_dots=use_ref)
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or (max_queries and done >= max_queries):
+            break
+    return done / el, used, done, use_ref
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    metric = METRIC_NAMES[args.metric]
+    v, q = make_data(args.n, args.dim, max(args.nq, 1))
+    import oracle as O
+    cores = os.cpu_count() or 1
+    used = min(cores, 32, max(1, v.shape[0] // 2048))
+    norms = O.row_norms(v) if metric in (0, 1) else None
+    use_ref = O.ref_lib() is not None
+    for i in range(args.warmup):
+        O.parallel_flat_scan(v, q[i % len(q)], args.k, metric, cores, norms=norms,
+                             use_reference_dots=use_ref)
+    times = []
+    for i in range(args.steps):
+        t = time.perf_counter()
+        for j in range(args.nq):
+            O.parallel_flat_scan(v, q[j], args.k, metric, cores, norms=norms,
+                                 use_reference_dots=use_ref)
+        times.append(time.perf_counter() - t)
+    total = sum(times)
+    value = args.nq * args.steps / total
+    line = {
+        "impl": "reference", "metric": "queries_per_sec", "value": value, "unit": "queries/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / args.steps, "p50_us": 1e6 * p50(times),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": workload_config(args),
+        "cpu_baseline": {"value": value, "unit": "queries/s", "cores": used,
+                         "kind": "port",
+                         "sample": f"{args.nq} quer{'y' if args.nq == 1 else 'ies'} per step, "
+                                   f"full {args.n}x{args.dim} scan; ParallelFlatScan restated, "
+                                   f"inner loop {'reference dots.c' if use_ref else 'restated dots.c'}"},
+        "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args):
+    return {"workload": f"exact_flat_{args.n}x{args.dim}_{args.metric}_top{args.k}_nq{args.nq}",
+            "n": args.n, "dim": args.dim, "nq": args.nq, "k": args.k, "metric": args.metric,
+            "parallelism": f"rowshard{args.gpus}",
+            "l2": "inputs larger than L2 (corpus 1.5 GB streamed per step)"}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    import meltan_b200 as mb
+    from meltan_b200._lib import lib
+
+    metric = METRIC_NAMES[args.metric]
+    v, q = make_data(args.n, args.dim, args.nq)
+    rows = np.array_split(np.arange(args.n), world)[rank]
+    r0, r1 = int(rows[0]), int(rows[-1]) + 1
+    ctx = mb.Context(local)
+    buf = mb.VectorBuffer(ctx, v[r0:r1], id_offset=r0)
+    ws = mb.Workspace(ctx)
+    kout = min(args.k, mb.MAX_TOP_K)
+    nq = args.nq
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    dq = torch.from_numpy(q).cuda()
+    ld = torch.empty((nq, kout), dtype=torch.float32, device="cuda")
+    li = torch.empty((nq, kout), dtype=torch.int32, device="cuda")
+    lc = torch.empty((nq,), dtype=torch.int32, device="cuda")
+    if world > 1:
+        gd = torch.empty((world, nq, kout), dtype=torch.float32, device="cuda")
+        gi = torch.empty((world, nq, kout), dtype=torch.int32, device="cuda")
+        gc = torch.empty((world, nq), dtype=torch.int32, device="cuda")
+        od = torch.empty((nq, kout), dtype=torch.float32, device="cuda")
+        oi = torch.empty((nq, kout), dtype=torch.int32, device="cuda")
+        oc = torch.empty((nq,), dtype=torch.int32, device="cuda")
+
+    def step(src):
+        mb.FlatGPUSearch.search_device(ctx, buf, ws, src.data_ptr(), nq, args.k, metric,
+                                       ld.data_ptr(), li.data_ptr(), lc.data_ptr(), sp)
+        if world > 1:
+            dist.all_gather_into_tensor(gd, ld)
+            dist.all_gather_into_tensor(gi, li)
+            dist.all_gather_into_tensor(gc, lc)
+            mb.topk_merge_device(ctx, ws, gd.data_ptr(), gi.data_ptr(), gc.data_ptr(), world, nq,
+                                 kout, args.k, od.data_ptr(), oi.data_ptr(), oc.data_ptr(), sp)
+            return od, oi, oc
+        return ld, li, lc
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- device-resident timing (value) ----
+    for _ in range(max(3, args.warmup)):
+        step(dq)
+    ws.check(sp)
+    ws.stats()
+    ws.set_timing(True)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_stop = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        step(dq)
+        ev[i][1].record(stream)
+    t_stop.record(stream)
+    barrier()
+    clock_info = clocks.stop()
+    ws.check(sp)
+    kern_ms, kern_launches, total_launches = ws.stats()
+    ws.set_timing(False)
+    total_ms = t_start.elapsed_time(t_stop)
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+
+    # ---- end to end through the C ABI with pinned host buffers (e2e) ----
+    hq = torch.from_numpy(q).pin_memory()
+    h_out_d = torch.empty((nq, kout), dtype=torch.float32).pin_memory()
+    h_out_i = torch.empty((nq, kout), dtype=torch.int32).pin_memory()
+    h_out_c = torch.empty((nq,), dtype=torch.int32).pin_memory()
+    L = lib()
+    dq2 = torch.empty_like(dq)
+
+    def e2e_step():
+        if world == 1:
+            rc = L.mans_flat_search(ctx.handle, buf.handle, C.c_void_p(hq.data_ptr()), nq,
+                                    args.dim, args.k, metric, C.c_void_p(h_out_d.data_ptr()),
+                                    C.c_void_p(h_out_i.data_ptr()), C.c_void_p(h_out_c.data_ptr()))
+            mb.check(rc)
+        else:
+            dq2.copy_(hq, non_blocking=True)
+            d_, i_, c_ = step(dq2)
+            h_out_d.copy_(d_, non_blocking=True)
+            h_out_i.copy_(i_, non_blocking=True)
+            h_out_c.copy_(c_, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+
+    for _ in range(max(3, args.warmup)):
+        e2e_step()
+    barrier()
+    e2e_times = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        e2e_step()
+        e2e_times.append(time.perf_counter() - t)
+    e2e_total = time.perf_counter() - t0
+    barrier()
+
+    # verify the final result of the last e2e step against the device path once
+    ok = True
+    if rank == 0 and args.n * args.dim <= 1_000_000 * 384:
+        fd, fi, fc = step(dq)
+        torch.cuda.synchronize()
+        ok = bool(torch.equal(fi.cpu(), h_out_i) and torch.equal(fc.cpu(), h_out_c))
+
+    stats = torch.tensor([total_ms, e2e_total * 1e3, kern_ms / max(kern_launches, 1)],
+                         dtype=torch.float64, device="cuda")
+    steps_t = torch.tensor(step_ms, dtype=torch.float64, device="cuda")
+    e2e_t = torch.tensor(e2e_times, dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+        dist.all_reduce(steps_t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    total_ms, e2e_ms, kern_avg_ms = stats.tolist()
+
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        shard_rows = r1 - r0
+        groups = math.ceil(nq / 8) if nq > 8 else 1
+        row_bytes = args.dim * 4 + (4 if metric in (0, 1) else 0)
+        alg_bytes = shard_rows * row_bytes * groups + nq * args.dim * 4
+        achieved = alg_bytes / (kern_avg_ms * 1e-3) / 1e9
+        workload = workload_config(args)["workload"]
+        traffic = committed_traffic(workload)
+        line = {
+            "metric": "queries_per_sec",
+            "value": nq * args.steps / (total_ms * 1e-3),
+            "unit": "queries/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps,
+            "p50_us": 1e3 * p50(steps_t.tolist()),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic (numpy default_rng(0) Gaussian rows, L2-normalised)",
+            "config": workload_config(args),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak,
+                         "traffic": traffic,
+                         "kernel": "scan_topk_kernel",
+                         "kernel_avg_us": kern_avg_ms * 1e3,
+                         "algorithmic_bytes_per_launch": alg_bytes,
+                         "peak_source": f"{peak_kind} hbm_gbs"},
+            "e2e": {"value": nq * args.steps / (e2e_ms * 1e-3), "unit": "queries/s",
+                    "p50_us": 1e6 * p50(e2e_t.tolist()),
+                    "h2d_bytes_per_step": nq * args.dim * 4,
+                    "d2h_bytes_per_step": nq * kout * 8 + nq * 4},
+            "gpu_launches": int(total_launches),
+            "clocks": clock_info,
+            "e2e_matches_device_path": ok,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            qps, used, done, use_ref = cpu_reference_qps(v, q, args.k, metric, args.cpu_seconds)
+            line["cpu_baseline"] = {
+                "value": qps, "unit": "queries/s", "cores": used, "kind": "port",
+                "sample": f"{done} single-query scans of the full {args.n}x{args.dim} corpus "
+                          f"(~{args.cpu_seconds:.0f} s); ParallelFlatScan restated, inner loop "
+                          f"{'reference dots.c' if use_ref else 'restated dots.c'}"}
+        print(json.dumps(line), flush=True)
+
+    ws.close()
+    buf.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

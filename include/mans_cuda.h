@@ -1,0 +1,163 @@
+/*
+ * mans_cuda.h -- C ABI of the B200 search hot path for MetalANNS.
+ *
+ * This library replaces the Metal dispatch layer under MetalANNSCore's search
+ * path: the exact flat scan with top-k, the IVF-flat probe-and-scan and the
+ * IVF-PQ asymmetric-distance scoring.  Paths below are relative to the
+ * MetalANNS source tree.
+ *
+ * Conventions (the style of Sources/MetalANNSC/include/MetalANNSC.h:13-38):
+ *   - plain C, int64_t counts, caller-owned host inputs read only during the
+ *     call, caller-owned outputs;
+ *   - every function returns an int32_t status (MANS_OK == 0);
+ *   - search results are sorted ascending by (distance, id): equal distances
+ *     are ordered by ascending id (the GPU tier order pinned by
+ *     Tests/MetalANNSTests/BoundedSelectionTests.swift:257-277), except IVF-PQ,
+ *     which keeps the reference's newest-first rule (BoundedSelection.swift
+ *     :158-214);
+ *   - a result row holds kout = min(k, MANS_MAX_TOPK) entries; entries past
+ *     out_counts[q] are (+inf, MANS_EMPTY_ID);
+ *   - distances follow the reference's CPU exact path (ParallelFlatScan.swift
+ *     :237-258): IP = -dot, L2 = max(0, |q|^2 - 2 dot + |v|^2), cosine =
+ *     1 - dot / sqrt(|q|^2 |v|^2) (1 when the denominator is below 1e-10),
+ *     with dot accumulated in the order of Sources/MetalANNSC/dots.c:40-47
+ *     (one fp32 accumulator, index order, no fused multiply-add) and squared
+ *     norms by the same sequential rule, so returned distances are bit-equal
+ *     to the reference's x86-64 build of dots.c.
+ *
+ * Thread safety: every entry point may be called concurrently on one context
+ * (each host-pointer call takes a private workspace and stream from a pool,
+ * like FlatGPUSearch's FlatWorkspacePool, FlatGPUSearch.swift:1070-1139).
+ * Objects must not be destroyed while calls that use them are running.
+ */
+#ifndef MANS_CUDA_H
+#define MANS_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__cplusplus)
+extern "C" {
+#endif
+
+/* Metric codes, FlatGPUSearch.swift:134-140. */
+#define MANS_METRIC_COSINE 0
+#define MANS_METRIC_L2 1
+#define MANS_METRIC_IP 2
+#define MANS_METRIC_HAMMING 3
+
+/* FlatGPUSearch.maxTopK (FlatGPUSearch.swift:13) and emptyID (:19). */
+#define MANS_MAX_TOPK 256
+#define MANS_EMPTY_ID 0xFFFFFFFFu
+
+/* Status codes.  Each maps to one ANNSError case (Errors.swift:6-21); the
+ * tier-degradeable ones (Errors.swift:23-30) are PIPELINE, OOM, EXEC, SEARCH. */
+#define MANS_OK 0
+#define MANS_ERR_DIM 1      /* dimensionMismatch(expected:got:) */
+#define MANS_ERR_SEARCH 2   /* searchFailed(_:) */
+#define MANS_ERR_PIPELINE 3 /* gpuPipelineUnavailable(_:) */
+#define MANS_ERR_OOM 4      /* gpuResourceExhausted(_:) */
+#define MANS_ERR_EXEC 5     /* gpuExecutionFailed(_:), includes device wait timeouts */
+#define MANS_ERR_INVALID 6  /* constructionFailed(_:) (bad argument or handle) */
+#define MANS_ERR_DEVICE 7   /* deviceNotSupported */
+
+typedef struct mans_ctx mans_ctx;
+typedef struct mans_corpus mans_corpus;
+typedef struct mans_workspace mans_workspace;
+typedef struct mans_ivf mans_ivf;
+typedef struct mans_ivfpq mans_ivfpq;
+
+/* ---- context ------------------------------------------------------------ */
+
+/* Replaces `MetalContext()` creation (Sources/MetalANNSCore/MetalDevice.swift
+ * :40-81, called at Sources/MetalANNS/ANNSIndex.swift:35 and IVFPQIndex.swift
+ * :51).  Fails with MANS_ERR_DEVICE when `device` is not an sm_100 GPU, which
+ * the caller treats like a nil MetalContext (host tiers only). */
+int32_t mans_ctx_create(int32_t device, mans_ctx **out_ctx);
+int32_t mans_ctx_destroy(mans_ctx *ctx);
+
+/* Message of the last failed call on the calling thread (NUL-terminated,
+ * truncated to buf_len).  Replaces the String payloads of ANNSError. */
+int32_t mans_last_error_message(char *buf, size_t buf_len);
+
+/* Number of streaming multiprocessors of the context's device. */
+int32_t mans_ctx_sm_count(const mans_ctx *ctx);
+
+/* ---- corpus (VectorBuffer) --------------------------------------------- */
+
+/* Uploads a row-major fp32 corpus (n x dim), the layout of VectorBuffer
+ * (Sources/MetalANNSCore/VectorBuffer.swift:12-111) and of the zero-copy MANN
+ * v3 vector section (MmapIndexLoader.swift:117-123), and computes the row
+ * squared norms on the device (replaces the host norm cache of
+ * FlatGPUSearch.withCorpusSquaredNorms, FlatGPUSearch.swift:465-521).
+ * `id_offset` is added to every row index when results are reported (row
+ * shards of one corpus use their first global row). */
+int32_t mans_corpus_create(mans_ctx *ctx, const float *rows, int64_t n, int64_t dim,
+                           uint32_t id_offset, mans_corpus **out_corpus);
+
+/* Overwrites rows [start, start+count) and refreshes their norms; mirrors
+ * VectorBuffer.insert + FlatGPUSearch.invalidateHostNormCache
+ * (VectorBuffer.swift:44-51,77-91). */
+int32_t mans_corpus_update_rows(mans_corpus *corpus, int64_t start, const float *rows,
+                                int64_t count);
+int32_t mans_corpus_destroy(mans_corpus *corpus);
+int64_t mans_corpus_count(const mans_corpus *corpus);
+int64_t mans_corpus_dim(const mans_corpus *corpus);
+
+/* ---- workspaces (device-pointer calls) ---------------------------------- */
+
+/* A workspace owns the scratch of one in-flight device-pointer search.  It
+ * must not be used by two calls at once. */
+int32_t mans_workspace_create(mans_ctx *ctx, mans_workspace **out_ws);
+int32_t mans_workspace_destroy(mans_workspace *ws);
+/* Waits for the stream of the last call made with `ws` and reports a device
+ * side failure (MANS_ERR_EXEC) recorded by its kernels. */
+int32_t mans_workspace_check(mans_workspace *ws, void *cuda_stream);
+
+/* Measurement hooks (no reference counterpart; the reference's benchmark CLI
+ * times whole calls, Sources/MetalANNSBenchmarks/HotPathProfiler.swift:22-304).
+ * With timing enabled every later search made with `ws` brackets its dominant
+ * kernel (the scan) with CUDA events on the launching stream;
+ * mans_workspace_stats waits for them, returns the summed kernel time, the
+ * number of timed launches and the number of library kernels enqueued, and
+ * resets the counters. */
+int32_t mans_workspace_set_timing(mans_workspace *ws, int32_t enable);
+int32_t mans_workspace_stats(mans_workspace *ws, double *kernel_ms, int64_t *kernel_launches,
+                             int64_t *total_launches);
+
+/* ---- exact flat search -------------------------------------------------- */
+
+/* Exact batched search, host buffers.  Replaces FlatGPUSearch.batchSearch's
+ * GPU tier: runChunk's `flat_scan_distances` dispatch plus the host
+ * selectTopK/boundedTopK (FlatGPUSearch.swift:103-181, 652-707, 786-933).
+ * queries: nq x dim row-major; out_dist/out_ids: nq x kout; out_counts: nq.
+ * Validation follows batchSearch: dim != corpus dim -> MANS_ERR_DIM; metric
+ * hamming -> MANS_ERR_SEARCH; k <= 0 or an empty corpus -> all counts 0. */
+int32_t mans_flat_search(mans_ctx *ctx, const mans_corpus *corpus, const float *queries,
+                         int64_t nq, int64_t dim, int32_t k, int32_t metric, float *out_dist,
+                         uint32_t *out_ids, int32_t *out_counts);
+
+/* Same search with device pointers, enqueued on `cuda_stream` (a
+ * cudaStream_t; NULL = legacy default stream) without synchronising.
+ * Scratch comes from `ws`; call mans_workspace_check to surface device errors. */
+int32_t mans_flat_search_device(mans_ctx *ctx, const mans_corpus *corpus, mans_workspace *ws,
+                                const float *d_queries, int64_t nq, int32_t k, int32_t metric,
+                                float *d_out_dist, uint32_t *d_out_ids, int32_t *d_out_counts,
+                                void *cuda_stream);
+
+/* Merges `n_lists` per-shard result blocks (each nq x kin, sorted ascending by
+ * (distance, id), laid out list-major: list l at offset l*nq*kin) into the
+ * global top-k per query, by (distance, id).  This is the device form of
+ * ParallelFlatScan.mergeSorted (ParallelFlatScan.swift:288-315) used after
+ * the all-gather of row-shard results.  Device pointers, async on the stream. */
+int32_t mans_topk_merge_device(mans_ctx *ctx, mans_workspace *ws, const float *d_in_dist,
+                               const uint32_t *d_in_ids, const int32_t *d_in_counts,
+                               int32_t n_lists, int64_t nq, int32_t kin, int32_t k,
+                               float *d_out_dist, uint32_t *d_out_ids, int32_t *d_out_counts,
+                               void *cuda_stream);
+
+#if defined(__cplusplus)
+}
+#endif
+
+#endif /* MANS_CUDA_H */

@@ -1,0 +1,26 @@
+"""meltan_b200 -- B200-native search hot path for MetalANNS.
+
+The exact flat scan with top-k, IVF-flat probe-and-scan and IVF-PQ ADC scoring
+run as hand-written sm_100a CUDA kernels in ``libmans_cuda.so`` behind the C
+ABI of ``include/mans_cuda.h``; this package is the host-side binding.
+"""
+from .core import (  # noqa: F401
+    ANNSError,
+    ConstructionFailed,
+    Context,
+    DeviceNotSupported,
+    DimensionMismatch,
+    EMPTY_ID,
+    FlatGPUSearch,
+    GPUExecutionFailed,
+    GPUPipelineUnavailable,
+    GPUResourceExhausted,
+    MAX_TOP_K,
+    Metric,
+    SearchFailed,
+    SearchResult,
+    VectorBuffer,
+    Workspace,
+    check,
+    topk_merge_device,
+)

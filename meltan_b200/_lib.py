@@ -1,0 +1,72 @@
+"""ctypes binding of ``libmans_cuda.so`` (declared in ``include/mans_cuda.h``).
+
+Loading fails loudly when the shared library is missing: there is no CPU
+fallback anywhere in this package.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libmans_cuda.so")
+
+_F = C.POINTER(C.c_float)
+_U32 = C.POINTER(C.c_uint32)
+_I32 = C.POINTER(C.c_int32)
+_I64 = C.POINTER(C.c_int64)
+_U8 = C.POINTER(C.c_uint8)
+_VP = C.c_void_p
+
+# (name, restype, argtypes) for every symbol of include/mans_cuda.h
+SIGNATURES = {
+    "mans_ctx_create": (C.c_int32, [C.c_int32, C.POINTER(_VP)]),
+    "mans_ctx_destroy": (C.c_int32, [_VP]),
+    "mans_last_error_message": (C.c_int32, [C.c_char_p, C.c_size_t]),
+    "mans_ctx_sm_count": (C.c_int32, [_VP]),
+    "mans_corpus_create": (C.c_int32, [_VP, _VP, C.c_int64, C.c_int64, C.c_uint32, C.POINTER(_VP)]),
+    "mans_corpus_update_rows": (C.c_int32, [_VP, C.c_int64, _VP, C.c_int64]),
+    "mans_corpus_destroy": (C.c_int32, [_VP]),
+    "mans_corpus_count": (C.c_int64, [_VP]),
+    "mans_corpus_dim": (C.c_int64, [_VP]),
+    "mans_workspace_create": (C.c_int32, [_VP, C.POINTER(_VP)]),
+    "mans_workspace_destroy": (C.c_int32, [_VP]),
+    "mans_workspace_check": (C.c_int32, [_VP, _VP]),
+    "mans_workspace_set_timing": (C.c_int32, [_VP, C.c_int32]),
+    "mans_workspace_stats": (C.c_int32, [_VP, C.POINTER(C.c_double), _I64, _I64]),
+    "mans_flat_search": (C.c_int32, [_VP, _VP, _VP, C.c_int64, C.c_int64, C.c_int32, C.c_int32,
+                                     _VP, _VP, _VP]),
+    "mans_flat_search_device": (C.c_int32, [_VP, _VP, _VP, _VP, C.c_int64, C.c_int32, C.c_int32,
+                                            _VP, _VP, _VP, _VP]),
+    "mans_topk_merge_device": (C.c_int32, [_VP, _VP, _VP, _VP, _VP, C.c_int32, C.c_int64,
+                                           C.c_int32, C.c_int32, _VP, _VP, _VP, _VP]),
+}
+
+_lib = None
+
+
+def lib():
+    """Load the CUDA library (raises if it was never built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python -m meltan_b200.build` "
+                "(there is no CPU fallback)")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    buf = C.create_string_buffer(1024)
+    lib().mans_last_error_message(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def exported_symbols():
+    return list(SIGNATURES)

@@ -1,0 +1,313 @@
+"""Host-side mirror of the MetalANNS search-path interface over the C ABI.
+
+Names, argument meaning and error behaviour follow the reference Swift types
+(paths relative to the MetalANNS source tree):
+
+* ``Metric``             -- Sources/MetalANNSCore/Metric.swift:1-6, codes of
+                            FlatGPUSearch.swift:134-140
+* ``ANNSError``          -- Sources/MetalANNSCore/Errors.swift:6-31
+* ``SearchResult``       -- Sources/MetalANNSCore/SearchResult.swift:1-13
+* ``Context``            -- MetalContext (MetalDevice.swift:9-111)
+* ``VectorBuffer``       -- VectorBuffer.swift:12-111 (row-major fp32 corpus)
+* ``FlatGPUSearch``      -- FlatGPUSearch.swift:12-181 (search / batchSearch /
+                            isEligible)
+
+All computation runs in ``libmans_cuda.so``; this module only validates,
+marshals and maps status codes to exceptions.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import enum
+from dataclasses import dataclass
+from typing import List, Optional, Sequence
+
+import numpy as np
+
+from ._lib import last_error, lib
+
+MAX_TOP_K = 256
+EMPTY_ID = 0xFFFFFFFF
+
+
+class Metric(enum.IntEnum):
+    cosine = 0
+    l2 = 1
+    innerProduct = 2
+    hamming = 3
+
+
+# ---- errors (Errors.swift:6-31) ---------------------------------------------
+
+
+class ANNSError(Exception):
+    degradeable = False
+
+    @property
+    def is_tier_degradeable(self) -> bool:
+        """Errors.swift:23-30: pipeline, resource, execution and search failures."""
+        return self.degradeable
+
+
+class DimensionMismatch(ANNSError):
+    pass
+
+
+class SearchFailed(ANNSError):
+    degradeable = True
+
+
+class GPUPipelineUnavailable(ANNSError):
+    degradeable = True
+
+
+class GPUResourceExhausted(ANNSError):
+    degradeable = True
+
+
+class GPUExecutionFailed(ANNSError):
+    degradeable = True
+
+
+class ConstructionFailed(ANNSError):
+    pass
+
+
+class DeviceNotSupported(ANNSError):
+    pass
+
+
+_STATUS = {
+    1: DimensionMismatch,
+    2: SearchFailed,
+    3: GPUPipelineUnavailable,
+    4: GPUResourceExhausted,
+    5: GPUExecutionFailed,
+    6: ConstructionFailed,
+    7: DeviceNotSupported,
+}
+
+
+def check(status: int) -> None:
+    if status != 0:
+        raise _STATUS.get(status, ANNSError)(last_error())
+
+
+@dataclass
+class SearchResult:
+    id: str
+    score: float
+    internalID: int
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _ptr(a: np.ndarray):
+    return C.c_void_p(a.ctypes.data)
+
+
+# ---- context / storage ----------------------------------------------------------
+
+
+class Context:
+    """One CUDA device; stands in for MetalContext."""
+
+    def __init__(self, device: int = 0):
+        h = C.c_void_p()
+        check(lib().mans_ctx_create(device, C.byref(h)))
+        self._h = h
+        self.device = device
+
+    @property
+    def handle(self):
+        return self._h
+
+    @property
+    def sm_count(self) -> int:
+        return lib().mans_ctx_sm_count(self._h)
+
+    def close(self):
+        if self._h:
+            lib().mans_ctx_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class VectorBuffer:
+    """Device-resident row-major fp32 corpus with cached squared norms."""
+
+    def __init__(self, context: Context, vectors, id_offset: int = 0):
+        v = _f32(vectors)
+        if v.ndim != 2:
+            raise ConstructionFailed("vectors must be a 2-D array")
+        self.context = context
+        h = C.c_void_p()
+        check(lib().mans_corpus_create(context.handle, _ptr(v), v.shape[0], v.shape[1],
+                                       id_offset, C.byref(h)))
+        self._h = h
+        self.id_offset = id_offset
+
+    @property
+    def handle(self):
+        return self._h
+
+    @property
+    def count(self) -> int:
+        return lib().mans_corpus_count(self._h)
+
+    @property
+    def dim(self) -> int:
+        return lib().mans_corpus_dim(self._h)
+
+    def insert(self, vector, at: int) -> None:
+        """In-place row write; norms refresh on the device (VectorBuffer.swift:57-91)."""
+        self.batch_insert(np.atleast_2d(vector), at)
+
+    def batch_insert(self, vectors, starting_at: int) -> None:
+        v = _f32(np.atleast_2d(vectors))
+        if v.shape[1] != self.dim:
+            raise DimensionMismatch(f"expected {self.dim}, got {v.shape[1]}")
+        check(lib().mans_corpus_update_rows(self._h, starting_at, _ptr(v), v.shape[0]))
+
+    def close(self):
+        if self._h:
+            lib().mans_corpus_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Workspace:
+    """Scratch for device-pointer calls (one in-flight call at a time)."""
+
+    def __init__(self, context: Context):
+        h = C.c_void_p()
+        check(lib().mans_workspace_create(context.handle, C.byref(h)))
+        self._h = h
+        self.context = context
+
+    @property
+    def handle(self):
+        return self._h
+
+    def check(self, stream_ptr: int = 0) -> None:
+        check(lib().mans_workspace_check(self._h, C.c_void_p(stream_ptr)))
+
+    def set_timing(self, enable: bool) -> None:
+        check(lib().mans_workspace_set_timing(self._h, 1 if enable else 0))
+
+    def stats(self):
+        """(summed dominant-kernel ms, timed launches, all library launches)."""
+        ms = C.c_double()
+        kl = C.c_int64()
+        tl = C.c_int64()
+        check(lib().mans_workspace_stats(self._h, C.byref(ms), C.byref(kl), C.byref(tl)))
+        return ms.value, kl.value, tl.value
+
+    def close(self):
+        if self._h:
+            lib().mans_workspace_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ---- FlatGPUSearch --------------------------------------------------------------
+
+
+class FlatGPUSearch:
+    """Exact flat search (FlatGPUSearch.swift).  Results ascend by (distance, id)."""
+
+    maxTopK = MAX_TOP_K
+    minEligibleVectorCount = 64  # FlatGPUSearch.swift:15
+
+    @staticmethod
+    def is_eligible(vectors: VectorBuffer, metric: Metric, k: int, max_vector_count: int) -> bool:
+        """FlatGPUSearch.isEligible (FlatGPUSearch.swift:193-205)."""
+        if metric == Metric.hamming:
+            return False
+        if not (1 <= k <= MAX_TOP_K):
+            return False
+        if vectors.count < FlatGPUSearch.minEligibleVectorCount:
+            return False
+        return max_vector_count > 0 and vectors.count <= max_vector_count
+
+    @staticmethod
+    def batch_search_arrays(context: Context, queries, vectors: VectorBuffer, k: int,
+                            metric: Metric):
+        """Array form of batchSearch: (dist[nq, kout], ids[nq, kout], counts[nq])."""
+        q = _f32(np.atleast_2d(queries))
+        nq, dim = q.shape
+        kout = max(0, min(k, MAX_TOP_K))
+        od = np.empty((nq, kout), np.float32)
+        oi = np.empty((nq, kout), np.uint32)
+        oc = np.empty(nq, np.int32)
+        check(lib().mans_flat_search(context.handle, vectors.handle, _ptr(q), nq, dim, k,
+                                     int(metric), _ptr(od), _ptr(oi), _ptr(oc)))
+        return od, oi, oc
+
+    @staticmethod
+    def batch_search(context: Context, queries: Sequence, vectors: VectorBuffer, k: int,
+                     metric: Metric) -> List[List[SearchResult]]:
+        """FlatGPUSearch.batchSearch (FlatGPUSearch.swift:103-181)."""
+        if len(queries) == 0:
+            return []
+        if k <= 0:
+            return [[] for _ in queries]
+        if vectors.count == 0:
+            return [[] for _ in queries]
+        if metric == Metric.hamming:
+            raise SearchFailed("FlatGPUSearch does not support metric .hamming")
+        for q in queries:
+            if len(q) != vectors.dim:
+                raise DimensionMismatch(f"expected {vectors.dim}, got {len(q)}")
+        od, oi, oc = FlatGPUSearch.batch_search_arrays(context, np.asarray(queries), vectors, k,
+                                                       metric)
+        return [[SearchResult("", float(od[r, i]), int(oi[r, i])) for i in range(oc[r])]
+                for r in range(len(queries))]
+
+    @staticmethod
+    def search(context: Optional[Context], query, vectors: VectorBuffer, k: int,
+               metric: Metric) -> List[SearchResult]:
+        """FlatGPUSearch.search for one query (GPU tier)."""
+        if context is None:
+            raise DeviceNotSupported("no CUDA context")
+        out = FlatGPUSearch.batch_search(context, [list(query)], vectors, k, metric)
+        if not out:
+            raise SearchFailed("FlatGPUSearch produced no results")
+        return out[0]
+
+    @staticmethod
+    def search_device(context: Context, vectors: VectorBuffer, ws: Workspace, d_queries: int,
+                      nq: int, k: int, metric: Metric, d_out_dist: int, d_out_ids: int,
+                      d_out_counts: int, stream: int = 0) -> None:
+        """Device-pointer search enqueued on `stream` (no synchronisation)."""
+        check(lib().mans_flat_search_device(context.handle, vectors.handle, ws.handle,
+                                            C.c_void_p(d_queries), nq, k, int(metric),
+                                            C.c_void_p(d_out_dist), C.c_void_p(d_out_ids),
+                                            C.c_void_p(d_out_counts), C.c_void_p(stream)))
+
+
+def topk_merge_device(context: Context, ws: Workspace, d_in_dist: int, d_in_ids: int,
+                      d_in_counts: int, n_lists: int, nq: int, kin: int, k: int,
+                      d_out_dist: int, d_out_ids: int, d_out_counts: int, stream: int = 0):
+    """Merge of row-shard result blocks by (distance, id) (mergeSorted semantics)."""
+    check(lib().mans_topk_merge_device(context.handle, ws.handle, C.c_void_p(d_in_dist),
+                                       C.c_void_p(d_in_ids), C.c_void_p(d_in_counts), n_lists, nq,
+                                       kin, k, C.c_void_p(d_out_dist), C.c_void_p(d_out_ids),
+                                       C.c_void_p(d_out_counts), C.c_void_p(stream)))

@@ -1,0 +1,623 @@
+// capi.cu -- the C ABI of include/mans_cuda.h: contexts, corpora, workspaces
+// and the host orchestration of the flat exact search.
+//
+// The orchestration restates FlatGPUSearch.batchSearch's contract
+// (Sources/MetalANNSCore/FlatGPUSearch.swift:103-181): empty query list ->
+// nothing; k <= 0 or an empty corpus -> empty results; metric hamming ->
+// searchFailed; a query of the wrong width -> dimensionMismatch; effective k =
+// min(k, 256, n).  Device work replaces runChunk + selectTopK.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "internal.h"
+#include "kernels.h"
+#include "mans_cuda.h"
+
+using namespace mans;
+
+namespace mans {
+
+thread_local std::string g_last_error;
+
+int32_t fail(int32_t code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int32_t fail_cuda(cudaError_t e, const char* what) {
+  std::string msg = std::string(what) + ": " + cudaGetErrorString(e);
+  if (e == cudaErrorMemoryAllocation) return fail(MANS_ERR_OOM, msg);
+  return fail(MANS_ERR_EXEC, msg);
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+static std::once_flag g_encode_once;
+
+static PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode;
+}
+
+int32_t encode_row_map(CUtensorMap* map, const float* base, int64_t rows, int64_t dim,
+                       int64_t ld) {
+  auto enc = encoder();
+  if (!enc) return fail(MANS_ERR_PIPELINE, "cuTensorMapEncodeTiled is unavailable");
+  if (rows <= 0) rows = 1;
+  cuuint64_t gdim[2] = {static_cast<cuuint64_t>(dim), static_cast<cuuint64_t>(rows)};
+  cuuint64_t gstride[1] = {static_cast<cuuint64_t>(ld) * 4};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kTileCols), static_cast<cuuint32_t>(kTileRows)};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), gdim,
+                   gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MANS_ERR_PIPELINE, "cuTensorMapEncodeTiled failed");
+  return MANS_OK;
+}
+
+int32_t DeviceBuffer::reserve(size_t need) {
+  if (need <= bytes) return MANS_OK;
+  if (ptr) cudaFree(ptr);
+  ptr = nullptr;
+  bytes = 0;
+  size_t want = std::max<size_t>(need, 256);
+  cudaError_t e = cudaMalloc(&ptr, want);
+  if (e != cudaSuccess) {
+    ptr = nullptr;
+    return fail_cuda(e, "cudaMalloc(workspace)");
+  }
+  bytes = want;
+  return MANS_OK;
+}
+
+void DeviceBuffer::release() {
+  if (ptr) cudaFree(ptr);
+  ptr = nullptr;
+  bytes = 0;
+}
+
+int32_t PinnedBuffer::reserve(size_t need) {
+  if (need <= bytes) return MANS_OK;
+  if (ptr) cudaFreeHost(ptr);
+  ptr = nullptr;
+  bytes = 0;
+  size_t want = std::max<size_t>(need, 4096);
+  cudaError_t e = cudaMallocHost(&ptr, want);
+  if (e != cudaSuccess) {
+    ptr = nullptr;
+    return fail_cuda(e, "cudaMallocHost(workspace)");
+  }
+  bytes = want;
+  return MANS_OK;
+}
+
+void PinnedBuffer::release() {
+  if (ptr) cudaFreeHost(ptr);
+  ptr = nullptr;
+  bytes = 0;
+}
+
+DeviceGuard::DeviceGuard(int dev) {
+  cudaGetDevice(&prev);
+  if (prev != dev) cudaSetDevice(dev);
+  cur = dev;
+}
+DeviceGuard::~DeviceGuard() {
+  if (prev != cur) cudaSetDevice(prev);
+}
+
+mans_workspace* acquire_workspace(mans_ctx* ctx) {
+  {
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (!ctx->pool.empty()) {
+      mans_workspace* ws = ctx->pool.back();
+      ctx->pool.pop_back();
+      return ws;
+    }
+  }
+  mans_workspace* ws = new mans_workspace();
+  ws->ctx = ctx;
+  if (cudaStreamCreateWithFlags(&ws->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    delete ws;
+    return nullptr;
+  }
+  ws->own_stream = true;
+  return ws;
+}
+
+void release_workspace(mans_ctx* ctx, mans_workspace* ws) {
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  ctx->pool.push_back(ws);
+}
+
+void destroy_workspace(mans_workspace* ws) {
+  DeviceGuard g(ws->ctx->device);
+  ws->err.release();
+  ws->qnorms.release();
+  ws->slot_keys.release();
+  ws->slot_counts.release();
+  ws->queries.release();
+  ws->out_dist.release();
+  ws->out_ids.release();
+  ws->out_counts.release();
+  ws->aux.release();
+  ws->aux2.release();
+  ws->h_err.release();
+  for (auto& pr : ws->events) {
+    cudaEventDestroy(pr.first);
+    cudaEventDestroy(pr.second);
+  }
+  if (ws->own_stream && ws->stream) cudaStreamDestroy(ws->stream);
+  delete ws;
+}
+
+// Records a start event before the dominant kernel when timing is enabled;
+// returns the matching stop event (or null).
+static cudaEvent_t timing_begin(mans_workspace* ws, cudaStream_t stream) {
+  if (!ws->timing) return nullptr;
+  if (ws->events_used == ws->events.size()) {
+    cudaEvent_t a, b;
+    if (cudaEventCreate(&a) != cudaSuccess) return nullptr;
+    if (cudaEventCreate(&b) != cudaSuccess) {
+      cudaEventDestroy(a);
+      return nullptr;
+    }
+    ws->events.emplace_back(a, b);
+  }
+  auto& pr = ws->events[ws->events_used++];
+  cudaEventRecord(pr.first, stream);
+  return pr.second;
+}
+
+static void timing_end(cudaEvent_t stop, cudaStream_t stream) {
+  if (stop) cudaEventRecord(stop, stream);
+}
+
+static int pow2_at_least(int v) {
+  int p = 1;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+// Query-group width for a batch: the smallest power of two >= nq, at most 8.
+static int choose_qb(int64_t nq) {
+  if (nq <= 1) return 1;
+  if (nq <= 2) return 2;
+  if (nq <= 4) return 4;
+  return 8;
+}
+
+int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace* ws,
+                        const float* d_queries, int64_t nq, int32_t k, int32_t metric,
+                        float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
+                        cudaStream_t stream) {
+  const int32_t kout = std::min<int32_t>(k, MANS_MAX_TOPK);
+  const int64_t n = corpus->n;
+  if (nq <= 0) return MANS_OK;
+  if (k <= 0 || n <= 0) {
+    if (kout <= 0) {
+      cudaError_t e = cudaMemsetAsync(d_out_counts, 0, sizeof(int32_t) * nq, stream);
+      return e == cudaSuccess ? MANS_OK : fail_cuda(e, "cudaMemsetAsync");
+    }
+    cudaError_t e = launch_fill_empty(d_out_dist, d_out_ids, d_out_counts, nq, kout, stream);
+    return e == cudaSuccess ? MANS_OK : fail_cuda(e, "fill_empty launch");
+  }
+  const int32_t keff = static_cast<int32_t>(std::min<int64_t>(kout, n));
+  const int32_t kp = pow2_at_least(keff);
+  const int qb = choose_qb(nq);
+  const int64_t groups = (nq + qb - 1) / qb;
+  const int64_t tiles = (n + kTileRows - 1) / kTileRows;
+  int64_t splits = std::max<int64_t>(1, ctx->num_sms / std::max<int64_t>(groups, 1));
+  splits = std::min<int64_t>(splits, tiles);
+  const int64_t nseg = groups * splits;
+  if (nseg > INT32_MAX / 2) return fail(MANS_ERR_SEARCH, "query batch too large");
+  const int nchunks = static_cast<int>((corpus->dim + kTileCols - 1) / kTileCols);
+  const int stages = scan_max_stages(qb, nchunks);
+  if (stages < 2) return fail(MANS_ERR_SEARCH, "dimension too large for the flat scan kernel");
+
+  int32_t rc;
+  const size_t nslots = static_cast<size_t>(groups) * qb * splits;
+  if ((rc = ws->slot_keys.reserve(nslots * kp * sizeof(uint64_t))) != MANS_OK) return rc;
+  if ((rc = ws->slot_counts.reserve(nslots * sizeof(int32_t))) != MANS_OK) return rc;
+  if ((rc = ws->err.reserve(sizeof(int))) != MANS_OK) return rc;
+  float* qn = nullptr;
+  if (metric == MANS_METRIC_COSINE || metric == MANS_METRIC_L2) {
+    if ((rc = ws->qnorms.reserve(nq * sizeof(float))) != MANS_OK) return rc;
+    qn = static_cast<float*>(ws->qnorms.ptr);
+    cudaError_t e = launch_query_norms(d_queries, nq, static_cast<int32_t>(corpus->dim), qn, stream);
+    if (e != cudaSuccess) return fail_cuda(e, "query_norms launch");
+  }
+  if (!ws->err_cleared) {
+    cudaError_t e = cudaMemsetAsync(ws->err.ptr, 0, sizeof(int), stream);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaMemsetAsync(err)");
+    ws->err_cleared = true;
+  }
+
+  ScanParams p{};
+  p.segs = nullptr;
+  p.nseg = static_cast<int32_t>(nseg);
+  p.stages = stages;
+  p.flat_splits = static_cast<int32_t>(splits);
+  p.flat_tiles = static_cast<int32_t>(tiles);
+  p.n = n;
+  p.nq = nq;
+  p.queries = d_queries;
+  p.qidx = nullptr;
+  p.qnorms = qn;
+  p.norms = (metric == MANS_METRIC_IP) ? nullptr : corpus->norms;
+  p.ids = nullptr;
+  p.id_offset = corpus->id_offset;
+  p.dim = static_cast<int32_t>(corpus->dim);
+  p.nchunks = nchunks;
+  p.metric = metric;
+  p.k = keff;
+  p.kp = kp;
+  p.slot_keys = static_cast<uint64_t*>(ws->slot_keys.ptr);
+  p.slot_counts = static_cast<int32_t*>(ws->slot_counts.ptr);
+  p.err = static_cast<int*>(ws->err.ptr);
+  int grid = static_cast<int>(std::min<int64_t>(nseg, ctx->num_sms));
+  cudaEvent_t ev_stop = timing_begin(ws, stream);
+  cudaError_t e = launch_scan(qb, corpus->map, p, grid, stream);
+  if (e != cudaSuccess) return fail_cuda(e, "scan launch");
+  timing_end(ev_stop, stream);
+  ws->launches += (qn ? 1 : 0) + 2;
+
+  MergeParams m{};
+  m.in_keys = p.slot_keys;
+  m.in_counts = p.slot_counts;
+  m.q_slot_offsets = nullptr;
+  m.slots_per_query = static_cast<int32_t>(splits);
+  m.kp_in = kp;
+  m.nq = nq;
+  m.k = keff;
+  m.kp = kp;
+  m.kout = kout;
+  m.out_dist = d_out_dist;
+  m.out_ids = d_out_ids;
+  m.out_counts = d_out_counts;
+  m.err = p.err;
+  e = launch_merge(m, stream);
+  if (e != cudaSuccess) return fail_cuda(e, "merge launch");
+  return MANS_OK;
+}
+
+// Reads and clears the device error word of `ws` after its stream finished.
+int32_t check_device_error(mans_workspace* ws, cudaStream_t stream) {
+  cudaError_t e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return fail_cuda(e, "stream synchronize");
+  if (!ws->err.ptr || !ws->err_cleared) return MANS_OK;
+  int h = 0;
+  e = cudaMemcpy(&h, ws->err.ptr, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return fail_cuda(e, "error word readback");
+  if (h != 0) {
+    ws->err_cleared = false;
+    return fail(MANS_ERR_EXEC, h == kErrTimeout ? "device wait timed out"
+                                                 : "device kernel reported an error");
+  }
+  return MANS_OK;
+}
+
+}  // namespace mans
+
+// ============================================================================
+// C ABI
+// ============================================================================
+
+extern "C" {
+
+int32_t mans_last_error_message(char* buf, size_t buf_len) {
+  if (!buf || buf_len == 0) return MANS_ERR_INVALID;
+  size_t n = std::min(buf_len - 1, g_last_error.size());
+  std::memcpy(buf, g_last_error.data(), n);
+  buf[n] = '\0';
+  return MANS_OK;
+}
+
+int32_t mans_ctx_create(int32_t device, mans_ctx** out_ctx) {
+  if (!out_ctx) return fail(MANS_ERR_INVALID, "out_ctx is null");
+  *out_ctx = nullptr;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count)
+    return fail(MANS_ERR_DEVICE, "no CUDA device with that index");
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess)
+    return fail(MANS_ERR_DEVICE, "cudaGetDeviceProperties failed");
+  if (prop.major != 10) return fail(MANS_ERR_DEVICE, "device is not an sm_100 (Blackwell) GPU");
+  DeviceGuard g(device);
+  cudaError_t e = scan_configure(static_cast<int>(prop.sharedMemPerBlockOptin));
+  if (e != cudaSuccess) return fail_cuda(e, "kernel configuration");
+  if (!encoder()) return fail(MANS_ERR_PIPELINE, "cuTensorMapEncodeTiled is unavailable");
+  mans_ctx* ctx = new mans_ctx();
+  ctx->device = device;
+  ctx->num_sms = prop.multiProcessorCount;
+  ctx->max_smem = static_cast<int>(prop.sharedMemPerBlockOptin);
+  *out_ctx = ctx;
+  return MANS_OK;
+}
+
+int32_t mans_ctx_destroy(mans_ctx* ctx) {
+  if (!ctx) return MANS_OK;
+  DeviceGuard g(ctx->device);
+  cudaDeviceSynchronize();
+  for (mans_workspace* ws : ctx->pool) destroy_workspace(ws);
+  ctx->pool.clear();
+  delete ctx;
+  return MANS_OK;
+}
+
+int32_t mans_ctx_sm_count(const mans_ctx* ctx) { return ctx ? ctx->num_sms : 0; }
+
+int32_t mans_corpus_create(mans_ctx* ctx, const float* rows, int64_t n, int64_t dim,
+                           uint32_t id_offset, mans_corpus** out_corpus) {
+  if (!ctx || !out_corpus) return fail(MANS_ERR_INVALID, "null context or output");
+  *out_corpus = nullptr;
+  if (n < 0 || dim <= 0) return fail(MANS_ERR_INVALID, "corpus needs n >= 0 and dim > 0");
+  if (n > 0 && !rows) return fail(MANS_ERR_INVALID, "rows is null");
+  if (n > static_cast<int64_t>(INT32_MAX)) return fail(MANS_ERR_INVALID, "corpus too large");
+  DeviceGuard g(ctx->device);
+  mans_corpus* c = new mans_corpus();
+  c->ctx = ctx;
+  c->n = n;
+  c->dim = dim;
+  c->ld = (dim + 3) / 4 * 4;  // 16-byte row pitch, required by TMA
+  c->id_offset = id_offset;
+  size_t rows_bytes = static_cast<size_t>(std::max<int64_t>(n, 1)) * c->ld * sizeof(float);
+  cudaError_t e = cudaMalloc(&c->rows, rows_bytes);
+  if (e != cudaSuccess) {
+    delete c;
+    return fail_cuda(e, "cudaMalloc(corpus)");
+  }
+  e = cudaMalloc(&c->norms, static_cast<size_t>(std::max<int64_t>(n, 1)) * sizeof(float));
+  if (e != cudaSuccess) {
+    cudaFree(c->rows);
+    delete c;
+    return fail_cuda(e, "cudaMalloc(norms)");
+  }
+  if (n > 0) {
+    if (c->ld != dim) cudaMemset(c->rows, 0, rows_bytes);
+    e = cudaMemcpy2D(c->rows, c->ld * sizeof(float), rows, dim * sizeof(float),
+                     dim * sizeof(float), n, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = launch_row_norms(c->rows, n, static_cast<int32_t>(dim), c->ld, c->norms, 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+      cudaFree(c->rows);
+      cudaFree(c->norms);
+      delete c;
+      return fail_cuda(e, "corpus upload");
+    }
+  }
+  int32_t rc = encode_row_map(&c->map, c->rows, n, dim, c->ld);
+  if (rc != MANS_OK) {
+    cudaFree(c->rows);
+    cudaFree(c->norms);
+    delete c;
+    return rc;
+  }
+  *out_corpus = c;
+  return MANS_OK;
+}
+
+int32_t mans_corpus_update_rows(mans_corpus* c, int64_t start, const float* rows, int64_t count) {
+  if (!c) return fail(MANS_ERR_INVALID, "corpus is null");
+  if (start < 0 || count < 0 || start + count > c->n)
+    return fail(MANS_ERR_INVALID, "row range outside the corpus");
+  if (count == 0) return MANS_OK;
+  if (!rows) return fail(MANS_ERR_INVALID, "rows is null");
+  DeviceGuard g(c->ctx->device);
+  float* dst = c->rows + start * c->ld;
+  cudaError_t e = cudaMemcpy2D(dst, c->ld * sizeof(float), rows, c->dim * sizeof(float),
+                               c->dim * sizeof(float), count, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = launch_row_norms(dst, count, static_cast<int32_t>(c->dim), c->ld, c->norms + start, 0);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail_cuda(e, "corpus update");
+  return MANS_OK;
+}
+
+int32_t mans_corpus_destroy(mans_corpus* c) {
+  if (!c) return MANS_OK;
+  DeviceGuard g(c->ctx->device);
+  cudaDeviceSynchronize();
+  cudaFree(c->rows);
+  cudaFree(c->norms);
+  delete c;
+  return MANS_OK;
+}
+
+int64_t mans_corpus_count(const mans_corpus* c) { return c ? c->n : 0; }
+int64_t mans_corpus_dim(const mans_corpus* c) { return c ? c->dim : 0; }
+
+int32_t mans_workspace_create(mans_ctx* ctx, mans_workspace** out_ws) {
+  if (!ctx || !out_ws) return fail(MANS_ERR_INVALID, "null context or output");
+  mans_workspace* ws = new mans_workspace();
+  ws->ctx = ctx;
+  ws->stream = nullptr;
+  ws->own_stream = false;
+  *out_ws = ws;
+  return MANS_OK;
+}
+
+int32_t mans_workspace_destroy(mans_workspace* ws) {
+  if (!ws) return MANS_OK;
+  {
+    DeviceGuard g(ws->ctx->device);
+    cudaDeviceSynchronize();
+  }
+  destroy_workspace(ws);
+  return MANS_OK;
+}
+
+int32_t mans_workspace_set_timing(mans_workspace* ws, int32_t enable) {
+  if (!ws) return fail(MANS_ERR_INVALID, "workspace is null");
+  ws->timing = enable != 0;
+  ws->events_used = 0;
+  ws->launches = 0;
+  return MANS_OK;
+}
+
+int32_t mans_workspace_stats(mans_workspace* ws, double* kernel_ms, int64_t* kernel_launches,
+                             int64_t* total_launches) {
+  if (!ws) return fail(MANS_ERR_INVALID, "workspace is null");
+  DeviceGuard g(ws->ctx->device);
+  double total = 0.0;
+  for (size_t i = 0; i < ws->events_used; ++i) {
+    float ms = 0.0f;
+    cudaError_t e = cudaEventSynchronize(ws->events[i].second);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, ws->events[i].first, ws->events[i].second);
+    if (e != cudaSuccess) return fail_cuda(e, "kernel timing");
+    total += ms;
+  }
+  if (kernel_ms) *kernel_ms = total;
+  if (kernel_launches) *kernel_launches = static_cast<int64_t>(ws->events_used);
+  if (total_launches) *total_launches = ws->launches;
+  ws->events_used = 0;
+  ws->launches = 0;
+  return MANS_OK;
+}
+
+int32_t mans_workspace_check(mans_workspace* ws, void* cuda_stream) {
+  if (!ws) return fail(MANS_ERR_INVALID, "workspace is null");
+  DeviceGuard g(ws->ctx->device);
+  return check_device_error(ws, static_cast<cudaStream_t>(cuda_stream));
+}
+
+static int32_t validate_flat(const mans_ctx* ctx, const mans_corpus* corpus, int64_t nq,
+                             int32_t metric) {
+  if (!ctx || !corpus) return fail(MANS_ERR_INVALID, "null context or corpus");
+  if (corpus->ctx != ctx) return fail(MANS_ERR_INVALID, "corpus belongs to another context");
+  if (nq < 0) return fail(MANS_ERR_INVALID, "negative query count");
+  if (metric == MANS_METRIC_HAMMING)
+    return fail(MANS_ERR_SEARCH, "FlatGPUSearch does not support metric .hamming");
+  if (metric < 0 || metric > MANS_METRIC_HAMMING) return fail(MANS_ERR_INVALID, "unknown metric");
+  return MANS_OK;
+}
+
+int32_t mans_flat_search(mans_ctx* ctx, const mans_corpus* corpus, const float* queries,
+                         int64_t nq, int64_t dim, int32_t k, int32_t metric, float* out_dist,
+                         uint32_t* out_ids, int32_t* out_counts) {
+  int32_t rc = validate_flat(ctx, corpus, nq, metric);
+  if (rc != MANS_OK) return rc;
+  if (nq == 0) return MANS_OK;
+  if (k <= 0 || corpus->n <= 0) {
+    const int32_t kout = std::max<int32_t>(0, std::min<int32_t>(k, MANS_MAX_TOPK));
+    for (int64_t i = 0; i < nq * kout; ++i) {
+      out_dist[i] = __builtin_inff();
+      out_ids[i] = MANS_EMPTY_ID;
+    }
+    for (int64_t i = 0; i < nq; ++i) out_counts[i] = 0;
+    return MANS_OK;
+  }
+  if (dim != corpus->dim) {
+    char msg[128];
+    std::snprintf(msg, sizeof msg, "dimensionMismatch(expected: %lld, got: %lld)",
+                  static_cast<long long>(corpus->dim), static_cast<long long>(dim));
+    return fail(MANS_ERR_DIM, msg);
+  }
+  if (!queries || !out_dist || !out_ids || !out_counts)
+    return fail(MANS_ERR_INVALID, "null buffer");
+  DeviceGuard g(ctx->device);
+  mans_workspace* ws = acquire_workspace(ctx);
+  if (!ws) return fail(MANS_ERR_OOM, "cannot create a workspace stream");
+  const int32_t kout = std::min<int32_t>(k, MANS_MAX_TOPK);
+  cudaStream_t st = ws->stream;
+  do {
+    if ((rc = ws->queries.reserve(nq * dim * sizeof(float))) != MANS_OK) break;
+    if ((rc = ws->out_dist.reserve(nq * kout * sizeof(float))) != MANS_OK) break;
+    if ((rc = ws->out_ids.reserve(nq * kout * sizeof(uint32_t))) != MANS_OK) break;
+    if ((rc = ws->out_counts.reserve(nq * sizeof(int32_t))) != MANS_OK) break;
+    cudaError_t e = cudaMemcpyAsync(ws->queries.ptr, queries, nq * dim * sizeof(float),
+                                    cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) {
+      rc = fail_cuda(e, "query upload");
+      break;
+    }
+    rc = run_flat_search(ctx, corpus, ws, static_cast<const float*>(ws->queries.ptr), nq, k, metric,
+                         static_cast<float*>(ws->out_dist.ptr),
+                         static_cast<uint32_t*>(ws->out_ids.ptr),
+                         static_cast<int32_t*>(ws->out_counts.ptr), st);
+    if (rc != MANS_OK) break;
+    e = cudaMemcpyAsync(out_dist, ws->out_dist.ptr, nq * kout * sizeof(float),
+                        cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(out_ids, ws->out_ids.ptr, nq * kout * sizeof(uint32_t),
+                          cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(out_counts, ws->out_counts.ptr, nq * sizeof(int32_t),
+                          cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) {
+      rc = fail_cuda(e, "result download");
+      break;
+    }
+    rc = check_device_error(ws, st);
+  } while (false);
+  release_workspace(ctx, ws);
+  return rc;
+}
+
+int32_t mans_flat_search_device(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace* ws,
+                                const float* d_queries, int64_t nq, int32_t k, int32_t metric,
+                                float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
+                                void* cuda_stream) {
+  int32_t rc = validate_flat(ctx, corpus, nq, metric);
+  if (rc != MANS_OK) return rc;
+  if (!ws || ws->ctx != ctx) return fail(MANS_ERR_INVALID, "workspace missing or foreign");
+  DeviceGuard g(ctx->device);
+  return run_flat_search(ctx, corpus, ws, d_queries, nq, k, metric, d_out_dist, d_out_ids,
+                         d_out_counts, static_cast<cudaStream_t>(cuda_stream));
+}
+
+int32_t mans_topk_merge_device(mans_ctx* ctx, mans_workspace* ws, const float* d_in_dist,
+                               const uint32_t* d_in_ids, const int32_t* d_in_counts,
+                               int32_t n_lists, int64_t nq, int32_t kin, int32_t k,
+                               float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
+                               void* cuda_stream) {
+  if (!ctx || !ws) return fail(MANS_ERR_INVALID, "null context or workspace");
+  if (n_lists < 0 || nq < 0 || kin < 0) return fail(MANS_ERR_INVALID, "negative size");
+  if (nq == 0) return MANS_OK;
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+  const int32_t kout = std::min<int32_t>(k, MANS_MAX_TOPK);
+  if (k <= 0 || n_lists == 0 || kin == 0) {
+    if (kout <= 0) {
+      cudaError_t e = cudaMemsetAsync(d_out_counts, 0, sizeof(int32_t) * nq, st);
+      return e == cudaSuccess ? MANS_OK : fail_cuda(e, "cudaMemsetAsync");
+    }
+    cudaError_t e = launch_fill_empty(d_out_dist, d_out_ids, d_out_counts, nq, kout, st);
+    return e == cudaSuccess ? MANS_OK : fail_cuda(e, "fill_empty launch");
+  }
+  int32_t rc;
+  if ((rc = ws->err.reserve(sizeof(int))) != MANS_OK) return rc;
+  MergeParams m{};
+  m.in_dist = d_in_dist;
+  m.in_ids = d_in_ids;
+  m.in_counts = d_in_counts;
+  m.n_lists = n_lists;
+  m.kp_in = kin;
+  m.nq = nq;
+  m.k = kout;
+  m.kp = pow2_at_least(kout);
+  m.kout = kout;
+  m.out_dist = d_out_dist;
+  m.out_ids = d_out_ids;
+  m.out_counts = d_out_counts;
+  m.err = static_cast<int*>(ws->err.ptr);
+  cudaError_t e = launch_merge(m, st);
+  if (e != cudaSuccess) return fail_cuda(e, "merge launch");
+  ws->launches += 1;
+  return MANS_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,223 @@
+// common.cuh -- device helpers shared by the search kernels (sm_100a).
+//
+// mbarrier / TMA wrappers are thin inline-PTX shims.  Every wait is bounded by
+// the global nanosecond timer: a wait that runs past kWaitLimitNs records
+// kErrTimeout in the launch's error word and returns false, so no kernel can
+// spin forever.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kernels.h"
+
+namespace mans {
+
+constexpr int kMaxTopK = 256;
+constexpr uint32_t kEmptyId = 0xFFFFFFFFu;
+constexpr uint64_t kKeyMax = ~0ull;
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+
+enum Metric : int { kCosine = 0, kL2 = 1, kIP = 2, kHamming = 3 };
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---- mbarrier ---------------------------------------------------------------
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the phase with the given parity to complete.  Returns false (and
+// records kErrTimeout) when kWaitLimitNs passes first.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  unsigned long long t0 = global_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 63u && global_ns() - t0 > kWaitLimitNs) {
+      if (err) atomicExch(err, kErrTimeout);
+      return false;
+    }
+  }
+}
+
+// ---- TMA ----------------------------------------------------------------------
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 2-D tiled bulk tensor load (no multicast) completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int32_t x,
+                                            int32_t y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---- named barriers -----------------------------------------------------------
+
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---- (distance, id) keys ---------------------------------------------------------
+//
+// A 64-bit key orders candidates by (distance, id): the high word is the
+// distance mapped to an order-preserving unsigned integer, the low word the id.
+// -0.0 is folded onto +0.0 first so that keys order exactly like float `<`
+// (which treats the two zeros as equal, leaving the id to break the tie).
+
+__device__ __forceinline__ uint32_t float_to_ordered(float f) {
+  uint32_t u = __float_as_uint(f);
+  if (u == 0x80000000u) u = 0u;
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ float ordered_to_float(uint32_t o) {
+  uint32_t u = (o & 0x80000000u) ? (o & 0x7FFFFFFFu) : ~o;
+  return __uint_as_float(u);
+}
+
+__device__ __forceinline__ uint64_t make_key(float d, uint32_t id) {
+  return (static_cast<uint64_t>(float_to_ordered(d)) << 32) | id;
+}
+
+__device__ __forceinline__ float key_distance(uint64_t key) {
+  return ordered_to_float(static_cast<uint32_t>(key >> 32));
+}
+
+__device__ __forceinline__ uint32_t key_id(uint64_t key) { return static_cast<uint32_t>(key); }
+
+// ---- metric finalize ---------------------------------------------------------------
+//
+// The reference CPU exact path (ParallelFlatScan.swift:237-258,
+// IVFFlatSearch.swift:293-311) with every operation rounded on its own:
+//   IP     : -dot
+//   L2     : max(0, (qn - 2*dot) + vn)
+//   cosine : denom = sqrt(qn*vn); denom < 1e-10 ? 1 : 1 - dot/denom
+
+__device__ __forceinline__ float finalize_distance(int metric, float dot, float qn, float vn) {
+  if (metric == kIP) return -dot;
+  if (metric == kL2) {
+    float t = __fadd_rn(__fsub_rn(qn, __fmul_rn(2.0f, dot)), vn);
+    return t > 0.0f ? t : 0.0f;
+  }
+  float denom = __fsqrt_rn(__fmul_rn(qn, vn));
+  if (denom < 1e-10f) return 1.0f;
+  return __fsub_rn(1.0f, __fdiv_rn(dot, denom));
+}
+
+// ---- block bitonic sort over shared-memory keys -------------------------------------
+//
+// Sorts n (a power of two) keys ascending with NT threads that share named
+// barrier `bar_id`.  The caller synchronises before the call; the call ends
+// with a barrier.
+template <int NT>
+__device__ __forceinline__ void bitonic_sort_keys(uint64_t* a, int n, int tid, int bar_id) {
+  for (int k = 2; k <= n; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = tid; i < n; i += NT) {
+        int ixj = i ^ j;
+        if (ixj > i) {
+          uint64_t x = a[i], y = a[ixj];
+          bool up = (i & k) == 0;
+          if ((x > y) == up) {
+            a[i] = y;
+            a[ixj] = x;
+          }
+        }
+      }
+      named_sync(bar_id, NT);
+    }
+  }
+}
+
+// Running top-k of one query inside a thread block:
+//   buf[0, kp)      -- the current best keys (ascending, `nbest` of them valid)
+//   buf[kp, sortn)  -- an append queue of candidates below the threshold
+// merge() sorts both regions together and keeps the first k keys.
+struct TopKState {
+  uint64_t* buf;
+  int* qcount;  // queue fill
+  int* nbest;   // valid best keys (<= k)
+  uint64_t* thr;  // k-th best key, or kKeyMax while fewer than k are known
+};
+
+template <int NT>
+__device__ __forceinline__ void topk_merge(TopKState s, int k, int kp, int sortn, int tid,
+                                           int bar_id) {
+  int qc = *s.qcount;
+  int nb = *s.nbest;
+  for (int i = tid; i < sortn; i += NT) {
+    bool keep = (i < nb) || (i >= kp && i < kp + qc);
+    if (!keep) s.buf[i] = kKeyMax;
+  }
+  named_sync(bar_id, NT);
+  bitonic_sort_keys<NT>(s.buf, sortn, tid, bar_id);
+  if (tid == 0) {
+    int total = nb + qc;
+    int keep = total < k ? total : k;
+    *s.nbest = keep;
+    *s.qcount = 0;
+    *s.thr = keep == k ? s.buf[k - 1] : kKeyMax;
+  }
+  named_sync(bar_id, NT);
+}
+
+// Appends `key` to the queue when it beats the threshold.  Warp-aggregated:
+// one shared atomic per warp and query.
+__device__ __forceinline__ void topk_offer(TopKState s, int kp, uint64_t key, bool valid) {
+  bool pass = valid && key < *s.thr;
+  unsigned mask = __ballot_sync(0xFFFFFFFFu, pass);
+  if (mask == 0) return;
+  int lane = threadIdx.x & 31;
+  int leader = __ffs(mask) - 1;
+  int base = 0;
+  if (lane == leader) base = atomicAdd(s.qcount, __popc(mask));
+  base = __shfl_sync(0xFFFFFFFFu, base, leader);
+  if (pass) {
+    int pos = base + __popc(mask & ((1u << lane) - 1u));
+    s.buf[kp + pos] = key;
+  }
+}
+
+}  // namespace mans

@@ -1,0 +1,95 @@
+// internal.h -- library-private object layouts behind the opaque C handles.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+struct mans_workspace;
+
+namespace mans {
+
+struct DeviceBuffer {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  int32_t reserve(size_t need);  // grows (contents not kept)
+  void release();
+};
+
+struct PinnedBuffer {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  int32_t reserve(size_t need);
+  void release();
+};
+
+struct DeviceGuard {
+  int prev = -1, cur = -1;
+  explicit DeviceGuard(int dev);
+  ~DeviceGuard();
+};
+
+int32_t fail(int32_t code, const std::string& msg);
+int32_t fail_cuda(cudaError_t e, const char* what);
+int32_t encode_row_map(CUtensorMap* map, const float* base, int64_t rows, int64_t dim, int64_t ld);
+
+}  // namespace mans
+
+struct mans_ctx {
+  int device = 0;
+  int num_sms = 0;
+  int max_smem = 0;
+  std::mutex mu;
+  std::vector<mans_workspace*> pool;  // idle workspaces for host-pointer calls
+};
+
+// Row-major fp32 rows with a 16-byte pitch (ld = dim rounded up to 4), the
+// squared row norms and the TMA descriptor over them.
+struct mans_corpus {
+  mans_ctx* ctx = nullptr;
+  int64_t n = 0;
+  int64_t dim = 0;
+  int64_t ld = 0;
+  uint32_t id_offset = 0;
+  float* rows = nullptr;
+  float* norms = nullptr;
+  CUtensorMap map;
+};
+
+struct mans_workspace {
+  mans_ctx* ctx = nullptr;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  bool err_cleared = false;
+  mans::DeviceBuffer err;
+  mans::DeviceBuffer qnorms;
+  mans::DeviceBuffer slot_keys;
+  mans::DeviceBuffer slot_counts;
+  mans::DeviceBuffer queries;
+  mans::DeviceBuffer out_dist;
+  mans::DeviceBuffer out_ids;
+  mans::DeviceBuffer out_counts;
+  mans::DeviceBuffer aux;
+  mans::DeviceBuffer aux2;
+  mans::PinnedBuffer h_err;
+  // optional CUDA-event timing of the dominant kernel (scan) launches
+  bool timing = false;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> events;
+  size_t events_used = 0;
+  int64_t launches = 0;  // library kernels enqueued through this workspace
+};
+
+namespace mans {
+mans_workspace* acquire_workspace(mans_ctx* ctx);
+void release_workspace(mans_ctx* ctx, mans_workspace* ws);
+void destroy_workspace(mans_workspace* ws);
+int32_t check_device_error(mans_workspace* ws, cudaStream_t stream);
+int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace* ws,
+                        const float* d_queries, int64_t nq, int32_t k, int32_t metric,
+                        float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
+                        cudaStream_t stream);
+}  // namespace mans
