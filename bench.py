@@ -40,8 +40,8 @@ METRIC_NAMES = {"cosine": 0, "l2": 1, "ip": 2}
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--n", type=int, default=1_000_000)
     ap.add_argument("--dim", type=int, default=384)
@@ -60,6 +60,58 @@ def make_data(n, dim, nq, seed=0):
     q = rng.standard_normal((nq, dim), dtype=np.float32)
     q /= np.linalg.norm(q, axis=1, keepdims=True)
     return v, q
+
+
+def make_mixture(n, dim, components, nq, sigma=0.3, seed=0):
+    """BASELINE.json configs[2..3] generator: centres = normalise(N(0,1)),
+    x = centre[assign] + sigma * N(0,1), renormalised; queries drawn from the
+    same mixture after the database."""
+    rng = np.random.default_rng(seed)
+    centres = rng.standard_normal((components, dim), dtype=np.float32)
+    centres /= np.linalg.norm(centres, axis=1, keepdims=True)
+
+    def draw(m):
+        a = rng.integers(0, components, m)
+        x = centres[a] + np.float32(sigma) * rng.standard_normal((m, dim), dtype=np.float32)
+        x /= np.linalg.norm(x, axis=1, keepdims=True)
+        return x.astype(np.float32)
+
+    return draw(n), draw(nq)
+
+
+def train_partition(v, nlist, metric, iters=4, seed=42, device=None):
+    """Coarse centroids + row assignment for an IVF partition (build-time step,
+    outside the search path): Lloyd iterations on a strided sample, as
+    IVFFlatSearch.buildPartition samples min(n, max(L, min(4096, 16L))) rows
+    (IVFFlatSearch.swift:529-551), computed with torch matmuls.  Returns
+    (centroids, assignment) with assignment = argmin of the metric key."""
+    import torch
+    dev = device or ("cuda" if torch.cuda.is_available() else "cpu")
+    n = v.shape[0]
+    sample = min(n, max(nlist, min(4096, 16 * nlist)))
+    stride = max(1, n // sample)
+    x = torch.from_numpy(v[::stride][:sample]).to(dev)
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    cent = x[torch.randperm(x.shape[0], generator=g)[:nlist].to(dev)].clone()
+    for _ in range(iters):
+        a = torch.argmax(x @ cent.T - 0.5 * (cent * cent).sum(1), dim=1)
+        s = torch.zeros_like(cent).index_add_(0, a, x)
+        c = torch.bincount(a, minlength=nlist).unsqueeze(1).to(s.dtype)
+        cent = torch.where(c > 0, s / c.clamp(min=1), cent)
+    full = torch.from_numpy(v).to(dev)
+    cn = (cent * cent).sum(1)
+    assign = torch.empty(n, dtype=torch.int64, device=dev)
+    for a0 in range(0, n, 65536):
+        xb = full[a0:a0 + 65536]
+        dots = xb @ cent.T
+        if metric == 2:
+            key = -dots
+        elif metric == 1:
+            key = cn - 2 * dots
+        else:
+            key = -dots / cn.clamp(min=1e-20).sqrt()
+        assign[a0:a0 + 65536] = torch.argmin(key, dim=1)
+    return cent.cpu().numpy().astype(np.float32), assign.cpu().numpy()
 
 
 def p50(xs):

@@ -156,6 +156,33 @@ int32_t mans_topk_merge_device(mans_ctx *ctx, mans_workspace *ws, const float *d
                                float *d_out_dist, uint32_t *d_out_ids, int32_t *d_out_counts,
                                void *cuda_stream);
 
+/* ---- IVF-flat ------------------------------------------------------------ */
+
+/* Uploads an IVF-flat partition in the layout of IVFFlatSearch.Partition
+ * (Sources/MetalANNSCore/IVFFlatSearch.swift:39-95): `centroids` nlist x dim,
+ * `packed_rows` n x dim with packed[p] = corpus[list_ids[p]], list p of
+ * list_offsets[l]..list_offsets[l+1].  Centroid and packed-row squared norms
+ * are computed on the device (the centroidNormSq / packedNormSq arrays). */
+int32_t mans_ivf_create(mans_ctx *ctx, const float *centroids, int32_t nlist, int64_t dim,
+                        const float *packed_rows, const uint32_t *list_ids,
+                        const int64_t *list_offsets, int64_t n, mans_ivf **out_ivf);
+int32_t mans_ivf_destroy(mans_ivf *ivf);
+int64_t mans_ivf_list_count(const mans_ivf *ivf);
+
+/* IVF-flat probe-and-scan, replacing IVFFlatSearch.search(query:partition:k:
+ * nprobe:metric:) / scanProbedLists (IVFFlatSearch.swift:115-133, 214-291)
+ * for a batch: nprobe is clamped to [1, nlist]; the nprobe lists with the
+ * smallest centroid keys (ties to the lower list) are scanned exactly and the
+ * top min(k, 256, candidates) are returned by (distance, id).  nprobe >= nlist
+ * scans every list (exact).  256 < nprobe < nlist fails with MANS_ERR_SEARCH. */
+int32_t mans_ivf_search(mans_ctx *ctx, mans_ivf *ivf, const float *queries, int64_t nq,
+                        int64_t dim, int32_t k, int32_t nprobe, int32_t metric, float *out_dist,
+                        uint32_t *out_ids, int32_t *out_counts);
+int32_t mans_ivf_search_device(mans_ctx *ctx, mans_ivf *ivf, mans_workspace *ws,
+                               const float *d_queries, int64_t nq, int32_t k, int32_t nprobe,
+                               int32_t metric, float *d_out_dist, uint32_t *d_out_ids,
+                               int32_t *d_out_counts, void *cuda_stream);
+
 #if defined(__cplusplus)
 }
 #endif

@@ -24,3 +24,4 @@ from .core import (  # noqa: F401
     check,
     topk_merge_device,
 )
+from .ivf import IVFFlatSearch, Partition  # noqa: F401,E402

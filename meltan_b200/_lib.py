@@ -40,6 +40,14 @@ SIGNATURES = {
                                             _VP, _VP, _VP, _VP]),
     "mans_topk_merge_device": (C.c_int32, [_VP, _VP, _VP, _VP, _VP, C.c_int32, C.c_int64,
                                            C.c_int32, C.c_int32, _VP, _VP, _VP, _VP]),
+    "mans_ivf_create": (C.c_int32, [_VP, _VP, C.c_int32, C.c_int64, _VP, _VP, _VP, C.c_int64,
+                                    C.POINTER(_VP)]),
+    "mans_ivf_destroy": (C.c_int32, [_VP]),
+    "mans_ivf_list_count": (C.c_int64, [_VP]),
+    "mans_ivf_search": (C.c_int32, [_VP, _VP, _VP, C.c_int64, C.c_int64, C.c_int32, C.c_int32,
+                                    C.c_int32, _VP, _VP, _VP]),
+    "mans_ivf_search_device": (C.c_int32, [_VP, _VP, _VP, _VP, C.c_int64, C.c_int32, C.c_int32,
+                                           C.c_int32, _VP, _VP, _VP, _VP]),
 }
 
 _lib = None

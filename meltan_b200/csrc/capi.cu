@@ -166,7 +166,7 @@ void destroy_workspace(mans_workspace* ws) {
 
 // Records a start event before the dominant kernel when timing is enabled;
 // returns the matching stop event (or null).
-static cudaEvent_t timing_begin(mans_workspace* ws, cudaStream_t stream) {
+cudaEvent_t timing_begin(mans_workspace* ws, cudaStream_t stream) {
   if (!ws->timing) return nullptr;
   if (ws->events_used == ws->events.size()) {
     cudaEvent_t a, b;
@@ -182,18 +182,18 @@ static cudaEvent_t timing_begin(mans_workspace* ws, cudaStream_t stream) {
   return pr.second;
 }
 
-static void timing_end(cudaEvent_t stop, cudaStream_t stream) {
+void timing_end(cudaEvent_t stop, cudaStream_t stream) {
   if (stop) cudaEventRecord(stop, stream);
 }
 
-static int pow2_at_least(int v) {
+int pow2_at_least(int v) {
   int p = 1;
   while (p < v) p <<= 1;
   return p;
 }
 
 // Query-group width for a batch: the smallest power of two >= nq, at most 8.
-static int choose_qb(int64_t nq) {
+int choose_qb(int64_t nq) {
   if (nq <= 1) return 1;
   if (nq <= 2) return 2;
   if (nq <= 4) return 4;
@@ -233,13 +233,7 @@ int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace
   if ((rc = ws->slot_keys.reserve(nslots * kp * sizeof(uint64_t))) != MANS_OK) return rc;
   if ((rc = ws->slot_counts.reserve(nslots * sizeof(int32_t))) != MANS_OK) return rc;
   if ((rc = ws->err.reserve(sizeof(int))) != MANS_OK) return rc;
-  float* qn = nullptr;
-  if (metric == MANS_METRIC_COSINE || metric == MANS_METRIC_L2) {
-    if ((rc = ws->qnorms.reserve(nq * sizeof(float))) != MANS_OK) return rc;
-    qn = static_cast<float*>(ws->qnorms.ptr);
-    cudaError_t e = launch_query_norms(d_queries, nq, static_cast<int32_t>(corpus->dim), qn, stream);
-    if (e != cudaSuccess) return fail_cuda(e, "query_norms launch");
-  }
+  float* qn = nullptr;  // query norms are computed inside the scan kernel
   if (!ws->err_cleared) {
     cudaError_t e = cudaMemsetAsync(ws->err.ptr, 0, sizeof(int), stream);
     if (e != cudaSuccess) return fail_cuda(e, "cudaMemsetAsync(err)");
@@ -258,7 +252,7 @@ int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace
   p.qidx = nullptr;
   p.qnorms = qn;
   p.norms = (metric == MANS_METRIC_IP) ? nullptr : corpus->norms;
-  p.ids = nullptr;
+  p.ids = corpus->ids;
   p.id_offset = corpus->id_offset;
   p.dim = static_cast<int32_t>(corpus->dim);
   p.nchunks = nchunks;
@@ -292,6 +286,61 @@ int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace
   e = launch_merge(m, stream);
   if (e != cudaSuccess) return fail_cuda(e, "merge launch");
   return MANS_OK;
+}
+
+int32_t corpus_upload(mans_ctx* ctx, const float* rows, int64_t n, int64_t dim, uint32_t id_offset,
+                      mans_corpus** out) {
+  if (n < 0 || dim <= 0) return fail(MANS_ERR_INVALID, "corpus needs n >= 0 and dim > 0");
+  if (n > 0 && !rows) return fail(MANS_ERR_INVALID, "rows is null");
+  if (n > static_cast<int64_t>(INT32_MAX)) return fail(MANS_ERR_INVALID, "corpus too large");
+  DeviceGuard g(ctx->device);
+  mans_corpus* c = new mans_corpus();
+  c->ctx = ctx;
+  c->n = n;
+  c->dim = dim;
+  c->ld = (dim + 3) / 4 * 4;  // 16-byte row pitch, required by TMA
+  c->id_offset = id_offset;
+  size_t rows_bytes = static_cast<size_t>(std::max<int64_t>(n, 1)) * c->ld * sizeof(float);
+  cudaError_t e = cudaMalloc(&c->rows, rows_bytes);
+  if (e != cudaSuccess) {
+    delete c;
+    return fail_cuda(e, "cudaMalloc(corpus)");
+  }
+  e = cudaMalloc(&c->norms, static_cast<size_t>(std::max<int64_t>(n, 1)) * sizeof(float));
+  if (e != cudaSuccess) {
+    cudaFree(c->rows);
+    delete c;
+    return fail_cuda(e, "cudaMalloc(norms)");
+  }
+  if (n > 0) {
+    if (c->ld != dim) cudaMemset(c->rows, 0, rows_bytes);
+    e = cudaMemcpy2D(c->rows, c->ld * sizeof(float), rows, dim * sizeof(float),
+                     dim * sizeof(float), n, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+      e = launch_row_norms(c->rows, n, static_cast<int32_t>(dim), c->ld, c->norms, 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+      corpus_free(c);
+      return fail_cuda(e, "corpus upload");
+    }
+  }
+  int32_t rc = encode_row_map(&c->map, c->rows, n, dim, c->ld);
+  if (rc != MANS_OK) {
+    corpus_free(c);
+    return rc;
+  }
+  *out = c;
+  return MANS_OK;
+}
+
+void corpus_free(mans_corpus* c) {
+  if (!c) return;
+  if (c->owned) {
+    if (c->rows) cudaFree(c->rows);
+    if (c->norms) cudaFree(c->norms);
+    if (c->ids) cudaFree(c->ids);
+  }
+  delete c;
 }
 
 // Reads and clears the device error word of `ws` after its stream finished.
@@ -364,50 +413,7 @@ int32_t mans_corpus_create(mans_ctx* ctx, const float* rows, int64_t n, int64_t 
                            uint32_t id_offset, mans_corpus** out_corpus) {
   if (!ctx || !out_corpus) return fail(MANS_ERR_INVALID, "null context or output");
   *out_corpus = nullptr;
-  if (n < 0 || dim <= 0) return fail(MANS_ERR_INVALID, "corpus needs n >= 0 and dim > 0");
-  if (n > 0 && !rows) return fail(MANS_ERR_INVALID, "rows is null");
-  if (n > static_cast<int64_t>(INT32_MAX)) return fail(MANS_ERR_INVALID, "corpus too large");
-  DeviceGuard g(ctx->device);
-  mans_corpus* c = new mans_corpus();
-  c->ctx = ctx;
-  c->n = n;
-  c->dim = dim;
-  c->ld = (dim + 3) / 4 * 4;  // 16-byte row pitch, required by TMA
-  c->id_offset = id_offset;
-  size_t rows_bytes = static_cast<size_t>(std::max<int64_t>(n, 1)) * c->ld * sizeof(float);
-  cudaError_t e = cudaMalloc(&c->rows, rows_bytes);
-  if (e != cudaSuccess) {
-    delete c;
-    return fail_cuda(e, "cudaMalloc(corpus)");
-  }
-  e = cudaMalloc(&c->norms, static_cast<size_t>(std::max<int64_t>(n, 1)) * sizeof(float));
-  if (e != cudaSuccess) {
-    cudaFree(c->rows);
-    delete c;
-    return fail_cuda(e, "cudaMalloc(norms)");
-  }
-  if (n > 0) {
-    if (c->ld != dim) cudaMemset(c->rows, 0, rows_bytes);
-    e = cudaMemcpy2D(c->rows, c->ld * sizeof(float), rows, dim * sizeof(float),
-                     dim * sizeof(float), n, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = launch_row_norms(c->rows, n, static_cast<int32_t>(dim), c->ld, c->norms, 0);
-    if (e == cudaSuccess) e = cudaDeviceSynchronize();
-    if (e != cudaSuccess) {
-      cudaFree(c->rows);
-      cudaFree(c->norms);
-      delete c;
-      return fail_cuda(e, "corpus upload");
-    }
-  }
-  int32_t rc = encode_row_map(&c->map, c->rows, n, dim, c->ld);
-  if (rc != MANS_OK) {
-    cudaFree(c->rows);
-    cudaFree(c->norms);
-    delete c;
-    return rc;
-  }
-  *out_corpus = c;
-  return MANS_OK;
+  return corpus_upload(ctx, rows, n, dim, id_offset, out_corpus);
 }
 
 int32_t mans_corpus_update_rows(mans_corpus* c, int64_t start, const float* rows, int64_t count) {
@@ -431,9 +437,7 @@ int32_t mans_corpus_destroy(mans_corpus* c) {
   if (!c) return MANS_OK;
   DeviceGuard g(c->ctx->device);
   cudaDeviceSynchronize();
-  cudaFree(c->rows);
-  cudaFree(c->norms);
-  delete c;
+  corpus_free(c);
   return MANS_OK;
 }
 

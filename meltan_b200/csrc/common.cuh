@@ -187,12 +187,16 @@ __device__ __forceinline__ void topk_merge(TopKState s, int k, int kp, int sortn
                                            int bar_id) {
   int qc = *s.qcount;
   int nb = *s.nbest;
-  for (int i = tid; i < sortn; i += NT) {
+  // sort only the occupied prefix, rounded up to a power of two
+  int n = kp;
+  while (n < kp + qc) n <<= 1;
+  if (n > sortn) n = sortn;
+  for (int i = tid; i < n; i += NT) {
     bool keep = (i < nb) || (i >= kp && i < kp + qc);
     if (!keep) s.buf[i] = kKeyMax;
   }
   named_sync(bar_id, NT);
-  bitonic_sort_keys<NT>(s.buf, sortn, tid, bar_id);
+  bitonic_sort_keys<NT>(s.buf, n, tid, bar_id);
   if (tid == 0) {
     int total = nb + qc;
     int keep = total < k ? total : k;

@@ -57,6 +57,8 @@ struct mans_corpus {
   uint32_t id_offset = 0;
   float* rows = nullptr;
   float* norms = nullptr;
+  uint32_t* ids = nullptr;  // optional row -> reported id (packed IVF lists)
+  bool owned = true;        // rows/norms/ids freed with the object
   CUtensorMap map;
 };
 
@@ -88,6 +90,14 @@ mans_workspace* acquire_workspace(mans_ctx* ctx);
 void release_workspace(mans_ctx* ctx, mans_workspace* ws);
 void destroy_workspace(mans_workspace* ws);
 int32_t check_device_error(mans_workspace* ws, cudaStream_t stream);
+int pow2_at_least(int v);
+int choose_qb(int64_t nq);
+cudaEvent_t timing_begin(mans_workspace* ws, cudaStream_t stream);
+void timing_end(cudaEvent_t stop, cudaStream_t stream);
+// Uploads rows (host, n x dim) into a new corpus object (norms on the device).
+int32_t corpus_upload(mans_ctx* ctx, const float* rows, int64_t n, int64_t dim, uint32_t id_offset,
+                      mans_corpus** out);
+void corpus_free(mans_corpus* c);
 int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace* ws,
                         const float* d_queries, int64_t nq, int32_t k, int32_t metric,
                         float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,

@@ -1,0 +1,524 @@
+// ivf.cu -- IVF-flat probe-and-scan on the device.
+//
+// Restates IVFFlatSearch.scanProbedLists (Sources/MetalANNSCore/
+// IVFFlatSearch.swift:214-291) for a batch of queries:
+//   1. centroid keys with the host-tier metric (same formula as the flat scan)
+//      and the nprobe smallest, ties to the lower list index
+//      (smallestIndices, :314-382) -- the flat scan kernel over the centroid
+//      matrix with k = nprobe;
+//   2. a one-block planner groups the (query, probed list) pairs by list, so
+//      every probed list is streamed once for all queries that probe it, and
+//      cuts lists into row chunks (work units for the persistent scan);
+//   3. the flat scan kernel over the packed list rows (the Partition layout,
+//      :39-95: packed[p] = corpus[listIDs[p]]) reporting listIDs[p] as ids;
+//   4. the slot merge per query.  The strict (distance, id) order of TopKHeap
+//      (:384-444) makes the result independent of the visiting order.
+// The planner runs on the device, so a search needs no host round trip.
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+#include "kernels.h"
+#include "mans_cuda.h"
+
+using namespace mans;
+
+struct mans_ivf {
+  mans_ctx* ctx = nullptr;
+  int32_t nlist = 0;
+  int64_t n = 0;
+  int64_t dim = 0;
+  int64_t max_len = 0;
+  mans_corpus* cent = nullptr;    // centroids (ids = list index)
+  mans_corpus* packed = nullptr;  // list-contiguous rows, ids = listIDs
+  int64_t* offsets = nullptr;     // device, nlist + 1
+  std::vector<int64_t> h_offsets;
+};
+
+namespace mans {
+namespace {
+
+constexpr int kPlanThreads = 1024;
+constexpr int kChunkRows = 512;  // rows per scan work unit (two TMA boxes)
+
+struct PlanParams {
+  const uint32_t* probe_ids;
+  const int32_t* probe_counts;
+  int32_t pk;
+  int32_t nq;
+  int32_t nlist;
+  const int64_t* offsets;
+  int32_t qb;
+  int32_t chunk;
+  int32_t* list_cnt;   // [nlist]
+  int32_t* list_tmp;   // [nlist]
+  int32_t* list_qoff;  // [nlist + 1]
+  int32_t* list_soff;  // [nlist + 1]
+  int32_t* qidx;       // [nq * pk]
+  ScanSegment* segs;   // [max_segs]
+  int32_t* nseg;       // [1]
+  int32_t* q_cnt;      // [nq]
+  int32_t* q_soff;     // [nq + 1]
+  int32_t* q_slots;    // [max_refs]
+  int32_t max_segs;
+  int32_t max_refs;
+  int* err;
+};
+
+__device__ __forceinline__ int list_chunks(const int64_t* off, int l, int chunk) {
+  int64_t len = off[l + 1] - off[l];
+  return static_cast<int>((len + chunk - 1) / chunk);
+}
+
+// Exclusive prefix sum of in[0, n) into out[0, n] by the whole block.
+__device__ void block_exclusive_scan(const int32_t* in, int n, int32_t* out, int32_t* part) {
+  const int t = threadIdx.x, nt = blockDim.x;
+  const int per = (n + nt - 1) / nt;
+  const int b = t * per;
+  const int e = min(n, b + per);
+  int32_t sum = 0;
+  for (int i = b; i < e; ++i) sum += in[i];
+  // warp-level inclusive scan of the per-thread sums, then across warps
+  const int lane = t & 31, w = t >> 5;
+  int32_t v = sum;
+  for (int o = 1; o < 32; o <<= 1) {
+    int32_t u = __shfl_up_sync(0xFFFFFFFFu, v, o);
+    if (lane >= o) v += u;
+  }
+  if (lane == 31) part[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    int32_t x = lane < (nt >> 5) ? part[lane] : 0;
+    for (int o = 1; o < 32; o <<= 1) {
+      int32_t u = __shfl_up_sync(0xFFFFFFFFu, x, o);
+      if (lane >= o) x += u;
+    }
+    part[32 + lane] = x;  // inclusive warp totals
+  }
+  __syncthreads();
+  int32_t acc = v - sum + (w > 0 ? part[32 + w - 1] : 0);
+  for (int i = b; i < e; ++i) {
+    out[i] = acc;
+    acc += in[i];
+  }
+  if (t == nt - 1) out[n] = acc;
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kPlanThreads) ivf_plan_kernel(const PlanParams p) {
+  __shared__ int32_t part[64];
+  const int t = threadIdx.x, nt = blockDim.x;
+  const int64_t pairs = static_cast<int64_t>(p.nq) * p.pk;
+  for (int i = t; i < p.nlist; i += nt) p.list_cnt[i] = 0;
+  for (int i = t; i < p.nq; i += nt) p.q_cnt[i] = 0;
+  __syncthreads();
+  for (int64_t i = t; i < pairs; i += nt) {
+    int q = static_cast<int>(i / p.pk), j = static_cast<int>(i - static_cast<int64_t>(q) * p.pk);
+    if (j < p.probe_counts[q]) {
+      int l = static_cast<int>(p.probe_ids[i]);
+      atomicAdd(&p.list_cnt[l], 1);
+      atomicAdd(&p.q_cnt[q], list_chunks(p.offsets, l, p.chunk));
+    }
+  }
+  __syncthreads();
+  block_exclusive_scan(p.list_cnt, p.nlist, p.list_qoff, part);
+  for (int l = t; l < p.nlist; l += nt) {
+    int c = p.list_cnt[l];
+    p.list_tmp[l] = c > 0 ? ((c + p.qb - 1) / p.qb) * list_chunks(p.offsets, l, p.chunk) : 0;
+  }
+  __syncthreads();
+  block_exclusive_scan(p.list_tmp, p.nlist, p.list_soff, part);
+  block_exclusive_scan(p.q_cnt, p.nq, p.q_soff, part);
+  for (int i = t; i < p.nlist; i += nt) p.list_cnt[i] = 0;
+  for (int i = t; i < p.nq; i += nt) p.q_cnt[i] = 0;
+  __syncthreads();
+  for (int64_t i = t; i < pairs; i += nt) {
+    int q = static_cast<int>(i / p.pk), j = static_cast<int>(i - static_cast<int64_t>(q) * p.pk);
+    if (j < p.probe_counts[q]) {
+      int l = static_cast<int>(p.probe_ids[i]);
+      int pos = atomicAdd(&p.list_cnt[l], 1);
+      p.qidx[p.list_qoff[l] + pos] = q;
+    }
+  }
+  const int total = p.list_soff[p.nlist];
+  const int nseg = min(total, p.max_segs);
+  if (t == 0) {
+    *p.nseg = nseg;
+    if (total > p.max_segs || p.q_soff[p.nq] > p.max_refs) atomicExch(p.err, kErrBadArg);
+  }
+  for (int l = t; l < p.nlist; l += nt) {
+    int cnt = p.list_qoff[l + 1] - p.list_qoff[l];
+    if (cnt == 0) continue;
+    int ch = list_chunks(p.offsets, l, p.chunk);
+    int groups = (cnt + p.qb - 1) / p.qb;
+    int64_t base = p.offsets[l];
+    int64_t len = p.offsets[l + 1] - base;
+    for (int g = 0; g < groups; ++g)
+      for (int c = 0; c < ch; ++c) {
+        int s = p.list_soff[l] + g * ch + c;
+        if (s >= nseg) continue;
+        ScanSegment sg;
+        sg.row_begin = base + static_cast<int64_t>(c) * p.chunk;
+        int64_t rem = len - static_cast<int64_t>(c) * p.chunk;
+        sg.row_count = static_cast<int32_t>(rem < p.chunk ? rem : p.chunk);
+        sg.qbase = p.list_qoff[l] + g * p.qb;
+        sg.qcount = min(p.qb, cnt - g * p.qb);
+        sg.slot_base = s * p.qb;
+        sg.slot_stride = 1;
+        sg.reserved = 0;
+        p.segs[s] = sg;
+      }
+  }
+  __syncthreads();
+  for (int s = t; s < nseg; s += nt) {
+    ScanSegment sg = p.segs[s];
+    for (int j = 0; j < sg.qcount; ++j) {
+      int q = p.qidx[sg.qbase + j];
+      int pos = atomicAdd(&p.q_cnt[q], 1);
+      int at = p.q_soff[q] + pos;
+      if (at < p.max_refs) p.q_slots[at] = s * p.qb + j;
+    }
+  }
+}
+
+// Squared query norms in index order, one warp per query: lanes load 32
+// consecutive elements, lane order is replayed through shuffles so every lane
+// accumulates the same sequential sum.
+__global__ void query_norms_warp_kernel(const float* __restrict__ q, int64_t nq, int32_t dim,
+                                        float* __restrict__ out) {
+  int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  int lane = threadIdx.x & 31;
+  if (w >= nq) return;
+  const float* v = q + w * dim;
+  float acc = 0.0f;
+  for (int c0 = 0; c0 < dim; c0 += 32) {
+    float x = c0 + lane < dim ? v[c0 + lane] : 0.0f;
+    int cnt = dim - c0 < 32 ? dim - c0 : 32;
+    for (int l = 0; l < cnt; ++l) {
+      float y = __shfl_sync(0xFFFFFFFFu, x, l);
+      acc = __fadd_rn(acc, __fmul_rn(y, y));
+    }
+  }
+  if (lane == 0) out[w] = acc;
+}
+
+}  // namespace
+
+// Byte layout of the per-call scratch carved from one device buffer.
+struct IvfScratch {
+  size_t off[16];
+  size_t total;
+};
+
+static size_t carve(size_t& o, size_t bytes) {
+  size_t at = (o + 255) / 256 * 256;
+  o = at + bytes;
+  return at;
+}
+
+static int32_t run_ivf_search(mans_ctx* ctx, mans_ivf* ivf, mans_workspace* ws,
+                              const float* d_queries, int64_t nq, int32_t k, int32_t nprobe,
+                              int32_t metric, float* d_out_dist, uint32_t* d_out_ids,
+                              int32_t* d_out_counts, cudaStream_t stream) {
+  const int32_t kout = std::min<int32_t>(k, MANS_MAX_TOPK);
+  if (nq <= 0) return MANS_OK;
+  if (k <= 0 || ivf->n <= 0) {
+    if (kout <= 0) {
+      cudaError_t e = cudaMemsetAsync(d_out_counts, 0, sizeof(int32_t) * nq, stream);
+      return e == cudaSuccess ? MANS_OK : fail_cuda(e, "cudaMemsetAsync");
+    }
+    cudaError_t e = launch_fill_empty(d_out_dist, d_out_ids, d_out_counts, nq, kout, stream);
+    return e == cudaSuccess ? MANS_OK : fail_cuda(e, "fill_empty launch");
+  }
+  const int32_t probe = std::max(1, std::min(nprobe, ivf->nlist));
+  if (probe >= ivf->nlist) {
+    // every list is probed: an exact scan of the packed rows (IVFFlatSearch
+    // .swift:161-165 hands this case to the exact host scan)
+    return run_flat_search(ctx, ivf->packed, ws, d_queries, nq, k, metric, d_out_dist, d_out_ids,
+                           d_out_counts, stream);
+  }
+  if (probe > MANS_MAX_TOPK)
+    return fail(MANS_ERR_SEARCH, "nprobe above 256 (and below nlist) is not supported on the GPU");
+  if (nq > INT32_MAX / std::max(probe, 1)) return fail(MANS_ERR_SEARCH, "query batch too large");
+
+  const int32_t keff = static_cast<int32_t>(std::min<int64_t>(kout, ivf->n));
+  const int32_t kp = pow2_at_least(keff);
+  const int64_t pairs = nq * probe;
+  const int qb = choose_qb((pairs + ivf->nlist - 1) / ivf->nlist);
+  const int64_t max_chunks = std::max<int64_t>(1, (ivf->max_len + kChunkRows - 1) / kChunkRows);
+  const int64_t max_refs = pairs * max_chunks;
+  const int64_t max_segs = max_refs;
+  if (max_refs * qb > INT32_MAX / 2) return fail(MANS_ERR_SEARCH, "query batch too large");
+  const int nchunks = static_cast<int>((ivf->dim + kTileCols - 1) / kTileCols);
+  const int stages = scan_max_stages(qb, nchunks);
+  if (stages < 2) return fail(MANS_ERR_SEARCH, "dimension too large for the scan kernel");
+
+  // scratch: centroid top-k + planner arrays + slots
+  size_t o = 0;
+  const size_t o_pd = carve(o, pairs * sizeof(float));
+  const size_t o_pi = carve(o, pairs * sizeof(uint32_t));
+  const size_t o_pc = carve(o, nq * sizeof(int32_t));
+  const size_t o_qn = carve(o, nq * sizeof(float));
+  const size_t o_lc = carve(o, ivf->nlist * sizeof(int32_t));
+  const size_t o_lt = carve(o, ivf->nlist * sizeof(int32_t));
+  const size_t o_lq = carve(o, (ivf->nlist + 1) * sizeof(int32_t));
+  const size_t o_ls = carve(o, (ivf->nlist + 1) * sizeof(int32_t));
+  const size_t o_qi = carve(o, pairs * sizeof(int32_t));
+  const size_t o_sg = carve(o, max_segs * sizeof(ScanSegment));
+  const size_t o_ns = carve(o, sizeof(int32_t));
+  const size_t o_qc = carve(o, nq * sizeof(int32_t));
+  const size_t o_qs = carve(o, (nq + 1) * sizeof(int32_t));
+  const size_t o_qr = carve(o, max_refs * sizeof(int32_t));
+  int32_t rc;
+  if ((rc = ws->aux.reserve(o)) != MANS_OK) return rc;
+  // slot buffers sized for both the centroid search and the list scan, so
+  // nothing is reallocated between launches
+  const int64_t cent_tiles = (ivf->nlist + kTileRows - 1) / kTileRows;
+  const size_t cent_slots = static_cast<size_t>((nq + 7) / 8 * 8) * std::min<int64_t>(ctx->num_sms, cent_tiles);
+  const size_t list_slots = static_cast<size_t>(max_segs) * qb;
+  const int kp_cent = pow2_at_least(probe);
+  const size_t need_keys = std::max(cent_slots * kp_cent, list_slots * kp) * sizeof(uint64_t);
+  const size_t need_cnts = std::max(cent_slots, list_slots) * sizeof(int32_t);
+  if ((rc = ws->slot_keys.reserve(need_keys)) != MANS_OK) return rc;
+  if ((rc = ws->slot_counts.reserve(need_cnts)) != MANS_OK) return rc;
+  if ((rc = ws->err.reserve(sizeof(int))) != MANS_OK) return rc;
+  if (!ws->err_cleared) {
+    cudaError_t e = cudaMemsetAsync(ws->err.ptr, 0, sizeof(int), stream);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaMemsetAsync(err)");
+    ws->err_cleared = true;
+  }
+  uint8_t* A = static_cast<uint8_t*>(ws->aux.ptr);
+  float* probe_d = reinterpret_cast<float*>(A + o_pd);
+  uint32_t* probe_i = reinterpret_cast<uint32_t*>(A + o_pi);
+  int32_t* probe_c = reinterpret_cast<int32_t*>(A + o_pc);
+  float* qn = reinterpret_cast<float*>(A + o_qn);
+
+  // 1. centroid keys + nprobe smallest (ties -> lower list index)
+  rc = run_flat_search(ctx, ivf->cent, ws, d_queries, nq, probe, metric, probe_d, probe_i, probe_c,
+                       stream);
+  if (rc != MANS_OK) return rc;
+
+  // 2. plan
+  PlanParams pp{};
+  pp.probe_ids = probe_i;
+  pp.probe_counts = probe_c;
+  pp.pk = probe;
+  pp.nq = static_cast<int32_t>(nq);
+  pp.nlist = ivf->nlist;
+  pp.offsets = ivf->offsets;
+  pp.qb = qb;
+  pp.chunk = kChunkRows;
+  pp.list_cnt = reinterpret_cast<int32_t*>(A + o_lc);
+  pp.list_tmp = reinterpret_cast<int32_t*>(A + o_lt);
+  pp.list_qoff = reinterpret_cast<int32_t*>(A + o_lq);
+  pp.list_soff = reinterpret_cast<int32_t*>(A + o_ls);
+  pp.qidx = reinterpret_cast<int32_t*>(A + o_qi);
+  pp.segs = reinterpret_cast<ScanSegment*>(A + o_sg);
+  pp.nseg = reinterpret_cast<int32_t*>(A + o_ns);
+  pp.q_cnt = reinterpret_cast<int32_t*>(A + o_qc);
+  pp.q_soff = reinterpret_cast<int32_t*>(A + o_qs);
+  pp.q_slots = reinterpret_cast<int32_t*>(A + o_qr);
+  pp.max_segs = static_cast<int32_t>(max_segs);
+  pp.max_refs = static_cast<int32_t>(max_refs);
+  pp.err = static_cast<int*>(ws->err.ptr);
+  if (metric != MANS_METRIC_IP) {
+    const int64_t threads = nq * 32;
+    query_norms_warp_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
+        d_queries, nq, static_cast<int32_t>(ivf->dim), qn);
+  }
+  ivf_plan_kernel<<<1, kPlanThreads, 0, stream>>>(pp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail_cuda(e, "ivf plan launch");
+
+  // 3. scan the probed lists
+  ScanParams p{};
+  p.segs = pp.segs;
+  p.nseg = static_cast<int32_t>(max_segs);
+  p.nseg_dev = pp.nseg;
+  p.stages = stages;
+  p.n = ivf->n;
+  p.nq = nq;
+  p.queries = d_queries;
+  p.qidx = pp.qidx;
+  p.qnorms = metric != MANS_METRIC_IP ? qn : nullptr;
+  p.norms = metric != MANS_METRIC_IP ? ivf->packed->norms : nullptr;
+  p.ids = ivf->packed->ids;
+  p.id_offset = 0;
+  p.dim = static_cast<int32_t>(ivf->dim);
+  p.nchunks = nchunks;
+  p.metric = metric;
+  p.k = keff;
+  p.kp = kp;
+  p.slot_keys = static_cast<uint64_t*>(ws->slot_keys.ptr);
+  p.slot_counts = static_cast<int32_t*>(ws->slot_counts.ptr);
+  p.err = pp.err;
+  cudaEvent_t stop = timing_begin(ws, stream);
+  e = launch_scan(qb, ivf->packed->map, p, ctx->num_sms, stream);
+  if (e != cudaSuccess) return fail_cuda(e, "ivf scan launch");
+  timing_end(stop, stream);
+
+  // 4. merge per query
+  MergeParams m{};
+  m.in_keys = p.slot_keys;
+  m.in_counts = p.slot_counts;
+  m.q_slot_offsets = pp.q_soff;
+  m.q_slot_list = pp.q_slots;
+  m.kp_in = kp;
+  m.nq = nq;
+  m.k = keff;
+  m.kp = kp;
+  m.kout = kout;
+  m.out_dist = d_out_dist;
+  m.out_ids = d_out_ids;
+  m.out_counts = d_out_counts;
+  m.err = p.err;
+  e = launch_merge(m, stream);
+  if (e != cudaSuccess) return fail_cuda(e, "ivf merge launch");
+  ws->launches += (metric != MANS_METRIC_IP ? 1 : 0) + 3;
+  return MANS_OK;
+}
+
+}  // namespace mans
+
+extern "C" {
+
+int32_t mans_ivf_create(mans_ctx* ctx, const float* centroids, int32_t nlist, int64_t dim,
+                        const float* packed_rows, const uint32_t* list_ids,
+                        const int64_t* list_offsets, int64_t n, mans_ivf** out_ivf) {
+  if (!ctx || !out_ivf) return fail(MANS_ERR_INVALID, "null context or output");
+  *out_ivf = nullptr;
+  if (nlist <= 0 || dim <= 0 || n < 0) return fail(MANS_ERR_INVALID, "bad IVF shape");
+  if (!centroids || !list_offsets || (n > 0 && (!packed_rows || !list_ids)))
+    return fail(MANS_ERR_INVALID, "null IVF buffer");
+  if (list_offsets[0] != 0 || list_offsets[nlist] != n)
+    return fail(MANS_ERR_INVALID, "list offsets must run from 0 to n");
+  int64_t max_len = 0;
+  for (int32_t l = 0; l < nlist; ++l) {
+    int64_t len = list_offsets[l + 1] - list_offsets[l];
+    if (len < 0) return fail(MANS_ERR_INVALID, "list offsets must be non-decreasing");
+    max_len = std::max(max_len, len);
+  }
+  DeviceGuard g(ctx->device);
+  mans_ivf* ivf = new mans_ivf();
+  ivf->ctx = ctx;
+  ivf->nlist = nlist;
+  ivf->n = n;
+  ivf->dim = dim;
+  ivf->max_len = max_len;
+  ivf->h_offsets.assign(list_offsets, list_offsets + nlist + 1);
+  int32_t rc = corpus_upload(ctx, centroids, nlist, dim, 0, &ivf->cent);
+  if (rc == MANS_OK) rc = corpus_upload(ctx, packed_rows, n, dim, 0, &ivf->packed);
+  if (rc == MANS_OK) {
+    cudaError_t e = cudaMalloc(&ivf->packed->ids, std::max<int64_t>(n, 1) * sizeof(uint32_t));
+    if (e == cudaSuccess && n > 0)
+      e = cudaMemcpy(ivf->packed->ids, list_ids, n * sizeof(uint32_t), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMalloc(&ivf->offsets, (nlist + 1) * sizeof(int64_t));
+    if (e == cudaSuccess)
+      e = cudaMemcpy(ivf->offsets, list_offsets, (nlist + 1) * sizeof(int64_t),
+                     cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) rc = fail_cuda(e, "IVF upload");
+  }
+  if (rc != MANS_OK) {
+    corpus_free(ivf->cent);
+    corpus_free(ivf->packed);
+    if (ivf->offsets) cudaFree(ivf->offsets);
+    delete ivf;
+    return rc;
+  }
+  *out_ivf = ivf;
+  return MANS_OK;
+}
+
+int32_t mans_ivf_destroy(mans_ivf* ivf) {
+  if (!ivf) return MANS_OK;
+  DeviceGuard g(ivf->ctx->device);
+  cudaDeviceSynchronize();
+  corpus_free(ivf->cent);
+  corpus_free(ivf->packed);
+  if (ivf->offsets) cudaFree(ivf->offsets);
+  delete ivf;
+  return MANS_OK;
+}
+
+static int32_t validate_ivf(const mans_ctx* ctx, const mans_ivf* ivf, int64_t nq, int32_t metric) {
+  if (!ctx || !ivf) return fail(MANS_ERR_INVALID, "null context or IVF index");
+  if (ivf->ctx != ctx) return fail(MANS_ERR_INVALID, "IVF index belongs to another context");
+  if (nq < 0) return fail(MANS_ERR_INVALID, "negative query count");
+  if (metric == MANS_METRIC_HAMMING)
+    return fail(MANS_ERR_SEARCH, "IVF-flat does not support metric .hamming");
+  if (metric < 0 || metric > MANS_METRIC_HAMMING) return fail(MANS_ERR_INVALID, "unknown metric");
+  return MANS_OK;
+}
+
+int32_t mans_ivf_search(mans_ctx* ctx, mans_ivf* ivf, const float* queries, int64_t nq,
+                        int64_t dim, int32_t k, int32_t nprobe, int32_t metric, float* out_dist,
+                        uint32_t* out_ids, int32_t* out_counts) {
+  int32_t rc = validate_ivf(ctx, ivf, nq, metric);
+  if (rc != MANS_OK) return rc;
+  if (nq == 0) return MANS_OK;
+  const int32_t kout = std::max<int32_t>(0, std::min<int32_t>(k, MANS_MAX_TOPK));
+  if (k <= 0 || ivf->n <= 0) {
+    for (int64_t i = 0; i < nq * kout; ++i) {
+      out_dist[i] = __builtin_inff();
+      out_ids[i] = MANS_EMPTY_ID;
+    }
+    for (int64_t i = 0; i < nq; ++i) out_counts[i] = 0;
+    return MANS_OK;
+  }
+  if (dim != ivf->dim) return fail(MANS_ERR_DIM, "dimensionMismatch");
+  if (!queries || !out_dist || !out_ids || !out_counts) return fail(MANS_ERR_INVALID, "null buffer");
+  DeviceGuard g(ctx->device);
+  mans_workspace* ws = acquire_workspace(ctx);
+  if (!ws) return fail(MANS_ERR_OOM, "cannot create a workspace stream");
+  cudaStream_t st = ws->stream;
+  do {
+    if ((rc = ws->queries.reserve(nq * dim * sizeof(float))) != MANS_OK) break;
+    if ((rc = ws->out_dist.reserve(nq * kout * sizeof(float))) != MANS_OK) break;
+    if ((rc = ws->out_ids.reserve(nq * kout * sizeof(uint32_t))) != MANS_OK) break;
+    if ((rc = ws->out_counts.reserve(nq * sizeof(int32_t))) != MANS_OK) break;
+    cudaError_t e = cudaMemcpyAsync(ws->queries.ptr, queries, nq * dim * sizeof(float),
+                                    cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) {
+      rc = fail_cuda(e, "query upload");
+      break;
+    }
+    rc = run_ivf_search(ctx, ivf, ws, static_cast<const float*>(ws->queries.ptr), nq, k, nprobe,
+                        metric, static_cast<float*>(ws->out_dist.ptr),
+                        static_cast<uint32_t*>(ws->out_ids.ptr),
+                        static_cast<int32_t*>(ws->out_counts.ptr), st);
+    if (rc != MANS_OK) break;
+    e = cudaMemcpyAsync(out_dist, ws->out_dist.ptr, nq * kout * sizeof(float),
+                        cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(out_ids, ws->out_ids.ptr, nq * kout * sizeof(uint32_t),
+                          cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(out_counts, ws->out_counts.ptr, nq * sizeof(int32_t),
+                          cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) {
+      rc = fail_cuda(e, "result download");
+      break;
+    }
+    rc = check_device_error(ws, st);
+  } while (false);
+  release_workspace(ctx, ws);
+  return rc;
+}
+
+int32_t mans_ivf_search_device(mans_ctx* ctx, mans_ivf* ivf, mans_workspace* ws,
+                               const float* d_queries, int64_t nq, int32_t k, int32_t nprobe,
+                               int32_t metric, float* d_out_dist, uint32_t* d_out_ids,
+                               int32_t* d_out_counts, void* cuda_stream) {
+  int32_t rc = validate_ivf(ctx, ivf, nq, metric);
+  if (rc != MANS_OK) return rc;
+  if (!ws || ws->ctx != ctx) return fail(MANS_ERR_INVALID, "workspace missing or foreign");
+  DeviceGuard g(ctx->device);
+  return run_ivf_search(ctx, ivf, ws, d_queries, nq, k, nprobe, metric, d_out_dist, d_out_ids,
+                        d_out_counts, static_cast<cudaStream_t>(cuda_stream));
+}
+
+int64_t mans_ivf_list_count(const mans_ivf* ivf) { return ivf ? ivf->nlist : 0; }
+
+}  // extern "C"

@@ -38,6 +38,7 @@ struct ScanSegment {
 struct ScanParams {
   const ScanSegment* segs;  // null: flat mode, segments derived arithmetically
   int32_t nseg;
+  const int32_t* nseg_dev;  // when set, the segment count is read on the device
   int32_t stages;
   // flat mode: nseg = groups * flat_splits; group g holds queries
   // [g*QB, min(nq, g*QB+QB)), split s holds tiles [s*T/S, (s+1)*T/S).
@@ -47,7 +48,7 @@ struct ScanParams {
   int64_t nq;
   const float* queries;  // nq x dim, row-major
   const int32_t* qidx;
-  const float* qnorms;   // squared query norms (cosine / L2), else null
+  const float* qnorms;   // squared query norms; null: computed in the kernel when needed
   const float* norms;    // squared row norms (cosine / L2), else null
   const uint32_t* ids;   // row -> reported id (null: row + id_offset)
   uint32_t id_offset;
@@ -83,6 +84,7 @@ struct MergeParams {
   const uint32_t* in_ids;
   const int32_t* in_counts;
   const int32_t* q_slot_offsets;
+  const int32_t* q_slot_list;  // with offsets: query q reads slots list[offs[q]..offs[q+1])
   int32_t slots_per_query;
   int32_t n_lists;
   int32_t kp_in;

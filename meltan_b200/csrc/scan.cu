@@ -125,6 +125,7 @@ __global__ void __launch_bounds__(kScanThreads, 1)
   __syncthreads();
 
   const int qw = p.nchunks * kTileCols;
+  const int nseg = p.nseg_dev ? *p.nseg_dev : p.nseg;
 
   if (warp == kConsumerWarps) {
     // ---------------- TMA producer ----------------
@@ -132,7 +133,7 @@ __global__ void __launch_bounds__(kScanThreads, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int s = blockIdx.x; s < p.nseg; s += gridDim.x) {
+      for (int s = blockIdx.x; s < nseg; s += gridDim.x) {
         ScanSegment seg;
         flat_segment(p, s, QB, seg);
         int ntiles = (seg.row_count + kTileRows - 1) / kTileRows;
@@ -177,7 +178,7 @@ __global__ void __launch_bounds__(kScanThreads, 1)
   uint32_t phase = 0;
   int consumed = 0;
   bool aborted = false;
-  for (int s = blockIdx.x; s < p.nseg && !aborted; s += gridDim.x) {
+  for (int s = blockIdx.x; s < nseg && !aborted; s += gridDim.x) {
     ScanSegment seg;
     flat_segment(p, s, QB, seg);
     for (int i = tid; i < QB * qw; i += kConsumers) {
@@ -200,6 +201,15 @@ __global__ void __launch_bounds__(kScanThreads, 1)
       sm.qcnt[tid] = 0;
       sm.nbest[tid] = 0;
       sm.thr[tid] = kKeyMax;
+    }
+    named_sync(1, kConsumers);
+    if (!p.qnorms && p.metric != kIP && tid < seg.qcount) {
+      // squared query norm in index order (FlatGPUSearch.swift:532-535), read
+      // from the staged copy while the TMA ring fills
+      const float* qv = sm.q + tid * qw;
+      float acc = 0.0f;
+      for (int c = 0; c < p.dim; ++c) acc = __fadd_rn(acc, __fmul_rn(qv[c], qv[c]));
+      sm.qn[tid] = acc;
     }
     named_sync(1, kConsumers);
 
@@ -362,6 +372,29 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const MergeParams 
   } else {
     nslots = p.n_lists;
   }
+  // Every slot is sorted, so the k-th smallest slot head bounds the global
+  // k-th key from above (k slots each hold a key <= it): start from there.
+  if (nslots >= p.k && nslots <= kSortN) {
+    int ns = 1;
+    while (ns < nslots) ns <<= 1;
+    for (int i = tid; i < ns; i += kMergeThreads) {
+      uint64_t h = kKeyMax;
+      if (i < nslots) {
+        if (p.in_keys) {
+          int64_t slot = p.q_slot_list ? p.q_slot_list[slot0 + i] : slot0 + i;
+          if (p.in_counts[slot] > 0) h = p.in_keys[slot * p.kp_in];
+        } else {
+          int64_t blk = static_cast<int64_t>(i) * p.nq + q;
+          if (p.in_counts[blk] > 0) h = make_key(p.in_dist[blk * p.kp_in], p.in_ids[blk * p.kp_in]);
+        }
+      }
+      buf[i] = h;
+    }
+    __syncthreads();
+    bitonic_sort_keys<kMergeThreads>(buf, ns, tid, 0);
+    if (tid == 0 && buf[p.k - 1] != kKeyMax) thr = buf[p.k - 1] + 1;
+    __syncthreads();
+  }
   const int64_t total = nslots * p.kp_in;
   for (int64_t b = 0; b < total; b += kMergeThreads) {
     int64_t pos = b + tid;
@@ -371,7 +404,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const MergeParams 
       int64_t sl = pos / p.kp_in;
       int i = static_cast<int>(pos - sl * p.kp_in);
       if (p.in_keys) {
-        int64_t slot = slot0 + sl;
+        int64_t slot = p.q_slot_list ? p.q_slot_list[slot0 + sl] : slot0 + sl;
         if (i < p.in_counts[slot]) {
           key = p.in_keys[slot * p.kp_in + i];
           valid = true;
