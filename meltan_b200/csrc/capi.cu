@@ -203,8 +203,8 @@ int choose_qb(int64_t nq) {
 int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace* ws,
                         const float* d_queries, int64_t nq, int32_t k, int32_t metric,
                         float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
-                        cudaStream_t stream) {
-  const int32_t kout = std::min<int32_t>(k, MANS_MAX_TOPK);
+                        cudaStream_t stream, int mode, int32_t kcap) {
+  const int32_t kout = std::min<int32_t>(k, kcap);
   const int64_t n = corpus->n;
   if (nq <= 0) return MANS_OK;
   if (k <= 0 || n <= 0) {
@@ -257,6 +257,7 @@ int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace
   p.dim = static_cast<int32_t>(corpus->dim);
   p.nchunks = nchunks;
   p.metric = metric;
+  p.mode = mode;
   p.k = keff;
   p.kp = kp;
   p.slot_keys = static_cast<uint64_t*>(ws->slot_keys.ptr);

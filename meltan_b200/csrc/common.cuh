@@ -146,6 +146,16 @@ __device__ __forceinline__ float finalize_distance(int metric, float dot, float 
   return __fsub_rn(1.0f, __fdiv_rn(dot, denom));
 }
 
+// SIMDDistance semantics (SIMDDistance.swift:17-80): `acc` is sum((q-v)^2)
+// for L2 and dot(q, v) otherwise; cosine divides by sqrt(|q|^2)*sqrt(|v|^2).
+__device__ __forceinline__ float finalize_simd(int metric, float acc, float qn, float vn) {
+  if (metric == kL2) return acc;
+  if (metric == kIP) return -acc;
+  float denom = __fmul_rn(__fsqrt_rn(qn), __fsqrt_rn(vn));
+  if (denom < 1e-10f) return 1.0f;
+  return __fsub_rn(1.0f, __fdiv_rn(acc, denom));
+}
+
 // ---- block bitonic sort over shared-memory keys -------------------------------------
 //
 // Sorts n (a power of two) keys ascending with NT threads that share named

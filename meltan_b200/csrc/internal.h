@@ -98,8 +98,11 @@ void timing_end(cudaEvent_t stop, cudaStream_t stream);
 int32_t corpus_upload(mans_ctx* ctx, const float* rows, int64_t n, int64_t dim, uint32_t id_offset,
                       mans_corpus** out);
 void corpus_free(mans_corpus* c);
+// Exact scan + top-k over `corpus`.  mode: kModeHost (host-tier distance) or
+// kModeSimd (SIMDDistance semantics).  kcap bounds k (256 for the public
+// searches; 512 for the internal 2k candidate lists of the IVF-PQ stages).
 int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace* ws,
                         const float* d_queries, int64_t nq, int32_t k, int32_t metric,
                         float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
-                        cudaStream_t stream);
+                        cudaStream_t stream, int mode = 0, int32_t kcap = 256);
 }  // namespace mans

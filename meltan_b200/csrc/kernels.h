@@ -55,8 +55,12 @@ struct ScanParams {
   int32_t dim;
   int32_t nchunks;       // ceil(dim / 32)
   int32_t metric;
+  // 0: host-tier distance from dot(q, v) (ParallelFlatScan.swift:237-258);
+  // 1: SIMDDistance semantics (SIMDDistance.swift:17-80): L2 accumulates
+  //    sum((q - v)^2), cosine uses sqrt(|q|^2) * sqrt(|v|^2), IP = -dot.
+  int32_t mode;
   int32_t k;             // effective k (<= kp)
-  int32_t kp;            // power of two >= k, <= 256
+  int32_t kp;            // power of two >= k, <= 512
   uint64_t* slot_keys;   // [slot][kp]
   int32_t* slot_counts;  // [slot]
   int* err;
@@ -67,6 +71,8 @@ int scan_max_stages(int qb, int nchunks);
 cudaError_t scan_configure(int max_smem_optin);
 cudaError_t launch_scan(int qb, const CUtensorMap& map, const ScanParams& p, int grid,
                         cudaStream_t stream);
+constexpr int kModeHost = 0;
+constexpr int kModeSimd = 1;
 
 cudaError_t launch_row_norms(const float* rows, int64_t n, int32_t dim, int64_t ld, float* out,
                              cudaStream_t stream);

@@ -88,7 +88,7 @@ __device__ inline void flat_segment(const ScanParams& p, int s, int qb, ScanSegm
   seg.reserved = 0;
 }
 
-template <int QB>
+template <int QB, bool DIFFSQ>
 __global__ void __launch_bounds__(kScanThreads, 1)
     scan_topk_kernel(const __grid_constant__ CUtensorMap map, const ScanParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -258,10 +258,22 @@ __global__ void __launch_bounds__(kScanThreads, 1)
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             float4 b = qv[j];
-            a = __fadd_rn(a, __fmul_rn(v[j].x, b.x));
-            a = __fadd_rn(a, __fmul_rn(v[j].y, b.y));
-            a = __fadd_rn(a, __fmul_rn(v[j].z, b.z));
-            a = __fadd_rn(a, __fmul_rn(v[j].w, b.w));
+            if (DIFFSQ) {
+              float t;
+              t = __fsub_rn(b.x, v[j].x);
+              a = __fadd_rn(a, __fmul_rn(t, t));
+              t = __fsub_rn(b.y, v[j].y);
+              a = __fadd_rn(a, __fmul_rn(t, t));
+              t = __fsub_rn(b.z, v[j].z);
+              a = __fadd_rn(a, __fmul_rn(t, t));
+              t = __fsub_rn(b.w, v[j].w);
+              a = __fadd_rn(a, __fmul_rn(t, t));
+            } else {
+              a = __fadd_rn(a, __fmul_rn(v[j].x, b.x));
+              a = __fadd_rn(a, __fmul_rn(v[j].y, b.y));
+              a = __fadd_rn(a, __fmul_rn(v[j].z, b.z));
+              a = __fadd_rn(a, __fmul_rn(v[j].w, b.w));
+            }
           }
           acc[q] = a;
         }
@@ -276,7 +288,8 @@ __global__ void __launch_bounds__(kScanThreads, 1)
 #pragma unroll
       for (int q = 0; q < QB; ++q) {
         if (q < seg.qcount) {
-          float d = finalize_distance(p.metric, acc[q], sm.qn[q], vn);
+          float d = p.mode == kModeSimd ? finalize_simd(p.metric, acc[q], sm.qn[q], vn)
+                                        : finalize_distance(p.metric, acc[q], sm.qn[q], vn);
           TopKState st{sm.topbuf + q * kSortN, &sm.qcnt[q], &sm.nbest[q], &sm.thr[q]};
           topk_offer(st, p.kp, make_key(d, id), valid);
         }
@@ -463,33 +476,44 @@ int scan_max_stages(int qb, int nchunks) {
   return st;
 }
 
+template <int QB, bool D>
+static cudaError_t set_smem(int bytes) {
+  return cudaFuncSetAttribute(scan_topk_kernel<QB, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              bytes);
+}
+
 cudaError_t scan_configure(int max_smem_optin) {
   g_max_smem = max_smem_optin;
   cudaError_t e;
-  if ((e = cudaFuncSetAttribute(scan_topk_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                max_smem_optin)) != cudaSuccess)
-    return e;
-  if ((e = cudaFuncSetAttribute(scan_topk_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                max_smem_optin)) != cudaSuccess)
-    return e;
-  if ((e = cudaFuncSetAttribute(scan_topk_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                max_smem_optin)) != cudaSuccess)
-    return e;
-  return cudaFuncSetAttribute(scan_topk_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              max_smem_optin);
+  if ((e = set_smem<1, false>(max_smem_optin)) != cudaSuccess) return e;
+  if ((e = set_smem<2, false>(max_smem_optin)) != cudaSuccess) return e;
+  if ((e = set_smem<4, false>(max_smem_optin)) != cudaSuccess) return e;
+  if ((e = set_smem<8, false>(max_smem_optin)) != cudaSuccess) return e;
+  if ((e = set_smem<1, true>(max_smem_optin)) != cudaSuccess) return e;
+  if ((e = set_smem<2, true>(max_smem_optin)) != cudaSuccess) return e;
+  if ((e = set_smem<4, true>(max_smem_optin)) != cudaSuccess) return e;
+  return set_smem<8, true>(max_smem_optin);
+}
+
+template <bool D>
+static cudaError_t launch_scan_t(int qb, const CUtensorMap& map, const ScanParams& p, int grid,
+                                 size_t smem, cudaStream_t stream) {
+  switch (qb) {
+    case 1: scan_topk_kernel<1, D><<<grid, kScanThreads, smem, stream>>>(map, p); break;
+    case 2: scan_topk_kernel<2, D><<<grid, kScanThreads, smem, stream>>>(map, p); break;
+    case 4: scan_topk_kernel<4, D><<<grid, kScanThreads, smem, stream>>>(map, p); break;
+    case 8: scan_topk_kernel<8, D><<<grid, kScanThreads, smem, stream>>>(map, p); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
 }
 
 cudaError_t launch_scan(int qb, const CUtensorMap& map, const ScanParams& p, int grid,
                         cudaStream_t stream) {
   size_t smem = scan_smem_bytes(qb, p.nchunks, p.stages);
-  switch (qb) {
-    case 1: scan_topk_kernel<1><<<grid, kScanThreads, smem, stream>>>(map, p); break;
-    case 2: scan_topk_kernel<2><<<grid, kScanThreads, smem, stream>>>(map, p); break;
-    case 4: scan_topk_kernel<4><<<grid, kScanThreads, smem, stream>>>(map, p); break;
-    case 8: scan_topk_kernel<8><<<grid, kScanThreads, smem, stream>>>(map, p); break;
-    default: return cudaErrorInvalidValue;
-  }
-  return cudaGetLastError();
+  // the (q - v)^2 accumulation is used only for SIMDDistance L2
+  if (p.mode == kModeSimd && p.metric == kL2) return launch_scan_t<true>(qb, map, p, grid, smem, stream);
+  return launch_scan_t<false>(qb, map, p, grid, smem, stream);
 }
 
 cudaError_t launch_row_norms(const float* rows, int64_t n, int32_t dim, int64_t ld, float* out,

@@ -70,8 +70,9 @@ def test_ivf_nprobe_all_equals_bruteforce(ctx):
 
 
 def test_ivf_recall_at_10(ctx):
-    """IVFFlatSearchTests.swift:77-142 asks recall@10 >= 0.95 on clustered data."""
-    v, q = bench.make_mixture(30000, 64, 64, 50, seed=6)
+    """IVFFlatSearchTests.swift:77-142 asks recall@10 >= 0.95 on clustered data
+    (tight clusters, as the reference test's +-0.02 jitter around centres)."""
+    v, q = bench.make_mixture(30000, 64, 64, 50, sigma=0.05, seed=6)
     cent, assign = bench.train_partition(v, 64, O.COSINE)
     part = mb.Partition.from_assignment(ctx, v, cent, assign)
     got = mb.IVFFlatSearch.search_arrays(ctx, q, part, 10, 8, mb.Metric.cosine)
