@@ -114,6 +114,45 @@ def train_partition(v, nlist, metric, iters=4, seed=42, device=None):
     return cent.cpu().numpy().astype(np.float32), assign.cpu().numpy()
 
 
+def train_ivfpq(v, nlist, m, metric=1, iters=4, seed=42, device=None):
+    """Trained IVF-PQ artefacts for synthetic data (a build-time step outside
+    the search path): coarse centroids by Lloyd iterations, per-subspace
+    256-centroid codebooks on residuals of a sample, codes by nearest
+    codebook entry and inverted lists in insertion (row) order.  Torch
+    matmuls; the search kernels take these as inputs."""
+    import torch
+    dev = device or ("cuda" if torch.cuda.is_available() else "cpu")
+    n, dim = v.shape
+    sub = dim // m
+    cent, assign = train_partition(v, nlist, metric, iters=iters, seed=seed, device=dev)
+    g = torch.Generator(device="cpu").manual_seed(seed + 1)
+    samp = torch.randperm(n, generator=g)[:min(n, 65536)]
+    x = torch.from_numpy(v[samp.numpy()]).to(dev) - torch.from_numpy(cent[assign[samp.numpy()]]).to(dev)
+    books = []
+    for s in range(m):
+        xs = x[:, s * sub:(s + 1) * sub]
+        cb = xs[torch.randperm(xs.shape[0], generator=g)[:256].to(dev)].clone()
+        for _ in range(iters):
+            a = torch.argmin(torch.cdist(xs, cb), dim=1)
+            acc = torch.zeros_like(cb).index_add_(0, a, xs)
+            c = torch.bincount(a, minlength=256).unsqueeze(1).to(acc.dtype)
+            cb = torch.where(c > 0, acc / c.clamp(min=1), cb)
+        books.append(cb)
+    codebooks = torch.stack(books)  # m x 256 x sub
+    codes = torch.empty((n, m), dtype=torch.uint8, device=dev)
+    ct = torch.from_numpy(cent).to(dev)
+    at = torch.from_numpy(assign).to(dev)
+    for a0 in range(0, n, 262144):
+        r = torch.from_numpy(v[a0:a0 + 262144]).to(dev) - ct[at[a0:a0 + 262144]]
+        for s in range(m):
+            d = torch.cdist(r[:, s * sub:(s + 1) * sub], codebooks[s])
+            codes[a0:a0 + 262144, s] = torch.argmin(d, dim=1).to(torch.uint8)
+    order = np.argsort(assign, kind="stable").astype(np.uint32)
+    offsets = np.concatenate([[0], np.cumsum(np.bincount(assign, minlength=nlist))]).astype(np.int64)
+    return (cent, codebooks.cpu().numpy().astype(np.float32), codes.cpu().numpy(),
+            offsets, order)
+
+
 def p50(xs):
     s = sorted(xs)
     return s[max(0, math.ceil(0.5 * len(s)) - 1)]  # nearest rank (LatencyDistribution.swift:154-160)

@@ -183,6 +183,47 @@ int32_t mans_ivf_search_device(mans_ctx *ctx, mans_ivf *ivf, mans_workspace *ws,
                                int32_t metric, float *d_out_dist, uint32_t *d_out_ids,
                                int32_t *d_out_counts, void *cuda_stream);
 
+/* ---- IVF-PQ ---------------------------------------------------------------- */
+
+/* Uploads a trained IVF-PQ index in the layout of _IVFPQIndex
+ * (Sources/MetalANNS/IVFPQIndex.swift:6-35): coarse centroids nlist x dim,
+ * codebooks m x ks x (dim/m) (GPUADCSearch.flattenCodebooks order,
+ * GPUADCSearch.swift:194-205), codes n x m stored per internal id
+ * (PQVectorBuffer, PQVectorBuffer.swift:26,34-51), and the inverted lists as
+ * CSR (list l = lists[list_offsets[l] .. list_offsets[l+1]), in insertion
+ * order).  ks must be 256 (IVFPQIndex.swift:45-47); metric 0/1/2.
+ * list_positions (may be NULL) gives each entry's position in its full list
+ * when this index holds one row shard of a larger one, so that insertion
+ * order survives the cross-shard merge.  Lists are limited to 2^20 entries. */
+int32_t mans_ivfpq_create(mans_ctx *ctx, const float *coarse, int32_t nlist, int64_t dim,
+                          const float *codebooks, int32_t m, int32_t ks, const uint8_t *codes,
+                          int64_t n, const int64_t *list_offsets, const uint32_t *lists,
+                          const uint32_t *list_positions, int32_t metric, mans_ivfpq **out);
+int32_t mans_ivfpq_destroy(mans_ivfpq *ix);
+
+/* _IVFPQIndex.search(query:k:nprobe:) (IVFPQIndex.swift:177-226) for a batch:
+ * coarse SIMDDistance ranking with newest-first ties, residual LUT
+ * (ProductQuantizer.distanceTableFlattened) and sequential ADC sums per
+ * probed list, merged with the BoundedSortedList rule.  out_ids are internal
+ * ids; results are min(k, 256) wide.  A query of the wrong width yields an
+ * empty result, as the reference returns []. */
+int32_t mans_ivfpq_search(mans_ctx *ctx, mans_ivfpq *ix, const float *queries, int64_t nq,
+                          int64_t dim, int32_t k, int32_t nprobe, float *out_dist,
+                          uint32_t *out_ids, int32_t *out_counts);
+int32_t mans_ivfpq_search_device(mans_ctx *ctx, mans_ivfpq *ix, mans_workspace *ws,
+                                 const float *d_queries, int64_t nq, int32_t k, int32_t nprobe,
+                                 float *d_out_dist, uint32_t *d_out_ids, int32_t *d_out_counts,
+                                 void *cuda_stream);
+
+/* GPUADCSearch.computeDistances(context:query:pq:packedCodes:vectorCount:
+ * flatCodebooks:) (GPUADCSearch.swift:35-173): squared-L2 LUT of `query`
+ * against the codebooks (pq_compute_distance_table) and the sequential sum
+ * per code (pq_adc_scan).  Codes >= ks -> MANS_ERR_SEARCH, as the reference's
+ * validation; count == 0 -> nothing written. */
+int32_t mans_pq_adc_list(mans_ctx *ctx, const float *query, int64_t dim, const float *codebooks,
+                         int32_t m, int32_t ks, const uint8_t *codes, int64_t count,
+                         float *out_dist);
+
 #if defined(__cplusplus)
 }
 #endif

@@ -25,3 +25,4 @@ from .core import (  # noqa: F401
     topk_merge_device,
 )
 from .ivf import IVFFlatSearch, Partition  # noqa: F401,E402
+from .pq import GPUADCSearch, IVFPQIndex  # noqa: F401,E402

@@ -48,6 +48,15 @@ SIGNATURES = {
                                     C.c_int32, _VP, _VP, _VP]),
     "mans_ivf_search_device": (C.c_int32, [_VP, _VP, _VP, _VP, C.c_int64, C.c_int32, C.c_int32,
                                            C.c_int32, _VP, _VP, _VP, _VP]),
+    "mans_ivfpq_create": (C.c_int32, [_VP, _VP, C.c_int32, C.c_int64, _VP, C.c_int32, C.c_int32,
+                                      _VP, C.c_int64, _VP, _VP, _VP, C.c_int32, C.POINTER(_VP)]),
+    "mans_ivfpq_destroy": (C.c_int32, [_VP]),
+    "mans_ivfpq_search": (C.c_int32, [_VP, _VP, _VP, C.c_int64, C.c_int64, C.c_int32, C.c_int32,
+                                      _VP, _VP, _VP]),
+    "mans_ivfpq_search_device": (C.c_int32, [_VP, _VP, _VP, _VP, C.c_int64, C.c_int32, C.c_int32,
+                                             _VP, _VP, _VP, _VP]),
+    "mans_pq_adc_list": (C.c_int32, [_VP, _VP, C.c_int64, _VP, C.c_int32, C.c_int32, _VP,
+                                     C.c_int64, _VP]),
 }
 
 _lib = None

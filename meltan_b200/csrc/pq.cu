@@ -1,0 +1,681 @@
+// pq.cu -- IVF-PQ search (coarse probe, per-list LUT + ADC, newest-first merge)
+// and the single-list ADC of GPUADCSearch.
+//
+// Restates _IVFPQIndex.search (Sources/MetalANNS/IVFPQIndex.swift:177-226):
+//   1. coarse scores SIMDDistance.distance(q, c) for every coarse centroid,
+//      ranked in a BoundedSortedList of capacity nprobe (:484-512);
+//   2. for each probed cluster in that order: residual q - c (:366-368), the
+//      LUT of ProductQuantizer.distanceTableFlattened over the residual
+//      (ProductQuantizer.swift:223-253) and the sequential ADC sum of
+//      cpuADCDistances (IVFPQIndex.swift:418-452);
+//   3. every candidate inserted, in probe order then list order, into a
+//      BoundedSortedList of capacity k (BoundedSelection.swift:158-214).
+//
+// BoundedSortedList keeps the list sorted by score with equal scores newest
+// first, rejects an equal-score newcomer when full and evicts the last entry
+// on overflow.  Its final content has a closed form that the device computes
+// from the 2K smallest candidates by (score, insertion sequence):
+//   w = K-th smallest score, L = candidates with score < w (always kept,
+//   |L| = l < K), E = candidates with score == w in insertion order.  Once the
+//   list first holds K entries it stays full, so only E entries that arrive
+//   while it is filling are inserted -- the E entries among the first K
+//   arrivals of L u E -- and later L arrivals evict the oldest of them.  The
+//   kept E entries are the newest K - l inserted ones.  Those first K
+//   arrivals contain at most K E entries, which are the K earliest E entries,
+//   and all of L u {K earliest E} lies within the 2K smallest (score, seq)
+//   keys.  Output order: score ascending, newest first among equal scores.
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+#include "kernels.h"
+#include "mans_cuda.h"
+
+using namespace mans;
+
+struct mans_ivfpq {
+  mans_ctx* ctx = nullptr;
+  int32_t nlist = 0;
+  int64_t n = 0;
+  int64_t dim = 0;
+  int32_t m = 0;
+  int32_t ks = 256;
+  int32_t sub = 0;
+  int32_t metric = 1;
+  int64_t max_len = 0;
+  mans_corpus* coarse = nullptr;  // coarse centroids (SIMDDistance scoring)
+  float* codebooks = nullptr;     // m x ks x sub
+  uint8_t* codes = nullptr;       // list-contiguous, n x m
+  uint32_t* ids = nullptr;        // list-contiguous internal ids
+  uint32_t* pos = nullptr;        // global position of each entry in its list (shards)
+  int64_t* offsets = nullptr;     // nlist + 1
+};
+
+namespace mans {
+namespace {
+
+constexpr int kPosBits = 20;  // insertion sequence = probe rank << 20 | list position
+constexpr int kAdcThreads = 256;
+
+struct ResolveParams {
+  const float* in_score;
+  const uint32_t* in_seq;
+  const uint32_t* in_payload;  // null: payload derived from seq
+  const int32_t* in_count;
+  int32_t kin;
+  int64_t nq;
+  int32_t cap;  // K
+  // seq -> internal id mapping (IVF-PQ candidates); null: payload = seq
+  const uint32_t* probe_lists;  // [nq][probe_stride]
+  int32_t probe_stride;
+  const int64_t* offsets;
+  const uint32_t* ids;
+  float* out_score;
+  uint32_t* out_id;
+  int32_t* out_count;
+  int32_t kout;
+};
+
+__device__ __forceinline__ uint32_t resolve_payload(const ResolveParams& p, int64_t q, int i) {
+  uint32_t seq = p.in_seq[q * p.kin + i];
+  if (p.in_payload) return p.in_payload[q * p.kin + i];
+  if (!p.probe_lists) return seq;
+  uint32_t rank = seq >> kPosBits;
+  uint32_t pos = seq & ((1u << kPosBits) - 1u);
+  uint32_t list = p.probe_lists[q * p.probe_stride + rank];
+  return p.ids[p.offsets[list] + pos];
+}
+
+// One block per query.  Input rows are sorted by (score, seq) ascending.
+__global__ void __launch_bounds__(256) bsl_resolve_kernel(const ResolveParams p) {
+  __shared__ uint64_t keys[1024];
+  __shared__ int sh_l, sh_e, sh_ins;
+  const int64_t q = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int c = p.in_count[q];
+  const int K = p.cap;
+  const float* sc = p.in_score + q * p.kin;
+  const uint32_t* sq = p.in_seq + q * p.kin;
+  int nout;
+  int l = 0, e_first = 0, e_keep = 0;  // kept E entries: E[e_first, e_first + e_keep)
+  if (c <= K) {
+    nout = c;
+    l = c;  // everything kept; output = input with equal-score runs reversed
+  } else {
+    const float w = sc[K - 1];
+    if (tid == 0) {
+      int a = 0;
+      while (a < c && sc[a] < w) ++a;
+      int b = a;
+      while (b < c && sc[b] == w) ++b;
+      sh_l = a;
+      sh_e = b - a;
+    }
+    __syncthreads();
+    l = sh_l;
+    const int ecount = min(sh_e, K);  // the K earliest E entries (seq ascending)
+    // first K arrivals among L u E': sort their sequences, tag E entries
+    const int total = l + ecount;
+    int n2 = 1;
+    while (n2 < total) n2 <<= 1;
+    for (int i = tid; i < n2; i += blockDim.x) {
+      uint64_t key = kKeyMax;
+      if (i < l) key = (static_cast<uint64_t>(sq[i]) << 1);
+      else if (i < total) key = (static_cast<uint64_t>(sq[i]) << 1) | 1u;
+      keys[i] = key;
+    }
+    __syncthreads();
+    bitonic_sort_keys<256>(keys, n2, tid, 0);
+    if (tid == 0) {
+      int ins = 0;
+      for (int i = 0; i < K && i < total; ++i) ins += static_cast<int>(keys[i] & 1u);
+      sh_ins = ins;
+    }
+    __syncthreads();
+    const int ins = sh_ins;
+    e_keep = K - l;
+    e_first = l + ins - e_keep;  // newest K - l of the inserted E entries
+    nout = K;
+  }
+  // write: L with equal-score runs reversed (newest first), then kept E newest first
+  for (int i = tid; i < l; i += blockDim.x) {
+    // find the equal-score run [a, b) that holds i; position inside it reversed
+    int a = i, b = i + 1;
+    while (a > 0 && sc[a - 1] == sc[i]) --a;
+    while (b < l && sc[b] == sc[i]) ++b;
+    int src = a + (b - 1 - i);
+    p.out_score[q * p.kout + i] = sc[src];
+    p.out_id[q * p.kout + i] = resolve_payload(p, q, src);
+  }
+  for (int j = tid; j < e_keep; j += blockDim.x) {
+    int src = e_first + (e_keep - 1 - j);
+    p.out_score[q * p.kout + l + j] = sc[src];
+    p.out_id[q * p.kout + l + j] = resolve_payload(p, q, src);
+  }
+  for (int i = nout + tid; i < p.kout; i += blockDim.x) {
+    p.out_score[q * p.kout + i] = __int_as_float(0x7F800000);
+    p.out_id[q * p.kout + i] = kEmptyId;
+  }
+  if (tid == 0) p.out_count[q] = nout;
+}
+
+struct AdcParams {
+  const float* queries;     // nq x dim
+  const float* coarse;      // coarse rows (ld pitch)
+  int64_t coarse_ld;
+  const float* codebooks;   // m x ks x sub
+  const uint8_t* codes;     // packed n x m
+  const uint32_t* pos;      // optional global list positions
+  const int64_t* offsets;
+  const uint32_t* probe_lists;  // [nq][probe]
+  const int32_t* probe_counts;
+  int32_t probe;
+  int64_t nq;
+  int32_t dim, m, ks, sub, metric;
+  int32_t k;   // candidates kept per (query, list)
+  int32_t kp;
+  int32_t cb_in_smem;
+  uint64_t* slot_keys;      // [q*probe + p][kp]
+  int32_t* slot_counts;
+};
+
+__device__ __forceinline__ float lut_entry(int metric, const float* r, const float* cb, int sub) {
+  if (metric == kL2) {
+    float s = 0.0f;
+    for (int d = 0; d < sub; ++d) {
+      float t = __fsub_rn(r[d], cb[d]);
+      s = __fadd_rn(s, __fmul_rn(t, t));
+    }
+    return s;
+  }
+  float dot = 0.0f;
+  for (int d = 0; d < sub; ++d) dot = __fadd_rn(dot, __fmul_rn(r[d], cb[d]));
+  if (metric == kIP) return -dot;
+  float na = 0.0f, nb = 0.0f;
+  for (int d = 0; d < sub; ++d) na = __fadd_rn(na, __fmul_rn(r[d], r[d]));
+  for (int d = 0; d < sub; ++d) nb = __fadd_rn(nb, __fmul_rn(cb[d], cb[d]));
+  float denom = __fmul_rn(__fsqrt_rn(na), __fsqrt_rn(nb));
+  if (denom < 1e-10f) return 1.0f;
+  return __fsub_rn(1.0f, __fdiv_rn(dot, denom));
+}
+
+// Persistent: block b handles items b, b + grid, ... ; item = (query, probe rank).
+__global__ void __launch_bounds__(kAdcThreads, 1) pq_adc_kernel(const AdcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<size_t>(smem_raw) + 15) / 16 * 16);
+  uint64_t* topbuf = reinterpret_cast<uint64_t*>(base);
+  float* lut = reinterpret_cast<float*>(base + kSortN * 8);
+  float* resid = lut + p.m * p.ks;
+  float* cbs = resid + ((p.dim + 3) / 4 * 4);
+  __shared__ uint64_t thr;
+  __shared__ int qc, nb;
+  const int tid = threadIdx.x;
+  const float* cb = p.cb_in_smem ? cbs : p.codebooks;
+  if (p.cb_in_smem) {
+    const int total = p.m * p.ks * p.sub;
+    for (int i = tid; i < total; i += kAdcThreads) cbs[i] = p.codebooks[i];
+  }
+  const int64_t items = p.nq * p.probe;
+  for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
+    const int64_t q = it / p.probe;
+    const int pr = static_cast<int>(it - q * p.probe);
+    __syncthreads();  // previous item fully done with the shared buffers
+    if (pr >= p.probe_counts[q]) {
+      if (tid == 0) p.slot_counts[it] = 0;
+      continue;
+    }
+    const uint32_t list = p.probe_lists[q * p.probe + pr];
+    for (int d = tid; d < p.dim; d += kAdcThreads)
+      resid[d] = __fsub_rn(p.queries[q * p.dim + d], p.coarse[list * p.coarse_ld + d]);
+    if (tid == 0) {
+      thr = kKeyMax;
+      qc = 0;
+      nb = 0;
+    }
+    __syncthreads();
+    for (int e = tid; e < p.m * p.ks; e += kAdcThreads) {
+      const int s = e / p.ks;
+      lut[e] = lut_entry(p.metric, resid + s * p.sub, cb + static_cast<int64_t>(e) * p.sub, p.sub);
+    }
+    __syncthreads();
+    TopKState st{topbuf, &qc, &nb, &thr};
+    const int64_t off = p.offsets[list];
+    const int64_t len = p.offsets[list + 1] - off;
+    for (int64_t b = 0; b < len; b += kAdcThreads) {
+      const int64_t e = b + tid;
+      const bool valid = e < len;
+      uint64_t key = kKeyMax;
+      if (valid) {
+        const uint8_t* code = p.codes + (off + e) * p.m;
+        float total = 0.0f;
+        for (int s = 0; s < p.m; ++s) total = __fadd_rn(total, lut[s * p.ks + code[s]]);
+        const uint32_t pos = p.pos ? p.pos[off + e] : static_cast<uint32_t>(e);
+        key = make_key(total, (static_cast<uint32_t>(pr) << kPosBits) | pos);
+      }
+      topk_offer(st, p.kp, key, valid);
+      __syncthreads();
+      if (qc > kSortN - p.kp - kAdcThreads) topk_merge<kAdcThreads>(st, p.k, p.kp, kSortN, tid, 0);
+    }
+    if (qc > 0) topk_merge<kAdcThreads>(st, p.k, p.kp, kSortN, tid, 0);
+    for (int i = tid; i < nb; i += kAdcThreads) p.slot_keys[it * p.kp + i] = topbuf[i];
+    if (tid == 0) p.slot_counts[it] = nb;
+  }
+}
+
+// GPUADCSearch.computeDistances for one list (GPUADCSearch.swift:35-173 with
+// pq_compute_distance_table + pq_adc_scan, PQDistance.metal:4-66): a squared
+// L2 LUT over the query, then the sequential sum per code.  Every block
+// rebuilds the LUT in shared memory and scores a stripe of codes.
+__global__ void __launch_bounds__(kAdcThreads) pq_adc_list_kernel(
+    const float* __restrict__ query, const float* __restrict__ codebooks, int m, int ks, int sub,
+    const uint8_t* __restrict__ codes, int64_t count, float* __restrict__ out) {
+  extern __shared__ float lut[];
+  for (int e = threadIdx.x; e < m * ks; e += blockDim.x) {
+    const int s = e / ks;
+    lut[e] = lut_entry(kL2, query + s * sub, codebooks + static_cast<int64_t>(e) * sub, sub);
+  }
+  __syncthreads();
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint8_t* code = codes + i * m;
+    float total = 0.0f;
+    for (int s = 0; s < m; ++s) {
+      const int c = code[s];
+      if (c >= ks) {
+        total = 3.40282347e+38f;  // FLT_MAX, as pq_adc_scan
+        break;
+      }
+      total = __fadd_rn(total, lut[s * ks + c]);
+    }
+    out[i] = total;
+  }
+}
+
+}  // namespace
+
+static size_t carve(size_t& o, size_t bytes) {
+  size_t at = (o + 255) / 256 * 256;
+  o = at + bytes;
+  return at;
+}
+
+static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* ws,
+                                const float* d_queries, int64_t nq, int32_t k, int32_t nprobe,
+                                float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
+                                cudaStream_t stream) {
+  const int32_t kout = std::min<int32_t>(k, MANS_MAX_TOPK);
+  if (nq <= 0) return MANS_OK;
+  if (k <= 0 || ix->n <= 0 || ix->nlist <= 0) {
+    if (kout <= 0) {
+      cudaError_t e = cudaMemsetAsync(d_out_counts, 0, sizeof(int32_t) * nq, stream);
+      return e == cudaSuccess ? MANS_OK : fail_cuda(e, "cudaMemsetAsync");
+    }
+    cudaError_t e = launch_fill_empty(d_out_dist, d_out_ids, d_out_counts, nq, kout, stream);
+    return e == cudaSuccess ? MANS_OK : fail_cuda(e, "fill_empty launch");
+  }
+  const int32_t probe = std::max(1, std::min(nprobe, ix->nlist));
+  const int32_t kc = std::min<int32_t>(2 * probe, ix->nlist);  // coarse candidates
+  if (kc > 512) return fail(MANS_ERR_SEARCH, "nprobe above 256 is not supported on the GPU");
+  const int32_t k2 = 2 * kout;  // ADC candidates per list and after the merge
+  const int32_t kp2 = pow2_at_least(k2);
+
+  size_t o = 0;
+  const size_t o_cd = carve(o, nq * kc * sizeof(float));
+  const size_t o_ci = carve(o, nq * kc * sizeof(uint32_t));
+  const size_t o_cc = carve(o, nq * sizeof(int32_t));
+  const size_t o_ps = carve(o, nq * probe * sizeof(float));
+  const size_t o_pl = carve(o, nq * probe * sizeof(uint32_t));
+  const size_t o_pc = carve(o, nq * sizeof(int32_t));
+  const size_t o_md = carve(o, nq * k2 * sizeof(float));
+  const size_t o_mi = carve(o, nq * k2 * sizeof(uint32_t));
+  const size_t o_mc = carve(o, nq * sizeof(int32_t));
+  int32_t rc;
+  if ((rc = ws->aux2.reserve(o)) != MANS_OK) return rc;
+  // slot buffers: coarse search and ADC items, reserved once before any launch
+  const int64_t cent_tiles = (ix->nlist + kTileRows - 1) / kTileRows;
+  const size_t cent_slots =
+      static_cast<size_t>((nq + 7) / 8 * 8) * std::min<int64_t>(ctx->num_sms, cent_tiles);
+  const size_t adc_slots = static_cast<size_t>(nq) * probe;
+  const size_t need_keys =
+      std::max(cent_slots * pow2_at_least(kc), adc_slots * kp2) * sizeof(uint64_t);
+  if ((rc = ws->slot_keys.reserve(need_keys)) != MANS_OK) return rc;
+  if ((rc = ws->slot_counts.reserve(std::max(cent_slots, adc_slots) * sizeof(int32_t))) != MANS_OK)
+    return rc;
+  uint8_t* A = static_cast<uint8_t*>(ws->aux2.ptr);
+  float* cd = reinterpret_cast<float*>(A + o_cd);
+  uint32_t* ci = reinterpret_cast<uint32_t*>(A + o_ci);
+  int32_t* cc = reinterpret_cast<int32_t*>(A + o_cc);
+  float* ps = reinterpret_cast<float*>(A + o_ps);
+  uint32_t* pl = reinterpret_cast<uint32_t*>(A + o_pl);
+  int32_t* pc = reinterpret_cast<int32_t*>(A + o_pc);
+  float* md = reinterpret_cast<float*>(A + o_md);
+  uint32_t* mi = reinterpret_cast<uint32_t*>(A + o_mi);
+  int32_t* mc = reinterpret_cast<int32_t*>(A + o_mc);
+
+  // 1. coarse: SIMDDistance scores, 2 x nprobe smallest by (score, index)
+  rc = run_flat_search(ctx, ix->coarse, ws, d_queries, nq, kc, ix->metric, cd, ci, cc, stream,
+                       kModeSimd, 512);
+  if (rc != MANS_OK) return rc;
+  ResolveParams r{};
+  r.in_score = cd;
+  r.in_seq = ci;
+  r.in_count = cc;
+  r.kin = kc;
+  r.nq = nq;
+  r.cap = probe;
+  r.out_score = ps;
+  r.out_id = pl;
+  r.out_count = pc;
+  r.kout = probe;
+  bsl_resolve_kernel<<<static_cast<unsigned>(nq), 256, 0, stream>>>(r);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail_cuda(e, "coarse resolve launch");
+
+  // 2. per (query, probed list): residual LUT + ADC, 2k best per list
+  AdcParams a{};
+  a.queries = d_queries;
+  a.coarse = ix->coarse->rows;
+  a.coarse_ld = ix->coarse->ld;
+  a.codebooks = ix->codebooks;
+  a.codes = ix->codes;
+  a.pos = ix->pos;
+  a.offsets = ix->offsets;
+  a.probe_lists = pl;
+  a.probe_counts = pc;
+  a.probe = probe;
+  a.nq = nq;
+  a.dim = static_cast<int32_t>(ix->dim);
+  a.m = ix->m;
+  a.ks = ix->ks;
+  a.sub = ix->sub;
+  a.metric = ix->metric;
+  a.k = k2;
+  a.kp = kp2;
+  a.slot_keys = static_cast<uint64_t*>(ws->slot_keys.ptr);
+  a.slot_counts = static_cast<int32_t*>(ws->slot_counts.ptr);
+  const size_t cb_bytes = static_cast<size_t>(ix->m) * ix->ks * ix->sub * sizeof(float);
+  size_t smem = 16 + kSortN * 8 + static_cast<size_t>(ix->m) * ix->ks * 4 +
+                static_cast<size_t>((ix->dim + 3) / 4 * 4) * 4;
+  a.cb_in_smem = smem + cb_bytes <= static_cast<size_t>(ctx->max_smem) - 64 ? 1 : 0;
+  if (a.cb_in_smem) smem += cb_bytes;
+  if (smem > static_cast<size_t>(ctx->max_smem) - 64)
+    return fail(MANS_ERR_SEARCH, "PQ distance table exceeds shared memory");
+  e = cudaFuncSetAttribute(pq_adc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem));
+  if (e != cudaSuccess) return fail_cuda(e, "adc configure");
+  const int64_t items = nq * probe;
+  const int grid = static_cast<int>(std::min<int64_t>(items, ctx->num_sms));
+  cudaEvent_t stop = timing_begin(ws, stream);
+  pq_adc_kernel<<<grid, kAdcThreads, smem, stream>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail_cuda(e, "adc launch");
+  timing_end(stop, stream);
+
+  // 3. 2k smallest (score, seq) per query over its probed lists
+  MergeParams m{};
+  m.in_keys = a.slot_keys;
+  m.in_counts = a.slot_counts;
+  m.slots_per_query = probe;
+  m.kp_in = kp2;
+  m.nq = nq;
+  m.k = k2;
+  m.kp = kp2;
+  m.kout = k2;
+  m.out_dist = md;
+  m.out_ids = mi;
+  m.out_counts = mc;
+  e = launch_merge(m, stream);
+  if (e != cudaSuccess) return fail_cuda(e, "adc merge launch");
+
+  // 4. BoundedSortedList(capacity k) outcome, seq -> internal id
+  ResolveParams f{};
+  f.in_score = md;
+  f.in_seq = mi;
+  f.in_count = mc;
+  f.kin = k2;
+  f.nq = nq;
+  f.cap = kout;
+  f.probe_lists = pl;
+  f.probe_stride = probe;
+  f.offsets = ix->offsets;
+  f.ids = ix->ids;
+  f.out_score = d_out_dist;
+  f.out_id = d_out_ids;
+  f.out_count = d_out_counts;
+  f.kout = kout;
+  bsl_resolve_kernel<<<static_cast<unsigned>(nq), 256, 0, stream>>>(f);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail_cuda(e, "resolve launch");
+  ws->launches += 4;
+  return MANS_OK;
+}
+
+}  // namespace mans
+
+extern "C" {
+
+int32_t mans_ivfpq_create(mans_ctx* ctx, const float* coarse, int32_t nlist, int64_t dim,
+                          const float* codebooks, int32_t m, int32_t ks, const uint8_t* codes,
+                          int64_t n, const int64_t* list_offsets, const uint32_t* lists,
+                          const uint32_t* list_positions, int32_t metric, mans_ivfpq** out) {
+  if (!ctx || !out) return fail(MANS_ERR_INVALID, "null context or output");
+  *out = nullptr;
+  if (nlist <= 0 || dim <= 0 || m <= 0 || n < 0) return fail(MANS_ERR_INVALID, "bad IVF-PQ shape");
+  if (ks != 256)
+    return fail(MANS_ERR_INVALID, "_IVFPQIndex requires numCentroids == 256 (UInt8 codes)");
+  if (dim % m != 0) return fail(MANS_ERR_INVALID, "dimension must be divisible by numSubspaces");
+  if (metric < 0 || metric > 2) return fail(MANS_ERR_INVALID, "unsupported metric");
+  if (!coarse || !codebooks || !list_offsets || (n > 0 && (!codes || !lists)))
+    return fail(MANS_ERR_INVALID, "null IVF-PQ buffer");
+  const int64_t total = list_offsets[nlist];
+  if (list_offsets[0] != 0 || total < 0) return fail(MANS_ERR_INVALID, "bad list offsets");
+  int64_t max_len = 0;
+  for (int32_t l = 0; l < nlist; ++l) {
+    int64_t len = list_offsets[l + 1] - list_offsets[l];
+    if (len < 0) return fail(MANS_ERR_INVALID, "list offsets must be non-decreasing");
+    max_len = std::max(max_len, len);
+  }
+  for (int64_t i = 0; i < total; ++i)
+    if (lists[i] >= static_cast<uint64_t>(n)) return fail(MANS_ERR_INVALID, "list id out of range");
+  if (max_len >= (1 << kPosBits) ||
+      (list_positions && [&] {
+        for (int64_t i = 0; i < total; ++i)
+          if (list_positions[i] >= (1u << kPosBits)) return true;
+        return false;
+      }()))
+    return fail(MANS_ERR_INVALID, "inverted list longer than 2^20 entries");
+  DeviceGuard g(ctx->device);
+  mans_ivfpq* ix = new mans_ivfpq();
+  ix->ctx = ctx;
+  ix->nlist = nlist;
+  ix->n = total;
+  ix->dim = dim;
+  ix->m = m;
+  ix->ks = ks;
+  ix->sub = static_cast<int32_t>(dim / m);
+  ix->metric = metric;
+  ix->max_len = max_len;
+  // gather codes into list order on the host (codes are stored per internal id)
+  std::vector<uint8_t> packed(static_cast<size_t>(std::max<int64_t>(total, 1)) * m);
+  for (int64_t i = 0; i < total; ++i)
+    std::memcpy(&packed[i * m], codes + static_cast<int64_t>(lists[i]) * m, m);
+  int32_t rc = corpus_upload(ctx, coarse, nlist, dim, 0, &ix->coarse);
+  cudaError_t e = cudaSuccess;
+  const size_t cb_count = static_cast<size_t>(m) * ks * ix->sub;
+  if (rc == MANS_OK) {
+    e = cudaMalloc(&ix->codebooks, cb_count * sizeof(float));
+    if (e == cudaSuccess)
+      e = cudaMemcpy(ix->codebooks, codebooks, cb_count * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMalloc(&ix->codes, packed.size());
+    if (e == cudaSuccess)
+      e = cudaMemcpy(ix->codes, packed.data(), packed.size(), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMalloc(&ix->ids, std::max<int64_t>(total, 1) * sizeof(uint32_t));
+    if (e == cudaSuccess && total > 0)
+      e = cudaMemcpy(ix->ids, lists, total * sizeof(uint32_t), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && list_positions) {
+      e = cudaMalloc(&ix->pos, std::max<int64_t>(total, 1) * sizeof(uint32_t));
+      if (e == cudaSuccess && total > 0)
+        e = cudaMemcpy(ix->pos, list_positions, total * sizeof(uint32_t), cudaMemcpyHostToDevice);
+    }
+    if (e == cudaSuccess) e = cudaMalloc(&ix->offsets, (nlist + 1) * sizeof(int64_t));
+    if (e == cudaSuccess)
+      e = cudaMemcpy(ix->offsets, list_offsets, (nlist + 1) * sizeof(int64_t),
+                     cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) rc = fail_cuda(e, "IVF-PQ upload");
+  }
+  if (rc != MANS_OK) {
+    corpus_free(ix->coarse);
+    cudaFree(ix->codebooks);
+    cudaFree(ix->codes);
+    cudaFree(ix->ids);
+    cudaFree(ix->pos);
+    cudaFree(ix->offsets);
+    delete ix;
+    return rc;
+  }
+  *out = ix;
+  return MANS_OK;
+}
+
+int32_t mans_ivfpq_destroy(mans_ivfpq* ix) {
+  if (!ix) return MANS_OK;
+  DeviceGuard g(ix->ctx->device);
+  cudaDeviceSynchronize();
+  corpus_free(ix->coarse);
+  cudaFree(ix->codebooks);
+  cudaFree(ix->codes);
+  cudaFree(ix->ids);
+  cudaFree(ix->pos);
+  cudaFree(ix->offsets);
+  delete ix;
+  return MANS_OK;
+}
+
+int32_t mans_ivfpq_search_device(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* ws,
+                                 const float* d_queries, int64_t nq, int32_t k, int32_t nprobe,
+                                 float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
+                                 void* cuda_stream) {
+  if (!ctx || !ix || ix->ctx != ctx) return fail(MANS_ERR_INVALID, "null or foreign IVF-PQ index");
+  if (!ws || ws->ctx != ctx) return fail(MANS_ERR_INVALID, "workspace missing or foreign");
+  if (nq < 0) return fail(MANS_ERR_INVALID, "negative query count");
+  DeviceGuard g(ctx->device);
+  return run_ivfpq_search(ctx, ix, ws, d_queries, nq, k, nprobe, d_out_dist, d_out_ids,
+                          d_out_counts, static_cast<cudaStream_t>(cuda_stream));
+}
+
+int32_t mans_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, const float* queries, int64_t nq,
+                          int64_t dim, int32_t k, int32_t nprobe, float* out_dist,
+                          uint32_t* out_ids, int32_t* out_counts) {
+  if (!ctx || !ix || ix->ctx != ctx) return fail(MANS_ERR_INVALID, "null or foreign IVF-PQ index");
+  if (nq < 0) return fail(MANS_ERR_INVALID, "negative query count");
+  if (nq == 0) return MANS_OK;
+  const int32_t kout = std::max<int32_t>(0, std::min<int32_t>(k, MANS_MAX_TOPK));
+  if (dim != ix->dim) {
+    // _IVFPQIndex.search returns [] for a query of the wrong width (:184-186)
+    for (int64_t i = 0; i < nq * kout; ++i) {
+      out_dist[i] = __builtin_inff();
+      out_ids[i] = MANS_EMPTY_ID;
+    }
+    for (int64_t i = 0; i < nq; ++i) out_counts[i] = 0;
+    return MANS_OK;
+  }
+  if (!queries || !out_dist || !out_ids || !out_counts) return fail(MANS_ERR_INVALID, "null buffer");
+  DeviceGuard g(ctx->device);
+  mans_workspace* ws = acquire_workspace(ctx);
+  if (!ws) return fail(MANS_ERR_OOM, "cannot create a workspace stream");
+  cudaStream_t st = ws->stream;
+  int32_t rc;
+  do {
+    if ((rc = ws->queries.reserve(nq * dim * sizeof(float))) != MANS_OK) break;
+    if ((rc = ws->out_dist.reserve(std::max<int64_t>(1, nq * kout) * sizeof(float))) != MANS_OK) break;
+    if ((rc = ws->out_ids.reserve(std::max<int64_t>(1, nq * kout) * sizeof(uint32_t))) != MANS_OK) break;
+    if ((rc = ws->out_counts.reserve(nq * sizeof(int32_t))) != MANS_OK) break;
+    if ((rc = ws->err.reserve(sizeof(int))) != MANS_OK) break;
+    cudaError_t e = cudaMemcpyAsync(ws->queries.ptr, queries, nq * dim * sizeof(float),
+                                    cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) {
+      rc = fail_cuda(e, "query upload");
+      break;
+    }
+    rc = run_ivfpq_search(ctx, ix, ws, static_cast<const float*>(ws->queries.ptr), nq, k, nprobe,
+                          static_cast<float*>(ws->out_dist.ptr),
+                          static_cast<uint32_t*>(ws->out_ids.ptr),
+                          static_cast<int32_t*>(ws->out_counts.ptr), st);
+    if (rc != MANS_OK) break;
+    if (kout > 0) {
+      e = cudaMemcpyAsync(out_dist, ws->out_dist.ptr, nq * kout * sizeof(float),
+                          cudaMemcpyDeviceToHost, st);
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(out_ids, ws->out_ids.ptr, nq * kout * sizeof(uint32_t),
+                            cudaMemcpyDeviceToHost, st);
+    }
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(out_counts, ws->out_counts.ptr, nq * sizeof(int32_t),
+                          cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) {
+      rc = fail_cuda(e, "result download");
+      break;
+    }
+    rc = check_device_error(ws, st);
+  } while (false);
+  release_workspace(ctx, ws);
+  return rc;
+}
+
+int32_t mans_pq_adc_list(mans_ctx* ctx, const float* query, int64_t dim, const float* codebooks,
+                         int32_t m, int32_t ks, const uint8_t* codes, int64_t count,
+                         float* out_dist) {
+  if (!ctx) return fail(MANS_ERR_INVALID, "null context");
+  if (count < 0) return fail(MANS_ERR_SEARCH, "Vector count must be non-negative");
+  if (m <= 0 || dim <= 0 || dim % m != 0) return fail(MANS_ERR_DIM, "dimensionMismatch");
+  if (count == 0) return MANS_OK;
+  if (ks > 256) return fail(MANS_ERR_SEARCH, "GPU ADC supports at most 256 centroids per subspace");
+  if (!query || !codebooks || !codes || !out_dist) return fail(MANS_ERR_INVALID, "null buffer");
+  for (int64_t i = 0; i < count * m; ++i)
+    if (codes[i] >= ks) return fail(MANS_ERR_SEARCH, "PQ code value out of range");
+  const size_t table = static_cast<size_t>(m) * ks * sizeof(float);
+  if (table > static_cast<size_t>(ctx->max_smem))
+    return fail(MANS_ERR_SEARCH, "PQ distance table exceeds device shared memory");
+  const int sub = static_cast<int>(dim / m);
+  DeviceGuard g(ctx->device);
+  mans_workspace* ws = acquire_workspace(ctx);
+  if (!ws) return fail(MANS_ERR_OOM, "cannot create a workspace stream");
+  cudaStream_t st = ws->stream;
+  int32_t rc = MANS_OK;
+  do {
+    size_t o = 0;
+    const size_t o_q = carve(o, dim * sizeof(float));
+    const size_t o_cb = carve(o, static_cast<size_t>(m) * ks * sub * sizeof(float));
+    const size_t o_c = carve(o, count * m);
+    const size_t o_d = carve(o, count * sizeof(float));
+    if ((rc = ws->aux.reserve(o)) != MANS_OK) break;
+    uint8_t* A = static_cast<uint8_t*>(ws->aux.ptr);
+    cudaError_t e = cudaMemcpyAsync(A + o_q, query, dim * sizeof(float), cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(A + o_cb, codebooks, static_cast<size_t>(m) * ks * sub * sizeof(float),
+                          cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(A + o_c, codes, count * m, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(pq_adc_list_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(table));
+    if (e != cudaSuccess) {
+      rc = fail_cuda(e, "ADC upload");
+      break;
+    }
+    const int64_t blocks = std::min<int64_t>((count + kAdcThreads - 1) / kAdcThreads, 4 * ctx->num_sms);
+    pq_adc_list_kernel<<<static_cast<unsigned>(blocks), kAdcThreads, table, st>>>(
+        reinterpret_cast<float*>(A + o_q), reinterpret_cast<float*>(A + o_cb), m, ks, sub,
+        A + o_c, count, reinterpret_cast<float*>(A + o_d));
+    e = cudaGetLastError();
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(out_dist, A + o_d, count * sizeof(float), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) rc = fail_cuda(e, "ADC execution");
+  } while (false);
+  release_workspace(ctx, ws);
+  return rc;
+}
+
+}  // extern "C"

@@ -1,0 +1,109 @@
+"""IVF-PQ search and single-list ADC over the C ABI.
+
+* ``IVFPQIndex``   -- the search side of ``_IVFPQIndex`` (Sources/MetalANNS/
+                      IVFPQIndex.swift:177-226) over a trained index: coarse
+                      centroids, PQ codebooks, codes per internal id and the
+                      inverted lists in insertion order.
+* ``GPUADCSearch`` -- ``GPUADCSearch.computeDistances`` (Sources/MetalANNSCore/
+                      GPUADCSearch.swift:35-173).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from ._lib import lib
+from .core import MAX_TOP_K, ConstructionFailed, Context, Metric, SearchResult, Workspace, check
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _vp(a):
+    return C.c_void_p(a.ctypes.data)
+
+
+class IVFPQIndex:
+    def __init__(self, context: Context, coarse, codebooks, codes, inverted_lists,
+                 metric: Metric = Metric.l2, list_positions=None):
+        """coarse [nlist, dim]; codebooks [m, 256, dim/m]; codes [n, m] uint8 per
+        internal id; inverted_lists: sequence of id arrays (insertion order) or
+        (offsets, flat_ids)."""
+        coarse = _f32(coarse)
+        codebooks = _f32(codebooks)
+        codes = np.ascontiguousarray(codes, np.uint8)
+        if isinstance(inverted_lists, tuple):
+            offsets, flat = inverted_lists
+        else:
+            sizes = [len(x) for x in inverted_lists]
+            offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+            flat = np.concatenate([np.asarray(x, np.uint32) for x in inverted_lists]) \
+                if len(inverted_lists) else np.zeros(0, np.uint32)
+        offsets = np.ascontiguousarray(offsets, np.int64)
+        flat = np.ascontiguousarray(flat, np.uint32)
+        if codebooks.ndim != 3:
+            raise ConstructionFailed("codebooks must be [m, ks, dim/m]")
+        m, ks, sub = codebooks.shape
+        pos = None if list_positions is None else np.ascontiguousarray(list_positions, np.uint32)
+        h = C.c_void_p()
+        check(lib().mans_ivfpq_create(context.handle, _vp(coarse), coarse.shape[0],
+                                      coarse.shape[1], _vp(codebooks), m, ks, _vp(codes),
+                                      codes.shape[0], _vp(offsets), _vp(flat),
+                                      None if pos is None else _vp(pos), int(metric),
+                                      C.byref(h)))
+        self._h = h
+        self.context = context
+        self.dim = coarse.shape[1]
+        self.nlist = coarse.shape[0]
+
+    @property
+    def handle(self):
+        return self._h
+
+    def search_arrays(self, queries, k: int, nprobe: int):
+        q = _f32(np.atleast_2d(queries))
+        nq, dim = q.shape
+        kout = max(0, min(k, MAX_TOP_K))
+        od = np.empty((nq, kout), np.float32)
+        oi = np.empty((nq, kout), np.uint32)
+        oc = np.empty(nq, np.int32)
+        check(lib().mans_ivfpq_search(self.context.handle, self._h, _vp(q), nq, dim, k, nprobe,
+                                      _vp(od), _vp(oi), _vp(oc)))
+        return od, oi, oc
+
+    def search(self, query, k: int, nprobe: int):
+        od, oi, oc = self.search_arrays([query], k, nprobe)
+        return [SearchResult("", float(od[0, i]), int(oi[0, i])) for i in range(oc[0])]
+
+    def search_device(self, ws: Workspace, d_queries: int, nq: int, k: int, nprobe: int,
+                      d_out_dist: int, d_out_ids: int, d_out_counts: int, stream: int = 0):
+        check(lib().mans_ivfpq_search_device(self.context.handle, self._h, ws.handle,
+                                             C.c_void_p(d_queries), nq, k, nprobe,
+                                             C.c_void_p(d_out_dist), C.c_void_p(d_out_ids),
+                                             C.c_void_p(d_out_counts), C.c_void_p(stream)))
+
+    def close(self):
+        if self._h:
+            lib().mans_ivfpq_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class GPUADCSearch:
+    @staticmethod
+    def compute_distances(context: Context, query, codebooks, codes) -> np.ndarray:
+        q = _f32(query)
+        cb = _f32(codebooks)
+        m, ks, sub = cb.shape
+        codes = np.ascontiguousarray(codes, np.uint8).reshape(-1, m)
+        out = np.empty(codes.shape[0], np.float32)
+        check(lib().mans_pq_adc_list(context.handle, _vp(q), q.shape[0], _vp(cb), m, ks,
+                                     _vp(codes), codes.shape[0], _vp(out)))
+        return out

@@ -1,0 +1,127 @@
+"""GPU parity of IVF-PQ search and single-list ADC against the oracle's
+restatement of _IVFPQIndex.search (coarse BoundedSortedList, residual LUT,
+sequential ADC, newest-first merge) and GPUADCSearch.computeDistances:
+identical internal ids, bit-equal scores, identical tie order.  Cases follow
+Tests/MetalANNSTests/{IVFPQIndexTests,IVFPQGPUTests,GPUADCSearchTests,
+BoundedSelectionTests}.swift."""
+import numpy as np
+import pytest
+
+import bench
+import meltan_b200 as mb
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def encode_all(v, coarse, codebooks, metric):
+    """_IVFPQIndex.add: nearest coarse centroid (strict <) then
+    encode(vector:subtracting:) per vector, lists in insertion order."""
+    nlist = coarse.shape[0]
+    m = codebooks.shape[0]
+    codes = np.zeros((len(v), m), np.uint8)
+    lists = [[] for _ in range(nlist)]
+    for i, x in enumerate(v):
+        c = O.nearest_coarse(x, coarse, metric)
+        codes[i] = O.pq_encode_subtracting(x, coarse[c], codebooks)
+        lists[c].append(i)
+    offsets = np.concatenate([[0], np.cumsum([len(x) for x in lists])]).astype(np.int64)
+    flat = np.array(sum(lists, []), np.uint32)
+    return codes, offsets, flat
+
+
+def make_index(n, dim, m, nlist, metric, seed, dup=False):
+    rng = np.random.default_rng(seed)
+    v, q = bench.make_mixture(n, dim, 16, 20, sigma=0.2, seed=seed)
+    if dup:
+        v = np.repeat(v[: n // 2], 2, axis=0)
+    coarse = v[rng.choice(len(v), nlist, replace=False)].copy()
+    codebooks = (rng.standard_normal((m, 256, dim // m)) * 0.1).astype(np.float32)
+    codes, offsets, flat = encode_all(v, coarse, codebooks, metric)
+    return v, q, coarse, codebooks, codes, offsets, flat
+
+
+def same(got, want):
+    np.testing.assert_array_equal(got[2], want[2])
+    np.testing.assert_array_equal(got[1], want[1])
+    np.testing.assert_array_equal(got[0], want[0])
+
+
+@pytest.mark.parametrize("metric", [O.L2, O.COSINE, O.IP])
+def test_ivfpq_parity(ctx, metric):
+    v, q, coarse, cb, codes, off, flat = make_index(3000, 32, 8, 16, metric, seed=11)
+    ix = mb.IVFPQIndex(ctx, coarse, cb, codes, (off, flat), metric=mb.Metric(metric))
+    for nprobe in (1, 3, 8, 16, 40):
+        for k in (1, 10, 57):
+            same(ix.search_arrays(q, k, nprobe),
+                 O.ivfpq_search(coarse, cb, codes, off, flat, q, k, nprobe, metric))
+    ix.close()
+
+
+def test_ivfpq_duplicates_merge_newest_first(ctx):
+    """BoundedSelectionTests.ivfpqMergeTieOrderPinned (:281-317): duplicate
+    vectors a_i, b_i (b inserted after a) come back b_i before a_i."""
+    v, q, coarse, cb, codes, off, flat = make_index(2000, 16, 4, 4, O.L2, seed=3, dup=True)
+    ix = mb.IVFPQIndex(ctx, coarse, cb, codes, (off, flat))
+    got = ix.search_arrays(v[:5], 6, 4)
+    want = O.ivfpq_search(coarse, cb, codes, off, flat, v[:5], 6, 4, O.L2)
+    same(got, want)
+    for r in range(5):
+        ids = got[1][r].tolist()
+        for a in range(0, 6, 2):
+            assert got[0][r, a] == got[0][r, a + 1]
+            assert ids[a] == ids[a + 1] + 1
+    # massive ties: every code identical -> the order is pure insertion order
+    codes0 = np.zeros_like(codes)
+    ix0 = mb.IVFPQIndex(ctx, coarse, cb, codes0, (off, flat))
+    for k in (1, 5, 37, 256):
+        same(ix0.search_arrays(q[:3], k, 4),
+             O.ivfpq_search(coarse, cb, codes0, off, flat, q[:3], k, 4, O.L2))
+    ix.close()
+    ix0.close()
+
+
+def test_ivfpq_sizes_and_empty_lists(ctx):
+    v, q, coarse, cb, codes, off, flat = make_index(5000, 64, 16, 32, O.L2, seed=5)
+    far = (np.ones((4, 64), np.float32) * 40)
+    coarse2 = np.concatenate([coarse, far])
+    codes2, off2, flat2 = encode_all(v, coarse2, cb, O.L2)
+    assert (np.diff(off2) == 0).any()
+    ix = mb.IVFPQIndex(ctx, coarse2, cb, codes2, (off2, flat2))
+    for nq in (1, 7, 20):
+        same(ix.search_arrays(q[:nq], 10, 36),
+             O.ivfpq_search(coarse2, cb, codes2, off2, flat2, q[:nq], 10, 36, O.L2))
+    assert ix.search_arrays(q[:2, :63], 10, 4)[2].tolist() == [0, 0]  # wrong width -> []
+    assert ix.search(q[0], 0, 4) == []
+    ix.close()
+
+
+def test_gpu_adc_matches_cpu_adc(ctx):
+    """GPUADCSearchTests.swift:10-33 (GPU vs CPU ADC) -- here bit-equal."""
+    rng = np.random.default_rng(9)
+    cb = rng.standard_normal((16, 256, 8)).astype(np.float32)
+    query = rng.standard_normal(128).astype(np.float32)
+    codes = rng.integers(0, 256, (5000, 16)).astype(np.uint8)
+    got = mb.GPUADCSearch.compute_distances(ctx, query, cb, codes)
+    want = O.pq_adc(O.pq_lut(query, cb, O.L2), codes)
+    np.testing.assert_array_equal(got, want)
+    assert mb.GPUADCSearch.compute_distances(ctx, query, cb, codes[:0]).shape == (0,)
+
+
+def test_gpu_adc_rejects_out_of_range_codes(ctx):
+    """GPUADCSearchTests: codes >= Ks are rejected with searchFailed."""
+    rng = np.random.default_rng(1)
+    cb = rng.standard_normal((4, 16, 2)).astype(np.float32)
+    codes = np.array([[1, 2, 3, 20]], np.uint8)
+    with pytest.raises(mb.SearchFailed):
+        mb.GPUADCSearch.compute_distances(ctx, rng.standard_normal(8).astype(np.float32), cb, codes)
+
+
+@pytest.mark.slow
+def test_ivfpq_large(ctx):
+    """200k x 128, nlist 256, m = 16 (scaled-down C4) against the oracle."""
+    v, q = bench.make_mixture(200_000, 128, 256, 12, seed=4)
+    coarse, cb, codes, off, flat = bench.train_ivfpq(v, 256, 16)
+    ix = mb.IVFPQIndex(ctx, coarse, cb, codes, (off, flat))
+    same(ix.search_arrays(q, 10, 32), O.ivfpq_search(coarse, cb, codes, off, flat, q, 10, 32, O.L2))
+    ix.close()
