@@ -145,6 +145,25 @@ int32_t mans_flat_search_device(mans_ctx *ctx, const mans_corpus *corpus, mans_w
                                 float *d_out_dist, uint32_t *d_out_ids, int32_t *d_out_counts,
                                 void *cuda_stream);
 
+/* Exact search with device pointers that allocates nothing.  No counterpart
+ * in the reference: it exists for callers that may not allocate device
+ * memory while searching -- a search recorded into a CUDA graph during stream
+ * capture, a service whose device memory is owned by its own allocator, or a
+ * latency-critical loop that cannot take cudaMalloc's implicit
+ * synchronisation.  Results equal mans_flat_search_device.  Scratch is a
+ * fixed 4 MiB __device__ array held by every GPU that loads the library until
+ * exit; a request whose candidate lists need more (roughly nq x min(k,256)
+ * beyond a few thousand keys per query group) fails with MANS_ERR_OOM and a
+ * message naming the sizes.  The first call on a device resolves the array's
+ * address (cudaGetSymbolAddress) and should come before any stream capture.
+ * All calls on a device share the array: calls whose GPU work may overlap race
+ * and must be serialised by the caller.  The call enqueues on `cuda_stream`
+ * and returns argument and launch errors only. */
+int32_t mans_flat_search_noalloc(mans_ctx *ctx, const mans_corpus *corpus,
+                                 const float *d_queries, int64_t nq, int32_t k, int32_t metric,
+                                 float *d_out_dist, uint32_t *d_out_ids, int32_t *d_out_counts,
+                                 void *cuda_stream);
+
 /* Merges `n_lists` per-shard result blocks (each nq x kin, sorted ascending by
  * (distance, id), laid out list-major: list l at offset l*nq*kin) into the
  * global top-k per query, by (distance, id).  This is the device form of
