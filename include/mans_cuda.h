@@ -83,6 +83,14 @@ int32_t mans_last_error_message(char *buf, size_t buf_len);
 /* Number of streaming multiprocessors of the context's device. */
 int32_t mans_ctx_sm_count(const mans_ctx *ctx);
 
+/* Query batches of at least `min_batch` queries run on the tensor cores
+ * (bf16 tcgen05 candidate GEMM with a certified error bound, then an exact
+ * fp32 re-score, so results are identical to the exact scan); smaller batches
+ * use the exact CUDA-core scan.  0 disables the tensor-core path.  Default 16.
+ * No reference counterpart (the reference has one GPU tier,
+ * FlatGPUSearch.swift:652-707). */
+int32_t mans_ctx_set_tensor_core_batch(mans_ctx *ctx, int32_t min_batch);
+
 /* ---- corpus (VectorBuffer) --------------------------------------------- */
 
 /* Uploads a row-major fp32 corpus (n x dim), the layout of VectorBuffer
@@ -113,6 +121,9 @@ int32_t mans_workspace_destroy(mans_workspace *ws);
 /* Waits for the stream of the last call made with `ws` and reports a device
  * side failure (MANS_ERR_EXEC) recorded by its kernels. */
 int32_t mans_workspace_check(mans_workspace *ws, void *cuda_stream);
+/* Number of queries of the last tensor-core search made with `ws` whose
+ * certificate failed and that were re-scanned exactly (synchronises). */
+int32_t mans_workspace_fallbacks(mans_workspace *ws, int32_t *out);
 
 /* Measurement hooks (no reference counterpart; the reference's benchmark CLI
  * times whole calls, Sources/MetalANNSBenchmarks/HotPathProfiler.swift:22-304).

@@ -128,6 +128,10 @@ class Context:
     def sm_count(self) -> int:
         return lib().mans_ctx_sm_count(self._h)
 
+    def set_tensor_core_batch(self, min_batch: int) -> None:
+        """Batches of >= min_batch queries use the tensor-core path (0: never)."""
+        check(lib().mans_ctx_set_tensor_core_batch(self._h, min_batch))
+
     def close(self):
         if self._h:
             lib().mans_ctx_destroy(self._h)
@@ -203,6 +207,11 @@ class Workspace:
 
     def check(self, stream_ptr: int = 0) -> None:
         check(lib().mans_workspace_check(self._h, C.c_void_p(stream_ptr)))
+
+    def fallbacks(self) -> int:
+        out = C.c_int32()
+        check(lib().mans_workspace_fallbacks(self._h, C.byref(out)))
+        return out.value
 
     def set_timing(self, enable: bool) -> None:
         check(lib().mans_workspace_set_timing(self._h, 1 if enable else 0))

@@ -207,6 +207,17 @@ int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace
   const int32_t kout = std::min<int32_t>(k, kcap);
   const int64_t n = corpus->n;
   if (nq <= 0) return MANS_OK;
+  if (mode == kModeHost && kcap == MANS_MAX_TOPK && ctx->tc_min_batch > 0 &&
+      nq >= ctx->tc_min_batch && k > 0 && n > 0 && !corpus->ids) {
+    mans_corpus* c = const_cast<mans_corpus*>(corpus);
+    std::unique_lock<std::mutex> lk(c->tc_mu);
+    int32_t rc = tc_prepare_corpus(c, metric);
+    lk.unlock();
+    if (rc != MANS_OK) return rc;
+    if (tc_applicable(c, metric))
+      return run_flat_search_tc(ctx, c, ws, d_queries, nq, k, metric, d_out_dist, d_out_ids,
+                                d_out_counts, stream);
+  }
   if (k <= 0 || n <= 0) {
     if (kout <= 0) {
       cudaError_t e = cudaMemsetAsync(d_out_counts, 0, sizeof(int32_t) * nq, stream);
@@ -336,6 +347,7 @@ int32_t corpus_upload(mans_ctx* ctx, const float* rows, int64_t n, int64_t dim, 
 
 void corpus_free(mans_corpus* c) {
   if (!c) return;
+  tc_free_corpus(c);
   if (c->owned) {
     if (c->rows) cudaFree(c->rows);
     if (c->norms) cudaFree(c->norms);
@@ -410,6 +422,22 @@ int32_t mans_ctx_destroy(mans_ctx* ctx) {
 
 int32_t mans_ctx_sm_count(const mans_ctx* ctx) { return ctx ? ctx->num_sms : 0; }
 
+int32_t mans_ctx_set_tensor_core_batch(mans_ctx* ctx, int32_t min_batch) {
+  if (!ctx) return fail(MANS_ERR_INVALID, "null context");
+  if (min_batch < 0) return fail(MANS_ERR_INVALID, "negative batch size");
+  ctx->tc_min_batch = min_batch;
+  return MANS_OK;
+}
+
+int32_t mans_workspace_fallbacks(mans_workspace* ws, int32_t* out) {
+  if (!ws || !out) return fail(MANS_ERR_INVALID, "null workspace or output");
+  *out = 0;
+  if (!ws->tc_fallbacks) return MANS_OK;
+  DeviceGuard g(ws->ctx->device);
+  cudaError_t e = cudaMemcpy(out, ws->tc_fallbacks, sizeof(int32_t), cudaMemcpyDeviceToHost);
+  return e == cudaSuccess ? MANS_OK : fail_cuda(e, "fallback counter readback");
+}
+
 int32_t mans_corpus_create(mans_ctx* ctx, const float* rows, int64_t n, int64_t dim,
                            uint32_t id_offset, mans_corpus** out_corpus) {
   if (!ctx || !out_corpus) return fail(MANS_ERR_INVALID, "null context or output");
@@ -424,6 +452,11 @@ int32_t mans_corpus_update_rows(mans_corpus* c, int64_t start, const float* rows
   if (count == 0) return MANS_OK;
   if (!rows) return fail(MANS_ERR_INVALID, "rows is null");
   DeviceGuard g(c->ctx->device);
+  {
+    std::lock_guard<std::mutex> lk(c->tc_mu);
+    cudaDeviceSynchronize();
+    tc_free_corpus(c);  // the bf16 copy and its bound terms are rebuilt on next use
+  }
   float* dst = c->rows + start * c->ld;
   cudaError_t e = cudaMemcpy2D(dst, c->ld * sizeof(float), rows, c->dim * sizeof(float),
                                c->dim * sizeof(float), count, cudaMemcpyHostToDevice);

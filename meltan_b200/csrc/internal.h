@@ -9,6 +9,8 @@
 #include <string>
 #include <vector>
 
+#include "tc.h"
+
 struct mans_workspace;
 
 namespace mans {
@@ -45,6 +47,8 @@ struct mans_ctx {
   int max_smem = 0;
   std::mutex mu;
   std::vector<mans_workspace*> pool;  // idle workspaces for host-pointer calls
+  // query batches of at least this size use the tensor-core path (0: never)
+  int tc_min_batch = 16;
 };
 
 // Row-major fp32 rows with a 16-byte pitch (ld = dim rounded up to 4), the
@@ -60,6 +64,18 @@ struct mans_corpus {
   uint32_t* ids = nullptr;  // optional row -> reported id (packed IVF lists)
   bool owned = true;        // rows/norms/ids freed with the object
   CUtensorMap map;
+  // bf16 copy and error-bound terms for the tensor-core batch path (built on
+  // first use, dropped when rows change)
+  std::mutex tc_mu;
+  bool tc_ready = false;
+  int tc_metric = -1;
+  void* tc_rows = nullptr;
+  int64_t tc_ld16 = 0;
+  float* tc_stats = nullptr;  // n x 4: |r|, |r - r~|, |r~|, |r| rounded down
+  float* tc_beta = nullptr;
+  float* tc_delta = nullptr;
+  mans::TcCorpusStats tc_stats_host{};
+  CUtensorMap tc_map;
 };
 
 struct mans_workspace {
@@ -83,6 +99,7 @@ struct mans_workspace {
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> events;
   size_t events_used = 0;
   int64_t launches = 0;  // library kernels enqueued through this workspace
+  int32_t* tc_fallbacks = nullptr;  // device counter of exact re-scans (last tc call)
 };
 
 namespace mans {
@@ -98,6 +115,14 @@ void timing_end(cudaEvent_t stop, cudaStream_t stream);
 int32_t corpus_upload(mans_ctx* ctx, const float* rows, int64_t n, int64_t dim, uint32_t id_offset,
                       mans_corpus** out);
 void corpus_free(mans_corpus* c);
+// tensor-core batch path (tc_scan.cu)
+int32_t tc_prepare_corpus(mans_corpus* c, int metric);
+bool tc_applicable(const mans_corpus* c, int metric);
+int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* ws,
+                           const float* d_queries, int64_t nq, int32_t k, int32_t metric,
+                           float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
+                           cudaStream_t stream);
+void tc_free_corpus(mans_corpus* c);
 // Exact scan + top-k over `corpus`.  mode: kModeHost (host-tier distance) or
 // kModeSimd (SIMDDistance semantics).  kcap bounds k (256 for the public
 // searches; 512 for the internal 2k candidate lists of the IVF-PQ stages).

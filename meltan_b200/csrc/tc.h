@@ -1,0 +1,41 @@
+// tc.h -- parameters of the tensor-core (tcgen05) batched exact search.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mans {
+
+// One pass of the bf16 candidate GEMM over rows [row0, row0 + rows).
+struct TcParams {
+  int64_t row0;
+  int64_t rows;
+  int64_t nq;
+  int32_t dim;
+  int32_t qblocks;          // ceil(nq / 256)
+  const float* row_beta;    // per-row additive term (L2: |r|^2), may be null
+  const float* row_delta;   // per-row factor (cosine: 1/|r|), may be null
+  const float* q_alpha;     // per-query additive term
+  const float* q_gamma;     // per-query factor of the dot
+  const float* q_thr;       // filter threshold (filter mode)
+  float* dense_out;         // dense mode: dense_out[q * dense_ld + (row - row0)]
+  int64_t dense_ld;
+  uint64_t* cand;           // filter mode: (distance, row) keys, cand_cap per query
+  int32_t* cand_count;
+  int32_t cand_cap;
+  int* err;
+};
+
+// Corpus-wide terms of the error bound (maxima over rows, rounded up).
+struct TcCorpusStats {
+  float max_norm;       // max |r|
+  float max_resid;      // max |r - bf16(r)|
+  float max_norm_bf16;  // max |bf16(r)|
+  float min_norm;       // min |r|
+  float max_inv_norm;   // max 1/|r| over rows (cosine)
+  float max_sqnorm;     // max |r|^2 (L2)
+};
+
+}  // namespace mans

@@ -1,0 +1,877 @@
+// tc_scan.cu -- large-batch exact flat search on the tensor cores.
+//
+// For query batches the exact CUDA-core scan (scan.cu) becomes FP32-issue
+// bound, so batches run as the dense contraction they are: a tcgen05 bf16 GEMM
+// produces approximate distances, a certified error bound turns them into a
+// candidate set that provably contains the exact top-k, and the candidates are
+// re-scored with the exact fp32 arithmetic of the reference CPU path
+// (sequential dot, dots.c:40-47; host-tier finalize, ParallelFlatScan.swift
+// :237-258).  Results therefore equal the exact scan's bit for bit.
+//
+// Per query q and row r let s = dot(q, r) (real), s~ the bf16 tensor-core dot.
+//   |s~ - s| <= |q - q~| |r| + |q~| |r - r~| + c_acc |q~| |r~|      (Cauchy-Schwarz)
+// with q~, r~ the bf16 roundings and c_acc bounding the fp32 accumulation.
+// The distance is affine in s per (q, r) -- IP: -s; L2: |q|^2 - 2s + |r|^2;
+// cosine: 1 - s / (|q| |r|) -- so with corpus-wide maxima the approximate
+// distance d~ and the exact fp32 distance d obey |d~ - d| <= eps_q.  If T_k is
+// the k-th smallest d~ over all rows, a row with d~ > T_k + 2 eps_q has
+// d > T_k + eps_q >= (k-th smallest d): it cannot be in the exact top-k, ties
+// included.
+//
+// Pipeline per batch:
+//   1. query prep: bf16 queries, exact |q|^2 (sequential), eps_q, affine terms;
+//   2. sample pass: GEMM over the first S rows writing d~ densely;
+//   3. per query: thr_q = (k-th smallest d~ of the sample) + 2 eps_q, which
+//      is >= T_k + 2 eps_q because the sample is a subset;
+//   4. full pass: GEMM over all rows, the epilogue appends (d~, row) when
+//      d~ <= thr_q;
+//   5. per query: T_k from the candidates, exact re-score of those with
+//      d~ <= T_k + 2 eps_q, (distance, id) top-k.  A query whose candidate
+//      list overflowed or whose certificate fails is re-scanned exactly by
+//      its block (slow, rare, still exact).
+//
+// GEMM layout (tcgen05 kind::f16, one CTA per SM, persistent over tiles):
+//   A = 128 corpus rows x 64 bf16 (K-major, 128-byte swizzle), B = 256 queries
+//   x 64 bf16, D = 128 x 256 fp32 in TMEM, two accumulators (512 columns) so
+//   the epilogue of one tile overlaps the MMAs of the next.  Warp 0 lane 0
+//   issues TMA, warp 1 lane 0 issues MMAs and commits, warps 4-7 read TMEM
+//   (TMEM lane = corpus row) in the epilogue.  No multicast anywhere.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+#include "kernels.h"
+#include "mans_cuda.h"
+#include "tc.h"
+
+namespace mans {
+namespace {
+
+constexpr int kBM = 128;   // corpus rows per tile (MMA M)
+constexpr int kBN = 256;   // queries per tile (MMA N)
+constexpr int kBK = 64;    // bf16 per 128-byte swizzle row
+constexpr int kStages = 4;
+constexpr int kABytes = kBM * kBK * 2;  // 16 KiB
+constexpr int kBBytes = kBN * kBK * 2;  // 32 KiB
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kTcThreads = 256;
+constexpr int kTmemCols = 512;
+constexpr int kRerankThreads = 256;
+constexpr int kMaxRerank = 2048;  // exact re-score list per query
+
+// ---- tcgen05 wrappers (inline PTX) ------------------------------------------
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, int ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols));
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, int ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (bf16 in, fp32 accumulate)
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+// arrive on `bar` once every MMA previously issued by this thread completed
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor of a K-major operand with 128-byte swizzle:
+// rows of 128 B, 8-row core groups 1024 B apart (SBO = 64 x 16 B), LBO field 1,
+// descriptor version 1 (bits 46-47), layout type 2 = SWIZZLE_128B (bits 61-63).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A bf16 (7-9 = 1),
+// B bf16 (10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* err,
+                                        volatile int* abort) {
+  if (*abort) return false;
+  if (mbar_wait_bounded(bar, parity, err)) return true;
+  *abort = 1;
+  return false;
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_scan_kernel(const __grid_constant__ CUtensorMap map_a,
+                   const __grid_constant__ CUtensorMap map_b, const TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<size_t>(smem_raw) + 1023) / 1024 * 1024);
+  uint8_t* stages = base;
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* qpar = reinterpret_cast<float*>(tmem_slot + 4);  // [2][3][kBN]: alpha, gamma, thr
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int nk = (p.dim + kBK - 1) / kBK;
+  const int64_t row_tiles = (p.rows + kBM - 1) / kBM;
+  const int64_t units = row_tiles * p.qblocks;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (tid == 64) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t issued = 0;
+      for (int64_t u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
+        const int64_t rt = u / p.qblocks;
+        const int32_t qb = static_cast<int32_t>(u - rt * p.qblocks);
+        const int32_t y = static_cast<int32_t>(p.row0 + rt * kBM);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!tc_wait(&empty[stage], phase ^ 1u, p.err, abort)) break;
+          uint8_t* st = stages + stage * kStageBytes;
+          mbar_arrive_expect_tx(&full[stage], kStageBytes);
+          tma_load_2d(st, &map_a, kb * kBK, y, &full[stage]);
+          tma_load_2d(st + kABytes, &map_b, kb * kBK, qb * kBN, &full[stage]);
+          ++issued;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // after an abort, wait (bounded) for the copies still in flight
+      if (*abort) {
+        for (int64_t i = issued > kStages ? issued - kStages : 0; i < issued; ++i)
+          mbar_wait_bounded(&full[i % kStages], static_cast<uint32_t>((i / kStages) & 1), nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t idesc = idesc_bf16(kBM, kBN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int64_t u = blockIdx.x; u < units && !*abort; u += gridDim.x, ++local) {
+        const int b = local & 1;
+        const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+        if (!tc_wait(&acc_empty[b], acc_phase ^ 1u, p.err, abort)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(b * kBN);
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!tc_wait(&full[stage], phase, p.err, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(stages + stage * kStageBytes);
+          const uint64_t adesc = smem_desc_sw128(sa);
+          const uint64_t bdesc = smem_desc_sw128(sa + kABytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            tc_mma(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+          tc_commit(&empty[stage]);  // frees the smem stage once these MMAs finish
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[b]);  // accumulator ready for the epilogue
+      }
+      // every MMA issued by this thread has completed once `drain` flips
+      tc_commit(drain);
+      mbar_wait_bounded(drain, 0, nullptr);
+    }
+  } else if (warp >= 4) {
+    // ---------------- epilogue: TMEM -> approximate distances ----------------
+    const int quarter = warp & 3;  // this warp reads TMEM lanes 32*quarter .. +31
+    const int et = tid - 128;      // 0..127
+    // The four epilogue warps meet at a named barrier every tile, so they must
+    // leave the loop together: they do not poll the abort flag (a flag set
+    // between their loop tests could split them) and only stop when their own
+    // bounded wait on the accumulator barrier gives up, which happens to all
+    // four on the same tile.
+    int local = 0;
+    for (int64_t u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+      const int64_t rt = u / p.qblocks;
+      const int32_t qb = static_cast<int32_t>(u - rt * p.qblocks);
+      const int b = local & 1;
+      const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+      // stage this tile's per-query terms (double-buffered by accumulator)
+      float* qa = qpar + b * 3 * kBN;
+      for (int i = et; i < kBN; i += 128) {
+        const int64_t q = static_cast<int64_t>(qb) * kBN + i;
+        const bool in = q < p.nq;
+        qa[i] = in ? p.q_alpha[q] : 0.0f;
+        qa[kBN + i] = in ? p.q_gamma[q] : 0.0f;
+        qa[2 * kBN + i] = (in && !p.dense_out) ? p.q_thr[q] : -__int_as_float(0x7F800000);
+      }
+      named_sync(1, 128);
+      if (!mbar_wait_bounded(&acc_full[b], acc_phase, p.err)) {
+        *abort = 1;
+        break;
+      }
+      tc_fence_after();
+      const int64_t lrow = rt * kBM + quarter * 32 + lane;  // row within the pass
+      const bool valid = lrow < p.rows;
+      const int64_t row = p.row0 + lrow;
+      float beta = 0.0f, delta = 1.0f;
+      if (valid) {
+        if (p.row_beta) beta = __ldg(p.row_beta + row);
+        if (p.row_delta) delta = __ldg(p.row_delta + row);
+      }
+      const uint32_t taddr =
+          tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(b * kBN);
+      const int64_t qleft = p.nq - static_cast<int64_t>(qb) * kBN;
+      const int qcols = qleft < kBN ? static_cast<int>(qleft) : kBN;
+      for (int c = 0; c < kBN / 32; ++c) {
+        float v[32];
+        tmem_ld32(taddr + c * 32, v);
+        if (!valid || c * 32 >= qcols) continue;
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const int j = c * 32 + t;
+          const float dist = qa[j] + beta - qa[kBN + j] * delta * v[t];
+          const int64_t q = static_cast<int64_t>(qb) * kBN + j;
+          if (j < qcols) {
+            if (p.dense_out) {
+              p.dense_out[q * p.dense_ld + lrow] = dist;
+            } else if (dist <= qa[2 * kBN + j]) {
+              const int pos = atomicAdd(p.cand_count + q, 1);
+              if (pos < p.cand_cap)
+                p.cand[q * p.cand_cap + pos] = make_key(dist, static_cast<uint32_t>(row));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+// fp32 rows -> bf16 rows (round to nearest even), one warp per row, with the
+// per-row error-bound terms |r|, |r - r~|, |r~| (double sums, rounded up).
+__global__ void to_bf16_rows_kernel(const float* __restrict__ rows, int64_t n, int32_t dim,
+                                    int64_t ld, __nv_bfloat16* __restrict__ out, int64_t ld16,
+                                    float* __restrict__ stats) {
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= n) return;
+  double nr = 0.0, nres = 0.0, nt = 0.0;
+  for (int c = lane; c < ld16; c += 32) {
+    const float x = c < dim ? rows[r * ld + c] : 0.0f;
+    const __nv_bfloat16 b = __float2bfloat16_rn(x);
+    out[r * ld16 + c] = b;
+    const double xb = static_cast<double>(__bfloat162float(b));
+    const double xx = static_cast<double>(x);
+    nr += xx * xx;
+    nres += (xx - xb) * (xx - xb);
+    nt += xb * xb;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    nr += __shfl_xor_sync(0xFFFFFFFFu, nr, o);
+    nres += __shfl_xor_sync(0xFFFFFFFFu, nres, o);
+    nt += __shfl_xor_sync(0xFFFFFFFFu, nt, o);
+  }
+  if (lane == 0) {
+    stats[r * 4 + 0] = __double2float_ru(sqrt(nr) * (1.0 + 1e-9));
+    stats[r * 4 + 1] = __double2float_ru(sqrt(nres) * (1.0 + 1e-9));
+    stats[r * 4 + 2] = __double2float_ru(sqrt(nt) * (1.0 + 1e-9));
+    stats[r * 4 + 3] = __double2float_rd(sqrt(nr) * (1.0 - 1e-9));
+  }
+}
+
+// Per-row affine terms of the approximate distance: L2 beta = |r|^2 (the
+// exact fp32 norm), cosine delta = 1/|r|.
+__global__ void row_affine_kernel(const float* __restrict__ norms, const float* __restrict__ stats,
+                                  int64_t n, int metric, float* __restrict__ beta,
+                                  float* __restrict__ delta) {
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  beta[r] = metric == kL2 ? norms[r] : 0.0f;
+  const float lo = stats[r * 4 + 3];
+  delta[r] = metric == kCosine ? (lo > 0.0f ? 1.0f / lo : 0.0f) : 1.0f;
+}
+
+struct TcQueryParams {
+  const float* queries;  // nq x dim fp32
+  int64_t nq;
+  int32_t dim;
+  int64_t ld16;
+  int metric;
+  TcCorpusStats cs;
+  __nv_bfloat16* qbf;  // nq_pad x ld16
+  float* qn_exact;     // nq, sequential |q|^2
+  float* alpha;
+  float* gamma;
+  float* eps;
+};
+
+// One warp per query: bf16 copy, exact squared norm in index order, the
+// affine terms and the certified bound eps_q of |d~ - d|.
+__global__ void tc_query_prep_kernel(const TcQueryParams p) {
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (q >= p.nq) return;
+  const float* v = p.queries + q * p.dim;
+  double nq2 = 0.0, nres = 0.0, nt = 0.0;
+  float acc = 0.0f;
+  for (int c0 = 0; c0 < p.ld16; c0 += 32) {
+    const int c = c0 + lane;
+    const float x = c < p.dim ? v[c] : 0.0f;
+    if (c < p.ld16) {
+      const __nv_bfloat16 b = __float2bfloat16_rn(x);
+      p.qbf[q * p.ld16 + c] = b;
+      const double xb = __bfloat162float(b), xx = x;
+      nq2 += xx * xx;
+      nres += (xx - xb) * (xx - xb);
+      nt += xb * xb;
+    }
+    const int cnt = min(32, p.dim - c0);
+    for (int l = 0; l < cnt; ++l) {
+      const float y = __shfl_sync(0xFFFFFFFFu, x, l);
+      acc = __fadd_rn(acc, __fmul_rn(y, y));
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    nq2 += __shfl_xor_sync(0xFFFFFFFFu, nq2, o);
+    nres += __shfl_xor_sync(0xFFFFFFFFu, nres, o);
+    nt += __shfl_xor_sync(0xFFFFFFFFu, nt, o);
+  }
+  if (lane != 0) return;
+  const double qnorm = sqrt(nq2), qres = sqrt(nres), qt = sqrt(nt);
+  // fp32 accumulation in the tensor core and in the exact sequential path:
+  // generously dim * 2^-22 of the magnitude sum each
+  const double cacc = static_cast<double>(p.dim) * 2.384185791015625e-07;
+  const double es = qres * p.cs.max_norm + qt * p.cs.max_resid +
+                    cacc * qt * p.cs.max_norm_bf16 + cacc * qnorm * p.cs.max_norm;
+  double alpha = 0.0, gamma = 1.0, lip = 1.0, mag;
+  if (p.metric == kL2) {
+    alpha = acc;
+    gamma = 2.0;
+    lip = 2.0;
+    mag = acc + p.cs.max_sqnorm + 2.0 * (qnorm * p.cs.max_norm + es);
+  } else if (p.metric == kCosine) {
+    alpha = 1.0;
+    gamma = qnorm > 0.0 ? 1.0 / qnorm : 0.0;
+    lip = gamma * p.cs.max_inv_norm;
+    mag = 1.0 + lip * (qnorm * p.cs.max_norm + es);
+  } else {
+    mag = qnorm * p.cs.max_norm + es;
+  }
+  // rounding of both distance formulas: 64 ulps of the largest magnitude
+  const double slack = mag * 64.0 * 5.960464477539063e-08 + 1e-30;
+  p.qn_exact[q] = acc;
+  p.alpha[q] = static_cast<float>(alpha);
+  p.gamma[q] = static_cast<float>(gamma);
+  p.eps[q] = static_cast<float>((lip * es + slack) * (1.0 + 1e-6));
+}
+
+// Per query: thr_q = (k-th smallest approximate distance of the dense sample)
+// + 2 eps_q, or +inf when the sample has fewer than k rows.
+__global__ void __launch_bounds__(kMergeThreads) tc_threshold_kernel(
+    const float* __restrict__ dense, int64_t ld, int64_t rows, int32_t k, int32_t kp,
+    const float* __restrict__ eps, float* __restrict__ thr_out) {
+  __shared__ uint64_t buf[kSortN];
+  __shared__ uint64_t thr;
+  __shared__ int qc, nb;
+  const int tid = threadIdx.x;
+  const int64_t q = blockIdx.x;
+  if (tid == 0) {
+    thr = kKeyMax;
+    qc = 0;
+    nb = 0;
+  }
+  __syncthreads();
+  TopKState st{buf, &qc, &nb, &thr};
+  for (int64_t b = 0; b < rows; b += kMergeThreads) {
+    const int64_t r = b + tid;
+    const bool valid = r < rows;
+    const uint64_t key = valid ? make_key(dense[q * ld + r], static_cast<uint32_t>(r)) : kKeyMax;
+    topk_offer(st, kp, key, valid);
+    __syncthreads();
+    if (qc > kSortN - kp - kMergeThreads) topk_merge<kMergeThreads>(st, k, kp, kSortN, tid, 0);
+  }
+  if (qc > 0) topk_merge<kMergeThreads>(st, k, kp, kSortN, tid, 0);
+  if (tid == 0) {
+    // same rounding-safe widening as the band in tc_rerank_kernel, so that
+    // band <= thr whenever T_k <= the sample's k-th distance
+    float t = __int_as_float(0x7F800000);
+    if (nb >= k) {
+      t = key_distance(buf[k - 1]) + 2.0f * eps[q];
+      t = t + fabsf(t) * 1e-6f;
+    }
+    thr_out[q] = t;
+  }
+}
+
+struct RerankParams {
+  const uint64_t* cand;
+  const int32_t* cand_count;
+  int32_t cand_cap;
+  const float* thr;
+  const float* eps;
+  const float* qn_exact;
+  const float* queries;  // fp32 nq x dim
+  const float* rows;     // fp32 corpus, ld pitch
+  int64_t ld;
+  const float* norms;
+  int64_t n;
+  int32_t dim;
+  int32_t metric;
+  uint32_t id_offset;
+  int32_t k;   // effective k
+  int32_t kp;
+  int32_t kout;
+  float* out_dist;
+  uint32_t* out_ids;
+  int32_t* out_counts;
+  int32_t* fallbacks;  // count of queries re-scanned exactly
+};
+
+// Exact distance of one corpus row in the reference order.
+__device__ __forceinline__ float exact_distance(const RerankParams& p, const float* q, float qn,
+                                                int64_t row) {
+  const float* r = p.rows + row * p.ld;
+  float acc = 0.0f;
+  for (int c = 0; c < p.dim; ++c) acc = __fadd_rn(acc, __fmul_rn(__ldg(r + c), q[c]));
+  return finalize_distance(p.metric, acc, qn, p.metric == kIP ? 0.0f : __ldg(p.norms + row));
+}
+
+__global__ void __launch_bounds__(kRerankThreads) tc_rerank_kernel(const RerankParams p) {
+  extern __shared__ float qsm[];  // query, dim floats
+  __shared__ uint64_t buf[kSortN];
+  __shared__ uint64_t thr;
+  __shared__ int qc, nb, fail_flag, nlist;
+  __shared__ uint32_t list[kMaxRerank];
+  const int tid = threadIdx.x;
+  const int64_t q = blockIdx.x;
+  for (int c = tid; c < p.dim; c += kRerankThreads) qsm[c] = p.queries[q * p.dim + c];
+  const int total = p.cand_count[q];
+  const int cnt = min(total, p.cand_cap);
+  const float e = p.eps[q];
+  const float qn = p.qn_exact[q];
+  if (tid == 0) {
+    thr = kKeyMax;
+    qc = 0;
+    nb = 0;
+    nlist = 0;
+    fail_flag = total > p.cand_cap ? 1 : 0;
+  }
+  __syncthreads();
+  TopKState st{buf, &qc, &nb, &thr};
+  const uint64_t* cq = p.cand + q * p.cand_cap;
+  float band = 0.0f;
+  if (!fail_flag) {
+    // T_k: k-th smallest approximate distance among the candidates
+    for (int b = 0; b < cnt; b += kRerankThreads) {
+      const int i = b + tid;
+      const bool valid = i < cnt;
+      topk_offer(st, p.kp, valid ? cq[i] : kKeyMax, valid);
+      __syncthreads();
+      if (qc > kSortN - p.kp - kRerankThreads) topk_merge<kRerankThreads>(st, p.k, p.kp, kSortN, tid, 0);
+    }
+    if (qc > 0) topk_merge<kRerankThreads>(st, p.k, p.kp, kSortN, tid, 0);
+    if (tid == 0) {
+      if (nb < p.k) {
+        fail_flag = 1;  // fewer candidates than k: the sample threshold was too tight
+      } else {
+        const float tk = key_distance(buf[p.k - 1]);
+        band = tk + 2.0f * e;
+        band = band + fabsf(band) * 1e-6f;
+        if (!(band <= p.thr[q])) fail_flag = 1;  // filter did not cover the band
+        thr = __float_as_uint(band);  // pass the band through shared memory
+      }
+    }
+    __syncthreads();
+  }
+  if (!fail_flag) {
+    band = __uint_as_float(static_cast<uint32_t>(thr));
+    // rows within the band
+    for (int i = tid; i < cnt; i += kRerankThreads) {
+      if (key_distance(cq[i]) <= band) {
+        const int pos = atomicAdd(&nlist, 1);
+        if (pos < kMaxRerank) list[pos] = key_id(cq[i]);
+      }
+    }
+    __syncthreads();
+    if (nlist > kMaxRerank) fail_flag = 1;
+    __syncthreads();
+  }
+  if (tid == 0) {
+    thr = kKeyMax;
+    qc = 0;
+    nb = 0;
+  }
+  __syncthreads();
+  if (!fail_flag) {
+    // exact re-score of the band, (distance, id) top-k
+    const int m = nlist;
+    for (int b = 0; b < m; b += kRerankThreads) {
+      const int i = b + tid;
+      const bool valid = i < m;
+      uint64_t key = kKeyMax;
+      if (valid) {
+        const int64_t row = list[i];
+        key = make_key(exact_distance(p, qsm, qn, row), static_cast<uint32_t>(row + p.id_offset));
+      }
+      topk_offer(st, p.kp, key, valid);
+      __syncthreads();
+      if (qc > kSortN - p.kp - kRerankThreads) topk_merge<kRerankThreads>(st, p.k, p.kp, kSortN, tid, 0);
+    }
+  } else {
+    // certificate failed: exact scan of every row by this block
+    if (tid == 0) atomicAdd(p.fallbacks, 1);
+    for (int64_t b = 0; b < p.n; b += kRerankThreads) {
+      const int64_t row = b + tid;
+      const bool valid = row < p.n;
+      uint64_t key = kKeyMax;
+      if (valid) key = make_key(exact_distance(p, qsm, qn, row), static_cast<uint32_t>(row + p.id_offset));
+      topk_offer(st, p.kp, key, valid);
+      __syncthreads();
+      if (qc > kSortN - p.kp - kRerankThreads) topk_merge<kRerankThreads>(st, p.k, p.kp, kSortN, tid, 0);
+    }
+  }
+  if (qc > 0) topk_merge<kRerankThreads>(st, p.k, p.kp, kSortN, tid, 0);
+  for (int i = tid; i < p.kout; i += kRerankThreads) {
+    const bool have = i < nb;
+    p.out_dist[q * p.kout + i] = have ? key_distance(buf[i]) : __int_as_float(0x7F800000);
+    p.out_ids[q * p.kout + i] = have ? key_id(buf[i]) : kEmptyId;
+  }
+  if (tid == 0) p.out_counts[q] = nb;
+}
+
+size_t tc_smem_bytes() {
+  return 1024 + static_cast<size_t>(kStages) * kStageBytes + 8 * (2 * kStages + 5) + 16 +
+         2 * 3 * kBN * sizeof(float);
+}
+
+int32_t encode_bf16_map(CUtensorMap* map, const void* base, int64_t rows, int64_t dim,
+                        int64_t ld16, int box_rows) {
+  auto enc_ptr = [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<void*>(nullptr);
+    return fn;
+  };
+  static void* fn = enc_ptr();
+  if (!fn) return fail(MANS_ERR_PIPELINE, "cuTensorMapEncodeTiled is unavailable");
+  using Enc = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                           const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                           CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                           CUtensorMapFloatOOBfill);
+  cuuint64_t gdim[2] = {static_cast<cuuint64_t>(dim), static_cast<cuuint64_t>(std::max<int64_t>(rows, 1))};
+  cuuint64_t gstride[1] = {static_cast<cuuint64_t>(ld16) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = reinterpret_cast<Enc>(fn)(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                                         const_cast<void*>(base), gdim, gstride, box, estride,
+                                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MANS_ERR_PIPELINE, "bf16 tensor map encoding failed");
+  return MANS_OK;
+}
+
+}  // namespace
+
+// Builds (once per corpus and metric) the bf16 copy and the bound terms.
+int32_t tc_prepare_corpus(mans_corpus* c, int metric) {
+  if (c->tc_ready && c->tc_metric == metric) return MANS_OK;
+  DeviceGuard g(c->ctx->device);
+  const int64_t n = c->n;
+  const int64_t ld16 = (c->dim + 7) / 8 * 8;
+  if (!c->tc_rows) {
+    cudaError_t e = cudaMalloc(&c->tc_rows, std::max<int64_t>(n, 1) * ld16 * sizeof(__nv_bfloat16));
+    if (e == cudaSuccess) e = cudaMalloc(&c->tc_stats, std::max<int64_t>(n, 1) * 4 * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&c->tc_beta, std::max<int64_t>(n, 1) * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&c->tc_delta, std::max<int64_t>(n, 1) * sizeof(float));
+    if (e != cudaSuccess) return fail_cuda(e, "cudaMalloc(bf16 corpus)");
+    c->tc_ld16 = ld16;
+    if (n > 0) {
+      to_bf16_rows_kernel<<<static_cast<unsigned>((n + 7) / 8), 256>>>(
+          c->rows, n, static_cast<int32_t>(c->dim), c->ld,
+          static_cast<__nv_bfloat16*>(c->tc_rows), ld16, c->tc_stats);
+      e = cudaGetLastError();
+      if (e == cudaSuccess) e = cudaDeviceSynchronize();
+      if (e != cudaSuccess) return fail_cuda(e, "bf16 corpus conversion");
+    }
+    // corpus-wide maxima of the bound terms (host reduction, once)
+    std::vector<float> st(static_cast<size_t>(std::max<int64_t>(n, 1)) * 4);
+    if (n > 0) {
+      e = cudaMemcpy(st.data(), c->tc_stats, n * 4 * sizeof(float), cudaMemcpyDeviceToHost);
+      if (e != cudaSuccess) return fail_cuda(e, "bf16 corpus stats");
+    }
+    TcCorpusStats cs{};
+    cs.min_norm = n > 0 ? INFINITY : 0.0f;
+    for (int64_t r = 0; r < n; ++r) {
+      cs.max_norm = std::max(cs.max_norm, st[r * 4 + 0]);
+      cs.max_resid = std::max(cs.max_resid, st[r * 4 + 1]);
+      cs.max_norm_bf16 = std::max(cs.max_norm_bf16, st[r * 4 + 2]);
+      cs.min_norm = std::min(cs.min_norm, st[r * 4 + 3]);
+      if (st[r * 4 + 3] > 0.0f) cs.max_inv_norm = std::max(cs.max_inv_norm, 1.0f / st[r * 4 + 3]);
+      const double sq = static_cast<double>(st[r * 4 + 0]) * st[r * 4 + 0];
+      cs.max_sqnorm = std::max(cs.max_sqnorm, static_cast<float>(sq * (1.0 + 1e-6)));
+    }
+    cs.max_inv_norm *= 1.0f + 1e-6f;
+    c->tc_stats_host = cs;
+    int32_t rc = encode_bf16_map(&c->tc_map, c->tc_rows, n, c->dim, ld16, kBM);
+    if (rc != MANS_OK) return rc;
+  }
+  if (n > 0) {
+    row_affine_kernel<<<static_cast<unsigned>((n + 255) / 256), 256>>>(
+        c->norms, c->tc_stats, n, metric, c->tc_beta, c->tc_delta);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return fail_cuda(e, "row affine terms");
+  }
+  c->tc_metric = metric;
+  c->tc_ready = true;
+  return MANS_OK;
+}
+
+static size_t carve(size_t& o, size_t bytes) {
+  size_t at = (o + 255) / 256 * 256;
+  o = at + bytes;
+  return at;
+}
+
+// Whether the tensor-core path applies to this corpus and metric: cosine
+// needs every row norm bounded away from zero so the bound stays finite.
+bool tc_applicable(const mans_corpus* c, int metric) {
+  if (c->n <= 0 || c->n >= (1ll << 31)) return false;
+  if (metric == kCosine && c->tc_ready && c->tc_stats_host.min_norm < 1e-6f) return false;
+  return true;
+}
+
+int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* ws,
+                           const float* d_queries, int64_t nq, int32_t k, int32_t metric,
+                           float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
+                           cudaStream_t stream) {
+  int32_t rc = tc_prepare_corpus(corpus, metric);
+  if (rc != MANS_OK) return rc;
+  if (!tc_applicable(corpus, metric))
+    return run_flat_search(ctx, corpus, ws, d_queries, nq, k, metric, d_out_dist, d_out_ids,
+                           d_out_counts, stream, kModeHost, MANS_MAX_TOPK);
+  const int64_t n = corpus->n;
+  const int32_t kout = std::min<int32_t>(k, MANS_MAX_TOPK);
+  const int32_t keff = static_cast<int32_t>(std::min<int64_t>(kout, n));
+  const int32_t kp = pow2_at_least(keff);
+  const int64_t ld16 = corpus->tc_ld16;
+  const int64_t qblocks = (nq + kBN - 1) / kBN;
+  const int64_t nq_pad = qblocks * kBN;
+  int64_t sample = std::min<int64_t>(n, std::max<int64_t>(16384, std::min<int64_t>(131072, 256ll * keff)));
+  sample = std::min<int64_t>(n, (sample + kBM - 1) / kBM * kBM);
+  const int32_t cap = 8192;
+
+  size_t o = 0;
+  const size_t o_qbf = carve(o, nq_pad * ld16 * sizeof(__nv_bfloat16));
+  const size_t o_qn = carve(o, nq * sizeof(float));
+  const size_t o_al = carve(o, nq * sizeof(float));
+  const size_t o_ga = carve(o, nq * sizeof(float));
+  const size_t o_ep = carve(o, nq * sizeof(float));
+  const size_t o_th = carve(o, nq * sizeof(float));
+  const size_t o_dn = carve(o, nq * sample * sizeof(float));
+  const size_t o_cc = carve(o, nq * sizeof(int32_t) + sizeof(int32_t));
+  const size_t o_cd = carve(o, nq * static_cast<size_t>(cap) * sizeof(uint64_t));
+  if ((rc = ws->aux.reserve(o)) != MANS_OK) return rc;
+  if ((rc = ws->err.reserve(sizeof(int))) != MANS_OK) return rc;
+  if (!ws->err_cleared) {
+    cudaError_t e = cudaMemsetAsync(ws->err.ptr, 0, sizeof(int), stream);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaMemsetAsync(err)");
+    ws->err_cleared = true;
+  }
+  uint8_t* A = static_cast<uint8_t*>(ws->aux.ptr);
+  auto F = [&](size_t off) { return reinterpret_cast<float*>(A + off); };
+  __nv_bfloat16* qbf = reinterpret_cast<__nv_bfloat16*>(A + o_qbf);
+  int32_t* ccount = reinterpret_cast<int32_t*>(A + o_cc);
+  int32_t* fallbacks = ccount + nq;
+  uint64_t* cand = reinterpret_cast<uint64_t*>(A + o_cd);
+
+  cudaError_t e = cudaMemsetAsync(qbf, 0, nq_pad * ld16 * sizeof(__nv_bfloat16), stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(ccount, 0, (nq + 1) * sizeof(int32_t), stream);
+  if (e != cudaSuccess) return fail_cuda(e, "tc scratch clear");
+
+  TcQueryParams qp{};
+  qp.queries = d_queries;
+  qp.nq = nq;
+  qp.dim = static_cast<int32_t>(corpus->dim);
+  qp.ld16 = ld16;
+  qp.metric = metric;
+  qp.cs = corpus->tc_stats_host;
+  qp.qbf = qbf;
+  qp.qn_exact = F(o_qn);
+  qp.alpha = F(o_al);
+  qp.gamma = F(o_ga);
+  qp.eps = F(o_ep);
+  tc_query_prep_kernel<<<static_cast<unsigned>((nq + 7) / 8), 256, 0, stream>>>(qp);
+  if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc query prep launch");
+
+  CUtensorMap map_b;
+  if ((rc = encode_bf16_map(&map_b, qbf, nq_pad, corpus->dim, ld16, kBN)) != MANS_OK) return rc;
+  const size_t smem = tc_smem_bytes();
+  // the attribute is per device; set it on every call (cheap, no allocation)
+  e = cudaFuncSetAttribute(tc_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem));
+  if (e != cudaSuccess) return fail_cuda(e, "tc configure");
+  if (corpus->dim * sizeof(float) > 48 * 1024)
+    return fail(MANS_ERR_SEARCH, "dimension too large for the tensor-core re-rank");
+
+  TcParams tp{};
+  tp.nq = nq;
+  tp.dim = static_cast<int32_t>(corpus->dim);
+  tp.qblocks = static_cast<int32_t>(qblocks);
+  tp.row_beta = metric == kL2 ? corpus->tc_beta : nullptr;
+  tp.row_delta = metric == kCosine ? corpus->tc_delta : nullptr;
+  tp.q_alpha = F(o_al);
+  tp.q_gamma = F(o_ga);
+  tp.q_thr = F(o_th);
+  tp.err = static_cast<int*>(ws->err.ptr);
+  // 2. sample pass (dense)
+  tp.row0 = 0;
+  tp.rows = sample;
+  tp.dense_out = F(o_dn);
+  tp.dense_ld = sample;
+  const int64_t units_s = (sample + kBM - 1) / kBM * qblocks;
+  tc_scan_kernel<<<static_cast<unsigned>(std::min<int64_t>(units_s, ctx->num_sms)), kTcThreads,
+                   smem, stream>>>(corpus->tc_map, map_b, tp);
+  if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc sample launch");
+  // 3. thresholds
+  tc_threshold_kernel<<<static_cast<unsigned>(nq), kMergeThreads, 0, stream>>>(
+      F(o_dn), sample, sample, keff, kp, F(o_ep), F(o_th));
+  if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc threshold launch");
+  // 4. full filtered pass
+  tp.rows = n;
+  tp.dense_out = nullptr;
+  tp.cand = cand;
+  tp.cand_count = ccount;
+  tp.cand_cap = cap;
+  const int64_t units = (n + kBM - 1) / kBM * qblocks;
+  cudaEvent_t stop = timing_begin(ws, stream);
+  tc_scan_kernel<<<static_cast<unsigned>(std::min<int64_t>(units, ctx->num_sms)), kTcThreads, smem,
+                   stream>>>(corpus->tc_map, map_b, tp);
+  if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc scan launch");
+  timing_end(stop, stream);
+  // 5. certify + exact re-rank
+  RerankParams rp{};
+  rp.cand = cand;
+  rp.cand_count = ccount;
+  rp.cand_cap = cap;
+  rp.thr = F(o_th);
+  rp.eps = F(o_ep);
+  rp.qn_exact = F(o_qn);
+  rp.queries = d_queries;
+  rp.rows = corpus->rows;
+  rp.ld = corpus->ld;
+  rp.norms = corpus->norms;
+  rp.n = n;
+  rp.dim = static_cast<int32_t>(corpus->dim);
+  rp.metric = metric;
+  rp.id_offset = corpus->id_offset;
+  rp.k = keff;
+  rp.kp = kp;
+  rp.kout = kout;
+  rp.out_dist = d_out_dist;
+  rp.out_ids = d_out_ids;
+  rp.out_counts = d_out_counts;
+  rp.fallbacks = fallbacks;
+  tc_rerank_kernel<<<static_cast<unsigned>(nq), kRerankThreads, corpus->dim * sizeof(float),
+                     stream>>>(rp);
+  if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc rerank launch");
+  ws->tc_fallbacks = fallbacks;
+  ws->launches += 5;
+  return MANS_OK;
+}
+
+void tc_free_corpus(mans_corpus* c) {
+  if (c->tc_rows) cudaFree(c->tc_rows);
+  if (c->tc_stats) cudaFree(c->tc_stats);
+  if (c->tc_beta) cudaFree(c->tc_beta);
+  if (c->tc_delta) cudaFree(c->tc_delta);
+  c->tc_rows = nullptr;
+  c->tc_stats = c->tc_beta = c->tc_delta = nullptr;
+  c->tc_ready = false;
+}
+
+}  // namespace mans
