@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--metric", default="cosine", choices=list(METRIC_NAMES))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-also", action="store_true",
+                    help="skip the nq = 32 and nq = 1024 measurements reported under `also`")
     return ap.parse_args()
 
 
@@ -296,11 +298,161 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def workload_config(args):
-    return {"workload": f"exact_flat_{args.n}x{args.dim}_{args.metric}_top{args.k}_nq{args.nq}",
-            "n": args.n, "dim": args.dim, "nq": args.nq, "k": args.k, "metric": args.metric,
+def workload_config(args, nq=None):
+    nq = args.nq if nq is None else nq
+    return {"workload": f"exact_flat_{args.n}x{args.dim}_{args.metric}_top{args.k}_nq{nq}",
+            "n": args.n, "dim": args.dim, "nq": nq, "k": args.k, "metric": args.metric,
             "parallelism": f"rowshard{args.gpus}",
             "l2": "inputs larger than L2 (corpus 1.5 GB streamed per step)"}
+
+
+def measured_bf16_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
+class Runner:
+    """Runs search steps of one batch size on this rank's row shard."""
+
+    def __init__(self, args, torch, mb, lib, ctx, buf, ws, world, rank, dist, metric):
+        self.a, self.torch, self.mb, self.lib = args, torch, mb, lib
+        self.ctx, self.buf, self.ws = ctx, buf, ws
+        self.world, self.rank, self.dist, self.metric = world, rank, dist, metric
+        self.stream = torch.cuda.current_stream()
+        self.sp = self.stream.cuda_stream
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
+
+    def measure(self, q, steps, warmup, with_clocks):
+        torch, mb, a = self.torch, self.mb, self.a
+        nq = q.shape[0]
+        kout = min(a.k, mb.MAX_TOP_K)
+        dq = torch.from_numpy(q).cuda()
+        P = 2 * nq * kout + nq  # packed [dist | ids | counts] per rank
+        loc = torch.empty((P,), dtype=torch.int32, device="cuda")
+        out = torch.empty((P,), dtype=torch.int32, device="cuda")
+        gat = torch.empty((self.world, P), dtype=torch.int32, device="cuda")
+        ws, ctx, buf, sp = self.ws, self.ctx, self.buf, self.sp
+
+        def step(src):
+            target = loc if self.world > 1 else out
+            mb.FlatGPUSearch.search_device(ctx, buf, ws, src.data_ptr(), nq, a.k, self.metric,
+                                           target.data_ptr(), target[nq * kout:].data_ptr(),
+                                           target[2 * nq * kout:].data_ptr(), sp)
+            if self.world > 1:
+                self.dist.all_gather_into_tensor(gat, loc)
+                mb.topk_merge_device(ctx, ws, gat.data_ptr(), gat[0, nq * kout:].data_ptr(),
+                                     gat[0, 2 * nq * kout:].data_ptr(), self.world, nq, kout,
+                                     a.k, out.data_ptr(), out[nq * kout:].data_ptr(),
+                                     out[2 * nq * kout:].data_ptr(), sp, list_stride=P)
+            return out
+
+        for _ in range(max(3, warmup)):
+            step(dq)
+        ws.check(sp)
+        ws.stats()
+        ws.set_timing(True)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(steps)]
+        clocks = ClockSampler(torch.cuda.current_device()) if with_clocks else None
+        if clocks:
+            clocks.start()
+            time.sleep(0.3)
+        self.barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(self.stream)
+        for i in range(steps):
+            ev[i][0].record(self.stream)
+            step(dq)
+            ev[i][1].record(self.stream)
+        t1.record(self.stream)
+        self.barrier()
+        clock_info = clocks.stop() if clocks else None
+        ws.check(sp)
+        kern_ms, kern_launches, total_launches = ws.stats()
+        ws.set_timing(False)
+        total_ms = t0.elapsed_time(t1)
+        step_ms = [x.elapsed_time(y) for x, y in ev]
+        device_out = out.clone()
+
+        # end to end through the C ABI with pinned host buffers
+        hq = torch.from_numpy(q).pin_memory()
+        h_out = torch.empty((P,), dtype=torch.int32).pin_memory()
+        dq2 = torch.empty_like(dq)
+        L = self.lib
+
+        def e2e_step():
+            if self.world == 1:
+                rc = L.mans_flat_search(ctx.handle, buf.handle, C.c_void_p(hq.data_ptr()), nq,
+                                        a.dim, a.k, self.metric, C.c_void_p(h_out.data_ptr()),
+                                        C.c_void_p(h_out[nq * kout:].data_ptr()),
+                                        C.c_void_p(h_out[2 * nq * kout:].data_ptr()))
+                mb.check(rc)
+            else:
+                dq2.copy_(hq, non_blocking=True)
+                r = step(dq2)
+                h_out.copy_(r, non_blocking=True)
+                torch.cuda.current_stream().synchronize()
+
+        for _ in range(max(3, warmup)):
+            e2e_step()
+        self.barrier()
+        e2e_times = []
+        for _ in range(steps):
+            t = time.perf_counter()
+            e2e_step()
+            e2e_times.append(time.perf_counter() - t)
+        self.barrier()
+        ok = bool(torch.equal(device_out.cpu(), h_out))
+
+        stats = torch.tensor([total_ms, sum(e2e_times) * 1e3, kern_ms / max(kern_launches, 1)],
+                             dtype=torch.float64, device="cuda")
+        steps_t = torch.tensor(step_ms, dtype=torch.float64, device="cuda")
+        e2e_t = torch.tensor(e2e_times, dtype=torch.float64, device="cuda")
+        if self.world > 1:
+            self.dist.all_reduce(stats, op=self.dist.ReduceOp.MAX)
+            self.dist.all_reduce(steps_t, op=self.dist.ReduceOp.MAX)
+            self.dist.all_reduce(e2e_t, op=self.dist.ReduceOp.MAX)
+        total_ms, e2e_ms, kern_avg_ms = stats.tolist()
+        return {"nq": nq, "steps": steps, "total_ms": total_ms, "e2e_ms": e2e_ms,
+                "kern_avg_ms": kern_avg_ms, "kern_launches": kern_launches,
+                "launches": total_launches, "p50_ms": p50(steps_t.tolist()),
+                "e2e_p50_s": p50(e2e_t.tolist()), "clocks": clock_info, "ok": ok, "kout": kout}
+
+
+def roofline(args, res, shard_rows, metric, tc_min_batch, workload):
+    nq = res["nq"]
+    kern_s = res["kern_avg_ms"] * 1e-3
+    if tc_min_batch and nq >= tc_min_batch:
+        flops = 2.0 * shard_rows * args.dim * nq
+        peak, kind = measured_bf16_peak()
+        achieved = flops / kern_s / 1e12
+        return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "traffic": committed_traffic(workload),
+                "kernel": "tc_scan_kernel (filtered full pass)",
+                "kernel_avg_us": res["kern_avg_ms"] * 1e3,
+                "algorithmic_flops_per_launch": flops,
+                "peak_source": f"{kind} bf16_tflops (dense, burst)"}
+    groups = math.ceil(nq / 8) if nq > 8 else 1
+    row_bytes = args.dim * 4 + (4 if metric in (0, 1) else 0)
+    alg = shard_rows * row_bytes * groups + nq * args.dim * 4
+    peak, kind = measured_peaks()
+    achieved = alg / kern_s / 1e9
+    traffic = committed_traffic(workload)
+    if traffic is not None:
+        traffic = traffic * shard_rows / args.n  # committed capture is of the unsharded launch
+    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "traffic": traffic, "kernel": "scan_topk_kernel",
+            "kernel_avg_us": res["kern_avg_ms"] * 1e3, "algorithmic_bytes_per_launch": alg,
+            "peak_source": f"{kind} hbm_gbs"}
 
 
 def main():
@@ -327,164 +479,63 @@ def main():
     from meltan_b200._lib import lib
 
     metric = METRIC_NAMES[args.metric]
-    v, q = make_data(args.n, args.dim, args.nq)
+    also_nq = [x for x in (32, 1024) if x != args.nq] if not args.no_also else []
+    v, q_all = make_data(args.n, args.dim, max([args.nq] + also_nq))
     rows = np.array_split(np.arange(args.n), world)[rank]
     r0, r1 = int(rows[0]), int(rows[-1]) + 1
     ctx = mb.Context(local)
+    tc_min = 16
+    ctx.set_tensor_core_batch(tc_min)
     buf = mb.VectorBuffer(ctx, v[r0:r1], id_offset=r0)
     ws = mb.Workspace(ctx)
-    kout = min(args.k, mb.MAX_TOP_K)
-    nq = args.nq
-    stream = torch.cuda.current_stream()
-    sp = stream.cuda_stream
-    dq = torch.from_numpy(q).cuda()
-    ld = torch.empty((nq, kout), dtype=torch.float32, device="cuda")
-    li = torch.empty((nq, kout), dtype=torch.int32, device="cuda")
-    lc = torch.empty((nq,), dtype=torch.int32, device="cuda")
-    if world > 1:
-        gd = torch.empty((world, nq, kout), dtype=torch.float32, device="cuda")
-        gi = torch.empty((world, nq, kout), dtype=torch.int32, device="cuda")
-        gc = torch.empty((world, nq), dtype=torch.int32, device="cuda")
-        od = torch.empty((nq, kout), dtype=torch.float32, device="cuda")
-        oi = torch.empty((nq, kout), dtype=torch.int32, device="cuda")
-        oc = torch.empty((nq,), dtype=torch.int32, device="cuda")
-
-    def step(src):
-        mb.FlatGPUSearch.search_device(ctx, buf, ws, src.data_ptr(), nq, args.k, metric,
-                                       ld.data_ptr(), li.data_ptr(), lc.data_ptr(), sp)
-        if world > 1:
-            dist.all_gather_into_tensor(gd, ld)
-            dist.all_gather_into_tensor(gi, li)
-            dist.all_gather_into_tensor(gc, lc)
-            mb.topk_merge_device(ctx, ws, gd.data_ptr(), gi.data_ptr(), gc.data_ptr(), world, nq,
-                                 kout, args.k, od.data_ptr(), oi.data_ptr(), oc.data_ptr(), sp)
-            return od, oi, oc
-        return ld, li, lc
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    # ---- device-resident timing (value) ----
-    for _ in range(max(3, args.warmup)):
-        step(dq)
-    ws.check(sp)
-    ws.stats()
-    ws.set_timing(True)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps)]
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(0.3)
-    barrier()
-    t_start = torch.cuda.Event(enable_timing=True)
-    t_stop = torch.cuda.Event(enable_timing=True)
-    t_start.record(stream)
-    for i in range(args.steps):
-        ev[i][0].record(stream)
-        step(dq)
-        ev[i][1].record(stream)
-    t_stop.record(stream)
-    barrier()
-    clock_info = clocks.stop()
-    ws.check(sp)
-    kern_ms, kern_launches, total_launches = ws.stats()
-    ws.set_timing(False)
-    total_ms = t_start.elapsed_time(t_stop)
-    step_ms = [a.elapsed_time(b) for a, b in ev]
-
-    # ---- end to end through the C ABI with pinned host buffers (e2e) ----
-    hq = torch.from_numpy(q).pin_memory()
-    h_out_d = torch.empty((nq, kout), dtype=torch.float32).pin_memory()
-    h_out_i = torch.empty((nq, kout), dtype=torch.int32).pin_memory()
-    h_out_c = torch.empty((nq,), dtype=torch.int32).pin_memory()
-    L = lib()
-    dq2 = torch.empty_like(dq)
-
-    def e2e_step():
-        if world == 1:
-            rc = L.mans_flat_search(ctx.handle, buf.handle, C.c_void_p(hq.data_ptr()), nq,
-                                    args.dim, args.k, metric, C.c_void_p(h_out_d.data_ptr()),
-                                    C.c_void_p(h_out_i.data_ptr()), C.c_void_p(h_out_c.data_ptr()))
-            mb.check(rc)
-        else:
-            dq2.copy_(hq, non_blocking=True)
-            d_, i_, c_ = step(dq2)
-            h_out_d.copy_(d_, non_blocking=True)
-            h_out_i.copy_(i_, non_blocking=True)
-            h_out_c.copy_(c_, non_blocking=True)
-            torch.cuda.current_stream().synchronize()
-
-    for _ in range(max(3, args.warmup)):
-        e2e_step()
-    barrier()
-    e2e_times = []
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        t = time.perf_counter()
-        e2e_step()
-        e2e_times.append(time.perf_counter() - t)
-    e2e_total = time.perf_counter() - t0
-    barrier()
-
-    # verify the result of the last e2e step against the device path once; every
-    # rank runs the step because it contains collectives
-    fd, fi, fc = step(dq)
-    torch.cuda.synchronize()
-    ok = bool(torch.equal(fi.cpu(), h_out_i) and torch.equal(fc.cpu(), h_out_c))
-
-    stats = torch.tensor([total_ms, e2e_total * 1e3, kern_ms / max(kern_launches, 1)],
-                         dtype=torch.float64, device="cuda")
-    steps_t = torch.tensor(step_ms, dtype=torch.float64, device="cuda")
-    e2e_t = torch.tensor(e2e_times, dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
-        dist.all_reduce(steps_t, op=dist.ReduceOp.MAX)
-        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
-    total_ms, e2e_ms, kern_avg_ms = stats.tolist()
+    R = Runner(args, torch, mb, lib(), ctx, buf, ws, world, rank, dist, metric)
+    main_res = R.measure(q_all[:args.nq], args.steps, args.warmup, with_clocks=True)
+    also = []
+    for nq2 in also_nq:
+        st = max(20, min(args.steps, int(20000 / nq2)))
+        also.append(R.measure(q_all[:nq2], st, 5, with_clocks=False))
 
     if rank == 0:
-        peak, peak_kind = measured_peaks()
-        shard_rows = r1 - r0
-        groups = math.ceil(nq / 8) if nq > 8 else 1
-        row_bytes = args.dim * 4 + (4 if metric in (0, 1) else 0)
-        alg_bytes = shard_rows * row_bytes * groups + nq * args.dim * 4
-        achieved = alg_bytes / (kern_avg_ms * 1e-3) / 1e9
         workload = workload_config(args)["workload"]
-        traffic = committed_traffic(workload)
+        res = main_res
         line = {
             "metric": "queries_per_sec",
-            "value": nq * args.steps / (total_ms * 1e-3),
+            "value": args.nq * args.steps / (res["total_ms"] * 1e-3),
             "unit": "queries/s",
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
-            "ms_per_step": total_ms / args.steps,
-            "p50_us": 1e3 * p50(steps_t.tolist()),
+            "ms_per_step": res["total_ms"] / args.steps,
+            "p50_us": 1e3 * res["p50_ms"],
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,
             "dtype": "f32",
             "data": "synthetic (numpy default_rng(0) Gaussian rows, L2-normalised)",
             "config": workload_config(args),
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak,
-                         "traffic": traffic,
-                         "kernel": "scan_topk_kernel",
-                         "kernel_avg_us": kern_avg_ms * 1e3,
-                         "algorithmic_bytes_per_launch": alg_bytes,
-                         "peak_source": f"{peak_kind} hbm_gbs"},
-            "e2e": {"value": nq * args.steps / (e2e_ms * 1e-3), "unit": "queries/s",
-                    "p50_us": 1e6 * p50(e2e_t.tolist()),
-                    "h2d_bytes_per_step": nq * args.dim * 4,
-                    "d2h_bytes_per_step": nq * kout * 8 + nq * 4},
-            "gpu_launches": int(total_launches),
-            "clocks": clock_info,
-            "e2e_matches_device_path": ok,
+            "roofline": roofline(args, res, r1 - r0, metric, tc_min, workload),
+            "e2e": {"value": args.nq * args.steps / (res["e2e_ms"] * 1e-3), "unit": "queries/s",
+                    "p50_us": 1e6 * res["e2e_p50_s"],
+                    "h2d_bytes_per_step": args.nq * args.dim * 4,
+                    "d2h_bytes_per_step": args.nq * res["kout"] * 8 + args.nq * 4},
+            "gpu_launches": int(res["launches"]),
+            "clocks": res["clocks"],
+            "e2e_matches_device_path": res["ok"],
         }
+        line["also"] = []
+        for r in also:
+            wl = workload_config(args, r["nq"])["workload"]
+            line["also"].append({
+                "workload": wl, "nq": r["nq"], "steps": r["steps"],
+                "value": r["nq"] * r["steps"] / (r["total_ms"] * 1e-3), "unit": "queries/s",
+                "ms_per_step": r["total_ms"] / r["steps"], "p50_us": 1e3 * r["p50_ms"],
+                "e2e_value": r["nq"] * r["steps"] / (r["e2e_ms"] * 1e-3),
+                "e2e_p50_us": 1e6 * r["e2e_p50_s"], "gpu_launches": int(r["launches"]),
+                "roofline": roofline(args, r, r1 - r0, metric, tc_min, wl),
+                "e2e_matches_device_path": r["ok"]})
         if world == 1 and not args.no_cpu_baseline:
-            qps, used, done, use_ref = cpu_reference_qps(v, q, args.k, metric, args.cpu_seconds)
+            qps, used, done, use_ref = cpu_reference_qps(v, q_all[:max(1, args.nq)], args.k, metric,
+                                                         args.cpu_seconds)
             line["cpu_baseline"] = {
                 "value": qps, "unit": "queries/s", "cores": used, "kind": "port",
                 "sample": f"{done} single-query scans of the full {args.n}x{args.dim} corpus "

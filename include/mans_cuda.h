@@ -176,15 +176,19 @@ int32_t mans_flat_search_noalloc(mans_ctx *ctx, const mans_corpus *corpus,
                                  void *cuda_stream);
 
 /* Merges `n_lists` per-shard result blocks (each nq x kin, sorted ascending by
- * (distance, id), laid out list-major: list l at offset l*nq*kin) into the
- * global top-k per query, by (distance, id).  This is the device form of
- * ParallelFlatScan.mergeSorted (ParallelFlatScan.swift:288-315) used after
- * the all-gather of row-shard results.  Device pointers, async on the stream. */
+ * (distance, id)) into the global top-k per query, by (distance, id).  This is
+ * the device form of ParallelFlatScan.mergeSorted (ParallelFlatScan.swift
+ * :288-315) used after the all-gather of row-shard results.  Block l starts at
+ * d_in_dist + l*list_stride, d_in_ids + l*list_stride and d_in_counts +
+ * l*list_stride (elements of 4 bytes); list_stride 0 means the plain
+ * list-major layout (dist/ids stride nq*kin, counts stride nq).  A packed
+ * per-shard buffer [dist | ids | counts] lets one all-gather move all three.
+ * Device pointers, async on the stream. */
 int32_t mans_topk_merge_device(mans_ctx *ctx, mans_workspace *ws, const float *d_in_dist,
                                const uint32_t *d_in_ids, const int32_t *d_in_counts,
-                               int32_t n_lists, int64_t nq, int32_t kin, int32_t k,
-                               float *d_out_dist, uint32_t *d_out_ids, int32_t *d_out_counts,
-                               void *cuda_stream);
+                               int32_t n_lists, int64_t list_stride, int64_t nq, int32_t kin,
+                               int32_t k, float *d_out_dist, uint32_t *d_out_ids,
+                               int32_t *d_out_counts, void *cuda_stream);
 
 /* ---- IVF-flat ------------------------------------------------------------ */
 

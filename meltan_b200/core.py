@@ -314,9 +314,13 @@ class FlatGPUSearch:
 
 def topk_merge_device(context: Context, ws: Workspace, d_in_dist: int, d_in_ids: int,
                       d_in_counts: int, n_lists: int, nq: int, kin: int, k: int,
-                      d_out_dist: int, d_out_ids: int, d_out_counts: int, stream: int = 0):
-    """Merge of row-shard result blocks by (distance, id) (mergeSorted semantics)."""
+                      d_out_dist: int, d_out_ids: int, d_out_counts: int, stream: int = 0,
+                      list_stride: int = 0):
+    """Merge of row-shard result blocks by (distance, id) (mergeSorted semantics).
+    list_stride (4-byte elements) locates block l of all three inputs at
+    base + l * list_stride; 0 means plain list-major arrays."""
     check(lib().mans_topk_merge_device(context.handle, ws.handle, C.c_void_p(d_in_dist),
-                                       C.c_void_p(d_in_ids), C.c_void_p(d_in_counts), n_lists, nq,
-                                       kin, k, C.c_void_p(d_out_dist), C.c_void_p(d_out_ids),
-                                       C.c_void_p(d_out_counts), C.c_void_p(stream)))
+                                       C.c_void_p(d_in_ids), C.c_void_p(d_in_counts), n_lists,
+                                       list_stride, nq, kin, k, C.c_void_p(d_out_dist),
+                                       C.c_void_p(d_out_ids), C.c_void_p(d_out_counts),
+                                       C.c_void_p(stream)))

@@ -619,11 +619,12 @@ int32_t mans_flat_search_device(mans_ctx* ctx, const mans_corpus* corpus, mans_w
 
 int32_t mans_topk_merge_device(mans_ctx* ctx, mans_workspace* ws, const float* d_in_dist,
                                const uint32_t* d_in_ids, const int32_t* d_in_counts,
-                               int32_t n_lists, int64_t nq, int32_t kin, int32_t k,
-                               float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
-                               void* cuda_stream) {
+                               int32_t n_lists, int64_t list_stride, int64_t nq, int32_t kin,
+                               int32_t k, float* d_out_dist, uint32_t* d_out_ids,
+                               int32_t* d_out_counts, void* cuda_stream) {
   if (!ctx || !ws) return fail(MANS_ERR_INVALID, "null context or workspace");
-  if (n_lists < 0 || nq < 0 || kin < 0) return fail(MANS_ERR_INVALID, "negative size");
+  if (n_lists < 0 || nq < 0 || kin < 0 || list_stride < 0)
+    return fail(MANS_ERR_INVALID, "negative size");
   if (nq == 0) return MANS_OK;
   DeviceGuard g(ctx->device);
   cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
@@ -643,6 +644,7 @@ int32_t mans_topk_merge_device(mans_ctx* ctx, mans_workspace* ws, const float* d
   m.in_ids = d_in_ids;
   m.in_counts = d_in_counts;
   m.n_lists = n_lists;
+  m.list_stride = list_stride;
   m.kp_in = kin;
   m.nq = nq;
   m.k = kout;

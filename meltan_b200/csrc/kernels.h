@@ -93,6 +93,7 @@ struct MergeParams {
   const int32_t* q_slot_list;  // with offsets: query q reads slots list[offs[q]..offs[q+1])
   int32_t slots_per_query;
   int32_t n_lists;
+  int64_t list_stride;   // pairs mode: elements between shard blocks (0: nq*kp_in / nq)
   int32_t kp_in;
   int64_t nq;
   int32_t k;

@@ -397,8 +397,12 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const MergeParams 
           int64_t slot = p.q_slot_list ? p.q_slot_list[slot0 + i] : slot0 + i;
           if (p.in_counts[slot] > 0) h = p.in_keys[slot * p.kp_in];
         } else {
-          int64_t blk = static_cast<int64_t>(i) * p.nq + q;
-          if (p.in_counts[blk] > 0) h = make_key(p.in_dist[blk * p.kp_in], p.in_ids[blk * p.kp_in]);
+          const int64_t ls = p.list_stride ? p.list_stride : p.nq * p.kp_in;
+          const int64_t cs = p.list_stride ? p.list_stride : p.nq;
+          if (p.in_counts[static_cast<int64_t>(i) * cs + q] > 0) {
+            const int64_t at = static_cast<int64_t>(i) * ls + q * p.kp_in;
+            h = make_key(p.in_dist[at], p.in_ids[at]);
+          }
         }
       }
       buf[i] = h;
@@ -423,9 +427,11 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const MergeParams 
           valid = true;
         }
       } else {
-        int64_t blk = sl * p.nq + q;
-        if (i < p.in_counts[blk]) {
-          key = make_key(p.in_dist[blk * p.kp_in + i], p.in_ids[blk * p.kp_in + i]);
+        const int64_t ls = p.list_stride ? p.list_stride : p.nq * p.kp_in;
+        const int64_t cs = p.list_stride ? p.list_stride : p.nq;
+        if (i < p.in_counts[sl * cs + q]) {
+          const int64_t at = sl * ls + q * p.kp_in + i;
+          key = make_key(p.in_dist[at], p.in_ids[at]);
           valid = true;
         }
       }

@@ -172,6 +172,20 @@ def test_device_api_and_shard_merge(ctx):
     want = O.flat_search(v, q, k, O.COSINE)
     got = (od.cpu().numpy(), oi.cpu().numpy().view(np.uint32), oc.cpu().numpy())
     assert_same(got, want)
+    # packed per-shard blocks [dist | ids | counts], merged with a list stride
+    P = 2 * nq * k + nq
+    packed = torch.empty((L, P), dtype=torch.int32, device="cuda")
+    for s_, buf in enumerate(shards):
+        base = packed[s_]
+        mb.FlatGPUSearch.search_device(ctx, buf, ws, dq.data_ptr(), nq, k, mb.Metric.cosine,
+                                       base.data_ptr(), base[nq * k:].data_ptr(),
+                                       base[2 * nq * k:].data_ptr())
+    mb.topk_merge_device(ctx, ws, packed.data_ptr(), packed[0, nq * k:].data_ptr(),
+                         packed[0, 2 * nq * k:].data_ptr(), L, nq, k, k, od.data_ptr(),
+                         oi.data_ptr(), oc.data_ptr(), list_stride=P)
+    ws.check()
+    got = (od.cpu().numpy(), oi.cpu().numpy().view(np.uint32), oc.cpu().numpy())
+    assert_same(got, want)
     ws.close()
     for b in shards:
         b.close()
