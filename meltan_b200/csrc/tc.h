@@ -14,12 +14,13 @@ struct TcParams {
   int64_t rows;
   int64_t nq;
   int32_t dim;
-  int32_t qblocks;          // ceil(nq / 256)
+  int32_t qblocks;          // ceil(nq / 128)
   const float* row_beta;    // per-row additive term (L2: |r|^2), may be null
   const float* row_delta;   // per-row factor (cosine: 1/|r|), may be null
   const float* q_alpha;     // per-query additive term
   const float* q_gamma;     // per-query factor of the dot
-  const float* q_thr;       // filter threshold (filter mode)
+  const float* q_c;         // filter constant in the score domain (filter mode)
+  float bias_scale;         // row bias of the score domain = bias_scale * row_beta
   float* dense_out;         // dense mode: dense_out[q * dense_ld + (row - row0)]
   int64_t dense_ld;
   uint64_t* cand;           // filter mode: (distance, row) keys, cand_cap per query

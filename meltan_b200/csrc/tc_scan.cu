@@ -50,17 +50,47 @@
 namespace mans {
 namespace {
 
-constexpr int kBM = 128;   // corpus rows per tile (MMA M)
-constexpr int kBN = 256;   // queries per tile (MMA N)
-constexpr int kBK = 64;    // bf16 per 128-byte swizzle row
-constexpr int kStages = 4;
-constexpr int kABytes = kBM * kBK * 2;  // 16 KiB
-constexpr int kBBytes = kBN * kBK * 2;  // 32 KiB
-constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kTcThreads = 256;
-constexpr int kTmemCols = 512;
+constexpr int kQM = 128;  // queries per block (MMA M, TMEM lanes)
+constexpr int kRN = 256;  // corpus rows per tile (MMA N, TMEM columns)
+constexpr int kBK = 64;   // bf16 per 128-byte swizzle row
+constexpr int kQBytes = kQM * kBK * 2;  // 16 KiB per k-block of queries
+constexpr int kRBytes = kRN * kBK * 2;  // 32 KiB per k-block of rows
+constexpr int kTcThreads = 384;         // warps 0-3 control, 4-11 epilogue
+constexpr int kEpiWarps = 8;
+constexpr int kTmemCols = 512;          // two 256-column accumulators
+constexpr size_t kResidentMax = 96 * 1024;
+constexpr size_t kPipeBudget = 196 * 1024;
 constexpr int kRerankThreads = 256;
 constexpr int kMaxRerank = 2048;  // exact re-score list per query
+
+// Shared-memory plan of tc_scan_kernel for a given width: the query block is
+// kept resident when its nk k-blocks fit in 96 KiB (dim <= 384), otherwise
+// it is streamed beside the rows in every stage.
+struct TcLayout {
+  int nk;
+  bool resident;
+  int stages;
+  size_t a_bytes;
+  size_t stage_bytes;
+  size_t bar_off;
+  size_t total;
+};
+
+__host__ __device__ inline TcLayout tc_layout(int dim) {
+  TcLayout L;
+  L.nk = (dim + kBK - 1) / kBK;
+  L.resident = static_cast<size_t>(L.nk) * kQBytes <= kResidentMax;
+  L.a_bytes = L.resident ? static_cast<size_t>(L.nk) * kQBytes : 0;
+  L.stage_bytes = kRBytes + (L.resident ? 0 : kQBytes);
+  size_t st = (kPipeBudget - L.a_bytes) / L.stage_bytes;
+  L.stages = static_cast<int>(st > 8 ? 8 : st);
+  L.bar_off = L.a_bytes + static_cast<size_t>(L.stages) * L.stage_bytes;
+  // barriers: full/empty per stage, acc_full/acc_empty x2, a_full, a_empty, drain
+  const size_t bars = 8 * (2 * static_cast<size_t>(L.stages) + 7);
+  // + tmem slot / abort (16 B) + row terms 2 x 3 x kRN floats
+  L.total = 1024 + L.bar_off + bars + 16 + 2 * 3 * kRN * sizeof(float);
+  return L;
+}
 
 // ---- tcgen05 wrappers (inline PTX) ------------------------------------------
 
@@ -137,38 +167,55 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* err
   return false;
 }
 
+// Approximate distance from the bf16 dot v; one expression shared by the
+// dense and the filtered pass so both produce the same value for a pair.
+__device__ __forceinline__ float approx_distance(float alpha, float gamma, float beta, float delta,
+                                                 float v) {
+  return (alpha + beta) - (gamma * delta) * v;
+}
+
 __global__ void __launch_bounds__(kTcThreads, 1)
-    tc_scan_kernel(const __grid_constant__ CUtensorMap map_a,
-                   const __grid_constant__ CUtensorMap map_b, const TcParams p) {
+    tc_scan_kernel(const __grid_constant__ CUtensorMap map_q,
+                   const __grid_constant__ CUtensorMap map_r, const TcParams p) {
   extern __shared__ uint8_t smem_raw[];
+  const TcLayout L = tc_layout(p.dim);
   uint8_t* base =
       reinterpret_cast<uint8_t*>((reinterpret_cast<size_t>(smem_raw) + 1023) / 1024 * 1024);
-  uint8_t* stages = base;
-  uint64_t* full = reinterpret_cast<uint64_t*>(base + kStages * kStageBytes);
-  uint64_t* empty = full + kStages;
-  uint64_t* acc_full = empty + kStages;
+  uint8_t* qres = base;                  // resident query block (nk x 16 KiB)
+  uint8_t* stages = base + L.a_bytes;    // ring of (rows [| queries]) stages
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + L.bar_off);
+  uint64_t* empty = full + L.stages;
+  uint64_t* acc_full = empty + L.stages;
   uint64_t* acc_empty = acc_full + 2;
-  uint64_t* drain = acc_empty + 2;
+  uint64_t* a_full = acc_empty + 2;
+  uint64_t* a_empty = a_full + 1;
+  uint64_t* drain = a_empty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* qpar = reinterpret_cast<float*>(tmem_slot + 4);  // [2][3][kBN]: alpha, gamma, thr
+  float* rowpar = reinterpret_cast<float*>(tmem_slot + 4);  // [2][3][kRN]: delta, bias, beta
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int nk = (p.dim + kBK - 1) / kBK;
-  const int64_t row_tiles = (p.rows + kBM - 1) / kBM;
-  const int64_t units = row_tiles * p.qblocks;
+  const int nk = L.nk;
+  const int64_t rtiles = (p.rows + kRN - 1) / kRN;
+  const int64_t units = rtiles * p.qblocks;
+  // contiguous unit range per block, query-block major: a block keeps one
+  // query block (rarely two) while the blocks sharing it walk the rows
+  const int64_t u_begin = units * blockIdx.x / gridDim.x;
+  const int64_t u_end = units * (blockIdx.x + 1) / gridDim.x;
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < L.stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], kEpiWarps);
     }
+    mbar_init(a_full, 1);
+    mbar_init(a_empty, 1);
     mbar_init(drain, 1);
     *abort = 0;
     fence_mbar_init();
@@ -178,8 +225,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tmem_relinquish();
   }
   if (tid == 64) {
-    tma_prefetch_desc(&map_a);
-    tma_prefetch_desc(&map_b);
+    tma_prefetch_desc(&map_q);
+    tma_prefetch_desc(&map_r);
   }
   tc_fence_before();
   __syncthreads();
@@ -191,43 +238,72 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // ---------------- TMA producer ----------------
       int stage = 0;
       uint32_t phase = 0;
+      int64_t cur_qb = -1;
+      uint32_t a_round = 0;
       int64_t issued = 0;
-      for (int64_t u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
-        const int64_t rt = u / p.qblocks;
-        const int32_t qb = static_cast<int32_t>(u - rt * p.qblocks);
-        const int32_t y = static_cast<int32_t>(p.row0 + rt * kBM);
+      bool a_pending = false;
+      for (int64_t u = u_begin; u < u_end && !*abort; ++u) {
+        const int64_t qb = u / rtiles;
+        const int64_t rt = u - qb * rtiles;
+        if (L.resident && qb != cur_qb) {
+          // refill the resident query block once the MMAs on the old one finished
+          if (cur_qb >= 0 && !tc_wait(a_empty, (a_round - 1) & 1u, p.err, abort)) break;
+          mbar_arrive_expect_tx(a_full, static_cast<uint32_t>(nk * kQBytes));
+          for (int kb = 0; kb < nk; ++kb)
+            tma_load_2d(qres + kb * kQBytes, &map_q, kb * kBK, static_cast<int32_t>(qb * kQM), a_full);
+          a_pending = true;
+          cur_qb = qb;
+          ++a_round;
+        }
+        const int32_t y = static_cast<int32_t>(p.row0 + rt * kRN);
+        bool ok = true;
         for (int kb = 0; kb < nk; ++kb) {
-          if (!tc_wait(&empty[stage], phase ^ 1u, p.err, abort)) break;
-          uint8_t* st = stages + stage * kStageBytes;
-          mbar_arrive_expect_tx(&full[stage], kStageBytes);
-          tma_load_2d(st, &map_a, kb * kBK, y, &full[stage]);
-          tma_load_2d(st + kABytes, &map_b, kb * kBK, qb * kBN, &full[stage]);
+          if (!tc_wait(&empty[stage], phase ^ 1u, p.err, abort)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = stages + stage * L.stage_bytes;
+          mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(L.stage_bytes));
+          tma_load_2d(st, &map_r, kb * kBK, y, &full[stage]);
+          if (!L.resident)
+            tma_load_2d(st + kRBytes, &map_q, kb * kBK, static_cast<int32_t>(qb * kQM), &full[stage]);
           ++issued;
-          if (++stage == kStages) {
+          if (++stage == L.stages) {
             stage = 0;
             phase ^= 1u;
           }
         }
+        if (!ok) break;
       }
       // after an abort, wait (bounded) for the copies still in flight
       if (*abort) {
-        for (int64_t i = issued > kStages ? issued - kStages : 0; i < issued; ++i)
-          mbar_wait_bounded(&full[i % kStages], static_cast<uint32_t>((i / kStages) & 1), nullptr);
+        for (int64_t i = issued > L.stages ? issued - L.stages : 0; i < issued; ++i)
+          mbar_wait_bounded(&full[i % L.stages], static_cast<uint32_t>((i / L.stages) & 1), nullptr);
+        if (a_pending) mbar_wait_bounded(a_full, (a_round - 1) & 1u, nullptr);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      const uint32_t idesc = idesc_bf16(kBM, kBN);
+      const uint32_t idesc = idesc_bf16(kQM, kRN);
       int stage = 0;
       uint32_t phase = 0;
+      int64_t cur_qb = -1;
+      uint32_t a_round = 0;
       int local = 0;
-      for (int64_t u = blockIdx.x; u < units && !*abort; u += gridDim.x, ++local) {
+      for (int64_t u = u_begin; u < u_end && !*abort; ++u, ++local) {
+        const int64_t qb = u / rtiles;
+        if (L.resident && qb != cur_qb) {
+          if (cur_qb >= 0) tc_commit(a_empty);  // old query block free once prior MMAs finish
+          if (!tc_wait(a_full, a_round & 1u, p.err, abort)) break;
+          cur_qb = qb;
+          ++a_round;
+        }
         const int b = local & 1;
         const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
         if (!tc_wait(&acc_empty[b], acc_phase ^ 1u, p.err, abort)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem + static_cast<uint32_t>(b * kBN);
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(b * kRN);
         bool ok = true;
         for (int kb = 0; kb < nk; ++kb) {
           if (!tc_wait(&full[stage], phase, p.err, abort)) {
@@ -235,14 +311,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(stages + stage * kStageBytes);
-          const uint64_t adesc = smem_desc_sw128(sa);
-          const uint64_t bdesc = smem_desc_sw128(sa + kABytes);
+          const uint32_t sr = smem_u32(stages + stage * L.stage_bytes);
+          const uint32_t sq = L.resident ? smem_u32(qres + kb * kQBytes) : sr + kRBytes;
+          const uint64_t adesc = smem_desc_sw128(sq);
+          const uint64_t bdesc = smem_desc_sw128(sr);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
             tc_mma(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
           tc_commit(&empty[stage]);  // frees the smem stage once these MMAs finish
-          if (++stage == kStages) {
+          if (++stage == L.stages) {
             stage = 0;
             phase ^= 1u;
           }
@@ -255,63 +332,90 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_wait_bounded(drain, 0, nullptr);
     }
   } else if (warp >= 4) {
-    // ---------------- epilogue: TMEM -> approximate distances ----------------
-    const int quarter = warp & 3;  // this warp reads TMEM lanes 32*quarter .. +31
-    const int et = tid - 128;      // 0..127
-    // The four epilogue warps meet at a named barrier every tile, so they must
-    // leave the loop together: they do not poll the abort flag (a flag set
-    // between their loop tests could split them) and only stop when their own
-    // bounded wait on the accumulator barrier gives up, which happens to all
-    // four on the same tile.
+    // ---------------- epilogue: TMEM -> candidates / distances ----------------
+    // Thread = one query (TMEM lane), its half of the tile's 256 rows.  The
+    // eight warps meet at a named barrier every tile, so they do not poll the
+    // abort flag; they stop together when their bounded accumulator wait
+    // gives up.
+    const int ew = warp - 4;
+    const int quarter = warp & 3;
+    const int half = ew >> 2;
+    const int et = tid - 128;  // 0..255
     int local = 0;
-    for (int64_t u = blockIdx.x; u < units; u += gridDim.x, ++local) {
-      const int64_t rt = u / p.qblocks;
-      const int32_t qb = static_cast<int32_t>(u - rt * p.qblocks);
+    int64_t cur_qb = -1;
+    float alpha = 0.0f, gamma = 0.0f, cq = __int_as_float(0x7F800000);
+    int64_t q = 0;
+    bool qvalid = false;
+    for (int64_t u = u_begin; u < u_end; ++u, ++local) {
+      const int64_t qb = u / rtiles;
+      const int64_t rt = u - qb * rtiles;
+      if (qb != cur_qb) {
+        cur_qb = qb;
+        q = qb * kQM + quarter * 32 + lane;
+        qvalid = q < p.nq;
+        alpha = qvalid ? p.q_alpha[q] : 0.0f;
+        gamma = qvalid ? p.q_gamma[q] : 0.0f;
+        cq = (qvalid && !p.dense_out) ? p.q_c[q] : __int_as_float(0x7F800000);
+      }
       const int b = local & 1;
       const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
-      // stage this tile's per-query terms (double-buffered by accumulator)
-      float* qa = qpar + b * 3 * kBN;
-      for (int i = et; i < kBN; i += 128) {
-        const int64_t q = static_cast<int64_t>(qb) * kBN + i;
-        const bool in = q < p.nq;
-        qa[i] = in ? p.q_alpha[q] : 0.0f;
-        qa[kBN + i] = in ? p.q_gamma[q] : 0.0f;
-        qa[2 * kBN + i] = (in && !p.dense_out) ? p.q_thr[q] : -__int_as_float(0x7F800000);
+      // per-row terms of this tile (double buffered by accumulator)
+      float* rp = rowpar + b * 3 * kRN;
+      {
+        const int64_t lrow = rt * kRN + et;
+        const bool in = lrow < p.rows;
+        const int64_t row = p.row0 + lrow;
+        const float delta = in ? (p.row_delta ? p.row_delta[row] : 1.0f) : 0.0f;
+        const float beta = in ? (p.row_beta ? p.row_beta[row] : 0.0f) : 0.0f;
+        rp[et] = delta;
+        rp[kRN + et] = in ? p.bias_scale * beta : __int_as_float(0x7F800000);
+        rp[2 * kRN + et] = beta;
       }
-      named_sync(1, 128);
+      named_sync(1, kEpiWarps * 32);
       if (!mbar_wait_bounded(&acc_full[b], acc_phase, p.err)) {
         *abort = 1;
         break;
       }
       tc_fence_after();
-      const int64_t lrow = rt * kBM + quarter * 32 + lane;  // row within the pass
-      const bool valid = lrow < p.rows;
-      const int64_t row = p.row0 + lrow;
-      float beta = 0.0f, delta = 1.0f;
-      if (valid) {
-        if (p.row_beta) beta = __ldg(p.row_beta + row);
-        if (p.row_delta) delta = __ldg(p.row_delta + row);
-      }
-      const uint32_t taddr =
-          tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(b * kBN);
-      const int64_t qleft = p.nq - static_cast<int64_t>(qb) * kBN;
-      const int qcols = qleft < kBN ? static_cast<int>(qleft) : kBN;
-      for (int c = 0; c < kBN / 32; ++c) {
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             static_cast<uint32_t>(b * kRN + half * 128);
+      const int64_t lrow0 = rt * kRN + half * 128;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
         float v[32];
         tmem_ld32(taddr + c * 32, v);
-        if (!valid || c * 32 >= qcols) continue;
+        const int j0 = half * 128 + c * 32;
+        if (p.dense_out) {
+          if (qvalid) {
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const int j = c * 32 + t;
-          const float dist = qa[j] + beta - qa[kBN + j] * delta * v[t];
-          const int64_t q = static_cast<int64_t>(qb) * kBN + j;
-          if (j < qcols) {
-            if (p.dense_out) {
-              p.dense_out[q * p.dense_ld + lrow] = dist;
-            } else if (dist <= qa[2 * kBN + j]) {
+            for (int t = 0; t < 32; t += 4) {
+              const int64_t lrow = lrow0 + c * 32 + t;
+              float4 o;
+              o.x = approx_distance(alpha, gamma, rp[2 * kRN + j0 + t], rp[j0 + t], v[t]);
+              o.y = approx_distance(alpha, gamma, rp[2 * kRN + j0 + t + 1], rp[j0 + t + 1], v[t + 1]);
+              o.z = approx_distance(alpha, gamma, rp[2 * kRN + j0 + t + 2], rp[j0 + t + 2], v[t + 2]);
+              o.w = approx_distance(alpha, gamma, rp[2 * kRN + j0 + t + 3], rp[j0 + t + 3], v[t + 3]);
+              if (lrow + 3 < p.rows) {
+                *reinterpret_cast<float4*>(p.dense_out + q * p.dense_ld + lrow) = o;
+              } else {
+                const float ov[4] = {o.x, o.y, o.z, o.w};
+                for (int i = 0; i < 4; ++i)
+                  if (lrow + i < p.rows) p.dense_out[q * p.dense_ld + lrow + i] = ov[i];
+              }
+            }
+          }
+        } else {
+#pragma unroll
+          for (int t = 0; t < 32; ++t) {
+            // score-domain filter: x >= c_q covers every d~ <= thr_q
+            const float x = fmaf(v[t], rp[j0 + t], -rp[kRN + j0 + t]);
+            if (x >= cq) {
+              const int j = j0 + t;
+              const float dist = approx_distance(alpha, gamma, rp[2 * kRN + j], rp[j], v[t]);
               const int pos = atomicAdd(p.cand_count + q, 1);
               if (pos < p.cand_cap)
-                p.cand[q * p.cand_cap + pos] = make_key(dist, static_cast<uint32_t>(row));
+                p.cand[q * p.cand_cap + pos] =
+                    make_key(dist, static_cast<uint32_t>(p.row0 + lrow0 + c * 32 + t));
             }
           }
         }
@@ -383,6 +487,7 @@ struct TcQueryParams {
   float* alpha;
   float* gamma;
   float* eps;
+  float* scale;  // magnitude bound of the score-domain value x
 };
 
 // One warp per query: bf16 copy, exact squared norm in index order, the
@@ -443,13 +548,19 @@ __global__ void tc_query_prep_kernel(const TcQueryParams p) {
   p.alpha[q] = static_cast<float>(alpha);
   p.gamma[q] = static_cast<float>(gamma);
   p.eps[q] = static_cast<float>((lip * es + slack) * (1.0 + 1e-6));
+  double sc = qt * p.cs.max_norm_bf16;
+  if (p.metric == kCosine) sc *= p.cs.max_inv_norm;
+  if (p.metric == kL2) sc += 0.5 * p.cs.max_sqnorm;
+  p.scale[q] = static_cast<float>(sc);
 }
 
 // Per query: thr_q = (k-th smallest approximate distance of the dense sample)
 // + 2 eps_q, or +inf when the sample has fewer than k rows.
 __global__ void __launch_bounds__(kMergeThreads) tc_threshold_kernel(
     const float* __restrict__ dense, int64_t ld, int64_t rows, int32_t k, int32_t kp,
-    const float* __restrict__ eps, float* __restrict__ thr_out) {
+    const float* __restrict__ eps, const float* __restrict__ alpha,
+    const float* __restrict__ gamma, const float* __restrict__ scale, int metric,
+    float* __restrict__ thr_out, float* __restrict__ c_out) {
   __shared__ uint64_t buf[kSortN];
   __shared__ uint64_t thr;
   __shared__ int qc, nb;
@@ -474,12 +585,35 @@ __global__ void __launch_bounds__(kMergeThreads) tc_threshold_kernel(
   if (tid == 0) {
     // same rounding-safe widening as the band in tc_rerank_kernel, so that
     // band <= thr whenever T_k <= the sample's k-th distance
-    float t = __int_as_float(0x7F800000);
+    const float inf = __int_as_float(0x7F800000);
+    float t = inf;
     if (nb >= k) {
       t = key_distance(buf[k - 1]) + 2.0f * eps[q];
       t = t + fabsf(t) * 1e-6f;
     }
     thr_out[q] = t;
+    // Score-domain constant: the filter keeps x >= c, x = v*delta - bias, where
+    //   cosine: d~ <= t  <=>  delta*v >= (1 - t)/gamma            (gamma > 0)
+    //   L2    : d~ <= t  <=>  v - beta/2 >= (alpha - t)/2
+    //   IP    : d~ <= t  <=>  v >= -t
+    // lowered by a margin far above the rounding of either side, so the kept
+    // set contains every row with d~ <= t (a few extra rows are harmless).
+    // "keep everything" is -FLT_MAX, not -inf: padding rows carry x = -inf
+    // and must never pass
+    const float keep_all = -3.40282347e+38f;
+    float c;
+    if (t == inf) {
+      c = keep_all;
+    } else if (metric == kCosine) {
+      const float g = gamma[q];
+      c = g > 0.0f ? (1.0f - t) / g : (1.0f <= t ? keep_all : inf);
+    } else if (metric == kL2) {
+      c = (alpha[q] - t) * 0.5f;
+    } else {
+      c = -t;
+    }
+    if (c != inf && c != keep_all) c = fmaxf(c - (fabsf(c) + scale[q]) * 6.103515625e-05f, keep_all);
+    c_out[q] = c;
   }
 }
 
@@ -619,10 +753,6 @@ __global__ void __launch_bounds__(kRerankThreads) tc_rerank_kernel(const RerankP
   if (tid == 0) p.out_counts[q] = nb;
 }
 
-size_t tc_smem_bytes() {
-  return 1024 + static_cast<size_t>(kStages) * kStageBytes + 8 * (2 * kStages + 5) + 16 +
-         2 * 3 * kBN * sizeof(float);
-}
 
 int32_t encode_bf16_map(CUtensorMap* map, const void* base, int64_t rows, int64_t dim,
                         int64_t ld16, int box_rows) {
@@ -696,7 +826,7 @@ int32_t tc_prepare_corpus(mans_corpus* c, int metric) {
     }
     cs.max_inv_norm *= 1.0f + 1e-6f;
     c->tc_stats_host = cs;
-    int32_t rc = encode_bf16_map(&c->tc_map, c->tc_rows, n, c->dim, ld16, kBM);
+    int32_t rc = encode_bf16_map(&c->tc_map, c->tc_rows, n, c->dim, ld16, kRN);
     if (rc != MANS_OK) return rc;
   }
   if (n > 0) {
@@ -739,10 +869,10 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   const int32_t keff = static_cast<int32_t>(std::min<int64_t>(kout, n));
   const int32_t kp = pow2_at_least(keff);
   const int64_t ld16 = corpus->tc_ld16;
-  const int64_t qblocks = (nq + kBN - 1) / kBN;
-  const int64_t nq_pad = qblocks * kBN;
+  const int64_t qblocks = (nq + kQM - 1) / kQM;
+  const int64_t nq_pad = qblocks * kQM;
   int64_t sample = std::min<int64_t>(n, std::max<int64_t>(16384, std::min<int64_t>(131072, 256ll * keff)));
-  sample = std::min<int64_t>(n, (sample + kBM - 1) / kBM * kBM);
+  sample = std::min<int64_t>(n, (sample + kRN - 1) / kRN * kRN);
   const int32_t cap = 8192;
 
   size_t o = 0;
@@ -752,6 +882,8 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   const size_t o_ga = carve(o, nq * sizeof(float));
   const size_t o_ep = carve(o, nq * sizeof(float));
   const size_t o_th = carve(o, nq * sizeof(float));
+  const size_t o_sc = carve(o, nq * sizeof(float));
+  const size_t o_cq = carve(o, nq * sizeof(float));
   const size_t o_dn = carve(o, nq * sample * sizeof(float));
   const size_t o_cc = carve(o, nq * sizeof(int32_t) + sizeof(int32_t));
   const size_t o_cd = carve(o, nq * static_cast<size_t>(cap) * sizeof(uint64_t));
@@ -785,12 +917,15 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   qp.alpha = F(o_al);
   qp.gamma = F(o_ga);
   qp.eps = F(o_ep);
+  qp.scale = F(o_sc);
   tc_query_prep_kernel<<<static_cast<unsigned>((nq + 7) / 8), 256, 0, stream>>>(qp);
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc query prep launch");
 
-  CUtensorMap map_b;
-  if ((rc = encode_bf16_map(&map_b, qbf, nq_pad, corpus->dim, ld16, kBN)) != MANS_OK) return rc;
-  const size_t smem = tc_smem_bytes();
+  CUtensorMap map_q;
+  if ((rc = encode_bf16_map(&map_q, qbf, nq_pad, corpus->dim, ld16, kQM)) != MANS_OK) return rc;
+  const TcLayout lay = tc_layout(static_cast<int>(corpus->dim));
+  const size_t smem = lay.total;
+  if (lay.stages < 2) return fail(MANS_ERR_SEARCH, "dimension too large for the tensor-core pass");
   // the attribute is per device; set it on every call (cheap, no allocation)
   e = cudaFuncSetAttribute(tc_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem));
@@ -806,20 +941,22 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   tp.row_delta = metric == kCosine ? corpus->tc_delta : nullptr;
   tp.q_alpha = F(o_al);
   tp.q_gamma = F(o_ga);
-  tp.q_thr = F(o_th);
+  tp.q_c = F(o_cq);
+  tp.bias_scale = metric == kL2 ? 0.5f : 0.0f;
   tp.err = static_cast<int*>(ws->err.ptr);
   // 2. sample pass (dense)
   tp.row0 = 0;
   tp.rows = sample;
   tp.dense_out = F(o_dn);
   tp.dense_ld = sample;
-  const int64_t units_s = (sample + kBM - 1) / kBM * qblocks;
+  const int64_t units_s = (sample + kRN - 1) / kRN * qblocks;
   tc_scan_kernel<<<static_cast<unsigned>(std::min<int64_t>(units_s, ctx->num_sms)), kTcThreads,
-                   smem, stream>>>(corpus->tc_map, map_b, tp);
+                   smem, stream>>>(map_q, corpus->tc_map, tp);
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc sample launch");
   // 3. thresholds
   tc_threshold_kernel<<<static_cast<unsigned>(nq), kMergeThreads, 0, stream>>>(
-      F(o_dn), sample, sample, keff, kp, F(o_ep), F(o_th));
+      F(o_dn), sample, sample, keff, kp, F(o_ep), F(o_al), F(o_ga), F(o_sc), metric, F(o_th),
+      F(o_cq));
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc threshold launch");
   // 4. full filtered pass
   tp.rows = n;
@@ -827,10 +964,10 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   tp.cand = cand;
   tp.cand_count = ccount;
   tp.cand_cap = cap;
-  const int64_t units = (n + kBM - 1) / kBM * qblocks;
+  const int64_t units = (n + kRN - 1) / kRN * qblocks;
   cudaEvent_t stop = timing_begin(ws, stream);
   tc_scan_kernel<<<static_cast<unsigned>(std::min<int64_t>(units, ctx->num_sms)), kTcThreads, smem,
-                   stream>>>(corpus->tc_map, map_b, tp);
+                   stream>>>(map_q, corpus->tc_map, tp);
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc scan launch");
   timing_end(stop, stream);
   // 5. certify + exact re-rank
