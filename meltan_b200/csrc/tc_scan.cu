@@ -884,7 +884,8 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   const size_t o_th = carve(o, nq * sizeof(float));
   const size_t o_sc = carve(o, nq * sizeof(float));
   const size_t o_cq = carve(o, nq * sizeof(float));
-  const size_t o_dn = carve(o, nq * sample * sizeof(float));
+  const int64_t dld = (sample + 3) / 4 * 4;  // float4-aligned pitch of the dense sample
+  const size_t o_dn = carve(o, nq * dld * sizeof(float));
   const size_t o_cc = carve(o, nq * sizeof(int32_t) + sizeof(int32_t));
   const size_t o_cd = carve(o, nq * static_cast<size_t>(cap) * sizeof(uint64_t));
   if ((rc = ws->aux.reserve(o)) != MANS_OK) return rc;
@@ -948,14 +949,14 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   tp.row0 = 0;
   tp.rows = sample;
   tp.dense_out = F(o_dn);
-  tp.dense_ld = sample;
+  tp.dense_ld = dld;
   const int64_t units_s = (sample + kRN - 1) / kRN * qblocks;
   tc_scan_kernel<<<static_cast<unsigned>(std::min<int64_t>(units_s, ctx->num_sms)), kTcThreads,
                    smem, stream>>>(map_q, corpus->tc_map, tp);
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc sample launch");
   // 3. thresholds
   tc_threshold_kernel<<<static_cast<unsigned>(nq), kMergeThreads, 0, stream>>>(
-      F(o_dn), sample, sample, keff, kp, F(o_ep), F(o_al), F(o_ga), F(o_sc), metric, F(o_th),
+      F(o_dn), dld, sample, keff, kp, F(o_ep), F(o_al), F(o_ga), F(o_sc), metric, F(o_th),
       F(o_cq));
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc threshold launch");
   // 4. full filtered pass
