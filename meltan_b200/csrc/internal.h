@@ -68,12 +68,10 @@ struct mans_corpus {
   // first use, dropped when rows change)
   std::mutex tc_mu;
   bool tc_ready = false;
-  int tc_metric = -1;
+  int tc_metric = -1;  // row scaling of the bf16 copy: 1 normalised (cosine), 0 as stored
   void* tc_rows = nullptr;
   int64_t tc_ld16 = 0;
-  float* tc_stats = nullptr;  // n x 4: |r|, |r - r~|, |r~|, |r| rounded down
-  float* tc_beta = nullptr;
-  float* tc_delta = nullptr;
+  float* tc_stats = nullptr;  // n x 4: |r'|, |r' - bf16(r')|, |bf16(r')|, |r| rounded down
   mans::TcCorpusStats tc_stats_host{};
   CUtensorMap tc_map;
 };

@@ -15,12 +15,11 @@ struct TcParams {
   int64_t nq;
   int32_t dim;
   int32_t qblocks;          // ceil(nq / 128)
+  int32_t groups;           // > 0: row groups walked in step by the query blocks
   const float* row_beta;    // per-row additive term (L2: |r|^2), may be null
-  const float* row_delta;   // per-row factor (cosine: 1/|r|), may be null
   const float* q_alpha;     // per-query additive term
   const float* q_gamma;     // per-query factor of the dot
   const float* q_c;         // filter constant in the score domain (filter mode)
-  float bias_scale;         // row bias of the score domain = bias_scale * row_beta
   float* dense_out;         // dense mode: dense_out[q * dense_ld + (row - row0)]
   int64_t dense_ld;
   uint64_t* cand;           // filter mode: (distance, row) keys, cand_cap per query
@@ -35,7 +34,6 @@ struct TcCorpusStats {
   float max_resid;      // max |r - bf16(r)|
   float max_norm_bf16;  // max |bf16(r)|
   float min_norm;       // min |r|
-  float max_inv_norm;   // max 1/|r| over rows (cosine)
   float max_sqnorm;     // max |r|^2 (L2)
 };
 

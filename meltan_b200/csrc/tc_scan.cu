@@ -55,8 +55,8 @@ constexpr int kRN = 256;  // corpus rows per tile (MMA N, TMEM columns)
 constexpr int kBK = 64;   // bf16 per 128-byte swizzle row
 constexpr int kQBytes = kQM * kBK * 2;  // 16 KiB per k-block of queries
 constexpr int kRBytes = kRN * kBK * 2;  // 32 KiB per k-block of rows
-constexpr int kTcThreads = 384;         // warps 0-3 control, 4-11 epilogue
-constexpr int kEpiWarps = 8;
+constexpr int kTcThreads = 640;         // warps 0-3 control, 4-19 epilogue
+constexpr int kEpiWarps = 16;
 constexpr int kTmemCols = 512;          // two 256-column accumulators
 constexpr size_t kResidentMax = 96 * 1024;
 constexpr size_t kPipeBudget = 196 * 1024;
@@ -87,8 +87,8 @@ __host__ __device__ inline TcLayout tc_layout(int dim) {
   L.bar_off = L.a_bytes + static_cast<size_t>(L.stages) * L.stage_bytes;
   // barriers: full/empty per stage, acc_full/acc_empty x2, a_full, a_empty, drain
   const size_t bars = 8 * (2 * static_cast<size_t>(L.stages) + 7);
-  // + tmem slot / abort (16 B) + row terms 2 x 3 x kRN floats
-  L.total = 1024 + L.bar_off + bars + 16 + 2 * 3 * kRN * sizeof(float);
+  // + tmem slot / abort (16 B) + row terms 2 x 2 x kRN floats
+  L.total = 1024 + L.bar_off + bars + 16 + 2 * 2 * kRN * sizeof(float);
   return L;
 }
 
@@ -167,13 +167,18 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* err
   return false;
 }
 
-// Approximate distance from the bf16 dot v; one expression shared by the
-// dense and the filtered pass so both produce the same value for a pair.
-__device__ __forceinline__ float approx_distance(float alpha, float gamma, float beta, float delta,
-                                                 float v) {
-  return (alpha + beta) - (gamma * delta) * v;
+// Approximate distance from the bf16 dot v (rows are pre-normalised for
+// cosine, so no per-row factor remains); one expression shared by the dense
+// and the filtered pass so both produce the same value for a pair.
+__device__ __forceinline__ float approx_distance(float alpha, float gamma, float beta, float v) {
+  return (alpha + beta) - gamma * v;
 }
 
+// Epilogue variants: the dense sample pass, the filter on the raw dot
+// (cosine on normalised rows, IP) and the filter with a per-row bias (L2).
+enum TcMode : int { kDense = 0, kFilterPlain = 1, kFilterBias = 2 };
+
+template <int MODE>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_scan_kernel(const __grid_constant__ CUtensorMap map_q,
                    const __grid_constant__ CUtensorMap map_r, const TcParams p) {
@@ -192,7 +197,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* drain = a_empty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* rowpar = reinterpret_cast<float*>(tmem_slot + 4);  // [2][3][kRN]: delta, bias, beta
+  float* rowpar = reinterpret_cast<float*>(tmem_slot + 4);  // [2][2][kRN]: bias, beta (L2)
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -200,10 +205,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int nk = L.nk;
   const int64_t rtiles = (p.rows + kRN - 1) / kRN;
   const int64_t units = rtiles * p.qblocks;
-  // contiguous unit range per block, query-block major: a block keeps one
-  // query block (rarely two) while the blocks sharing it walk the rows
-  const int64_t u_begin = units * blockIdx.x / gridDim.x;
-  const int64_t u_end = units * (blockIdx.x + 1) / gridDim.x;
+  // Work split.  With `groups` > 0 block c owns query block c % qblocks and
+  // the row tiles of group c / qblocks: the qblocks blocks of a group walk
+  // the same rows in step, so each row tile comes from HBM once and from L2
+  // for the others.  Otherwise blocks take contiguous query-block-major
+  // ranges of (query block, row tile) units.
+  int64_t u_begin, u_end;
+  if (p.groups > 0) {
+    const int64_t qb = blockIdx.x % p.qblocks;
+    const int64_t g = blockIdx.x / p.qblocks;
+    u_begin = qb * rtiles + rtiles * g / p.groups;
+    u_end = qb * rtiles + rtiles * (g + 1) / p.groups;
+  } else {
+    u_begin = units * blockIdx.x / gridDim.x;
+    u_end = units * (blockIdx.x + 1) / gridDim.x;
+  }
+
 
   if (tid == 0) {
     for (int s = 0; s < L.stages; ++s) {
@@ -333,14 +350,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else if (warp >= 4) {
     // ---------------- epilogue: TMEM -> candidates / distances ----------------
-    // Thread = one query (TMEM lane), its half of the tile's 256 rows.  The
-    // eight warps meet at a named barrier every tile, so they do not poll the
-    // abort flag; they stop together when their bounded accumulator wait
+    // Thread = one query (TMEM lane) over a quarter of the tile's 256 rows
+    // (four warps per TMEM lane quarter).  With per-row terms (L2) the sixteen
+    // warps stage them and meet at a named barrier every tile, so they must not
+    // poll the abort flag; they all stop when their bounded accumulator wait
     // gives up.
     const int ew = warp - 4;
     const int quarter = warp & 3;
-    const int half = ew >> 2;
-    const int et = tid - 128;  // 0..255
+    const int part = ew >> 2;          // columns part*64 .. +63
+    const int et = tid - 128;          // 0..511
+    constexpr bool kRowTerms = MODE == kFilterBias || MODE == kDense;
     int local = 0;
     int64_t cur_qb = -1;
     float alpha = 0.0f, gamma = 0.0f, cq = __int_as_float(0x7F800000);
@@ -355,67 +374,75 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         qvalid = q < p.nq;
         alpha = qvalid ? p.q_alpha[q] : 0.0f;
         gamma = qvalid ? p.q_gamma[q] : 0.0f;
-        cq = (qvalid && !p.dense_out) ? p.q_c[q] : __int_as_float(0x7F800000);
+        cq = (qvalid && MODE != kDense) ? p.q_c[q] : __int_as_float(0x7F800000);
       }
       const int b = local & 1;
       const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
-      // per-row terms of this tile (double buffered by accumulator)
-      float* rp = rowpar + b * 3 * kRN;
-      {
-        const int64_t lrow = rt * kRN + et;
-        const bool in = lrow < p.rows;
-        const int64_t row = p.row0 + lrow;
-        const float delta = in ? (p.row_delta ? p.row_delta[row] : 1.0f) : 0.0f;
-        const float beta = in ? (p.row_beta ? p.row_beta[row] : 0.0f) : 0.0f;
-        rp[et] = delta;
-        rp[kRN + et] = in ? p.bias_scale * beta : __int_as_float(0x7F800000);
-        rp[2 * kRN + et] = beta;
+      float* rp = rowpar + b * 2 * kRN;
+      if (kRowTerms && p.row_beta) {
+        if (et < kRN) {
+          const int64_t lrow = rt * kRN + et;
+          const bool in = lrow < p.rows;
+          const float beta = in ? p.row_beta[p.row0 + lrow] : 0.0f;
+          rp[et] = in ? 0.5f * beta : __int_as_float(0x7F800000);
+          rp[kRN + et] = beta;
+        }
+        named_sync(1, kEpiWarps * 32);
       }
-      named_sync(1, kEpiWarps * 32);
       if (!mbar_wait_bounded(&acc_full[b], acc_phase, p.err)) {
         *abort = 1;
         break;
       }
       tc_fence_after();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) +
-                             static_cast<uint32_t>(b * kRN + half * 128);
-      const int64_t lrow0 = rt * kRN + half * 128;
+                             static_cast<uint32_t>(b * kRN + part * 64);
+      const int64_t lrow0 = rt * kRN + part * 64;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         float v[32];
         tmem_ld32(taddr + c * 32, v);
-        const int j0 = half * 128 + c * 32;
-        if (p.dense_out) {
+        const int j0 = part * 64 + c * 32;
+        const int64_t lr = lrow0 + c * 32;
+        if (MODE == kDense) {
           if (qvalid) {
 #pragma unroll
             for (int t = 0; t < 32; t += 4) {
-              const int64_t lrow = lrow0 + c * 32 + t;
-              float4 o;
-              o.x = approx_distance(alpha, gamma, rp[2 * kRN + j0 + t], rp[j0 + t], v[t]);
-              o.y = approx_distance(alpha, gamma, rp[2 * kRN + j0 + t + 1], rp[j0 + t + 1], v[t + 1]);
-              o.z = approx_distance(alpha, gamma, rp[2 * kRN + j0 + t + 2], rp[j0 + t + 2], v[t + 2]);
-              o.w = approx_distance(alpha, gamma, rp[2 * kRN + j0 + t + 3], rp[j0 + t + 3], v[t + 3]);
-              if (lrow + 3 < p.rows) {
-                *reinterpret_cast<float4*>(p.dense_out + q * p.dense_ld + lrow) = o;
+              float o[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                o[i] = approx_distance(alpha, gamma, p.row_beta ? rp[kRN + j0 + t + i] : 0.0f,
+                                       v[t + i]);
+              if (lr + t + 3 < p.rows) {
+                *reinterpret_cast<float4*>(p.dense_out + q * p.dense_ld + lr + t) =
+                    make_float4(o[0], o[1], o[2], o[3]);
               } else {
-                const float ov[4] = {o.x, o.y, o.z, o.w};
                 for (int i = 0; i < 4; ++i)
-                  if (lrow + i < p.rows) p.dense_out[q * p.dense_ld + lrow + i] = ov[i];
+                  if (lr + t + i < p.rows) p.dense_out[q * p.dense_ld + lr + t + i] = o[i];
               }
             }
           }
         } else {
+          float x[32];
 #pragma unroll
-          for (int t = 0; t < 32; ++t) {
-            // score-domain filter: x >= c_q covers every d~ <= thr_q
-            const float x = fmaf(v[t], rp[j0 + t], -rp[kRN + j0 + t]);
-            if (x >= cq) {
-              const int j = j0 + t;
-              const float dist = approx_distance(alpha, gamma, rp[2 * kRN + j], rp[j], v[t]);
-              const int pos = atomicAdd(p.cand_count + q, 1);
-              if (pos < p.cand_cap)
-                p.cand[q * p.cand_cap + pos] =
-                    make_key(dist, static_cast<uint32_t>(p.row0 + lrow0 + c * 32 + t));
+          for (int t = 0; t < 32; ++t) x[t] = MODE == kFilterBias ? v[t] - rp[j0 + t] : v[t];
+          // only rows of the pass: the tail of the last tile reads zero rows
+          const int64_t rem = p.rows - lr;
+          const int tmax = rem >= 32 ? 32 : (rem < 0 ? 0 : static_cast<int>(rem));
+          float m = -__int_as_float(0x7F800000);
+#pragma unroll
+          for (int t = 0; t < 32; ++t)
+            if (t < tmax) m = fmaxf(m, x[t]);
+          if (m >= cq) {
+#pragma unroll
+            for (int t = 0; t < 32; ++t) {
+              if (t < tmax && x[t] >= cq) {
+                const float beta = MODE == kFilterBias ? rp[kRN + j0 + t] : 0.0f;
+                const float dist = approx_distance(alpha, gamma, beta, v[t]);
+                const int pos = atomicAdd(p.cand_count + q, 1);
+                if (pos < p.cand_cap)
+                  p.cand[q * p.cand_cap + pos] =
+                      make_key(dist, static_cast<uint32_t>(p.row0 + lr + t));
+              }
             }
           }
         }
@@ -431,21 +458,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
-// fp32 rows -> bf16 rows (round to nearest even), one warp per row, with the
-// per-row error-bound terms |r|, |r - r~|, |r~| (double sums, rounded up).
+// fp32 rows -> bf16 rows (round to nearest even), one warp per row.  With
+// `normalise` (cosine) each row is first divided by its norm (in double), so
+// the tensor-core dot approximates dot(q, r)/|r|.  Per-row error-bound terms
+// (double sums, rounded up): |r'|, |r' - bf16(r')|, |bf16(r')| for the row r'
+// that is rounded, and |r| rounded down.
 __global__ void to_bf16_rows_kernel(const float* __restrict__ rows, int64_t n, int32_t dim,
                                     int64_t ld, __nv_bfloat16* __restrict__ out, int64_t ld16,
-                                    float* __restrict__ stats) {
+                                    float* __restrict__ stats, int normalise) {
   const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (r >= n) return;
+  double n0 = 0.0;
+  for (int c = lane; c < dim; c += 32) {
+    const double xx = rows[r * ld + c];
+    n0 += xx * xx;
+  }
+  for (int o = 16; o > 0; o >>= 1) n0 += __shfl_xor_sync(0xFFFFFFFFu, n0, o);
+  const double norm = sqrt(n0);
+  const double scale = (normalise && norm > 0.0) ? 1.0 / norm : 1.0;
   double nr = 0.0, nres = 0.0, nt = 0.0;
   for (int c = lane; c < ld16; c += 32) {
-    const float x = c < dim ? rows[r * ld + c] : 0.0f;
-    const __nv_bfloat16 b = __float2bfloat16_rn(x);
+    const double xx = c < dim ? static_cast<double>(rows[r * ld + c]) * scale : 0.0;
+    const __nv_bfloat16 b = __double2bfloat16(xx);
     out[r * ld16 + c] = b;
     const double xb = static_cast<double>(__bfloat162float(b));
-    const double xx = static_cast<double>(x);
     nr += xx * xx;
     nres += (xx - xb) * (xx - xb);
     nt += xb * xb;
@@ -459,20 +496,8 @@ __global__ void to_bf16_rows_kernel(const float* __restrict__ rows, int64_t n, i
     stats[r * 4 + 0] = __double2float_ru(sqrt(nr) * (1.0 + 1e-9));
     stats[r * 4 + 1] = __double2float_ru(sqrt(nres) * (1.0 + 1e-9));
     stats[r * 4 + 2] = __double2float_ru(sqrt(nt) * (1.0 + 1e-9));
-    stats[r * 4 + 3] = __double2float_rd(sqrt(nr) * (1.0 - 1e-9));
+    stats[r * 4 + 3] = __double2float_rd(norm * (1.0 - 1e-9));
   }
-}
-
-// Per-row affine terms of the approximate distance: L2 beta = |r|^2 (the
-// exact fp32 norm), cosine delta = 1/|r|.
-__global__ void row_affine_kernel(const float* __restrict__ norms, const float* __restrict__ stats,
-                                  int64_t n, int metric, float* __restrict__ beta,
-                                  float* __restrict__ delta) {
-  const int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (r >= n) return;
-  beta[r] = metric == kL2 ? norms[r] : 0.0f;
-  const float lo = stats[r * 4 + 3];
-  delta[r] = metric == kCosine ? (lo > 0.0f ? 1.0f / lo : 0.0f) : 1.0f;
 }
 
 struct TcQueryParams {
@@ -528,28 +553,32 @@ __global__ void tc_query_prep_kernel(const TcQueryParams p) {
   const double cacc = static_cast<double>(p.dim) * 2.384185791015625e-07;
   const double es = qres * p.cs.max_norm + qt * p.cs.max_resid +
                     cacc * qt * p.cs.max_norm_bf16 + cacc * qnorm * p.cs.max_norm;
-  double alpha = 0.0, gamma = 1.0, lip = 1.0, mag;
+  double alpha = 0.0, gamma = 1.0, lip = 1.0, mag, extra = 0.0;
   if (p.metric == kL2) {
+    // alpha and the row terms are the exact path's own fp32 |q|^2, |r|^2
     alpha = acc;
     gamma = 2.0;
     lip = 2.0;
     mag = acc + p.cs.max_sqnorm + 2.0 * (qnorm * p.cs.max_norm + es);
   } else if (p.metric == kCosine) {
+    // rows are normalised in double before rounding, so s~ ~ dot(q, r)/|r|
     alpha = 1.0;
     gamma = qnorm > 0.0 ? 1.0 / qnorm : 0.0;
-    lip = gamma * p.cs.max_inv_norm;
+    lip = gamma;
     mag = 1.0 + lip * (qnorm * p.cs.max_norm + es);
+    // the exact path divides by sqrt(fp32 |q|^2 * fp32 |r|^2); each sequential
+    // sum of squares is off by at most dim*2^-24 relatively, and |cos| <= 1
+    extra = (2.0 * p.dim + 16.0) * 5.960464477539063e-08;
   } else {
     mag = qnorm * p.cs.max_norm + es;
   }
   // rounding of both distance formulas: 64 ulps of the largest magnitude
-  const double slack = mag * 64.0 * 5.960464477539063e-08 + 1e-30;
+  const double slack = mag * 64.0 * 5.960464477539063e-08 + extra + 1e-30;
   p.qn_exact[q] = acc;
   p.alpha[q] = static_cast<float>(alpha);
   p.gamma[q] = static_cast<float>(gamma);
   p.eps[q] = static_cast<float>((lip * es + slack) * (1.0 + 1e-6));
   double sc = qt * p.cs.max_norm_bf16;
-  if (p.metric == kCosine) sc *= p.cs.max_inv_norm;
   if (p.metric == kL2) sc += 0.5 * p.cs.max_sqnorm;
   p.scale[q] = static_cast<float>(sc);
 }
@@ -786,57 +815,51 @@ int32_t encode_bf16_map(CUtensorMap* map, const void* base, int64_t rows, int64_
 
 }  // namespace
 
-// Builds (once per corpus and metric) the bf16 copy and the bound terms.
+// Builds (once per corpus and row scaling) the bf16 copy and the bound terms:
+// cosine rounds the normalised rows, L2 and IP the rows as stored.
 int32_t tc_prepare_corpus(mans_corpus* c, int metric) {
-  if (c->tc_ready && c->tc_metric == metric) return MANS_OK;
+  const int norm_mode = metric == kCosine ? 1 : 0;
+  if (c->tc_ready && c->tc_metric == norm_mode) return MANS_OK;
   DeviceGuard g(c->ctx->device);
   const int64_t n = c->n;
   const int64_t ld16 = (c->dim + 7) / 8 * 8;
+  cudaError_t e = cudaSuccess;
   if (!c->tc_rows) {
-    cudaError_t e = cudaMalloc(&c->tc_rows, std::max<int64_t>(n, 1) * ld16 * sizeof(__nv_bfloat16));
+    e = cudaMalloc(&c->tc_rows, std::max<int64_t>(n, 1) * ld16 * sizeof(__nv_bfloat16));
     if (e == cudaSuccess) e = cudaMalloc(&c->tc_stats, std::max<int64_t>(n, 1) * 4 * sizeof(float));
-    if (e == cudaSuccess) e = cudaMalloc(&c->tc_beta, std::max<int64_t>(n, 1) * sizeof(float));
-    if (e == cudaSuccess) e = cudaMalloc(&c->tc_delta, std::max<int64_t>(n, 1) * sizeof(float));
     if (e != cudaSuccess) return fail_cuda(e, "cudaMalloc(bf16 corpus)");
     c->tc_ld16 = ld16;
-    if (n > 0) {
-      to_bf16_rows_kernel<<<static_cast<unsigned>((n + 7) / 8), 256>>>(
-          c->rows, n, static_cast<int32_t>(c->dim), c->ld,
-          static_cast<__nv_bfloat16*>(c->tc_rows), ld16, c->tc_stats);
-      e = cudaGetLastError();
-      if (e == cudaSuccess) e = cudaDeviceSynchronize();
-      if (e != cudaSuccess) return fail_cuda(e, "bf16 corpus conversion");
-    }
-    // corpus-wide maxima of the bound terms (host reduction, once)
-    std::vector<float> st(static_cast<size_t>(std::max<int64_t>(n, 1)) * 4);
-    if (n > 0) {
-      e = cudaMemcpy(st.data(), c->tc_stats, n * 4 * sizeof(float), cudaMemcpyDeviceToHost);
-      if (e != cudaSuccess) return fail_cuda(e, "bf16 corpus stats");
-    }
-    TcCorpusStats cs{};
-    cs.min_norm = n > 0 ? INFINITY : 0.0f;
-    for (int64_t r = 0; r < n; ++r) {
-      cs.max_norm = std::max(cs.max_norm, st[r * 4 + 0]);
-      cs.max_resid = std::max(cs.max_resid, st[r * 4 + 1]);
-      cs.max_norm_bf16 = std::max(cs.max_norm_bf16, st[r * 4 + 2]);
-      cs.min_norm = std::min(cs.min_norm, st[r * 4 + 3]);
-      if (st[r * 4 + 3] > 0.0f) cs.max_inv_norm = std::max(cs.max_inv_norm, 1.0f / st[r * 4 + 3]);
-      const double sq = static_cast<double>(st[r * 4 + 0]) * st[r * 4 + 0];
-      cs.max_sqnorm = std::max(cs.max_sqnorm, static_cast<float>(sq * (1.0 + 1e-6)));
-    }
-    cs.max_inv_norm *= 1.0f + 1e-6f;
-    c->tc_stats_host = cs;
     int32_t rc = encode_bf16_map(&c->tc_map, c->tc_rows, n, c->dim, ld16, kRN);
     if (rc != MANS_OK) return rc;
   }
   if (n > 0) {
-    row_affine_kernel<<<static_cast<unsigned>((n + 255) / 256), 256>>>(
-        c->norms, c->tc_stats, n, metric, c->tc_beta, c->tc_delta);
-    cudaError_t e = cudaGetLastError();
+    to_bf16_rows_kernel<<<static_cast<unsigned>((n + 7) / 8), 256>>>(
+        c->rows, n, static_cast<int32_t>(c->dim), c->ld, static_cast<__nv_bfloat16*>(c->tc_rows),
+        ld16, c->tc_stats, norm_mode);
+    e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
-    if (e != cudaSuccess) return fail_cuda(e, "row affine terms");
+    if (e != cudaSuccess) return fail_cuda(e, "bf16 corpus conversion");
   }
-  c->tc_metric = metric;
+  // corpus-wide maxima of the bound terms (host reduction, once)
+  std::vector<float> st(static_cast<size_t>(std::max<int64_t>(n, 1)) * 4);
+  if (n > 0) {
+    e = cudaMemcpy(st.data(), c->tc_stats, n * 4 * sizeof(float), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return fail_cuda(e, "bf16 corpus stats");
+  }
+  TcCorpusStats cs{};
+  cs.min_norm = n > 0 ? INFINITY : 0.0f;
+  for (int64_t r = 0; r < n; ++r) {
+    cs.max_norm = std::max(cs.max_norm, st[r * 4 + 0]);
+    cs.max_resid = std::max(cs.max_resid, st[r * 4 + 1]);
+    cs.max_norm_bf16 = std::max(cs.max_norm_bf16, st[r * 4 + 2]);
+    cs.min_norm = std::min(cs.min_norm, st[r * 4 + 3]);
+    // |r|^2 of the stored row, bounded above (L2 uses it; for L2 / IP the
+    // rounded row is the stored one, so stats[0] is |r| rounded up)
+    const double up = norm_mode ? static_cast<double>(st[r * 4 + 3]) * (1.0 + 1e-6) : st[r * 4 + 0];
+    cs.max_sqnorm = std::max(cs.max_sqnorm, static_cast<float>(up * up * (1.0 + 1e-5)));
+  }
+  c->tc_stats_host = cs;
+  c->tc_metric = norm_mode;
   c->tc_ready = true;
   return MANS_OK;
 }
@@ -928,8 +951,14 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   const size_t smem = lay.total;
   if (lay.stages < 2) return fail(MANS_ERR_SEARCH, "dimension too large for the tensor-core pass");
   // the attribute is per device; set it on every call (cheap, no allocation)
-  e = cudaFuncSetAttribute(tc_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  e = cudaFuncSetAttribute(tc_scan_kernel<kDense>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tc_scan_kernel<kFilterPlain>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tc_scan_kernel<kFilterBias>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return fail_cuda(e, "tc configure");
   if (corpus->dim * sizeof(float) > 48 * 1024)
     return fail(MANS_ERR_SEARCH, "dimension too large for the tensor-core re-rank");
@@ -938,21 +967,25 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   tp.nq = nq;
   tp.dim = static_cast<int32_t>(corpus->dim);
   tp.qblocks = static_cast<int32_t>(qblocks);
-  tp.row_beta = metric == kL2 ? corpus->tc_beta : nullptr;
-  tp.row_delta = metric == kCosine ? corpus->tc_delta : nullptr;
+  tp.row_beta = metric == kL2 ? corpus->norms : nullptr;  // the exact path's fp32 |r|^2
   tp.q_alpha = F(o_al);
   tp.q_gamma = F(o_ga);
   tp.q_c = F(o_cq);
-  tp.bias_scale = metric == kL2 ? 0.5f : 0.0f;
   tp.err = static_cast<int*>(ws->err.ptr);
   // 2. sample pass (dense)
   tp.row0 = 0;
   tp.rows = sample;
   tp.dense_out = F(o_dn);
   tp.dense_ld = dld;
+  // lockstep grouping when every query block gets at least one block
+  tp.groups = qblocks <= ctx->num_sms ? static_cast<int32_t>(ctx->num_sms / qblocks) : 0;
   const int64_t units_s = (sample + kRN - 1) / kRN * qblocks;
-  tc_scan_kernel<<<static_cast<unsigned>(std::min<int64_t>(units_s, ctx->num_sms)), kTcThreads,
-                   smem, stream>>>(map_q, corpus->tc_map, tp);
+  int grid_s = static_cast<int>(std::min<int64_t>(units_s, ctx->num_sms));
+  if (tp.groups > 0) {
+    tp.groups = static_cast<int32_t>(std::min<int64_t>(tp.groups, (sample + kRN - 1) / kRN));
+    grid_s = static_cast<int>(tp.groups * qblocks);
+  }
+  tc_scan_kernel<kDense><<<grid_s, kTcThreads, smem, stream>>>(map_q, corpus->tc_map, tp);
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc sample launch");
   // 3. thresholds
   tc_threshold_kernel<<<static_cast<unsigned>(nq), kMergeThreads, 0, stream>>>(
@@ -966,9 +999,17 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   tp.cand_count = ccount;
   tp.cand_cap = cap;
   const int64_t units = (n + kRN - 1) / kRN * qblocks;
+  int grid = static_cast<int>(std::min<int64_t>(units, ctx->num_sms));
+  tp.groups = qblocks <= ctx->num_sms ? static_cast<int32_t>(ctx->num_sms / qblocks) : 0;
+  if (tp.groups > 0) {
+    tp.groups = static_cast<int32_t>(std::min<int64_t>(tp.groups, (n + kRN - 1) / kRN));
+    grid = static_cast<int>(tp.groups * qblocks);
+  }
   cudaEvent_t stop = timing_begin(ws, stream);
-  tc_scan_kernel<<<static_cast<unsigned>(std::min<int64_t>(units, ctx->num_sms)), kTcThreads, smem,
-                   stream>>>(map_q, corpus->tc_map, tp);
+  if (metric == kL2)
+    tc_scan_kernel<kFilterBias><<<grid, kTcThreads, smem, stream>>>(map_q, corpus->tc_map, tp);
+  else
+    tc_scan_kernel<kFilterPlain><<<grid, kTcThreads, smem, stream>>>(map_q, corpus->tc_map, tp);
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc scan launch");
   timing_end(stop, stream);
   // 5. certify + exact re-rank
@@ -1005,10 +1046,8 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
 void tc_free_corpus(mans_corpus* c) {
   if (c->tc_rows) cudaFree(c->tc_rows);
   if (c->tc_stats) cudaFree(c->tc_stats);
-  if (c->tc_beta) cudaFree(c->tc_beta);
-  if (c->tc_delta) cudaFree(c->tc_delta);
   c->tc_rows = nullptr;
-  c->tc_stats = c->tc_beta = c->tc_delta = nullptr;
+  c->tc_stats = nullptr;
   c->tc_ready = false;
 }
 
