@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--metric", default="cosine", choices=list(METRIC_NAMES))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--tc-min-batch", type=int, default=16,
+                    help="batches of at least this many queries use the tensor-core path")
     ap.add_argument("--no-also", action="store_true",
                     help="skip the nq = 32 and nq = 1024 measurements reported under `also`")
     return ap.parse_args()
@@ -484,7 +486,7 @@ def main():
     rows = np.array_split(np.arange(args.n), world)[rank]
     r0, r1 = int(rows[0]), int(rows[-1]) + 1
     ctx = mb.Context(local)
-    tc_min = 16
+    tc_min = args.tc_min_batch
     ctx.set_tensor_core_batch(tc_min)
     buf = mb.VectorBuffer(ctx, v[r0:r1], id_offset=r0)
     ws = mb.Workspace(ctx)

@@ -76,10 +76,10 @@ struct TcLayout {
   size_t total;
 };
 
-__host__ __device__ inline TcLayout tc_layout(int dim) {
+__host__ __device__ inline TcLayout tc_layout(int dim, int stream_queries) {
   TcLayout L;
   L.nk = (dim + kBK - 1) / kBK;
-  L.resident = static_cast<size_t>(L.nk) * kQBytes <= kResidentMax;
+  L.resident = !stream_queries && static_cast<size_t>(L.nk) * kQBytes <= kResidentMax;
   L.a_bytes = L.resident ? static_cast<size_t>(L.nk) * kQBytes : 0;
   L.stage_bytes = kRBytes + (L.resident ? 0 : kQBytes);
   size_t st = (kPipeBudget - L.a_bytes) / L.stage_bytes;
@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_scan_kernel(const __grid_constant__ CUtensorMap map_q,
                    const __grid_constant__ CUtensorMap map_r, const TcParams p) {
   extern __shared__ uint8_t smem_raw[];
-  const TcLayout L = tc_layout(p.dim);
+  const TcLayout L = tc_layout(p.dim, p.stream_queries);
   uint8_t* base =
       reinterpret_cast<uint8_t*>((reinterpret_cast<size_t>(smem_raw) + 1023) / 1024 * 1024);
   uint8_t* qres = base;                  // resident query block (nk x 16 KiB)
@@ -583,52 +583,70 @@ __global__ void tc_query_prep_kernel(const TcQueryParams p) {
   p.scale[q] = static_cast<float>(sc);
 }
 
+// k-th smallest of n values (counting repeats) by most-significant-digit
+// radix select on the order-preserving integer image of the floats: four
+// 8-bit rounds of a shared histogram.  Called by a whole block; returns the
+// value in every thread.
+template <typename Get>
+__device__ float block_kth_smallest(Get get, int64_t n, int k, uint32_t* hist, uint32_t* sh) {
+  uint32_t prefix = 0, mask = 0;
+  uint32_t kk = static_cast<uint32_t>(k);
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+      const uint32_t o = float_to_ordered(get(i));
+      if ((o & mask) == prefix) atomicAdd(&hist[(o >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t cum = 0, d = 0;
+      for (; d < 255; ++d) {
+        if (cum + hist[d] >= kk) break;
+        cum += hist[d];
+      }
+      sh[0] = kk - cum;
+      sh[1] = prefix | (d << shift);
+    }
+    __syncthreads();
+    kk = sh[0];
+    prefix = sh[1];
+    mask |= 255u << shift;
+    __syncthreads();
+  }
+  return ordered_to_float(prefix);
+}
+
 // Per query: thr_q = (k-th smallest approximate distance of the dense sample)
-// + 2 eps_q, or +inf when the sample has fewer than k rows.
-__global__ void __launch_bounds__(kMergeThreads) tc_threshold_kernel(
-    const float* __restrict__ dense, int64_t ld, int64_t rows, int32_t k, int32_t kp,
+// + 2 eps_q (+inf when the sample has fewer than k rows) and the matching
+// score-domain filter constant.
+__global__ void __launch_bounds__(256) tc_threshold_kernel(
+    const float* __restrict__ dense, int64_t ld, int64_t rows, int32_t k,
     const float* __restrict__ eps, const float* __restrict__ alpha,
     const float* __restrict__ gamma, const float* __restrict__ scale, int metric,
     float* __restrict__ thr_out, float* __restrict__ c_out) {
-  __shared__ uint64_t buf[kSortN];
-  __shared__ uint64_t thr;
-  __shared__ int qc, nb;
-  const int tid = threadIdx.x;
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t sh[2];
   const int64_t q = blockIdx.x;
-  if (tid == 0) {
-    thr = kKeyMax;
-    qc = 0;
-    nb = 0;
-  }
-  __syncthreads();
-  TopKState st{buf, &qc, &nb, &thr};
-  for (int64_t b = 0; b < rows; b += kMergeThreads) {
-    const int64_t r = b + tid;
-    const bool valid = r < rows;
-    const uint64_t key = valid ? make_key(dense[q * ld + r], static_cast<uint32_t>(r)) : kKeyMax;
-    topk_offer(st, kp, key, valid);
-    __syncthreads();
-    if (qc > kSortN - kp - kMergeThreads) topk_merge<kMergeThreads>(st, k, kp, kSortN, tid, 0);
-  }
-  if (qc > 0) topk_merge<kMergeThreads>(st, k, kp, kSortN, tid, 0);
-  if (tid == 0) {
+  const float* row = dense + q * ld;
+  const float inf = __int_as_float(0x7F800000);
+  float t = inf;
+  if (rows >= k) {
+    const float kth = block_kth_smallest([&](int64_t i) { return row[i]; }, rows, k, hist, sh);
     // same rounding-safe widening as the band in tc_rerank_kernel, so that
     // band <= thr whenever T_k <= the sample's k-th distance
-    const float inf = __int_as_float(0x7F800000);
-    float t = inf;
-    if (nb >= k) {
-      t = key_distance(buf[k - 1]) + 2.0f * eps[q];
-      t = t + fabsf(t) * 1e-6f;
-    }
+    t = kth + 2.0f * eps[q];
+    t = t + fabsf(t) * 1e-6f;
+  }
+  if (threadIdx.x == 0) {
     thr_out[q] = t;
-    // Score-domain constant: the filter keeps x >= c, x = v*delta - bias, where
-    //   cosine: d~ <= t  <=>  delta*v >= (1 - t)/gamma            (gamma > 0)
-    //   L2    : d~ <= t  <=>  v - beta/2 >= (alpha - t)/2
-    //   IP    : d~ <= t  <=>  v >= -t
+    // Score-domain constant: the filter keeps x >= c, where
+    //   cosine (normalised rows): d~ <= t  <=>  v >= (1 - t)/gamma   (gamma > 0)
+    //   L2: d~ <= t  <=>  v - beta/2 >= (alpha - t)/2
+    //   IP: d~ <= t  <=>  v >= -t
     // lowered by a margin far above the rounding of either side, so the kept
     // set contains every row with d~ <= t (a few extra rows are harmless).
-    // "keep everything" is -FLT_MAX, not -inf: padding rows carry x = -inf
-    // and must never pass
+    // "keep everything" is -FLT_MAX, not -inf: padding rows carry x = -inf.
     const float keep_all = -3.40282347e+38f;
     float c;
     if (t == inf) {
@@ -673,9 +691,24 @@ struct RerankParams {
 // Exact distance of one corpus row in the reference order.
 __device__ __forceinline__ float exact_distance(const RerankParams& p, const float* q, float qn,
                                                 int64_t row) {
+  // rows have a 16-byte pitch: 32 columns per batch of eight 16-byte loads,
+  // accumulated strictly in index order
   const float* r = p.rows + row * p.ld;
   float acc = 0.0f;
-  for (int c = 0; c < p.dim; ++c) acc = __fadd_rn(acc, __fmul_rn(__ldg(r + c), q[c]));
+  int c = 0;
+  for (; c + 32 <= p.dim; c += 32) {
+    float4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __ldg(reinterpret_cast<const float4*>(r + c) + j);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      acc = __fadd_rn(acc, __fmul_rn(v[j].x, q[c + 4 * j]));
+      acc = __fadd_rn(acc, __fmul_rn(v[j].y, q[c + 4 * j + 1]));
+      acc = __fadd_rn(acc, __fmul_rn(v[j].z, q[c + 4 * j + 2]));
+      acc = __fadd_rn(acc, __fmul_rn(v[j].w, q[c + 4 * j + 3]));
+    }
+  }
+  for (; c < p.dim; ++c) acc = __fadd_rn(acc, __fmul_rn(__ldg(r + c), q[c]));
   return finalize_distance(p.metric, acc, qn, p.metric == kIP ? 0.0f : __ldg(p.norms + row));
 }
 
@@ -947,7 +980,11 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
 
   CUtensorMap map_q;
   if ((rc = encode_bf16_map(&map_q, qbf, nq_pad, corpus->dim, ld16, kQM)) != MANS_OK) return rc;
-  const TcLayout lay = tc_layout(static_cast<int>(corpus->dim));
+  static const int stream_q = [] {
+    const char* e = getenv("MANS_TC_STREAM_QUERIES");
+    return e && e[0] == '1' ? 1 : 0;
+  }();
+  const TcLayout lay = tc_layout(static_cast<int>(corpus->dim), stream_q);
   const size_t smem = lay.total;
   if (lay.stages < 2) return fail(MANS_ERR_SEARCH, "dimension too large for the tensor-core pass");
   // the attribute is per device; set it on every call (cheap, no allocation)
@@ -964,6 +1001,7 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
     return fail(MANS_ERR_SEARCH, "dimension too large for the tensor-core re-rank");
 
   TcParams tp{};
+  tp.stream_queries = stream_q;
   tp.nq = nq;
   tp.dim = static_cast<int32_t>(corpus->dim);
   tp.qblocks = static_cast<int32_t>(qblocks);
@@ -988,9 +1026,8 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   tc_scan_kernel<kDense><<<grid_s, kTcThreads, smem, stream>>>(map_q, corpus->tc_map, tp);
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc sample launch");
   // 3. thresholds
-  tc_threshold_kernel<<<static_cast<unsigned>(nq), kMergeThreads, 0, stream>>>(
-      F(o_dn), dld, sample, keff, kp, F(o_ep), F(o_al), F(o_ga), F(o_sc), metric, F(o_th),
-      F(o_cq));
+  tc_threshold_kernel<<<static_cast<unsigned>(nq), 256, 0, stream>>>(
+      F(o_dn), dld, sample, keff, F(o_ep), F(o_al), F(o_ga), F(o_sc), metric, F(o_th), F(o_cq));
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc threshold launch");
   // 4. full filtered pass
   tp.rows = n;
