@@ -594,9 +594,18 @@ __device__ float block_kth_smallest(Get get, int64_t n, int k, uint32_t* hist, u
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
-    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-      const uint32_t o = float_to_ordered(get(i));
-      if ((o & mask) == prefix) atomicAdd(&hist[(o >> shift) & 255u], 1u);
+    // whole-warp iterations so lanes that hit the same bin can be merged into
+    // one shared atomic (values cluster in few bins, which would serialise)
+    const int64_t nround = (n + blockDim.x - 1) / blockDim.x * blockDim.x;
+    for (int64_t i = threadIdx.x; i < nround; i += blockDim.x) {
+      uint32_t bin = 0xFFFFFFFFu;
+      if (i < n) {
+        const uint32_t o = float_to_ordered(get(i));
+        if ((o & mask) == prefix) bin = (o >> shift) & 255u;
+      }
+      const unsigned peers = __match_any_sync(0xFFFFFFFFu, bin);
+      if (bin != 0xFFFFFFFFu && (threadIdx.x & 31) == __ffs(peers) - 1)
+        atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -718,6 +727,8 @@ __global__ void __launch_bounds__(kRerankThreads) tc_rerank_kernel(const RerankP
   __shared__ uint64_t thr;
   __shared__ int qc, nb, fail_flag, nlist;
   __shared__ uint32_t list[kMaxRerank];
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t hsh[2];
   const int tid = threadIdx.x;
   const int64_t q = blockIdx.x;
   for (int c = tid; c < p.dim; c += kRerankThreads) qsm[c] = p.queries[q * p.dim + c];
@@ -737,20 +748,13 @@ __global__ void __launch_bounds__(kRerankThreads) tc_rerank_kernel(const RerankP
   const uint64_t* cq = p.cand + q * p.cand_cap;
   float band = 0.0f;
   if (!fail_flag) {
-    // T_k: k-th smallest approximate distance among the candidates
-    for (int b = 0; b < cnt; b += kRerankThreads) {
-      const int i = b + tid;
-      const bool valid = i < cnt;
-      topk_offer(st, p.kp, valid ? cq[i] : kKeyMax, valid);
-      __syncthreads();
-      if (qc > kSortN - p.kp - kRerankThreads) topk_merge<kRerankThreads>(st, p.k, p.kp, kSortN, tid, 0);
-    }
-    if (qc > 0) topk_merge<kRerankThreads>(st, p.k, p.kp, kSortN, tid, 0);
-    if (tid == 0) {
-      if (nb < p.k) {
-        fail_flag = 1;  // fewer candidates than k: the sample threshold was too tight
-      } else {
-        const float tk = key_distance(buf[p.k - 1]);
+    if (cnt < p.k) {
+      if (tid == 0) fail_flag = 1;  // fewer candidates than k: the sample threshold was too tight
+    } else {
+      // T_k: k-th smallest approximate distance among the candidates
+      const float tk = block_kth_smallest([&](int64_t i) { return key_distance(cq[i]); }, cnt,
+                                          p.k, hist, hsh);
+      if (tid == 0) {
         band = tk + 2.0f * e;
         band = band + fabsf(band) * 1e-6f;
         if (!(band <= p.thr[q])) fail_flag = 1;  // filter did not cover the band
