@@ -337,24 +337,14 @@ class Runner:
         nq = q.shape[0]
         kout = min(a.k, mb.MAX_TOP_K)
         dq = torch.from_numpy(q).cuda()
-        P = 2 * nq * kout + nq  # packed [dist | ids | counts] per rank
-        loc = torch.empty((P,), dtype=torch.int32, device="cuda")
-        out = torch.empty((P,), dtype=torch.int32, device="cuda")
-        gat = torch.empty((self.world, P), dtype=torch.int32, device="cuda")
+        P = mb.shard.packed_words(nq, kout)  # packed [dist | ids | counts] per rank
         ws, ctx, buf, sp = self.ws, self.ctx, self.buf, self.sp
+        sharded = mb.ShardedFlatSearch(ctx, buf, self.world, self.dist)
+        bufs = sharded.buffers(nq, kout)
+        out = bufs[2]
 
         def step(src):
-            target = loc if self.world > 1 else out
-            mb.FlatGPUSearch.search_device(ctx, buf, ws, src.data_ptr(), nq, a.k, self.metric,
-                                           target.data_ptr(), target[nq * kout:].data_ptr(),
-                                           target[2 * nq * kout:].data_ptr(), sp)
-            if self.world > 1:
-                self.dist.all_gather_into_tensor(gat, loc)
-                mb.topk_merge_device(ctx, ws, gat.data_ptr(), gat[0, nq * kout:].data_ptr(),
-                                     gat[0, 2 * nq * kout:].data_ptr(), self.world, nq, kout,
-                                     a.k, out.data_ptr(), out[nq * kout:].data_ptr(),
-                                     out[2 * nq * kout:].data_ptr(), sp, list_stride=P)
-            return out
+            return sharded.search_device(ws, src.data_ptr(), nq, a.k, self.metric, bufs, sp)
 
         for _ in range(max(3, warmup)):
             step(dq)
@@ -483,8 +473,7 @@ def main():
     metric = METRIC_NAMES[args.metric]
     also_nq = [x for x in (32, 1024) if x != args.nq] if not args.no_also else []
     v, q_all = make_data(args.n, args.dim, max([args.nq] + also_nq))
-    rows = np.array_split(np.arange(args.n), world)[rank]
-    r0, r1 = int(rows[0]), int(rows[-1]) + 1
+    r0, r1 = mb.row_shard(args.n, world, rank)
     ctx = mb.Context(local)
     tc_min = args.tc_min_batch
     ctx.set_tensor_core_batch(tc_min)

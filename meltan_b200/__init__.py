@@ -26,3 +26,5 @@ from .core import (  # noqa: F401
 )
 from .ivf import IVFFlatSearch, Partition  # noqa: F401,E402
 from .pq import GPUADCSearch, IVFPQIndex  # noqa: F401,E402
+from . import shard  # noqa: F401,E402
+from .shard import ShardedFlatSearch, row_shard  # noqa: F401,E402

@@ -1,0 +1,99 @@
+"""Row sharding of the exact flat search, one process per GPU.
+
+The corpus rows are split contiguously: rank r holds rows [r0, r1) and
+reports global ids (r0 + local row, through the corpus ``id_offset``).  Each
+rank's per-query top-k is written into one int32 block
+
+    [ distances (nq * kout float32 bits) | ids (nq * kout uint32) | counts (nq) ]
+
+so that a single all-gather moves every rank's lists; the gathered blocks are
+then merged by (distance, id) on the device (``topk_merge_device`` with
+``list_stride`` = the block size).  This is the slice-and-merge structure of
+``ParallelFlatScan.search`` (Sources/MetalANNSCore/ParallelFlatScan.swift:
+96-155 slices, 288-315 ``mergeSorted``) with GPUs in place of host threads.
+"""
+from __future__ import annotations
+
+from . import core
+
+__all__ = ["row_shard", "packed_words", "block_views", "all_gather_blocks",
+           "ShardedFlatSearch"]
+
+
+def row_shard(n: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows [r0, r1) of ``rank``: the first n % world ranks hold one extra row
+    (the split of ``numpy.array_split``)."""
+    if world < 1 or not 0 <= rank < world or n < 0:
+        raise ValueError(f"bad shard request n={n} world={world} rank={rank}")
+    base, extra = divmod(n, world)
+    r0 = rank * base + min(rank, extra)
+    return r0, r0 + base + (1 if rank < extra else 0)
+
+
+def packed_words(nq: int, kout: int) -> int:
+    """int32 words of one rank's packed block."""
+    return 2 * nq * kout + nq
+
+
+def block_views(block, nq: int, kout: int):
+    """(distances, ids, counts) views of one packed block (a 1-D int32 torch
+    tensor); the distance view reinterprets the words as float32."""
+    import torch
+
+    if block.dim() != 1 or block.dtype != torch.int32 or block.numel() != packed_words(nq, kout):
+        raise ValueError("block must be a 1-D int32 tensor of packed_words(nq, kout) words")
+    d = block[: nq * kout].view(torch.float32).view(nq, kout)
+    i = block[nq * kout: 2 * nq * kout].view(nq, kout)
+    c = block[2 * nq * kout:]
+    return d, i, c
+
+
+def all_gather_blocks(dist, local_block, gathered):
+    """One collective: ``gathered[r]`` = rank r's block (a (world, words)
+    tensor).  Every rank calls it in the same order."""
+    if gathered.dim() != 2 or gathered.shape[1] != local_block.numel():
+        raise ValueError("gathered must be (world, words)")
+    if gathered.shape[0] == 1:
+        gathered[0].copy_(local_block)
+        return gathered
+    # the concatenated 1-D form is accepted by both NCCL and gloo
+    dist.all_gather_into_tensor(gathered.view(-1), local_block)
+    return gathered
+
+
+class ShardedFlatSearch:
+    """Exact flat search over a row-sharded corpus: this rank's shard is a
+    ``VectorBuffer`` created with ``id_offset`` = its first global row."""
+
+    def __init__(self, ctx, shard: "core.VectorBuffer", world: int, dist=None):
+        self.ctx, self.shard, self.world, self.dist = ctx, shard, world, dist
+
+    def buffers(self, nq: int, kout: int):
+        """(local block, gathered blocks, merged block) device tensors."""
+        import torch
+
+        P = packed_words(nq, kout)
+        loc = torch.empty((P,), dtype=torch.int32, device="cuda")
+        gat = torch.empty((self.world, P), dtype=torch.int32, device="cuda")
+        out = torch.empty((P,), dtype=torch.int32, device="cuda")
+        return loc, gat, out
+
+    def search_device(self, ws, d_queries: int, nq: int, k: int, metric, bufs,
+                      stream: int = 0):
+        """Search this rank's shard, gather every rank's block and merge;
+        returns the merged packed block (identical on every rank)."""
+        loc, gat, out = bufs
+        kout = min(k, core.MAX_TOP_K)
+        target = loc if self.world > 1 else out
+        core.FlatGPUSearch.search_device(self.ctx, self.shard, ws, d_queries, nq, k, metric,
+                                         target.data_ptr(), target[nq * kout:].data_ptr(),
+                                         target[2 * nq * kout:].data_ptr(), stream)
+        if self.world == 1:
+            return out
+        all_gather_blocks(self.dist, loc, gat)
+        core.topk_merge_device(self.ctx, ws, gat.data_ptr(), gat[0, nq * kout:].data_ptr(),
+                               gat[0, 2 * nq * kout:].data_ptr(), self.world, nq, kout, k,
+                               out.data_ptr(), out[nq * kout:].data_ptr(),
+                               out[2 * nq * kout:].data_ptr(), stream,
+                               list_stride=packed_words(nq, kout))
+        return out
