@@ -513,6 +513,8 @@ struct TcQueryParams {
   float* gamma;
   float* eps;
   float* scale;  // magnitude bound of the score-domain value x
+  int64_t nq_pad;      // query rows of the bf16 block (multiple of 128); rows >= nq are zeroed
+  int32_t* ccount;     // candidate counters (nq + 1, the last one counts fallbacks), zeroed
 };
 
 // One warp per query: bf16 copy, exact squared norm in index order, the
@@ -520,10 +522,17 @@ struct TcQueryParams {
 __global__ void tc_query_prep_kernel(const TcQueryParams p) {
   const int64_t q = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (q >= p.nq) return;
+  if (q >= p.nq_pad) return;
+  if (q >= p.nq) {  // padding row of the last query block
+    for (int c = lane; c < p.ld16; c += 32) p.qbf[q * p.ld16 + c] = __float2bfloat16_rn(0.0f);
+    return;
+  }
+  if (lane == 0) {
+    p.ccount[q] = 0;
+    if (q == 0) p.ccount[p.nq] = 0;
+  }
   const float* v = p.queries + q * p.dim;
   double nq2 = 0.0, nres = 0.0, nt = 0.0;
-  float acc = 0.0f;
   for (int c0 = 0; c0 < p.ld16; c0 += 32) {
     const int c = c0 + lane;
     const float x = c < p.dim ? v[c] : 0.0f;
@@ -535,11 +544,6 @@ __global__ void tc_query_prep_kernel(const TcQueryParams p) {
       nres += (xx - xb) * (xx - xb);
       nt += xb * xb;
     }
-    const int cnt = min(32, p.dim - c0);
-    for (int l = 0; l < cnt; ++l) {
-      const float y = __shfl_sync(0xFFFFFFFFu, x, l);
-      acc = __fadd_rn(acc, __fmul_rn(y, y));
-    }
   }
   for (int o = 16; o > 0; o >>= 1) {
     nq2 += __shfl_xor_sync(0xFFFFFFFFu, nq2, o);
@@ -547,6 +551,14 @@ __global__ void tc_query_prep_kernel(const TcQueryParams p) {
     nt += __shfl_xor_sync(0xFFFFFFFFu, nt, o);
   }
   if (lane != 0) return;
+  // |q|^2 of the exact path: sequential fp32 sum in index order (the warp
+  // just read the row, so these loads hit L1)
+  float acc = 0.0f;
+#pragma unroll 8
+  for (int c = 0; c < p.dim; ++c) {
+    const float y = v[c];
+    acc = __fadd_rn(acc, __fmul_rn(y, y));
+  }
   const double qnorm = sqrt(nq2), qres = sqrt(nres), qt = sqrt(nt);
   // fp32 accumulation in the tensor core and in the exact sequential path:
   // generously dim * 2^-22 of the magnitude sum each
@@ -583,65 +595,161 @@ __global__ void tc_query_prep_kernel(const TcQueryParams p) {
   p.scale[q] = static_cast<float>(sc);
 }
 
-// k-th smallest of n values (counting repeats) by most-significant-digit
-// radix select on the order-preserving integer image of the floats: four
-// 8-bit rounds of a shared histogram.  Called by a whole block; returns the
-// value in every thread.
+// Shared scratch of block_kth_smallest.
+struct KthSmem {
+  uint32_t hist[2048];
+  float list[1024];
+  float red[64];
+  float lo[4], scale[4];
+  int sel[4];
+  uint32_t sh[4];
+};
+
+__device__ __forceinline__ int kth_bin(float v, float lo, float scale) {
+  return min(2047, max(0, static_cast<int>((v - lo) * scale)));
+}
+
+// k-th smallest of n finite values (counting repeats), by a block of 256
+// threads.  Each level takes the values still in play, reduces their min and
+// max, builds a 2048-bin linear histogram over [min, max] (the bin is a
+// monotone function of the value, so order is preserved) and scans to the bin
+// holding the k-th value.  A bin of at most 1024 values is sorted exactly;
+// a larger one becomes the set in play of the next level (membership = the
+// same bin at every earlier level).  Equal min and max end the search.  The
+// result is exact, or after four levels an upper bound (see below).
 template <typename Get>
-__device__ float block_kth_smallest(Get get, int64_t n, int k, uint32_t* hist, uint32_t* sh) {
-  uint32_t prefix = 0, mask = 0;
+__device__ float block_kth_smallest(Get get, int64_t n, int k, KthSmem& S) {
+  const int tid = threadIdx.x;
+  const int nw = static_cast<int>(blockDim.x >> 5);
   uint32_t kk = static_cast<uint32_t>(k);
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
-    __syncthreads();
-    // whole-warp iterations so lanes that hit the same bin can be merged into
-    // one shared atomic (values cluster in few bins, which would serialise)
-    const int64_t nround = (n + blockDim.x - 1) / blockDim.x * blockDim.x;
-    for (int64_t i = threadIdx.x; i < nround; i += blockDim.x) {
-      uint32_t bin = 0xFFFFFFFFu;
-      if (i < n) {
-        const uint32_t o = float_to_ordered(get(i));
-        if ((o & mask) == prefix) bin = (o >> shift) & 255u;
+  auto member = [&](float v, int level) {
+    for (int l = 0; l < level; ++l)
+      if (kth_bin(v, S.lo[l], S.scale[l]) != S.sel[l]) return false;
+    return true;
+  };
+  for (int level = 0; level < 4; ++level) {
+    float lo = __int_as_float(0x7F800000), hi = -__int_as_float(0x7F800000);
+    for (int64_t i = tid; i < n; i += blockDim.x) {
+      const float v = get(i);
+      if (member(v, level)) {
+        lo = fminf(lo, v);
+        hi = fmaxf(hi, v);
       }
-      const unsigned peers = __match_any_sync(0xFFFFFFFFu, bin);
-      if (bin != 0xFFFFFFFFu && (threadIdx.x & 31) == __ffs(peers) - 1)
-        atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      lo = fminf(lo, __shfl_xor_sync(0xFFFFFFFFu, lo, o));
+      hi = fmaxf(hi, __shfl_xor_sync(0xFFFFFFFFu, hi, o));
+    }
+    if ((tid & 31) == 0) {
+      S.red[tid >> 5] = lo;
+      S.red[32 + (tid >> 5)] = hi;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      uint32_t cum = 0, d = 0;
-      for (; d < 255; ++d) {
-        if (cum + hist[d] >= kk) break;
-        cum += hist[d];
+    if (tid == 0) {
+      for (int w = 1; w < nw; ++w) {
+        S.red[0] = fminf(S.red[0], S.red[w]);
+        S.red[32] = fmaxf(S.red[32], S.red[32 + w]);
       }
-      sh[0] = kk - cum;
-      sh[1] = prefix | (d << shift);
     }
     __syncthreads();
-    kk = sh[0];
-    prefix = sh[1];
-    mask |= 255u << shift;
+    lo = S.red[0];
+    hi = S.red[32];
     __syncthreads();
+    if (!(hi > lo)) return lo;  // every value in play is equal
+    const float scale = 2047.0f / (hi - lo);
+    for (int i = tid; i < 2048; i += blockDim.x) S.hist[i] = 0;
+    __syncthreads();
+    for (int64_t i = tid; i < n; i += blockDim.x) {
+      const float v = get(i);
+      if (member(v, level)) atomicAdd(&S.hist[kth_bin(v, lo, scale)], 1u);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      uint32_t cum = 0;
+      int b = 0;
+      for (; b < 2047; ++b) {
+        if (cum + S.hist[b] >= kk) break;
+        cum += S.hist[b];
+      }
+      S.lo[level] = lo;
+      S.scale[level] = scale;
+      S.sel[level] = b;
+      S.sh[1] = kk - cum;
+      S.sh[2] = S.hist[b];
+      S.sh[3] = 0;
+    }
+    __syncthreads();
+    kk = S.sh[1];
+    const uint32_t cnt = S.sh[2];
+    // four levels without isolating 1024 values (only for value sets of
+    // extreme dynamic range): the largest value in play bounds the k-th from
+    // above, which both callers accept (a looser threshold, a wider band)
+    if (cnt > 1024 && level == 3) return hi;
+    if (cnt <= 1024) {
+      for (int64_t i = tid; i < n; i += blockDim.x) {
+        const float v = get(i);
+        if (member(v, level + 1)) {
+          const uint32_t at = atomicAdd(&S.sh[3], 1u);
+          if (at < 1024) S.list[at] = v;
+        }
+      }
+      __syncthreads();
+      const int c = static_cast<int>(min(cnt, 1024u));
+      int m = 1;
+      while (m < c) m <<= 1;
+      for (int i = c + tid; i < m; i += blockDim.x) S.list[i] = __int_as_float(0x7F800000);
+      __syncthreads();
+      for (int a = 2; a <= m; a <<= 1) {
+        for (int j = a >> 1; j > 0; j >>= 1) {
+          for (int i = tid; i < m; i += blockDim.x) {
+            const int ixj = i ^ j;
+            if (ixj > i) {
+              const float x = S.list[i], y = S.list[ixj];
+              const bool up = (i & a) == 0;
+              if ((x > y) == up) {
+                S.list[i] = y;
+                S.list[ixj] = x;
+              }
+            }
+          }
+          __syncthreads();
+        }
+      }
+      const float r = S.list[min(kk, static_cast<uint32_t>(c)) - 1];
+      __syncthreads();
+      return r;
+    }
   }
-  return ordered_to_float(prefix);
+  return 0.0f;  // not reached
 }
 
 // Per query: thr_q = (k-th smallest approximate distance of the dense sample)
 // + 2 eps_q (+inf when the sample has fewer than k rows) and the matching
 // score-domain filter constant.
-__global__ void __launch_bounds__(256) tc_threshold_kernel(
-    const float* __restrict__ dense, int64_t ld, int64_t rows, int32_t k,
+constexpr int kThresholdThreads = 1024;
+constexpr int kThresholdStageMax = 160 * 1024;  // bytes of a staged sample row
+
+__global__ void __launch_bounds__(kThresholdThreads) tc_threshold_kernel(
+    const float* __restrict__ dense, int64_t ld, int64_t rows, int32_t k, int staged,
     const float* __restrict__ eps, const float* __restrict__ alpha,
     const float* __restrict__ gamma, const float* __restrict__ scale, int metric,
     float* __restrict__ thr_out, float* __restrict__ c_out) {
-  __shared__ uint32_t hist[256];
-  __shared__ uint32_t sh[2];
+  __shared__ KthSmem ks;
+  extern __shared__ __align__(16) float stage[];  // the sample row, when staged
   const int64_t q = blockIdx.x;
   const float* row = dense + q * ld;
   const float inf = __int_as_float(0x7F800000);
   float t = inf;
+  if (staged) {
+    // every pass of the selection then reads shared memory
+    for (int64_t i = threadIdx.x; i < rows / 4; i += blockDim.x)
+      reinterpret_cast<float4*>(stage)[i] = __ldg(reinterpret_cast<const float4*>(row) + i);
+    for (int64_t i = rows / 4 * 4 + threadIdx.x; i < rows; i += blockDim.x) stage[i] = row[i];
+    __syncthreads();
+    row = stage;
+  }
   if (rows >= k) {
-    const float kth = block_kth_smallest([&](int64_t i) { return row[i]; }, rows, k, hist, sh);
+    const float kth = block_kth_smallest([&](int64_t i) { return row[i]; }, rows, k, ks);
     // same rounding-safe widening as the band in tc_rerank_kernel, so that
     // band <= thr whenever T_k <= the sample's k-th distance
     t = kth + 2.0f * eps[q];
@@ -695,6 +803,7 @@ struct RerankParams {
   uint32_t* out_ids;
   int32_t* out_counts;
   int32_t* fallbacks;  // count of queries re-scanned exactly
+  int32_t region;      // bytes of the shared staging region
 };
 
 // Exact distance of one corpus row in the reference order.
@@ -721,14 +830,61 @@ __device__ __forceinline__ float exact_distance(const RerankParams& p, const flo
   return finalize_distance(p.metric, acc, qn, p.metric == kIP ? 0.0f : __ldg(p.norms + row));
 }
 
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+}
+
+// Dynamic shared memory of tc_rerank_kernel: the query (dim floats, 16-byte
+// rounded), then one region that first holds the candidate keys and later the
+// staged corpus rows of the exact re-score.
+// The region is large (64 KB) while the query blocks fit on the SMs in one
+// wave, small (16 KB, more blocks per SM) for large batches.
+inline int rerank_region_bytes(int64_t nq, int num_sms) {
+  return nq <= num_sms ? 64 * 1024 : 16 * 1024;
+}
+inline size_t rerank_smem_bytes(int64_t dim, int region) {
+  return static_cast<size_t>((dim + 3) / 4 * 4) * sizeof(float) + region;
+}
+
+// Exact distance of a row staged in shared memory, in the reference order.
+__device__ __forceinline__ float exact_distance_smem(const RerankParams& p, const float* q,
+                                                     float qn, const float* r, int64_t row) {
+  float acc = 0.0f;
+  int c = 0;
+  for (; c + 4 <= p.dim; c += 4) {
+    const float4 v = *reinterpret_cast<const float4*>(r + c);
+    acc = __fadd_rn(acc, __fmul_rn(v.x, q[c]));
+    acc = __fadd_rn(acc, __fmul_rn(v.y, q[c + 1]));
+    acc = __fadd_rn(acc, __fmul_rn(v.z, q[c + 2]));
+    acc = __fadd_rn(acc, __fmul_rn(v.w, q[c + 3]));
+  }
+  for (; c < p.dim; ++c) acc = __fadd_rn(acc, __fmul_rn(r[c], q[c]));
+  return finalize_distance(p.metric, acc, qn, p.metric == kIP ? 0.0f : __ldg(p.norms + row));
+}
+
+// Per query: certify the candidate list, then re-score the band exactly.
+//   T_k  = k-th smallest approximate distance among the candidates
+//   band = T_k + 2 eps (rounded up); every row of the exact top-k has an
+//          approximate distance <= band, so the exact top-k of the band rows
+//          is the exact top-k of the corpus, provided the filter kept every
+//          row up to band (band <= thr) and the list did not overflow.
+// Otherwise the query is re-scanned exactly over all rows by this block.
 __global__ void __launch_bounds__(kRerankThreads) tc_rerank_kernel(const RerankParams p) {
-  extern __shared__ float qsm[];  // query, dim floats
-  __shared__ uint64_t buf[kSortN];
+  extern __shared__ __align__(16) unsigned char rsm[];
+  float* qsm = reinterpret_cast<float*>(rsm);
+  unsigned char* region = rsm + static_cast<size_t>((p.dim + 3) / 4 * 4) * sizeof(float);
+  uint64_t* skeys = reinterpret_cast<uint64_t*>(region);  // candidate keys (phase 1)
+  float* srows = reinterpret_cast<float*>(region);         // staged rows (phase 2)
+  __shared__ uint64_t ekeys[kMaxRerank];                    // exact keys of the band
   __shared__ uint64_t thr;
   __shared__ int qc, nb, fail_flag, nlist;
+  __shared__ float band_sh;
   __shared__ uint32_t list[kMaxRerank];
-  __shared__ uint32_t hist[256];
-  __shared__ uint32_t hsh[2];
+  __shared__ KthSmem ks;
   const int tid = threadIdx.x;
   const int64_t q = blockIdx.x;
   for (int c = tid; c < p.dim; c += kRerankThreads) qsm[c] = p.queries[q * p.dim + c];
@@ -737,84 +893,97 @@ __global__ void __launch_bounds__(kRerankThreads) tc_rerank_kernel(const RerankP
   const float e = p.eps[q];
   const float qn = p.qn_exact[q];
   if (tid == 0) {
-    thr = kKeyMax;
-    qc = 0;
-    nb = 0;
     nlist = 0;
-    fail_flag = total > p.cand_cap ? 1 : 0;
+    fail_flag = (total > p.cand_cap || cnt < p.k) ? 1 : 0;
   }
-  __syncthreads();
-  TopKState st{buf, &qc, &nb, &thr};
   const uint64_t* cq = p.cand + q * p.cand_cap;
-  float band = 0.0f;
+  const bool stage_keys = cnt * 8 <= p.region;
+  if (stage_keys)
+    for (int i = tid; i < cnt; i += kRerankThreads) skeys[i] = cq[i];
+  const uint64_t* keys = stage_keys ? skeys : cq;
+  __syncthreads();
   if (!fail_flag) {
-    if (cnt < p.k) {
-      if (tid == 0) fail_flag = 1;  // fewer candidates than k: the sample threshold was too tight
-    } else {
-      // T_k: k-th smallest approximate distance among the candidates
-      const float tk = block_kth_smallest([&](int64_t i) { return key_distance(cq[i]); }, cnt,
-                                          p.k, hist, hsh);
-      if (tid == 0) {
-        band = tk + 2.0f * e;
-        band = band + fabsf(band) * 1e-6f;
-        if (!(band <= p.thr[q])) fail_flag = 1;  // filter did not cover the band
-        thr = __float_as_uint(band);  // pass the band through shared memory
-      }
+    const float tk = block_kth_smallest([&](int64_t i) { return key_distance(keys[i]); }, cnt,
+                                        p.k, ks);
+    if (tid == 0) {
+      float band = tk + 2.0f * e;
+      band = band + fabsf(band) * 1e-6f;
+      if (!(band <= p.thr[q])) fail_flag = 1;  // the filter did not cover the band
+      band_sh = band;
     }
     __syncthreads();
+    if (!fail_flag) {
+      const float band = band_sh;
+      for (int i = tid; i < cnt; i += kRerankThreads) {
+        const uint64_t key = keys[i];
+        if (key_distance(key) <= band) {
+          const int pos = atomicAdd(&nlist, 1);
+          if (pos < kMaxRerank) list[pos] = key_id(key);
+        }
+      }
+      __syncthreads();
+      if (tid == 0 && nlist > kMaxRerank) fail_flag = 1;
+      __syncthreads();
+    }
   }
   if (!fail_flag) {
-    band = __uint_as_float(static_cast<uint32_t>(thr));
-    // rows within the band
-    for (int i = tid; i < cnt; i += kRerankThreads) {
-      if (key_distance(cq[i]) <= band) {
-        const int pos = atomicAdd(&nlist, 1);
-        if (pos < kMaxRerank) list[pos] = key_id(cq[i]);
+    // exact re-score of the band: rows staged in shared memory by cp.async
+    // (all loads of a round in flight), one thread per row
+    const int m = nlist;
+    const int pitch = (p.dim + 3) / 4 * 4 + 4;  // floats; +4 spreads rows over the banks
+    const int per_round = max(1, min(kRerankThreads, p.region / (pitch * 4)));
+    const int chunks = (p.dim + 3) / 4;  // 16-byte pieces of one row
+    for (int b = 0; b < m; b += per_round) {
+      const int rn = min(per_round, m - b);
+      for (int t = tid; t < rn * chunks; t += kRerankThreads) {
+        const int r = t / chunks, c = t - r * chunks;
+        cp_async16(srows + r * pitch + 4 * c, p.rows + static_cast<int64_t>(list[b + r]) * p.ld + 4 * c);
       }
+      cp_async_wait_all();
+      __syncthreads();
+      if (tid < rn) {
+        const int64_t row = list[b + tid];
+        ekeys[b + tid] = make_key(exact_distance_smem(p, qsm, qn, srows + tid * pitch, row),
+                                  static_cast<uint32_t>(row + p.id_offset));
+      }
+      __syncthreads();
     }
+    int mp = 1;
+    while (mp < m) mp <<= 1;
+    for (int i = m + tid; i < mp; i += kRerankThreads) ekeys[i] = kKeyMax;
     __syncthreads();
-    if (nlist > kMaxRerank) fail_flag = 1;
-    __syncthreads();
+    bitonic_sort_keys<kRerankThreads>(ekeys, mp, tid, 0);
+    const int have = min(m, p.k);
+    for (int i = tid; i < p.kout; i += kRerankThreads) {
+      p.out_dist[q * p.kout + i] = i < have ? key_distance(ekeys[i]) : __int_as_float(0x7F800000);
+      p.out_ids[q * p.kout + i] = i < have ? key_id(ekeys[i]) : kEmptyId;
+    }
+    if (tid == 0) p.out_counts[q] = have;
+    return;
   }
+  // certificate failed: exact scan of every row by this block
   if (tid == 0) {
+    atomicAdd(p.fallbacks, 1);
     thr = kKeyMax;
     qc = 0;
     nb = 0;
   }
   __syncthreads();
-  if (!fail_flag) {
-    // exact re-score of the band, (distance, id) top-k
-    const int m = nlist;
-    for (int b = 0; b < m; b += kRerankThreads) {
-      const int i = b + tid;
-      const bool valid = i < m;
-      uint64_t key = kKeyMax;
-      if (valid) {
-        const int64_t row = list[i];
-        key = make_key(exact_distance(p, qsm, qn, row), static_cast<uint32_t>(row + p.id_offset));
-      }
-      topk_offer(st, p.kp, key, valid);
-      __syncthreads();
-      if (qc > kSortN - p.kp - kRerankThreads) topk_merge<kRerankThreads>(st, p.k, p.kp, kSortN, tid, 0);
-    }
-  } else {
-    // certificate failed: exact scan of every row by this block
-    if (tid == 0) atomicAdd(p.fallbacks, 1);
-    for (int64_t b = 0; b < p.n; b += kRerankThreads) {
-      const int64_t row = b + tid;
-      const bool valid = row < p.n;
-      uint64_t key = kKeyMax;
-      if (valid) key = make_key(exact_distance(p, qsm, qn, row), static_cast<uint32_t>(row + p.id_offset));
-      topk_offer(st, p.kp, key, valid);
-      __syncthreads();
-      if (qc > kSortN - p.kp - kRerankThreads) topk_merge<kRerankThreads>(st, p.k, p.kp, kSortN, tid, 0);
-    }
+  TopKState st{ekeys, &qc, &nb, &thr};
+  for (int64_t b = 0; b < p.n; b += kRerankThreads) {
+    const int64_t row = b + tid;
+    const bool valid = row < p.n;
+    uint64_t key = kKeyMax;
+    if (valid) key = make_key(exact_distance(p, qsm, qn, row), static_cast<uint32_t>(row + p.id_offset));
+    topk_offer(st, p.kp, key, valid);
+    __syncthreads();
+    if (qc > kSortN - p.kp - kRerankThreads) topk_merge<kRerankThreads>(st, p.k, p.kp, kSortN, tid, 0);
   }
   if (qc > 0) topk_merge<kRerankThreads>(st, p.k, p.kp, kSortN, tid, 0);
   for (int i = tid; i < p.kout; i += kRerankThreads) {
     const bool have = i < nb;
-    p.out_dist[q * p.kout + i] = have ? key_distance(buf[i]) : __int_as_float(0x7F800000);
-    p.out_ids[q * p.kout + i] = have ? key_id(buf[i]) : kEmptyId;
+    p.out_dist[q * p.kout + i] = have ? key_distance(ekeys[i]) : __int_as_float(0x7F800000);
+    p.out_ids[q * p.kout + i] = have ? key_id(ekeys[i]) : kEmptyId;
   }
   if (tid == 0) p.out_counts[q] = nb;
 }
@@ -885,7 +1054,9 @@ int32_t tc_prepare_corpus(mans_corpus* c, int metric) {
   }
   TcCorpusStats cs{};
   cs.min_norm = n > 0 ? INFINITY : 0.0f;
+  bool finite = true;
   for (int64_t r = 0; r < n; ++r) {
+    for (int j = 0; j < 4; ++j) finite = finite && std::isfinite(st[r * 4 + j]);
     cs.max_norm = std::max(cs.max_norm, st[r * 4 + 0]);
     cs.max_resid = std::max(cs.max_resid, st[r * 4 + 1]);
     cs.max_norm_bf16 = std::max(cs.max_norm_bf16, st[r * 4 + 2]);
@@ -895,6 +1066,7 @@ int32_t tc_prepare_corpus(mans_corpus* c, int metric) {
     const double up = norm_mode ? static_cast<double>(st[r * 4 + 3]) * (1.0 + 1e-6) : st[r * 4 + 0];
     cs.max_sqnorm = std::max(cs.max_sqnorm, static_cast<float>(up * up * (1.0 + 1e-5)));
   }
+  if (!finite) cs.max_norm = INFINITY;  // a NaN / infinite row: the bound does not apply
   c->tc_stats_host = cs;
   c->tc_metric = norm_mode;
   c->tc_ready = true;
@@ -912,6 +1084,10 @@ static size_t carve(size_t& o, size_t bytes) {
 bool tc_applicable(const mans_corpus* c, int metric) {
   if (c->n <= 0 || c->n >= (1ll << 31)) return false;
   if (metric == kCosine && c->tc_ready && c->tc_stats_host.min_norm < 1e-6f) return false;
+  // a NaN or infinite row makes the bound meaningless: exact scan
+  if (c->tc_ready && !(std::isfinite(c->tc_stats_host.max_norm) &&
+                       std::isfinite(c->tc_stats_host.max_sqnorm)))
+    return false;
   return true;
 }
 
@@ -962,10 +1138,7 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   int32_t* fallbacks = ccount + nq;
   uint64_t* cand = reinterpret_cast<uint64_t*>(A + o_cd);
 
-  cudaError_t e = cudaMemsetAsync(qbf, 0, nq_pad * ld16 * sizeof(__nv_bfloat16), stream);
-  if (e == cudaSuccess) e = cudaMemsetAsync(ccount, 0, (nq + 1) * sizeof(int32_t), stream);
-  if (e != cudaSuccess) return fail_cuda(e, "tc scratch clear");
-
+  cudaError_t e = cudaSuccess;
   TcQueryParams qp{};
   qp.queries = d_queries;
   qp.nq = nq;
@@ -979,7 +1152,9 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   qp.gamma = F(o_ga);
   qp.eps = F(o_ep);
   qp.scale = F(o_sc);
-  tc_query_prep_kernel<<<static_cast<unsigned>((nq + 7) / 8), 256, 0, stream>>>(qp);
+  qp.nq_pad = nq_pad;
+  qp.ccount = ccount;
+  tc_query_prep_kernel<<<static_cast<unsigned>((nq_pad + 7) / 8), 256, 0, stream>>>(qp);
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc query prep launch");
 
   CUtensorMap map_q;
@@ -1000,6 +1175,12 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(tc_scan_kernel<kFilterBias>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tc_threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kThresholdStageMax);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tc_rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(rerank_smem_bytes(corpus->dim, 64 * 1024)));
   if (e != cudaSuccess) return fail_cuda(e, "tc configure");
   if (corpus->dim * sizeof(float) > 48 * 1024)
     return fail(MANS_ERR_SEARCH, "dimension too large for the tensor-core re-rank");
@@ -1030,8 +1211,16 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   tc_scan_kernel<kDense><<<grid_s, kTcThreads, smem, stream>>>(map_q, corpus->tc_map, tp);
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc sample launch");
   // 3. thresholds
-  tc_threshold_kernel<<<static_cast<unsigned>(nq), 256, 0, stream>>>(
-      F(o_dn), dld, sample, keff, F(o_ep), F(o_al), F(o_ga), F(o_sc), metric, F(o_th), F(o_cq));
+  // one wave of queries: wide blocks over a staged row (latency); larger
+  // batches: narrow blocks reading global memory (occupancy)
+  const bool one_wave = nq <= ctx->num_sms;
+  const int staged =
+      one_wave && dld * sizeof(float) <= static_cast<size_t>(kThresholdStageMax) ? 1 : 0;
+  const size_t th_smem = staged ? dld * sizeof(float) : 0;
+  tc_threshold_kernel<<<static_cast<unsigned>(nq), one_wave ? kThresholdThreads : 256, th_smem,
+                        stream>>>(
+      F(o_dn), dld, sample, keff, staged, F(o_ep), F(o_al), F(o_ga), F(o_sc), metric, F(o_th),
+      F(o_cq));
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc threshold launch");
   // 4. full filtered pass
   tp.rows = n;
@@ -1076,8 +1265,9 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   rp.out_ids = d_out_ids;
   rp.out_counts = d_out_counts;
   rp.fallbacks = fallbacks;
-  tc_rerank_kernel<<<static_cast<unsigned>(nq), kRerankThreads, corpus->dim * sizeof(float),
-                     stream>>>(rp);
+  rp.region = rerank_region_bytes(nq, ctx->num_sms);
+  tc_rerank_kernel<<<static_cast<unsigned>(nq), kRerankThreads,
+                     rerank_smem_bytes(corpus->dim, rp.region), stream>>>(rp);
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc rerank launch");
   ws->tc_fallbacks = fallbacks;
   ws->launches += 5;

@@ -132,3 +132,23 @@ def test_tc_full_size_1m_x_384_batch_1024(ctx):
         pick = np.arange(0, 1024, 128)
         same(tuple(a[pick] for a in got), O.flat_search(v, q[pick], k, O.COSINE))
     buf.close()
+
+
+def test_tc_nonfinite_rows_match_the_exact_scan():
+    """A NaN or infinite row voids the bf16 error bound: the batch goes to the
+    exact CUDA-core scan, so both settings return the same lists."""
+    rng = np.random.default_rng(9)
+    v = unit_rows(rng, 6000, 64)
+    v[17, 3] = np.nan
+    v[4000, 0] = np.inf
+    q = unit_rows(rng, 20, 64)
+    c = mb.Context(0)
+    try:
+        for mg, _ in MET:
+            c.set_tensor_core_batch(1)
+            got = run(c, v, q, 10, mg)
+            c.set_tensor_core_batch(0)
+            ref = run(c, v, q, 10, mg)
+            same(got, ref)
+    finally:
+        c.close()
