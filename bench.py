@@ -53,8 +53,33 @@ def parse():
     ap.add_argument("--tc-min-batch", type=int, default=16,
                     help="batches of at least this many queries use the tensor-core path")
     ap.add_argument("--no-also", action="store_true",
-                    help="skip the nq = 32 and nq = 1024 measurements reported under `also`")
-    return ap.parse_args()
+                    help="skip the extra measurements reported under `also`")
+    ap.add_argument("--workload", default="flat", choices=["flat", "ivf", "ivfpq"],
+                    help="flat: exact scan (configs[1]); ivf: IVF-flat (configs[2]); "
+                         "ivfpq: IVF-PQ ADC (configs[3])")
+    ap.add_argument("--nlist", type=int, default=None)
+    ap.add_argument("--nprobe", type=int, default=None)
+    ap.add_argument("--components", type=int, default=None)
+    ap.add_argument("--pq-m", type=int, default=16)
+    a = ap.parse_args()
+    # per-workload defaults (BASELINE.json configs[2] and [3])
+    if a.workload == "ivf":
+        a.nlist = a.nlist or 1024
+        a.nprobe = a.nprobe or 8
+        a.components = a.components or 1024
+    elif a.workload == "ivfpq":
+        a.nlist = a.nlist or 4096
+        a.nprobe = a.nprobe or 32
+        a.components = a.components or 4096
+        if "--n" not in sys.argv:
+            a.n = 10_000_000
+        if "--dim" not in sys.argv:
+            a.dim = 128
+        if "--metric" not in sys.argv:
+            a.metric = "l2"
+        if "--nq" not in sys.argv:
+            a.nq = 1024
+    return a
 
 
 def make_data(n, dim, nq, seed=0):
@@ -69,16 +94,21 @@ def make_data(n, dim, nq, seed=0):
 def make_mixture(n, dim, components, nq, sigma=0.3, seed=0):
     """BASELINE.json configs[2..3] generator: centres = normalise(N(0,1)),
     x = centre[assign] + sigma * N(0,1), renormalised; queries drawn from the
-    same mixture after the database."""
+    same mixture after the database.  The noise is drawn in row chunks, which
+    yields the same values as one draw and bounds the temporaries."""
     rng = np.random.default_rng(seed)
     centres = rng.standard_normal((components, dim), dtype=np.float32)
     centres /= np.linalg.norm(centres, axis=1, keepdims=True)
 
     def draw(m):
         a = rng.integers(0, components, m)
-        x = centres[a] + np.float32(sigma) * rng.standard_normal((m, dim), dtype=np.float32)
-        x /= np.linalg.norm(x, axis=1, keepdims=True)
-        return x.astype(np.float32)
+        x = np.empty((m, dim), np.float32)
+        for c0 in range(0, m, 1 << 20):
+            c1 = min(m, c0 + (1 << 20))
+            x[c0:c1] = centres[a[c0:c1]] + np.float32(sigma) * rng.standard_normal(
+                (c1 - c0, dim), dtype=np.float32)
+            x[c0:c1] /= np.linalg.norm(x[c0:c1], axis=1, keepdims=True)
+        return x
 
     return draw(n), draw(nq)
 
@@ -264,6 +294,9 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    if args.workload != "flat":
+        run_reference_index(args)
+        return
     metric = METRIC_NAMES[args.metric]
     v, q = make_data(args.n, args.dim, max(args.nq, 1))
     import oracle as O
@@ -298,6 +331,34 @@ def run_reference(args):
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def run_reference_index(args):
+    """Reference arm of the IVF workloads: the restated single-threaded
+    reference search per query (index artefacts trained as in our arm)."""
+    v, q, art = build_index_data(args, max(args.nq, 1))
+    qs = q[:max(args.nq, 1)]
+    one = index_searcher(args, v, art)
+    for i in range(args.warmup):
+        one(qs[i % len(qs)])
+    times = []
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        for j in range(args.nq):
+            one(qs[j])
+        times.append(time.perf_counter() - t)
+    total = sum(times)
+    value = args.nq * args.steps / total
+    print(json.dumps({
+        "impl": "reference", "metric": "queries_per_sec", "value": value, "unit": "queries/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / args.steps, "p50_us": 1e6 * p50(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": index_workload_config(args),
+        "cpu_baseline": {"value": value, "unit": "queries/s", "cores": 1, "kind": "port",
+                         "sample": f"{args.nq} queries per step, one thread"},
+        "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0}}), flush=True)
 
 
 def workload_config(args, nq=None):
@@ -447,6 +508,292 @@ def roofline(args, res, shard_rows, metric, tc_min_batch, workload):
             "peak_source": f"{kind} hbm_gbs"}
 
 
+# ---------------------------------------------------------------------------
+# IVF-flat and IVF-PQ workloads
+# ---------------------------------------------------------------------------
+
+def index_workload_config(args, nq=None, nprobe=None):
+    nq = args.nq if nq is None else nq
+    nprobe = args.nprobe if nprobe is None else nprobe
+    base = f"{args.n}x{args.dim}_mix{args.components}_nlist{args.nlist}"
+    if args.workload == "ivf":
+        name = f"ivf_flat_{base}_nprobe{nprobe}_{args.metric}_top{args.k}_nq{nq}"
+    else:
+        name = f"ivfpq_{base}_m{args.pq_m}_nprobe{nprobe}_{args.metric}_top{args.k}_nq{nq}"
+    cfg = {"workload": name, "n": args.n, "dim": args.dim, "nq": nq, "k": args.k,
+           "metric": args.metric, "nlist": args.nlist, "nprobe": nprobe,
+           "components": args.components, "parallelism": f"replica{args.gpus}",
+           "l2": "probed lists differ per query; each step streams its lists once "
+                 "(no flush; lists of one batch may hit L2)"}
+    if args.workload == "ivfpq":
+        cfg["pq_m"] = args.pq_m
+        cfg["pq_ks"] = 256
+    return cfg
+
+
+def build_index_data(args, nq_max, device=None):
+    """Synthetic mixture data and the trained index artefacts (build-time
+    steps outside the timed search path)."""
+    metric = METRIC_NAMES[args.metric]
+    v, q = make_mixture(args.n, args.dim, args.components, nq_max)
+    if args.workload == "ivf":
+        cent, assign = train_partition(v, args.nlist, metric, device=device)
+        return v, q, {"centroids": cent, "assign": assign}
+    coarse, cb, codes, off, flat = train_ivfpq(v, args.nlist, args.pq_m, metric=metric,
+                                               device=device)
+    return v, q, {"coarse": coarse, "codebooks": cb, "codes": codes, "offsets": off,
+                  "lists": flat}
+
+
+def probed_list_rows(args, art, q):
+    """Rows of the lists each query probes (the per-query unit of the
+    roofline): top-nprobe centroids by the search's own key, with torch."""
+    import torch
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    qt = torch.from_numpy(q).to(dev)
+    if args.workload == "ivf":
+        c = torch.from_numpy(art["centroids"]).to(dev)
+        sizes = torch.bincount(torch.from_numpy(art["assign"]).to(dev), minlength=args.nlist)
+        dots = qt @ c.T
+        cn = (c * c).sum(1)
+        metric = METRIC_NAMES[args.metric]
+        key = -dots if metric == 2 else (cn - 2 * dots if metric == 1 else
+                                         -dots / cn.clamp(min=1e-20).sqrt())
+    else:
+        c = torch.from_numpy(art["coarse"]).to(dev)
+        off = torch.from_numpy(art["offsets"]).to(dev)
+        sizes = off[1:] - off[:-1]
+        key = torch.cdist(qt, c)
+    top = torch.topk(key, min(args.nprobe, key.shape[1]), dim=1, largest=False).indices
+    return sizes[top].sum(1).cpu().numpy().astype(np.int64)
+
+
+def index_searcher(args, v, art):
+    """One query through the restated reference search (single-threaded, as
+    IVFFlatSearch.scanProbedLists / _IVFPQIndex.search run)."""
+    import oracle as O
+    metric = METRIC_NAMES[args.metric]
+    if args.workload == "ivf":
+        assign = art["assign"]
+        order = np.argsort(assign, kind="stable").astype(np.uint32)
+        off = np.concatenate([[0], np.cumsum(np.bincount(assign, minlength=args.nlist))])
+        packed = v[order]
+        pn = O.row_norms(packed)
+
+        def one(x):
+            O.ivf_search(art["centroids"], packed, pn, order, off, x, args.k, args.nprobe, metric)
+    else:
+        def one(x):
+            O.ivfpq_search(art["coarse"], art["codebooks"], art["codes"], art["offsets"],
+                           art["lists"], x, args.k, args.nprobe, metric)
+    return one
+
+
+def cpu_index_qps(args, v, q, art, seconds):
+    """The restated reference search on a bounded sample of queries."""
+    one = index_searcher(args, v, art)
+    one(q[0])
+    t0 = time.perf_counter()
+    done = 0
+    while True:
+        one(q[done % len(q)])
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return done / el, done
+
+
+def measure_index(torch, ws, search_dev, search_host, q, kout, steps, warmup, with_clocks):
+    """Device-timed steps (inputs resident) and end-to-end steps through the
+    host C ABI (pinned buffers), as Runner.measure does for the flat scan."""
+    nq = q.shape[0]
+    dq = torch.from_numpy(q).cuda()
+    od = torch.empty((nq, kout), dtype=torch.float32, device="cuda")
+    oi = torch.empty((nq, kout), dtype=torch.int32, device="cuda")
+    oc = torch.empty((nq,), dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step():
+        search_dev(dq.data_ptr(), nq, od.data_ptr(), oi.data_ptr(), oc.data_ptr(), sp)
+
+    for _ in range(max(3, warmup)):
+        step()
+    ws.check(sp)
+    ws.stats()
+    ws.set_timing(True)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    clocks = ClockSampler(torch.cuda.current_device()) if with_clocks else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(steps):
+        ev[i][0].record(stream)
+        step()
+        ev[i][1].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clock_info = clocks.stop() if clocks else None
+    ws.check(sp)
+    kern_ms, kern_launches, total_launches = ws.stats()
+    ws.set_timing(False)
+    total_ms = t0.elapsed_time(t1)
+    step_ms = [x.elapsed_time(y) for x, y in ev]
+    dev_out = (od.cpu().numpy(), oi.cpu().numpy(), oc.cpu().numpy())
+
+    hq = torch.from_numpy(q).pin_memory()
+    hd = torch.empty((nq, kout), dtype=torch.float32).pin_memory()
+    hi = torch.empty((nq, kout), dtype=torch.int32).pin_memory()
+    hc = torch.empty((nq,), dtype=torch.int32).pin_memory()
+
+    def e2e():
+        search_host(hq.data_ptr(), nq, hd.data_ptr(), hi.data_ptr(), hc.data_ptr())
+
+    for _ in range(max(3, warmup)):
+        e2e()
+    e2e_times = []
+    for _ in range(steps):
+        t = time.perf_counter()
+        e2e()
+        e2e_times.append(time.perf_counter() - t)
+    ok = bool(np.array_equal(dev_out[2], hc.numpy()) and np.array_equal(dev_out[1], hi.numpy())
+              and np.array_equal(dev_out[0], hd.numpy()))
+    return {"nq": nq, "steps": steps, "total_ms": total_ms, "e2e_ms": 1e3 * sum(e2e_times),
+            "kern_avg_ms": kern_ms / max(kern_launches, 1), "kern_launches": kern_launches,
+            "launches": total_launches, "p50_ms": p50(step_ms), "e2e_p50_s": p50(e2e_times),
+            "clocks": clock_info, "ok": ok, "kout": kout}
+
+
+def index_roofline(args, res, list_rows):
+    """HBM roofline of the timed kernel: the list scan (IVF-flat) or the ADC
+    scoring kernel (IVF-PQ), with the per-query bytes of the probed lists:
+    IVF-flat rows (d*4) + norm (4) + id (4); IVF-PQ code (m) + id (4)."""
+    peak, src = measured_peaks()
+    per_row = args.dim * 4 + 8 if args.workload == "ivf" else args.pq_m + 4
+    alg = float(list_rows.sum()) * per_row
+    kern_s = res["kern_avg_ms"] * 1e-3
+    achieved = alg / kern_s / 1e9 if kern_s > 0 else 0.0
+    wl = index_workload_config(args, res["nq"])["workload"]
+    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "traffic": committed_traffic(wl),
+            "kernel": "scan_topk_kernel (probed lists)" if args.workload == "ivf"
+            else "pq_adc_kernel", "kernel_avg_us": 1e3 * res["kern_avg_ms"],
+            "algorithmic_bytes_per_launch": alg,
+            "peak_source": f"{src} hbm_gbs (STREAM copy)"}
+
+
+def run_index(args, torch, mb, lib, world, rank, dist):
+    metric = METRIC_NAMES[args.metric]
+    extra = [] if args.no_also else (
+        [(1, p) for p in (4, 32) if p != args.nprobe] + [(256, args.nprobe)]
+        if args.workload == "ivf" else [(256, args.nprobe)])
+    nq_max = max([args.nq] + [x for x, _ in extra])
+    t_build = time.perf_counter()
+    v, q_all, art = build_index_data(args, nq_max)
+    ctx = mb.Context(torch.cuda.current_device())
+    ws = mb.Workspace(ctx)
+    L = lib
+    kout = min(args.k, mb.MAX_TOP_K)
+    if args.workload == "ivf":
+        part = mb.Partition.from_assignment(ctx, v, art["centroids"], art["assign"])
+        index = part
+
+        def dev_fn(nprobe):
+            return lambda qp, nq, d, i, c, s: mb.IVFFlatSearch.search_device(
+                ctx, part, ws, qp, nq, args.k, nprobe, metric, d, i, c, s)
+
+        def host_fn(nprobe):
+            return lambda qp, nq, d, i, c: mb.check(L.mans_ivf_search(
+                ctx.handle, part.handle, C.c_void_p(qp), nq, args.dim, args.k, nprobe, metric,
+                C.c_void_p(d), C.c_void_p(i), C.c_void_p(c)))
+    else:
+        ix = mb.IVFPQIndex(ctx, art["coarse"], art["codebooks"], art["codes"],
+                           (art["offsets"], art["lists"]), metric=mb.Metric(metric))
+        index = ix
+
+        def dev_fn(nprobe):
+            return lambda qp, nq, d, i, c, s: ix.search_device(ws, qp, nq, args.k, nprobe, d, i,
+                                                               c, s)
+
+        def host_fn(nprobe):
+            return lambda qp, nq, d, i, c: mb.check(L.mans_ivfpq_search(
+                ctx.handle, ix.handle, C.c_void_p(qp), nq, args.dim, args.k, nprobe,
+                C.c_void_p(d), C.c_void_p(i), C.c_void_p(c)))
+    build_s = time.perf_counter() - t_build
+
+    def one(nq, nprobe, steps, warmup, with_clocks):
+        saved = args.nprobe
+        args.nprobe = nprobe
+        try:
+            q = q_all[:nq]
+            r = measure_index(torch, ws, dev_fn(nprobe), host_fn(nprobe), q, kout, steps, warmup,
+                              with_clocks)
+            r["nprobe"] = nprobe
+            r["roofline"] = index_roofline(args, r, probed_list_rows(args, art, q))
+            r["workload"] = index_workload_config(args, nq, nprobe)["workload"]
+            return r
+        finally:
+            args.nprobe = saved
+
+    main_res = one(args.nq, args.nprobe, args.steps, args.warmup, True)
+    also = [one(nq2, p2, max(20, min(args.steps, int(20000 / nq2))), 5, False)
+            for nq2, p2 in extra]
+    if world > 1:
+        t = torch.tensor([main_res["total_ms"]], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        main_res["total_ms"] = float(t.item())
+    if rank == 0:
+        res = main_res
+        line = {
+            "metric": "queries_per_sec",
+            "value": world * args.nq * args.steps / (res["total_ms"] * 1e-3),
+            "unit": "queries/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": res["total_ms"] / args.steps, "p50_us": 1e3 * res["p50_ms"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32" if args.workload == "ivf" else "f32 (u8 codes)",
+            "data": f"synthetic (numpy default_rng(0) {args.components}-component Gaussian "
+                    f"mixture, sigma 0.3, L2-normalised); index trained with torch "
+                    f"(build {build_s:.0f} s, outside the timed region)",
+            "config": index_workload_config(args),
+            "roofline": res["roofline"],
+            "e2e": {"value": args.nq * args.steps / (res["e2e_ms"] * 1e-3), "unit": "queries/s",
+                    "p50_us": 1e6 * res["e2e_p50_s"],
+                    "h2d_bytes_per_step": args.nq * args.dim * 4,
+                    "d2h_bytes_per_step": args.nq * kout * 8 + args.nq * 4},
+            "gpu_launches": int(res["launches"]),
+            "clocks": res["clocks"],
+            "e2e_matches_device_path": res["ok"],
+            "also": [{"workload": r["workload"], "nq": r["nq"], "nprobe": r["nprobe"],
+                      "steps": r["steps"],
+                      "value": r["nq"] * r["steps"] / (r["total_ms"] * 1e-3),
+                      "unit": "queries/s", "ms_per_step": r["total_ms"] / r["steps"],
+                      "p50_us": 1e3 * r["p50_ms"],
+                      "e2e_value": r["nq"] * r["steps"] / (r["e2e_ms"] * 1e-3),
+                      "e2e_p50_us": 1e6 * r["e2e_p50_s"], "gpu_launches": int(r["launches"]),
+                      "roofline": r["roofline"], "e2e_matches_device_path": r["ok"]}
+                     for r in also],
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            qps, done = cpu_index_qps(args, v, q_all[:max(1, args.nq)], art, args.cpu_seconds)
+            line["cpu_baseline"] = {
+                "value": qps, "unit": "queries/s", "cores": 1, "kind": "port",
+                "sample": f"{done} single-query searches (~{args.cpu_seconds:.0f} s), "
+                          f"nprobe {args.nprobe}; "
+                          + ("IVFFlatSearch.scanProbedLists restated" if args.workload == "ivf"
+                             else "_IVFPQIndex.search restated (coarse BoundedSortedList, "
+                                  "sequential ADC, newest-first merge)")}
+        print(json.dumps(line), flush=True)
+    ws.close()
+    index.close()
+    ctx.close()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -469,6 +816,13 @@ def main():
 
     import meltan_b200 as mb
     from meltan_b200._lib import lib
+
+    if args.workload != "flat":
+        run_index(args, torch, mb, lib(), world, rank, dist)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     metric = METRIC_NAMES[args.metric]
     also_nq = [x for x in (32, 1024) if x != args.nq] if not args.no_also else []

@@ -155,6 +155,7 @@ void destroy_workspace(mans_workspace* ws) {
   ws->out_counts.release();
   ws->aux.release();
   ws->aux2.release();
+  ws->tc_aux.release();
   ws->h_err.release();
   for (auto& pr : ws->events) {
     cudaEventDestroy(pr.first);
@@ -167,7 +168,7 @@ void destroy_workspace(mans_workspace* ws) {
 // Records a start event before the dominant kernel when timing is enabled;
 // returns the matching stop event (or null).
 cudaEvent_t timing_begin(mans_workspace* ws, cudaStream_t stream) {
-  if (!ws->timing) return nullptr;
+  if (!ws->timing || ws->timing_hold > 0) return nullptr;
   if (ws->events_used == ws->events.size()) {
     cudaEvent_t a, b;
     if (cudaEventCreate(&a) != cudaSuccess) return nullptr;

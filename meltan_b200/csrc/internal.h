@@ -91,9 +91,13 @@ struct mans_workspace {
   mans::DeviceBuffer out_counts;
   mans::DeviceBuffer aux;
   mans::DeviceBuffer aux2;
+  // scratch of the tensor-core batch path alone: it runs nested inside other
+  // searches (the IVF centroid scan) whose own scratch lives in `aux`
+  mans::DeviceBuffer tc_aux;
   mans::PinnedBuffer h_err;
   // optional CUDA-event timing of the dominant kernel (scan) launches
   bool timing = false;
+  int timing_hold = 0;  // > 0 while an inner step (e.g. a centroid scan) runs untimed
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> events;
   size_t events_used = 0;
   int64_t launches = 0;  // library kernels enqueued through this workspace
@@ -108,6 +112,12 @@ int32_t check_device_error(mans_workspace* ws, cudaStream_t stream);
 int pow2_at_least(int v);
 int choose_qb(int64_t nq);
 cudaEvent_t timing_begin(mans_workspace* ws, cudaStream_t stream);
+// Keeps the inner steps of a search out of the dominant-kernel timing.
+struct TimingHold {
+  mans_workspace* ws;
+  explicit TimingHold(mans_workspace* w) : ws(w) { ++ws->timing_hold; }
+  ~TimingHold() { --ws->timing_hold; }
+};
 void timing_end(cudaEvent_t stop, cudaStream_t stream);
 // Uploads rows (host, n x dim) into a new corpus object (norms on the device).
 int32_t corpus_upload(mans_ctx* ctx, const float* rows, int64_t n, int64_t dim, uint32_t id_offset,

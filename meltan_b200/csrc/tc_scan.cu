@@ -1124,14 +1124,14 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   const size_t o_dn = carve(o, nq * dld * sizeof(float));
   const size_t o_cc = carve(o, nq * sizeof(int32_t) + sizeof(int32_t));
   const size_t o_cd = carve(o, nq * static_cast<size_t>(cap) * sizeof(uint64_t));
-  if ((rc = ws->aux.reserve(o)) != MANS_OK) return rc;
+  if ((rc = ws->tc_aux.reserve(o)) != MANS_OK) return rc;
   if ((rc = ws->err.reserve(sizeof(int))) != MANS_OK) return rc;
   if (!ws->err_cleared) {
     cudaError_t e = cudaMemsetAsync(ws->err.ptr, 0, sizeof(int), stream);
     if (e != cudaSuccess) return fail_cuda(e, "cudaMemsetAsync(err)");
     ws->err_cleared = true;
   }
-  uint8_t* A = static_cast<uint8_t*>(ws->aux.ptr);
+  uint8_t* A = static_cast<uint8_t*>(ws->tc_aux.ptr);
   auto F = [&](size_t off) { return reinterpret_cast<float*>(A + off); };
   __nv_bfloat16* qbf = reinterpret_cast<__nv_bfloat16*>(A + o_qbf);
   int32_t* ccount = reinterpret_cast<int32_t*>(A + o_cc);

@@ -50,6 +50,17 @@ def test_tc_parity_small(tctx, mg, mo, n, d):
         same(run(tctx, v, q, k, mg), O.flat_search(v, q, k, mo))
 
 
+@pytest.mark.parametrize("n", [1, 7, 64, 255, 257])
+def test_tc_tiny_corpora(tctx, n):
+    """Corpora shorter than one 256-row tile (an IVF centroid table is one)."""
+    rng = np.random.default_rng(n)
+    v = unit_rows(rng, n, 64)
+    q = unit_rows(rng, 20, 64)
+    for mg, mo in MET:
+        for k in (1, 10):
+            same(run(tctx, v, q, k, mg), O.flat_search(v, q, k, mo))
+
+
 def test_tc_unnormalised_rows_and_k256(tctx):
     rng = np.random.default_rng(7)
     v = rng.standard_normal((30000, 128), dtype=np.float32) * rng.uniform(0.5, 3, (30000, 1)).astype(np.float32)
