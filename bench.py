@@ -260,14 +260,15 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def committed_traffic(workload):
-    """Per-launch DRAM bytes of the scan kernel from the committed ncu summary."""
+def committed_traffic(workload, kernel="scan"):
+    """Per-launch DRAM bytes (read + write) of the dominant kernel from the
+    committed ncu summaries, keyed "<workload>/<kernel>"."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
     if not os.path.exists(path):
         return None
     with open(path) as f:
         d = json.load(f)
-    return d.get(workload)
+    return d.get(f"{workload}/{kernel}")
 
 
 def cpu_reference_qps(v, q, k, metric, seconds, max_queries=None):
@@ -432,6 +433,7 @@ class Runner:
         ws.check(sp)
         kern_ms, kern_launches, total_launches = ws.stats()
         ws.set_timing(False)
+        path = ws.last_path()
         total_ms = t0.elapsed_time(t1)
         step_ms = [x.elapsed_time(y) for x, y in ev]
         device_out = out.clone()
@@ -478,34 +480,53 @@ class Runner:
         return {"nq": nq, "steps": steps, "total_ms": total_ms, "e2e_ms": e2e_ms,
                 "kern_avg_ms": kern_avg_ms, "kern_launches": kern_launches,
                 "launches": total_launches, "p50_ms": p50(steps_t.tolist()),
-                "e2e_p50_s": p50(e2e_t.tolist()), "clocks": clock_info, "ok": ok, "kout": kout}
+                "e2e_p50_s": p50(e2e_t.tolist()), "clocks": clock_info, "ok": ok, "kout": kout,
+                "path": path}
 
 
 def roofline(args, res, shard_rows, metric, tc_min_batch, workload):
+    """Roofline of the dominant kernel of the path that ran (reported by the
+    workspace): the exact scan is HBM bound on the fp32 rows; the tensor-core
+    pass is bound by the slower of its operand stream (the bf16 / int8 copy,
+    plus |r|^2 for L2) and its MMA work, whichever takes longer at peak."""
     nq = res["nq"]
     kern_s = res["kern_avg_ms"] * 1e-3
-    if tc_min_batch and nq >= tc_min_batch:
+    hbm_peak, hbm_kind = measured_peaks()
+    label = {0: "scan", 1: "tc_bf16", 2: "tc_int8"}[res.get("path", 0)]
+    traffic = committed_traffic(workload, label)
+    if traffic is not None:
+        traffic = traffic * shard_rows / args.n  # committed capture is of the unsharded launch
+    if res.get("path", 0) in (1, 2):
+        esize = 2 if res["path"] == 1 else 1
+        ld = -(-args.dim // 64) * 64 if esize == 2 else -(-args.dim // 128) * 128
+        bytes_ = shard_rows * ld * esize + (shard_rows * 4 if metric == 1 else 0)
         flops = 2.0 * shard_rows * args.dim * nq
-        peak, kind = measured_bf16_peak()
-        achieved = flops / kern_s / 1e12
-        return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "traffic": committed_traffic(workload),
-                "kernel": "tc_scan_kernel (filtered full pass)",
-                "kernel_avg_us": res["kern_avg_ms"] * 1e3,
-                "algorithmic_flops_per_launch": flops,
-                "peak_source": f"{kind} bf16_tflops (dense, burst)"}
+        tc_peak, tc_kind = measured_bf16_peak()
+        if res["path"] == 2:
+            tc_peak, tc_kind = 2 * tc_peak, tc_kind + " x2 (int8 MMA rate)"
+        kname = "tc_scan_kernel (filtered full pass, %s)" % ("bf16" if esize == 2 else "int8")
+        if flops / (tc_peak * 1e12) >= bytes_ / (hbm_peak * 1e9):
+            achieved = flops / kern_s / 1e12
+            return {"bound": "tensor", "achieved": achieved, "peak": tc_peak, "unit": "TFLOP/s",
+                    "frac": achieved / tc_peak, "traffic": traffic, "kernel": kname,
+                    "kernel_avg_us": res["kern_avg_ms"] * 1e3,
+                    "algorithmic_flops_per_launch": flops,
+                    "peak_source": f"{tc_kind} bf16_tflops (dense, burst)"}
+        achieved = bytes_ / kern_s / 1e9
+        return {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                "frac": achieved / hbm_peak, "traffic": traffic, "kernel": kname,
+                "kernel_avg_us": res["kern_avg_ms"] * 1e3, "algorithmic_bytes_per_launch": bytes_,
+                "note": "bytes of the low-precision row copy the pass streams; the exact "
+                        "re-score reads the fp32 rows of the certified candidates only",
+                "peak_source": f"{hbm_kind} hbm_gbs"}
     groups = math.ceil(nq / 8) if nq > 8 else 1
     row_bytes = args.dim * 4 + (4 if metric in (0, 1) else 0)
     alg = shard_rows * row_bytes * groups + nq * args.dim * 4
-    peak, kind = measured_peaks()
     achieved = alg / kern_s / 1e9
-    traffic = committed_traffic(workload)
-    if traffic is not None:
-        traffic = traffic * shard_rows / args.n  # committed capture is of the unsharded launch
-    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-            "frac": achieved / peak, "traffic": traffic, "kernel": "scan_topk_kernel",
+    return {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+            "frac": achieved / hbm_peak, "traffic": traffic, "kernel": "scan_topk_kernel",
             "kernel_avg_us": res["kern_avg_ms"] * 1e3, "algorithmic_bytes_per_launch": alg,
-            "peak_source": f"{kind} hbm_gbs"}
+            "peak_source": f"{hbm_kind} hbm_gbs"}
 
 
 # ---------------------------------------------------------------------------
@@ -681,7 +702,8 @@ def index_roofline(args, res, list_rows):
     achieved = alg / kern_s / 1e9 if kern_s > 0 else 0.0
     wl = index_workload_config(args, res["nq"])["workload"]
     return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-            "frac": achieved / peak, "traffic": committed_traffic(wl),
+            "frac": achieved / peak,
+            "traffic": committed_traffic(wl, "list_scan" if args.workload == "ivf" else "adc"),
             "kernel": "scan_topk_kernel (probed lists)" if args.workload == "ivf"
             else "pq_adc_kernel", "kernel_avg_us": 1e3 * res["kern_avg_ms"],
             "algorithmic_bytes_per_launch": alg,

@@ -90,6 +90,23 @@ int32_t mans_ctx_sm_count(const mans_ctx *ctx);
  * No reference counterpart (the reference has one GPU tier,
  * FlatGPUSearch.swift:652-707). */
 int32_t mans_ctx_set_tensor_core_batch(mans_ctx *ctx, int32_t min_batch);
+/* (Batches smaller than min_batch also take that path when the corpus holds at
+ * least 2^28 elements, where reading half the bytes outweighs its fixed cost.) */
+
+/* Operand format of that path.  MANS_TC_BF16: bf16 rows; MANS_TC_INT8:
+ * signed 8-bit codes quantised as the reference's int8 prefilter does
+ * (Int8CodeBuffer.fill, Int8CodeCache.swift:64-99; query quantised as
+ * BoundedExactScan.swift:52-64), half the bytes per row and a looser bound;
+ * MANS_TC_AUTO (default): bf16 (on L2-normalised 384-d rows the int8 bound is
+ * about 6x wider and its larger candidate sets cost more than the halved row
+ * bytes save).  Results are identical to the exact scan in every format.  The
+ * GPU counterpart of BoundedExactScan.search (BoundedExactScan.swift:30-122):
+ * a bounded low-precision pass, then an exact fp32 re-score of the provable
+ * candidates. */
+#define MANS_TC_AUTO 0
+#define MANS_TC_BF16 1
+#define MANS_TC_INT8 2
+int32_t mans_ctx_set_tensor_core_format(mans_ctx *ctx, int32_t format);
 
 /* ---- corpus (VectorBuffer) --------------------------------------------- */
 
@@ -112,6 +129,12 @@ int32_t mans_corpus_destroy(mans_corpus *corpus);
 int64_t mans_corpus_count(const mans_corpus *corpus);
 int64_t mans_corpus_dim(const mans_corpus *corpus);
 
+/* Host copy of the corpus's signed 8-bit codes (n x dim, row-major) and
+ * per-row scales u, as Int8CodeBuffer.fill computes them
+ * (Int8CodeCache.swift:64-99); either output may be null.  Builds the int8
+ * copy on the device when it does not exist yet. */
+int32_t mans_corpus_int8_codes(mans_corpus *corpus, int8_t *codes, float *scales);
+
 /* ---- workspaces (device-pointer calls) ---------------------------------- */
 
 /* A workspace owns the scratch of one in-flight device-pointer search.  It
@@ -124,6 +147,10 @@ int32_t mans_workspace_check(mans_workspace *ws, void *cuda_stream);
 /* Number of queries of the last tensor-core search made with `ws` whose
  * certificate failed and that were re-scanned exactly (synchronises). */
 int32_t mans_workspace_fallbacks(mans_workspace *ws, int32_t *out);
+/* Path of the last flat search made with `ws`: 0 the exact CUDA-core scan,
+ * 1 the bf16 tensor-core pass, 2 the int8 tensor-core pass (no reference
+ * counterpart; for measurement). */
+int32_t mans_workspace_last_path(mans_workspace *ws, int32_t *out);
 
 /* Measurement hooks (no reference counterpart; the reference's benchmark CLI
  * times whole calls, Sources/MetalANNSBenchmarks/HotPathProfiler.swift:22-304).

@@ -19,6 +19,9 @@ from .core import (  # noqa: F401
     Metric,
     SearchFailed,
     SearchResult,
+    TC_AUTO,
+    TC_BF16,
+    TC_INT8,
     VectorBuffer,
     Workspace,
     check,

@@ -28,6 +28,7 @@ from ._lib import last_error, lib
 
 MAX_TOP_K = 256
 EMPTY_ID = 0xFFFFFFFF
+TC_AUTO, TC_BF16, TC_INT8 = 0, 1, 2  # MANS_TC_* operand formats
 
 
 class Metric(enum.IntEnum):
@@ -132,6 +133,10 @@ class Context:
         """Batches of >= min_batch queries use the tensor-core path (0: never)."""
         check(lib().mans_ctx_set_tensor_core_batch(self._h, min_batch))
 
+    def set_tensor_core_format(self, fmt: int) -> None:
+        """Operand format of the tensor-core path: TC_AUTO, TC_BF16 or TC_INT8."""
+        check(lib().mans_ctx_set_tensor_core_format(self._h, fmt))
+
     def close(self):
         if self._h:
             lib().mans_ctx_destroy(self._h)
@@ -180,6 +185,16 @@ class VectorBuffer:
             raise DimensionMismatch(f"expected {self.dim}, got {v.shape[1]}")
         check(lib().mans_corpus_update_rows(self._h, starting_at, _ptr(v), v.shape[0]))
 
+    def int8_codes(self):
+        """(codes [n, dim] int8, scales [n]) of the int8 prefilter copy, as
+        Int8CodeBuffer.fill quantises the rows (Int8CodeCache.swift:64-99)."""
+        n, d = self.count, self.dim
+        codes = np.empty((n, d), np.int8)
+        scales = np.empty(n, np.float32)
+        check(lib().mans_corpus_int8_codes(self._h, C.c_void_p(codes.ctypes.data),
+                                           C.c_void_p(scales.ctypes.data)))
+        return codes, scales
+
     def close(self):
         if self._h:
             lib().mans_corpus_destroy(self._h)
@@ -211,6 +226,12 @@ class Workspace:
     def fallbacks(self) -> int:
         out = C.c_int32()
         check(lib().mans_workspace_fallbacks(self._h, C.byref(out)))
+        return out.value
+
+    def last_path(self) -> int:
+        """Path of the last flat search: 0 scan, 1 bf16 tensor core, 2 int8."""
+        out = C.c_int32()
+        check(lib().mans_workspace_last_path(self._h, C.byref(out)))
         return out.value
 
     def set_timing(self, enable: bool) -> None:

@@ -208,16 +208,22 @@ int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace
   const int32_t kout = std::min<int32_t>(k, kcap);
   const int64_t n = corpus->n;
   if (nq <= 0) return MANS_OK;
-  if (mode == kModeHost && kcap == MANS_MAX_TOPK && ctx->tc_min_batch > 0 &&
-      nq >= ctx->tc_min_batch && k > 0 && n > 0 && !corpus->ids) {
+  // Tensor-core path: batches of at least tc_min_batch queries, and any batch
+  // over a corpus of at least 2^28 elements, where halving the bytes read
+  // outweighs the fixed cost of the sample, threshold and re-rank steps.
+  const bool tc_size = nq >= ctx->tc_min_batch || n * corpus->dim >= (int64_t{1} << 28);
+  ws->last_path = 0;
+  if (mode == kModeHost && kcap == MANS_MAX_TOPK && ctx->tc_min_batch > 0 && tc_size && k > 0 &&
+      n > 0 && !corpus->ids) {
     mans_corpus* c = const_cast<mans_corpus*>(corpus);
+    const bool i8 = tc_use_int8(ctx, nq);
     std::unique_lock<std::mutex> lk(c->tc_mu);
-    int32_t rc = tc_prepare_corpus(c, metric);
+    int32_t rc = tc_prepare_corpus(c, metric, i8);
     lk.unlock();
     if (rc != MANS_OK) return rc;
-    if (tc_applicable(c, metric))
+    if (tc_applicable(c, metric, i8))
       return run_flat_search_tc(ctx, c, ws, d_queries, nq, k, metric, d_out_dist, d_out_ids,
-                                d_out_counts, stream);
+                                d_out_counts, stream, i8);
   }
   if (k <= 0 || n <= 0) {
     if (kout <= 0) {
@@ -427,6 +433,26 @@ int32_t mans_ctx_set_tensor_core_batch(mans_ctx* ctx, int32_t min_batch) {
   if (!ctx) return fail(MANS_ERR_INVALID, "null context");
   if (min_batch < 0) return fail(MANS_ERR_INVALID, "negative batch size");
   ctx->tc_min_batch = min_batch;
+  return MANS_OK;
+}
+
+int32_t mans_ctx_set_tensor_core_format(mans_ctx* ctx, int32_t format) {
+  if (!ctx) return fail(MANS_ERR_INVALID, "null context");
+  if (format < MANS_TC_AUTO || format > MANS_TC_INT8)
+    return fail(MANS_ERR_INVALID, "unknown tensor-core operand format");
+  ctx->tc_format = format;
+  return MANS_OK;
+}
+
+int32_t mans_corpus_int8_codes(mans_corpus* corpus, int8_t* codes, float* scales) {
+  if (!corpus || (!codes && !scales)) return fail(MANS_ERR_INVALID, "null corpus or outputs");
+  std::lock_guard<std::mutex> lk(corpus->tc_mu);
+  return tc_export_int8(corpus, codes, scales);
+}
+
+int32_t mans_workspace_last_path(mans_workspace* ws, int32_t* out) {
+  if (!ws || !out) return fail(MANS_ERR_INVALID, "null workspace or output");
+  *out = ws->last_path;
   return MANS_OK;
 }
 

@@ -49,6 +49,8 @@ struct mans_ctx {
   std::vector<mans_workspace*> pool;  // idle workspaces for host-pointer calls
   // query batches of at least this size use the tensor-core path (0: never)
   int tc_min_batch = 16;
+  // operand format of that path: MANS_TC_AUTO / MANS_TC_BF16 / MANS_TC_INT8
+  int tc_format = 0;
 };
 
 // Row-major fp32 rows with a 16-byte pitch (ld = dim rounded up to 4), the
@@ -74,6 +76,16 @@ struct mans_corpus {
   float* tc_stats = nullptr;  // n x 4: |r'|, |r' - bf16(r')|, |bf16(r')|, |r| rounded down
   mans::TcCorpusStats tc_stats_host{};
   CUtensorMap tc_map;
+  // signed 8-bit codes (Int8CodeBuffer quantisation), built on first use
+  bool tc8_ready = false;
+  void* tc8_rows = nullptr;  // n x tc8_ld int8
+  int64_t tc8_ld = 0;
+  float* tc8_u = nullptr;     // per-row scale u
+  float* tc8_wcos = nullptr;  // u / |r| (cosine factor)
+  float* tc8_stats = nullptr; // n x 4: |r|, |r - u code|, |u code|, |r| rounded down
+  mans::TcCorpusStats tc8_plain{};  // L2 / IP bound terms
+  mans::TcCorpusStats tc8_cos{};    // cosine: terms relative to |r|
+  CUtensorMap tc8_map;
 };
 
 struct mans_workspace {
@@ -101,6 +113,7 @@ struct mans_workspace {
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> events;
   size_t events_used = 0;
   int64_t launches = 0;  // library kernels enqueued through this workspace
+  int last_path = 0;     // path of the last flat search: 0 scan, 1 bf16 tensor, 2 int8 tensor
   int32_t* tc_fallbacks = nullptr;  // device counter of exact re-scans (last tc call)
 };
 
@@ -124,12 +137,16 @@ int32_t corpus_upload(mans_ctx* ctx, const float* rows, int64_t n, int64_t dim, 
                       mans_corpus** out);
 void corpus_free(mans_corpus* c);
 // tensor-core batch path (tc_scan.cu)
-int32_t tc_prepare_corpus(mans_corpus* c, int metric);
-bool tc_applicable(const mans_corpus* c, int metric);
+// i8: the int8 operand format (else bf16); tc_use_int8 picks it for a batch.
+bool tc_use_int8(const mans_ctx* ctx, int64_t nq);
+int32_t tc_prepare_corpus(mans_corpus* c, int metric, bool i8);
+bool tc_applicable(const mans_corpus* c, int metric, bool i8);
 int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* ws,
                            const float* d_queries, int64_t nq, int32_t k, int32_t metric,
                            float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
-                           cudaStream_t stream);
+                           cudaStream_t stream, bool i8);
+// host copy of the int8 codes and scales (prepared on demand)
+int32_t tc_export_int8(mans_corpus* c, int8_t* codes, float* scales);
 void tc_free_corpus(mans_corpus* c);
 // Exact scan + top-k over `corpus`.  mode: kModeHost (host-tier distance) or
 // kModeSimd (SIMDDistance semantics).  kcap bounds k (256 for the public

@@ -18,6 +18,7 @@ struct TcParams {
   int32_t groups;           // > 0: row groups walked in step by the query blocks
   int32_t stream_queries;   // 1: stream the query block with every stage instead of keeping it
   const float* row_beta;    // per-row additive term (L2: |r|^2), may be null
+  const float* row_w;       // int8 pass: per-row factor of the integer dot
   const float* q_alpha;     // per-query additive term
   const float* q_gamma;     // per-query factor of the dot
   const float* q_c;         // filter constant in the score domain (filter mode)

@@ -76,9 +76,14 @@ struct TcLayout {
   size_t total;
 };
 
-__host__ __device__ inline TcLayout tc_layout(int dim, int stream_queries) {
+// k-blocks of 128 bytes per row: 64 bf16 or 128 int8 elements
+__host__ __device__ inline int tc_kblocks(int dim, bool i8) {
+  return i8 ? (dim + 127) / 128 : (dim + kBK - 1) / kBK;
+}
+
+__host__ __device__ inline TcLayout tc_layout(int nk, int stream_queries) {
   TcLayout L;
-  L.nk = (dim + kBK - 1) / kBK;
+  L.nk = nk;
   L.resident = !stream_queries && static_cast<size_t>(L.nk) * kQBytes <= kResidentMax;
   L.a_bytes = L.resident ? static_cast<size_t>(L.nk) * kQBytes : 0;
   L.stage_bytes = kRBytes + (L.resident ? 0 : kQBytes);
@@ -121,6 +126,16 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_
           d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
 }
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::i8 (s8 in, s32 accumulate)
+__device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+}
 // arrive on `bar` once every MMA previously issued by this thread completed
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile(
@@ -159,6 +174,13 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
          (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// Instruction descriptor, kind::i8: D s32 (bits 4-5 = 2), A and B signed
+// 8-bit (bits 7-9 = 1, 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at 24.
+__host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* err,
                                         volatile int* abort) {
   if (*abort) return false;
@@ -178,12 +200,14 @@ __device__ __forceinline__ float approx_distance(float alpha, float gamma, float
 // (cosine on normalised rows, IP) and the filter with a per-row bias (L2).
 enum TcMode : int { kDense = 0, kFilterPlain = 1, kFilterBias = 2 };
 
-template <int MODE>
+// I8: signed 8-bit codes with a per-row factor (TcParams::row_w) instead of
+// bf16 rows; the s32 accumulator is converted and scaled in the epilogue.
+template <int MODE, bool I8>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_scan_kernel(const __grid_constant__ CUtensorMap map_q,
                    const __grid_constant__ CUtensorMap map_r, const TcParams p) {
   extern __shared__ uint8_t smem_raw[];
-  const TcLayout L = tc_layout(p.dim, p.stream_queries);
+  const TcLayout L = tc_layout(tc_kblocks(p.dim, I8), p.stream_queries);
   uint8_t* base =
       reinterpret_cast<uint8_t*>((reinterpret_cast<size_t>(smem_raw) + 1023) / 1024 * 1024);
   uint8_t* qres = base;                  // resident query block (nk x 16 KiB)
@@ -203,6 +227,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int nk = L.nk;
+  constexpr int kKElems = I8 ? 128 : kBK;  // elements per 128-byte k-block (TMA x step)
   const int64_t rtiles = (p.rows + kRN - 1) / kRN;
   const int64_t units = rtiles * p.qblocks;
   // Work split.  With `groups` > 0 block c owns query block c % qblocks and
@@ -267,7 +292,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (cur_qb >= 0 && !tc_wait(a_empty, (a_round - 1) & 1u, p.err, abort)) break;
           mbar_arrive_expect_tx(a_full, static_cast<uint32_t>(nk * kQBytes));
           for (int kb = 0; kb < nk; ++kb)
-            tma_load_2d(qres + kb * kQBytes, &map_q, kb * kBK, static_cast<int32_t>(qb * kQM), a_full);
+            tma_load_2d(qres + kb * kQBytes, &map_q, kb * kKElems, static_cast<int32_t>(qb * kQM), a_full);
           a_pending = true;
           cur_qb = qb;
           ++a_round;
@@ -281,9 +306,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
           uint8_t* st = stages + stage * L.stage_bytes;
           mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(L.stage_bytes));
-          tma_load_2d(st, &map_r, kb * kBK, y, &full[stage]);
+          tma_load_2d(st, &map_r, kb * kKElems, y, &full[stage]);
           if (!L.resident)
-            tma_load_2d(st + kRBytes, &map_q, kb * kBK, static_cast<int32_t>(qb * kQM), &full[stage]);
+            tma_load_2d(st + kRBytes, &map_q, kb * kKElems, static_cast<int32_t>(qb * kQM), &full[stage]);
           ++issued;
           if (++stage == L.stages) {
             stage = 0;
@@ -302,7 +327,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      const uint32_t idesc = idesc_bf16(kQM, kRN);
+      const uint32_t idesc = I8 ? idesc_i8(kQM, kRN) : idesc_bf16(kQM, kRN);
       int stage = 0;
       uint32_t phase = 0;
       int64_t cur_qb = -1;
@@ -332,9 +357,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const uint32_t sq = L.resident ? smem_u32(qres + kb * kQBytes) : sr + kRBytes;
           const uint64_t adesc = smem_desc_sw128(sq);
           const uint64_t bdesc = smem_desc_sw128(sr);
+          // four MMAs of 32 bytes of K per 128-byte stage (16 bf16 / 32 int8)
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            tc_mma(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+          for (int kk = 0; kk < 4; ++kk) {
+            if (I8)
+              tc_mma_i8(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+            else
+              tc_mma(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+          }
           tc_commit(&empty[stage]);  // frees the smem stage once these MMAs finish
           if (++stage == L.stages) {
             stage = 0;
@@ -359,10 +389,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int quarter = warp & 3;
     const int part = ew >> 2;          // columns part*64 .. +63
     const int et = tid - 128;          // 0..511
-    constexpr bool kRowTerms = MODE == kFilterBias || MODE == kDense;
+    constexpr bool kRowTerms = I8 || MODE == kFilterBias || MODE == kDense;
     int local = 0;
     int64_t cur_qb = -1;
-    float alpha = 0.0f, gamma = 0.0f, cq = __int_as_float(0x7F800000);
+    float alpha = 0.0f, gamma = 0.0f, hq = 0.0f, cq = __int_as_float(0x7F800000);
     int64_t q = 0;
     bool qvalid = false;
     for (int64_t u = u_begin; u < u_end; ++u, ++local) {
@@ -374,17 +404,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         qvalid = q < p.nq;
         alpha = qvalid ? p.q_alpha[q] : 0.0f;
         gamma = qvalid ? p.q_gamma[q] : 0.0f;
+        hq = gamma > 0.0f ? 1.0f / gamma : 0.0f;
         cq = (qvalid && MODE != kDense) ? p.q_c[q] : __int_as_float(0x7F800000);
       }
       const int b = local & 1;
       const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
       float* rp = rowpar + b * 2 * kRN;
-      if (kRowTerms && p.row_beta) {
+      if (kRowTerms && (I8 || p.row_beta)) {
         if (et < kRN) {
           const int64_t lrow = rt * kRN + et;
           const bool in = lrow < p.rows;
-          const float beta = in ? p.row_beta[p.row0 + lrow] : 0.0f;
-          rp[et] = in ? 0.5f * beta : __int_as_float(0x7F800000);
+          const float beta = (in && p.row_beta) ? p.row_beta[p.row0 + lrow] : 0.0f;
+          if (I8)
+            rp[et] = in ? p.row_w[p.row0 + lrow] : 0.0f;  // factor of the integer dot
+          else
+            rp[et] = in ? 0.5f * beta : __int_as_float(0x7F800000);
           rp[kRN + et] = beta;
         }
         named_sync(1, kEpiWarps * 32);
@@ -402,6 +436,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         float v[32];
         tmem_ld32(taddr + c * 32, v);
         const int j0 = part * 64 + c * 32;
+        if (I8) {
+#pragma unroll
+          for (int t = 0; t < 32; ++t) v[t] = __int2float_rn(__float_as_int(v[t])) * rp[j0 + t];
+        }
         const int64_t lr = lrow0 + c * 32;
         if (MODE == kDense) {
           if (qvalid) {
@@ -410,8 +448,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               float o[4];
 #pragma unroll
               for (int i = 0; i < 4; ++i)
-                o[i] = approx_distance(alpha, gamma, p.row_beta ? rp[kRN + j0 + t + i] : 0.0f,
-                                       v[t + i]);
+                o[i] = approx_distance(alpha, gamma,
+                                       (I8 || p.row_beta) ? rp[kRN + j0 + t + i] : 0.0f, v[t + i]);
               if (lr + t + 3 < p.rows) {
                 *reinterpret_cast<float4*>(p.dense_out + q * p.dense_ld + lr + t) =
                     make_float4(o[0], o[1], o[2], o[3]);
@@ -424,7 +462,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         } else {
           float x[32];
 #pragma unroll
-          for (int t = 0; t < 32; ++t) x[t] = MODE == kFilterBias ? v[t] - rp[j0 + t] : v[t];
+          for (int t = 0; t < 32; ++t)
+            x[t] = MODE != kFilterBias ? v[t]
+                   : I8                ? fmaf(-rp[kRN + j0 + t], hq, v[t])
+                                       : v[t] - rp[j0 + t];
           // only rows of the pass: the tail of the last tile reads zero rows
           const int64_t rem = p.rows - lr;
           const int tmax = rem >= 32 ? 32 : (rem < 0 ? 0 : static_cast<int>(rem));
@@ -500,6 +541,59 @@ __global__ void to_bf16_rows_kernel(const float* __restrict__ rows, int64_t n, i
   }
 }
 
+// Signed 8-bit codes of each row as Int8CodeBuffer.fill quantises them
+// (Sources/MetalANNSCore/Int8CodeCache.swift:64-99): scale u = maxAbs / 127
+// (1 for a zero row), inverse 1 / u, code = trunc(v * inverse +- 0.5) (half
+// away from zero) clamped to +-127, all in fp32.  One warp per row.  Also the
+// per-row factor of the integer dot (u, and u / |r| for cosine) and the bound
+// terms (double, rounded up): |r|, |r - u code|, |u code|, and |r| rounded
+// down.
+__global__ void to_i8_rows_kernel(const float* __restrict__ rows, int64_t n, int32_t dim,
+                                  int64_t ld, int8_t* __restrict__ out, int64_t ld8,
+                                  float* __restrict__ u_out, float* __restrict__ wcos_out,
+                                  float* __restrict__ stats) {
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= n) return;
+  const float* v = rows + r * ld;
+  float mx = 0.0f;
+  for (int c = lane; c < dim; c += 32) mx = fmaxf(mx, fabsf(v[c]));
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+  const float scale = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
+  const float inverse = __fdiv_rn(1.0f, scale);
+  double n0 = 0.0, nres = 0.0, nt = 0.0;
+  for (int c = lane; c < ld8; c += 32) {
+    int code = 0;
+    double xx = 0.0;
+    if (c < dim) {
+      const float x = v[c];
+      const float scaled = __fmul_rn(x, inverse);
+      code = __float2int_rz(scaled >= 0.0f ? __fadd_rn(scaled, 0.5f) : __fsub_rn(scaled, 0.5f));
+      code = code > 127 ? 127 : (code < -127 ? -127 : code);
+      xx = x;
+    }
+    out[r * ld8 + c] = static_cast<int8_t>(code);
+    const double xb = static_cast<double>(scale) * code;
+    n0 += xx * xx;
+    nres += (xx - xb) * (xx - xb);
+    nt += xb * xb;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    n0 += __shfl_xor_sync(0xFFFFFFFFu, n0, o);
+    nres += __shfl_xor_sync(0xFFFFFFFFu, nres, o);
+    nt += __shfl_xor_sync(0xFFFFFFFFu, nt, o);
+  }
+  if (lane == 0) {
+    const double norm = sqrt(n0);
+    u_out[r] = scale;
+    wcos_out[r] = norm > 0.0 ? static_cast<float>(static_cast<double>(scale) / norm) : 0.0f;
+    stats[r * 4 + 0] = __double2float_ru(norm * (1.0 + 1e-9));
+    stats[r * 4 + 1] = __double2float_ru(sqrt(nres) * (1.0 + 1e-9));
+    stats[r * 4 + 2] = __double2float_ru(sqrt(nt) * (1.0 + 1e-9));
+    stats[r * 4 + 3] = __double2float_rd(norm * (1.0 - 1e-9));
+  }
+}
+
 struct TcQueryParams {
   const float* queries;  // nq x dim fp32
   int64_t nq;
@@ -507,7 +601,8 @@ struct TcQueryParams {
   int64_t ld16;
   int metric;
   TcCorpusStats cs;
-  __nv_bfloat16* qbf;  // nq_pad x ld16
+  __nv_bfloat16* qbf;  // nq_pad x ld16 (bf16 pass)
+  int8_t* q8;          // nq_pad x ld16 (int8 pass; ld16 is then the int8 pitch)
   float* qn_exact;     // nq, sequential |q|^2
   float* alpha;
   float* gamma;
@@ -517,14 +612,22 @@ struct TcQueryParams {
   int32_t* ccount;     // candidate counters (nq + 1, the last one counts fallbacks), zeroed
 };
 
-// One warp per query: bf16 copy, exact squared norm in index order, the
-// affine terms and the certified bound eps_q of |d~ - d|.
+// One warp per query: the bf16 copy (or the int8 codes with their scale
+// s_q, quantised in double as BoundedExactScan.swift:52-64 does), the exact
+// squared norm in index order, the affine terms and the certified bound eps_q
+// of |d~ - d|.
+template <bool I8>
 __global__ void tc_query_prep_kernel(const TcQueryParams p) {
   const int64_t q = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (q >= p.nq_pad) return;
   if (q >= p.nq) {  // padding row of the last query block
-    for (int c = lane; c < p.ld16; c += 32) p.qbf[q * p.ld16 + c] = __float2bfloat16_rn(0.0f);
+    for (int c = lane; c < p.ld16; c += 32) {
+      if (I8)
+        p.q8[q * p.ld16 + c] = 0;
+      else
+        p.qbf[q * p.ld16 + c] = __float2bfloat16_rn(0.0f);
+    }
     return;
   }
   if (lane == 0) {
@@ -532,14 +635,31 @@ __global__ void tc_query_prep_kernel(const TcQueryParams p) {
     if (q == 0) p.ccount[p.nq] = 0;
   }
   const float* v = p.queries + q * p.dim;
+  double qs = 1.0;  // query scale (int8)
+  if (I8) {
+    float mx = 0.0f;
+    for (int c = lane; c < p.dim; c += 32) mx = fmaxf(mx, fabsf(v[c]));
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    qs = mx > 0.0f ? static_cast<double>(mx) / 127.0 : 1.0;
+  }
   double nq2 = 0.0, nres = 0.0, nt = 0.0;
   for (int c0 = 0; c0 < p.ld16; c0 += 32) {
     const int c = c0 + lane;
     const float x = c < p.dim ? v[c] : 0.0f;
     if (c < p.ld16) {
-      const __nv_bfloat16 b = __float2bfloat16_rn(x);
-      p.qbf[q * p.ld16 + c] = b;
-      const double xb = __bfloat162float(b), xx = x;
+      double xb;
+      if (I8) {
+        const double sc = static_cast<double>(x) / qs;
+        int code = static_cast<int>(sc >= 0.0 ? sc + 0.5 : sc - 0.5);
+        code = code > 127 ? 127 : (code < -127 ? -127 : code);
+        p.q8[q * p.ld16 + c] = static_cast<int8_t>(code);
+        xb = qs * code;
+      } else {
+        const __nv_bfloat16 b = __float2bfloat16_rn(x);
+        p.qbf[q * p.ld16 + c] = b;
+        xb = __bfloat162float(b);
+      }
+      const double xx = x;
       nq2 += xx * xx;
       nres += (xx - xb) * (xx - xb);
       nt += xb * xb;
@@ -560,8 +680,10 @@ __global__ void tc_query_prep_kernel(const TcQueryParams p) {
     acc = __fadd_rn(acc, __fmul_rn(y, y));
   }
   const double qnorm = sqrt(nq2), qres = sqrt(nres), qt = sqrt(nt);
-  // fp32 accumulation in the tensor core and in the exact sequential path:
-  // generously dim * 2^-22 of the magnitude sum each
+  // |dot(q, r) - dot(q', r')| <= |q - q'||r| + |q'||r - r'| plus the fp32
+  // accumulation of the tensor core (bf16) and of the exact sequential path:
+  // generously dim * 2^-22 of the magnitude sum each.  (For cosine the row
+  // terms are relative to |r|.)
   const double cacc = static_cast<double>(p.dim) * 2.384185791015625e-07;
   const double es = qres * p.cs.max_norm + qt * p.cs.max_resid +
                     cacc * qt * p.cs.max_norm_bf16 + cacc * qnorm * p.cs.max_norm;
@@ -573,7 +695,8 @@ __global__ void tc_query_prep_kernel(const TcQueryParams p) {
     lip = 2.0;
     mag = acc + p.cs.max_sqnorm + 2.0 * (qnorm * p.cs.max_norm + es);
   } else if (p.metric == kCosine) {
-    // rows are normalised in double before rounding, so s~ ~ dot(q, r)/|r|
+    // the tensor-core dot approximates dot(q, r)/|r| (bf16: rows normalised
+    // before rounding; int8: the row factor is u/|r|)
     alpha = 1.0;
     gamma = qnorm > 0.0 ? 1.0 / qnorm : 0.0;
     lip = gamma;
@@ -584,14 +707,17 @@ __global__ void tc_query_prep_kernel(const TcQueryParams p) {
   } else {
     mag = qnorm * p.cs.max_norm + es;
   }
-  // rounding of both distance formulas: 64 ulps of the largest magnitude
+  // rounding of both distance formulas (and, for int8, of the row factor and
+  // the product with the converted integer dot): 64 ulps of the largest magnitude
   const double slack = mag * 64.0 * 5.960464477539063e-08 + extra + 1e-30;
   p.qn_exact[q] = acc;
   p.alpha[q] = static_cast<float>(alpha);
-  p.gamma[q] = static_cast<float>(gamma);
+  // the integer dot counts in units of the query scale
+  p.gamma[q] = static_cast<float>(gamma * qs);
   p.eps[q] = static_cast<float>((lip * es + slack) * (1.0 + 1e-6));
-  double sc = qt * p.cs.max_norm_bf16;
-  if (p.metric == kL2) sc += 0.5 * p.cs.max_sqnorm;
+  // magnitude bound of the score-domain value x = v - beta / gamma
+  double sc = qt / qs * p.cs.max_norm_bf16;
+  if (p.metric == kL2) sc += p.cs.max_sqnorm / (gamma * qs);
   p.scale[q] = static_cast<float>(sc);
 }
 
@@ -600,6 +726,7 @@ struct KthSmem {
   uint32_t hist[2048];
   float list[1024];
   float red[64];
+  uint32_t wsum[32];
   float lo[4], scale[4];
   int sel[4];
   uint32_t sh[4];
@@ -664,21 +791,38 @@ __device__ float block_kth_smallest(Get get, int64_t n, int k, KthSmem& S) {
       if (member(v, level)) atomicAdd(&S.hist[kth_bin(v, lo, scale)], 1u);
     }
     __syncthreads();
-    if (tid == 0) {
-      uint32_t cum = 0;
-      int b = 0;
-      for (; b < 2047; ++b) {
-        if (cum + S.hist[b] >= kk) break;
-        cum += S.hist[b];
+    {
+      // bin of the kk-th value: each thread sums a run of bins, a block-wide
+      // exclusive scan of the runs locates the crossing, whose owner scans it
+      const int per = 2048 / static_cast<int>(blockDim.x);
+      uint32_t run = 0;
+      for (int j = 0; j < per; ++j) run += S.hist[tid * per + j];
+      uint32_t inc = run;
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+        if ((tid & 31) >= o) inc += y;
       }
-      S.lo[level] = lo;
-      S.scale[level] = scale;
-      S.sel[level] = b;
-      S.sh[1] = kk - cum;
-      S.sh[2] = S.hist[b];
-      S.sh[3] = 0;
+      if ((tid & 31) == 31) S.wsum[tid >> 5] = inc;
+      __syncthreads();
+      uint32_t before = 0;
+      for (int w = 0; w < (tid >> 5); ++w) before += S.wsum[w];
+      const uint32_t excl = before + inc - run;
+      if (excl < kk && excl + run >= kk) {
+        uint32_t cum = excl;
+        int b = tid * per;
+        for (int j = 0; j < per - 1; ++j, ++b) {
+          if (cum + S.hist[b] >= kk) break;
+          cum += S.hist[b];
+        }
+        S.lo[level] = lo;
+        S.scale[level] = scale;
+        S.sel[level] = b;
+        S.sh[1] = kk - cum;
+        S.sh[2] = S.hist[b];
+        S.sh[3] = 0;
+      }
+      __syncthreads();
     }
-    __syncthreads();
     kk = S.sh[1];
     const uint32_t cnt = S.sh[2];
     // four levels without isolating 1024 values (only for value sets of
@@ -757,24 +901,22 @@ __global__ void __launch_bounds__(kThresholdThreads) tc_threshold_kernel(
   }
   if (threadIdx.x == 0) {
     thr_out[q] = t;
-    // Score-domain constant: the filter keeps x >= c, where
-    //   cosine (normalised rows): d~ <= t  <=>  v >= (1 - t)/gamma   (gamma > 0)
-    //   L2: d~ <= t  <=>  v - beta/2 >= (alpha - t)/2
-    //   IP: d~ <= t  <=>  v >= -t
-    // lowered by a margin far above the rounding of either side, so the kept
-    // set contains every row with d~ <= t (a few extra rows are harmless).
-    // "keep everything" is -FLT_MAX, not -inf: padding rows carry x = -inf.
+    // Score-domain constant: with d~ = alpha + beta - gamma v the filter keeps
+    // x = v - beta/gamma >= c = (alpha - t)/gamma  (beta = 0 for cosine / IP;
+    // alpha = 1 for cosine, 0 for IP), lowered by a margin far above the
+    // rounding of either side, so the kept set contains every row with
+    // d~ <= t (a few extra rows are harmless).  "Keep everything" is
+    // -FLT_MAX, not -inf: padding rows carry x = -inf.
+    (void)metric;
     const float keep_all = -3.40282347e+38f;
     float c;
+    const float g = gamma[q];
     if (t == inf) {
       c = keep_all;
-    } else if (metric == kCosine) {
-      const float g = gamma[q];
-      c = g > 0.0f ? (1.0f - t) / g : (1.0f <= t ? keep_all : inf);
-    } else if (metric == kL2) {
-      c = (alpha[q] - t) * 0.5f;
+    } else if (g > 0.0f) {
+      c = (alpha[q] - t) / g;
     } else {
-      c = -t;
+      c = alpha[q] <= t ? keep_all : inf;
     }
     if (c != inf && c != keep_all) c = fmaxf(c - (fabsf(c) + scale[q]) * 6.103515625e-05f, keep_all);
     c_out[q] = c;
@@ -989,8 +1131,10 @@ __global__ void __launch_bounds__(kRerankThreads) tc_rerank_kernel(const RerankP
 }
 
 
-int32_t encode_bf16_map(CUtensorMap* map, const void* base, int64_t rows, int64_t dim,
-                        int64_t ld16, int box_rows) {
+// 2-D tensor map of a row-major matrix with a 128-byte inner box (64 bf16 or
+// 128 int8 elements) and 128-byte swizzle; `ld` in elements.
+int32_t encode_tc_map(CUtensorMap* map, const void* base, int64_t rows, int64_t dim, int64_t ld,
+                      int box_rows, bool i8) {
   auto enc_ptr = [] {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -1007,15 +1151,16 @@ int32_t encode_bf16_map(CUtensorMap* map, const void* base, int64_t rows, int64_
                            CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
                            CUtensorMapFloatOOBfill);
   cuuint64_t gdim[2] = {static_cast<cuuint64_t>(dim), static_cast<cuuint64_t>(std::max<int64_t>(rows, 1))};
-  cuuint64_t gstride[1] = {static_cast<cuuint64_t>(ld16) * 2};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  cuuint64_t gstride[1] = {static_cast<cuuint64_t>(ld) * (i8 ? 1 : 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(i8 ? 128 : kBK), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estride[2] = {1, 1};
-  CUresult r = reinterpret_cast<Enc>(fn)(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+  CUresult r = reinterpret_cast<Enc>(fn)(map, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                                 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                                          const_cast<void*>(base), gdim, gstride, box, estride,
                                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(MANS_ERR_PIPELINE, "bf16 tensor map encoding failed");
+  if (r != CUDA_SUCCESS) return fail(MANS_ERR_PIPELINE, "tensor-core map encoding failed");
   return MANS_OK;
 }
 
@@ -1023,7 +1168,7 @@ int32_t encode_bf16_map(CUtensorMap* map, const void* base, int64_t rows, int64_
 
 // Builds (once per corpus and row scaling) the bf16 copy and the bound terms:
 // cosine rounds the normalised rows, L2 and IP the rows as stored.
-int32_t tc_prepare_corpus(mans_corpus* c, int metric) {
+static int32_t tc_prepare_bf16(mans_corpus* c, int metric) {
   const int norm_mode = metric == kCosine ? 1 : 0;
   if (c->tc_ready && c->tc_metric == norm_mode) return MANS_OK;
   DeviceGuard g(c->ctx->device);
@@ -1035,7 +1180,7 @@ int32_t tc_prepare_corpus(mans_corpus* c, int metric) {
     if (e == cudaSuccess) e = cudaMalloc(&c->tc_stats, std::max<int64_t>(n, 1) * 4 * sizeof(float));
     if (e != cudaSuccess) return fail_cuda(e, "cudaMalloc(bf16 corpus)");
     c->tc_ld16 = ld16;
-    int32_t rc = encode_bf16_map(&c->tc_map, c->tc_rows, n, c->dim, ld16, kRN);
+    int32_t rc = encode_tc_map(&c->tc_map, c->tc_rows, n, c->dim, ld16, kRN, false);
     if (rc != MANS_OK) return rc;
   }
   if (n > 0) {
@@ -1081,38 +1226,129 @@ static size_t carve(size_t& o, size_t bytes) {
 
 // Whether the tensor-core path applies to this corpus and metric: cosine
 // needs every row norm bounded away from zero so the bound stays finite.
-bool tc_applicable(const mans_corpus* c, int metric) {
+// The int8 codes and scales (metric independent) and both sets of bound terms.
+static int32_t tc_prepare_int8(mans_corpus* c) {
+  if (c->tc8_ready) return MANS_OK;
+  DeviceGuard g(c->ctx->device);
+  const int64_t n = c->n;
+  const int64_t ld8 = (c->dim + 127) / 128 * 128;
+  cudaError_t e = cudaSuccess;
+  if (!c->tc8_rows) {
+    const int64_t nn = std::max<int64_t>(n, 1);
+    e = cudaMalloc(&c->tc8_rows, nn * ld8);
+    if (e == cudaSuccess) e = cudaMalloc(&c->tc8_u, nn * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&c->tc8_wcos, nn * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&c->tc8_stats, nn * 4 * sizeof(float));
+    if (e != cudaSuccess) return fail_cuda(e, "cudaMalloc(int8 corpus)");
+    c->tc8_ld = ld8;
+    int32_t rc = encode_tc_map(&c->tc8_map, c->tc8_rows, n, c->dim, ld8, kRN, true);
+    if (rc != MANS_OK) return rc;
+  }
+  if (n > 0) {
+    to_i8_rows_kernel<<<static_cast<unsigned>((n + 7) / 8), 256>>>(
+        c->rows, n, static_cast<int32_t>(c->dim), c->ld, static_cast<int8_t*>(c->tc8_rows), ld8,
+        c->tc8_u, c->tc8_wcos, c->tc8_stats);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return fail_cuda(e, "int8 corpus conversion");
+  }
+  std::vector<float> st(static_cast<size_t>(std::max<int64_t>(n, 1)) * 4);
+  if (n > 0) {
+    e = cudaMemcpy(st.data(), c->tc8_stats, n * 4 * sizeof(float), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return fail_cuda(e, "int8 corpus stats");
+  }
+  TcCorpusStats pl{}, co{};
+  pl.min_norm = co.min_norm = n > 0 ? INFINITY : 0.0f;
+  co.max_norm = static_cast<float>(1.0 + 1e-6);
+  bool finite = true;
+  for (int64_t r = 0; r < n; ++r) {
+    const float* x = &st[r * 4];
+    for (int j = 0; j < 4; ++j) finite = finite && std::isfinite(x[j]);
+    pl.max_norm = std::max(pl.max_norm, x[0]);
+    pl.max_resid = std::max(pl.max_resid, x[1]);
+    pl.max_norm_bf16 = std::max(pl.max_norm_bf16, x[2]);
+    pl.min_norm = std::min(pl.min_norm, x[3]);
+    const double up = static_cast<double>(x[0]);
+    pl.max_sqnorm = std::max(pl.max_sqnorm, static_cast<float>(up * up * (1.0 + 1e-5)));
+    if (x[3] > 0.0f) {  // relative terms; a zero row keeps cosine off this path
+      co.max_resid = std::max(co.max_resid, static_cast<float>(x[1] / static_cast<double>(x[3]) * (1.0 + 1e-6)));
+      co.max_norm_bf16 = std::max(co.max_norm_bf16, static_cast<float>(x[2] / static_cast<double>(x[3]) * (1.0 + 1e-6)));
+    }
+    co.min_norm = std::min(co.min_norm, x[3]);
+  }
+  if (!finite) pl.max_norm = co.max_norm = INFINITY;
+  c->tc8_plain = pl;
+  c->tc8_cos = co;
+  c->tc8_ready = true;
+  return MANS_OK;
+}
+
+int32_t tc_prepare_corpus(mans_corpus* c, int metric, bool i8) {
+  return i8 ? tc_prepare_int8(c) : tc_prepare_bf16(c, metric);
+}
+
+static const TcCorpusStats& tc_stats_for(const mans_corpus* c, int metric, bool i8) {
+  if (!i8) return c->tc_stats_host;
+  return metric == kCosine ? c->tc8_cos : c->tc8_plain;
+}
+
+// AUTO is bf16: on L2-normalised data the int8 bound is about 6x wider
+// (|q - q'| |r| + |q'| |r - r'| with per-row scales maxAbs/127), which grows
+// the candidate and re-score sets more than the halved row bytes save.
+bool tc_use_int8(const mans_ctx* ctx, int64_t nq) {
+  (void)nq;
+  return ctx->tc_format == MANS_TC_INT8;
+}
+
+bool tc_applicable(const mans_corpus* c, int metric, bool i8) {
   if (c->n <= 0 || c->n >= (1ll << 31)) return false;
-  if (metric == kCosine && c->tc_ready && c->tc_stats_host.min_norm < 1e-6f) return false;
+  if (!(i8 ? c->tc8_ready : c->tc_ready)) return true;
+  const TcCorpusStats& cs = tc_stats_for(c, metric, i8);
+  if (metric == kCosine && cs.min_norm < 1e-6f) return false;
   // a NaN or infinite row makes the bound meaningless: exact scan
-  if (c->tc_ready && !(std::isfinite(c->tc_stats_host.max_norm) &&
-                       std::isfinite(c->tc_stats_host.max_sqnorm)))
-    return false;
+  if (!(std::isfinite(cs.max_norm) && std::isfinite(cs.max_sqnorm))) return false;
   return true;
+}
+
+int32_t tc_export_int8(mans_corpus* c, int8_t* codes, float* scales) {
+  int32_t rc = tc_prepare_int8(c);
+  if (rc != MANS_OK) return rc;
+  DeviceGuard g(c->ctx->device);
+  cudaError_t e = cudaSuccess;
+  if (codes && c->n > 0)
+    e = cudaMemcpy2D(codes, c->dim, c->tc8_rows, c->tc8_ld, c->dim, c->n, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && scales && c->n > 0)
+    e = cudaMemcpy(scales, c->tc8_u, c->n * sizeof(float), cudaMemcpyDeviceToHost);
+  return e == cudaSuccess ? MANS_OK : fail_cuda(e, "int8 code download");
 }
 
 int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* ws,
                            const float* d_queries, int64_t nq, int32_t k, int32_t metric,
                            float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
-                           cudaStream_t stream) {
-  int32_t rc = tc_prepare_corpus(corpus, metric);
+                           cudaStream_t stream, bool i8) {
+  int32_t rc = tc_prepare_corpus(corpus, metric, i8);
   if (rc != MANS_OK) return rc;
-  if (!tc_applicable(corpus, metric))
+  if (!tc_applicable(corpus, metric, i8))
     return run_flat_search(ctx, corpus, ws, d_queries, nq, k, metric, d_out_dist, d_out_ids,
                            d_out_counts, stream, kModeHost, MANS_MAX_TOPK);
   const int64_t n = corpus->n;
   const int32_t kout = std::min<int32_t>(k, MANS_MAX_TOPK);
   const int32_t keff = static_cast<int32_t>(std::min<int64_t>(kout, n));
   const int32_t kp = pow2_at_least(keff);
-  const int64_t ld16 = corpus->tc_ld16;
+  // row pitch of the operand copy, in elements (128-byte multiple)
+  const int64_t ld16 = i8 ? corpus->tc8_ld : corpus->tc_ld16;
+  const size_t esize = i8 ? 1 : sizeof(__nv_bfloat16);
   const int64_t qblocks = (nq + kQM - 1) / kQM;
   const int64_t nq_pad = qblocks * kQM;
-  int64_t sample = std::min<int64_t>(n, std::max<int64_t>(16384, std::min<int64_t>(131072, 256ll * keff)));
+  // The int8 bound is about 4x wider than the bf16 one; a larger sample keeps
+  // its filter threshold (sample k-th + 2 eps) and candidate lists small.
+  const int64_t smin = i8 ? 65536 : 16384;
+  int64_t sample = std::min<int64_t>(n, std::max<int64_t>(smin, std::min<int64_t>(131072, 256ll * keff)));
   sample = std::min<int64_t>(n, (sample + kRN - 1) / kRN * kRN);
-  const int32_t cap = 8192;
+  const int32_t cap = i8 ? 32768 : 8192;
 
   size_t o = 0;
-  const size_t o_qbf = carve(o, nq_pad * ld16 * sizeof(__nv_bfloat16));
+  const size_t o_qbf = carve(o, nq_pad * ld16 * esize);
   const size_t o_qn = carve(o, nq * sizeof(float));
   const size_t o_al = carve(o, nq * sizeof(float));
   const size_t o_ga = carve(o, nq * sizeof(float));
@@ -1145,8 +1381,9 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   qp.dim = static_cast<int32_t>(corpus->dim);
   qp.ld16 = ld16;
   qp.metric = metric;
-  qp.cs = corpus->tc_stats_host;
+  qp.cs = tc_stats_for(corpus, metric, i8);
   qp.qbf = qbf;
+  qp.q8 = reinterpret_cast<int8_t*>(qbf);
   qp.qn_exact = F(o_qn);
   qp.alpha = F(o_al);
   qp.gamma = F(o_ga);
@@ -1154,27 +1391,36 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   qp.scale = F(o_sc);
   qp.nq_pad = nq_pad;
   qp.ccount = ccount;
-  tc_query_prep_kernel<<<static_cast<unsigned>((nq_pad + 7) / 8), 256, 0, stream>>>(qp);
+  if (i8)
+    tc_query_prep_kernel<true><<<static_cast<unsigned>((nq_pad + 7) / 8), 256, 0, stream>>>(qp);
+  else
+    tc_query_prep_kernel<false><<<static_cast<unsigned>((nq_pad + 7) / 8), 256, 0, stream>>>(qp);
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc query prep launch");
 
   CUtensorMap map_q;
-  if ((rc = encode_bf16_map(&map_q, qbf, nq_pad, corpus->dim, ld16, kQM)) != MANS_OK) return rc;
+  if ((rc = encode_tc_map(&map_q, qbf, nq_pad, corpus->dim, ld16, kQM, i8)) != MANS_OK) return rc;
+  const CUtensorMap& map_r = i8 ? corpus->tc8_map : corpus->tc_map;
   static const int stream_q = [] {
     const char* e = getenv("MANS_TC_STREAM_QUERIES");
     return e && e[0] == '1' ? 1 : 0;
   }();
-  const TcLayout lay = tc_layout(static_cast<int>(corpus->dim), stream_q);
+  const TcLayout lay = tc_layout(tc_kblocks(static_cast<int>(corpus->dim), i8), stream_q);
   const size_t smem = lay.total;
   if (lay.stages < 2) return fail(MANS_ERR_SEARCH, "dimension too large for the tensor-core pass");
   // the attribute is per device; set it on every call (cheap, no allocation)
-  e = cudaFuncSetAttribute(tc_scan_kernel<kDense>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(smem));
+  const void* kd = i8 ? reinterpret_cast<const void*>(tc_scan_kernel<kDense, true>)
+                     : reinterpret_cast<const void*>(tc_scan_kernel<kDense, false>);
+  const void* kp_ = i8 ? reinterpret_cast<const void*>(tc_scan_kernel<kFilterPlain, true>)
+                       : reinterpret_cast<const void*>(tc_scan_kernel<kFilterPlain, false>);
+  const void* kb_ = i8 ? reinterpret_cast<const void*>(tc_scan_kernel<kFilterBias, true>)
+                       : reinterpret_cast<const void*>(tc_scan_kernel<kFilterBias, false>);
+  e = cudaFuncSetAttribute(kd, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(tc_scan_kernel<kFilterPlain>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    e = cudaFuncSetAttribute(kp_, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(tc_scan_kernel<kFilterBias>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    e = cudaFuncSetAttribute(kb_, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(tc_threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kThresholdStageMax);
@@ -1191,6 +1437,7 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   tp.dim = static_cast<int32_t>(corpus->dim);
   tp.qblocks = static_cast<int32_t>(qblocks);
   tp.row_beta = metric == kL2 ? corpus->norms : nullptr;  // the exact path's fp32 |r|^2
+  tp.row_w = i8 ? (metric == kCosine ? corpus->tc8_wcos : corpus->tc8_u) : nullptr;
   tp.q_alpha = F(o_al);
   tp.q_gamma = F(o_ga);
   tp.q_c = F(o_cq);
@@ -1208,7 +1455,10 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
     tp.groups = static_cast<int32_t>(std::min<int64_t>(tp.groups, (sample + kRN - 1) / kRN));
     grid_s = static_cast<int>(tp.groups * qblocks);
   }
-  tc_scan_kernel<kDense><<<grid_s, kTcThreads, smem, stream>>>(map_q, corpus->tc_map, tp);
+  if (i8)
+    tc_scan_kernel<kDense, true><<<grid_s, kTcThreads, smem, stream>>>(map_q, map_r, tp);
+  else
+    tc_scan_kernel<kDense, false><<<grid_s, kTcThreads, smem, stream>>>(map_q, map_r, tp);
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc sample launch");
   // 3. thresholds
   // one wave of queries: wide blocks over a staged row (latency); larger
@@ -1236,10 +1486,14 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
     grid = static_cast<int>(tp.groups * qblocks);
   }
   cudaEvent_t stop = timing_begin(ws, stream);
-  if (metric == kL2)
-    tc_scan_kernel<kFilterBias><<<grid, kTcThreads, smem, stream>>>(map_q, corpus->tc_map, tp);
+  if (metric == kL2 && i8)
+    tc_scan_kernel<kFilterBias, true><<<grid, kTcThreads, smem, stream>>>(map_q, map_r, tp);
+  else if (metric == kL2)
+    tc_scan_kernel<kFilterBias, false><<<grid, kTcThreads, smem, stream>>>(map_q, map_r, tp);
+  else if (i8)
+    tc_scan_kernel<kFilterPlain, true><<<grid, kTcThreads, smem, stream>>>(map_q, map_r, tp);
   else
-    tc_scan_kernel<kFilterPlain><<<grid, kTcThreads, smem, stream>>>(map_q, corpus->tc_map, tp);
+    tc_scan_kernel<kFilterPlain, false><<<grid, kTcThreads, smem, stream>>>(map_q, map_r, tp);
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc scan launch");
   timing_end(stop, stream);
   // 5. certify + exact re-rank
@@ -1271,6 +1525,7 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc rerank launch");
   ws->tc_fallbacks = fallbacks;
   ws->launches += 5;
+  ws->last_path = i8 ? 2 : 1;
   return MANS_OK;
 }
 
@@ -1280,6 +1535,15 @@ void tc_free_corpus(mans_corpus* c) {
   c->tc_rows = nullptr;
   c->tc_stats = nullptr;
   c->tc_ready = false;
+  if (c->tc8_rows) cudaFree(c->tc8_rows);
+  if (c->tc8_u) cudaFree(c->tc8_u);
+  if (c->tc8_wcos) cudaFree(c->tc8_wcos);
+  if (c->tc8_stats) cudaFree(c->tc8_stats);
+  c->tc8_rows = nullptr;
+  c->tc8_u = nullptr;
+  c->tc8_wcos = nullptr;
+  c->tc8_stats = nullptr;
+  c->tc8_ready = false;
 }
 
 }  // namespace mans

@@ -38,6 +38,7 @@ def lib():
         L = C.CDLL(path)
         L.orc_lcg_vectors.argtypes = [C.c_uint64, C.c_int64, C.c_int64, _F]
         L.orc_lcg32_vectors.argtypes = [C.c_uint64, C.c_int64, C.c_int64, _F]
+        L.orc_int8_fill.argtypes = [_F, C.c_int64, C.c_int64, C.c_void_p, _F]
         for name in ("orc_dot_rows_seq", "orc_dot_rows_neon"):
             getattr(L, name).argtypes = [_F, _F, C.c_int64, C.c_int64, _F]
         L.orc_norm_sq.argtypes = [_F, C.c_int64]
@@ -114,6 +115,16 @@ def lcg32_vectors(count, dim, seed):
     out = np.empty((count, dim), np.float32)
     lib().orc_lcg32_vectors(seed, count, dim, _p(out, _F))
     return out
+
+
+def int8_fill(rows):
+    """Int8CodeBuffer.fill codes (n x d int8) and per-row scales."""
+    rows = f32(rows)
+    n, d = rows.shape
+    codes = np.empty((n, d), np.int8)
+    scales = np.empty(n, np.float32)
+    lib().orc_int8_fill(_p(rows, _F), n, d, codes.ctypes.data, _p(scales, _F))
+    return codes, scales
 
 
 def dot_rows(corpus, query, order="seq"):

@@ -65,6 +65,36 @@ void orc_lcg32_vectors(uint64_t seed, int64_t count, int64_t dim, float *out) {
 }
 
 /* ------------------------------------------------------------------------ */
+/* Int8 codes (Sources/MetalANNSCore/Int8CodeCache.swift:64-99)              */
+/* ------------------------------------------------------------------------ */
+
+/* Int8CodeBuffer.fill: per row, maxAbs (exact), scale = maxAbs / 127 (1 for a
+ * zero row), inverse = 1 / scale, code = Int32(v * inverse +- 0.5) (the
+ * conversion truncates toward zero, so this rounds half away from zero),
+ * clamped to +-127; every step in fp32. */
+void orc_int8_fill(const float *rows, int64_t n, int64_t dim, int8_t *codes, float *scales) {
+    for (int64_t r = 0; r < n; ++r) {
+        const float *v = rows + r * dim;
+        float max_abs = 0.0f;
+        for (int64_t d = 0; d < dim; ++d) {
+            float a = fabsf(v[d]);
+            if (a > max_abs) max_abs = a;
+        }
+        float scale = max_abs > 0.0f ? max_abs / 127.0f : 1.0f;
+        float inverse = 1.0f / scale;
+        for (int64_t d = 0; d < dim; ++d) {
+            float scaled = v[d] * inverse;
+            float shifted = scaled >= 0.0f ? scaled + 0.5f : scaled - 0.5f;
+            int32_t rounded = (int32_t)shifted;
+            if (rounded > 127) rounded = 127;
+            else if (rounded < -127) rounded = -127;
+            codes[r * dim + d] = (int8_t)rounded;
+        }
+        scales[r] = scale;
+    }
+}
+
+/* ------------------------------------------------------------------------ */
 /* Dot products (Sources/MetalANNSC/dots.c)                                   */
 /* ------------------------------------------------------------------------ */
 

@@ -210,3 +210,32 @@ def test_pq_adc_is_sequential_lut_sum():
         for s in range(16):
             t = np.float32(t + lut[s, codes[r, s]])
         assert out[r] == t
+
+
+def _int8_fill_numpy(rows):
+    """Independent float32 restatement of Int8CodeBuffer.fill
+    (Int8CodeCache.swift:64-99) in numpy."""
+    rows = np.asarray(rows, np.float32)
+    mx = np.abs(rows).max(axis=1)
+    scale = np.where(mx > 0, mx / np.float32(127.0), np.float32(1.0)).astype(np.float32)
+    inv = (np.float32(1.0) / scale).astype(np.float32)
+    scaled = (rows * inv[:, None]).astype(np.float32)
+    shifted = np.where(scaled >= 0, scaled + np.float32(0.5), scaled - np.float32(0.5)).astype(np.float32)
+    codes = np.clip(np.trunc(shifted), -127, 127).astype(np.int8)
+    return codes, scale
+
+
+def test_int8_fill_matches_numpy_restatement():
+    """Codes and scales of the int8 prefilter (BoundedExactScan's Int8CodeBuffer)
+    on the reference test generator's data, zero rows and extreme magnitudes."""
+    v = O.lcg32_vectors(700, 384, 7)
+    v[::50] = 0.0
+    v[1::50] *= np.float32(1e5)
+    v[2::50] *= np.float32(1e-5)
+    v[3, :5] = [0.5, -0.5, 127.0, -127.0, 63.5]  # exact halves after scaling
+    codes, scales = O.int8_fill(v)
+    want_c, want_s = _int8_fill_numpy(v)
+    np.testing.assert_array_equal(scales, want_s)
+    np.testing.assert_array_equal(codes, want_c)
+    assert codes.min() >= -127 and codes.max() <= 127
+    assert (codes[::50] == 0).all() and (scales[::50] == 1.0).all()
