@@ -22,8 +22,9 @@ struct TcParams {
   const float* q_alpha;     // per-query additive term
   const float* q_gamma;     // per-query factor of the dot
   const float* q_c;         // filter constant in the score domain (filter mode)
-  float* dense_out;         // dense mode: dense_out[q * dense_ld + (row - row0)]
+  float* dense_out;         // dense mode: dense_out[q * dense_ld + (row - row0) / dense_group]
   int64_t dense_ld;
+  int32_t dense_group;      // 1: every row's distance; 32: the minimum of each 32-row group
   uint64_t* cand;           // filter mode: (distance, row) keys, cand_cap per query
   int32_t* cand_count;
   int32_t cand_cap;

@@ -441,7 +441,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           for (int t = 0; t < 32; ++t) v[t] = __int2float_rn(__float_as_int(v[t])) * rp[j0 + t];
         }
         const int64_t lr = lrow0 + c * 32;
-        if (MODE == kDense) {
+        if (MODE == kDense && p.dense_group == 32) {
+          // minimum of each 32-row group: the k-th smallest group minimum bounds
+          // the sample's k-th smallest distance from above (k distinct rows lie
+          // at or below it), at 1/32 of the output
+          const int64_t rem = p.rows - lr;
+          const int tmax = rem >= 32 ? 32 : (rem < 0 ? 0 : static_cast<int>(rem));
+          if (qvalid && tmax > 0) {
+            float m = __int_as_float(0x7F800000);
+#pragma unroll
+            for (int t = 0; t < 32; ++t)
+              if (t < tmax)
+                m = fminf(m, approx_distance(alpha, gamma,
+                                             (I8 || p.row_beta) ? rp[kRN + j0 + t] : 0.0f, v[t]));
+            p.dense_out[q * p.dense_ld + (lr >> 5)] = m;
+          }
+        } else if (MODE == kDense) {
           if (qvalid) {
 #pragma unroll
             for (int t = 0; t < 32; t += 4) {
@@ -643,9 +658,11 @@ __global__ void tc_query_prep_kernel(const TcQueryParams p) {
     qs = mx > 0.0f ? static_cast<double>(mx) / 127.0 : 1.0;
   }
   double nq2 = 0.0, nres = 0.0, nt = 0.0;
+  // read-only loads (no aliasing with the stores below), four in flight
+#pragma unroll 4
   for (int c0 = 0; c0 < p.ld16; c0 += 32) {
     const int c = c0 + lane;
-    const float x = c < p.dim ? v[c] : 0.0f;
+    const float x = c < p.dim ? __ldg(v + c) : 0.0f;
     if (c < p.ld16) {
       double xb;
       if (I8) {
@@ -676,7 +693,7 @@ __global__ void tc_query_prep_kernel(const TcQueryParams p) {
   float acc = 0.0f;
 #pragma unroll 8
   for (int c = 0; c < p.dim; ++c) {
-    const float y = v[c];
+    const float y = __ldg(v + c);
     acc = __fadd_rn(acc, __fmul_rn(y, y));
   }
   const double qnorm = sqrt(nq2), qres = sqrt(nres), qt = sqrt(nt);
@@ -867,9 +884,10 @@ __device__ float block_kth_smallest(Get get, int64_t n, int k, KthSmem& S) {
   return 0.0f;  // not reached
 }
 
-// Per query: thr_q = (k-th smallest approximate distance of the dense sample)
-// + 2 eps_q (+inf when the sample has fewer than k rows) and the matching
-// score-domain filter constant.
+// Per query: thr_q = (k-th smallest value of the dense sample: row distances
+// or 32-row group minima, either at or above the sample's k-th smallest
+// distance) + 2 eps_q (+inf when the sample has fewer than k values) and the
+// matching score-domain filter constant.
 constexpr int kThresholdThreads = 1024;
 constexpr int kThresholdStageMax = 160 * 1024;  // bytes of a staged sample row
 
@@ -886,6 +904,7 @@ __global__ void __launch_bounds__(kThresholdThreads) tc_threshold_kernel(
   float t = inf;
   if (staged) {
     // every pass of the selection then reads shared memory
+#pragma unroll 4
     for (int64_t i = threadIdx.x; i < rows / 4; i += blockDim.x)
       reinterpret_cast<float4*>(stage)[i] = __ldg(reinterpret_cast<const float4*>(row) + i);
     for (int64_t i = rows / 4 * 4 + threadIdx.x; i < rows; i += blockDim.x) stage[i] = row[i];
@@ -1029,7 +1048,8 @@ __global__ void __launch_bounds__(kRerankThreads) tc_rerank_kernel(const RerankP
   __shared__ KthSmem ks;
   const int tid = threadIdx.x;
   const int64_t q = blockIdx.x;
-  for (int c = tid; c < p.dim; c += kRerankThreads) qsm[c] = p.queries[q * p.dim + c];
+#pragma unroll 2
+  for (int c = tid; c < p.dim; c += kRerankThreads) qsm[c] = __ldg(p.queries + q * p.dim + c);
   const int total = p.cand_count[q];
   const int cnt = min(total, p.cand_cap);
   const float e = p.eps[q];
@@ -1040,8 +1060,10 @@ __global__ void __launch_bounds__(kRerankThreads) tc_rerank_kernel(const RerankP
   }
   const uint64_t* cq = p.cand + q * p.cand_cap;
   const bool stage_keys = cnt * 8 <= p.region;
-  if (stage_keys)
-    for (int i = tid; i < cnt; i += kRerankThreads) skeys[i] = cq[i];
+  if (stage_keys) {
+#pragma unroll 4
+    for (int i = tid; i < cnt; i += kRerankThreads) skeys[i] = __ldg(cq + i);
+  }
   const uint64_t* keys = stage_keys ? skeys : cq;
   __syncthreads();
   if (!fail_flag) {
@@ -1356,7 +1378,11 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   const size_t o_th = carve(o, nq * sizeof(float));
   const size_t o_sc = carve(o, nq * sizeof(float));
   const size_t o_cq = carve(o, nq * sizeof(float));
-  const int64_t dld = (sample + 3) / 4 * 4;  // float4-aligned pitch of the dense sample
+  // the sample pass writes one value per 32-row group when that leaves at
+  // least 4k groups, otherwise every row
+  const int dgroup = (sample / 32 >= 4ll * keff) ? 32 : 1;
+  const int64_t dvals = (sample + dgroup - 1) / dgroup;
+  const int64_t dld = (dvals + 3) / 4 * 4;  // float4-aligned pitch of the dense sample
   const size_t o_dn = carve(o, nq * dld * sizeof(float));
   const size_t o_cc = carve(o, nq * sizeof(int32_t) + sizeof(int32_t));
   const size_t o_cd = carve(o, nq * static_cast<size_t>(cap) * sizeof(uint64_t));
@@ -1447,6 +1473,7 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   tp.rows = sample;
   tp.dense_out = F(o_dn);
   tp.dense_ld = dld;
+  tp.dense_group = dgroup;
   // lockstep grouping when every query block gets at least one block
   tp.groups = qblocks <= ctx->num_sms ? static_cast<int32_t>(ctx->num_sms / qblocks) : 0;
   const int64_t units_s = (sample + kRN - 1) / kRN * qblocks;
@@ -1469,7 +1496,7 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   const size_t th_smem = staged ? dld * sizeof(float) : 0;
   tc_threshold_kernel<<<static_cast<unsigned>(nq), one_wave ? kThresholdThreads : 256, th_smem,
                         stream>>>(
-      F(o_dn), dld, sample, keff, staged, F(o_ep), F(o_al), F(o_ga), F(o_sc), metric, F(o_th),
+      F(o_dn), dld, dvals, keff, staged, F(o_ep), F(o_al), F(o_ga), F(o_sc), metric, F(o_th),
       F(o_cq));
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc threshold launch");
   // 4. full filtered pass
