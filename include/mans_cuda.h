@@ -230,6 +230,25 @@ int32_t mans_ivf_create(mans_ctx *ctx, const float *centroids, int32_t nlist, in
 int32_t mans_ivf_destroy(mans_ivf *ivf);
 int64_t mans_ivf_list_count(const mans_ivf *ivf);
 
+/* IVFFlatSearch.assignRows (IVFFlatSearch.swift:633-703) on the device: for
+ * every row of `corpus` the list whose centroid (host, nlist x dim) has the
+ * smallest host-tier key, ties to the lower list.  The row's dot with each
+ * centroid uses the reference's sequential fp32 order (the reference calls
+ * cblas_sgemm, whose order is closed).  out_assign: host, n entries. */
+int32_t mans_ivf_assign(mans_ctx *ctx, mans_corpus *corpus, const float *centroids,
+                        int32_t nlist, int32_t metric, int32_t *out_assign);
+/* IVFFlatSearch.buildPartition after its k-means (IVFFlatSearch.swift:
+ * 559-631): assignment as mans_ivf_assign, list sizes, offsets, list ids in
+ * ascending row order per list, packed rows and norms -- all on the device,
+ * from a corpus already uploaded; the result equals mans_ivf_create on the
+ * host-built layout.  Centroid training (KMeans.cluster, seeded by Swift's
+ * generator) stays with the caller. */
+int32_t mans_ivf_build(mans_ctx *ctx, mans_corpus *corpus, const float *centroids,
+                       int32_t nlist, int32_t metric, mans_ivf **out_ivf);
+/* Host copy of the partition layout: offsets (nlist + 1) and list ids (n);
+ * either may be null. */
+int32_t mans_ivf_layout(const mans_ivf *ivf, int64_t *list_offsets, uint32_t *list_ids);
+
 /* IVF-flat probe-and-scan, replacing IVFFlatSearch.search(query:partition:k:
  * nprobe:metric:) / scanProbedLists (IVFFlatSearch.swift:115-133, 214-291)
  * for a batch: nprobe is clamped to [1, nlist]; the nprobe lists with the
@@ -261,6 +280,17 @@ int32_t mans_ivfpq_create(mans_ctx *ctx, const float *coarse, int32_t nlist, int
                           int64_t n, const int64_t *list_offsets, const uint32_t *lists,
                           const uint32_t *list_positions, int32_t metric, mans_ivfpq **out);
 int32_t mans_ivfpq_destroy(mans_ivfpq *ix);
+
+/* IVFPQIndex.add's encoding on the device: per vector the nearest coarse
+ * centroid (nearestCoarseCentroid, IVFPQIndex.swift:514-550: SIMDDistance,
+ * strict '<', first index wins) and the codes of the residual
+ * (ProductQuantizer.encode(vector:subtracting:), ProductQuantizer.swift:
+ * 120-169: sequential fp32 sum of ((v - c) - cb)^2 over the subspace, strict
+ * '<').  vectors: host n x dim; coarse: nlist x dim; codebooks: m x ks x
+ * (dim/m); out_codes: host n x m; out_assign (may be null): host n. */
+int32_t mans_pq_encode(mans_ctx *ctx, const float *vectors, int64_t n, int64_t dim,
+                       const float *coarse, int32_t nlist, const float *codebooks, int32_t m,
+                       int32_t ks, int32_t metric, uint8_t *out_codes, int32_t *out_assign);
 
 /* _IVFPQIndex.search(query:k:nprobe:) (IVFPQIndex.swift:177-226) for a batch:
  * coarse SIMDDistance ranking with newest-first ties, residual LUT

@@ -52,6 +52,9 @@ SIGNATURES = {
                                     C.POINTER(_VP)]),
     "mans_ivf_destroy": (C.c_int32, [_VP]),
     "mans_ivf_list_count": (C.c_int64, [_VP]),
+    "mans_ivf_assign": (C.c_int32, [_VP, _VP, _VP, C.c_int32, C.c_int32, _VP]),
+    "mans_ivf_build": (C.c_int32, [_VP, _VP, _VP, C.c_int32, C.c_int32, _VP]),
+    "mans_ivf_layout": (C.c_int32, [_VP, _VP, _VP]),
     "mans_ivf_search": (C.c_int32, [_VP, _VP, _VP, C.c_int64, C.c_int64, C.c_int32, C.c_int32,
                                     C.c_int32, _VP, _VP, _VP]),
     "mans_ivf_search_device": (C.c_int32, [_VP, _VP, _VP, _VP, C.c_int64, C.c_int32, C.c_int32,
@@ -59,6 +62,8 @@ SIGNATURES = {
     "mans_ivfpq_create": (C.c_int32, [_VP, _VP, C.c_int32, C.c_int64, _VP, C.c_int32, C.c_int32,
                                       _VP, C.c_int64, _VP, _VP, _VP, C.c_int32, C.POINTER(_VP)]),
     "mans_ivfpq_destroy": (C.c_int32, [_VP]),
+    "mans_pq_encode": (C.c_int32, [_VP, _VP, C.c_int64, C.c_int64, _VP, C.c_int32, _VP,
+                                   C.c_int32, C.c_int32, C.c_int32, _VP, _VP]),
     "mans_ivfpq_search": (C.c_int32, [_VP, _VP, _VP, C.c_int64, C.c_int64, C.c_int32, C.c_int32,
                                       _VP, _VP, _VP]),
     "mans_ivfpq_search_device": (C.c_int32, [_VP, _VP, _VP, _VP, C.c_int64, C.c_int32, C.c_int32,

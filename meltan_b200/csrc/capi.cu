@@ -308,7 +308,8 @@ int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace
 }
 
 int32_t corpus_upload(mans_ctx* ctx, const float* rows, int64_t n, int64_t dim, uint32_t id_offset,
-                      mans_corpus** out) {
+                      mans_corpus** out, int64_t src_ld) {
+  if (src_ld <= 0) src_ld = dim;
   if (n < 0 || dim <= 0) return fail(MANS_ERR_INVALID, "corpus needs n >= 0 and dim > 0");
   if (n > 0 && !rows) return fail(MANS_ERR_INVALID, "rows is null");
   if (n > static_cast<int64_t>(INT32_MAX)) return fail(MANS_ERR_INVALID, "corpus too large");
@@ -333,8 +334,9 @@ int32_t corpus_upload(mans_ctx* ctx, const float* rows, int64_t n, int64_t dim, 
   }
   if (n > 0) {
     if (c->ld != dim) cudaMemset(c->rows, 0, rows_bytes);
-    e = cudaMemcpy2D(c->rows, c->ld * sizeof(float), rows, dim * sizeof(float),
-                     dim * sizeof(float), n, cudaMemcpyHostToDevice);
+    // host or device source (unified addressing tells them apart)
+    e = cudaMemcpy2D(c->rows, c->ld * sizeof(float), rows, src_ld * sizeof(float),
+                     dim * sizeof(float), n, cudaMemcpyDefault);
     if (e == cudaSuccess)
       e = launch_row_norms(c->rows, n, static_cast<int32_t>(dim), c->ld, c->norms, 0);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();

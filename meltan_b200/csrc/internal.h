@@ -132,9 +132,10 @@ struct TimingHold {
   ~TimingHold() { --ws->timing_hold; }
 };
 void timing_end(cudaEvent_t stop, cudaStream_t stream);
-// Uploads rows (host, n x dim) into a new corpus object (norms on the device).
+// Copies rows (host or device, n x dim with a row pitch of src_ld elements,
+// 0 = dim) into a new corpus object (norms on the device).
 int32_t corpus_upload(mans_ctx* ctx, const float* rows, int64_t n, int64_t dim, uint32_t id_offset,
-                      mans_corpus** out);
+                      mans_corpus** out, int64_t src_ld = 0);
 void corpus_free(mans_corpus* c);
 // tensor-core batch path (tc_scan.cu)
 // i8: the int8 operand format (else bf16); tc_use_int8 picks it for a batch.

@@ -525,3 +525,254 @@ int32_t mans_ivf_search_device(mans_ctx* ctx, mans_ivf* ivf, mans_workspace* ws,
 int64_t mans_ivf_list_count(const mans_ivf* ivf) { return ivf ? ivf->nlist : 0; }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Partition build on the device (IVFFlatSearch.buildPartition after the
+// k-means, IVFFlatSearch.swift:559-631, and assignRows, :633-703).
+// ---------------------------------------------------------------------------
+
+namespace mans {
+namespace {
+
+__global__ void iota_u32_kernel(uint32_t* __restrict__ out, int64_t n) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = static_cast<uint32_t>(i);
+}
+
+__global__ void list_histogram_kernel(const uint32_t* __restrict__ assign, int64_t n,
+                                      int64_t* __restrict__ counts) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) atomicAdd(reinterpret_cast<unsigned long long*>(counts + assign[i]), 1ull);
+}
+
+// offsets[0] = 0, offsets[l + 1] = offsets[l] + counts[l] (one block; nlist
+// lists scanned in chunks of the block width, carried in shared memory)
+__global__ void list_offsets_kernel(const int64_t* __restrict__ counts, int32_t nlist,
+                                    int64_t* __restrict__ offsets) {
+  __shared__ int64_t part[1024];
+  __shared__ int64_t carry;
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    carry = 0;
+    offsets[0] = 0;
+  }
+  __syncthreads();
+  for (int base = 0; base < nlist; base += blockDim.x) {
+    const int l = base + tid;
+    part[tid] = l < nlist ? counts[l] : 0;
+    __syncthreads();
+    for (int o = 1; o < static_cast<int>(blockDim.x); o <<= 1) {
+      const int64_t y = tid >= o ? part[tid - o] : 0;
+      __syncthreads();
+      part[tid] += y;
+      __syncthreads();
+    }
+    if (l < nlist) offsets[l + 1] = carry + part[tid];
+    __syncthreads();
+    if (tid == blockDim.x - 1) carry += part[tid];
+    __syncthreads();
+  }
+}
+
+// packed[p] = rows[list_ids[p]], one warp per packed row
+__global__ void gather_rows_kernel(const float* __restrict__ rows, int64_t ld,
+                                   const uint32_t* __restrict__ ids, int64_t n, int32_t dim,
+                                   float* __restrict__ packed) {
+  const int64_t p = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (p >= n) return;
+  const float* src = rows + static_cast<int64_t>(ids[p]) * ld;
+  float* dst = packed + p * dim;
+  for (int c = lane; c < dim; c += 32) dst[c] = src[c];
+}
+
+}  // namespace
+
+// assign[r] = the list whose centroid has the smallest key for row r, ties
+// to the lower list: assignRows' key is the host-tier distance of the row
+// (as query) to each centroid, so this is the exact flat search with k = 1
+// over the centroids, run in row chunks.
+static int32_t assign_rows_device(mans_ctx* ctx, const mans_corpus* corpus,
+                                  const mans_corpus* cent, int32_t metric, uint32_t* d_assign) {
+  const int64_t n = corpus->n, dim = corpus->dim;
+  if (n == 0) return MANS_OK;
+  mans_workspace* ws = acquire_workspace(ctx);
+  if (!ws) return fail(MANS_ERR_OOM, "no workspace stream");
+  const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(65536, (256ll << 20) / (dim * 4)));
+  float* d_q = nullptr;
+  float* d_dist = nullptr;
+  int32_t* d_cnt = nullptr;
+  cudaError_t e = cudaMalloc(&d_q, chunk * dim * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&d_dist, chunk * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&d_cnt, chunk * sizeof(int32_t));
+  int32_t rc = e == cudaSuccess ? MANS_OK : fail_cuda(e, "cudaMalloc(assignment)");
+  for (int64_t r0 = 0; rc == MANS_OK && r0 < n; r0 += chunk) {
+    const int64_t m = std::min(chunk, n - r0);
+    e = cudaMemcpy2DAsync(d_q, dim * sizeof(float), corpus->rows + r0 * corpus->ld,
+                          corpus->ld * sizeof(float), dim * sizeof(float), m,
+                          cudaMemcpyDeviceToDevice, ws->stream);
+    if (e != cudaSuccess) {
+      rc = fail_cuda(e, "assignment rows");
+      break;
+    }
+    rc = run_flat_search(ctx, cent, ws, d_q, m, 1, metric, d_dist, d_assign + r0, d_cnt,
+                         ws->stream);
+  }
+  if (rc == MANS_OK) {
+    e = cudaStreamSynchronize(ws->stream);
+    if (e != cudaSuccess) rc = fail_cuda(e, "assignment");
+  }
+  if (rc == MANS_OK) rc = check_device_error(ws, ws->stream);
+  cudaFree(d_q);
+  cudaFree(d_dist);
+  cudaFree(d_cnt);
+  release_workspace(ctx, ws);
+  return rc;
+}
+
+}  // namespace mans
+
+#include <cub/cub.cuh>
+
+extern "C" {
+
+int32_t mans_ivf_assign(mans_ctx* ctx, mans_corpus* corpus, const float* centroids,
+                        int32_t nlist, int32_t metric, int32_t* out_assign) {
+  if (!ctx || !corpus || !centroids || !out_assign)
+    return fail(MANS_ERR_INVALID, "null context, corpus or buffer");
+  if (nlist <= 0) return fail(MANS_ERR_INVALID, "nlist must be positive");
+  if (metric < 0 || metric > 2) return fail(MANS_ERR_SEARCH, "IVF assignment needs cosine, l2 or ip");
+  DeviceGuard g(ctx->device);
+  mans_corpus* cent = nullptr;
+  int32_t rc = corpus_upload(ctx, centroids, nlist, corpus->dim, 0, &cent);
+  if (rc != MANS_OK) return rc;
+  uint32_t* d_assign = nullptr;
+  cudaError_t e = cudaMalloc(&d_assign, std::max<int64_t>(corpus->n, 1) * sizeof(uint32_t));
+  if (e != cudaSuccess) rc = fail_cuda(e, "cudaMalloc(assignment)");
+  if (rc == MANS_OK) rc = assign_rows_device(ctx, corpus, cent, metric, d_assign);
+  if (rc == MANS_OK && corpus->n > 0) {
+    e = cudaMemcpy(out_assign, d_assign, corpus->n * sizeof(uint32_t), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) rc = fail_cuda(e, "assignment download");
+  }
+  cudaFree(d_assign);
+  corpus_free(cent);
+  return rc;
+}
+
+int32_t mans_ivf_build(mans_ctx* ctx, mans_corpus* corpus, const float* centroids,
+                       int32_t nlist, int32_t metric, mans_ivf** out_ivf) {
+  if (!ctx || !corpus || !centroids || !out_ivf)
+    return fail(MANS_ERR_INVALID, "null context, corpus or output");
+  *out_ivf = nullptr;
+  if (nlist <= 0) return fail(MANS_ERR_INVALID, "nlist must be positive");
+  if (metric < 0 || metric > 2) return fail(MANS_ERR_SEARCH, "IVF build needs cosine, l2 or ip");
+  DeviceGuard g(ctx->device);
+  const int64_t n = corpus->n, dim = corpus->dim;
+  mans_ivf* ivf = new mans_ivf();
+  ivf->ctx = ctx;
+  ivf->nlist = nlist;
+  ivf->n = n;
+  ivf->dim = dim;
+  int32_t rc = corpus_upload(ctx, centroids, nlist, dim, 0, &ivf->cent);
+  uint32_t *d_assign = nullptr, *d_keys = nullptr, *d_iota = nullptr, *d_ids = nullptr;
+  int64_t* d_counts = nullptr;
+  float* d_packed = nullptr;
+  void* d_tmp = nullptr;
+  const int64_t nn = std::max<int64_t>(n, 1);
+  cudaError_t e = cudaSuccess;
+  auto ck = [&](cudaError_t x, const char* what) {
+    if (rc == MANS_OK && x != cudaSuccess) rc = fail_cuda(x, what);
+  };
+  if (rc == MANS_OK) {
+    ck(cudaMalloc(&d_assign, nn * sizeof(uint32_t)), "cudaMalloc(build)");
+    ck(cudaMalloc(&d_keys, nn * sizeof(uint32_t)), "cudaMalloc(build)");
+    ck(cudaMalloc(&d_iota, nn * sizeof(uint32_t)), "cudaMalloc(build)");
+    ck(cudaMalloc(&d_ids, nn * sizeof(uint32_t)), "cudaMalloc(build)");
+    ck(cudaMalloc(&d_counts, nlist * sizeof(int64_t)), "cudaMalloc(build)");
+    ck(cudaMalloc(&ivf->offsets, (nlist + 1) * sizeof(int64_t)), "cudaMalloc(build)");
+    ck(cudaMalloc(&d_packed, nn * dim * sizeof(float)), "cudaMalloc(build)");
+  }
+  // 1. assignment (exact, ties to the lower list)
+  if (rc == MANS_OK) rc = assign_rows_device(ctx, corpus, ivf->cent, metric, d_assign);
+  // 2. stable counting sort of the rows by list: list ids ascend by row
+  if (rc == MANS_OK && n > 0) {
+    int bits = 1;
+    while ((1ll << bits) < nlist) ++bits;
+    size_t tmp_bytes = 0;
+    ck(cub::DeviceRadixSort::SortPairs(nullptr, tmp_bytes, d_assign, d_keys, d_iota, d_ids,
+                                       static_cast<int>(n), 0, bits),
+       "radix sort size");
+    if (rc == MANS_OK) ck(cudaMalloc(&d_tmp, tmp_bytes), "cudaMalloc(sort)");
+    if (rc == MANS_OK) {
+      iota_u32_kernel<<<static_cast<unsigned>((n + 255) / 256), 256>>>(d_iota, n);
+      ck(cudaGetLastError(), "iota");
+      ck(cub::DeviceRadixSort::SortPairs(d_tmp, tmp_bytes, d_assign, d_keys, d_iota, d_ids,
+                                         static_cast<int>(n), 0, bits),
+         "radix sort");
+    }
+  }
+  // 3. offsets from the list sizes
+  if (rc == MANS_OK) {
+    ck(cudaMemset(d_counts, 0, nlist * sizeof(int64_t)), "counts clear");
+    if (rc == MANS_OK && n > 0) {
+      list_histogram_kernel<<<static_cast<unsigned>((n + 255) / 256), 256>>>(d_assign, n, d_counts);
+      ck(cudaGetLastError(), "list sizes");
+    }
+    if (rc == MANS_OK) {
+      list_offsets_kernel<<<1, 1024>>>(d_counts, nlist, ivf->offsets);
+      ck(cudaGetLastError(), "list offsets");
+    }
+  }
+  // 4. packed rows in list order
+  if (rc == MANS_OK && n > 0) {
+    gather_rows_kernel<<<static_cast<unsigned>((n * 32 + 255) / 256), 256>>>(
+        corpus->rows, corpus->ld, d_ids, n, static_cast<int32_t>(dim), d_packed);
+    ck(cudaGetLastError(), "gather rows");
+  }
+  if (rc == MANS_OK) ck(cudaDeviceSynchronize(), "partition build");
+  if (rc == MANS_OK) rc = corpus_upload(ctx, d_packed, n, dim, 0, &ivf->packed);
+  if (rc == MANS_OK) {
+    ivf->packed->ids = d_ids;  // owned by the packed corpus from here on
+    d_ids = nullptr;
+    ivf->h_offsets.resize(nlist + 1);
+    ck(cudaMemcpy(ivf->h_offsets.data(), ivf->offsets, (nlist + 1) * sizeof(int64_t),
+                  cudaMemcpyDeviceToHost),
+       "offsets download");
+  }
+  if (rc == MANS_OK) {
+    for (int32_t l = 0; l < nlist; ++l)
+      ivf->max_len = std::max(ivf->max_len, ivf->h_offsets[l + 1] - ivf->h_offsets[l]);
+  }
+  cudaFree(d_assign);
+  cudaFree(d_keys);
+  cudaFree(d_iota);
+  if (d_ids) cudaFree(d_ids);
+  cudaFree(d_counts);
+  cudaFree(d_packed);
+  if (d_tmp) cudaFree(d_tmp);
+  (void)e;
+  if (rc != MANS_OK) {
+    corpus_free(ivf->cent);
+    corpus_free(ivf->packed);
+    if (ivf->offsets) cudaFree(ivf->offsets);
+    delete ivf;
+    return rc;
+  }
+  *out_ivf = ivf;
+  return MANS_OK;
+}
+
+int32_t mans_ivf_layout(const mans_ivf* ivf, int64_t* list_offsets, uint32_t* list_ids) {
+  if (!ivf) return fail(MANS_ERR_INVALID, "null IVF index");
+  DeviceGuard g(ivf->ctx->device);
+  if (list_offsets)
+    std::memcpy(list_offsets, ivf->h_offsets.data(), (ivf->nlist + 1) * sizeof(int64_t));
+  if (list_ids && ivf->n > 0) {
+    cudaError_t e = cudaMemcpy(list_ids, ivf->packed->ids, ivf->n * sizeof(uint32_t),
+                               cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return fail_cuda(e, "list id download");
+  }
+  return MANS_OK;
+}
+
+}  // extern "C"

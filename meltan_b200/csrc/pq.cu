@@ -710,3 +710,145 @@ int32_t mans_pq_adc_list(mans_ctx* ctx, const float* query, int64_t dim, const f
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Encoding on the device (IVFPQIndex.add: nearestCoarseCentroid,
+// IVFPQIndex.swift:514-550, then ProductQuantizer.encode(vector:subtracting:),
+// ProductQuantizer.swift:120-169).
+// ---------------------------------------------------------------------------
+
+namespace mans {
+namespace {
+
+// One warp per vector.  Per subspace every lane scores the codewords
+// lane, lane + 32, ... with the reference's sequential sum of ((v - c) - cb)^2
+// and keeps the first strict minimum; the warp then takes the smallest
+// (distance, index).  No distance below FLT_MAX leaves code 0, as the
+// reference's `bestDistance = greatestFiniteMagnitude` start does.
+__global__ void pq_encode_kernel(const float* __restrict__ vecs, int64_t n, int32_t dim,
+                                 const float* __restrict__ coarse, int64_t coarse_ld,
+                                 const uint32_t* __restrict__ assign,
+                                 const float* __restrict__ codebooks, int32_t m, int32_t ks,
+                                 int32_t sub, int32_t cb_in_smem, uint8_t* __restrict__ out) {
+  extern __shared__ float cbs[];
+  if (cb_in_smem) {
+    for (int64_t i = threadIdx.x; i < static_cast<int64_t>(m) * ks * sub; i += blockDim.x)
+      cbs[i] = codebooks[i];
+    __syncthreads();
+  }
+  const float* cb = cb_in_smem ? cbs : codebooks;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; i < n;
+       i += warps) {
+    const float* v = vecs + i * dim;
+    const float* c = coarse + static_cast<int64_t>(assign[i]) * coarse_ld;
+    for (int s = 0; s < m; ++s) {
+      float bd = 3.40282347e+38f;
+      int bi = 0x7FFFFFFF;
+      for (int w = lane; w < ks; w += 32) {
+        const float* code = cb + (static_cast<int64_t>(s) * ks + w) * sub;
+        float sum = 0.0f;
+        for (int d = 0; d < sub; ++d) {
+          const float delta = __fsub_rn(__fsub_rn(v[s * sub + d], c[s * sub + d]), code[d]);
+          sum = __fadd_rn(sum, __fmul_rn(delta, delta));
+        }
+        if (sum < bd) {
+          bd = sum;
+          bi = w;
+        }
+      }
+      for (int o = 16; o > 0; o >>= 1) {
+        const float od = __shfl_xor_sync(0xFFFFFFFFu, bd, o);
+        const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+        if (od < bd || (od == bd && oi < bi)) {
+          bd = od;
+          bi = oi;
+        }
+      }
+      if (lane == 0) out[i * m + s] = static_cast<uint8_t>(bi == 0x7FFFFFFF ? 0 : bi);
+    }
+  }
+}
+
+}  // namespace
+}  // namespace mans
+
+extern "C" int32_t mans_pq_encode(mans_ctx* ctx, const float* vectors, int64_t n, int64_t dim,
+                                  const float* coarse, int32_t nlist, const float* codebooks,
+                                  int32_t m, int32_t ks, int32_t metric, uint8_t* out_codes,
+                                  int32_t* out_assign) {
+  using namespace mans;
+  if (!ctx || (n > 0 && (!vectors || !out_codes)) || !coarse || !codebooks)
+    return fail(MANS_ERR_INVALID, "null context or buffer");
+  if (n < 0 || dim <= 0 || nlist <= 0 || m <= 0 || ks <= 0 || ks > 256 || dim % m != 0)
+    return fail(MANS_ERR_INVALID, "bad PQ shape (dim must split into m subspaces, ks <= 256)");
+  if (metric < 0 || metric > 2) return fail(MANS_ERR_SEARCH, "PQ encode needs cosine, l2 or ip");
+  if (n == 0) return MANS_OK;
+  DeviceGuard g(ctx->device);
+  const int32_t sub = static_cast<int32_t>(dim / m);
+  mans_corpus* cc = nullptr;
+  int32_t rc = corpus_upload(ctx, coarse, nlist, dim, 0, &cc);
+  if (rc != MANS_OK) return rc;
+  mans_workspace* ws = acquire_workspace(ctx);
+  if (!ws) {
+    corpus_free(cc);
+    return fail(MANS_ERR_OOM, "no workspace stream");
+  }
+  const size_t cb_bytes = static_cast<size_t>(m) * ks * sub * sizeof(float);
+  const int cb_in_smem = cb_bytes <= static_cast<size_t>(ctx->max_smem) - 1024 ? 1 : 0;
+  const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(1 << 20, (512ll << 20) / (dim * 4)));
+  float *d_v = nullptr, *d_cb = nullptr, *d_dist = nullptr;
+  uint32_t* d_assign = nullptr;
+  int32_t* d_cnt = nullptr;
+  uint8_t* d_codes = nullptr;
+  auto ck = [&](cudaError_t x, const char* what) {
+    if (rc == MANS_OK && x != cudaSuccess) rc = fail_cuda(x, what);
+  };
+  ck(cudaMalloc(&d_v, chunk * dim * sizeof(float)), "cudaMalloc(encode)");
+  ck(cudaMalloc(&d_cb, cb_bytes), "cudaMalloc(encode)");
+  ck(cudaMalloc(&d_dist, chunk * sizeof(float)), "cudaMalloc(encode)");
+  ck(cudaMalloc(&d_assign, chunk * sizeof(uint32_t)), "cudaMalloc(encode)");
+  ck(cudaMalloc(&d_cnt, chunk * sizeof(int32_t)), "cudaMalloc(encode)");
+  ck(cudaMalloc(&d_codes, chunk * m), "cudaMalloc(encode)");
+  if (rc == MANS_OK) ck(cudaMemcpy(d_cb, codebooks, cb_bytes, cudaMemcpyHostToDevice), "codebooks");
+  if (rc == MANS_OK && cb_in_smem)
+    ck(cudaFuncSetAttribute(pq_encode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            static_cast<int>(cb_bytes)),
+       "encode configure");
+  for (int64_t r0 = 0; rc == MANS_OK && r0 < n; r0 += chunk) {
+    const int64_t rows = std::min(chunk, n - r0);
+    ck(cudaMemcpyAsync(d_v, vectors + r0 * dim, rows * dim * sizeof(float),
+                       cudaMemcpyHostToDevice, ws->stream),
+       "vectors upload");
+    // nearestCoarseCentroid: SIMDDistance, strict '<' = (distance, index) minimum
+    if (rc == MANS_OK)
+      rc = run_flat_search(ctx, cc, ws, d_v, rows, 1, metric, d_dist, d_assign, d_cnt, ws->stream,
+                           kModeSimd, 512);
+    if (rc == MANS_OK) {
+      const int grid = static_cast<int>(std::min<int64_t>((rows + 7) / 8, ctx->num_sms * 8ll));
+      pq_encode_kernel<<<grid, 256, cb_in_smem ? cb_bytes : 0, ws->stream>>>(
+          d_v, rows, static_cast<int32_t>(dim), cc->rows, cc->ld, d_assign, d_cb, m, ks, sub,
+          cb_in_smem, d_codes);
+      ck(cudaGetLastError(), "encode launch");
+    }
+    if (rc == MANS_OK)
+      ck(cudaMemcpyAsync(out_codes + r0 * m, d_codes, rows * m, cudaMemcpyDeviceToHost, ws->stream),
+         "codes download");
+    if (rc == MANS_OK && out_assign)
+      ck(cudaMemcpyAsync(out_assign + r0, d_assign, rows * sizeof(uint32_t),
+                         cudaMemcpyDeviceToHost, ws->stream),
+         "assignment download");
+    if (rc == MANS_OK) ck(cudaStreamSynchronize(ws->stream), "encode");
+  }
+  if (rc == MANS_OK) rc = check_device_error(ws, ws->stream);
+  cudaFree(d_v);
+  cudaFree(d_cb);
+  cudaFree(d_dist);
+  cudaFree(d_assign);
+  cudaFree(d_cnt);
+  cudaFree(d_codes);
+  release_workspace(ctx, ws);
+  corpus_free(cc);
+  return rc;
+}

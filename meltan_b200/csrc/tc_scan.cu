@@ -1367,7 +1367,7 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   const int64_t smin = i8 ? 65536 : 16384;
   int64_t sample = std::min<int64_t>(n, std::max<int64_t>(smin, std::min<int64_t>(131072, 256ll * keff)));
   sample = std::min<int64_t>(n, (sample + kRN - 1) / kRN * kRN);
-  const int32_t cap = i8 ? 32768 : 8192;
+  const int32_t cap = static_cast<int32_t>(std::min<int64_t>(i8 ? 32768 : 8192, n));
 
   size_t o = 0;
   const size_t o_qbf = carve(o, nq_pad * ld16 * esize);

@@ -71,6 +71,33 @@ class Partition:
         offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
         return cls(context, centroids, corpus[order], order, offsets)
 
+    @classmethod
+    def build(cls, context: Context, corpus, centroids, metric: Metric):
+        """Partition built on the device from an uploaded corpus (a
+        VectorBuffer) and trained centroids: IVFFlatSearch.buildPartition
+        after its k-means (IVFFlatSearch.swift:559-631)."""
+        c = _f32(centroids)
+        if c.ndim != 2 or c.shape[1] != corpus.dim:
+            raise DimensionMismatch(f"expected {corpus.dim}-wide centroids")
+        self = cls.__new__(cls)
+        h = C.c_void_p()
+        check(lib().mans_ivf_build(context.handle, corpus.handle, C.c_void_p(c.ctypes.data),
+                                   c.shape[0], int(metric), C.byref(h)))
+        self._h = h
+        self.context = context
+        self.nlist = c.shape[0]
+        self.dim = c.shape[1]
+        self.count = corpus.count
+        return self
+
+    def layout(self):
+        """(list offsets [nlist + 1] int64, list ids [n] uint32)."""
+        off = np.empty(self.nlist + 1, np.int64)
+        ids = np.empty(self.count, np.uint32)
+        check(lib().mans_ivf_layout(self._h, C.c_void_p(off.ctypes.data),
+                                    C.c_void_p(ids.ctypes.data)))
+        return off, ids
+
     @property
     def handle(self):
         return self._h
@@ -85,6 +112,15 @@ class Partition:
             self.close()
         except Exception:
             pass
+
+
+def assign_rows(context: Context, corpus, centroids, metric: Metric) -> np.ndarray:
+    """IVFFlatSearch.assignRows on the device (IVFFlatSearch.swift:633-703)."""
+    c = _f32(centroids)
+    out = np.empty(corpus.count, np.int32)
+    check(lib().mans_ivf_assign(context.handle, corpus.handle, C.c_void_p(c.ctypes.data),
+                                c.shape[0], int(metric), C.c_void_p(out.ctypes.data)))
+    return out
 
 
 class IVFFlatSearch:

@@ -96,6 +96,23 @@ class IVFPQIndex:
             pass
 
 
+def encode(context: Context, vectors, coarse, codebooks, metric: Metric = Metric.l2):
+    """IVFPQIndex.add's encoding on the device: (codes [n, m] uint8, coarse
+    assignment [n] int32) -- nearestCoarseCentroid (IVFPQIndex.swift:514-550)
+    and ProductQuantizer.encode(vector:subtracting:) (ProductQuantizer.swift:
+    120-169), bit-exact."""
+    v = _f32(np.atleast_2d(vectors))
+    coarse = _f32(coarse)
+    cb = _f32(codebooks)
+    m, ks, sub = cb.shape
+    n, dim = v.shape
+    codes = np.empty((n, m), np.uint8)
+    assign = np.empty(n, np.int32)
+    check(lib().mans_pq_encode(context.handle, _vp(v), n, dim, _vp(coarse), coarse.shape[0],
+                               _vp(cb), m, ks, int(metric), _vp(codes), _vp(assign)))
+    return codes, assign
+
+
 class GPUADCSearch:
     @staticmethod
     def compute_distances(context: Context, query, codebooks, codes) -> np.ndarray:

@@ -111,3 +111,43 @@ def test_ivf_full_size_1m_x_384(ctx):
         for a, b in zip(got, want):
             np.testing.assert_array_equal(a, b)
     part.close()
+
+
+@pytest.mark.parametrize("mg,mo", MET)
+def test_gpu_partition_build_equals_host_layout(ctx, mg, mo):
+    """buildPartition on the device (assignRows + counting-sort layout +
+    packed rows): the assignment, offsets and list ids equal the oracle's
+    restatement (IVFFlatSearch.swift:559-703), and searches match the oracle
+    on that layout."""
+    v, q = bench.make_mixture(30000, 48, 40, 21, seed=11)
+    rng = np.random.default_rng(12)
+    cent = v[rng.choice(len(v), 40, replace=False)] + np.float32(0.01)
+    buf = mb.VectorBuffer(ctx, v)
+    got_assign = mb.assign_rows(ctx, buf, cent, mg)
+    want_assign = O.ivf_assign(v, cent, mo)
+    np.testing.assert_array_equal(got_assign, want_assign)
+    part = mb.Partition.build(ctx, buf, cent, mg)
+    off, ids = part.layout()
+    woff, wids, packed, pn = O.ivf_layout(v, want_assign, len(cent))
+    np.testing.assert_array_equal(off, woff)
+    np.testing.assert_array_equal(ids, wids)
+    for nprobe in (1, 5, 40):
+        got = mb.IVFFlatSearch.search_arrays(ctx, q, part, 10, nprobe, mg)
+        want = O.ivf_search(cent, packed, pn, wids, woff, q, 10, nprobe, mo)
+        for a, b in zip(got, want):
+            np.testing.assert_array_equal(a, b)
+    part.close()
+    buf.close()
+
+
+def test_gpu_partition_build_single_list_and_tiny(ctx):
+    v, q = bench.make_mixture(700, 20, 3, 4, seed=13)
+    buf = mb.VectorBuffer(ctx, v)
+    for cent in (v[:1].copy(), v[:700:100].copy()):
+        part = mb.Partition.build(ctx, buf, cent, mb.Metric.l2)
+        off, ids = part.layout()
+        woff, wids, _, _ = O.ivf_layout(v, O.ivf_assign(v, cent, O.L2), len(cent))
+        np.testing.assert_array_equal(off, woff)
+        np.testing.assert_array_equal(ids, wids)
+        part.close()
+    buf.close()

@@ -125,3 +125,34 @@ def test_ivfpq_large(ctx):
     ix = mb.IVFPQIndex(ctx, coarse, cb, codes, (off, flat))
     same(ix.search_arrays(q, 10, 32), O.ivfpq_search(coarse, cb, codes, off, flat, q, 10, 32, O.L2))
     ix.close()
+
+
+@pytest.mark.parametrize("metric", [O.L2, O.COSINE, O.IP])
+def test_gpu_encode_matches_reference_encode(ctx, metric):
+    """IVFPQIndex.add's encoding on the device: coarse assignment
+    (nearestCoarseCentroid) and residual codes (encode(vector:subtracting:))
+    equal the oracle's restatement for every vector, including tied codewords
+    (duplicated codebook rows: the first index wins)."""
+    rng = np.random.default_rng(21)
+    n, dim, m = 3000, 64, 8
+    v = rng.standard_normal((n, dim), dtype=np.float32)
+    coarse = rng.standard_normal((24, dim), dtype=np.float32)
+    cb = rng.standard_normal((m, 256, dim // m), dtype=np.float32) * np.float32(0.5)
+    cb[:, 200:] = cb[:, 100:156]  # exact duplicates
+    codes, assign = mb.pq_encode(ctx, v, coarse, cb, mb.Metric(metric))
+    for i in range(0, n, 7):
+        a = O.nearest_coarse(v[i], coarse, metric)
+        assert assign[i] == a
+        np.testing.assert_array_equal(codes[i], O.pq_encode_subtracting(v[i], coarse[a], cb))
+
+
+def test_gpu_encode_small_codebooks_and_scalar_subspaces(ctx):
+    rng = np.random.default_rng(22)
+    v = rng.standard_normal((777, 12), dtype=np.float32)
+    coarse = v[:5].copy()
+    cb = rng.standard_normal((12, 16, 1), dtype=np.float32)  # ks 16, sub 1
+    codes, assign = mb.pq_encode(ctx, v, coarse, cb)
+    for i in range(777):
+        a = O.nearest_coarse(v[i], coarse, O.L2)
+        assert assign[i] == a
+        np.testing.assert_array_equal(codes[i], O.pq_encode_subtracting(v[i], coarse[a], cb))
