@@ -113,12 +113,12 @@ def make_mixture(n, dim, components, nq, sigma=0.3, seed=0):
     return draw(n), draw(nq)
 
 
-def train_partition(v, nlist, metric, iters=4, seed=42, device=None):
-    """Coarse centroids + row assignment for an IVF partition (build-time step,
-    outside the search path): Lloyd iterations on a strided sample, as
-    IVFFlatSearch.buildPartition samples min(n, max(L, min(4096, 16L))) rows
-    (IVFFlatSearch.swift:529-551), computed with torch matmuls.  Returns
-    (centroids, assignment) with assignment = argmin of the metric key."""
+def train_centroids(v, nlist, iters=4, seed=42, device=None):
+    """Coarse centroids: Lloyd iterations on a strided sample of
+    min(n, max(L, min(4096, 16L))) rows, the sample size of
+    IVFFlatSearch.buildPartition (IVFFlatSearch.swift:529-551), with torch
+    matmuls (the reference's KMeans is seeded by Swift's generator, which
+    cannot be reproduced here)."""
     import torch
     dev = device or ("cuda" if torch.cuda.is_available() else "cpu")
     n = v.shape[0]
@@ -132,6 +132,45 @@ def train_partition(v, nlist, metric, iters=4, seed=42, device=None):
         s = torch.zeros_like(cent).index_add_(0, a, x)
         c = torch.bincount(a, minlength=nlist).unsqueeze(1).to(s.dtype)
         cent = torch.where(c > 0, s / c.clamp(min=1), cent)
+    return cent.cpu().numpy().astype(np.float32)
+
+
+def train_pq_codebooks(v, coarse, m, iters=4, seed=43, device=None):
+    """Per-subspace 256-centroid codebooks on the residuals of a 65,536-row
+    sample (torch; codebook training is outside the search path)."""
+    import torch
+    dev = device or ("cuda" if torch.cuda.is_available() else "cpu")
+    n, dim = v.shape
+    sub = dim // m
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    samp = torch.randperm(n, generator=g)[:min(n, 65536)].numpy()
+    x = torch.from_numpy(v[samp]).to(dev)
+    ct = torch.from_numpy(coarse).to(dev)
+    near = torch.argmin(torch.cdist(x, ct), dim=1)
+    x = x - ct[near]
+    books = []
+    for s in range(m):
+        xs = x[:, s * sub:(s + 1) * sub]
+        cb = xs[torch.randperm(xs.shape[0], generator=g)[:256].to(dev)].clone()
+        for _ in range(iters):
+            a = torch.argmin(torch.cdist(xs, cb), dim=1)
+            acc = torch.zeros_like(cb).index_add_(0, a, xs)
+            c = torch.bincount(a, minlength=256).unsqueeze(1).to(acc.dtype)
+            cb = torch.where(c > 0, acc / c.clamp(min=1), cb)
+        books.append(cb)
+    return torch.stack(books).cpu().numpy().astype(np.float32)
+
+
+def train_partition(v, nlist, metric, iters=4, seed=42, device=None):
+    """Coarse centroids + row assignment for an IVF partition (build-time step,
+    outside the search path): Lloyd iterations on a strided sample, as
+    IVFFlatSearch.buildPartition samples min(n, max(L, min(4096, 16L))) rows
+    (IVFFlatSearch.swift:529-551), computed with torch matmuls.  Returns
+    (centroids, assignment) with assignment = argmin of the metric key."""
+    import torch
+    dev = device or ("cuda" if torch.cuda.is_available() else "cpu")
+    n = v.shape[0]
+    cent = torch.from_numpy(train_centroids(v, nlist, iters=iters, seed=seed, device=dev)).to(dev)
     full = torch.from_numpy(v).to(dev)
     cn = (cent * cent).sum(1)
     assign = torch.empty(n, dtype=torch.int64, device=dev)
@@ -552,14 +591,42 @@ def index_workload_config(args, nq=None, nprobe=None):
     return cfg
 
 
-def build_index_data(args, nq_max, device=None):
-    """Synthetic mixture data and the trained index artefacts (build-time
-    steps outside the timed search path)."""
+def build_index_data(args, nq_max, device=None, mb=None, ctx=None):
+    """Synthetic mixture data and the index artefacts (build-time steps
+    outside the timed search path).  With the library (`mb`, `ctx`) the
+    partition layout / the PQ codes are built on the device by
+    mans_ivf_build / mans_pq_encode (timed as `build_gpu_s`); otherwise
+    (the reference arm) with torch."""
     metric = METRIC_NAMES[args.metric]
     v, q = make_mixture(args.n, args.dim, args.components, nq_max)
+    if mb is not None and args.workload == "ivf":
+        import torch
+        cent = train_centroids(v, args.nlist)
+        buf = mb.VectorBuffer(ctx, v)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        part = mb.Partition.build(ctx, buf, cent, mb.Metric(metric))
+        gpu_s = time.perf_counter() - t0
+        off, ids = part.layout()
+        return v, q, {"centroids": cent, "offsets": off, "ids": ids, "partition": part,
+                      "corpus": buf, "build_gpu_s": gpu_s,
+                      "build_gpu": "mans_ivf_build: assignRows + layout + packed rows"}
+    if mb is not None:
+        coarse = train_centroids(v, args.nlist, seed=42)
+        cb = train_pq_codebooks(v, coarse, args.pq_m)
+        t0 = time.perf_counter()
+        codes, assign = mb.pq_encode(ctx, v, coarse, cb, mb.Metric(metric))
+        gpu_s = time.perf_counter() - t0
+        flat = np.argsort(assign, kind="stable").astype(np.uint32)
+        off = np.concatenate([[0], np.cumsum(np.bincount(assign, minlength=args.nlist))])
+        return v, q, {"coarse": coarse, "codebooks": cb, "codes": codes,
+                      "offsets": off.astype(np.int64), "lists": flat, "build_gpu_s": gpu_s,
+                      "build_gpu": "mans_pq_encode: nearestCoarseCentroid + residual codes"}
     if args.workload == "ivf":
         cent, assign = train_partition(v, args.nlist, metric, device=device)
-        return v, q, {"centroids": cent, "assign": assign}
+        order = np.argsort(assign, kind="stable").astype(np.uint32)
+        off = np.concatenate([[0], np.cumsum(np.bincount(assign, minlength=args.nlist))])
+        return v, q, {"centroids": cent, "offsets": off.astype(np.int64), "ids": order}
     coarse, cb, codes, off, flat = train_ivfpq(v, args.nlist, args.pq_m, metric=metric,
                                                device=device)
     return v, q, {"coarse": coarse, "codebooks": cb, "codes": codes, "offsets": off,
@@ -574,7 +641,8 @@ def probed_list_rows(args, art, q):
     qt = torch.from_numpy(q).to(dev)
     if args.workload == "ivf":
         c = torch.from_numpy(art["centroids"]).to(dev)
-        sizes = torch.bincount(torch.from_numpy(art["assign"]).to(dev), minlength=args.nlist)
+        off = torch.from_numpy(art["offsets"]).to(dev)
+        sizes = off[1:] - off[:-1]
         dots = qt @ c.T
         cn = (c * c).sum(1)
         metric = METRIC_NAMES[args.metric]
@@ -595,9 +663,8 @@ def index_searcher(args, v, art):
     import oracle as O
     metric = METRIC_NAMES[args.metric]
     if args.workload == "ivf":
-        assign = art["assign"]
-        order = np.argsort(assign, kind="stable").astype(np.uint32)
-        off = np.concatenate([[0], np.cumsum(np.bincount(assign, minlength=args.nlist))])
+        order = art["ids"]
+        off = art["offsets"]
         packed = v[order]
         pn = O.row_norms(packed)
 
@@ -717,13 +784,13 @@ def run_index(args, torch, mb, lib, world, rank, dist):
         if args.workload == "ivf" else [(256, args.nprobe)])
     nq_max = max([args.nq] + [x for x, _ in extra])
     t_build = time.perf_counter()
-    v, q_all, art = build_index_data(args, nq_max)
     ctx = mb.Context(torch.cuda.current_device())
+    v, q_all, art = build_index_data(args, nq_max, mb=mb, ctx=ctx)
     ws = mb.Workspace(ctx)
     L = lib
     kout = min(args.k, mb.MAX_TOP_K)
     if args.workload == "ivf":
-        part = mb.Partition.from_assignment(ctx, v, art["centroids"], art["assign"])
+        part = art["partition"]
         index = part
 
         def dev_fn(nprobe):
@@ -791,6 +858,8 @@ def run_index(args, torch, mb, lib, world, rank, dist):
             "gpu_launches": int(res["launches"]),
             "clocks": res["clocks"],
             "e2e_matches_device_path": res["ok"],
+            "build": {"device_s": art["build_gpu_s"], "what": art["build_gpu"],
+                      "rows": args.n},
             "also": [{"workload": r["workload"], "nq": r["nq"], "nprobe": r["nprobe"],
                       "steps": r["steps"],
                       "value": r["nq"] * r["steps"] / (r["total_ms"] * 1e-3),
@@ -813,6 +882,8 @@ def run_index(args, torch, mb, lib, world, rank, dist):
         print(json.dumps(line), flush=True)
     ws.close()
     index.close()
+    if "corpus" in art:
+        art["corpus"].close()
     ctx.close()
 
 
