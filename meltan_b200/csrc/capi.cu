@@ -52,13 +52,13 @@ static PFN_cuTensorMapEncodeTiled_v12000 encoder() {
 }
 
 int32_t encode_row_map(CUtensorMap* map, const float* base, int64_t rows, int64_t dim,
-                       int64_t ld) {
+                       int64_t ld, int box_rows) {
   auto enc = encoder();
   if (!enc) return fail(MANS_ERR_PIPELINE, "cuTensorMapEncodeTiled is unavailable");
   if (rows <= 0) rows = 1;
   cuuint64_t gdim[2] = {static_cast<cuuint64_t>(dim), static_cast<cuuint64_t>(rows)};
   cuuint64_t gstride[1] = {static_cast<cuuint64_t>(ld) * 4};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(kTileCols), static_cast<cuuint32_t>(kTileRows)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kTileCols), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estride[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), gdim,
                    gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -237,7 +237,10 @@ int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace
   const int32_t kp = pow2_at_least(keff);
   const int qb = choose_qb(nq);
   const int64_t groups = (nq + qb - 1) / qb;
-  const int64_t tiles = (n + kTileRows - 1) / kTileRows;
+  // a scan that would leave most SMs idle with 256-row tiles uses 64-row ones
+  const int tile_rows =
+      groups * ((n + kTileRows - 1) / kTileRows) * 2 <= ctx->num_sms ? kSmallTileRows : kTileRows;
+  const int64_t tiles = (n + tile_rows - 1) / tile_rows;
   int64_t splits = std::max<int64_t>(1, ctx->num_sms / std::max<int64_t>(groups, 1));
   splits = std::min<int64_t>(splits, tiles);
   const int64_t nseg = groups * splits;
@@ -264,6 +267,7 @@ int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace
   p.stages = stages;
   p.flat_splits = static_cast<int32_t>(splits);
   p.flat_tiles = static_cast<int32_t>(tiles);
+  p.tile_rows = tile_rows;
   p.n = n;
   p.nq = nq;
   p.queries = d_queries;
@@ -283,7 +287,8 @@ int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace
   p.err = static_cast<int*>(ws->err.ptr);
   int grid = static_cast<int>(std::min<int64_t>(nseg, ctx->num_sms));
   cudaEvent_t ev_stop = timing_begin(ws, stream);
-  cudaError_t e = launch_scan(qb, corpus->map, p, grid, stream);
+  cudaError_t e =
+      launch_scan(qb, tile_rows == kTileRows ? corpus->map : corpus->map_small, p, grid, stream);
   if (e != cudaSuccess) return fail_cuda(e, "scan launch");
   timing_end(ev_stop, stream);
   ws->launches += (qn ? 1 : 0) + 2;
@@ -346,6 +351,7 @@ int32_t corpus_upload(mans_ctx* ctx, const float* rows, int64_t n, int64_t dim, 
     }
   }
   int32_t rc = encode_row_map(&c->map, c->rows, n, dim, c->ld);
+  if (rc == MANS_OK) rc = encode_row_map(&c->map_small, c->rows, n, dim, c->ld, kSmallTileRows);
   if (rc != MANS_OK) {
     corpus_free(c);
     return rc;

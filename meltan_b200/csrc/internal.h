@@ -37,7 +37,8 @@ struct DeviceGuard {
 
 int32_t fail(int32_t code, const std::string& msg);
 int32_t fail_cuda(cudaError_t e, const char* what);
-int32_t encode_row_map(CUtensorMap* map, const float* base, int64_t rows, int64_t dim, int64_t ld);
+int32_t encode_row_map(CUtensorMap* map, const float* base, int64_t rows, int64_t dim, int64_t ld,
+                       int box_rows = 256);
 
 }  // namespace mans
 
@@ -66,6 +67,7 @@ struct mans_corpus {
   uint32_t* ids = nullptr;  // optional row -> reported id (packed IVF lists)
   bool owned = true;        // rows/norms/ids freed with the object
   CUtensorMap map;
+  CUtensorMap map_small;  // the same rows in boxes of kSmallTileRows
   // bf16 copy and error-bound terms for the tensor-core batch path (built on
   // first use, dropped when rows change)
   std::mutex tc_mu;

@@ -247,7 +247,19 @@ static int32_t run_ivf_search(mans_ctx* ctx, mans_ivf* ivf, mans_workspace* ws,
   const int32_t kp = pow2_at_least(keff);
   const int64_t pairs = nq * probe;
   const int qb = choose_qb((pairs + ivf->nlist - 1) / ivf->nlist);
-  const int64_t max_chunks = std::max<int64_t>(1, (ivf->max_len + kChunkRows - 1) / kChunkRows);
+  // Work units: list chunks of 64 rows (64-row tiles) or 256 / 512 rows
+  // (256-row tiles) -- the smallest chunk whose unit count still fits in one
+  // wave of CTAs, so a short probe spreads over many SMs without giving one
+  // CTA several units in a row.
+  const int64_t avg_len = (ivf->n + ivf->nlist - 1) / ivf->nlist;
+  auto units_for = [&](int64_t chunk) { return pairs * ((avg_len + chunk - 1) / chunk); };
+  int chunk_rows = kChunkRows;
+  if (units_for(kSmallTileRows) <= ctx->num_sms)
+    chunk_rows = kSmallTileRows;
+  else if (units_for(kTileRows) <= ctx->num_sms)
+    chunk_rows = kTileRows;
+  const bool small = chunk_rows == kSmallTileRows;
+  const int64_t max_chunks = std::max<int64_t>(1, (ivf->max_len + chunk_rows - 1) / chunk_rows);
   const int64_t max_refs = pairs * max_chunks;
   const int64_t max_segs = max_refs;
   if (max_refs * qb > INT32_MAX / 2) return fail(MANS_ERR_SEARCH, "query batch too large");
@@ -312,7 +324,7 @@ static int32_t run_ivf_search(mans_ctx* ctx, mans_ivf* ivf, mans_workspace* ws,
   pp.nlist = ivf->nlist;
   pp.offsets = ivf->offsets;
   pp.qb = qb;
-  pp.chunk = kChunkRows;
+  pp.chunk = chunk_rows;
   pp.list_cnt = reinterpret_cast<int32_t*>(A + o_lc);
   pp.list_tmp = reinterpret_cast<int32_t*>(A + o_lt);
   pp.list_qoff = reinterpret_cast<int32_t*>(A + o_lq);
@@ -354,11 +366,12 @@ static int32_t run_ivf_search(mans_ctx* ctx, mans_ivf* ivf, mans_workspace* ws,
   p.metric = metric;
   p.k = keff;
   p.kp = kp;
+  p.tile_rows = small ? kSmallTileRows : kTileRows;
   p.slot_keys = static_cast<uint64_t*>(ws->slot_keys.ptr);
   p.slot_counts = static_cast<int32_t*>(ws->slot_counts.ptr);
   p.err = pp.err;
   cudaEvent_t stop = timing_begin(ws, stream);
-  e = launch_scan(qb, ivf->packed->map, p, ctx->num_sms, stream);
+  e = launch_scan(qb, small ? ivf->packed->map_small : ivf->packed->map, p, ctx->num_sms, stream);
   if (e != cudaSuccess) return fail_cuda(e, "ivf scan launch");
   timing_end(stop, stream);
 

@@ -7,7 +7,8 @@
 
 namespace mans {
 
-constexpr int kTileRows = 256;                               // rows per TMA box
+constexpr int kTileRows = 256;                               // rows per TMA box (largest)
+constexpr int kSmallTileRows = 64;  // box rows for small scans: more CTAs share a short scan
 constexpr int kTileCols = 32;                                // fp32 columns per box (128 B)
 constexpr int kTileBytes = kTileRows * kTileCols * 4;        // 32 KiB per pipeline stage
 constexpr int kConsumerWarps = 8;                            // one corpus row per thread
@@ -64,6 +65,7 @@ struct ScanParams {
   uint64_t* slot_keys;   // [slot][kp]
   int32_t* slot_counts;  // [slot]
   int* err;
+  int32_t tile_rows;  // rows per TMA box / tile: kTileRows or kSmallTileRows
 };
 
 size_t scan_smem_bytes(int qb, int nchunks, int stages);

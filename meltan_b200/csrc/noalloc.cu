@@ -122,6 +122,7 @@ extern "C" int32_t mans_flat_search_noalloc(mans_ctx* ctx, const mans_corpus* co
   p.nseg = static_cast<int32_t>(groups * splits);
   p.nseg_dev = nullptr;
   p.stages = stages;
+  p.tile_rows = kTileRows;
   p.flat_splits = static_cast<int32_t>(splits);
   p.flat_tiles = static_cast<int32_t>(tiles);
   p.n = n;

@@ -76,8 +76,8 @@ __device__ inline void flat_segment(const ScanParams& p, int s, int qb, ScanSegm
   int r = s - g * p.flat_splits;
   int64_t t0 = static_cast<int64_t>(p.flat_tiles) * r / p.flat_splits;
   int64_t t1 = static_cast<int64_t>(p.flat_tiles) * (r + 1) / p.flat_splits;
-  int64_t row0 = t0 * kTileRows;
-  int64_t row1 = t1 * kTileRows < p.n ? t1 * kTileRows : p.n;
+  int64_t row0 = t0 * p.tile_rows;
+  int64_t row1 = t1 * p.tile_rows < p.n ? t1 * p.tile_rows : p.n;
   seg.row_begin = row0;
   seg.row_count = static_cast<int32_t>(row1 > row0 ? row1 - row0 : 0);
   seg.qbase = g * qb;
@@ -136,16 +136,16 @@ __global__ void __launch_bounds__(kScanThreads, 1)
       for (int s = blockIdx.x; s < nseg; s += gridDim.x) {
         ScanSegment seg;
         flat_segment(p, s, QB, seg);
-        int ntiles = (seg.row_count + kTileRows - 1) / kTileRows;
+        int ntiles = (seg.row_count + p.tile_rows - 1) / p.tile_rows;
         for (int rt = 0; rt < ntiles; ++rt) {
-          int32_t y = static_cast<int32_t>(seg.row_begin + static_cast<int64_t>(rt) * kTileRows);
+          int32_t y = static_cast<int32_t>(seg.row_begin + static_cast<int64_t>(rt) * p.tile_rows);
           for (int cc = 0; cc < p.nchunks; ++cc) {
             bool ok = mbar_wait_bounded(&sm.empty[stage], phase ^ 1u, p.err);
             if (!ok || *(volatile int*)&sm.ctrl[0]) {
               *(volatile int*)&sm.ctrl[0] = 1;
               goto producer_done;
             }
-            mbar_arrive_expect_tx(&sm.full[stage], kTileBytes);
+            mbar_arrive_expect_tx(&sm.full[stage], static_cast<uint32_t>(p.tile_rows) * kTileCols * 4);
             tma_load_2d(sm.tiles + static_cast<size_t>(stage) * (kTileBytes / 4), &map,
                         cc * kTileCols, y, &sm.full[stage]);
             ++issued;
@@ -213,10 +213,10 @@ __global__ void __launch_bounds__(kScanThreads, 1)
     }
     named_sync(1, kConsumers);
 
-    int ntiles = (seg.row_count + kTileRows - 1) / kTileRows;
+    int ntiles = (seg.row_count + p.tile_rows - 1) / p.tile_rows;
     for (int rt = 0; rt < ntiles; ++rt) {
-      int64_t local = static_cast<int64_t>(rt) * kTileRows + tid;
-      bool valid = local < seg.row_count;
+      int64_t local = static_cast<int64_t>(rt) * p.tile_rows + tid;
+      bool valid = tid < p.tile_rows && local < seg.row_count;
       int64_t row = seg.row_begin + local;
       float vn = 0.0f;
       uint32_t id = 0;
