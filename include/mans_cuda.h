@@ -60,6 +60,7 @@ extern "C" {
 #define MANS_ERR_EXEC 5     /* gpuExecutionFailed(_:), includes device wait timeouts */
 #define MANS_ERR_INVALID 6  /* constructionFailed(_:) (bad argument or handle) */
 #define MANS_ERR_DEVICE 7   /* deviceNotSupported */
+#define MANS_ERR_CORRUPT 8  /* corruptFile(_:) (index file loader) */
 
 typedef struct mans_ctx mans_ctx;
 typedef struct mans_corpus mans_corpus;
@@ -134,6 +135,32 @@ int64_t mans_corpus_dim(const mans_corpus *corpus);
  * (Int8CodeCache.swift:64-99); either output may be null.  Builds the int8
  * copy on the device when it does not exist yet. */
 int32_t mans_corpus_int8_codes(mans_corpus *corpus, int8_t *codes, float *scales);
+
+/* ---- index files (loadReadOnly) ------------------------------------------ */
+
+/* Header and section offsets of a reference index file (IndexSerializer
+ * format versions 1-3, Sources/MetalANNSCore/IndexSerializer.swift:11-137;
+ * version 3 is the page-aligned layout MmapIndexLoader maps,
+ * MmapIndexLoader.swift:38-200). */
+typedef struct {
+  uint32_t version, count, degree, dim, metric, storage; /* storage 0 fp32, 1 fp16, 2 binary */
+  uint32_t page_size;                                    /* version 3: the writer's page size */
+  uint32_t idmap_bytes, entry_point;
+  uint64_t vector_offset, vector_bytes, adjacency_offset, distance_offset, idmap_offset;
+} mans_mann_info;
+
+/* Parses and validates the file (the checks of IndexSerializer.load /
+ * MmapIndexLoader.load); no GPU work.  MANS_ERR_CORRUPT on a bad file. */
+int32_t mans_mann_read_info(const char *path, mans_mann_info *out);
+
+/* ANNSIndex.loadReadOnly(.mmap)'s vector section into a device corpus: the
+ * file is memory-mapped and rows [r0, r1) of shard `shard_index` of
+ * `shard_count` (the first count % shard_count shards hold one extra row)
+ * are uploaded with id_offset = r0; fp16 storage is widened to fp32 exactly;
+ * binary storage fails with MANS_ERR_SEARCH.  The graph sections and the JSON
+ * IDMap stay with the caller (mans_mann_read_info gives their offsets). */
+int32_t mans_corpus_load_mann(mans_ctx *ctx, const char *path, int32_t shard_index,
+                              int32_t shard_count, mans_corpus **out_corpus);
 
 /* ---- workspaces (device-pointer calls) ---------------------------------- */
 

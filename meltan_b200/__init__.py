@@ -7,6 +7,8 @@ ABI of ``include/mans_cuda.h``; this package is the host-side binding.
 from .core import (  # noqa: F401
     ANNSError,
     ConstructionFailed,
+    CorruptFile,
+    MannInfo,
     Context,
     DeviceNotSupported,
     DimensionMismatch,
@@ -25,6 +27,7 @@ from .core import (  # noqa: F401
     VectorBuffer,
     Workspace,
     check,
+    mann_info,
     topk_merge_device,
 )
 from .ivf import IVFFlatSearch, Partition, assign_rows  # noqa: F401,E402

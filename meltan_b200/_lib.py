@@ -27,6 +27,8 @@ SIGNATURES = {
     "mans_ctx_set_tensor_core_batch": (C.c_int32, [_VP, C.c_int32]),
     "mans_ctx_set_tensor_core_format": (C.c_int32, [_VP, C.c_int32]),
     "mans_corpus_int8_codes": (C.c_int32, [_VP, _VP, _VP]),
+    "mans_mann_read_info": (C.c_int32, [C.c_char_p, _VP]),
+    "mans_corpus_load_mann": (C.c_int32, [_VP, C.c_char_p, C.c_int32, C.c_int32, _VP]),
     "mans_workspace_last_path": (C.c_int32, [_VP, _VP]),
     "mans_workspace_fallbacks": (C.c_int32, [_VP, _I32]),
     "mans_corpus_create": (C.c_int32, [_VP, _VP, C.c_int64, C.c_int64, C.c_uint32, C.POINTER(_VP)]),

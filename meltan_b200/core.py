@@ -18,6 +18,7 @@ marshals and maps status codes to exceptions.
 from __future__ import annotations
 
 import ctypes as C
+import os
 import enum
 from dataclasses import dataclass
 from typing import List, Optional, Sequence
@@ -78,6 +79,10 @@ class DeviceNotSupported(ANNSError):
     pass
 
 
+class CorruptFile(ANNSError):
+    """ANNSError.corruptFile (Errors.swift:11): a malformed index file."""
+
+
 _STATUS = {
     1: DimensionMismatch,
     2: SearchFailed,
@@ -86,6 +91,7 @@ _STATUS = {
     5: GPUExecutionFailed,
     6: ConstructionFailed,
     7: DeviceNotSupported,
+    8: CorruptFile,
 }
 
 
@@ -149,6 +155,23 @@ class Context:
             pass
 
 
+class MannInfo(C.Structure):
+    """mans_mann_info: header and section offsets of a reference index file."""
+    _fields_ = [(name, C.c_uint32) for name in
+                ("version", "count", "degree", "dim", "metric", "storage", "page_size",
+                 "idmap_bytes", "entry_point")] + \
+               [(name, C.c_uint64) for name in
+                ("vector_offset", "vector_bytes", "adjacency_offset", "distance_offset",
+                 "idmap_offset")]
+
+
+def mann_info(path) -> MannInfo:
+    """Parses a reference index file (IndexSerializer versions 1-3)."""
+    info = MannInfo()
+    check(lib().mans_mann_read_info(os.fsencode(path), C.byref(info)))
+    return info
+
+
 class VectorBuffer:
     """Device-resident row-major fp32 corpus with cached squared norms."""
 
@@ -162,6 +185,22 @@ class VectorBuffer:
                                        id_offset, C.byref(h)))
         self._h = h
         self.id_offset = id_offset
+
+    @classmethod
+    def load_mann(cls, context: Context, path, shard_index: int = 0, shard_count: int = 1):
+        """Vector section of a reference index file (loadReadOnly(.mmap)):
+        rows of shard `shard_index` of `shard_count`, ids offset by the shard's
+        first row."""
+        self = cls.__new__(cls)
+        h = C.c_void_p()
+        check(lib().mans_corpus_load_mann(context.handle, os.fsencode(path), shard_index,
+                                          shard_count, C.byref(h)))
+        self._h = h
+        self.context = context
+        info = mann_info(path)
+        base, extra = divmod(info.count, shard_count)
+        self.id_offset = shard_index * base + min(shard_index, extra)
+        return self
 
     @property
     def handle(self):
