@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--nprobe", type=int, default=None)
     ap.add_argument("--components", type=int, default=None)
     ap.add_argument("--pq-m", type=int, default=16)
+    ap.add_argument("--transport", default="p2p", choices=["p2p", "nccl"],
+                    help="how row shards exchange their top-k blocks (N > 1)")
     a = ap.parse_args()
     # per-workload defaults (BASELINE.json configs[2] and [3])
     if a.workload == "ivf":
@@ -440,7 +442,8 @@ class Runner:
         dq = torch.from_numpy(q).cuda()
         P = mb.shard.packed_words(nq, kout)  # packed [dist | ids | counts] per rank
         ws, ctx, buf, sp = self.ws, self.ctx, self.buf, self.sp
-        sharded = mb.ShardedFlatSearch(ctx, buf, self.world, self.dist)
+        sharded = mb.ShardedFlatSearch(ctx, buf, self.world, self.dist,
+                                       transport=self.a.transport, rank=self.rank)
         bufs = sharded.buffers(nq, kout)
         out = bufs[2]
 
@@ -516,6 +519,9 @@ class Runner:
             self.dist.all_reduce(steps_t, op=self.dist.ReduceOp.MAX)
             self.dist.all_reduce(e2e_t, op=self.dist.ReduceOp.MAX)
         total_ms, e2e_ms, kern_avg_ms = stats.tolist()
+        # every rank is done with the peers' buffers before any is released
+        self.barrier()
+        sharded.close()
         return {"nq": nq, "steps": steps, "total_ms": total_ms, "e2e_ms": e2e_ms,
                 "kern_avg_ms": kern_avg_ms, "kern_launches": kern_launches,
                 "launches": total_launches, "p50_ms": p50(steps_t.tolist()),

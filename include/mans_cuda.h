@@ -92,7 +92,7 @@ int32_t mans_ctx_sm_count(const mans_ctx *ctx);
  * FlatGPUSearch.swift:652-707). */
 int32_t mans_ctx_set_tensor_core_batch(mans_ctx *ctx, int32_t min_batch);
 /* (Batches smaller than min_batch also take that path when the corpus holds at
- * least 2^28 elements, where reading half the bytes outweighs its fixed cost.) */
+ * least 2^27 elements, where reading half the bytes outweighs its fixed cost.) */
 
 /* Operand format of that path.  MANS_TC_BF16: bf16 rows; MANS_TC_INT8:
  * signed 8-bit codes quantised as the reference's int8 prefilter does
@@ -243,6 +243,32 @@ int32_t mans_topk_merge_device(mans_ctx *ctx, mans_workspace *ws, const float *d
                                int32_t n_lists, int64_t list_stride, int64_t nq, int32_t kin,
                                int32_t k, float *d_out_dist, uint32_t *d_out_ids,
                                int32_t *d_out_counts, void *cuda_stream);
+
+/* ---- peer-memory exchange (row shards on several GPUs) -------------------- */
+
+/* All-gather of the per-shard packed top-k blocks [distances | ids | counts]
+ * over NVLink peer memory, fused with the final (distance, id) merge -- the
+ * exchange step of ParallelFlatScan.mergeSorted (ParallelFlatScan.swift:
+ * 288-315) applied to row shards, without a collective library.  One
+ * exchange per rank (one process per GPU): create it, share the 64-byte IPC
+ * handle of every rank (any host channel), open, then every rank calls
+ * allgather in the same order.  A rank whose peers do not publish within 2 s
+ * gets MANS_ERR_EXEC from its next mans_workspace_check.  No reference
+ * counterpart (the reference runs on one GPU). */
+typedef struct mans_exchange mans_exchange;
+#define MANS_IPC_HANDLE_BYTES 64
+int32_t mans_exchange_create(mans_ctx *ctx, int32_t world, int32_t rank, int64_t max_block_words,
+                             mans_exchange **out);
+int32_t mans_exchange_handle(const mans_exchange *ex, void *out_handle);
+/* handles: world x MANS_IPC_HANDLE_BYTES, rank order. */
+int32_t mans_exchange_open(mans_exchange *ex, const void *handles);
+/* d_block: this rank's packed block for nq queries of kin entries; outputs:
+ * the merged top-min(k, 256) per query (device pointers, enqueued on the
+ * stream). */
+int32_t mans_exchange_allgather(mans_exchange *ex, mans_workspace *ws, const int32_t *d_block,
+                                int64_t nq, int32_t kin, int32_t k, float *d_out_dist,
+                                uint32_t *d_out_ids, int32_t *d_out_counts, void *cuda_stream);
+int32_t mans_exchange_destroy(mans_exchange *ex);
 
 /* ---- IVF-flat ------------------------------------------------------------ */
 

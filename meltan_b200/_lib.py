@@ -50,6 +50,12 @@ SIGNATURES = {
     "mans_topk_merge_device": (C.c_int32, [_VP, _VP, _VP, _VP, _VP, C.c_int32, C.c_int64,
                                            C.c_int64, C.c_int32, C.c_int32, _VP, _VP, _VP,
                                            _VP]),
+    "mans_exchange_create": (C.c_int32, [_VP, C.c_int32, C.c_int32, C.c_int64, _VP]),
+    "mans_exchange_handle": (C.c_int32, [_VP, _VP]),
+    "mans_exchange_open": (C.c_int32, [_VP, _VP]),
+    "mans_exchange_allgather": (C.c_int32, [_VP, _VP, _VP, C.c_int64, C.c_int32, C.c_int32, _VP,
+                                            _VP, _VP, _VP]),
+    "mans_exchange_destroy": (C.c_int32, [_VP]),
     "mans_ivf_create": (C.c_int32, [_VP, _VP, C.c_int32, C.c_int64, _VP, _VP, _VP, C.c_int64,
                                     C.POINTER(_VP)]),
     "mans_ivf_destroy": (C.c_int32, [_VP]),

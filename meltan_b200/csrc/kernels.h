@@ -105,6 +105,11 @@ struct MergeParams {
   uint32_t* out_ids;
   int32_t* out_counts;
   int* err;
+  // optional: before merging, wait (bounded) until wait_flags[0..wait_count)
+  // all hold wait_epoch (peer ranks' blocks have landed in in_* memory)
+  const uint32_t* wait_flags;
+  int32_t wait_count;
+  uint32_t wait_epoch;
 };
 cudaError_t launch_merge(const MergeParams& p, cudaStream_t stream);
 

@@ -370,6 +370,19 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const MergeParams 
     qc = 0;
     nb = 0;
   }
+  if (p.wait_flags && tid < p.wait_count) {
+    // peer blocks: acquire-load the flag a peer release-stored after its data
+    const unsigned long long t0 = global_ns();
+    for (uint32_t it = 0;; ++it) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p.wait_flags + tid) : "memory");
+      if (v == p.wait_epoch) break;
+      if ((it & 63u) == 63u && global_ns() - t0 > kWaitLimitNs) {
+        atomicExch(p.err, kErrTimeout);
+        break;
+      }
+    }
+  }
   __syncthreads();
   TopKState st{buf, &qc, &nb, &thr};
 

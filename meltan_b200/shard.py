@@ -14,9 +14,12 @@ then merged by (distance, id) on the device (``topk_merge_device`` with
 """
 from __future__ import annotations
 
-from . import core
+import ctypes as C
 
-__all__ = ["row_shard", "packed_words", "block_views", "all_gather_blocks",
+from . import core
+from ._lib import lib
+
+__all__ = ["row_shard", "packed_words", "block_views", "all_gather_blocks", "PeerExchange",
            "ShardedFlatSearch"]
 
 
@@ -61,12 +64,61 @@ def all_gather_blocks(dist, local_block, gathered):
     return gathered
 
 
+class PeerExchange:
+    """mans_exchange: the packed blocks of all ranks gathered over NVLink peer
+    memory and merged in one kernel (CUDA IPC handles shared once through
+    ``dist.all_gather_object``).  Every rank calls ``allgather`` in the same
+    order."""
+
+    HANDLE_BYTES = 64
+
+    def __init__(self, ctx, world: int, rank: int, max_block_words: int, dist):
+        h = C.c_void_p()
+        core.check(lib().mans_exchange_create(ctx.handle, world, rank, max_block_words,
+                                              C.byref(h)))
+        self._h = h
+        mine = (C.c_uint8 * self.HANDLE_BYTES)()
+        core.check(lib().mans_exchange_handle(h, mine))
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(mine))
+        flat = (C.c_uint8 * (self.HANDLE_BYTES * world)).from_buffer_copy(b"".join(handles))
+        core.check(lib().mans_exchange_open(h, flat))
+
+    def allgather(self, ws, block_ptr: int, nq: int, kin: int, k: int, out_dist: int,
+                  out_ids: int, out_counts: int, stream: int = 0):
+        core.check(lib().mans_exchange_allgather(
+            self._h, ws.handle, C.c_void_p(block_ptr), nq, kin, k, C.c_void_p(out_dist),
+            C.c_void_p(out_ids), C.c_void_p(out_counts), C.c_void_p(stream)))
+
+    def close(self):
+        if self._h:
+            lib().mans_exchange_destroy(self._h)
+            self._h = None
+
+
 class ShardedFlatSearch:
     """Exact flat search over a row-sharded corpus: this rank's shard is a
-    ``VectorBuffer`` created with ``id_offset`` = its first global row."""
+    ``VectorBuffer`` created with ``id_offset`` = its first global row.  The
+    per-rank blocks move by peer-memory exchange (``transport="p2p"``) or by
+    one NCCL all-gather (``"nccl"``)."""
 
-    def __init__(self, ctx, shard: "core.VectorBuffer", world: int, dist=None):
+    def __init__(self, ctx, shard: "core.VectorBuffer", world: int, dist=None,
+                 transport: str = "nccl", rank: int = 0):
         self.ctx, self.shard, self.world, self.dist = ctx, shard, world, dist
+        self.transport = transport if world > 1 else "none"
+        self.rank = rank
+        self._ex = {}
+
+    def _exchange(self, words: int):
+        ex = self._ex.get(words)
+        if ex is None:
+            ex = self._ex[words] = PeerExchange(self.ctx, self.world, self.rank, words, self.dist)
+        return ex
+
+    def close(self):
+        for ex in self._ex.values():
+            ex.close()
+        self._ex = {}
 
     def buffers(self, nq: int, kout: int):
         """(local block, gathered blocks, merged block) device tensors."""
@@ -89,6 +141,11 @@ class ShardedFlatSearch:
                                          target.data_ptr(), target[nq * kout:].data_ptr(),
                                          target[2 * nq * kout:].data_ptr(), stream)
         if self.world == 1:
+            return out
+        if self.transport == "p2p":
+            self._exchange(packed_words(nq, kout)).allgather(
+                ws, loc.data_ptr(), nq, kout, k, out.data_ptr(), out[nq * kout:].data_ptr(),
+                out[2 * nq * kout:].data_ptr(), stream)
             return out
         all_gather_blocks(self.dist, loc, gat)
         core.topk_merge_device(self.ctx, ws, gat.data_ptr(), gat[0, nq * kout:].data_ptr(),

@@ -1,0 +1,82 @@
+"""Peer-memory exchange (mans_exchange) on two GPUs: row shards searched on
+their own GPUs, blocks gathered over NVLink and merged in one kernel, equal to
+the oracle's search of the whole corpus; many calls in a row exercise both
+parities of the slots.  Needs two GPUs (skipped otherwise); the host logic of
+the split and the packed block is covered on CPU by test_shard_gloo.py."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, out_dir):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import meltan_b200 as mb
+    import oracle as O
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        n, dim, nq, k = 30011, 64, 6, 10
+        v = O.lcg_vectors(n, dim, 91)
+        q = O.lcg_vectors(nq, dim, 92)
+        ctx = mb.Context(rank)
+        r0, r1 = mb.row_shard(n, world, rank)
+        buf = mb.VectorBuffer(ctx, v[r0:r1], id_offset=r0)
+        ws = mb.Workspace(ctx)
+        sh = mb.ShardedFlatSearch(ctx, buf, world, dist, transport="p2p", rank=rank)
+        bufs = sh.buffers(nq, k)
+        dq = torch.from_numpy(q).cuda()
+        results = []
+        for it in range(7):
+            out = sh.search_device(ws, dq.data_ptr(), nq, k, mb.Metric.cosine, bufs)
+            ws.check()
+            results.append(out.cpu().numpy().copy())
+        torch.cuda.synchronize()
+        dist.barrier()
+        sh.close()
+        np.save(os.path.join(out_dir, f"r{rank}.npy"), np.stack(results))
+        ws.close()
+        buf.close()
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gpu_peer_exchange_equals_unsharded(tmp_path):
+    import torch
+    import torch.multiprocessing as mp
+
+    import oracle as O
+    from meltan_b200 import shard
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.start_processes(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    n, dim, nq, k = 30011, 64, 6, 10
+    want = O.flat_search(O.lcg_vectors(n, dim, 91), O.lcg_vectors(nq, dim, 92), k, O.COSINE)
+    for rank in range(2):
+        res = np.load(tmp_path / f"r{rank}.npy")
+        for blk in res:
+            d, i, c = shard.block_views(torch.from_numpy(blk), nq, k)
+            np.testing.assert_array_equal(c.numpy(), want[2])
+            np.testing.assert_array_equal(i.numpy().view(np.uint32), want[1])
+            np.testing.assert_array_equal(d.numpy(), want[0])
