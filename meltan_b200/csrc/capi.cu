@@ -156,6 +156,7 @@ void destroy_workspace(mans_workspace* ws) {
   ws->aux.release();
   ws->aux2.release();
   ws->tc_aux.release();
+  ws->tc_bar.release();
   ws->h_err.release();
   for (auto& pr : ws->events) {
     cudaEventDestroy(pr.first);
@@ -381,6 +382,10 @@ int32_t check_device_error(mans_workspace* ws, cudaStream_t stream) {
   if (e != cudaSuccess) return fail_cuda(e, "error word readback");
   if (h != 0) {
     ws->err_cleared = false;
+    if (ws->tc_bar.ptr) {  // a pass that gave up left the barrier count out of step
+      cudaMemset(ws->tc_bar.ptr, 0, sizeof(unsigned long long));
+      ws->tc_bar_base = 0;
+    }
     return fail(MANS_ERR_EXEC, h == kErrTimeout ? "device wait timed out"
                                                  : "device kernel reported an error");
   }

@@ -108,6 +108,10 @@ struct mans_workspace {
   // scratch of the tensor-core batch path alone: it runs nested inside other
   // searches (the IVF centroid scan) whose own scratch lives in `aux`
   mans::DeviceBuffer tc_aux;
+  // grid-barrier counter of the fused tensor-core pass (monotonic; the host
+  // keeps its expected value, both reset after a device error)
+  mans::DeviceBuffer tc_bar;
+  unsigned long long tc_bar_base = 0;
   mans::PinnedBuffer h_err;
   // optional CUDA-event timing of the dominant kernel (scan) launches
   bool timing = false;

@@ -29,6 +29,21 @@ struct TcParams {
   int32_t* cand_count;
   int32_t cand_cap;
   int* err;
+  // Fused sampling (sample_tiles > 0): each block first runs its first
+  // sample_tiles tiles as a sample (32-row group minima into samp_out
+  // [q][groups][sample_tiles][8]), meets the grid at a barrier, derives the
+  // thresholds of a share of its block's queries, meets it again and then
+  // runs its whole range filtered.  Needs a cooperative (co-resident) launch.
+  int32_t sample_tiles;
+  float* samp_out;
+  int64_t samp_ld;              // groups * sample_tiles * 8
+  unsigned long long* bar;      // grid barrier counter (monotonic across calls)
+  unsigned long long bar_base;  // its value at launch
+  int32_t k;
+  const float* q_eps;
+  const float* q_scale;
+  float* thr_out;               // per query: sample k-th + 2 eps
+  float* c_out;                 // per query: score-domain constant (also read as q_c)
 };
 
 // Corpus-wide terms of the error bound (maxima over rows, rounded up).

@@ -63,6 +63,17 @@ constexpr size_t kPipeBudget = 196 * 1024;
 constexpr int kRerankThreads = 256;
 constexpr int kMaxRerank = 2048;  // exact re-score list per query
 
+// Shared scratch of block_kth_smallest.
+struct KthSmem {
+  uint32_t hist[2048];
+  float list[1024];
+  float red[64];
+  uint32_t wsum[32];
+  float lo[4], scale[4];
+  int sel[4];
+  uint32_t sh[4];
+};
+
 // Shared-memory plan of tc_scan_kernel for a given width: the query block is
 // kept resident when its nk k-blocks fit in 96 KiB (dim <= 384), otherwise
 // it is streamed beside the rows in every stage.
@@ -73,6 +84,7 @@ struct TcLayout {
   size_t a_bytes;
   size_t stage_bytes;
   size_t bar_off;
+  size_t kth_off;
   size_t total;
 };
 
@@ -92,8 +104,10 @@ __host__ __device__ inline TcLayout tc_layout(int nk, int stream_queries) {
   L.bar_off = L.a_bytes + static_cast<size_t>(L.stages) * L.stage_bytes;
   // barriers: full/empty per stage, acc_full/acc_empty x2, a_full, a_empty, drain
   const size_t bars = 8 * (2 * static_cast<size_t>(L.stages) + 7);
-  // + tmem slot / abort (16 B) + row terms 2 x 2 x kRN floats
-  L.total = 1024 + L.bar_off + bars + 16 + 2 * 2 * kRN * sizeof(float);
+  // + tmem slot / abort (16 B) + row terms 2 x 2 x kRN floats + the k-th
+  // selection scratch of the fused sampling
+  L.kth_off = L.bar_off + bars + 16 + 2 * 2 * kRN * sizeof(float);
+  L.total = 1024 + L.kth_off + sizeof(KthSmem);
   return L;
 }
 
@@ -196,13 +210,216 @@ __device__ __forceinline__ float approx_distance(float alpha, float gamma, float
   return (alpha + beta) - gamma * v;
 }
 
+
+__device__ __forceinline__ int kth_bin(float v, float lo, float scale) {
+  return min(2047, max(0, static_cast<int>((v - lo) * scale)));
+}
+
+// k-th smallest of n finite values (counting repeats), by `nthreads` threads
+// (thread ids 0..nthreads-1) that meet at `sync`.  Each level takes the values still in play, reduces their min and
+// max, builds a 2048-bin linear histogram over [min, max] (the bin is a
+// monotone function of the value, so order is preserved) and scans to the bin
+// holding the k-th value.  A bin of at most 1024 values is sorted exactly;
+// a larger one becomes the set in play of the next level (membership = the
+// same bin at every earlier level).  Equal min and max end the search.  The
+// result is exact, or after four levels an upper bound (see below).
+template <typename Get, typename Sync>
+__device__ float block_kth_smallest(Get get, int64_t n, int k, KthSmem& S, int tid, int nthreads,
+                                    Sync sync) {
+  const int nw = nthreads >> 5;
+  const float inf = __int_as_float(0x7F800000);
+  uint32_t kk = static_cast<uint32_t>(k);
+  // only finite values take part (+inf marks an empty sample slot); with
+  // fewer than k of them the result is +inf
+  auto member = [&](float v, int level) {
+    if (!(v < inf) || !(v > -inf)) return false;
+    for (int l = 0; l < level; ++l)
+      if (kth_bin(v, S.lo[l], S.scale[l]) != S.sel[l]) return false;
+    return true;
+  };
+  for (int level = 0; level < 4; ++level) {
+    float lo = inf, hi = -inf;
+    uint32_t nfin = 0;
+    for (int64_t i = tid; i < n; i += nthreads) {
+      const float v = get(i);
+      if (member(v, level)) {
+        lo = fminf(lo, v);
+        hi = fmaxf(hi, v);
+        ++nfin;
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      lo = fminf(lo, __shfl_xor_sync(0xFFFFFFFFu, lo, o));
+      hi = fmaxf(hi, __shfl_xor_sync(0xFFFFFFFFu, hi, o));
+      nfin += __shfl_xor_sync(0xFFFFFFFFu, nfin, o);
+    }
+    if ((tid & 31) == 0) {
+      S.red[tid >> 5] = lo;
+      S.red[32 + (tid >> 5)] = hi;
+      S.wsum[tid >> 5] = nfin;
+    }
+    sync();
+    if (tid == 0) {
+      for (int w = 1; w < nw; ++w) {
+        S.red[0] = fminf(S.red[0], S.red[w]);
+        S.red[32] = fmaxf(S.red[32], S.red[32 + w]);
+        S.wsum[0] += S.wsum[w];
+      }
+    }
+    sync();
+    lo = S.red[0];
+    hi = S.red[32];
+    const uint32_t total = S.wsum[0];
+    sync();
+    if (total < kk) return inf;  // (level 0 only: deeper levels hold >= kk)
+    if (!(hi > lo)) return lo;   // every value in play is equal
+    const float scale = 2047.0f / (hi - lo);
+    for (int i = tid; i < 2048; i += nthreads) S.hist[i] = 0;
+    sync();
+    for (int64_t i = tid; i < n; i += nthreads) {
+      const float v = get(i);
+      if (member(v, level)) atomicAdd(&S.hist[kth_bin(v, lo, scale)], 1u);
+    }
+    sync();
+    {
+      // bin of the kk-th value: each thread sums a run of bins, a block-wide
+      // exclusive scan of the runs locates the crossing, whose owner scans it
+      const int per = 2048 / nthreads;
+      uint32_t run = 0;
+      for (int j = 0; j < per; ++j) run += S.hist[tid * per + j];
+      uint32_t inc = run;
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+        if ((tid & 31) >= o) inc += y;
+      }
+      if ((tid & 31) == 31) S.wsum[tid >> 5] = inc;
+      sync();
+      uint32_t before = 0;
+      for (int w = 0; w < (tid >> 5); ++w) before += S.wsum[w];
+      const uint32_t excl = before + inc - run;
+      if (excl < kk && excl + run >= kk) {
+        uint32_t cum = excl;
+        int b = tid * per;
+        for (int j = 0; j < per - 1; ++j, ++b) {
+          if (cum + S.hist[b] >= kk) break;
+          cum += S.hist[b];
+        }
+        S.lo[level] = lo;
+        S.scale[level] = scale;
+        S.sel[level] = b;
+        S.sh[1] = kk - cum;
+        S.sh[2] = S.hist[b];
+        S.sh[3] = 0;
+      }
+      sync();
+    }
+    kk = S.sh[1];
+    const uint32_t cnt = S.sh[2];
+    // four levels without isolating 1024 values (only for value sets of
+    // extreme dynamic range): the largest value in play bounds the k-th from
+    // above, which both callers accept (a looser threshold, a wider band)
+    if (cnt > 1024 && level == 3) return hi;
+    if (cnt <= 1024) {
+      for (int64_t i = tid; i < n; i += nthreads) {
+        const float v = get(i);
+        if (member(v, level + 1)) {
+          const uint32_t at = atomicAdd(&S.sh[3], 1u);
+          if (at < 1024) S.list[at] = v;
+        }
+      }
+      sync();
+      const int c = static_cast<int>(min(cnt, 1024u));
+      int m = 1;
+      while (m < c) m <<= 1;
+      for (int i = c + tid; i < m; i += nthreads) S.list[i] = __int_as_float(0x7F800000);
+      sync();
+      for (int a = 2; a <= m; a <<= 1) {
+        for (int j = a >> 1; j > 0; j >>= 1) {
+          for (int i = tid; i < m; i += nthreads) {
+            const int ixj = i ^ j;
+            if (ixj > i) {
+              const float x = S.list[i], y = S.list[ixj];
+              const bool up = (i & a) == 0;
+              if ((x > y) == up) {
+                S.list[i] = y;
+                S.list[ixj] = x;
+              }
+            }
+          }
+          sync();
+        }
+      }
+      const float r = S.list[min(kk, static_cast<uint32_t>(c)) - 1];
+      sync();
+      return r;
+    }
+  }
+  return 0.0f;  // not reached
+}
+
+
+// Filter threshold of one query from the k-th smallest sampled value `kth`
+// (+inf when the sample holds fewer than k values): t = kth + 2 eps (rounded
+// up) and the score-domain constant c.  With d~ = alpha + beta - gamma v the
+// filter keeps x = v - beta/gamma >= c = (alpha - t)/gamma (beta = 0 for
+// cosine / IP; alpha = 1 for cosine, 0 for IP), lowered by a margin far above
+// the rounding of either side, so the kept set contains every row with
+// d~ <= t (a few extra rows are harmless).  "Keep everything" is -FLT_MAX,
+// not -inf: padding rows carry x = -inf.
+__device__ __forceinline__ void threshold_from_kth(float kth, float eps, float alpha, float gamma,
+                                                   float scale, float* t_out, float* c_out) {
+  const float inf = __int_as_float(0x7F800000);
+  float t = inf;
+  if (kth != inf) {
+    // same rounding-safe widening as the band in tc_rerank_kernel, so that
+    // band <= thr whenever T_k <= the sample's k-th distance
+    t = kth + 2.0f * eps;
+    t = t + fabsf(t) * 1e-6f;
+  }
+  const float keep_all = -3.40282347e+38f;
+  float c;
+  if (t == inf) {
+    c = keep_all;
+  } else if (gamma > 0.0f) {
+    c = (alpha - t) / gamma;
+  } else {
+    c = alpha <= t ? keep_all : inf;
+  }
+  if (c != inf && c != keep_all) c = fmaxf(c - (fabsf(c) + scale) * 6.103515625e-05f, keep_all);
+  *t_out = t;
+  *c_out = c;
+}
+
+// Fused sampling, between the two grid barriers: the thresholds of the
+// queries qb*128 + l, l = grp, grp + groups, ... (this block's share of its
+// query block), from the sample minima all blocks wrote.  The 512 epilogue
+// threads (`et`) meet at named barrier 1.  Out of line, so that its registers
+// do not weigh on the epilogue's main loop.
+__device__ __noinline__ void fused_thresholds(const float* samp, int64_t samp_ld, int32_t k,
+                                              int64_t nq, int64_t gstep, const float* eps,
+                                              const float* alpha, const float* gamma,
+                                              const float* scale, float* thr_out, float* c_out,
+                                              KthSmem* ks, int et, int64_t qb, int64_t grp) {
+  for (int64_t l = grp; l < kQM; l += gstep) {
+    const int64_t qq = qb * kQM + l;
+    if (qq >= nq) break;
+    const float* vals = samp + qq * samp_ld;
+    float kth = __int_as_float(0x7F800000);
+    if (samp_ld >= k)
+      kth = block_kth_smallest([&](int64_t i) { return __ldcg(vals + i); }, samp_ld, k, *ks, et,
+                               kEpiWarps * 32, [] { named_sync(1, kEpiWarps * 32); });
+    if (et == 0)
+      threshold_from_kth(kth, eps[qq], alpha[qq], gamma[qq], scale[qq], thr_out + qq, c_out + qq);
+  }
+}
+
 // Epilogue variants: the dense sample pass, the filter on the raw dot
 // (cosine on normalised rows, IP) and the filter with a per-row bias (L2).
 enum TcMode : int { kDense = 0, kFilterPlain = 1, kFilterBias = 2 };
 
 // I8: signed 8-bit codes with a per-row factor (TcParams::row_w) instead of
 // bf16 rows; the s32 accumulator is converted and scaled in the epilogue.
-template <int MODE, bool I8>
+template <int MODE, bool I8, bool FUSED = false>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_scan_kernel(const __grid_constant__ CUtensorMap map_q,
                    const __grid_constant__ CUtensorMap map_r, const TcParams p) {
@@ -245,6 +462,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     u_begin = units * blockIdx.x / gridDim.x;
     u_end = units * (blockIdx.x + 1) / gridDim.x;
   }
+  // Fused sampling: the block's first s_c units run twice, first as the
+  // sample, then again with the filter (virtual unit v -> unit_of(v)).
+  const int64_t nown = u_end - u_begin;
+  const int64_t s_c =
+      FUSED ? (nown < p.sample_tiles ? nown : static_cast<int64_t>(p.sample_tiles)) : 0;
+  const int64_t nvirt = s_c + nown;
+  auto unit_of = [&](int64_t v) { return u_begin + (v < s_c ? v : v - s_c); };
 
 
   if (tid == 0) {
@@ -284,7 +508,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint32_t a_round = 0;
       int64_t issued = 0;
       bool a_pending = false;
-      for (int64_t u = u_begin; u < u_end && !*abort; ++u) {
+      for (int64_t v = 0; v < nvirt && !*abort; ++v) {
+        const int64_t u = unit_of(v);
         const int64_t qb = u / rtiles;
         const int64_t rt = u - qb * rtiles;
         if (L.resident && qb != cur_qb) {
@@ -333,7 +558,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int64_t cur_qb = -1;
       uint32_t a_round = 0;
       int local = 0;
-      for (int64_t u = u_begin; u < u_end && !*abort; ++u, ++local) {
+      for (int64_t v = 0; v < nvirt && !*abort; ++v, ++local) {
+        const int64_t u = unit_of(v);
         const int64_t qb = u / rtiles;
         if (L.resident && qb != cur_qb) {
           if (cur_qb >= 0) tc_commit(a_empty);  // old query block free once prior MMAs finish
@@ -395,7 +621,47 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     float alpha = 0.0f, gamma = 0.0f, hq = 0.0f, cq = __int_as_float(0x7F800000);
     int64_t q = 0;
     bool qvalid = false;
-    for (int64_t u = u_begin; u < u_end; ++u, ++local) {
+    const int64_t grp = p.groups > 0 ? blockIdx.x / p.qblocks : 0;
+    KthSmem* ks = reinterpret_cast<KthSmem*>(base + L.kth_off);
+    volatile int* bar_ok = reinterpret_cast<volatile int*>(&ks->sh[0]);
+    bool synced = !FUSED;
+    // grid barrier n (1 or 2) of this call: arrive, then wait (bounded)
+    auto grid_barrier = [&](unsigned long long n) -> bool {
+      named_sync(1, kEpiWarps * 32);
+      if (et == 0) {
+        __threadfence();
+        atomicAdd(p.bar, 1ull);
+        const unsigned long long target = p.bar_base + n * gridDim.x;
+        const unsigned long long t0 = global_ns();
+        int ok = 1;
+        for (uint32_t it = 0;; ++it) {
+          unsigned long long cur;
+          asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(cur) : "l"(p.bar) : "memory");
+          if (cur >= target) break;
+          if ((it & 63u) == 63u && global_ns() - t0 > kWaitLimitNs) {
+            atomicExch(p.err, kErrTimeout);
+            ok = 0;
+            break;
+          }
+        }
+        *bar_ok = ok;
+      }
+      named_sync(1, kEpiWarps * 32);
+      return *bar_ok != 0;
+    };
+    // after the sample tiles: thresholds of this block's share of its query
+    // block's queries (query qb*128 + l for l = grp, grp + groups, ...), then
+    // every block reads its queries' constants
+    auto fused_sync = [&](int64_t qb) -> bool {
+      if (!grid_barrier(1)) return false;
+      fused_thresholds(p.samp_out, p.samp_ld, p.k, p.nq, p.groups > 0 ? p.groups : 1, p.q_eps,
+                       p.q_alpha, p.q_gamma, p.q_scale, p.thr_out, p.c_out, ks, et, qb, grp);
+      if (!grid_barrier(2)) return false;
+      cq = qvalid ? __ldcg(p.c_out + q) : __int_as_float(0x7F800000);
+      return true;
+    };
+    for (int64_t vu = 0; vu < nvirt; ++vu, ++local) {
+      const int64_t u = unit_of(vu);
       const int64_t qb = u / rtiles;
       const int64_t rt = u - qb * rtiles;
       if (qb != cur_qb) {
@@ -405,7 +671,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         alpha = qvalid ? p.q_alpha[q] : 0.0f;
         gamma = qvalid ? p.q_gamma[q] : 0.0f;
         hq = gamma > 0.0f ? 1.0f / gamma : 0.0f;
-        cq = (qvalid && MODE != kDense) ? p.q_c[q] : __int_as_float(0x7F800000);
+        cq = (qvalid && MODE != kDense && synced) ? p.q_c[q] : __int_as_float(0x7F800000);
+        if (FUSED && !synced && qvalid) {
+          // sample slots this block has no tile for stay +inf
+          for (int64_t w = s_c; w < p.sample_tiles; ++w)
+            for (int c = 0; c < 2; ++c)
+              p.samp_out[q * p.samp_ld + (grp * p.sample_tiles + w) * 8 + part * 2 + c] =
+                  __int_as_float(0x7F800000);
+        }
+      }
+      const bool sampling = FUSED && vu < s_c;
+      if (FUSED && !synced && !sampling) {
+        synced = true;
+        if (!fused_sync(qb)) {
+          *abort = 1;
+          break;
+        }
       }
       const int b = local & 1;
       const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
@@ -441,7 +722,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           for (int t = 0; t < 32; ++t) v[t] = __int2float_rn(__float_as_int(v[t])) * rp[j0 + t];
         }
         const int64_t lr = lrow0 + c * 32;
-        if (MODE == kDense && p.dense_group == 32) {
+        if (sampling) {
+          // fused sample tile: one minimum per 32 rows (as the dense pass below)
+          const int64_t rem = p.rows - lr;
+          const int tmax = rem >= 32 ? 32 : (rem < 0 ? 0 : static_cast<int>(rem));
+          if (qvalid) {
+            float m = __int_as_float(0x7F800000);
+#pragma unroll
+            for (int t = 0; t < 32; ++t)
+              if (t < tmax)
+                m = fminf(m, approx_distance(alpha, gamma,
+                                             (I8 || p.row_beta) ? rp[kRN + j0 + t] : 0.0f, v[t]));
+            p.samp_out[q * p.samp_ld + (grp * p.sample_tiles + vu) * 8 + part * 2 + c] = m;
+          }
+        } else if (MODE == kDense && p.dense_group == 32) {
           // minimum of each 32-row group: the k-th smallest group minimum bounds
           // the sample's k-th smallest distance from above (k distinct rows lie
           // at or below it), at 1/32 of the output
@@ -506,6 +800,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
+    }
+    // a block whose range held only sample tiles (or none) still takes its
+    // part in both grid barriers
+    if (FUSED && !synced && !*abort) {
+      synced = true;
+      if (!fused_sync(cur_qb >= 0 ? cur_qb : static_cast<int64_t>(blockIdx.x % p.qblocks)))
+        *abort = 1;
     }
   }
   tc_fence_before();
@@ -738,152 +1039,6 @@ __global__ void tc_query_prep_kernel(const TcQueryParams p) {
   p.scale[q] = static_cast<float>(sc);
 }
 
-// Shared scratch of block_kth_smallest.
-struct KthSmem {
-  uint32_t hist[2048];
-  float list[1024];
-  float red[64];
-  uint32_t wsum[32];
-  float lo[4], scale[4];
-  int sel[4];
-  uint32_t sh[4];
-};
-
-__device__ __forceinline__ int kth_bin(float v, float lo, float scale) {
-  return min(2047, max(0, static_cast<int>((v - lo) * scale)));
-}
-
-// k-th smallest of n finite values (counting repeats), by a block of 256
-// threads.  Each level takes the values still in play, reduces their min and
-// max, builds a 2048-bin linear histogram over [min, max] (the bin is a
-// monotone function of the value, so order is preserved) and scans to the bin
-// holding the k-th value.  A bin of at most 1024 values is sorted exactly;
-// a larger one becomes the set in play of the next level (membership = the
-// same bin at every earlier level).  Equal min and max end the search.  The
-// result is exact, or after four levels an upper bound (see below).
-template <typename Get>
-__device__ float block_kth_smallest(Get get, int64_t n, int k, KthSmem& S) {
-  const int tid = threadIdx.x;
-  const int nw = static_cast<int>(blockDim.x >> 5);
-  uint32_t kk = static_cast<uint32_t>(k);
-  auto member = [&](float v, int level) {
-    for (int l = 0; l < level; ++l)
-      if (kth_bin(v, S.lo[l], S.scale[l]) != S.sel[l]) return false;
-    return true;
-  };
-  for (int level = 0; level < 4; ++level) {
-    float lo = __int_as_float(0x7F800000), hi = -__int_as_float(0x7F800000);
-    for (int64_t i = tid; i < n; i += blockDim.x) {
-      const float v = get(i);
-      if (member(v, level)) {
-        lo = fminf(lo, v);
-        hi = fmaxf(hi, v);
-      }
-    }
-    for (int o = 16; o > 0; o >>= 1) {
-      lo = fminf(lo, __shfl_xor_sync(0xFFFFFFFFu, lo, o));
-      hi = fmaxf(hi, __shfl_xor_sync(0xFFFFFFFFu, hi, o));
-    }
-    if ((tid & 31) == 0) {
-      S.red[tid >> 5] = lo;
-      S.red[32 + (tid >> 5)] = hi;
-    }
-    __syncthreads();
-    if (tid == 0) {
-      for (int w = 1; w < nw; ++w) {
-        S.red[0] = fminf(S.red[0], S.red[w]);
-        S.red[32] = fmaxf(S.red[32], S.red[32 + w]);
-      }
-    }
-    __syncthreads();
-    lo = S.red[0];
-    hi = S.red[32];
-    __syncthreads();
-    if (!(hi > lo)) return lo;  // every value in play is equal
-    const float scale = 2047.0f / (hi - lo);
-    for (int i = tid; i < 2048; i += blockDim.x) S.hist[i] = 0;
-    __syncthreads();
-    for (int64_t i = tid; i < n; i += blockDim.x) {
-      const float v = get(i);
-      if (member(v, level)) atomicAdd(&S.hist[kth_bin(v, lo, scale)], 1u);
-    }
-    __syncthreads();
-    {
-      // bin of the kk-th value: each thread sums a run of bins, a block-wide
-      // exclusive scan of the runs locates the crossing, whose owner scans it
-      const int per = 2048 / static_cast<int>(blockDim.x);
-      uint32_t run = 0;
-      for (int j = 0; j < per; ++j) run += S.hist[tid * per + j];
-      uint32_t inc = run;
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, inc, o);
-        if ((tid & 31) >= o) inc += y;
-      }
-      if ((tid & 31) == 31) S.wsum[tid >> 5] = inc;
-      __syncthreads();
-      uint32_t before = 0;
-      for (int w = 0; w < (tid >> 5); ++w) before += S.wsum[w];
-      const uint32_t excl = before + inc - run;
-      if (excl < kk && excl + run >= kk) {
-        uint32_t cum = excl;
-        int b = tid * per;
-        for (int j = 0; j < per - 1; ++j, ++b) {
-          if (cum + S.hist[b] >= kk) break;
-          cum += S.hist[b];
-        }
-        S.lo[level] = lo;
-        S.scale[level] = scale;
-        S.sel[level] = b;
-        S.sh[1] = kk - cum;
-        S.sh[2] = S.hist[b];
-        S.sh[3] = 0;
-      }
-      __syncthreads();
-    }
-    kk = S.sh[1];
-    const uint32_t cnt = S.sh[2];
-    // four levels without isolating 1024 values (only for value sets of
-    // extreme dynamic range): the largest value in play bounds the k-th from
-    // above, which both callers accept (a looser threshold, a wider band)
-    if (cnt > 1024 && level == 3) return hi;
-    if (cnt <= 1024) {
-      for (int64_t i = tid; i < n; i += blockDim.x) {
-        const float v = get(i);
-        if (member(v, level + 1)) {
-          const uint32_t at = atomicAdd(&S.sh[3], 1u);
-          if (at < 1024) S.list[at] = v;
-        }
-      }
-      __syncthreads();
-      const int c = static_cast<int>(min(cnt, 1024u));
-      int m = 1;
-      while (m < c) m <<= 1;
-      for (int i = c + tid; i < m; i += blockDim.x) S.list[i] = __int_as_float(0x7F800000);
-      __syncthreads();
-      for (int a = 2; a <= m; a <<= 1) {
-        for (int j = a >> 1; j > 0; j >>= 1) {
-          for (int i = tid; i < m; i += blockDim.x) {
-            const int ixj = i ^ j;
-            if (ixj > i) {
-              const float x = S.list[i], y = S.list[ixj];
-              const bool up = (i & a) == 0;
-              if ((x > y) == up) {
-                S.list[i] = y;
-                S.list[ixj] = x;
-              }
-            }
-          }
-          __syncthreads();
-        }
-      }
-      const float r = S.list[min(kk, static_cast<uint32_t>(c)) - 1];
-      __syncthreads();
-      return r;
-    }
-  }
-  return 0.0f;  // not reached
-}
-
 // Per query: thr_q = (k-th smallest value of the dense sample: row distances
 // or 32-row group minima, either at or above the sample's k-th smallest
 // distance) + 2 eps_q (+inf when the sample has fewer than k values) and the
@@ -901,7 +1056,6 @@ __global__ void __launch_bounds__(kThresholdThreads) tc_threshold_kernel(
   const int64_t q = blockIdx.x;
   const float* row = dense + q * ld;
   const float inf = __int_as_float(0x7F800000);
-  float t = inf;
   if (staged) {
     // every pass of the selection then reads shared memory
 #pragma unroll 4
@@ -911,35 +1065,14 @@ __global__ void __launch_bounds__(kThresholdThreads) tc_threshold_kernel(
     __syncthreads();
     row = stage;
   }
-  if (rows >= k) {
-    const float kth = block_kth_smallest([&](int64_t i) { return row[i]; }, rows, k, ks);
-    // same rounding-safe widening as the band in tc_rerank_kernel, so that
-    // band <= thr whenever T_k <= the sample's k-th distance
-    t = kth + 2.0f * eps[q];
-    t = t + fabsf(t) * 1e-6f;
-  }
-  if (threadIdx.x == 0) {
-    thr_out[q] = t;
-    // Score-domain constant: with d~ = alpha + beta - gamma v the filter keeps
-    // x = v - beta/gamma >= c = (alpha - t)/gamma  (beta = 0 for cosine / IP;
-    // alpha = 1 for cosine, 0 for IP), lowered by a margin far above the
-    // rounding of either side, so the kept set contains every row with
-    // d~ <= t (a few extra rows are harmless).  "Keep everything" is
-    // -FLT_MAX, not -inf: padding rows carry x = -inf.
-    (void)metric;
-    const float keep_all = -3.40282347e+38f;
-    float c;
-    const float g = gamma[q];
-    if (t == inf) {
-      c = keep_all;
-    } else if (g > 0.0f) {
-      c = (alpha[q] - t) / g;
-    } else {
-      c = alpha[q] <= t ? keep_all : inf;
-    }
-    if (c != inf && c != keep_all) c = fmaxf(c - (fabsf(c) + scale[q]) * 6.103515625e-05f, keep_all);
-    c_out[q] = c;
-  }
+  float kth = inf;
+  if (rows >= k)
+    kth = block_kth_smallest([&](int64_t i) { return row[i]; }, rows, k, ks,
+                             static_cast<int>(threadIdx.x), static_cast<int>(blockDim.x),
+                             [] { __syncthreads(); });
+  (void)metric;
+  if (threadIdx.x == 0)
+    threshold_from_kth(kth, eps[q], alpha[q], gamma[q], scale[q], thr_out + q, c_out + q);
 }
 
 struct RerankParams {
@@ -1068,7 +1201,7 @@ __global__ void __launch_bounds__(kRerankThreads) tc_rerank_kernel(const RerankP
   __syncthreads();
   if (!fail_flag) {
     const float tk = block_kth_smallest([&](int64_t i) { return key_distance(keys[i]); }, cnt,
-                                        p.k, ks);
+                                        p.k, ks, tid, kRerankThreads, [] { __syncthreads(); });
     if (tid == 0) {
       float band = tk + 2.0f * e;
       band = band + fabsf(band) * 1e-6f;
@@ -1369,6 +1502,33 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   sample = std::min<int64_t>(n, (sample + kRN - 1) / kRN * kRN);
   const int32_t cap = static_cast<int32_t>(std::min<int64_t>(i8 ? 32768 : 8192, n));
 
+  static const int stream_q = [] {
+    const char* e = getenv("MANS_TC_STREAM_QUERIES");
+    return e && e[0] == '1' ? 1 : 0;
+  }();
+  const TcLayout lay = tc_layout(tc_kblocks(static_cast<int>(corpus->dim), i8), stream_q);
+  // Full-pass grid: lockstep row groups when every query block gets a block.
+  const int64_t rtiles_all = (n + kRN - 1) / kRN;
+  int32_t groups_full =
+      qblocks <= ctx->num_sms ? static_cast<int32_t>(ctx->num_sms / qblocks) : 0;
+  groups_full = static_cast<int32_t>(std::min<int64_t>(groups_full, rtiles_all));
+  // Fused sampling (one cooperative launch instead of sample + threshold +
+  // pass): each block samples its first S tiles, S chosen so that the sample
+  // holds at least max(16384, 256 k) rows per query.
+  int coop = 0;
+  cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, ctx->device);
+  // (Only for one query block: with several, sampling S tiles per block
+  // inside the pass and deriving thresholds between the barriers stalls the
+  // MMA pipeline longer than the separate sample and threshold launches take.)
+  const bool fused = qblocks == 1 && groups_full > 0 && lay.resident && coop != 0;
+  int64_t samp_tiles = 0, samp_ld = 0;
+  if (fused) {
+    const int64_t want = std::max<int64_t>(16384, 256ll * keff);
+    samp_tiles = (want + kRN * groups_full - 1) / (kRN * groups_full);
+    samp_tiles = std::max<int64_t>(1, std::min<int64_t>(samp_tiles, rtiles_all / groups_full));
+    samp_ld = groups_full * samp_tiles * 8;
+  }
+
   size_t o = 0;
   const size_t o_qbf = carve(o, nq_pad * ld16 * esize);
   const size_t o_qn = carve(o, nq * sizeof(float));
@@ -1383,10 +1543,16 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   const int dgroup = (sample / 32 >= 4ll * keff) ? 32 : 1;
   const int64_t dvals = (sample + dgroup - 1) / dgroup;
   const int64_t dld = (dvals + 3) / 4 * 4;  // float4-aligned pitch of the dense sample
-  const size_t o_dn = carve(o, nq * dld * sizeof(float));
+  const size_t o_dn = carve(o, nq * (fused ? samp_ld : dld) * sizeof(float));
   const size_t o_cc = carve(o, nq * sizeof(int32_t) + sizeof(int32_t));
   const size_t o_cd = carve(o, nq * static_cast<size_t>(cap) * sizeof(uint64_t));
   if ((rc = ws->tc_aux.reserve(o)) != MANS_OK) return rc;
+  if (fused && !ws->tc_bar.ptr) {
+    if ((rc = ws->tc_bar.reserve(sizeof(unsigned long long))) != MANS_OK) return rc;
+    cudaError_t e0 = cudaMemsetAsync(ws->tc_bar.ptr, 0, sizeof(unsigned long long), stream);
+    if (e0 != cudaSuccess) return fail_cuda(e0, "barrier clear");
+    ws->tc_bar_base = 0;
+  }
   if ((rc = ws->err.reserve(sizeof(int))) != MANS_OK) return rc;
   if (!ws->err_cleared) {
     cudaError_t e = cudaMemsetAsync(ws->err.ptr, 0, sizeof(int), stream);
@@ -1426,11 +1592,6 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   CUtensorMap map_q;
   if ((rc = encode_tc_map(&map_q, qbf, nq_pad, corpus->dim, ld16, kQM, i8)) != MANS_OK) return rc;
   const CUtensorMap& map_r = i8 ? corpus->tc8_map : corpus->tc_map;
-  static const int stream_q = [] {
-    const char* e = getenv("MANS_TC_STREAM_QUERIES");
-    return e && e[0] == '1' ? 1 : 0;
-  }();
-  const TcLayout lay = tc_layout(tc_kblocks(static_cast<int>(corpus->dim), i8), stream_q);
   const size_t smem = lay.total;
   if (lay.stages < 2) return fail(MANS_ERR_SEARCH, "dimension too large for the tensor-core pass");
   // the attribute is per device; set it on every call (cheap, no allocation)
@@ -1468,7 +1629,8 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   tp.q_gamma = F(o_ga);
   tp.q_c = F(o_cq);
   tp.err = static_cast<int*>(ws->err.ptr);
-  // 2. sample pass (dense)
+  // 2. sample pass (dense) and 3. thresholds -- inside the full pass when fused
+  if (!fused) {
   tp.row0 = 0;
   tp.rows = sample;
   tp.dense_out = F(o_dn);
@@ -1499,6 +1661,7 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
       F(o_dn), dld, dvals, keff, staged, F(o_ep), F(o_al), F(o_ga), F(o_sc), metric, F(o_th),
       F(o_cq));
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc threshold launch");
+  }
   // 4. full filtered pass
   tp.rows = n;
   tp.dense_out = nullptr;
@@ -1512,16 +1675,44 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
     tp.groups = static_cast<int32_t>(std::min<int64_t>(tp.groups, (n + kRN - 1) / kRN));
     grid = static_cast<int>(tp.groups * qblocks);
   }
+  tp.row0 = 0;
+  if (fused) {
+    tp.sample_tiles = static_cast<int32_t>(samp_tiles);
+    tp.samp_out = F(o_dn);
+    tp.samp_ld = samp_ld;
+    tp.bar = static_cast<unsigned long long*>(ws->tc_bar.ptr);
+    tp.bar_base = ws->tc_bar_base;
+    tp.k = keff;
+    tp.q_eps = F(o_ep);
+    tp.q_scale = F(o_sc);
+    tp.thr_out = F(o_th);
+    tp.c_out = F(o_cq);
+  }
   cudaEvent_t stop = timing_begin(ws, stream);
-  if (metric == kL2 && i8)
+  if (fused) {
+    // co-resident blocks (one per SM) meet at two grid barriers
+    const void* fn =
+        metric == kL2 ? (i8 ? reinterpret_cast<const void*>(tc_scan_kernel<kFilterBias, true, true>)
+                            : reinterpret_cast<const void*>(tc_scan_kernel<kFilterBias, false, true>))
+                      : (i8 ? reinterpret_cast<const void*>(tc_scan_kernel<kFilterPlain, true, true>)
+                            : reinterpret_cast<const void*>(tc_scan_kernel<kFilterPlain, false, true>));
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+    if (e != cudaSuccess) return fail_cuda(e, "tc configure");
+    void* args[] = {const_cast<CUtensorMap*>(&map_q), const_cast<CUtensorMap*>(&map_r), &tp};
+    e = cudaLaunchCooperativeKernel(fn, grid, kTcThreads, args, smem, stream);
+    if (e == cudaSuccess) ws->tc_bar_base += 2ull * static_cast<unsigned long long>(grid);
+  } else if (metric == kL2 && i8) {
     tc_scan_kernel<kFilterBias, true><<<grid, kTcThreads, smem, stream>>>(map_q, map_r, tp);
-  else if (metric == kL2)
+  } else if (metric == kL2) {
     tc_scan_kernel<kFilterBias, false><<<grid, kTcThreads, smem, stream>>>(map_q, map_r, tp);
-  else if (i8)
+  } else if (i8) {
     tc_scan_kernel<kFilterPlain, true><<<grid, kTcThreads, smem, stream>>>(map_q, map_r, tp);
-  else
+  } else {
     tc_scan_kernel<kFilterPlain, false><<<grid, kTcThreads, smem, stream>>>(map_q, map_r, tp);
-  if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc scan launch");
+  }
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return fail_cuda(e, "tc scan launch");
   timing_end(stop, stream);
   // 5. certify + exact re-rank
   RerankParams rp{};
@@ -1551,7 +1742,7 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
                      rerank_smem_bytes(corpus->dim, rp.region), stream>>>(rp);
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc rerank launch");
   ws->tc_fallbacks = fallbacks;
-  ws->launches += 5;
+  ws->launches += fused ? 3 : 5;
   ws->last_path = i8 ? 2 : 1;
   return MANS_OK;
 }
