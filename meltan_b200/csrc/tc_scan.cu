@@ -413,6 +413,62 @@ __device__ __noinline__ void fused_thresholds(const float* samp, int64_t samp_ld
   }
 }
 
+// Per-query terms of the tensor-core pass from the query's sums (double):
+// |q|^2 (nq2), |q - q'|^2 (nres), |q'|^2 (nt) for the rounded query q', its
+// scale qs (int8; 1 for bf16) and the exact path's sequential fp32 |q|^2
+// (acc): the affine map d~ = alpha + beta - gamma s, the certified bound eps of
+// |d~ - d| and the magnitude bound `scale` of the score-domain value.
+struct QueryTerms {
+  float qn, alpha, gamma, eps, scale;
+};
+
+__device__ __forceinline__ QueryTerms query_terms(const TcCorpusStats& cs, int metric, int dim,
+                                                  float acc, double nq2, double nres, double nt,
+                                                  double qs) {
+  const double qnorm = sqrt(nq2), qres = sqrt(nres), qt = sqrt(nt);
+  // |dot(q, r) - dot(q', r')| <= |q - q'||r| + |q'||r - r'| plus the fp32
+  // accumulation of the tensor core (bf16) and of the exact sequential path:
+  // generously dim * 2^-22 of the magnitude sum each.  (For cosine the row
+  // terms are relative to |r|.)
+  const double cacc = static_cast<double>(dim) * 2.384185791015625e-07;
+  const double es = qres * cs.max_norm + qt * cs.max_resid + cacc * qt * cs.max_norm_bf16 +
+                    cacc * qnorm * cs.max_norm;
+  double alpha = 0.0, gamma = 1.0, lip = 1.0, mag, extra = 0.0;
+  if (metric == kL2) {
+    // alpha and the row terms are the exact path's own fp32 |q|^2, |r|^2
+    alpha = acc;
+    gamma = 2.0;
+    lip = 2.0;
+    mag = acc + cs.max_sqnorm + 2.0 * (qnorm * cs.max_norm + es);
+  } else if (metric == kCosine) {
+    // the tensor-core dot approximates dot(q, r)/|r| (bf16: rows normalised
+    // before rounding; int8: the row factor is u/|r|)
+    alpha = 1.0;
+    gamma = qnorm > 0.0 ? 1.0 / qnorm : 0.0;
+    lip = gamma;
+    mag = 1.0 + lip * (qnorm * cs.max_norm + es);
+    // the exact path divides by sqrt(fp32 |q|^2 * fp32 |r|^2); each sequential
+    // sum of squares is off by at most dim*2^-24 relatively, and |cos| <= 1
+    extra = (2.0 * dim + 16.0) * 5.960464477539063e-08;
+  } else {
+    mag = qnorm * cs.max_norm + es;
+  }
+  // rounding of both distance formulas (and, for int8, of the row factor and
+  // the product with the converted integer dot): 64 ulps of the largest magnitude
+  const double slack = mag * 64.0 * 5.960464477539063e-08 + extra + 1e-30;
+  QueryTerms t;
+  t.qn = acc;
+  t.alpha = static_cast<float>(alpha);
+  // the integer dot counts in units of the query scale
+  t.gamma = static_cast<float>(gamma * qs);
+  t.eps = static_cast<float>((lip * es + slack) * (1.0 + 1e-6));
+  // magnitude bound of the score-domain value x = v - beta / gamma
+  double sc = qt / qs * cs.max_norm_bf16;
+  if (metric == kL2) sc += cs.max_sqnorm / (gamma * qs);
+  t.scale = static_cast<float>(sc);
+  return t;
+}
+
 // Epilogue variants: the dense sample pass, the filter on the raw dot
 // (cosine on normalised rows, IP) and the filter with a per-row bias (L2).
 enum TcMode : int { kDense = 0, kFilterPlain = 1, kFilterBias = 2 };
@@ -997,46 +1053,12 @@ __global__ void tc_query_prep_kernel(const TcQueryParams p) {
     const float y = __ldg(v + c);
     acc = __fadd_rn(acc, __fmul_rn(y, y));
   }
-  const double qnorm = sqrt(nq2), qres = sqrt(nres), qt = sqrt(nt);
-  // |dot(q, r) - dot(q', r')| <= |q - q'||r| + |q'||r - r'| plus the fp32
-  // accumulation of the tensor core (bf16) and of the exact sequential path:
-  // generously dim * 2^-22 of the magnitude sum each.  (For cosine the row
-  // terms are relative to |r|.)
-  const double cacc = static_cast<double>(p.dim) * 2.384185791015625e-07;
-  const double es = qres * p.cs.max_norm + qt * p.cs.max_resid +
-                    cacc * qt * p.cs.max_norm_bf16 + cacc * qnorm * p.cs.max_norm;
-  double alpha = 0.0, gamma = 1.0, lip = 1.0, mag, extra = 0.0;
-  if (p.metric == kL2) {
-    // alpha and the row terms are the exact path's own fp32 |q|^2, |r|^2
-    alpha = acc;
-    gamma = 2.0;
-    lip = 2.0;
-    mag = acc + p.cs.max_sqnorm + 2.0 * (qnorm * p.cs.max_norm + es);
-  } else if (p.metric == kCosine) {
-    // the tensor-core dot approximates dot(q, r)/|r| (bf16: rows normalised
-    // before rounding; int8: the row factor is u/|r|)
-    alpha = 1.0;
-    gamma = qnorm > 0.0 ? 1.0 / qnorm : 0.0;
-    lip = gamma;
-    mag = 1.0 + lip * (qnorm * p.cs.max_norm + es);
-    // the exact path divides by sqrt(fp32 |q|^2 * fp32 |r|^2); each sequential
-    // sum of squares is off by at most dim*2^-24 relatively, and |cos| <= 1
-    extra = (2.0 * p.dim + 16.0) * 5.960464477539063e-08;
-  } else {
-    mag = qnorm * p.cs.max_norm + es;
-  }
-  // rounding of both distance formulas (and, for int8, of the row factor and
-  // the product with the converted integer dot): 64 ulps of the largest magnitude
-  const double slack = mag * 64.0 * 5.960464477539063e-08 + extra + 1e-30;
-  p.qn_exact[q] = acc;
-  p.alpha[q] = static_cast<float>(alpha);
-  // the integer dot counts in units of the query scale
-  p.gamma[q] = static_cast<float>(gamma * qs);
-  p.eps[q] = static_cast<float>((lip * es + slack) * (1.0 + 1e-6));
-  // magnitude bound of the score-domain value x = v - beta / gamma
-  double sc = qt / qs * p.cs.max_norm_bf16;
-  if (p.metric == kL2) sc += p.cs.max_sqnorm / (gamma * qs);
-  p.scale[q] = static_cast<float>(sc);
+  const QueryTerms t = query_terms(p.cs, p.metric, p.dim, acc, nq2, nres, nt, qs);
+  p.qn_exact[q] = t.qn;
+  p.alpha[q] = t.alpha;
+  p.gamma[q] = t.gamma;
+  p.eps[q] = t.eps;
+  p.scale[q] = t.scale;
 }
 
 // Per query: thr_q = (k-th smallest value of the dense sample: row distances
