@@ -92,7 +92,7 @@ int32_t mans_ctx_sm_count(const mans_ctx *ctx);
  * FlatGPUSearch.swift:652-707). */
 int32_t mans_ctx_set_tensor_core_batch(mans_ctx *ctx, int32_t min_batch);
 /* (Batches smaller than min_batch also take that path when the corpus holds at
- * least 2^27 elements, where reading half the bytes outweighs its fixed cost.) */
+ * least 2^25 elements, where reading half the bytes outweighs its fixed cost.) */
 
 /* Operand format of that path.  MANS_TC_BF16: bf16 rows; MANS_TC_INT8:
  * signed 8-bit codes quantised as the reference's int8 prefilter does

@@ -210,9 +210,11 @@ int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace
   const int64_t n = corpus->n;
   if (nq <= 0) return MANS_OK;
   // Tensor-core path: batches of at least tc_min_batch queries, and any batch
-  // over a corpus of at least 2^27 elements, where halving the bytes read
-  // outweighs the fixed cost (~50 us) of the sample, threshold and re-rank.
-  const bool tc_size = nq >= ctx->tc_min_batch || n * corpus->dim >= (int64_t{1} << 27);
+  // over a corpus of at least 2^25 elements (87k rows at d = 384): there the
+  // bf16 pass over half the bytes, fused with its sampling, plus prep and
+  // re-rank (~35 us) beats the fp32 scan, whose short shards also leave
+  // SMs idle.
+  const bool tc_size = nq >= ctx->tc_min_batch || n * corpus->dim >= (int64_t{1} << 25);
   ws->last_path = 0;
   if (mode == kModeHost && kcap == MANS_MAX_TOPK && ctx->tc_min_batch > 0 && tc_size && k > 0 &&
       n > 0 && !corpus->ids) {
