@@ -588,7 +588,9 @@ def index_workload_config(args, nq=None, nprobe=None):
         name = f"ivfpq_{base}_m{args.pq_m}_nprobe{nprobe}_{args.metric}_top{args.k}_nq{nq}"
     cfg = {"workload": name, "n": args.n, "dim": args.dim, "nq": nq, "k": args.k,
            "metric": args.metric, "nlist": args.nlist, "nprobe": nprobe,
-           "components": args.components, "parallelism": f"replica{args.gpus}",
+           "components": args.components,
+           "parallelism": (f"rowshard{args.gpus}" if args.workload == "ivf" and args.gpus > 1
+                           else f"replica{args.gpus}"),
            "l2": "probed lists differ per query; each step streams its lists once "
                  "(no flush; lists of one batch may hit L2)"}
     if args.workload == "ivfpq":
@@ -597,7 +599,7 @@ def index_workload_config(args, nq=None, nprobe=None):
     return cfg
 
 
-def build_index_data(args, nq_max, device=None, mb=None, ctx=None):
+def build_index_data(args, nq_max, device=None, mb=None, ctx=None, shard=None, dist=None):
     """Synthetic mixture data and the index artefacts (build-time steps
     outside the timed search path).  With the library (`mb`, `ctx`) the
     partition layout / the PQ codes are built on the device by
@@ -608,7 +610,12 @@ def build_index_data(args, nq_max, device=None, mb=None, ctx=None):
     if mb is not None and args.workload == "ivf":
         import torch
         cent = train_centroids(v, args.nlist)
-        buf = mb.VectorBuffer(ctx, v)
+        if dist is not None:  # one set of centroids for every shard
+            ct = torch.from_numpy(cent).cuda()
+            dist.broadcast(ct, 0)
+            cent = ct.cpu().numpy()
+        r0, r1 = shard if shard else (0, v.shape[0])
+        buf = mb.VectorBuffer(ctx, v[r0:r1], id_offset=r0)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         part = mb.Partition.build(ctx, buf, cent, mb.Metric(metric))
@@ -698,22 +705,27 @@ def cpu_index_qps(args, v, q, art, seconds):
     return done / el, done
 
 
-def measure_index(torch, ws, search_dev, search_host, q, kout, steps, warmup, with_clocks):
+def measure_index(torch, ws, search_dev, search_host, q, kout, steps, warmup, with_clocks,
+                  barrier=None):
     """Device-timed steps (inputs resident) and end-to-end steps through the
-    host C ABI (pinned buffers), as Runner.measure does for the flat scan."""
+    host C ABI (pinned buffers), as Runner.measure does for the flat scan.
+    Row shards (``search_host`` None): ``search_dev`` returns the merged
+    packed block and the end-to-end step copies the queries in and the block
+    out around it; ``barrier`` lines the ranks up around the timed loops."""
     nq = q.shape[0]
     dq = torch.from_numpy(q).cuda()
+    sync = barrier or torch.cuda.synchronize
     od = torch.empty((nq, kout), dtype=torch.float32, device="cuda")
     oi = torch.empty((nq, kout), dtype=torch.int32, device="cuda")
     oc = torch.empty((nq,), dtype=torch.int32, device="cuda")
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
 
-    def step():
-        search_dev(dq.data_ptr(), nq, od.data_ptr(), oi.data_ptr(), oc.data_ptr(), sp)
+    def step(src=dq):
+        return search_dev(src.data_ptr(), nq, od.data_ptr(), oi.data_ptr(), oc.data_ptr(), sp)
 
     for _ in range(max(3, warmup)):
-        step()
+        last = step()
     ws.check(sp)
     ws.stats()
     ws.set_timing(True)
@@ -723,34 +735,53 @@ def measure_index(torch, ws, search_dev, search_host, q, kout, steps, warmup, wi
     if clocks:
         clocks.start()
         time.sleep(0.3)
+    sync()
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
     for i in range(steps):
         ev[i][0].record(stream)
-        step()
+        last = step()
         ev[i][1].record(stream)
     t1.record(stream)
     torch.cuda.synchronize()
+    sync()
     clock_info = clocks.stop() if clocks else None
     ws.check(sp)
     kern_ms, kern_launches, total_launches = ws.stats()
     ws.set_timing(False)
     total_ms = t0.elapsed_time(t1)
     step_ms = [x.elapsed_time(y) for x, y in ev]
-    dev_out = (od.cpu().numpy(), oi.cpu().numpy(), oc.cpu().numpy())
-
     hq = torch.from_numpy(q).pin_memory()
     hd = torch.empty((nq, kout), dtype=torch.float32).pin_memory()
     hi = torch.empty((nq, kout), dtype=torch.int32).pin_memory()
     hc = torch.empty((nq,), dtype=torch.int32).pin_memory()
+    if search_host is None:
+        from meltan_b200 import shard as _shard
+        d, i, c = _shard.block_views(last, nq, kout)
+        dev_out = (d.cpu().numpy(), i.cpu().numpy(), c.cpu().numpy())
+        dq2 = torch.empty_like(dq)
+        hblk = torch.empty_like(last, device="cpu").pin_memory()
 
-    def e2e():
-        search_host(hq.data_ptr(), nq, hd.data_ptr(), hi.data_ptr(), hc.data_ptr())
+        def e2e():
+            dq2.copy_(hq, non_blocking=True)
+            r = step(dq2)
+            hblk.copy_(r, non_blocking=True)
+            stream.synchronize()
+            bd, bi, bc = _shard.block_views(hblk, nq, kout)
+            hd.copy_(bd)
+            hi.copy_(bi)
+            hc.copy_(bc)
+    else:
+        dev_out = (od.cpu().numpy(), oi.cpu().numpy(), oc.cpu().numpy())
+
+        def e2e():
+            search_host(hq.data_ptr(), nq, hd.data_ptr(), hi.data_ptr(), hc.data_ptr())
 
     for _ in range(max(3, warmup)):
         e2e()
+    sync()
     e2e_times = []
     for _ in range(steps):
         t = time.perf_counter()
@@ -791,11 +822,35 @@ def run_index(args, torch, mb, lib, world, rank, dist):
     nq_max = max([args.nq] + [x for x, _ in extra])
     t_build = time.perf_counter()
     ctx = mb.Context(torch.cuda.current_device())
-    v, q_all, art = build_index_data(args, nq_max, mb=mb, ctx=ctx)
+    # IVF-flat shards its rows over the ranks (same centroids, global ids,
+    # per-rank blocks exchanged and merged); IVF-PQ runs replicas
+    ivf_sharded = args.workload == "ivf" and world > 1
+    shard = mb.row_shard(args.n, world, rank) if ivf_sharded else None
+    v, q_all, art = build_index_data(args, nq_max, mb=mb, ctx=ctx, shard=shard,
+                                     dist=dist if ivf_sharded else None)
     ws = mb.Workspace(ctx)
     L = lib
     kout = min(args.k, mb.MAX_TOP_K)
-    if args.workload == "ivf":
+    barrier = None
+    if ivf_sharded:
+        part = art["partition"]
+        index = part
+        sharded = mb.ShardedIVFSearch(ctx, part, world, dist, transport=args.transport, rank=rank)
+        bufs_by_nq = {}
+
+        def dev_fn(nprobe):
+            def f(qp, nq, d, i, c, s):
+                b = bufs_by_nq.setdefault(nq, sharded.buffers(nq, kout))
+                return sharded.search_device(ws, qp, nq, args.k, nprobe, metric, b, s)
+            return f
+
+        def host_fn(nprobe):
+            return None
+
+        def barrier():
+            dist.barrier()
+            torch.cuda.synchronize()
+    elif args.workload == "ivf":
         part = art["partition"]
         index = part
 
@@ -828,7 +883,7 @@ def run_index(args, torch, mb, lib, world, rank, dist):
         try:
             q = q_all[:nq]
             r = measure_index(torch, ws, dev_fn(nprobe), host_fn(nprobe), q, kout, steps, warmup,
-                              with_clocks)
+                              with_clocks, barrier=barrier)
             r["nprobe"] = nprobe
             r["roofline"] = index_roofline(args, r, probed_list_rows(args, art, q))
             r["workload"] = index_workload_config(args, nq, nprobe)["workload"]
@@ -847,10 +902,11 @@ def run_index(args, torch, mb, lib, world, rank, dist):
         res = main_res
         line = {
             "metric": "queries_per_sec",
-            "value": world * args.nq * args.steps / (res["total_ms"] * 1e-3),
+            "value": (1 if ivf_sharded else world) * args.nq * args.steps / (res["total_ms"] * 1e-3),
             "unit": "queries/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": res["total_ms"] / args.steps, "p50_us": 1e3 * res["p50_ms"],
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if ivf_sharded else "weak",
+            "vs_baseline": None,
             "dtype": "f32" if args.workload == "ivf" else "f32 (u8 codes)",
             "data": f"synthetic (numpy default_rng(0) {args.components}-component Gaussian "
                     f"mixture, sigma 0.3, L2-normalised); index trained with torch "
@@ -886,6 +942,9 @@ def run_index(args, torch, mb, lib, world, rank, dist):
                              else "_IVFPQIndex.search restated (coarse BoundedSortedList, "
                                   "sequential ADC, newest-first merge)")}
         print(json.dumps(line), flush=True)
+    if ivf_sharded:
+        barrier()  # every rank is done with the peers' buffers
+        sharded.close()
     ws.close()
     index.close()
     if "corpus" in art:

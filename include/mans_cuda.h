@@ -294,8 +294,9 @@ int32_t mans_ivf_assign(mans_ctx *ctx, mans_corpus *corpus, const float *centroi
  * 559-631): assignment as mans_ivf_assign, list sizes, offsets, list ids in
  * ascending row order per list, packed rows and norms -- all on the device,
  * from a corpus already uploaded; the result equals mans_ivf_create on the
- * host-built layout.  Centroid training (KMeans.cluster, seeded by Swift's
- * generator) stays with the caller. */
+ * host-built layout.  The list ids carry the corpus's id_offset, so a row
+ * shard's partition reports global ids.  Centroid training (KMeans.cluster,
+ * seeded by Swift's generator) stays with the caller. */
 int32_t mans_ivf_build(mans_ctx *ctx, mans_corpus *corpus, const float *centroids,
                        int32_t nlist, int32_t metric, mans_ivf **out_ivf);
 /* Host copy of the partition layout: offsets (nlist + 1) and list ids (n);

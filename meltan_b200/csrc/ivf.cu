@@ -590,10 +590,13 @@ __global__ void list_offsets_kernel(const int64_t* __restrict__ counts, int32_t 
 // packed[p] = rows[list_ids[p]], one warp per packed row
 __global__ void gather_rows_kernel(const float* __restrict__ rows, int64_t ld,
                                    const uint32_t* __restrict__ ids, int64_t n, int32_t dim,
-                                   float* __restrict__ packed) {
+                                   float* __restrict__ packed, uint32_t* __restrict__ out_ids,
+                                   uint32_t id_offset) {
   const int64_t p = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (p >= n) return;
+  // reported ids: the corpus's own (a row shard's rows carry its first row)
+  if (lane == 0) out_ids[p] = ids[p] + id_offset;
   const float* src = rows + static_cast<int64_t>(ids[p]) * ld;
   float* dst = packed + p * dim;
   for (int c = lane; c < dim; c += 32) dst[c] = src[c];
@@ -739,14 +742,15 @@ int32_t mans_ivf_build(mans_ctx* ctx, mans_corpus* corpus, const float* centroid
   // 4. packed rows in list order
   if (rc == MANS_OK && n > 0) {
     gather_rows_kernel<<<static_cast<unsigned>((n * 32 + 255) / 256), 256>>>(
-        corpus->rows, corpus->ld, d_ids, n, static_cast<int32_t>(dim), d_packed);
+        corpus->rows, corpus->ld, d_ids, n, static_cast<int32_t>(dim), d_packed, d_keys,
+        corpus->id_offset);
     ck(cudaGetLastError(), "gather rows");
   }
   if (rc == MANS_OK) ck(cudaDeviceSynchronize(), "partition build");
   if (rc == MANS_OK) rc = corpus_upload(ctx, d_packed, n, dim, 0, &ivf->packed);
   if (rc == MANS_OK) {
-    ivf->packed->ids = d_ids;  // owned by the packed corpus from here on
-    d_ids = nullptr;
+    ivf->packed->ids = d_keys;  // (global) ids, owned by the packed corpus from here on
+    d_keys = nullptr;
     ivf->h_offsets.resize(nlist + 1);
     ck(cudaMemcpy(ivf->h_offsets.data(), ivf->offsets, (nlist + 1) * sizeof(int64_t),
                   cudaMemcpyDeviceToHost),
@@ -757,9 +761,9 @@ int32_t mans_ivf_build(mans_ctx* ctx, mans_corpus* corpus, const float* centroid
       ivf->max_len = std::max(ivf->max_len, ivf->h_offsets[l + 1] - ivf->h_offsets[l]);
   }
   cudaFree(d_assign);
-  cudaFree(d_keys);
+  if (d_keys) cudaFree(d_keys);
   cudaFree(d_iota);
-  if (d_ids) cudaFree(d_ids);
+  cudaFree(d_ids);
   cudaFree(d_counts);
   cudaFree(d_packed);
   if (d_tmp) cudaFree(d_tmp);

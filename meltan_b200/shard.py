@@ -20,7 +20,7 @@ from . import core
 from ._lib import lib
 
 __all__ = ["row_shard", "packed_words", "block_views", "all_gather_blocks", "PeerExchange",
-           "ShardedFlatSearch"]
+           "ShardedFlatSearch", "ShardedIVFSearch"]
 
 
 def row_shard(n: int, world: int, rank: int) -> tuple[int, int]:
@@ -96,15 +96,11 @@ class PeerExchange:
             self._h = None
 
 
-class ShardedFlatSearch:
-    """Exact flat search over a row-sharded corpus: this rank's shard is a
-    ``VectorBuffer`` created with ``id_offset`` = its first global row.  The
-    per-rank blocks move by peer-memory exchange (``transport="p2p"``) or by
-    one NCCL all-gather (``"nccl"``)."""
+class _ShardedSearch:
+    """Per-rank packed block -> every rank's block -> merged top-k."""
 
-    def __init__(self, ctx, shard: "core.VectorBuffer", world: int, dist=None,
-                 transport: str = "nccl", rank: int = 0):
-        self.ctx, self.shard, self.world, self.dist = ctx, shard, world, dist
+    def __init__(self, ctx, world: int, dist=None, transport: str = "nccl", rank: int = 0):
+        self.ctx, self.world, self.dist = ctx, world, dist
         self.transport = transport if world > 1 else "none"
         self.rank = rank
         self._ex = {}
@@ -114,11 +110,6 @@ class ShardedFlatSearch:
         if ex is None:
             ex = self._ex[words] = PeerExchange(self.ctx, self.world, self.rank, words, self.dist)
         return ex
-
-    def close(self):
-        for ex in self._ex.values():
-            ex.close()
-        self._ex = {}
 
     def buffers(self, nq: int, kout: int):
         """(local block, gathered blocks, merged block) device tensors."""
@@ -130,16 +121,12 @@ class ShardedFlatSearch:
         out = torch.empty((P,), dtype=torch.int32, device="cuda")
         return loc, gat, out
 
-    def search_device(self, ws, d_queries: int, nq: int, k: int, metric, bufs,
-                      stream: int = 0):
-        """Search this rank's shard, gather every rank's block and merge;
-        returns the merged packed block (identical on every rank)."""
+    def _local_target(self, bufs):
+        loc, _, out = bufs
+        return loc if self.world > 1 else out
+
+    def _gather_merge(self, ws, bufs, nq: int, kout: int, k: int, stream: int):
         loc, gat, out = bufs
-        kout = min(k, core.MAX_TOP_K)
-        target = loc if self.world > 1 else out
-        core.FlatGPUSearch.search_device(self.ctx, self.shard, ws, d_queries, nq, k, metric,
-                                         target.data_ptr(), target[nq * kout:].data_ptr(),
-                                         target[2 * nq * kout:].data_ptr(), stream)
         if self.world == 1:
             return out
         if self.transport == "p2p":
@@ -154,3 +141,54 @@ class ShardedFlatSearch:
                                out[2 * nq * kout:].data_ptr(), stream,
                                list_stride=packed_words(nq, kout))
         return out
+
+    def close(self):
+        for ex in self._ex.values():
+            ex.close()
+        self._ex = {}
+
+
+class ShardedFlatSearch(_ShardedSearch):
+    """Exact flat search over a row-sharded corpus: this rank's shard is a
+    ``VectorBuffer`` created with ``id_offset`` = its first global row.  The
+    per-rank blocks move by peer-memory exchange (``transport="p2p"``) or by
+    one NCCL all-gather (``"nccl"``)."""
+
+    def __init__(self, ctx, shard: "core.VectorBuffer", world: int, dist=None,
+                 transport: str = "nccl", rank: int = 0):
+        super().__init__(ctx, world, dist, transport, rank)
+        self.shard = shard
+
+    def search_device(self, ws, d_queries: int, nq: int, k: int, metric, bufs,
+                      stream: int = 0):
+        """Search this rank's shard, gather every rank's block and merge;
+        returns the merged packed block (identical on every rank)."""
+        kout = min(k, core.MAX_TOP_K)
+        t = self._local_target(bufs)
+        core.FlatGPUSearch.search_device(self.ctx, self.shard, ws, d_queries, nq, k, metric,
+                                         t.data_ptr(), t[nq * kout:].data_ptr(),
+                                         t[2 * nq * kout:].data_ptr(), stream)
+        return self._gather_merge(ws, bufs, nq, kout, k, stream)
+
+
+class ShardedIVFSearch(_ShardedSearch):
+    """IVF-flat over row shards: every rank holds the partition of its rows
+    under the same centroids (``Partition.build`` on a shard ``VectorBuffer``
+    reports global ids), so every rank probes the same lists; the per-rank
+    top-k blocks merge by (distance, id) into the unsharded result."""
+
+    def __init__(self, ctx, partition, world: int, dist=None, transport: str = "nccl",
+                 rank: int = 0):
+        super().__init__(ctx, world, dist, transport, rank)
+        self.partition = partition
+
+    def search_device(self, ws, d_queries: int, nq: int, k: int, nprobe: int, metric, bufs,
+                      stream: int = 0):
+        from .ivf import IVFFlatSearch
+
+        kout = min(k, core.MAX_TOP_K)
+        t = self._local_target(bufs)
+        IVFFlatSearch.search_device(self.ctx, self.partition, ws, d_queries, nq, k, nprobe,
+                                    metric, t.data_ptr(), t[nq * kout:].data_ptr(),
+                                    t[2 * nq * kout:].data_ptr(), stream)
+        return self._gather_merge(ws, bufs, nq, kout, k, stream)

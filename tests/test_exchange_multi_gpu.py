@@ -80,3 +80,74 @@ def test_two_gpu_peer_exchange_equals_unsharded(tmp_path):
             np.testing.assert_array_equal(c.numpy(), want[2])
             np.testing.assert_array_equal(i.numpy().view(np.uint32), want[1])
             np.testing.assert_array_equal(d.numpy(), want[0])
+
+
+def _ivf_worker(rank, world, port, out_dir):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import bench
+    import meltan_b200 as mb
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        v, q = bench.make_mixture(40000, 48, 30, 9, seed=21)
+        cent = v[::1000][:30].copy()
+        ctx = mb.Context(rank)
+        r0, r1 = mb.row_shard(len(v), world, rank)
+        buf = mb.VectorBuffer(ctx, v[r0:r1], id_offset=r0)
+        part = mb.Partition.build(ctx, buf, cent, mb.Metric.cosine)
+        ws = mb.Workspace(ctx)
+        sh = mb.ShardedIVFSearch(ctx, part, world, dist, transport="p2p", rank=rank)
+        bufs = sh.buffers(len(q), 10)
+        dq = torch.from_numpy(q).cuda()
+        res = []
+        for nprobe in (1, 4, 30):
+            out = sh.search_device(ws, dq.data_ptr(), len(q), 10, nprobe, mb.Metric.cosine, bufs)
+            ws.check()
+            res.append(out.cpu().numpy().copy())
+        torch.cuda.synchronize()
+        dist.barrier()
+        sh.close()
+        np.save(os.path.join(out_dir, f"ivf{rank}.npy"), np.stack(res))
+        part.close()
+        ws.close()
+        buf.close()
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gpu_sharded_ivf_equals_unsharded(tmp_path):
+    """IVF-flat over row shards (each rank's partition of its rows under the
+    same centroids, global ids) merged over peer memory equals the oracle's
+    scanProbedLists on the whole corpus."""
+    import torch
+    import torch.multiprocessing as mp
+
+    import bench
+    import oracle as O
+    from meltan_b200 import shard
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.start_processes(_ivf_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    v, q = bench.make_mixture(40000, 48, 30, 9, seed=21)
+    cent = v[::1000][:30].copy()
+    off, ids, packed, pn = O.ivf_layout(v, O.ivf_assign(v, cent, O.COSINE), len(cent))
+    for rank in range(2):
+        res = np.load(tmp_path / f"ivf{rank}.npy")
+        for blk, nprobe in zip(res, (1, 4, 30)):
+            want = O.ivf_search(cent, packed, pn, ids, off, q, 10, nprobe, O.COSINE)
+            d, i, c = shard.block_views(torch.from_numpy(blk), len(q), 10)
+            np.testing.assert_array_equal(c.numpy(), want[2])
+            np.testing.assert_array_equal(i.numpy().view(np.uint32), want[1])
+            np.testing.assert_array_equal(d.numpy(), want[0])
