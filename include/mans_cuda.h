@@ -360,6 +360,24 @@ int32_t mans_ivfpq_search_device(mans_ctx *ctx, mans_ivfpq *ix, mans_workspace *
                                  float *d_out_dist, uint32_t *d_out_ids, int32_t *d_out_counts,
                                  void *cuda_stream);
 
+/* Row shards of one IVF-PQ index (one process per GPU; every shard holds the
+ * same coarse centroids and codebooks, its rows' codes, and for each list
+ * entry its position in the global list, `list_positions` of
+ * mans_ivfpq_create).  Each shard writes a packed block of nq*(3*kin + 1)
+ * int32 words, kin = 2*min(k, 256): [scores | sequences | internal ids |
+ * counts], its (score, insertion sequence) 2k-smallest candidates; after an
+ * all-gather, mans_ivfpq_resolve_device merges the blocks (block r at
+ * d_blocks + r*block_stride words) and applies the BoundedSortedList outcome
+ * (BoundedSelection.swift:158-214) -- the same result as the unsharded
+ * search, newest-first ties included.  No reference counterpart (one GPU). */
+int32_t mans_ivfpq_search_partial_device(mans_ctx *ctx, mans_ivfpq *ix, mans_workspace *ws,
+                                         const float *d_queries, int64_t nq, int32_t k,
+                                         int32_t nprobe, int32_t *d_block, void *cuda_stream);
+int32_t mans_ivfpq_resolve_device(mans_ctx *ctx, mans_workspace *ws, const int32_t *d_blocks,
+                                  int32_t n_blocks, int64_t block_stride, int64_t nq, int32_t k,
+                                  float *d_out_dist, uint32_t *d_out_ids, int32_t *d_out_counts,
+                                  void *cuda_stream);
+
 /* GPUADCSearch.computeDistances(context:query:pq:packedCodes:vectorCount:
  * flatCodebooks:) (GPUADCSearch.swift:35-173): squared-L2 LUT of `query`
  * against the codebooks (pq_compute_distance_table) and the sequential sum

@@ -76,6 +76,10 @@ SIGNATURES = {
                                       _VP, _VP, _VP]),
     "mans_ivfpq_search_device": (C.c_int32, [_VP, _VP, _VP, _VP, C.c_int64, C.c_int32, C.c_int32,
                                              _VP, _VP, _VP, _VP]),
+    "mans_ivfpq_search_partial_device": (C.c_int32, [_VP, _VP, _VP, _VP, C.c_int64, C.c_int32,
+                                                     C.c_int32, _VP, _VP]),
+    "mans_ivfpq_resolve_device": (C.c_int32, [_VP, _VP, _VP, C.c_int32, C.c_int64, C.c_int64,
+                                              C.c_int32, _VP, _VP, _VP, _VP]),
     "mans_pq_adc_list": (C.c_int32, [_VP, _VP, C.c_int64, _VP, C.c_int32, C.c_int32, _VP,
                                      C.c_int64, _VP]),
 }

@@ -320,16 +320,130 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_list_kernel(
 
 }  // namespace
 
+namespace {
+
+// Shard output of the IVF-PQ search: the (score, seq) 2k-lists of the merge
+// step with each entry's internal id.  seq = probe rank << 20 | the entry's
+// position in its global list; a shard's list holds a subset of the global
+// entries with their global positions (`pos`, ascending), found by binary
+// search.
+__global__ void ivfpq_payload_kernel(int64_t nq, int32_t kin, const float* __restrict__ md,
+                                     const uint32_t* __restrict__ mi,
+                                     const int32_t* __restrict__ mc,
+                                     const uint32_t* __restrict__ probe_lists, int32_t probe,
+                                     const int64_t* __restrict__ offsets,
+                                     const uint32_t* __restrict__ ids,
+                                     const uint32_t* __restrict__ pos, float* out_score,
+                                     uint32_t* out_seq, uint32_t* out_id, int32_t* out_count) {
+  const int64_t q = blockIdx.x;
+  const int cnt = mc[q];
+  for (int i = threadIdx.x; i < kin; i += blockDim.x) {
+    const int64_t at = q * kin + i;
+    if (i < cnt) {
+      const uint32_t seq = mi[at];
+      const uint32_t rank = seq >> kPosBits, gpos = seq & ((1u << kPosBits) - 1u);
+      const uint32_t list = probe_lists[q * probe + rank];
+      const int64_t off = offsets[list], len = offsets[list + 1] - off;
+      int64_t idx = gpos;
+      if (pos) {
+        int64_t lo = 0, hi = len;
+        while (lo < hi) {
+          const int64_t mid = (lo + hi) >> 1;
+          if (pos[off + mid] < gpos) lo = mid + 1;
+          else hi = mid;
+        }
+        idx = lo;
+      }
+      out_score[at] = md[at];
+      out_seq[at] = seq;
+      out_id[at] = ids[off + idx];
+    } else {
+      out_score[at] = __int_as_float(0x7F800000);
+      out_seq[at] = 0xFFFFFFFFu;
+      out_id[at] = kEmptyId;
+    }
+  }
+  if (threadIdx.x == 0) out_count[q] = cnt;
+}
+
+// Per query: the (score, seq) smallest kin entries over the shard blocks
+// (block r at blocks + r * stride words: score | seq | id | count), with
+// their ids.  Sequences are unique per query (each global entry lives in
+// one shard), so (score, seq) orders them totally.
+__global__ void __launch_bounds__(256) ivfpq_shard_merge_kernel(
+    const int32_t* __restrict__ blocks, int32_t n_blocks, int64_t stride, int64_t nq, int32_t kin,
+    float* m_score, uint32_t* m_seq, uint32_t* m_id, int32_t* m_count) {
+  extern __shared__ uint64_t mk[];  // n2 keys, then n2 ids (uint32)
+  const int64_t q = blockIdx.x;
+  int n2 = 1;
+  while (n2 < n_blocks * kin) n2 <<= 1;
+  uint32_t* mv = reinterpret_cast<uint32_t*>(mk + n2);
+  for (int i = threadIdx.x; i < n2; i += blockDim.x) {
+    const int r = i / kin, j = i - r * kin;
+    uint64_t key = kKeyMax;
+    uint32_t id = kEmptyId;
+    if (r < n_blocks) {
+      const int32_t* b = blocks + r * stride;
+      const int32_t cnt = b[3 * nq * kin + q];
+      if (j < cnt) {
+        const float sc = __int_as_float(b[q * kin + j]);
+        const uint32_t seq = static_cast<uint32_t>(b[nq * kin + q * kin + j]);
+        key = (static_cast<uint64_t>(float_to_ordered(sc)) << 32) | seq;
+        id = static_cast<uint32_t>(b[2 * nq * kin + q * kin + j]);
+      }
+    }
+    mk[i] = key;
+    mv[i] = id;
+  }
+  __syncthreads();
+  for (int a = 2; a <= n2; a <<= 1) {
+    for (int jj = a >> 1; jj > 0; jj >>= 1) {
+      for (int i = threadIdx.x; i < n2; i += blockDim.x) {
+        const int ixj = i ^ jj;
+        if (ixj > i) {
+          const uint64_t x = mk[i], y = mk[ixj];
+          const bool up = (i & a) == 0;
+          if ((x > y) == up) {
+            mk[i] = y;
+            mk[ixj] = x;
+            const uint32_t t = mv[i];
+            mv[i] = mv[ixj];
+            mv[ixj] = t;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  __shared__ int valid;
+  if (threadIdx.x == 0) valid = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < kin; i += blockDim.x) {
+    const uint64_t key = mk[i];
+    const bool ok = key != kKeyMax;
+    m_score[q * kin + i] = ok ? ordered_to_float(static_cast<uint32_t>(key >> 32)) : __int_as_float(0x7F800000);
+    m_seq[q * kin + i] = ok ? static_cast<uint32_t>(key) : 0xFFFFFFFFu;
+    m_id[q * kin + i] = ok ? mv[i] : kEmptyId;
+    if (ok) atomicAdd(&valid, 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) m_count[q] = valid;
+}
+
+}  // namespace
+
 static size_t carve(size_t& o, size_t bytes) {
   size_t at = (o + 255) / 256 * 256;
   o = at + bytes;
   return at;
 }
 
+// partial: null, or this shard's block [score | seq | id | count] (2k
+// entries per query) instead of the resolved top-k (the row-sharded search)
 static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* ws,
                                 const float* d_queries, int64_t nq, int32_t k, int32_t nprobe,
                                 float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
-                                cudaStream_t stream) {
+                                cudaStream_t stream, int32_t* partial = nullptr) {
   const int32_t kout = std::min<int32_t>(k, MANS_MAX_TOPK);
   if (nq <= 0) return MANS_OK;
   if (k <= 0 || ix->n <= 0 || ix->nlist <= 0) {
@@ -460,6 +574,18 @@ static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* w
   e = launch_merge(m, stream);
   if (e != cudaSuccess) return fail_cuda(e, "adc merge launch");
 
+  if (partial) {
+    float* ps_ = reinterpret_cast<float*>(partial);
+    uint32_t* pq_ = reinterpret_cast<uint32_t*>(partial) + nq * k2;
+    uint32_t* pi_ = reinterpret_cast<uint32_t*>(partial) + 2 * nq * k2;
+    int32_t* pc_ = partial + 3 * nq * k2;
+    ivfpq_payload_kernel<<<static_cast<unsigned>(nq), 128, 0, stream>>>(
+        nq, k2, md, mi, mc, pl, probe, ix->offsets, ix->ids, ix->pos, ps_, pq_, pi_, pc_);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_cuda(e, "payload launch");
+    ws->launches += 4;
+    return MANS_OK;
+  }
   // 4. BoundedSortedList(capacity k) outcome, seq -> internal id
   ResolveParams f{};
   f.in_score = md;
@@ -594,6 +720,78 @@ int32_t mans_ivfpq_search_device(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* 
   DeviceGuard g(ctx->device);
   return run_ivfpq_search(ctx, ix, ws, d_queries, nq, k, nprobe, d_out_dist, d_out_ids,
                           d_out_counts, static_cast<cudaStream_t>(cuda_stream));
+}
+
+int32_t mans_ivfpq_search_partial_device(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* ws,
+                                         const float* d_queries, int64_t nq, int32_t k,
+                                         int32_t nprobe, int32_t* d_block, void* cuda_stream) {
+  if (!ctx || !ix || ix->ctx != ctx) return fail(MANS_ERR_INVALID, "null or foreign IVF-PQ index");
+  if (!ws || ws->ctx != ctx) return fail(MANS_ERR_INVALID, "workspace missing or foreign");
+  if (nq < 0 || k <= 0 || !d_block) return fail(MANS_ERR_INVALID, "bad partial search request");
+  if (nq == 0) return MANS_OK;
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+  const int64_t kin = 2 * std::min<int32_t>(k, MANS_MAX_TOPK);
+  if (ix->n <= 0 || ix->nlist <= 0) {  // an empty shard contributes nothing
+    cudaError_t e = cudaMemsetAsync(d_block + 3 * nq * kin, 0, nq * sizeof(int32_t), st);
+    return e == cudaSuccess ? MANS_OK : fail_cuda(e, "cudaMemsetAsync");
+  }
+  return run_ivfpq_search(ctx, ix, ws, d_queries, nq, k, nprobe, nullptr, nullptr, nullptr, st,
+                          d_block);
+}
+
+int32_t mans_ivfpq_resolve_device(mans_ctx* ctx, mans_workspace* ws, const int32_t* d_blocks,
+                                  int32_t n_blocks, int64_t block_stride, int64_t nq, int32_t k,
+                                  float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
+                                  void* cuda_stream) {
+  if (!ctx || !ws || ws->ctx != ctx) return fail(MANS_ERR_INVALID, "null context or workspace");
+  if (nq < 0 || k <= 0 || n_blocks < 1 || !d_blocks) return fail(MANS_ERR_INVALID, "bad resolve request");
+  if (nq == 0) return MANS_OK;
+  const int32_t kout = std::min<int32_t>(k, MANS_MAX_TOPK);
+  const int64_t kin = 2 * kout;
+  if (block_stride < nq * (3 * kin + 1)) return fail(MANS_ERR_INVALID, "block stride too small");
+  int n2 = 1;
+  while (n2 < n_blocks * kin) n2 <<= 1;
+  const size_t smem = static_cast<size_t>(n2) * (sizeof(uint64_t) + sizeof(uint32_t));
+  if (smem > static_cast<size_t>(ctx->max_smem) - 1024)
+    return fail(MANS_ERR_SEARCH, "too many shards x candidates to merge in shared memory");
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+  size_t o = 0;
+  const size_t o_s = carve(o, nq * kin * sizeof(float));
+  const size_t o_q = carve(o, nq * kin * sizeof(uint32_t));
+  const size_t o_i = carve(o, nq * kin * sizeof(uint32_t));
+  const size_t o_c = carve(o, nq * sizeof(int32_t));
+  int32_t rc;
+  if ((rc = ws->aux2.reserve(o)) != MANS_OK) return rc;
+  uint8_t* A = static_cast<uint8_t*>(ws->aux2.ptr);
+  float* ms = reinterpret_cast<float*>(A + o_s);
+  uint32_t* mq = reinterpret_cast<uint32_t*>(A + o_q);
+  uint32_t* mi = reinterpret_cast<uint32_t*>(A + o_i);
+  int32_t* mc = reinterpret_cast<int32_t*>(A + o_c);
+  cudaError_t e = cudaFuncSetAttribute(ivfpq_shard_merge_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return fail_cuda(e, "shard merge configure");
+  ivfpq_shard_merge_kernel<<<static_cast<unsigned>(nq), 256, smem, st>>>(
+      d_blocks, n_blocks, block_stride, nq, static_cast<int32_t>(kin), ms, mq, mi, mc);
+  if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "shard merge launch");
+  ResolveParams f{};
+  f.in_score = ms;
+  f.in_seq = mq;
+  f.in_payload = mi;
+  f.in_count = mc;
+  f.kin = static_cast<int32_t>(kin);
+  f.nq = nq;
+  f.cap = kout;
+  f.out_score = d_out_dist;
+  f.out_id = d_out_ids;
+  f.out_count = d_out_counts;
+  f.kout = kout;
+  bsl_resolve_kernel<<<static_cast<unsigned>(nq), 256, 0, st>>>(f);
+  if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "resolve launch");
+  ws->launches += 2;
+  return MANS_OK;
 }
 
 int32_t mans_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, const float* queries, int64_t nq,

@@ -84,6 +84,27 @@ class IVFPQIndex:
                                              C.c_void_p(d_out_dist), C.c_void_p(d_out_ids),
                                              C.c_void_p(d_out_counts), C.c_void_p(stream)))
 
+    def search_partial_device(self, ws: Workspace, d_queries: int, nq: int, k: int, nprobe: int,
+                              d_block: int, stream: int = 0):
+        """This shard's packed block [scores | seqs | ids | counts] (2k entries
+        per query) for mans_ivfpq_resolve_device."""
+        check(lib().mans_ivfpq_search_partial_device(
+            self.context.handle, self._h, ws.handle, C.c_void_p(d_queries), nq, k, nprobe,
+            C.c_void_p(d_block), C.c_void_p(stream)))
+
+    @staticmethod
+    def shard_lists(offsets, flat, r0: int, r1: int):
+        """The inverted lists of the row shard [r0, r1) of a global index:
+        (offsets, ids, positions in the global lists), insertion order kept."""
+        offsets = np.asarray(offsets, np.int64)
+        flat = np.asarray(flat, np.uint32)
+        keep = (flat >= r0) & (flat < r1)
+        lists = np.repeat(np.arange(len(offsets) - 1), np.diff(offsets))
+        pos = np.arange(len(flat), dtype=np.int64) - offsets[lists]
+        sizes = np.bincount(lists[keep], minlength=len(offsets) - 1)
+        soff = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+        return soff, flat[keep], pos[keep].astype(np.uint32)
+
     def close(self):
         if self._h:
             lib().mans_ivfpq_destroy(self._h)
@@ -94,6 +115,22 @@ class IVFPQIndex:
             self.close()
         except Exception:
             pass
+
+
+def partial_words(nq: int, k: int) -> int:
+    """int32 words of one shard's IVF-PQ block."""
+    kin = 2 * min(k, MAX_TOP_K)
+    return nq * (3 * kin + 1)
+
+
+def resolve_device(context: Context, ws: Workspace, d_blocks: int, n_blocks: int,
+                   block_stride: int, nq: int, k: int, d_out_dist: int, d_out_ids: int,
+                   d_out_counts: int, stream: int = 0):
+    """Merge the shards' blocks and apply the BoundedSortedList outcome."""
+    check(lib().mans_ivfpq_resolve_device(context.handle, ws.handle, C.c_void_p(d_blocks),
+                                          n_blocks, block_stride, nq, k, C.c_void_p(d_out_dist),
+                                          C.c_void_p(d_out_ids), C.c_void_p(d_out_counts),
+                                          C.c_void_p(stream)))
 
 
 def encode(context: Context, vectors, coarse, codebooks, metric: Metric = Metric.l2):

@@ -156,3 +156,50 @@ def test_gpu_encode_small_codebooks_and_scalar_subspaces(ctx):
         a = O.nearest_coarse(v[i], coarse, O.L2)
         assert assign[i] == a
         np.testing.assert_array_equal(codes[i], O.pq_encode_subtracting(v[i], coarse[a], cb))
+
+
+@pytest.mark.parametrize("shards", [2, 3])
+def test_row_sharded_ivfpq_equals_unsharded(ctx, shards):
+    """IVF-PQ over row shards (each with its rows' list entries and their
+    global list positions): the shards' (score, sequence) 2k-blocks, merged
+    and resolved, equal the oracle's _IVFPQIndex.search on the whole index --
+    ties included (duplicate codes make equal scores that newest-first
+    ordering decides)."""
+    import torch
+    from meltan_b200 import pq as mpq
+    rng = np.random.default_rng(33)
+    n, dim, m, nlist = 6000, 32, 8, 24
+    v = rng.standard_normal((n, dim), dtype=np.float32)
+    coarse = v[rng.choice(n, nlist, replace=False)].copy()
+    cb = rng.standard_normal((m, 256, dim // m), dtype=np.float32)
+    codes, assign = mb.pq_encode(ctx, v, coarse, cb)
+    codes[4000:4100] = codes[10]  # equal scores across shards
+    flat = np.argsort(assign, kind="stable").astype(np.uint32)
+    off = np.concatenate([[0], np.cumsum(np.bincount(assign, minlength=nlist))]).astype(np.int64)
+    q = rng.standard_normal((7, dim), dtype=np.float32)
+    ws = mb.Workspace(ctx)
+    dq = torch.from_numpy(q).cuda()
+    for k, nprobe in ((10, 4), (25, 24)):
+        words = mpq.partial_words(len(q), k)
+        blocks = torch.empty((shards, words), dtype=torch.int32, device="cuda")
+        idx = []
+        for s_ in range(shards):
+            r0, r1 = mb.row_shard(n, shards, s_)
+            soff, sflat, spos = mb.IVFPQIndex.shard_lists(off, flat, r0, r1)
+            ix = mb.IVFPQIndex(ctx, coarse, cb, codes, (soff, sflat), list_positions=spos)
+            ix.search_partial_device(ws, dq.data_ptr(), len(q), k, nprobe, blocks[s_].data_ptr())
+            idx.append(ix)
+        kout = min(k, 256)
+        od = torch.empty((len(q), kout), dtype=torch.float32, device="cuda")
+        oi = torch.empty((len(q), kout), dtype=torch.int32, device="cuda")
+        oc = torch.empty((len(q),), dtype=torch.int32, device="cuda")
+        mpq.resolve_device(ctx, ws, blocks.data_ptr(), shards, words, len(q), k, od.data_ptr(),
+                           oi.data_ptr(), oc.data_ptr())
+        ws.check()
+        want = O.ivfpq_search(coarse, cb, codes, off, flat, q, k, nprobe, O.L2)
+        np.testing.assert_array_equal(oc.cpu().numpy(), want[2])
+        np.testing.assert_array_equal(oi.cpu().numpy().view(np.uint32), want[1])
+        np.testing.assert_array_equal(od.cpu().numpy(), want[0])
+        for ix in idx:
+            ix.close()
+    ws.close()
