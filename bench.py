@@ -589,8 +589,7 @@ def index_workload_config(args, nq=None, nprobe=None):
     cfg = {"workload": name, "n": args.n, "dim": args.dim, "nq": nq, "k": args.k,
            "metric": args.metric, "nlist": args.nlist, "nprobe": nprobe,
            "components": args.components,
-           "parallelism": (f"rowshard{args.gpus}" if args.workload == "ivf" and args.gpus > 1
-                           else f"replica{args.gpus}"),
+           "parallelism": f"rowshard{args.gpus}",
            "l2": "probed lists differ per query; each step streams its lists once "
                  "(no flush; lists of one batch may hit L2)"}
     if args.workload == "ivfpq":
@@ -627,6 +626,35 @@ def build_index_data(args, nq_max, device=None, mb=None, ctx=None, shard=None, d
     if mb is not None:
         coarse = train_centroids(v, args.nlist, seed=42)
         cb = train_pq_codebooks(v, coarse, args.pq_m)
+        if dist is not None:  # one coarse quantiser and codebook set for every shard
+            import torch
+            ct, bt = torch.from_numpy(coarse).cuda(), torch.from_numpy(cb).cuda()
+            dist.broadcast(ct, 0)
+            dist.broadcast(bt, 0)
+            coarse, cb = ct.cpu().numpy(), bt.cpu().numpy()
+        if shard is not None:
+            # this rank's rows; list entries carry their positions in the
+            # global lists (earlier shards' entries of a list come first)
+            import torch
+            r0, r1 = shard
+            t0 = time.perf_counter()
+            scodes, sassign = mb.pq_encode(ctx, v[r0:r1], coarse, cb, mb.Metric(metric))
+            gpu_s = time.perf_counter() - t0
+            cnt = torch.from_numpy(np.bincount(sassign, minlength=args.nlist)).cuda()
+            allc = [torch.empty_like(cnt) for _ in range(dist.get_world_size())]
+            dist.all_gather(allc, cnt)
+            before = sum(c.cpu().numpy() for c in allc[:dist.get_rank()]) if dist.get_rank() else \
+                np.zeros(args.nlist, np.int64)
+            order = np.argsort(sassign, kind="stable")
+            soff = np.concatenate([[0], np.cumsum(np.bincount(sassign, minlength=args.nlist))])
+            lists_of = np.repeat(np.arange(args.nlist), np.diff(soff))
+            spos = (before[lists_of] + np.arange(len(order)) - soff[lists_of]).astype(np.uint32)
+            codes = np.zeros((v.shape[0], args.pq_m), np.uint8)
+            codes[r0:r1] = scodes
+            return v, q, {"coarse": coarse, "codebooks": cb, "codes": codes,
+                          "offsets": soff.astype(np.int64), "lists": (order + r0).astype(np.uint32),
+                          "positions": spos, "build_gpu_s": gpu_s,
+                          "build_gpu": "mans_pq_encode of this rank's rows"}
         t0 = time.perf_counter()
         codes, assign = mb.pq_encode(ctx, v, coarse, cb, mb.Metric(metric))
         gpu_s = time.perf_counter() - t0
@@ -822,9 +850,10 @@ def run_index(args, torch, mb, lib, world, rank, dist):
     nq_max = max([args.nq] + [x for x, _ in extra])
     t_build = time.perf_counter()
     ctx = mb.Context(torch.cuda.current_device())
-    # IVF-flat shards its rows over the ranks (same centroids, global ids,
-    # per-rank blocks exchanged and merged); IVF-PQ runs replicas
-    ivf_sharded = args.workload == "ivf" and world > 1
+    # N > 1: both index kinds shard their rows over the ranks (shared
+    # centroids / codebooks, global ids or list positions, per-rank blocks
+    # gathered and merged into the unsharded result)
+    ivf_sharded = world > 1
     shard = mb.row_shard(args.n, world, rank) if ivf_sharded else None
     v, q_all, art = build_index_data(args, nq_max, mb=mb, ctx=ctx, shard=shard,
                                      dist=dist if ivf_sharded else None)
@@ -832,7 +861,27 @@ def run_index(args, torch, mb, lib, world, rank, dist):
     L = lib
     kout = min(args.k, mb.MAX_TOP_K)
     barrier = None
-    if ivf_sharded:
+    if ivf_sharded and args.workload == "ivfpq":
+        ix = mb.IVFPQIndex(ctx, art["coarse"], art["codebooks"], art["codes"],
+                           (art["offsets"], art["lists"]), metric=mb.Metric(metric),
+                           list_positions=art["positions"])
+        index = ix
+        sharded = mb.ShardedIVFPQSearch(ctx, ix, world, dist)
+        bufs_by_nq = {}
+
+        def dev_fn(nprobe):
+            def f(qp, nq, d, i, c, s):
+                b = bufs_by_nq.setdefault(nq, sharded.buffers(nq, args.k))
+                return sharded.search_device(ws, qp, nq, args.k, nprobe, b, s)
+            return f
+
+        def host_fn(nprobe):
+            return None
+
+        def barrier():
+            dist.barrier()
+            torch.cuda.synchronize()
+    elif ivf_sharded:
         part = art["partition"]
         index = part
         sharded = mb.ShardedIVFSearch(ctx, part, world, dist, transport=args.transport, rank=rank)

@@ -20,7 +20,7 @@ from . import core
 from ._lib import lib
 
 __all__ = ["row_shard", "packed_words", "block_views", "all_gather_blocks", "PeerExchange",
-           "ShardedFlatSearch", "ShardedIVFSearch"]
+           "ShardedFlatSearch", "ShardedIVFSearch", "ShardedIVFPQSearch"]
 
 
 def row_shard(n: int, world: int, rank: int) -> tuple[int, int]:
@@ -192,3 +192,42 @@ class ShardedIVFSearch(_ShardedSearch):
                                     metric, t.data_ptr(), t[nq * kout:].data_ptr(),
                                     t[2 * nq * kout:].data_ptr(), stream)
         return self._gather_merge(ws, bufs, nq, kout, k, stream)
+
+
+class ShardedIVFPQSearch:
+    """IVF-PQ over row shards: every rank holds the same coarse centroids and
+    codebooks and its rows' list entries with their global list positions;
+    each search writes the shard's (score, sequence, id) block, one
+    all-gather moves the blocks, and ``mans_ivfpq_resolve_device`` merges
+    them and applies the BoundedSortedList outcome -- the unsharded result."""
+
+    def __init__(self, ctx, index_shard, world: int, dist=None):
+        self.ctx, self.index, self.world, self.dist = ctx, index_shard, world, dist
+
+    def buffers(self, nq: int, k: int):
+        import torch
+
+        from .pq import partial_words
+
+        w = partial_words(nq, k)
+        loc = torch.empty((w,), dtype=torch.int32, device="cuda")
+        gat = torch.empty((self.world, w), dtype=torch.int32, device="cuda")
+        out = torch.empty((packed_words(nq, min(k, core.MAX_TOP_K)),), dtype=torch.int32,
+                          device="cuda")
+        return loc, gat, out
+
+    def search_device(self, ws, d_queries: int, nq: int, k: int, nprobe: int, bufs,
+                      stream: int = 0):
+        from .pq import resolve_device
+
+        loc, gat, out = bufs
+        kout = min(k, core.MAX_TOP_K)
+        self.index.search_partial_device(ws, d_queries, nq, k, nprobe, loc.data_ptr(), stream)
+        all_gather_blocks(self.dist, loc, gat)
+        resolve_device(self.ctx, ws, gat.data_ptr(), self.world, gat.shape[1], nq, k,
+                       out.data_ptr(), out[nq * kout:].data_ptr(), out[2 * nq * kout:].data_ptr(),
+                       stream)
+        return out
+
+    def close(self):
+        pass
