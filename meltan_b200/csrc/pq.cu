@@ -261,9 +261,30 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
       nb = 0;
     }
     __syncthreads();
-    for (int e = tid; e < p.m * p.ks; e += kAdcThreads) {
-      const int s = e / p.ks;
-      lut[e] = lut_entry(p.metric, resid + s * p.sub, cb + static_cast<int64_t>(e) * p.sub, p.sub);
+    if (p.metric == kL2 && p.sub == 8) {
+      // the common shape (d/m = 8): two 16-byte codebook loads per entry and
+      // the subspace's residual from shared memory (one subspace per warp
+      // step, so a broadcast); same operations in the same order as lut_entry
+      for (int e = tid; e < p.m * p.ks; e += kAdcThreads) {
+        const int s = e / p.ks;
+        const float4* c4 = reinterpret_cast<const float4*>(cb + static_cast<int64_t>(e) * 8);
+        const float4 a = __ldg(c4), b = __ldg(c4 + 1);
+        const float* r = resid + s * 8;
+        const float cw[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        float sum = 0.0f;
+#pragma unroll
+        for (int d = 0; d < 8; ++d) {
+          const float t = __fsub_rn(r[d], cw[d]);
+          sum = __fadd_rn(sum, __fmul_rn(t, t));
+        }
+        lut[e] = sum;
+      }
+    } else {
+      for (int e = tid; e < p.m * p.ks; e += kAdcThreads) {
+        const int s = e / p.ks;
+        lut[e] = lut_entry(p.metric, resid + s * p.sub, cb + static_cast<int64_t>(e) * p.sub,
+                           p.sub);
+      }
     }
     __syncthreads();
     TopKState st{topbuf, &qc, &nb, &thr};
