@@ -54,6 +54,8 @@ def parse():
                     help="batches of at least this many queries use the tensor-core path")
     ap.add_argument("--no-also", action="store_true",
                     help="skip the extra measurements reported under `also`")
+    ap.add_argument("--also-nq", default="32,1024",
+                    help="comma-separated batch sizes of the extra flat measurements")
     ap.add_argument("--workload", default="flat", choices=["flat", "ivf", "ivfpq"],
                     help="flat: exact scan (configs[1]); ivf: IVF-flat (configs[2]); "
                          "ivfpq: IVF-PQ ADC (configs[3])")
@@ -1032,7 +1034,8 @@ def main():
         return
 
     metric = METRIC_NAMES[args.metric]
-    also_nq = [x for x in (32, 1024) if x != args.nq] if not args.no_also else []
+    also_nq = [] if args.no_also else [
+        x for x in (int(t) for t in args.also_nq.split(",") if t.strip()) if x != args.nq]
     v, q_all = make_data(args.n, args.dim, max([args.nq] + also_nq))
     r0, r1 = mb.row_shard(args.n, world, rank)
     ctx = mb.Context(local)

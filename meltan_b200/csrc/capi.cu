@@ -334,7 +334,10 @@ int32_t corpus_upload(mans_ctx* ctx, const float* rows, int64_t n, int64_t dim, 
     delete c;
     return fail_cuda(e, "cudaMalloc(corpus)");
   }
-  e = cudaMalloc(&c->norms, static_cast<size_t>(std::max<int64_t>(n, 1)) * sizeof(float));
+  // rounded up to 64 floats: the tensor-core pass bulk-copies whole 16-byte
+  // pieces of the last tile's norms
+  e = cudaMalloc(&c->norms, static_cast<size_t>((std::max<int64_t>(n, 1) + 63) / 64 * 64) *
+                                sizeof(float));
   if (e != cudaSuccess) {
     cudaFree(c->rows);
     delete c;

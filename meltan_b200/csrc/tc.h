@@ -28,6 +28,7 @@ struct TcParams {
   uint64_t* cand;           // filter mode: (distance, row) keys, cand_cap per query
   int32_t* cand_count;
   int32_t cand_cap;
+  int32_t cand_reserve;     // list slots a thread reserves per atomic (unused ones padded)
   int* err;
   // Fused sampling (sample_tiles > 0): each block first runs its first
   // sample_tiles tiles as a sample (32-row group minima into samp_out

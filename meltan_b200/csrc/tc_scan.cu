@@ -62,6 +62,7 @@ constexpr size_t kResidentMax = 96 * 1024;
 constexpr size_t kPipeBudget = 196 * 1024;
 constexpr int kRerankThreads = 256;
 constexpr int kMaxRerank = 2048;  // exact re-score list per query
+constexpr int kRtSlots = 4;       // row-term ring depth (tiles)
 
 // Shared scratch of block_kth_smallest.
 struct KthSmem {
@@ -83,6 +84,7 @@ struct TcLayout {
   int stages;
   size_t a_bytes;
   size_t stage_bytes;
+  size_t rt_off;  // ring of per-row terms (kRtSlots x [row factor | |r|^2] x kRN floats)
   size_t bar_off;
   size_t kth_off;
   size_t total;
@@ -101,12 +103,13 @@ __host__ __device__ inline TcLayout tc_layout(int nk, int stream_queries) {
   L.stage_bytes = kRBytes + (L.resident ? 0 : kQBytes);
   size_t st = (kPipeBudget - L.a_bytes) / L.stage_bytes;
   L.stages = static_cast<int>(st > 8 ? 8 : st);
-  L.bar_off = L.a_bytes + static_cast<size_t>(L.stages) * L.stage_bytes;
-  // barriers: full/empty per stage, acc_full/acc_empty x2, a_full, a_empty, drain
-  const size_t bars = 8 * (2 * static_cast<size_t>(L.stages) + 7);
-  // + tmem slot / abort (16 B) + row terms 2 x 2 x kRN floats + the k-th
-  // selection scratch of the fused sampling
-  L.kth_off = L.bar_off + bars + 16 + 2 * 2 * kRN * sizeof(float);
+  L.rt_off = L.a_bytes + static_cast<size_t>(L.stages) * L.stage_bytes;  // 1 KiB aligned
+  L.bar_off = L.rt_off + static_cast<size_t>(kRtSlots) * 2 * kRN * sizeof(float);
+  // barriers: full/empty per stage, acc_full/acc_empty x2, a_full, a_empty,
+  // drain, rt_full/rt_empty per row-term slot
+  const size_t bars = 8 * (2 * static_cast<size_t>(L.stages) + 7 + 2 * kRtSlots);
+  // + tmem slot / abort (16 B) + the k-th selection scratch of the fused sampling
+  L.kth_off = L.bar_off + bars + 16;
   L.total = 1024 + L.kth_off + sizeof(KthSmem);
   return L;
 }
@@ -201,6 +204,16 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* err
   if (mbar_wait_bounded(bar, parity, err)) return true;
   *abort = 1;
   return false;
+}
+
+// 16-byte shared load the compiler may not merge with an earlier one (keeping
+// 32 row terms live between two loops of the epilogue would spill).
+__device__ __forceinline__ float4 lds4(const float* p) {
+  float4 r;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "r"(smem_u32(p)));
+  return r;
 }
 
 // Approximate distance from the bf16 dot v (rows are pre-normalised for
@@ -492,9 +505,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* a_full = acc_empty + 2;
   uint64_t* a_empty = a_full + 1;
   uint64_t* drain = a_empty + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* rt_full = drain + 1;
+  uint64_t* rt_empty = rt_full + kRtSlots;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rt_empty + kRtSlots);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* rowpar = reinterpret_cast<float*>(tmem_slot + 4);  // [2][2][kRN]: bias, beta (L2)
+  // per tile: [kRN] row factor of the integer dot (int8), [kRN] |r|^2 (L2)
+  float* rowpar = reinterpret_cast<float*>(base + L.rt_off);
+  // Per-row terms come with the tile: the producer bulk-copies them into the
+  // ring slot of virtual unit v (v % kRtSlots), the epilogue warps release it.
+  constexpr bool kRowTerms = I8 || MODE == kFilterBias || MODE == kDense;
+  const bool row_terms = kRowTerms && (I8 || p.row_beta != nullptr);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -539,6 +559,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     mbar_init(a_full, 1);
     mbar_init(a_empty, 1);
     mbar_init(drain, 1);
+    for (int r = 0; r < kRtSlots; ++r) {
+      mbar_init(&rt_full[r], 1);
+      mbar_init(&rt_empty[r], kEpiWarps);
+    }
     *abort = 0;
     fence_mbar_init();
   }
@@ -563,6 +587,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int64_t cur_qb = -1;
       uint32_t a_round = 0;
       int64_t issued = 0;
+      int64_t rt_issued = 0;
       bool a_pending = false;
       for (int64_t v = 0; v < nvirt && !*abort; ++v) {
         const int64_t u = unit_of(v);
@@ -579,6 +604,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           ++a_round;
         }
         const int32_t y = static_cast<int32_t>(p.row0 + rt * kRN);
+        if (row_terms) {
+          const int r = static_cast<int>(v % kRtSlots);
+          if (!tc_wait(&rt_empty[r], static_cast<uint32_t>((v / kRtSlots) & 1) ^ 1u, p.err, abort))
+            break;
+          // rows of the tile rounded up to 16 bytes: the arrays are allocated
+          // in multiples of 64 floats, and rows past the pass are masked
+          const int64_t left = p.rows - rt * kRN;
+          const uint32_t bytes =
+              static_cast<uint32_t>(((left < kRN ? left : kRN) + 3) / 4 * 16);
+          float* slot = rowpar + r * 2 * kRN;
+          mbar_arrive_expect_tx(&rt_full[r], bytes * ((I8 ? 1u : 0u) + (p.row_beta ? 1u : 0u)));
+          if (I8) bulk_load(slot, p.row_w + p.row0 + rt * kRN, bytes, &rt_full[r]);
+          if (p.row_beta) bulk_load(slot + kRN, p.row_beta + p.row0 + rt * kRN, bytes, &rt_full[r]);
+          rt_issued = v + 1;
+        }
         bool ok = true;
         for (int kb = 0; kb < nk; ++kb) {
           if (!tc_wait(&empty[stage], phase ^ 1u, p.err, abort)) {
@@ -603,6 +643,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int64_t i = issued > L.stages ? issued - L.stages : 0; i < issued; ++i)
           mbar_wait_bounded(&full[i % L.stages], static_cast<uint32_t>((i / L.stages) & 1), nullptr);
         if (a_pending) mbar_wait_bounded(a_full, (a_round - 1) & 1u, nullptr);
+        for (int64_t i = rt_issued > kRtSlots ? rt_issued - kRtSlots : 0; i < rt_issued; ++i)
+          mbar_wait_bounded(&rt_full[i % kRtSlots], static_cast<uint32_t>((i / kRtSlots) & 1),
+                            nullptr);
       }
     }
   } else if (warp == 1) {
@@ -671,7 +714,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int quarter = warp & 3;
     const int part = ew >> 2;          // columns part*64 .. +63
     const int et = tid - 128;          // 0..511
-    constexpr bool kRowTerms = I8 || MODE == kFilterBias || MODE == kDense;
     int local = 0;
     int64_t cur_qb = -1;
     float alpha = 0.0f, gamma = 0.0f, hq = 0.0f, cq = __int_as_float(0x7F800000);
@@ -681,6 +723,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     KthSmem* ks = reinterpret_cast<KthSmem*>(base + L.kth_off);
     volatile int* bar_ok = reinterpret_cast<volatile int*>(&ks->sh[0]);
     bool synced = !FUSED;
+    // Candidate slots: a thread reserves p.cand_reserve slots of its query's
+    // list at a time (one returning atomic, an L2 round trip that stalls the
+    // warp) and fills them without atomics; slots it does not use are padded
+    // with kKeyMax, whose NaN distance the re-rank skips.  One atomic per
+    // passing row bounded the batched pass at ~2 round trips per warp and tile.
+    int rbase = 0, rleft = 0;
+    uint64_t* cdst = nullptr;
+    auto cand_pad = [&]() {
+      for (int i = 0; i < rleft; ++i)
+        if (rbase + i < p.cand_cap) cdst[rbase + i] = kKeyMax;
+      rleft = 0;
+    };
     // grid barrier n (1 or 2) of this call: arrive, then wait (bounded)
     auto grid_barrier = [&](unsigned long long n) -> bool {
       named_sync(1, kEpiWarps * 32);
@@ -721,8 +775,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int64_t qb = u / rtiles;
       const int64_t rt = u - qb * rtiles;
       if (qb != cur_qb) {
+        cand_pad();  // the reserved slots belong to the previous query
         cur_qb = qb;
         q = qb * kQM + quarter * 32 + lane;
+        cdst = p.cand + q * p.cand_cap;
         qvalid = q < p.nq;
         alpha = qvalid ? p.q_alpha[q] : 0.0f;
         gamma = qvalid ? p.q_gamma[q] : 0.0f;
@@ -746,19 +802,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       const int b = local & 1;
       const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
-      float* rp = rowpar + b * 2 * kRN;
-      if (kRowTerms && (I8 || p.row_beta)) {
-        if (et < kRN) {
-          const int64_t lrow = rt * kRN + et;
-          const bool in = lrow < p.rows;
-          const float beta = (in && p.row_beta) ? p.row_beta[p.row0 + lrow] : 0.0f;
-          if (I8)
-            rp[et] = in ? p.row_w[p.row0 + lrow] : 0.0f;  // factor of the integer dot
-          else
-            rp[et] = in ? 0.5f * beta : __int_as_float(0x7F800000);
-          rp[kRN + et] = beta;
-        }
-        named_sync(1, kEpiWarps * 32);
+      const int rslot = static_cast<int>(vu % kRtSlots);
+      const float* rp = rowpar + rslot * 2 * kRN;
+      if (row_terms &&
+          !mbar_wait_bounded(&rt_full[rslot], static_cast<uint32_t>((vu / kRtSlots) & 1), p.err)) {
+        *abort = 1;
+        break;
       }
       if (!mbar_wait_bounded(&acc_full[b], acc_phase, p.err)) {
         *abort = 1;
@@ -774,8 +823,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tmem_ld32(taddr + c * 32, v);
         const int j0 = part * 64 + c * 32;
         if (I8) {
+          // s32 dot x row factor, four factors per 16-byte shared load
+          const float4* w4 = reinterpret_cast<const float4*>(rp + j0);
 #pragma unroll
-          for (int t = 0; t < 32; ++t) v[t] = __int2float_rn(__float_as_int(v[t])) * rp[j0 + t];
+          for (int t4 = 0; t4 < 8; ++t4) {
+            const float4 w = w4[t4];
+            v[4 * t4] = __int2float_rn(__float_as_int(v[4 * t4])) * w.x;
+            v[4 * t4 + 1] = __int2float_rn(__float_as_int(v[4 * t4 + 1])) * w.y;
+            v[4 * t4 + 2] = __int2float_rn(__float_as_int(v[4 * t4 + 2])) * w.z;
+            v[4 * t4 + 3] = __int2float_rn(__float_as_int(v[4 * t4 + 3])) * w.w;
+          }
         }
         const int64_t lr = lrow0 + c * 32;
         if (sampling) {
@@ -788,7 +845,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int t = 0; t < 32; ++t)
               if (t < tmax)
                 m = fminf(m, approx_distance(alpha, gamma,
-                                             (I8 || p.row_beta) ? rp[kRN + j0 + t] : 0.0f, v[t]));
+                                             p.row_beta ? rp[kRN + j0 + t] : 0.0f, v[t]));
             p.samp_out[q * p.samp_ld + (grp * p.sample_tiles + vu) * 8 + part * 2 + c] = m;
           }
         } else if (MODE == kDense && p.dense_group == 32) {
@@ -803,7 +860,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int t = 0; t < 32; ++t)
               if (t < tmax)
                 m = fminf(m, approx_distance(alpha, gamma,
-                                             (I8 || p.row_beta) ? rp[kRN + j0 + t] : 0.0f, v[t]));
+                                             p.row_beta ? rp[kRN + j0 + t] : 0.0f, v[t]));
             p.dense_out[q * p.dense_ld + (lr >> 5)] = m;
           }
         } else if (MODE == kDense) {
@@ -814,7 +871,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
               for (int i = 0; i < 4; ++i)
                 o[i] = approx_distance(alpha, gamma,
-                                       (I8 || p.row_beta) ? rp[kRN + j0 + t + i] : 0.0f, v[t + i]);
+                                       p.row_beta ? rp[kRN + j0 + t + i] : 0.0f, v[t + i]);
               if (lr + t + 3 < p.rows) {
                 *reinterpret_cast<float4*>(p.dense_out + q * p.dense_ld + lr + t) =
                     make_float4(o[0], o[1], o[2], o[3]);
@@ -825,38 +882,86 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
           }
         } else {
-          float x[32];
+          // Filtered score of rows 4 t4 .. 4 t4 + 3: v (plain) or v less the
+          // row's bias (L2), from one 16-byte shared load of |r|^2 (the same
+          // address in every lane: a broadcast).  Recomputed where needed
+          // rather than kept beside v, which would cost 32 registers.
+          auto score4 = [&](int t4, float* sc) {
+            if (MODE != kFilterBias) {
 #pragma unroll
-          for (int t = 0; t < 32; ++t)
-            x[t] = MODE != kFilterBias ? v[t]
-                   : I8                ? fmaf(-rp[kRN + j0 + t], hq, v[t])
-                                       : v[t] - rp[j0 + t];
+              for (int i = 0; i < 4; ++i) sc[i] = v[4 * t4 + i];
+            } else {
+              const float4 bb = lds4(rp + kRN + j0 + 4 * t4);
+              const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                sc[i] = I8 ? fmaf(-bv[i], hq, v[4 * t4 + i]) : fmaf(-0.5f, bv[i], v[4 * t4 + i]);
+            }
+          };
           // only rows of the pass: the tail of the last tile reads zero rows
           const int64_t rem = p.rows - lr;
           const int tmax = rem >= 32 ? 32 : (rem < 0 ? 0 : static_cast<int>(rem));
           float m = -__int_as_float(0x7F800000);
+          if (MODE != kFilterBias && tmax == 32) {  // full chunk: no row predicates
 #pragma unroll
-          for (int t = 0; t < 32; ++t)
-            if (t < tmax) m = fmaxf(m, x[t]);
-          if (m >= cq) {
+            for (int t4 = 0; t4 < 8; ++t4) {
+              float sc[4];
+              score4(t4, sc);
+              m = fmaxf(fmaxf(m, fmaxf(sc[0], sc[1])), fmaxf(sc[2], sc[3]));
+            }
+          } else {
+#pragma unroll
+            for (int t4 = 0; t4 < 8; ++t4) {
+              float sc[4];
+              score4(t4, sc);
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                if (4 * t4 + i < tmax) m = fmaxf(m, sc[i]);
+            }
+          }
+          if (__any_sync(0xFFFFFFFFu, m >= cq)) {
+            uint32_t pass = 0;
+#pragma unroll
+            for (int t4 = 0; t4 < 8; ++t4) {
+              float sc[4];
+              score4(t4, sc);
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                if (4 * t4 + i < tmax && sc[i] >= cq) pass |= 1u << (4 * t4 + i);
+            }
+            const int np = __popc(pass);
+            if (np > rleft) {
+              cand_pad();
+              rleft = np > p.cand_reserve ? np : p.cand_reserve;
+              rbase = atomicAdd(p.cand_count + q, rleft);
+            }
+            // rows that pass for some lane of the warp: a warp-uniform branch
+            // per row keeps the write loop at the cost of the rows found
+            const uint32_t wpass = __reduce_or_sync(0xFFFFFFFFu, pass);
+            int w = rbase;
 #pragma unroll
             for (int t = 0; t < 32; ++t) {
-              if (t < tmax && x[t] >= cq) {
+              if (((wpass >> t) & 1u) && ((pass >> t) & 1u)) {
                 const float beta = MODE == kFilterBias ? rp[kRN + j0 + t] : 0.0f;
-                const float dist = approx_distance(alpha, gamma, beta, v[t]);
-                const int pos = atomicAdd(p.cand_count + q, 1);
-                if (pos < p.cand_cap)
-                  p.cand[q * p.cand_cap + pos] =
-                      make_key(dist, static_cast<uint32_t>(p.row0 + lr + t));
+                if (w < p.cand_cap)
+                  cdst[w] = make_key(approx_distance(alpha, gamma, beta, v[t]),
+                                     static_cast<uint32_t>(p.row0 + lr + t));
+                ++w;
               }
             }
+            rbase = w;
+            rleft -= np;
           }
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      if (lane == 0) {
+        mbar_arrive(&acc_empty[b]);
+        if (row_terms) mbar_arrive(&rt_empty[rslot]);
+      }
     }
+    cand_pad();
     // a block whose range held only sample tiles (or none) still takes its
     // part in both grid barriers
     if (FUSED && !synced && !*abort) {
@@ -1412,9 +1517,10 @@ static int32_t tc_prepare_int8(mans_corpus* c) {
   cudaError_t e = cudaSuccess;
   if (!c->tc8_rows) {
     const int64_t nn = std::max<int64_t>(n, 1);
+    const int64_t nn64 = (nn + 63) / 64 * 64;  // whole 16-byte pieces per tile (bulk copies)
     e = cudaMalloc(&c->tc8_rows, nn * ld8);
-    if (e == cudaSuccess) e = cudaMalloc(&c->tc8_u, nn * sizeof(float));
-    if (e == cudaSuccess) e = cudaMalloc(&c->tc8_wcos, nn * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&c->tc8_u, nn64 * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&c->tc8_wcos, nn64 * sizeof(float));
     if (e == cudaSuccess) e = cudaMalloc(&c->tc8_stats, nn * 4 * sizeof(float));
     if (e != cudaSuccess) return fail_cuda(e, "cudaMalloc(int8 corpus)");
     c->tc8_ld = ld8;
@@ -1517,12 +1623,19 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   const size_t esize = i8 ? 1 : sizeof(__nv_bfloat16);
   const int64_t qblocks = (nq + kQM - 1) / kQM;
   const int64_t nq_pad = qblocks * kQM;
-  // The int8 bound is about 4x wider than the bf16 one; a larger sample keeps
-  // its filter threshold (sample k-th + 2 eps) and candidate lists small.
+  // Sample size.  The filter threshold (sample k-th + 2 eps) sits near rank
+  // k n / S of the corpus, so the candidate lists hold about k n / S rows plus
+  // the rows of the 2 eps band: S >= k n / 2048 keeps that near two thousand
+  // for every k.  Several query blocks run the sample as its own GEMM costing
+  // S / n of the pass; there S >= n / 16 also thins the candidates, which
+  // saves more epilogue work (list appends) than the sample costs.  The int8
+  // bound is about 4x wider than the bf16 one, hence its larger minimum.
   const int64_t smin = i8 ? 65536 : 16384;
-  int64_t sample = std::min<int64_t>(n, std::max<int64_t>(smin, std::min<int64_t>(131072, 256ll * keff)));
+  int64_t sample = std::max<int64_t>(smin, static_cast<int64_t>(keff) * n / 2048);
+  if (qblocks > 1) sample = std::max<int64_t>(sample, n / 16);
   sample = std::min<int64_t>(n, (sample + kRN - 1) / kRN * kRN);
-  const int32_t cap = static_cast<int32_t>(std::min<int64_t>(i8 ? 32768 : 8192, n));
+  const int32_t cap = static_cast<int32_t>(
+      std::min<int64_t>(std::max<int64_t>(i8 ? 32768 : 8192, 64ll * keff), n));
 
   static const int stream_q = [] {
     const char* e = getenv("MANS_TC_STREAM_QUERIES");
@@ -1545,7 +1658,7 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   const bool fused = qblocks == 1 && groups_full > 0 && lay.resident && coop != 0;
   int64_t samp_tiles = 0, samp_ld = 0;
   if (fused) {
-    const int64_t want = std::max<int64_t>(16384, 256ll * keff);
+    const int64_t want = sample;
     samp_tiles = (want + kRN * groups_full - 1) / (kRN * groups_full);
     samp_tiles = std::max<int64_t>(1, std::min<int64_t>(samp_tiles, rtiles_all / groups_full));
     samp_ld = groups_full * samp_tiles * 8;
@@ -1641,12 +1754,15 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
     return fail(MANS_ERR_SEARCH, "dimension too large for the tensor-core re-rank");
 
   TcParams tp{};
+  tp.row_beta = metric == kL2 ? corpus->norms : nullptr;  // the exact path's fp32 |r|^2
+  tp.row_w = i8 ? (metric == kCosine ? corpus->tc8_wcos : corpus->tc8_u) : nullptr;
+  // the row terms travel by bulk copies of 16-byte pieces from tile starts
+  if ((reinterpret_cast<uintptr_t>(tp.row_beta) | reinterpret_cast<uintptr_t>(tp.row_w)) & 15u)
+    return fail(MANS_ERR_SEARCH, "row terms not 16-byte aligned");
   tp.stream_queries = stream_q;
   tp.nq = nq;
   tp.dim = static_cast<int32_t>(corpus->dim);
   tp.qblocks = static_cast<int32_t>(qblocks);
-  tp.row_beta = metric == kL2 ? corpus->norms : nullptr;  // the exact path's fp32 |r|^2
-  tp.row_w = i8 ? (metric == kCosine ? corpus->tc8_wcos : corpus->tc8_u) : nullptr;
   tp.q_alpha = F(o_al);
   tp.q_gamma = F(o_ga);
   tp.q_c = F(o_cq);
@@ -1698,6 +1814,16 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
     grid = static_cast<int>(tp.groups * qblocks);
   }
   tp.row0 = 0;
+  {
+    // Reservation size: padding may take at most 1/8 of the list over the
+    // (block, column part) writers of one query.  The fused pass (at most 128
+    // queries, HBM bound) reserves exactly what each chunk needs: no padding
+    // for the re-rank to read past.
+    const int64_t writers = 4 * (tp.groups > 0 ? tp.groups : grid / qblocks + 1);
+    tp.cand_reserve = fused ? 1
+                            : static_cast<int32_t>(std::max<int64_t>(
+                                  1, std::min<int64_t>(8, cap / (8 * writers))));
+  }
   if (fused) {
     tp.sample_tiles = static_cast<int32_t>(samp_tiles);
     tp.samp_out = F(o_dn);

@@ -41,7 +41,8 @@ def same(got, want):
 
 
 @pytest.mark.parametrize("mg,mo", MET)
-@pytest.mark.parametrize("n,d", [(1000, 32), (70001, 100), (20000, 384), (5000, 768)])
+@pytest.mark.parametrize("n,d", [(1000, 32), (70001, 100), (20000, 384), (5000, 768),
+                                 (3000, 1536)])
 def test_tc_parity_small(tctx, mg, mo, n, d):
     rng = np.random.default_rng(n + d)
     v = unit_rows(rng, n, d)
@@ -59,6 +60,15 @@ def test_tc_tiny_corpora(tctx, n):
     for mg, mo in MET:
         for k in (1, 10):
             same(run(tctx, v, q, k, mg), O.flat_search(v, q, k, mo))
+
+
+def test_tc_many_query_blocks_wide_rows(tctx):
+    """Five 128-query blocks over 1536-wide rows (queries streamed per tile)."""
+    rng = np.random.default_rng(1536)
+    v = unit_rows(rng, 4000, 1536)
+    q = unit_rows(rng, 600, 1536)
+    for mg, mo in (MET[0], MET[2]):
+        same(run(tctx, v, q, 10, mg), O.flat_search(v, q, 10, mo))
 
 
 def test_tc_unnormalised_rows_and_k256(tctx):
