@@ -1120,11 +1120,22 @@ __global__ void tc_query_prep_kernel(const TcQueryParams p) {
     qs = mx > 0.0f ? static_cast<double>(mx) / 127.0 : 1.0;
   }
   double nq2 = 0.0, nres = 0.0, nt = 0.0;
+  // |q|^2 of the exact path: sequential fp32 sum in index order.  Each lane
+  // squares its element of the 32-wide chunk and the warp adds the chunk's
+  // squares lane by lane through shuffles, so every lane carries the same
+  // running sum without a serial pass over memory.  Lanes past `dim` add
+  // +0, which leaves a sum of non-negative squares (never -0) unchanged.
+  float acc = 0.0f;
   // read-only loads (no aliasing with the stores below), four in flight
 #pragma unroll 4
   for (int c0 = 0; c0 < p.ld16; c0 += 32) {
     const int c = c0 + lane;
     const float x = c < p.dim ? __ldg(v + c) : 0.0f;
+    if (c0 < p.dim) {
+      const float sq = __fmul_rn(x, x);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc = __fadd_rn(acc, __shfl_sync(0xFFFFFFFFu, sq, j));
+    }
     if (c < p.ld16) {
       double xb;
       if (I8) {
@@ -1150,14 +1161,6 @@ __global__ void tc_query_prep_kernel(const TcQueryParams p) {
     nt += __shfl_xor_sync(0xFFFFFFFFu, nt, o);
   }
   if (lane != 0) return;
-  // |q|^2 of the exact path: sequential fp32 sum in index order (the warp
-  // just read the row, so these loads hit L1)
-  float acc = 0.0f;
-#pragma unroll 8
-  for (int c = 0; c < p.dim; ++c) {
-    const float y = __ldg(v + c);
-    acc = __fadd_rn(acc, __fmul_rn(y, y));
-  }
   const QueryTerms t = query_terms(p.cs, p.metric, p.dim, acc, nq2, nres, nt, qs);
   p.qn_exact[q] = t.qn;
   p.alpha[q] = t.alpha;
@@ -1271,20 +1274,22 @@ inline size_t rerank_smem_bytes(int64_t dim, int region) {
   return static_cast<size_t>((dim + 3) / 4 * 4) * sizeof(float) + region;
 }
 
-// Exact distance of a row staged in shared memory, in the reference order.
+// Exact distance of a row staged in shared memory, in the reference order;
+// `q` (shared, 16-byte aligned) is the query, `vn` the row's |r|^2 (0 for IP).
 __device__ __forceinline__ float exact_distance_smem(const RerankParams& p, const float* q,
-                                                     float qn, const float* r, int64_t row) {
+                                                     float qn, const float* r, float vn) {
   float acc = 0.0f;
   int c = 0;
   for (; c + 4 <= p.dim; c += 4) {
     const float4 v = *reinterpret_cast<const float4*>(r + c);
-    acc = __fadd_rn(acc, __fmul_rn(v.x, q[c]));
-    acc = __fadd_rn(acc, __fmul_rn(v.y, q[c + 1]));
-    acc = __fadd_rn(acc, __fmul_rn(v.z, q[c + 2]));
-    acc = __fadd_rn(acc, __fmul_rn(v.w, q[c + 3]));
+    const float4 w = *reinterpret_cast<const float4*>(q + c);
+    acc = __fadd_rn(acc, __fmul_rn(v.x, w.x));
+    acc = __fadd_rn(acc, __fmul_rn(v.y, w.y));
+    acc = __fadd_rn(acc, __fmul_rn(v.z, w.z));
+    acc = __fadd_rn(acc, __fmul_rn(v.w, w.w));
   }
   for (; c < p.dim; ++c) acc = __fadd_rn(acc, __fmul_rn(r[c], q[c]));
-  return finalize_distance(p.metric, acc, qn, p.metric == kIP ? 0.0f : __ldg(p.norms + row));
+  return finalize_distance(p.metric, acc, qn, vn);
 }
 
 // Per query: certify the candidate list, then re-score the band exactly.
@@ -1314,6 +1319,7 @@ __global__ void __launch_bounds__(kRerankThreads) tc_rerank_kernel(const RerankP
   const int cnt = min(total, p.cand_cap);
   const float e = p.eps[q];
   const float qn = p.qn_exact[q];
+  const float thr_q = p.thr[q];  // loaded with the others, read after the k-th selection
   if (tid == 0) {
     nlist = 0;
     fail_flag = (total > p.cand_cap || cnt < p.k) ? 1 : 0;
@@ -1332,7 +1338,7 @@ __global__ void __launch_bounds__(kRerankThreads) tc_rerank_kernel(const RerankP
     if (tid == 0) {
       float band = tk + 2.0f * e;
       band = band + fabsf(band) * 1e-6f;
-      if (!(band <= p.thr[q])) fail_flag = 1;  // the filter did not cover the band
+      if (!(band <= thr_q)) fail_flag = 1;  // the filter did not cover the band
       band_sh = band;
     }
     __syncthreads();
@@ -1359,6 +1365,8 @@ __global__ void __launch_bounds__(kRerankThreads) tc_rerank_kernel(const RerankP
     const int chunks = (p.dim + 3) / 4;  // 16-byte pieces of one row
     for (int b = 0; b < m; b += per_round) {
       const int rn = min(per_round, m - b);
+      // the row's |r|^2, loaded while its row is in flight
+      const float vn = (tid < rn && p.metric != kIP) ? __ldg(p.norms + list[b + tid]) : 0.0f;
       for (int t = tid; t < rn * chunks; t += kRerankThreads) {
         const int r = t / chunks, c = t - r * chunks;
         cp_async16(srows + r * pitch + 4 * c, p.rows + static_cast<int64_t>(list[b + r]) * p.ld + 4 * c);
@@ -1367,7 +1375,7 @@ __global__ void __launch_bounds__(kRerankThreads) tc_rerank_kernel(const RerankP
       __syncthreads();
       if (tid < rn) {
         const int64_t row = list[b + tid];
-        ekeys[b + tid] = make_key(exact_distance_smem(p, qsm, qn, srows + tid * pitch, row),
+        ekeys[b + tid] = make_key(exact_distance_smem(p, qsm, qn, srows + tid * pitch, vn),
                                   static_cast<uint32_t>(row + p.id_offset));
       }
       __syncthreads();
