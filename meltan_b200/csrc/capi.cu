@@ -156,6 +156,7 @@ void destroy_workspace(mans_workspace* ws) {
   ws->aux.release();
   ws->aux2.release();
   ws->tc_aux.release();
+  ws->small_scores.release();
   ws->tc_bar.release();
   ws->h_err.release();
   for (auto& pr : ws->events) {
@@ -205,10 +206,15 @@ int choose_qb(int64_t nq) {
 int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace* ws,
                         const float* d_queries, int64_t nq, int32_t k, int32_t metric,
                         float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
-                        cudaStream_t stream, int mode, int32_t kcap) {
+                        cudaStream_t stream, int mode, int32_t kcap, bool centroid_scan) {
   const int32_t kout = std::min<int32_t>(k, kcap);
   const int64_t n = corpus->n;
   if (nq <= 0) return MANS_OK;
+  if (centroid_scan && k > 0 && small_batch_applies(corpus, nq)) {
+    ws->last_path = 0;
+    return run_small_batch_search(ctx, corpus, ws, d_queries, nq, kout, metric, d_out_dist,
+                                  d_out_ids, d_out_counts, stream, mode);
+  }
   // Tensor-core path: batches of at least tc_min_batch queries, and any batch
   // over a corpus of at least 2^25 elements (87k rows at d = 384): there the
   // bf16 pass over half the bytes, fused with its sampling, plus prep and
@@ -236,6 +242,9 @@ int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace
     cudaError_t e = launch_fill_empty(d_out_dist, d_out_ids, d_out_counts, nq, kout, stream);
     return e == cudaSuccess ? MANS_OK : fail_cuda(e, "fill_empty launch");
   }
+  if (small_batch_applies(corpus, nq))
+    return run_small_batch_search(ctx, corpus, ws, d_queries, nq, kout, metric, d_out_dist,
+                                  d_out_ids, d_out_counts, stream, mode);
   const int32_t keff = static_cast<int32_t>(std::min<int64_t>(kout, n));
   const int32_t kp = pow2_at_least(keff);
   const int qb = choose_qb(nq);

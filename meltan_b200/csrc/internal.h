@@ -108,6 +108,8 @@ struct mans_workspace {
   // scratch of the tensor-core batch path alone: it runs nested inside other
   // searches (the IVF centroid scan) whose own scratch lives in `aux`
   mans::DeviceBuffer tc_aux;
+  // score matrix chunk of the small-corpus batch search (centroid scans)
+  mans::DeviceBuffer small_scores;
   // grid-barrier counter of the fused tensor-core pass (monotonic; the host
   // keeps its expected value, both reset after a device error)
   mans::DeviceBuffer tc_bar;
@@ -158,8 +160,21 @@ void tc_free_corpus(mans_corpus* c);
 // Exact scan + top-k over `corpus`.  mode: kModeHost (host-tier distance) or
 // kModeSimd (SIMDDistance semantics).  kcap bounds k (256 for the public
 // searches; 512 for the internal 2k candidate lists of the IVF-PQ stages).
+// centroid_scan: a batch over a small corpus takes the small-corpus path even
+// where the tensor-core path would apply (the centroid steps of the indexes).
 int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace* ws,
                         const float* d_queries, int64_t nq, int32_t k, int32_t metric,
                         float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
-                        cudaStream_t stream, int mode = 0, int32_t kcap = 256);
+                        cudaStream_t stream, int mode = 0, int32_t kcap = 256,
+                        bool centroid_scan = false);
+// Batches of at least kSmallBatchMinQueries queries over a corpus of at most
+// kSmallBatchMaxRows rows (centroid sets): score tiles + per-query sort
+// (small_scan.cu), the same results as the streaming scan.
+constexpr int64_t kSmallBatchMinQueries = 64;
+constexpr int64_t kSmallBatchMaxRows = 8192;
+bool small_batch_applies(const mans_corpus* corpus, int64_t nq);
+int32_t run_small_batch_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace* ws,
+                               const float* d_queries, int64_t nq, int32_t kout, int32_t metric,
+                               float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
+                               cudaStream_t stream, int mode);
 }  // namespace mans

@@ -311,7 +311,7 @@ static int32_t run_ivf_search(mans_ctx* ctx, mans_ivf* ivf, mans_workspace* ws,
   {
     TimingHold hold(ws);  // the centroid scan is not the timed list scan
     rc = run_flat_search(ctx, ivf->cent, ws, d_queries, nq, probe, metric, probe_d, probe_i,
-                         probe_c, stream);
+                         probe_c, stream, kModeHost, MANS_MAX_TOPK, true);
   }
   if (rc != MANS_OK) return rc;
 
@@ -632,7 +632,7 @@ static int32_t assign_rows_device(mans_ctx* ctx, const mans_corpus* corpus,
       break;
     }
     rc = run_flat_search(ctx, cent, ws, d_q, m, 1, metric, d_dist, d_assign + r0, d_cnt,
-                         ws->stream);
+                         ws->stream, kModeHost, MANS_MAX_TOPK, true);
   }
   if (rc == MANS_OK) {
     e = cudaStreamSynchronize(ws->stream);

@@ -253,6 +253,12 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
       continue;
     }
     const uint32_t list = p.probe_lists[q * p.probe + pr];
+    const int64_t off = p.offsets[list];
+    const int64_t len = p.offsets[list + 1] - off;
+    if (len == 0) {  // an empty list (a shard holding other lists): no table to build
+      if (tid == 0) p.slot_counts[it] = 0;
+      continue;
+    }
     for (int d = tid; d < p.dim; d += kAdcThreads)
       resid[d] = __fsub_rn(p.queries[q * p.dim + d], p.coarse[list * p.coarse_ld + d]);
     if (tid == 0) {
@@ -288,8 +294,6 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
     }
     __syncthreads();
     TopKState st{topbuf, &qc, &nb, &thr};
-    const int64_t off = p.offsets[list];
-    const int64_t len = p.offsets[list + 1] - off;
     for (int64_t b = 0; b < len; b += kAdcThreads) {
       const int64_t e = b + tid;
       const bool valid = e < len;
