@@ -63,6 +63,9 @@ def parse():
     ap.add_argument("--nprobe", type=int, default=None)
     ap.add_argument("--components", type=int, default=None)
     ap.add_argument("--pq-m", type=int, default=16)
+    ap.add_argument("--pq-shard", default="list", choices=["list", "row"],
+                    help="IVF-PQ over N > 1 GPUs: whole inverted lists per rank (each rank "
+                         "builds tables only for the probed lists it holds) or row ranges")
     ap.add_argument("--transport", default="p2p", choices=["p2p", "nccl"],
                     help="how row shards exchange their top-k blocks (N > 1)")
     a = ap.parse_args()
@@ -591,7 +594,8 @@ def index_workload_config(args, nq=None, nprobe=None):
     cfg = {"workload": name, "n": args.n, "dim": args.dim, "nq": nq, "k": args.k,
            "metric": args.metric, "nlist": args.nlist, "nprobe": nprobe,
            "components": args.components,
-           "parallelism": f"rowshard{args.gpus}",
+           "parallelism": (f"listshard{args.gpus}" if args.workload == "ivfpq" and args.gpus > 1
+                           and args.pq_shard == "list" else f"rowshard{args.gpus}"),
            "l2": "probed lists differ per query; each step streams its lists once "
                  "(no flush; lists of one batch may hit L2)"}
     if args.workload == "ivfpq":
@@ -634,6 +638,38 @@ def build_index_data(args, nq_max, device=None, mb=None, ctx=None, shard=None, d
             dist.broadcast(ct, 0)
             dist.broadcast(bt, 0)
             coarse, cb = ct.cpu().numpy(), bt.cpu().numpy()
+        if shard is not None and args.pq_shard == "list":
+            # whole lists per rank: every rank learns every row's list from one
+            # all-gather of the ranks' coarse assignments, the lists are spread
+            # by size (pq.list_owners) and each rank encodes the rows of its own
+            import torch
+            from meltan_b200 import pq as mpq
+            world, rank = dist.get_world_size(), dist.get_rank()
+            bounds = [mb.row_shard(v.shape[0], world, r) for r in range(world)]
+            r0, r1 = shard
+            t0 = time.perf_counter()
+            _, sassign = mb.pq_encode(ctx, v[r0:r1], coarse, cb, mb.Metric(metric))
+            width = max(b - a for a, b in bounds)
+            mine = torch.full((width,), -1, dtype=torch.int32, device="cuda")
+            mine[: r1 - r0] = torch.from_numpy(sassign.astype(np.int32)).cuda()
+            parts = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(parts, mine)
+            assign = np.concatenate([pt.cpu().numpy()[: b - a] for pt, (a, b) in zip(parts, bounds)])
+            off = np.concatenate([[0], np.cumsum(np.bincount(assign, minlength=args.nlist))])
+            flat = np.argsort(assign, kind="stable").astype(np.uint32)
+            owner = mpq.list_owners(np.diff(off), world)
+            soff, sflat, spos = mb.IVFPQIndex.shard_lists_by_list(off, flat, owner == rank)
+            mcodes, massign = mb.pq_encode(ctx, v[sflat], coarse, cb, mb.Metric(metric))
+            gpu_s = time.perf_counter() - t0
+            if not np.array_equal(massign, assign[sflat]):
+                raise RuntimeError("list shard: the re-encoded rows changed lists")
+            codes = np.zeros((v.shape[0], args.pq_m), np.uint8)
+            codes[sflat] = mcodes
+            return v, q, {"coarse": coarse, "codebooks": cb, "codes": codes,
+                          "offsets": soff, "lists": sflat, "positions": spos,
+                          "build_gpu_s": gpu_s,
+                          "build_gpu": "mans_pq_encode: every rank's rows (assignment), then "
+                                       "the rows of this rank's lists (codes)"}
         if shard is not None:
             # this rank's rows; list entries carry their positions in the
             # global lists (earlier shards' entries of a list come first)

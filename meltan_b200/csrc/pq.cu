@@ -229,19 +229,57 @@ __device__ __forceinline__ float adc_sum(const float* lut, int ks, const uint8_t
   return total;
 }
 
+// ---- warp-resident top-k of (score, seq) keys (at most 32 kept) ----------------
+
+__device__ __forceinline__ uint64_t key_min(uint64_t a, uint64_t b) { return a < b ? a : b; }
+__device__ __forceinline__ uint64_t key_max(uint64_t a, uint64_t b) { return a < b ? b : a; }
+
+// Ascending bitonic sort of one key per lane.
+__device__ __forceinline__ uint64_t warp_sort32(uint64_t x, int lane) {
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1)
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const uint64_t y = __shfl_xor_sync(0xFFFFFFFFu, x, j);
+      x = (((lane & j) == 0) == ((lane & k) == 0)) ? key_min(x, y) : key_max(x, y);
+    }
+  return x;
+}
+
+// The 32 smallest of two ascending lane-sorted lists, ascending: the lane-wise
+// minimum of t and x reversed is a bitonic sequence holding them, which a
+// half-cleaner cascade sorts.
+__device__ __forceinline__ uint64_t warp_merge32(uint64_t t, uint64_t x, int lane) {
+  uint64_t y = key_min(t, __shfl_sync(0xFFFFFFFFu, x, 31 - lane));
+#pragma unroll
+  for (int j = 16; j > 0; j >>= 1) {
+    const uint64_t z = __shfl_xor_sync(0xFFFFFFFFu, y, j);
+    y = (lane & j) == 0 ? key_min(y, z) : key_max(y, z);
+  }
+  return y;
+}
+
 // Block b handles items b, b + grid, ... ; item = (query, probe rank).  Small
 // blocks (several resident per SM) hide the latency of the per-item steps:
-// residual, LUT in shared memory, sequential ADC per code with a running
-// (score, seq) top-k.
+// residual, LUT in shared memory, sequential ADC per code, the item's k
+// smallest (score, seq) keys.  WARP_TOPK (k <= 32): every warp keeps its own
+// 32 smallest keys in registers (one per lane; a batch of 32 codes that beats
+// the k-th is sorted by shuffles and merged in), and warp 0 merges the four
+// lists at the end -- no block barrier while scanning.  Otherwise a running
+// top-k in shared memory (append queue + block bitonic merges).
+template <bool WARP_TOPK>
 __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<size_t>(smem_raw) + 15) / 16 * 16);
   uint64_t* topbuf = reinterpret_cast<uint64_t*>(base);
-  float* lut = reinterpret_cast<float*>(base + static_cast<size_t>(p.sortn) * 8);
+  float* lut = reinterpret_cast<float*>(base + (WARP_TOPK ? 0 : static_cast<size_t>(p.sortn) * 8));
   float* resid = lut + p.m * p.ks;
   __shared__ uint64_t thr;
   __shared__ int qc, nb;
+  __shared__ uint64_t wlist[kAdcThreads / 32][32];
   const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
   const float* cb = p.codebooks;
   const int64_t items = p.nq * p.probe;
   for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
@@ -261,7 +299,7 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
     }
     for (int d = tid; d < p.dim; d += kAdcThreads)
       resid[d] = __fsub_rn(p.queries[q * p.dim + d], p.coarse[list * p.coarse_ld + d]);
-    if (tid == 0) {
+    if (!WARP_TOPK && tid == 0) {
       thr = kKeyMax;
       qc = 0;
       nb = 0;
@@ -293,6 +331,45 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
       }
     }
     __syncthreads();
+    if (WARP_TOPK) {
+      uint64_t best = kKeyMax;  // lane i: this warp's (i+1)-th smallest key
+      for (int64_t b = static_cast<int64_t>(warp) * 32; b < len; b += kAdcThreads) {
+        const int64_t e = b + lane;
+        uint64_t key = kKeyMax;
+        if (e < len) {
+          const float total = adc_sum(lut, p.ks, p.codes + (off + e) * p.m, p.m);
+          const uint32_t pos = p.pos ? p.pos[off + e] : static_cast<uint32_t>(e);
+          key = make_key(total, (static_cast<uint32_t>(pr) << kPosBits) | pos);
+        }
+        const uint64_t kth = __shfl_sync(0xFFFFFFFFu, best, p.k - 1);
+        uint32_t pass = __ballot_sync(0xFFFFFFFFu, key < kth);
+        if (__popc(pass) > 6) {
+          best = warp_merge32(best, warp_sort32(key < kth ? key : kKeyMax, lane), lane);
+        } else {
+          // a few keys: insert each at its rank (keys are distinct); the
+          // last entry drops out.  A key that no longer beats the k-th after
+          // an earlier insertion lands at rank k or is dropped: harmless.
+          while (pass) {
+            const int src = __ffs(pass) - 1;
+            pass &= pass - 1;
+            const uint64_t x = __shfl_sync(0xFFFFFFFFu, key, src);
+            const int at = __popc(__ballot_sync(0xFFFFFFFFu, best < x));
+            const uint64_t up = __shfl_up_sync(0xFFFFFFFFu, best, 1);
+            best = lane < at ? best : (lane == at ? x : up);
+          }
+        }
+      }
+      wlist[warp][lane] = best;
+      __syncthreads();
+      if (warp == 0) {
+#pragma unroll
+        for (int w = 1; w < kAdcThreads / 32; ++w) best = warp_merge32(best, wlist[w][lane], lane);
+        const int have = static_cast<int>(len < p.k ? len : p.k);
+        if (lane < have) p.slot_keys[it * p.kp + lane] = best;
+        if (lane == 0) p.slot_counts[it] = have;
+      }
+      continue;
+    }
     TopKState st{topbuf, &qc, &nb, &thr};
     for (int64_t b = 0; b < len; b += kAdcThreads) {
       const int64_t e = b + tid;
@@ -563,22 +640,29 @@ static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* w
   a.slot_keys = static_cast<uint64_t*>(ws->slot_keys.ptr);
   a.slot_counts = static_cast<int32_t*>(ws->slot_counts.ptr);
   a.sortn = std::max(512, pow2_at_least(kp2 + kAdcThreads));
-  const size_t smem = 16 + static_cast<size_t>(a.sortn) * 8 +
+  // up to 32 kept keys per item: warp-resident lists, no shared top-k buffer
+  const bool warp_topk = k2 <= 32;
+  const void* kfn = warp_topk ? reinterpret_cast<const void*>(pq_adc_kernel<true>)
+                              : reinterpret_cast<const void*>(pq_adc_kernel<false>);
+  const size_t smem = 16 + (warp_topk ? 0 : static_cast<size_t>(a.sortn) * 8) +
                       static_cast<size_t>(ix->m) * ix->ks * 4 +
                       static_cast<size_t>((ix->dim + 3) / 4 * 4) * 4;
   if (smem > static_cast<size_t>(ctx->max_smem) - 64)
     return fail(MANS_ERR_SEARCH, "PQ distance table exceeds shared memory");
-  e = cudaFuncSetAttribute(pq_adc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem));
   if (e != cudaSuccess) return fail_cuda(e, "adc configure");
   int per_sm = 1;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pq_adc_kernel, kAdcThreads, smem);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kAdcThreads, smem);
   if (e != cudaSuccess) return fail_cuda(e, "adc occupancy");
   const int64_t items = nq * probe;
   const int grid = static_cast<int>(
       std::min<int64_t>(items, static_cast<int64_t>(ctx->num_sms) * std::max(1, per_sm)));
   cudaEvent_t stop = timing_begin(ws, stream);
-  pq_adc_kernel<<<grid, kAdcThreads, smem, stream>>>(a);
+  if (warp_topk)
+    pq_adc_kernel<true><<<grid, kAdcThreads, smem, stream>>>(a);
+  else
+    pq_adc_kernel<false><<<grid, kAdcThreads, smem, stream>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "adc launch");
   timing_end(stop, stream);

@@ -105,6 +105,22 @@ class IVFPQIndex:
         soff = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
         return soff, flat[keep], pos[keep].astype(np.uint32)
 
+    @staticmethod
+    def shard_lists_by_list(offsets, flat, owned):
+        """The whole inverted lists a list shard owns (`owned`: a boolean mask
+        over the lists) of a global index: (offsets with every other list
+        empty, ids, positions in the lists), insertion order kept.  A search
+        of the shard builds distance tables only for probed lists it holds."""
+        offsets = np.asarray(offsets, np.int64)
+        flat = np.asarray(flat, np.uint32)
+        owned = np.asarray(owned, bool)
+        lists = np.repeat(np.arange(len(offsets) - 1), np.diff(offsets))
+        keep = owned[lists]
+        pos = np.arange(len(flat), dtype=np.int64) - offsets[lists]
+        sizes = np.diff(offsets) * owned
+        soff = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+        return soff, flat[keep], pos[keep].astype(np.uint32)
+
     def close(self):
         if self._h:
             lib().mans_ivfpq_destroy(self._h)
@@ -115,6 +131,20 @@ class IVFPQIndex:
             self.close()
         except Exception:
             pass
+
+
+def list_owners(sizes, world: int) -> np.ndarray:
+    """Rank owning each inverted list when whole lists are spread over
+    `world` shards: largest list first to the least-loaded rank (ties to the
+    lower rank), the same answer on every rank."""
+    sizes = np.asarray(sizes, np.int64)
+    owner = np.empty(len(sizes), np.int32)
+    load = np.zeros(world, np.int64)
+    for lst in np.argsort(-sizes, kind="stable"):
+        r = int(np.argmin(load))
+        owner[lst] = r
+        load[r] += sizes[lst]
+    return owner
 
 
 def partial_words(nq: int, k: int) -> int:

@@ -203,3 +203,49 @@ def test_row_sharded_ivfpq_equals_unsharded(ctx, shards):
         for ix in idx:
             ix.close()
     ws.close()
+
+
+@pytest.mark.parametrize("shards", [2, 3])
+def test_list_sharded_ivfpq_equals_unsharded(ctx, shards):
+    """IVF-PQ over list shards (whole inverted lists per shard, spread by
+    pq.list_owners): each shard builds tables only for the probed lists it
+    holds, and its (score, sequence) 2k-blocks, merged and resolved, equal the
+    oracle's _IVFPQIndex.search on the whole index -- ties included."""
+    import torch
+    from meltan_b200 import pq as mpq
+    rng = np.random.default_rng(34)
+    n, dim, m, nlist = 6000, 32, 8, 24
+    v = rng.standard_normal((n, dim), dtype=np.float32)
+    coarse = v[rng.choice(n, nlist, replace=False)].copy()
+    cb = rng.standard_normal((m, 256, dim // m), dtype=np.float32)
+    codes, assign = mb.pq_encode(ctx, v, coarse, cb)
+    codes[4000:4100] = codes[10]  # equal scores in different lists and shards
+    flat = np.argsort(assign, kind="stable").astype(np.uint32)
+    off = np.concatenate([[0], np.cumsum(np.bincount(assign, minlength=nlist))]).astype(np.int64)
+    owner = mpq.list_owners(np.diff(off), shards)
+    q = rng.standard_normal((70, dim), dtype=np.float32)  # the small-corpus coarse step too
+    ws = mb.Workspace(ctx)
+    dq = torch.from_numpy(q).cuda()
+    for k, nprobe in ((10, 4), (25, 24), (3, 1)):
+        words = mpq.partial_words(len(q), k)
+        blocks = torch.empty((shards, words), dtype=torch.int32, device="cuda")
+        idx = []
+        for s_ in range(shards):
+            soff, sflat, spos = mb.IVFPQIndex.shard_lists_by_list(off, flat, owner == s_)
+            ix = mb.IVFPQIndex(ctx, coarse, cb, codes, (soff, sflat), list_positions=spos)
+            ix.search_partial_device(ws, dq.data_ptr(), len(q), k, nprobe, blocks[s_].data_ptr())
+            idx.append(ix)
+        kout = min(k, 256)
+        od = torch.empty((len(q), kout), dtype=torch.float32, device="cuda")
+        oi = torch.empty((len(q), kout), dtype=torch.int32, device="cuda")
+        oc = torch.empty((len(q),), dtype=torch.int32, device="cuda")
+        mpq.resolve_device(ctx, ws, blocks.data_ptr(), shards, words, len(q), k, od.data_ptr(),
+                           oi.data_ptr(), oc.data_ptr())
+        ws.check()
+        want = O.ivfpq_search(coarse, cb, codes, off, flat, q, k, nprobe, O.L2)
+        np.testing.assert_array_equal(oc.cpu().numpy(), want[2])
+        np.testing.assert_array_equal(oi.cpu().numpy().view(np.uint32), want[1])
+        np.testing.assert_array_equal(od.cpu().numpy(), want[0])
+        for ix in idx:
+            ix.close()
+    ws.close()
