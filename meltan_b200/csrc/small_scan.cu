@@ -123,25 +123,33 @@ __global__ void __launch_bounds__(kSsThreads) small_scores_kernel(const SsParams
 }
 
 // Per query (block): the keff smallest (distance, id) keys of its n scores,
-// ascending; slots keff .. kout - 1 empty.  keff = 1 is a block minimum,
-// otherwise the n keys (padded to np2) are sorted in shared memory.
+// ascending; slots keff .. kout - 1 empty.  keff = 1 is a block minimum.
+// Otherwise a radix select (four 8-bit passes over the order-preserving
+// 32-bit image of the distances, staged in shared memory) finds T, the
+// keff-th smallest distance; the keys of distance <= T -- every key below T
+// and all keys tied at T, whose ids decide -- are sorted and the first keff
+// written.  Far more ties at T than the staging room leaves (duplicate rows)
+// fall back to sorting all n keys.
 __global__ void __launch_bounds__(kSelThreads) small_select_kernel(
     const float* __restrict__ scores, int64_t sld, int64_t n, const uint32_t* __restrict__ ids,
     uint32_t id_offset, int32_t keff, int32_t kout, int np2, float* __restrict__ out_dist,
     uint32_t* __restrict__ out_ids, int32_t* __restrict__ out_counts) {
-  extern __shared__ uint64_t keys[];
+  extern __shared__ uint64_t keys[];  // np2 keys; the radix select uses it as
+                                      // [n ordered distances | np2/2 candidate keys]
   __shared__ uint64_t wmin[kSelThreads / 32];
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t sel_prefix, sel_rank, ncand;
   const int tid = threadIdx.x;
   const int64_t q = blockIdx.x;
   const float* row = scores + q * sld;
-  auto key_of = [&](int64_t i) {
-    const uint32_t id = ids ? __ldg(ids + i) : static_cast<uint32_t>(i + id_offset);
-    return make_key(__ldcg(row + i), id);
+  auto id_of = [&](int64_t i) {
+    return ids ? __ldg(ids + i) : static_cast<uint32_t>(i + id_offset);
   };
+  int sorted_n = 0;  // keys[0 .. keff) hold the result once set
   if (keff == 1) {
     uint64_t m = kKeyMax;
     for (int64_t i = tid; i < n; i += kSelThreads) {
-      const uint64_t x = key_of(i);
+      const uint64_t x = make_key(__ldcg(row + i), id_of(i));
       m = x < m ? x : m;
     }
     for (int o = 16; o > 0; o >>= 1) {
@@ -159,8 +167,75 @@ __global__ void __launch_bounds__(kSelThreads) small_select_kernel(
       if (tid == 0) keys[0] = m;
     }
     __syncthreads();
+    sorted_n = 1;
   } else {
-    for (int i = tid; i < np2; i += kSelThreads) keys[i] = i < n ? key_of(i) : kKeyMax;
+    uint32_t* u = reinterpret_cast<uint32_t*>(keys);  // n ordered distances
+    uint64_t* cand = keys + np2 / 2;                  // np2 / 2 candidate keys
+    const int cap = np2 / 2;
+    for (int64_t i = tid; i < n; i += kSelThreads) u[i] = float_to_ordered(__ldcg(row + i));
+    if (tid == 0) {
+      sel_prefix = 0;
+      sel_rank = static_cast<uint32_t>(keff);
+      ncand = 0;
+    }
+    uint32_t mask = 0;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int i = tid; i < 256; i += kSelThreads) hist[i] = 0;
+      __syncthreads();
+      const uint32_t prefix = sel_prefix;
+      for (int64_t i = tid; i < n; i += kSelThreads)
+        if ((u[i] & mask) == prefix) atomicAdd(&hist[(u[i] >> shift) & 255u], 1u);
+      __syncthreads();
+      if (tid < 32) {
+        // digit holding the rank-th value: lane l sums bins 8l .. 8l + 7
+        uint32_t c[8], run = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          c[j] = hist[tid * 8 + j];
+          run += c[j];
+        }
+        uint32_t incl = run;
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+          if (tid >= o) incl += y;
+        }
+        const uint32_t rank = sel_rank;
+        uint32_t before = incl - run;
+        if (before < rank && incl >= rank) {
+          int d = 0;
+          while (before + c[d] < rank) before += c[d++];
+          sel_prefix = prefix | (static_cast<uint32_t>(tid * 8 + d) << shift);
+          sel_rank = rank - before;
+        }
+      }
+      mask |= 255u << shift;
+      __syncthreads();
+    }
+    const uint32_t t = sel_prefix;  // keff-th smallest ordered distance
+    for (int64_t i = tid; i < n; i += kSelThreads) {
+      if (u[i] <= t) {
+        const uint32_t at = atomicAdd(&ncand, 1u);
+        if (at < static_cast<uint32_t>(cap))
+          cand[at] = (static_cast<uint64_t>(u[i]) << 32) | id_of(i);
+      }
+    }
+    __syncthreads();
+    const int c = static_cast<int>(ncand);
+    if (c <= cap) {
+      int m = 1;
+      while (m < c) m <<= 1;
+      for (int i = c + tid; i < m; i += kSelThreads) cand[i] = kKeyMax;
+      __syncthreads();
+      bitonic_sort_keys<kSelThreads>(cand, m, tid, 0);
+      for (int i = tid; i < keff; i += kSelThreads) keys[i] = cand[i];  // keff <= c < np2 / 2
+      __syncthreads();
+      sorted_n = keff;
+    }
+  }
+  if (sorted_n == 0) {
+    // heavy ties: sort every key
+    for (int i = tid; i < np2; i += kSelThreads)
+      keys[i] = i < n ? make_key(__ldcg(row + i), id_of(i)) : kKeyMax;
     __syncthreads();
     bitonic_sort_keys<kSelThreads>(keys, np2, tid, 0);
   }
