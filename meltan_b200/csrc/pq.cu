@@ -308,7 +308,9 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
     if (p.metric == kL2 && p.sub == 8) {
       // the common shape (d/m = 8): two 16-byte codebook loads per entry and
       // the subspace's residual from shared memory (one subspace per warp
-      // step, so a broadcast); same operations in the same order as lut_entry
+      // step, so a broadcast); same operations in the same order as lut_entry.
+      // Unrolled so that several entries' codebook loads are in flight.
+#pragma unroll 4
       for (int e = tid; e < p.m * p.ks; e += kAdcThreads) {
         const int s = e / p.ks;
         const float4* c4 = reinterpret_cast<const float4*>(cb + static_cast<int64_t>(e) * 8);
@@ -333,14 +335,43 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
     __syncthreads();
     if (WARP_TOPK) {
       uint64_t best = kKeyMax;  // lane i: this warp's (i+1)-th smallest key
+      // m = 16: one 16-byte code row per lane, the next batch's row (and list
+      // position) loaded before the current one is scored
+      const bool wide = p.m == 16;
+      const uint4* crow = reinterpret_cast<const uint4*>(p.codes + off * 16);
+      auto fetch = [&](int64_t e, uint4& w, uint32_t& ps) {
+        if (wide && e < len) {
+          w = __ldg(crow + e);
+          ps = p.pos ? __ldg(p.pos + off + e) : static_cast<uint32_t>(e);
+        }
+      };
+      uint4 w = make_uint4(0u, 0u, 0u, 0u);
+      uint32_t ps = 0;
+      fetch(static_cast<int64_t>(warp) * 32 + lane, w, ps);
       for (int64_t b = static_cast<int64_t>(warp) * 32; b < len; b += kAdcThreads) {
         const int64_t e = b + lane;
+        uint4 wn = w;
+        uint32_t psn = ps;
+        fetch(e + kAdcThreads, wn, psn);
         uint64_t key = kKeyMax;
         if (e < len) {
-          const float total = adc_sum(lut, p.ks, p.codes + (off + e) * p.m, p.m);
-          const uint32_t pos = p.pos ? p.pos[off + e] : static_cast<uint32_t>(e);
+          float total;
+          uint32_t pos;
+          if (wide) {
+            const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+            total = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              total = __fadd_rn(total, lut[j * p.ks + ((words[j >> 2] >> (8 * (j & 3))) & 0xFFu)]);
+            pos = ps;
+          } else {
+            total = adc_sum(lut, p.ks, p.codes + (off + e) * p.m, p.m);
+            pos = p.pos ? p.pos[off + e] : static_cast<uint32_t>(e);
+          }
           key = make_key(total, (static_cast<uint32_t>(pr) << kPosBits) | pos);
         }
+        w = wn;
+        ps = psn;
         const uint64_t kth = __shfl_sync(0xFFFFFFFFu, best, p.k - 1);
         uint32_t pass = __ballot_sync(0xFFFFFFFFu, key < kth);
         if (__popc(pass) > 6) {
