@@ -192,6 +192,23 @@ __device__ __forceinline__ void bitonic_sort_keys(uint64_t* a, int n, int tid, i
   }
 }
 
+// ---- warp sort of one key per lane -------------------------------------------------
+
+__device__ __forceinline__ uint64_t key_min(uint64_t a, uint64_t b) { return a < b ? a : b; }
+__device__ __forceinline__ uint64_t key_max(uint64_t a, uint64_t b) { return a < b ? b : a; }
+
+// Ascending bitonic sort of one key per lane.
+__device__ __forceinline__ uint64_t warp_sort32(uint64_t x, int lane) {
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1)
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const uint64_t y = __shfl_xor_sync(0xFFFFFFFFu, x, j);
+      x = (((lane & j) == 0) == ((lane & k) == 0)) ? key_min(x, y) : key_max(x, y);
+    }
+  return x;
+}
+
 // Running top-k of one query inside a thread block:
 //   buf[0, kp)      -- the current best keys (ascending, `nbest` of them valid)
 //   buf[kp, sortn)  -- an append queue of candidates below the threshold

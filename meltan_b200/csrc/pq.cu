@@ -231,21 +231,6 @@ __device__ __forceinline__ float adc_sum(const float* lut, int ks, const uint8_t
 
 // ---- warp-resident top-k of (score, seq) keys (at most 32 kept) ----------------
 
-__device__ __forceinline__ uint64_t key_min(uint64_t a, uint64_t b) { return a < b ? a : b; }
-__device__ __forceinline__ uint64_t key_max(uint64_t a, uint64_t b) { return a < b ? b : a; }
-
-// Ascending bitonic sort of one key per lane.
-__device__ __forceinline__ uint64_t warp_sort32(uint64_t x, int lane) {
-#pragma unroll
-  for (int k = 2; k <= 32; k <<= 1)
-#pragma unroll
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      const uint64_t y = __shfl_xor_sync(0xFFFFFFFFu, x, j);
-      x = (((lane & j) == 0) == ((lane & k) == 0)) ? key_min(x, y) : key_max(x, y);
-    }
-  return x;
-}
-
 // The 32 smallest of two ascending lane-sorted lists, ascending: the lane-wise
 // minimum of t and x reversed is a bitonic sequence holding them, which a
 // half-cleaner cascade sorts.

@@ -1380,11 +1380,17 @@ __global__ void __launch_bounds__(kRerankThreads) tc_rerank_kernel(const RerankP
       }
       __syncthreads();
     }
-    int mp = 1;
-    while (mp < m) mp <<= 1;
-    for (int i = m + tid; i < mp; i += kRerankThreads) ekeys[i] = kKeyMax;
-    __syncthreads();
-    bitonic_sort_keys<kRerankThreads>(ekeys, mp, tid, 0);
+    if (m <= 32) {
+      // the usual band (about k rows): one warp sorts it by shuffles
+      if (tid < 32) ekeys[tid] = warp_sort32(tid < m ? ekeys[tid] : kKeyMax, tid);
+      __syncthreads();
+    } else {
+      int mp = 1;
+      while (mp < m) mp <<= 1;
+      for (int i = m + tid; i < mp; i += kRerankThreads) ekeys[i] = kKeyMax;
+      __syncthreads();
+      bitonic_sort_keys<kRerankThreads>(ekeys, mp, tid, 0);
+    }
     const int have = min(m, p.k);
     for (int i = tid; i < p.kout; i += kRerankThreads) {
       p.out_dist[q * p.kout + i] = i < have ? key_distance(ekeys[i]) : __int_as_float(0x7F800000);
