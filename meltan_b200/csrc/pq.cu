@@ -379,7 +379,8 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
       __syncthreads();
       if (warp == 0) {
 #pragma unroll
-        for (int w = 1; w < kAdcThreads / 32; ++w) best = warp_merge32(best, wlist[w][lane], lane);
+        for (int ow = 1; ow < kAdcThreads / 32; ++ow)
+          best = warp_merge32(best, wlist[ow][lane], lane);
         const int have = static_cast<int>(len < p.k ? len : p.k);
         if (lane < have) p.slot_keys[it * p.kp + lane] = best;
         if (lane == 0) p.slot_counts[it] = have;

@@ -262,6 +262,7 @@ int32_t run_small_batch_search(mans_ctx* ctx, const mans_corpus* corpus, mans_wo
   const int64_t sld = (n + 3) / 4 * 4;
   int64_t chunk = static_cast<int64_t>(kScoreBudget / (static_cast<size_t>(sld) * sizeof(float)));
   chunk = std::max<int64_t>(kSsQ, chunk / kSsQ * kSsQ);
+  chunk = std::min<int64_t>(chunk, 65535ll * kSsQ);  // query tiles fit grid.y
   chunk = std::min<int64_t>(chunk, (nq + kSsQ - 1) / kSsQ * kSsQ);
   int32_t rc = ws->small_scores.reserve(static_cast<size_t>(chunk) * sld * sizeof(float));
   if (rc != MANS_OK) return rc;
