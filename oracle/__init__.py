@@ -67,6 +67,18 @@ def lib():
                                        _I64, _U32, _F, C.c_int64, C.c_int32, C.c_int32, C.c_int32,
                                        _F, _U32, _I32]
         L.orc_pq_adc.argtypes = [_F, C.c_int32, C.c_int32, _U8, C.c_int64, _F]
+        _I8 = C.POINTER(C.c_int8)
+        L.orc_i8_dot_rows.argtypes = [_I8, _I8, C.c_int64, C.c_int64, _F]
+        L.orc_dot_rows_gather.argtypes = [_F, _F, _U32, C.c_int64, C.c_int64, _F]
+        L.orc_int8_planes.argtypes = [_F, C.c_int64, C.c_int64, _I8, _F, _F, _F, _F]
+        L.orc_bounded_exact_scan.argtypes = [_F, _F, _F, C.c_float, C.c_int64, C.c_int64,
+                                             C.c_int32, C.c_int32, C.c_int32, _I8, _F, _F, _F,
+                                             _F, C.c_void_p, C.c_void_p, _F, _U32]
+        L.orc_bounded_exact_scan.restype = C.c_int
+        L.orc_bounded_exact_batch.argtypes = [_F, C.c_int64, _F, _F, _F, C.c_int64, C.c_int64,
+                                              C.c_int32, C.c_int32, C.c_int32, C.c_int32, _I8,
+                                              _F, _F, _F, _F, C.c_void_p, C.c_void_p, C.c_int32,
+                                              _F, _U32, _I32]
         _lib = L
     return _lib
 
@@ -298,4 +310,62 @@ def ivfpq_search(coarse, codebooks, codes, list_offsets, lists, queries, k, npro
     lib().orc_ivfpq_search(_p(coarse, _F), nlist, d, _p(codebooks, _F), m, ks, _p(codes, _U8),
                            _p(list_offsets, _I64), _p(lists, _U32), _p(queries, _F), nq, k, nprobe,
                            metric, _p(od, _F), _p(oi, _U32), _p(oc, _I32))
+    return od, oi, oc
+
+
+# ---- BoundedExactScan (the reference's CPU batch route) ---------------------
+
+_I8P = C.POINTER(C.c_int8)
+
+
+def slice_count(n, cores):
+    """ParallelFlatScan.sliceCount: max(1, min(cores, 32, n / 2048))."""
+    return max(1, min(cores, 32, n // 2048))
+
+
+def int8_planes(rows):
+    """Int8CodeBuffer.fill: (codes n x d int8, u, w, |v|^2, 1/|v|) planes."""
+    rows = f32(rows)
+    n, d = rows.shape
+    codes = np.empty((n, d), np.int8)
+    u, w, nsq, inv = (np.empty(n, np.float32) for _ in range(4))
+    lib().orc_int8_planes(_p(rows, _F), n, d, _p(codes, _I8P), _p(u, _F), _p(w, _F),
+                          _p(nsq, _F), _p(inv, _F))
+    return codes, u, w, nsq, inv
+
+
+def _ref_bounded_fns(use_reference_dots):
+    if not use_reference_dots:
+        return None, None
+    R = ref_lib()
+    if R is None:
+        return None, None
+    return (C.cast(R.mans_i8_dot_rows_f32, C.c_void_p).value,
+            C.cast(R.mans_f32_dot_rows_gather, C.c_void_p).value)
+
+
+def bounded_exact_batch(corpus, planes, queries, k, metric, threads, cores=None, norms=None,
+                        use_reference_dots=True):
+    """FlatGPUSearch's CPU batch route at n >= 16384: BoundedExactScan per
+    query, queries spread over `threads` workers.  Returns (dist[nq, k'],
+    ids, counts) with k' = min(k, n); a count of -1 marks a declined query."""
+    corpus, queries = f32(corpus), f32(np.atleast_2d(queries))
+    n, d = corpus.shape
+    nq = queries.shape[0]
+    if norms is None and metric in (COSINE, L2):
+        norms = row_norms(corpus)
+    qn = (np.array([norm_sq(x) for x in queries], np.float32) if metric in (COSINE, L2)
+          else np.zeros(nq, np.float32))
+    codes, u, w, nsq, inv = planes
+    kout = max(1, min(k, n))
+    od = np.full((nq, kout), np.inf, np.float32)
+    oi = np.full((nq, kout), 0xFFFFFFFF, np.uint32)
+    oc = np.empty(nq, np.int32)
+    i8fn, gfn = _ref_bounded_fns(use_reference_dots)
+    npn = None if norms is None else f32(norms)
+    lib().orc_bounded_exact_batch(
+        _p(queries, _F), nq, _p(qn, _F), _p(corpus, _F), None if npn is None else _p(npn, _F),
+        n, d, k, metric, slice_count(n, cores or os.cpu_count() or 1), threads,
+        _p(codes, _I8P), _p(u, _F), _p(w, _F), _p(nsq, _F), _p(inv, _F), i8fn, gfn, kout,
+        _p(od, _F), _p(oi, _U32), _p(oc, _I32))
     return od, oi, oc

@@ -828,3 +828,346 @@ void orc_pq_adc(const float *lut, int32_t m, int32_t ks, const uint8_t *codes, i
         out[i] = total;
     }
 }
+
+/* ------------------------------------------------------------------------ */
+/* BoundedExactScan: the int8-prefiltered exact scan of the CPU batch route   */
+/* (Sources/MetalANNSCore/BoundedExactScan.swift, Int8CodeCache.swift,        */
+/* FlatGPUSearch.swift:754-779,1024-1035)                                     */
+/* ------------------------------------------------------------------------ */
+
+typedef void (*orc_i8_dot_rows_fn)(const int8_t *codes, const int8_t *query_codes, int64_t rows,
+                                   int64_t dim, float *out);
+typedef void (*orc_dot_gather_fn)(const float *corpus, const float *query, const uint32_t *ids,
+                                  int64_t count, int64_t dim, float *out);
+
+/* Portable branch of mans_i8_dot_rows_f32 (dots.c:50-88): exact int32 sum,
+ * one conversion to fp32. */
+void orc_i8_dot_rows(const int8_t *codes, const int8_t *query_codes, int64_t rows, int64_t dim,
+                     float *out) {
+    for (int64_t r = 0; r < rows; ++r) {
+        const int8_t *row = codes + r * dim;
+        int32_t total = 0;
+        for (int64_t d = 0; d < dim; ++d) total += (int32_t)row[d] * (int32_t)query_codes[d];
+        out[r] = (float)total;
+    }
+}
+
+/* Scalar branch of mans_f32_dot_rows_gather (dots.c:90-125). */
+void orc_dot_rows_gather(const float *corpus, const float *query, const uint32_t *ids,
+                         int64_t count, int64_t dim, float *out) {
+    for (int64_t i = 0; i < count; ++i) {
+        const float *row = corpus + (int64_t)ids[i] * dim;
+        float acc = 0.0f;
+        for (int64_t d = 0; d < dim; ++d) {
+            float p = row[d] * query[d];
+            acc = acc + p;
+        }
+        out[i] = acc;
+    }
+}
+
+/* Int8CodeBuffer.fill (Int8CodeCache.swift:64-99): the codes of orc_int8_fill
+ * plus the planes u = scale, w = scale * eBase with eBase = (|c|_1 / 2 +
+ * dim / 4) * (1 + 1e-6) + 16, the sequential fp32 |v|^2 and 1 / sqrt(|v|^2)
+ * (0 below 1e-20); every step in fp32. */
+void orc_int8_planes(const float *rows, int64_t n, int64_t dim, int8_t *codes, float *u,
+                     float *w, float *norm_sq, float *inv_sqrt) {
+    for (int64_t r = 0; r < n; ++r) {
+        const float *v = rows + r * dim;
+        float max_abs = 0.0f;
+        for (int64_t d = 0; d < dim; ++d) {
+            float a = fabsf(v[d]);
+            if (a > max_abs) max_abs = a;
+        }
+        float scale = max_abs > 0.0f ? max_abs / 127.0f : 1.0f;
+        float inverse = 1.0f / scale;
+        int32_t abs_sum = 0;
+        float nsq = 0.0f;
+        for (int64_t d = 0; d < dim; ++d) {
+            float value = v[d];
+            float p = value * value;
+            nsq = nsq + p;
+            float scaled = value * inverse;
+            float shifted = scaled >= 0.0f ? scaled + 0.5f : scaled - 0.5f;
+            int32_t rounded = (int32_t)shifted;
+            if (rounded > 127) rounded = 127;
+            else if (rounded < -127) rounded = -127;
+            codes[r * dim + d] = (int8_t)rounded;
+            abs_sum += rounded < 0 ? -rounded : rounded;
+        }
+        float ebase = ((float)abs_sum / 2.0f + (float)dim / 4.0f) * (1.0f + 1e-6f) + 16.0f;
+        u[r] = scale;
+        w[r] = scale * ebase;
+        norm_sq[r] = nsq;
+        inv_sqrt[r] = nsq > 1e-20f ? 1.0f / sqrtf(nsq) : 0.0f;
+    }
+}
+
+typedef struct {
+    float key;
+    uint32_t id;
+} bes_entry;
+
+/* admit / siftUpHeap / siftDownHeap (BoundedExactScan.swift:238-276): a
+ * key-only max-heap, a newcomer replaces the root only when strictly lower. */
+static void bes_sift_down(bes_entry *h, int pos, int size) {
+    for (;;) {
+        int l = 2 * pos + 1, r = l + 1, big = pos;
+        if (l < size && h[l].key > h[big].key) big = l;
+        if (r < size && h[r].key > h[big].key) big = r;
+        if (big == pos) return;
+        bes_entry t = h[pos];
+        h[pos] = h[big];
+        h[big] = t;
+        pos = big;
+    }
+}
+
+static void bes_admit(bes_entry *h, int *count, int cap, float key, uint32_t id) {
+    if (*count < cap) {
+        int pos = (*count)++;
+        h[pos].key = key;
+        h[pos].id = id;
+        while (pos > 0) {
+            int parent = (pos - 1) / 2;
+            if (h[pos].key > h[parent].key) {
+                bes_entry t = h[pos];
+                h[pos] = h[parent];
+                h[parent] = t;
+                pos = parent;
+            } else {
+                break;
+            }
+        }
+    } else if (key < h[0].key) {
+        h[0].key = key;
+        h[0].id = id;
+        bes_sift_down(h, 0, *count);
+    }
+}
+
+/* heapSortedAscending (:279-288). */
+static void bes_sorted_ascending(bes_entry *h, int count) {
+    while (count > 1) {
+        bes_entry t = h[0];
+        h[0] = h[count - 1];
+        h[count - 1] = t;
+        count -= 1;
+        bes_sift_down(h, 0, count);
+    }
+}
+
+static int cmp_entry(const void *a, const void *b) {
+    const orc_entry *x = (const orc_entry *)a, *y = (const orc_entry *)b;
+    if (x->d < y->d) return -1;
+    if (y->d < x->d) return 1;
+    return x->id < y->id ? -1 : (x->id > y->id ? 1 : 0);
+}
+
+/* BoundedExactScan.search (:30-122) for one query, its slices run in turn
+ * (the caller parallelises over queries, as parallelHostBatchSearch does).
+ * The query is quantised in double (:52-64); each slice ranks its rows by the
+ * metric's lower-bound key (:178-228, same operation order and types) in a
+ * heap of min(budget, chunk); the slices' ascending lists are merged
+ * (:290-316, lowest slice first on equal keys) into `budget` candidates whose
+ * last key is the cutoff; the candidates are rescored in fp32 with the
+ * ParallelFlatScan formulas (:320-369) and sorted; the result is proven when
+ * cutoff >= tau + max(1e-7, |tau| 1e-6) (tau = k-th rescored distance) or
+ * every row is a candidate, else the budget grows x4.  Swift's sort of the
+ * rescored entries is unstable; here equal distances order by id.
+ * Returns the count written, or -1 where the reference returns nil (fewer
+ * than 16384 rows, hamming, or missing norms for cosine / L2). */
+int orc_bounded_exact_scan(const float *query, const float *corpus, const float *norms, float qn,
+                           int64_t n, int64_t dim, int32_t topk, int32_t metric, int32_t slices_in,
+                           const int8_t *codes, const float *u, const float *w,
+                           const float *norm_sq, const float *inv_sqrt, orc_i8_dot_rows_fn i8dot,
+                           orc_dot_gather_fn gather, float *out_d, uint32_t *out_i) {
+    if (n < 16384 || dim <= 0 || topk <= 0 || metric == ORC_HAMMING) return -1;
+    if ((metric == ORC_COSINE || metric == ORC_L2) && !norms) return -1;
+    if (!i8dot) i8dot = orc_i8_dot_rows;
+    if (!gather) gather = orc_dot_rows_gather;
+    int k = (int64_t)topk < n ? topk : (int)n;
+    float qmax = 0.0f;
+    for (int64_t d = 0; d < dim; ++d) {
+        float a = fabsf(query[d]);
+        if (a > qmax) qmax = a;
+    }
+    double qscale = qmax > 0.0f ? (double)qmax / 127.0 : 1.0;
+    int8_t *qc = (int8_t *)malloc((size_t)dim);
+    int64_t qabs = 0;
+    for (int64_t d = 0; d < dim; ++d) {
+        double scaled = (double)query[d] / qscale;
+        int32_t r = (int32_t)(scaled >= 0 ? scaled + 0.5 : scaled - 0.5);
+        if (r > 127) r = 127;
+        else if (r < -127) r = -127;
+        qc[d] = (int8_t)r;
+        qabs += r < 0 ? -r : r;
+    }
+    const float qs = (float)qscale;
+    const float qabs_half = (float)qabs / 2.0f;
+    const float qs_dot = qs, qs_w = qs, qs_qh = qs * qabs_half;
+    const float inv_q = qn > 1e-20f ? 1.0f / sqrtf(qn) : 0.0f;
+    const float cos_dot = qs * inv_q, cos_h = qs * qabs_half * inv_q, cos_w = qs * inv_q;
+    const double qn_d = (double)qn;
+    const float two_dot = 2.0f * qs_dot, two_qh = 2.0f * qs_qh, two_w = 2.0f * qs_w;
+
+    int64_t slices = slices_in > 0 ? slices_in : 1;
+    int64_t chunk = (n + slices - 1) / slices;
+    float *dots = (float *)malloc(sizeof(float) * (size_t)(slices * chunk));
+    int64_t budget = k * 16 > 256 ? (int64_t)k * 16 : 256;
+    int result = -1;
+    for (;;) {
+        /* selectCandidates recomputes the slice dots every round (:154-172) */
+        for (int64_t s = 0; s < slices; ++s) {
+            int64_t start = s * chunk, end = start + chunk < n ? start + chunk : n;
+            if (start < end) i8dot(codes + start * dim, qc, end - start, dim, dots + start);
+        }
+        int64_t per = budget < chunk ? budget : chunk;
+        bes_entry *heaps = (bes_entry *)malloc(sizeof(bes_entry) * (size_t)(slices * per));
+        int *cnt = (int *)calloc((size_t)slices, sizeof(int));
+        for (int64_t s = 0; s < slices; ++s) {
+            int64_t start = s * chunk, end = start + chunk < n ? start + chunk : n;
+            bes_entry *h = heaps + s * per;
+            for (int64_t r = start; r < end; ++r) {
+                float key;
+                if (metric == ORC_IP) {
+                    float a = qs_dot * u[r] * dots[r];
+                    float b = qs_qh * u[r];
+                    float c = qs_w * w[r];
+                    key = -(a + b + c);
+                } else if (metric == ORC_L2) {
+                    double t = qn_d + (double)norm_sq[r];
+                    t = t - (double)(two_dot * u[r] * dots[r]);
+                    t = t - (double)(two_qh * u[r]);
+                    t = t - (double)(two_w * w[r]);
+                    key = (float)t;
+                } else {
+                    float a = cos_dot * u[r] * dots[r];
+                    float b = cos_h * u[r];
+                    float c = cos_w * w[r];
+                    float inner = a + b + c;
+                    key = 1.0f - inner * inv_sqrt[r];
+                }
+                bes_admit(h, &cnt[s], (int)per, key, (uint32_t)r);
+            }
+            bes_sorted_ascending(h, cnt[s]);
+        }
+        /* mergeAscending */
+        uint32_t *ids = (uint32_t *)malloc(sizeof(uint32_t) * (size_t)budget);
+        int *cur = (int *)calloc((size_t)slices, sizeof(int));
+        int64_t taken = 0;
+        double cutoff = INFINITY;
+        while (taken < budget) {
+            int best = -1;
+            float best_key = INFINITY;
+            for (int64_t s = 0; s < slices; ++s)
+                if (cur[s] < cnt[s] && heaps[s * per + cur[s]].key < best_key) {
+                    best_key = heaps[s * per + cur[s]].key;
+                    best = (int)s;
+                }
+            if (best < 0) break;
+            ids[taken++] = heaps[(int64_t)best * per + cur[best]].id;
+            cutoff = (double)best_key;
+            cur[best] += 1;
+        }
+        /* rescore */
+        float *rd = (float *)malloc(sizeof(float) * (size_t)(taken > 0 ? taken : 1));
+        orc_entry *ent = (orc_entry *)malloc(sizeof(orc_entry) * (size_t)(taken > 0 ? taken : 1));
+        if (taken > 0) gather(corpus, query, ids, taken, dim, rd);
+        for (int64_t i = 0; i < taken; ++i) {
+            float vn = norms ? norms[ids[i]] : 0.0f;
+            ent[i].d = orc_distance(metric, rd[i], qn, vn);
+            ent[i].id = ids[i];
+        }
+        qsort(ent, (size_t)taken, sizeof(orc_entry), cmp_entry);
+        int done = 0;
+        if (taken < k) {
+            for (int64_t i = 0; i < taken; ++i) {
+                out_d[i] = ent[i].d;
+                out_i[i] = ent[i].id;
+            }
+            result = (int)taken;
+            done = 1;
+        } else {
+            double tau = (double)ent[k - 1].d;
+            double margin = fabs(tau) * 1e-6 > 1e-7 ? fabs(tau) * 1e-6 : 1e-7;
+            if (cutoff >= tau + margin || taken >= n) {
+                for (int i = 0; i < k; ++i) {
+                    out_d[i] = ent[i].d;
+                    out_i[i] = ent[i].id;
+                }
+                result = k;
+                done = 1;
+            }
+        }
+        free(ent);
+        free(rd);
+        free(cur);
+        free(ids);
+        free(cnt);
+        free(heaps);
+        if (done || budget >= n) break;
+        budget = budget * 4 < n ? budget * 4 : n;
+    }
+    free(dots);
+    free(qc);
+    return result;
+}
+
+typedef struct {
+    const float *queries, *corpus, *norms, *qnorms;
+    int64_t n, dim, nq;
+    int32_t topk, metric, slices, kout, stride;
+    const int8_t *codes;
+    const float *u, *w, *norm_sq, *inv_sqrt;
+    orc_i8_dot_rows_fn i8dot;
+    orc_dot_gather_fn gather;
+    float *out_d;
+    uint32_t *out_i;
+    int32_t *out_c;
+    int t;
+} bes_work;
+
+static void *bes_thread(void *arg) {
+    bes_work *b = (bes_work *)arg;
+    for (int64_t q = b->t; q < b->nq; q += b->stride) {
+        int c = orc_bounded_exact_scan(b->queries + q * b->dim, b->corpus, b->norms,
+                                       b->qnorms ? b->qnorms[q] : 0.0f, b->n, b->dim, b->topk,
+                                       b->metric, b->slices, b->codes, b->u, b->w, b->norm_sq,
+                                       b->inv_sqrt, b->i8dot, b->gather, b->out_d + q * b->kout,
+                                       b->out_i + q * b->kout);
+        b->out_c[q] = c;
+    }
+    return NULL;
+}
+
+/* parallelHostBatchSearch (FlatGPUSearch.swift:754-779) over the bounded
+ * scan: queries spread over `threads` workers, each query's slices run by
+ * its worker.  out_* are nq x kout (kout >= min(topk, n)); counts of -1 mark
+ * queries the bounded scan declines. */
+void orc_bounded_exact_batch(const float *queries, int64_t nq, const float *qnorms,
+                             const float *corpus, const float *norms, int64_t n, int64_t dim,
+                             int32_t topk, int32_t metric, int32_t slices, int32_t threads,
+                             const int8_t *codes, const float *u, const float *w,
+                             const float *norm_sq, const float *inv_sqrt, orc_i8_dot_rows_fn i8dot,
+                             orc_dot_gather_fn gather, int32_t kout, float *out_d, uint32_t *out_i,
+                             int32_t *out_c) {
+    if (threads < 1) threads = 1;
+    if (threads > nq) threads = (int32_t)(nq > 0 ? nq : 1);
+    bes_work *work = (bes_work *)malloc(sizeof(bes_work) * (size_t)threads);
+    pthread_t *th = (pthread_t *)malloc(sizeof(pthread_t) * (size_t)threads);
+    for (int t = 0; t < threads; ++t) {
+        bes_work b = {queries, corpus, norms, qnorms, n, dim, nq, topk, metric, slices, kout,
+                      threads, codes, u, w, norm_sq, inv_sqrt, i8dot, gather, out_d, out_i,
+                      out_c, t};
+        work[t] = b;
+    }
+    if (threads == 1) {
+        bes_thread(&work[0]);
+    } else {
+        for (int t = 0; t < threads; ++t) pthread_create(&th[t], NULL, bes_thread, &work[t]);
+        for (int t = 0; t < threads; ++t) pthread_join(th[t], NULL);
+    }
+    free(th);
+    free(work);
+}

@@ -43,6 +43,16 @@ def test_reference_arm_flat_line():
     assert d["steps"] == 2 and d["warmup"] == 1
 
 
+def test_reference_arm_batch_takes_the_bounded_route():
+    """Batches over n >= 16384 take the reference's CPU batch route
+    (BoundedExactScan per query, queries in parallel)."""
+    lines = run_bench(["--impl", "reference", "--n", "20000", "--dim", "32", "--nq", "8",
+                       "--steps", "1", "--warmup", "0"])
+    assert len(lines) == 1
+    d = check_line(lines[0], "exact_flat_20000x32_cosine_top10_nq8")
+    assert "BoundedExactScan" in d["cpu_baseline"]["sample"]
+
+
 @pytest.mark.parametrize("workload,extra", [
     ("ivf", []),
     ("ivfpq", ["--pq-m", "8"]),
