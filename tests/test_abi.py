@@ -49,3 +49,46 @@ def test_errors_map_to_reference_degradeable_set():
     assert mb.GPUPipelineUnavailable("x").is_tier_degradeable
     assert not mb.DimensionMismatch("x").is_tier_degradeable
     assert not mb.ConstructionFailed("x").is_tier_degradeable
+
+
+def test_plain_c_client_compiles_links_and_runs(tmp_path):
+    """The header is plain C: a C11 client that takes the address of every
+    declared entry point compiles warning-free with gcc, links against
+    libmans_cuda.so and, without a GPU, gets MANS_ERR_DEVICE and a message
+    from mans_ctx_create -- what a cgo / Swift / ctypes binding relies on."""
+    import shutil
+    import subprocess
+
+    import torch
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    names = _declared()
+    src = tmp_path / "client.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <string.h>\n#include "mans_cuda.h"\n'
+        "typedef void (*fnp)(void);\n"
+        "static fnp entry_points[] = {\n"
+        + "".join(f"    (fnp){n},\n" for n in names)
+        + "};\n"
+        "int main(void) {\n"
+        "    for (size_t i = 0; i < sizeof entry_points / sizeof entry_points[0]; ++i)\n"
+        "        if (!entry_points[i]) return 10;\n"
+        "    mans_ctx *ctx = NULL;\n"
+        "    int32_t rc = mans_ctx_create(0, &ctx);\n"
+        "    char msg[256] = {0};\n"
+        "    mans_last_error_message(msg, sizeof msg);\n"
+        '    printf("%d %s\\n", (int)rc, msg);\n'
+        "    if (rc == MANS_OK) { mans_ctx_destroy(ctx); return 0; }\n"
+        "    return rc == MANS_ERR_DEVICE && strlen(msg) > 0 ? 0 : 11;\n"
+        "}\n")
+    lib_dir = os.path.join(ROOT, "meltan_b200")
+    exe = tmp_path / "client"
+    cc = subprocess.run(["gcc", "-std=c11", "-Wall", "-Wextra", "-Werror", "-Wno-cast-function-type",
+                         "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe),
+                         "-L", lib_dir, "-lmans_cuda", f"-Wl,-rpath,{lib_dir}"],
+                        capture_output=True, text=True)
+    assert cc.returncode == 0, cc.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert run.returncode == 0, run.stdout + run.stderr
+    if not torch.cuda.is_available():
+        assert run.stdout.startswith("7 "), run.stdout  # MANS_ERR_DEVICE
