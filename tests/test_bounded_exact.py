@@ -87,3 +87,88 @@ def test_reference_dots_give_the_same_answer():
     b = O.bounded_exact_batch(v, planes, q, 10, O.COSINE, threads=2, use_reference_dots=False)
     for x, y in zip(a, b):
         np.testing.assert_array_equal(x, y)
+
+
+# ---- the cases of Tests/MetalANNSTests/BoundedExactScanTests.swift, on the
+# oracle's restatement (data from its seeded generator, restated as
+# oracle.lcg32_vectors) ------------------------------------------------------
+
+CORPUS = 16384 + 512  # BoundedExactScanTests.corpusSize
+MET = (O.COSINE, O.L2, O.IP)
+
+
+@pytest.mark.parametrize("dim", [384, 128, 333, 16])
+@pytest.mark.parametrize("seed", [7, 99])
+def test_reference_cases_across_metrics_dims_seeds(dim, seed):
+    """exactAcrossMetricsDimsAndSeeds (:176-208)."""
+    v = O.lcg32_vectors(CORPUS, dim, seed)
+    q = O.lcg32_vectors(4, dim, seed + 123)
+    planes = O.int8_planes(v)
+    for metric in MET:
+        for k in (1, 24, 97):
+            same(O.bounded_exact_batch(v, planes, q, k, metric, threads=4),
+                 O.flat_search(v, q, k, metric), k)
+
+
+def test_reference_case_adversarial_rows():
+    """adversarialDataStaysExact (:212-250): quarter zero rows, quarter
+    copies of one row, the rest spread over magnitudes 1e-5 .. 1e5."""
+    dim = 64
+    nrand = sum(1 for row in range(CORPUS) if row % 4 >= 2)
+    draws = O.lcg32_vectors(1 + nrand + 1, dim, 2024)
+    v = np.empty((CORPUS, dim), np.float32)
+    j = 1
+    for row in range(CORPUS):
+        m = row % 4
+        if m == 0:
+            v[row] = 0.0
+        elif m == 1:
+            v[row] = draws[0]
+        else:
+            mag = (np.float32(1e-5) if row % 8 == 0 else
+                   (np.float32(1e5) if row % 8 == 4 else np.float32(1)))
+            v[row] = draws[j] * mag
+            j += 1
+    q = draws[j:j + 1].copy()
+    planes = O.int8_planes(v)
+    for metric in MET:
+        for k in (24, 256):
+            same(O.bounded_exact_batch(v, planes, q, k, metric, threads=2),
+                 O.flat_search(v, q, k, metric), k)
+
+
+def test_reference_cases_zero_query_and_large_k():
+    """zeroQueryStaysExact (:253-274) and largeKMultiRoundGrowthStaysExact
+    (:277-303)."""
+    v = O.lcg32_vectors(CORPUS, 96, 31)
+    zq = np.zeros((1, 96), np.float32)
+    planes = O.int8_planes(v)
+    for metric in MET:
+        same(O.bounded_exact_batch(v, planes, zq, 24, metric, threads=1),
+             O.flat_search(v, zq, 24, metric), 24)
+    v = O.lcg32_vectors(CORPUS, 384, 55)
+    q = O.lcg32_vectors(1, 384, 77)
+    planes = O.int8_planes(v)
+    for metric in MET:
+        for k in (97, 256):
+            same(O.bounded_exact_batch(v, planes, q, k, metric, threads=1),
+                 O.flat_search(v, q, k, metric), k)
+
+
+def test_reference_case_tail_rows_are_covered():
+    """sliceCoverageCoversEntireCorpus (:355-393): targets in the last rows
+    of a 4 x 16384-row corpus, perturbed so they are the strict nearest."""
+    dim, count = 64, 4 * 16384
+    v = O.lcg32_vectors(count, dim, 404)
+    targets = [count - 1, count - 7, count // 2 + 3]
+    queries = [v[t].copy() for t in targets]
+    noise = O.lcg32_vectors(2 * len(targets), dim, 405)
+    for i, t in enumerate(targets):
+        v[t] = v[t] + noise[i] * np.float32(1e-3)
+    q = np.stack([queries[i] + noise[len(targets) + i] * np.float32(1e-3)
+                  for i in range(len(targets))]).astype(np.float32)
+    planes = O.int8_planes(v)
+    got = O.bounded_exact_batch(v, planes, q, 5, O.L2, threads=3)
+    want = O.flat_search(v, q, 5, O.L2)
+    same(got, want, 5)
+    np.testing.assert_array_equal(got[1][:, 0], targets)
