@@ -360,10 +360,12 @@ int32_t mans_ivfpq_search_device(mans_ctx *ctx, mans_ivfpq *ix, mans_workspace *
                                  float *d_out_dist, uint32_t *d_out_ids, int32_t *d_out_counts,
                                  void *cuda_stream);
 
-/* Row shards of one IVF-PQ index (one process per GPU; every shard holds the
- * same coarse centroids and codebooks, its rows' codes, and for each list
+/* Shards of one IVF-PQ index (one process per GPU; every shard holds the
+ * same coarse centroids and codebooks, its entries' codes, and for each list
  * entry its position in the global list, `list_positions` of
- * mans_ivfpq_create).  Each shard writes a packed block of nq*(3*kin + 1)
+ * mans_ivfpq_create).  A shard may hold row ranges (entries of every list)
+ * or whole lists (the other lists empty: their distance tables are never
+ * built, so the table work divides over the shards).  Each shard writes a packed block of nq*(3*kin + 1)
  * int32 words, kin = 2*min(k, 256): [scores | sequences | internal ids |
  * counts], its (score, insertion sequence) 2k-smallest candidates; after an
  * all-gather, mans_ivfpq_resolve_device merges the blocks (block r at
