@@ -54,6 +54,8 @@ def parse():
                     help="batches of at least this many queries use the tensor-core path")
     ap.add_argument("--no-also", action="store_true",
                     help="skip the extra measurements reported under `also`")
+    ap.add_argument("--no-index", action="store_true",
+                    help="skip the IVF-flat / IVF-PQ lines of the default flat run")
     ap.add_argument("--also-nq", default="32,1024",
                     help="comma-separated batch sizes of the extra flat measurements")
     ap.add_argument("--workload", default="flat", choices=["flat", "ivf", "ivfpq"],
@@ -98,11 +100,26 @@ def make_data(n, dim, nq, seed=0):
     return v, q
 
 
+# Draws of at least this many elements use torch's CUDA generator when a GPU
+# is present: numpy's single-stream generator takes minutes for 10M x 128.
+_DEVICE_DRAW_ELEMENTS = 1 << 26
+
+
 def make_mixture(n, dim, components, nq, sigma=0.3, seed=0):
     """BASELINE.json configs[2..3] generator: centres = normalise(N(0,1)),
     x = centre[assign] + sigma * N(0,1), renormalised; queries drawn from the
     same mixture after the database.  The noise is drawn in row chunks, which
-    yields the same values as one draw and bounds the temporaries."""
+    yields the same values as one draw and bounds the temporaries.  Below
+    2^26 elements (or without a GPU) the draws come from numpy
+    default_rng(seed); above, from torch's CUDA Philox generator seeded with
+    `seed` (same distribution, same values on every GPU of a run)."""
+    if n * dim >= _DEVICE_DRAW_ELEMENTS:
+        try:
+            import torch
+            if torch.cuda.is_available():
+                return _mixture_on_device(n, dim, components, nq, sigma, seed)
+        except ImportError:
+            pass
     rng = np.random.default_rng(seed)
     centres = rng.standard_normal((components, dim), dtype=np.float32)
     centres /= np.linalg.norm(centres, axis=1, keepdims=True)
@@ -118,6 +135,28 @@ def make_mixture(n, dim, components, nq, sigma=0.3, seed=0):
         return x
 
     return draw(n), draw(nq)
+
+
+def _mixture_on_device(n, dim, components, nq, sigma, seed):
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    centres = torch.randn((components, dim), generator=g, device="cuda", dtype=torch.float32)
+    centres /= centres.norm(dim=1, keepdim=True)
+
+    def draw(m):
+        out = np.empty((m, dim), np.float32)
+        for c0 in range(0, m, 1 << 21):
+            c1 = min(m, c0 + (1 << 21))
+            a = torch.randint(0, components, (c1 - c0,), generator=g, device="cuda")
+            x = centres[a] + sigma * torch.randn((c1 - c0, dim), generator=g, device="cuda",
+                                                 dtype=torch.float32)
+            x /= x.norm(dim=1, keepdim=True)
+            out[c0:c1] = x.cpu().numpy()
+        return out
+
+    v = draw(n)
+    q = draw(nq)
+    return v, q
 
 
 def train_centroids(v, nlist, iters=4, seed=42, device=None):
@@ -317,10 +356,11 @@ def committed_traffic(workload, kernel="scan"):
     return d.get(f"{workload}/{kernel}")
 
 
-def cpu_reference_qps(v, q, k, metric, seconds, max_queries=None):
-    """ParallelFlatScan (the reference CPU exact path) on the host cores."""
+def cpu_reference_qps(v, q, k, metric, seconds, max_queries=None, cores=None):
+    """ParallelFlatScan (the reference CPU exact path) on the host cores
+    (all of them unless `cores` is given)."""
     import oracle as O
-    cores = os.cpu_count() or 1
+    cores = cores or os.cpu_count() or 1
     used = min(cores, 32, max(1, v.shape[0] // 2048))  # ParallelFlatScan.sliceCount
     norms = O.row_norms(v) if metric in (0, 1) else None
     use_ref = O.ref_lib() is not None
@@ -498,23 +538,36 @@ class Runner:
             self.dist.barrier()
         self.torch.cuda.synchronize()
 
+    def _sharded(self, nq, kout):
+        sharded = self.mb.ShardedFlatSearch(self.ctx, self.buf, self.world, self.dist,
+                                            transport=self.a.transport, rank=self.rank)
+        return sharded, sharded.buffers(nq, kout)
+
+    def _host_search(self, hq_ptr, nq, h_out, kout):
+        rc = self.lib.mans_flat_search(self.ctx.handle, self.buf.handle, C.c_void_p(hq_ptr), nq,
+                                       self.a.dim, self.a.k, self.metric,
+                                       C.c_void_p(h_out.data_ptr()),
+                                       C.c_void_p(h_out[nq * kout:].data_ptr()),
+                                       C.c_void_p(h_out[2 * nq * kout:].data_ptr()))
+        self.mb.check(rc)
+
     def measure(self, q, steps, warmup, with_clocks):
+        """`q` is (P, nq, dim): step i searches batch i % P (P distinct
+        single queries for the nq = 1 line, one batch otherwise)."""
         torch, mb, a = self.torch, self.mb, self.a
-        nq = q.shape[0]
+        pool, nq = q.shape[0], q.shape[1]
         kout = min(a.k, mb.MAX_TOP_K)
-        dq = torch.from_numpy(q).cuda()
+        dq = torch.from_numpy(np.ascontiguousarray(q)).cuda()
         P = mb.shard.packed_words(nq, kout)  # packed [dist | ids | counts] per rank
-        ws, ctx, buf, sp = self.ws, self.ctx, self.buf, self.sp
-        sharded = mb.ShardedFlatSearch(ctx, buf, self.world, self.dist,
-                                       transport=self.a.transport, rank=self.rank)
-        bufs = sharded.buffers(nq, kout)
+        ws, sp = self.ws, self.sp
+        sharded, bufs = self._sharded(nq, kout)
         out = bufs[2]
 
         def step(src):
             return sharded.search_device(ws, src.data_ptr(), nq, a.k, self.metric, bufs, sp)
 
-        for _ in range(max(3, warmup)):
-            step(dq)
+        for i in range(max(3, warmup)):
+            step(dq[i % pool])
         ws.check(sp)
         ws.stats()
         ws.set_timing(True)
@@ -530,7 +583,7 @@ class Runner:
         t0.record(self.stream)
         for i in range(steps):
             ev[i][0].record(self.stream)
-            step(dq)
+            step(dq[i % pool])
             ev[i][1].record(self.stream)
         t1.record(self.stream)
         self.barrier()
@@ -539,36 +592,32 @@ class Runner:
         kern_ms, kern_launches, total_launches = ws.stats()
         ws.set_timing(False)
         path = ws.last_path()
+        fallbacks = ws.fallbacks()
         total_ms = t0.elapsed_time(t1)
         step_ms = [x.elapsed_time(y) for x, y in ev]
         device_out = out.clone()
 
         # end to end through the C ABI with pinned host buffers
-        hq = torch.from_numpy(q).pin_memory()
+        hq = torch.from_numpy(np.ascontiguousarray(q)).pin_memory()
         h_out = torch.empty((P,), dtype=torch.int32).pin_memory()
-        dq2 = torch.empty_like(dq)
-        L = self.lib
+        dq2 = torch.empty_like(dq[0])
 
-        def e2e_step():
+        def e2e_step(i):
             if self.world == 1:
-                rc = L.mans_flat_search(ctx.handle, buf.handle, C.c_void_p(hq.data_ptr()), nq,
-                                        a.dim, a.k, self.metric, C.c_void_p(h_out.data_ptr()),
-                                        C.c_void_p(h_out[nq * kout:].data_ptr()),
-                                        C.c_void_p(h_out[2 * nq * kout:].data_ptr()))
-                mb.check(rc)
+                self._host_search(hq[i % pool].data_ptr(), nq, h_out, kout)
             else:
-                dq2.copy_(hq, non_blocking=True)
+                dq2.copy_(hq[i % pool], non_blocking=True)
                 r = step(dq2)
                 h_out.copy_(r, non_blocking=True)
                 torch.cuda.current_stream().synchronize()
 
-        for _ in range(max(3, warmup)):
-            e2e_step()
+        for i in range(max(3, warmup)):
+            e2e_step(i)
         self.barrier()
         e2e_times = []
-        for _ in range(steps):
+        for i in range(steps):
             t = time.perf_counter()
-            e2e_step()
+            e2e_step(i)
             e2e_times.append(time.perf_counter() - t)
         self.barrier()
         ok = bool(torch.equal(device_out.cpu(), h_out))
@@ -589,7 +638,67 @@ class Runner:
                 "kern_avg_ms": kern_avg_ms, "kern_launches": kern_launches,
                 "launches": total_launches, "p50_ms": p50(steps_t.tolist()),
                 "e2e_p50_s": p50(e2e_t.tolist()), "clocks": clock_info, "ok": ok, "kout": kout,
-                "path": path}
+                "path": path, "fallbacks_last_step": fallbacks,
+                "distinct_batches": min(pool, steps)}
+
+    def latency(self, qs):
+        """Single-query latency over len(qs) distinct queries, each timed on
+        its own (the reference's protocol: >= 200 queries timed individually,
+        p50 by nearest rank, LatencyDistribution.swift:154-160).  Device time
+        per query (CUDA events on the launching stream, queries not
+        overlapped; max over ranks) and end-to-end time through the host C
+        ABI; exact re-scans of the tensor-core path are counted."""
+        torch, mb, a = self.torch, self.mb, self.a
+        kout = min(a.k, mb.MAX_TOP_K)
+        count = qs.shape[0]
+        dq = torch.from_numpy(np.ascontiguousarray(qs)).cuda()
+        ws, sp = self.ws, self.sp
+        sharded, bufs = self._sharded(1, kout)
+        for i in range(5):
+            sharded.search_device(ws, dq[i % count].data_ptr(), 1, a.k, self.metric, bufs, sp)
+        ws.check(sp)
+        dev_ms, fallbacks = [], 0
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        self.barrier()
+        for i in range(count):
+            e0.record(self.stream)
+            sharded.search_device(ws, dq[i].data_ptr(), 1, a.k, self.metric, bufs, sp)
+            e1.record(self.stream)
+            e1.synchronize()
+            dev_ms.append(e0.elapsed_time(e1))
+            fallbacks += ws.fallbacks()
+            if self.world > 1:
+                self.dist.barrier()
+        ws.check(sp)
+        e2e_s = []
+        if self.world == 1:
+            hq = torch.from_numpy(np.ascontiguousarray(qs)).pin_memory()
+            h_out = torch.empty((self.mb.shard.packed_words(1, kout),),
+                                dtype=torch.int32).pin_memory()
+            for i in range(count):
+                t = time.perf_counter()
+                self._host_search(hq[i].data_ptr(), 1, h_out, kout)
+                e2e_s.append(time.perf_counter() - t)
+        d = torch.tensor(dev_ms, dtype=torch.float64, device="cuda")
+        if self.world > 1:
+            self.dist.all_reduce(d, op=self.dist.ReduceOp.MAX)
+        self.barrier()
+        sharded.close()
+        dev = sorted(d.tolist())
+
+        def rank_at(xs, f):
+            return xs[max(0, math.ceil(f * len(xs)) - 1)]
+
+        out = {"queries": count, "distinct": True, "p50_us": 1e3 * rank_at(dev, 0.5),
+               "p90_us": 1e3 * rank_at(dev, 0.9), "p99_us": 1e3 * rank_at(dev, 0.99),
+               "mean_us": 1e3 * sum(dev) / len(dev), "exact_fallbacks": int(fallbacks),
+               "timing": "device (CUDA events per query, one query in flight)"}
+        if e2e_s:
+            e2 = sorted(e2e_s)
+            out["e2e_p50_us"] = 1e6 * rank_at(e2, 0.5)
+            out["e2e_p99_us"] = 1e6 * rank_at(e2, 0.99)
+        return out
 
 
 def roofline(args, res, shard_rows, metric, tc_min_batch, workload):
@@ -938,12 +1047,29 @@ def index_roofline(args, res, list_rows):
             "peak_source": f"{src} hbm_gbs (STREAM copy)"}
 
 
-def run_index(args, torch, mb, lib, world, rank, dist):
+def index_args(base, workload):
+    """The IVF-flat or IVF-PQ workload with its
+    BASELINE defaults, for the extra lines of the default run."""
+    import copy
+    a = copy.copy(base)
+    a.workload = workload
+    a.k = 10
+    if workload == "ivf":
+        a.n, a.dim, a.metric, a.nq = 1_000_000, 384, "cosine", 1
+        a.nlist, a.nprobe, a.components = 1024, 8, 1024
+    else:
+        a.n, a.dim, a.metric, a.nq = 10_000_000, 128, "l2", 1024
+        a.nlist, a.nprobe, a.components, a.pq_m = 4096, 32, 4096, 16
+    return a
+
+
+def index_session(args, torch, mb, lib, world, rank, dist, cases):
+    """Builds the index of args.workload on this rank (its shard for N > 1)
+    and measures each case (nq, nprobe, steps, warmup, with_clocks).  Returns
+    (results, build seconds, host data for the CPU baselines); the device
+    objects are released before returning."""
     metric = METRIC_NAMES[args.metric]
-    extra = [] if args.no_also else (
-        [(1, p) for p in (4, 32) if p != args.nprobe] + [(256, args.nprobe)]
-        if args.workload == "ivf" else [(256, args.nprobe)])
-    nq_max = max([args.nq] + [x for x, _ in extra])
+    nq_max = max(c[0] for c in cases)
     t_build = time.perf_counter()
     ctx = mb.Context(torch.cuda.current_device())
     # N > 1: both index kinds shard their rows over the ranks (shared
@@ -957,6 +1083,7 @@ def run_index(args, torch, mb, lib, world, rank, dist):
     L = lib
     kout = min(args.k, mb.MAX_TOP_K)
     barrier = None
+    sharded = None
     if ivf_sharded and args.workload == "ivfpq":
         ix = mb.IVFPQIndex(ctx, art["coarse"], art["codebooks"], art["codes"],
                            (art["offsets"], art["lists"]), metric=mb.Metric(metric),
@@ -1022,29 +1149,112 @@ def run_index(args, torch, mb, lib, world, rank, dist):
                 C.c_void_p(d), C.c_void_p(i), C.c_void_p(c)))
     build_s = time.perf_counter() - t_build
 
-    def one(nq, nprobe, steps, warmup, with_clocks):
+    results = []
+    for nq, nprobe, steps, warmup, with_clocks in cases:
         saved = args.nprobe
         args.nprobe = nprobe
         try:
             q = q_all[:nq]
             r = measure_index(torch, ws, dev_fn(nprobe), host_fn(nprobe), q, kout, steps, warmup,
                               with_clocks, barrier=barrier)
+            if world > 1:
+                t = torch.tensor([r["total_ms"], r["e2e_ms"]], dtype=torch.float64,
+                                 device="cuda")
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                r["total_ms"], r["e2e_ms"] = t.tolist()
             r["nprobe"] = nprobe
             r["roofline"] = index_roofline(args, r, probed_list_rows(args, art, q))
             r["workload"] = index_workload_config(args, nq, nprobe)["workload"]
-            return r
+            r["config"] = index_workload_config(args, nq, nprobe)
+            results.append(r)
         finally:
             args.nprobe = saved
+    if sharded is not None:
+        barrier()  # every rank is done with the peers' buffers
+        if hasattr(sharded, "close"):
+            sharded.close()
+    ws.close()
+    index.close()
+    if "corpus" in art:
+        art["corpus"].close()
+    ctx.close()
+    torch.cuda.synchronize()
+    host = {"v": v, "q": q_all, "art": {kk: vv for kk, vv in art.items()
+                                        if kk not in ("partition", "corpus")},
+            "build_gpu_s": art.get("build_gpu_s"), "build_gpu": art.get("build_gpu")}
+    return results, build_s, host
 
-    main_res = one(args.nq, args.nprobe, args.steps, args.warmup, True)
-    also = [one(nq2, p2, max(20, min(args.steps, int(20000 / nq2))), 5, False)
-            for nq2, p2 in extra]
-    if world > 1:
-        t = torch.tensor([main_res["total_ms"]], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        main_res["total_ms"] = float(t.item())
+
+def index_entry(args, r, world, ivf_sharded):
+    """One measured case as a JSON object (the main line's keys)."""
+    return {"workload": r["workload"], "nq": r["nq"], "nprobe": r["nprobe"],
+            "steps": r["steps"], "metric": "queries_per_sec",
+            "value": (1 if ivf_sharded else world) * r["nq"] * r["steps"] / (r["total_ms"] * 1e-3),
+            "unit": "queries/s", "ms_per_step": r["total_ms"] / r["steps"],
+            "p50_us": 1e3 * r["p50_ms"],
+            "e2e": {"value": r["nq"] * r["steps"] / (r["e2e_ms"] * 1e-3), "unit": "queries/s",
+                    "p50_us": 1e6 * r["e2e_p50_s"],
+                    "h2d_bytes_per_step": r["nq"] * args.dim * 4,
+                    "d2h_bytes_per_step": r["nq"] * r["kout"] * 8 + r["nq"] * 4},
+            "gpu_launches": int(r["launches"]), "roofline": r["roofline"],
+            "config": r["config"], "e2e_matches_device_path": r["ok"],
+            "dtype": "f32" if args.workload == "ivf" else "f32 (u8 codes)"}
+
+
+def index_cpu_baseline(args, host, seconds, threads):
+    """The restated reference search on a bounded sample of queries: one
+    thread per query as the reference runs it; with threads > 1 the queries
+    are spread over that many host threads (the ctypes calls release the
+    GIL)."""
+    one = index_searcher(args, host["v"], host["art"])
+    q = host["q"]
+    one(q[0])
+    if threads <= 1:
+        qps, done = cpu_index_qps(args, host["v"], q, host["art"], seconds)
+        kind = ("IVFFlatSearch.scanProbedLists restated" if args.workload == "ivf"
+                else "_IVFPQIndex.search restated (coarse BoundedSortedList, sequential ADC, "
+                     "newest-first merge)")
+        return {"value": qps, "unit": "queries/s", "cores": 1, "kind": "port",
+                "sample": f"{done} single-query searches (~{seconds:.0f} s), nprobe "
+                          f"{args.nprobe}, one thread; {kind}"}
+    from concurrent.futures import ThreadPoolExecutor
+    done = 0
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(threads) as ex:
+        while True:
+            idx = [(done + i) % len(q) for i in range(threads)]
+            list(ex.map(lambda j: one(q[j]), idx))
+            done += threads
+            el = time.perf_counter() - t0
+            if el >= seconds:
+                break
+    return {"value": done / el, "unit": "queries/s", "cores": threads, "kind": "port",
+            "sample": f"{done} queries (~{seconds:.0f} s), nprobe {args.nprobe}, queries spread "
+                      f"over {threads} host threads, each query single-threaded as the "
+                      f"reference runs it; "
+                      + ("IVFFlatSearch.scanProbedLists restated" if args.workload == "ivf"
+                         else "_IVFPQIndex.search restated")}
+
+
+def index_cases(args):
+    """(nq, nprobe, steps, warmup, clocks) of the main line and its extras."""
+    main = (args.nq, args.nprobe, args.steps, args.warmup, True)
+    if args.no_also:
+        return [main]
+    if args.workload == "ivf":
+        extra = [(1, p) for p in (4, 32) if p != args.nprobe] + [(256, args.nprobe)]
+    else:
+        extra = [(256, args.nprobe)]
+    return [main] + [(nq2, p2, max(20, min(args.steps, int(20000 / nq2))), 5, False)
+                     for nq2, p2 in extra]
+
+
+def run_index(args, torch, mb, lib, world, rank, dist):
+    ivf_sharded = world > 1
+    results, build_s, host = index_session(args, torch, mb, lib, world, rank, dist,
+                                           index_cases(args))
     if rank == 0:
-        res = main_res
+        res = results[0]
         line = {
             "metric": "queries_per_sec",
             "value": (1 if ivf_sharded else world) * args.nq * args.steps / (res["total_ms"] * 1e-3),
@@ -1053,48 +1263,33 @@ def run_index(args, torch, mb, lib, world, rank, dist):
             "higher_is_better": True, "scaling": "strong" if ivf_sharded else "weak",
             "vs_baseline": None,
             "dtype": "f32" if args.workload == "ivf" else "f32 (u8 codes)",
-            "data": f"synthetic (numpy default_rng(0) {args.components}-component Gaussian "
-                    f"mixture, sigma 0.3, L2-normalised); index trained with torch "
-                    f"(build {build_s:.0f} s, outside the timed region)",
+            "data": index_data_note(args, build_s),
             "config": index_workload_config(args),
             "roofline": res["roofline"],
             "e2e": {"value": args.nq * args.steps / (res["e2e_ms"] * 1e-3), "unit": "queries/s",
                     "p50_us": 1e6 * res["e2e_p50_s"],
                     "h2d_bytes_per_step": args.nq * args.dim * 4,
-                    "d2h_bytes_per_step": args.nq * kout * 8 + args.nq * 4},
+                    "d2h_bytes_per_step": args.nq * res["kout"] * 8 + args.nq * 4},
             "gpu_launches": int(res["launches"]),
             "clocks": res["clocks"],
             "e2e_matches_device_path": res["ok"],
-            "build": {"device_s": art["build_gpu_s"], "what": art["build_gpu"],
+            "build": {"device_s": host["build_gpu_s"], "what": host["build_gpu"],
                       "rows": args.n},
-            "also": [{"workload": r["workload"], "nq": r["nq"], "nprobe": r["nprobe"],
-                      "steps": r["steps"],
-                      "value": r["nq"] * r["steps"] / (r["total_ms"] * 1e-3),
-                      "unit": "queries/s", "ms_per_step": r["total_ms"] / r["steps"],
-                      "p50_us": 1e3 * r["p50_ms"],
-                      "e2e_value": r["nq"] * r["steps"] / (r["e2e_ms"] * 1e-3),
-                      "e2e_p50_us": 1e6 * r["e2e_p50_s"], "gpu_launches": int(r["launches"]),
-                      "roofline": r["roofline"], "e2e_matches_device_path": r["ok"]}
-                     for r in also],
+            "also": [index_entry(args, r, world, ivf_sharded) for r in results[1:]],
         }
         if world == 1 and not args.no_cpu_baseline:
-            qps, done = cpu_index_qps(args, v, q_all[:max(1, args.nq)], art, args.cpu_seconds)
-            line["cpu_baseline"] = {
-                "value": qps, "unit": "queries/s", "cores": 1, "kind": "port",
-                "sample": f"{done} single-query searches (~{args.cpu_seconds:.0f} s), "
-                          f"nprobe {args.nprobe}; "
-                          + ("IVFFlatSearch.scanProbedLists restated" if args.workload == "ivf"
-                             else "_IVFPQIndex.search restated (coarse BoundedSortedList, "
-                                  "sequential ADC, newest-first merge)")}
+            line["cpu_baseline"] = index_cpu_baseline(args, host, args.cpu_seconds, 1)
+            if args.workload == "ivfpq":
+                line["cpu_baseline_all_cores"] = index_cpu_baseline(
+                    args, host, args.cpu_seconds, os.cpu_count() or 1)
         print(json.dumps(line), flush=True)
-    if ivf_sharded:
-        barrier()  # every rank is done with the peers' buffers
-        sharded.close()
-    ws.close()
-    index.close()
-    if "corpus" in art:
-        art["corpus"].close()
-    ctx.close()
+
+
+def index_data_note(args, build_s):
+    return (f"synthetic {args.components}-component Gaussian mixture (sigma 0.3, "
+            f"L2-normalised; numpy default_rng(0) below 2^26 elements, torch CUDA Philox "
+            f"seed 0 above); index trained with torch (build {build_s:.0f} s, outside the "
+            f"timed region)")
 
 
 def main():
@@ -1130,7 +1325,9 @@ def main():
     metric = METRIC_NAMES[args.metric]
     also_nq = [] if args.no_also else [
         x for x in (int(t) for t in args.also_nq.split(",") if t.strip()) if x != args.nq]
-    v, q_all = make_data(args.n, args.dim, max([args.nq] + also_nq))
+    # the nq = 1 line times distinct queries: step i searches query i % pool
+    pool = max(LATENCY_QUERIES, args.steps) if args.nq == 1 else 1
+    v, q_all = make_data(args.n, args.dim, max([args.nq * pool, LATENCY_QUERIES] + also_nq))
     r0, r1 = mb.row_shard(args.n, world, rank)
     ctx = mb.Context(local)
     tc_min = args.tc_min_batch
@@ -1138,11 +1335,41 @@ def main():
     buf = mb.VectorBuffer(ctx, v[r0:r1], id_offset=r0)
     ws = mb.Workspace(ctx)
     R = Runner(args, torch, mb, lib(), ctx, buf, ws, world, rank, dist, metric)
-    main_res = R.measure(q_all[:args.nq], args.steps, args.warmup, with_clocks=True)
+    main_res = R.measure(q_all[:args.nq * pool].reshape(pool, args.nq, args.dim), args.steps,
+                         args.warmup, with_clocks=True)
+    latency = R.latency(q_all[:LATENCY_QUERIES]) if args.nq == 1 else None
     also = []
     for nq2 in also_nq:
         st = max(20, min(args.steps, int(20000 / nq2)))
-        also.append(R.measure(q_all[:nq2], st, 5, with_clocks=False))
+        also.append(R.measure(q_all[:nq2][None], st, 5, with_clocks=False))
+    fp32 = None
+    if not args.no_also and args.nq == 1:
+        # the exact fp32 CUDA-core scan alone (tensor-core path off): the
+        # single-query scan of the fp32 rows the north star's HBM target names
+        ctx.set_tensor_core_batch(0)
+        st = max(20, min(args.steps, 200))
+        fp32 = R.measure(q_all[:st].reshape(st, 1, args.dim), st, 5, with_clocks=False)
+        fp32["latency"] = R.latency(q_all[:LATENCY_QUERIES])
+        ctx.set_tensor_core_batch(tc_min)
+    ws.close()
+    buf.close()
+    ctx.close()
+
+    index_results = []
+    if not args.no_also and not args.no_index and args.n == 1_000_000 and args.dim == 384:
+        # BASELINE.json configs[2] (IVF-flat) and configs[3] (IVF-PQ) on the
+        # same run, each with its own roofline and CPU baseline
+        for wl in ("ivf", "ivfpq"):
+            ia = index_args(args, wl)
+            if wl == "ivf":
+                cases = [(1, 8, max(20, min(args.steps, 200)), 5, False),
+                         (1, 4, max(20, min(args.steps, 200)), 5, False),
+                         (1, 32, max(20, min(args.steps, 200)), 5, False),
+                         (256, 8, max(20, min(args.steps, 80)), 5, False)]
+            else:
+                cases = [(1024, 32, max(20, min(args.steps, 20)), 5, False)]
+            res, build_s, host = index_session(ia, torch, mb, lib(), world, rank, dist, cases)
+            index_results.append((ia, res, build_s, host))
 
     if rank == 0:
         workload = workload_config(args)["workload"]
@@ -1155,7 +1382,7 @@ def main():
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": res["total_ms"] / args.steps,
-            "p50_us": 1e3 * res["p50_ms"],
+            "p50_us": 1e3 * (latency["p50_us"] / 1e3 if latency else res["p50_ms"]),
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,
@@ -1170,51 +1397,115 @@ def main():
             "gpu_launches": int(res["launches"]),
             "clocks": res["clocks"],
             "e2e_matches_device_path": res["ok"],
+            "distinct_queries_timed": res["distinct_batches"] * args.nq,
+            "exact_fallbacks_last_step": res["fallbacks_last_step"],
         }
+        if latency:
+            line["p50_steps_us"] = 1e3 * res["p50_ms"]
+            line["latency"] = latency
         line["also"] = []
         for r in also:
             wl = workload_config(args, r["nq"])["workload"]
-            line["also"].append({
-                "workload": wl, "nq": r["nq"], "steps": r["steps"],
-                "value": r["nq"] * r["steps"] / (r["total_ms"] * 1e-3), "unit": "queries/s",
-                "ms_per_step": r["total_ms"] / r["steps"], "p50_us": 1e3 * r["p50_ms"],
-                "e2e_value": r["nq"] * r["steps"] / (r["e2e_ms"] * 1e-3),
-                "e2e_p50_us": 1e6 * r["e2e_p50_s"], "gpu_launches": int(r["launches"]),
-                "roofline": roofline(args, r, r1 - r0, metric, tc_min, wl),
-                "e2e_matches_device_path": r["ok"]})
+            line["also"].append(flat_entry(args, r, r1 - r0, metric, tc_min, wl))
+        if fp32 is not None:
+            entry = flat_entry(args, fp32, r1 - r0, metric, 0,
+                               workload_config(args, 1)["workload"] + "_fp32scan")
+            entry["path"] = "exact fp32 CUDA-core scan (tensor-core path off)"
+            entry["latency"] = fp32["latency"]
+            entry["p50_us"] = fp32["latency"]["p50_us"]
+            line["also"].append(entry)
+        for ia, results, build_s, host in index_results:
+            for i, r in enumerate(results):
+                e = index_entry(ia, r, world, world > 1)
+                e["data"] = index_data_note(ia, build_s)
+                if i == 0:
+                    e["build"] = {"device_s": host["build_gpu_s"], "what": host["build_gpu"],
+                                  "rows": ia.n}
+                line["also"].append(e)
         if world == 1 and not args.no_cpu_baseline:
-            batch_base = None
-            if args.n >= 16384 and (args.nq > 1 or any(r["nq"] > 1 for r in also)):
-                # the reference's CPU route for batches (BoundedExactScan per query)
-                bq, bused, bdone, buse_ref = cpu_batch_qps(v, q_all, args.k, metric,
-                                                           args.cpu_seconds)
-                batch_base = {
-                    "value": bq, "unit": "queries/s", "cores": bused, "kind": "port",
-                    "sample": f"{bdone} queries (~{args.cpu_seconds:.0f} s) through the batch "
-                              f"route: BoundedExactScan restated (int8 prefilter, provable "
-                              f"lower bounds, fp32 rescore) per query, queries in parallel over "
-                              f"{bused} threads; inner loops "
-                              f"{'reference dots.c' if buse_ref else 'restated dots.c'}"}
-                for entry, r in zip(line["also"], also):
-                    if r["nq"] > 1:
-                        entry["cpu_baseline"] = batch_base
-            if args.nq > 1 and batch_base is not None:
-                line["cpu_baseline"] = batch_base
-            else:
-                qps, used, done, use_ref = cpu_reference_qps(v, q_all[:max(1, args.nq)], args.k,
-                                                             metric, args.cpu_seconds)
-                line["cpu_baseline"] = {
-                    "value": qps, "unit": "queries/s", "cores": used, "kind": "port",
-                    "sample": f"{done} single-query scans of the full {args.n}x{args.dim} corpus "
-                              f"(~{args.cpu_seconds:.0f} s); ParallelFlatScan restated, inner "
-                              f"loop {'reference dots.c' if use_ref else 'restated dots.c'}"}
+            add_cpu_baselines(args, line, also, fp32, index_results, v, q_all, metric)
         print(json.dumps(line), flush=True)
 
-    ws.close()
-    buf.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+LATENCY_QUERIES = 200
+
+
+def flat_entry(args, r, shard_rows, metric, tc_min, wl):
+    return {"workload": wl, "nq": r["nq"], "steps": r["steps"],
+            "metric": "queries_per_sec",
+            "value": r["nq"] * r["steps"] / (r["total_ms"] * 1e-3), "unit": "queries/s",
+            "ms_per_step": r["total_ms"] / r["steps"], "p50_us": 1e3 * r["p50_ms"],
+            "e2e_value": r["nq"] * r["steps"] / (r["e2e_ms"] * 1e-3),
+            "e2e_p50_us": 1e6 * r["e2e_p50_s"], "gpu_launches": int(r["launches"]),
+            "roofline": roofline(args, r, shard_rows, metric, tc_min, wl),
+            "e2e_matches_device_path": r["ok"],
+            "distinct_queries_timed": r["distinct_batches"] * r["nq"],
+            "exact_fallbacks_last_step": r["fallbacks_last_step"],
+            "config": workload_config(args, r["nq"])}
+
+
+def add_cpu_baselines(args, line, also, fp32, index_results, v, q_all, metric):
+    """The reference's CPU routes, timed on bounded samples on this host:
+    ParallelFlatScan for single queries (all cores, and one core), the
+    BoundedExactScan batch route for batches, scanProbedLists (one thread per
+    query, as the reference runs it) for IVF-flat, _IVFPQIndex.search for
+    IVF-PQ (one thread, and queries spread over all cores)."""
+    batch_base = None
+    if args.n >= 16384 and (args.nq > 1 or any(r["nq"] > 1 for r in also)):
+        # the reference's CPU route for batches (BoundedExactScan per query)
+        bq, bused, bdone, buse_ref = cpu_batch_qps(v, q_all, args.k, metric, args.cpu_seconds)
+        batch_base = {
+            "value": bq, "unit": "queries/s", "cores": bused, "kind": "port",
+            "sample": f"{bdone} queries (~{args.cpu_seconds:.0f} s) through the batch "
+                      f"route: BoundedExactScan restated (int8 prefilter, provable "
+                      f"lower bounds, fp32 rescore) per query, queries in parallel over "
+                      f"{bused} threads; inner loops "
+                      f"{'reference dots.c' if buse_ref else 'restated dots.c'}"}
+        for entry, r in zip(line["also"], also):
+            if r["nq"] > 1:
+                entry["cpu_baseline"] = batch_base
+    if args.nq > 1 and batch_base is not None:
+        line["cpu_baseline"] = batch_base
+        return_single = False
+    else:
+        return_single = True
+    if return_single or fp32 is not None:
+        qps, used, done, use_ref = cpu_reference_qps(v, q_all, args.k, metric, args.cpu_seconds)
+        single = {
+            "value": qps, "unit": "queries/s", "cores": used, "kind": "port",
+            "sample": f"{done} single-query scans of the full {args.n}x{args.dim} corpus "
+                      f"(~{args.cpu_seconds:.0f} s), {used} threads; ParallelFlatScan restated, "
+                      f"inner loop {'reference dots.c' if use_ref else 'restated dots.c'}"}
+        qps1, _, done1, _ = cpu_reference_qps(v, q_all, args.k, metric, args.cpu_seconds / 2,
+                                              cores=1)
+        one_core = {
+            "value": qps1, "unit": "queries/s", "cores": 1, "kind": "port",
+            "sample": f"{done1} single-query scans (~{args.cpu_seconds / 2:.0f} s) on one core "
+                      f"(ParallelFlatScan with one slice)"}
+        if return_single:
+            line["cpu_baseline"] = single
+            line["cpu_baseline_1core"] = one_core
+        for entry in line["also"]:
+            if entry["workload"].endswith("_fp32scan"):
+                entry["cpu_baseline"] = single
+                entry["cpu_baseline_1core"] = one_core
+    for ia, results, build_s, host in index_results:
+        for entry, r in zip([e for e in line["also"] if e["workload"] in
+                             {x["workload"] for x in results}], results):
+            saved = ia.nprobe
+            ia.nprobe = r["nprobe"]
+            try:
+                secs = args.cpu_seconds if r["nprobe"] in (8, 32) else args.cpu_seconds / 2
+                entry["cpu_baseline"] = index_cpu_baseline(ia, host, secs, 1)
+                if ia.workload == "ivfpq":
+                    entry["cpu_baseline_all_cores"] = index_cpu_baseline(
+                        ia, host, secs, os.cpu_count() or 1)
+            finally:
+                ia.nprobe = saved
 
 
 if __name__ == "__main__":

@@ -84,6 +84,11 @@ int32_t mans_last_error_message(char *buf, size_t buf_len);
 /* Number of streaming multiprocessors of the context's device. */
 int32_t mans_ctx_sm_count(const mans_ctx *ctx);
 
+/* "sha256:<hex>" digest of the CUDA sources and headers this library was
+ * built from (NUL-terminated, truncated to buf_len), so a deployment can tell
+ * which sources a binary belongs to.  No reference counterpart. */
+int32_t mans_build_info(char *buf, size_t buf_len);
+
 /* Query batches of at least `min_batch` queries run on the tensor cores
  * (bf16 tcgen05 candidate GEMM with a certified error bound, then an exact
  * fp32 re-score, so results are identical to the exact scan); smaller batches
@@ -217,13 +222,18 @@ int32_t mans_flat_search_device(mans_ctx *ctx, const mans_corpus *corpus, mans_w
  * latency-critical loop that cannot take cudaMalloc's implicit
  * synchronisation.  Results equal mans_flat_search_device.  Scratch is a
  * fixed 4 MiB __device__ array held by every GPU that loads the library until
- * exit; a request whose candidate lists need more (roughly nq x min(k,256)
- * beyond a few thousand keys per query group) fails with MANS_ERR_OOM and a
- * message naming the sizes.  The first call on a device resolves the array's
+ * exit.  One call needs 256 + round_up(4 S, 256) + 8 S kp bytes of it, with
+ * S = G qb splits, qb = the smallest power of two >= nq capped at 8,
+ * G = ceil(nq / qb), splits = min(max(1, SMs / G), ceil(n / 256)) and kp = the
+ * smallest power of two >= min(k, 256, n) (so k = 129 costs as much as
+ * k = 256); a request needing more fails with MANS_ERR_OOM and a message
+ * naming the sizes.  The first call on a device resolves the array's
  * address (cudaGetSymbolAddress) and should come before any stream capture.
  * All calls on a device share the array: calls whose GPU work may overlap race
  * and must be serialised by the caller.  The call enqueues on `cuda_stream`
- * and returns argument and launch errors only. */
+ * and returns argument and launch errors only; a device wait that timed out
+ * (a stalled GPU) turns every query's result empty (count 0) instead of
+ * leaving a partial top-k. */
 int32_t mans_flat_search_noalloc(mans_ctx *ctx, const mans_corpus *corpus,
                                  const float *d_queries, int64_t nq, int32_t k, int32_t metric,
                                  float *d_out_dist, uint32_t *d_out_ids, int32_t *d_out_counts,

@@ -82,6 +82,7 @@ SIGNATURES = {
                                               C.c_int32, _VP, _VP, _VP, _VP]),
     "mans_pq_adc_list": (C.c_int32, [_VP, _VP, C.c_int64, _VP, C.c_int32, C.c_int32, _VP,
                                      C.c_int64, _VP]),
+    "mans_build_info": (C.c_int32, [C.c_char_p, C.c_size_t]),
 }
 
 _lib = None
@@ -100,8 +101,27 @@ def lib():
             fn = getattr(L, name)
             fn.restype = res
             fn.argtypes = args
+        _check_build(L)
         _lib = L
     return _lib
+
+
+def build_info(L=None) -> str:
+    """Digest of the sources the loaded library was built from."""
+    buf = C.create_string_buffer(128)
+    (L or lib()).mans_build_info(buf, len(buf))
+    return buf.value.decode()
+
+
+def _check_build(L):
+    """The library must come from the sources beside it: a stale build is an
+    error, never silently used."""
+    from . import build as _build
+    want = "sha256:" + _build.source_hash()
+    got = build_info(L)
+    if got != want:
+        raise RuntimeError(f"{LIB_PATH} was built from other sources ({got[:19]}..., these "
+                           f"are {want[:19]}...): rebuild with `python -m meltan_b200.build`")
 
 
 def last_error() -> str:

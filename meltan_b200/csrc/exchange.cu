@@ -177,6 +177,7 @@ int32_t mans_exchange_allgather(mans_exchange* ex, mans_workspace* ws, const int
                  parity * ex->world;
   m.wait_count = ex->world;
   m.wait_epoch = epoch;
+  m.empty_on_error = true;  // a peer that never published: empty results, not a partial merge
   e = launch_merge(m, st);
   if (e != cudaSuccess) return fail_cuda(e, "exchange merge launch");
   ws->launches += 2;

@@ -110,6 +110,9 @@ struct MergeParams {
   const uint32_t* wait_flags;
   int32_t wait_count;
   uint32_t wait_epoch;
+  // when set (err must then be a cleared word), a non-zero *err seen after
+  // the waits makes every query's result empty (count 0)
+  bool empty_on_error;
 };
 cudaError_t launch_merge(const MergeParams& p, cudaStream_t stream);
 

@@ -21,9 +21,19 @@
 // without ordering, or several threads) race on it and must be serialised by
 // the caller.  The error word is cleared on the stream at the start of every
 // call; candidate counts are always written before they are read.  The call
-// only enqueues work: it returns argument and launch errors, while a device
-// wait timeout (which only a stalled GPU produces) is left in the scratch
-// error word and not reported, since reading it back would synchronise.
+// only enqueues work and returns argument and launch errors.  Reading the
+// error word back would synchronise, so a device wait that timed out (which
+// only a stalled GPU produces) is reported in the results instead: the merge
+// kernel sees the word set and writes every query's result as empty (count 0,
+// ids MANS_EMPTY_ID), never a partial top-k.
+//
+// Scratch use of one call, in bytes (the MANS_ERR_OOM test below):
+//   256 + round256(4 * S) + 8 * S * kp,   S = G * qb * splits,
+//   qb = smallest power of two >= nq capped at 8, G = ceil(nq / qb),
+//   splits = min(max(1, SMs / G), ceil(n / 256)), kp = smallest power of two
+//   >= min(k, 256, n).
+// So k = 129 costs as much as k = 256, and below about 8 x SMs queries the
+// need is near SMs x 8 x kp x 8 bytes whatever nq is.
 #include <algorithm>
 #include <cstdio>
 #include <mutex>
@@ -159,6 +169,7 @@ extern "C" int32_t mans_flat_search_noalloc(mans_ctx* ctx, const mans_corpus* co
   m.out_ids = d_out_ids;
   m.out_counts = d_out_counts;
   m.err = err;
+  m.empty_on_error = true;
   e = launch_merge(m, stream);
   return e == cudaSuccess ? MANS_OK : fail_cuda(e, "merge launch");
 }

@@ -362,13 +362,14 @@ __global__ void query_norms_kernel(const float* __restrict__ q, int64_t nq, int3
 __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const MergeParams p) {
   __shared__ uint64_t buf[kSortN];
   __shared__ uint64_t thr;
-  __shared__ int qc, nb;
+  __shared__ int qc, nb, failed;
   const int tid = threadIdx.x;
   const int64_t q = blockIdx.x;
   if (tid == 0) {
     thr = kKeyMax;
     qc = 0;
     nb = 0;
+    failed = 0;
   }
   if (p.wait_flags && tid < p.wait_count) {
     // peer blocks: acquire-load the flag a peer release-stored after its data
@@ -384,6 +385,21 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const MergeParams 
     }
   }
   __syncthreads();
+  if (p.empty_on_error) {
+    // An earlier kernel of this call (or a peer wait above) gave up: its
+    // candidate lists are incomplete, so report no results instead of a
+    // plausible-looking partial top-k.
+    if (tid == 0) failed = atomicAdd(p.err, 0) != 0;
+    __syncthreads();
+    if (failed) {
+      for (int i = tid; i < p.kout; i += kMergeThreads) {
+        p.out_dist[q * p.kout + i] = __int_as_float(0x7F800000);
+        p.out_ids[q * p.kout + i] = kEmptyId;
+      }
+      if (tid == 0) p.out_counts[q] = 0;
+      return;
+    }
+  }
   TopKState st{buf, &qc, &nb, &thr};
 
   int64_t nslots;

@@ -15,7 +15,10 @@ import subprocess
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_ROOT = os.environ.get("MANS_REFERENCE_DIR", "/root/reference")
+# The reference tree: MANS_REFERENCE_DIR, else a checkout named "reference"
+# beside this repository (absent on machines that only run the prebuilt files).
+REF_ROOT = os.environ.get("MANS_REFERENCE_DIR") or os.path.join(
+    os.path.dirname(os.path.dirname(HERE)), "reference")
 CFLAGS = ["-O2", "-std=c11", "-ffp-contract=off", "-fPIC", "-Wall", "-Wno-unused-function"]
 
 ORACLE_SO = os.path.join(HERE, "libmans_oracle.so")

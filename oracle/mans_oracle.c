@@ -16,7 +16,7 @@
  *     order; they are restated as sequential fp32 sums (index 0 first).
  *
  * Parity pins: orc_dot_rows_seq is checked bit-for-bit against the
- * reference's own mans_f32_dot_rows compiled from dots.c (oracle/build_ref.sh
+ * reference's own mans_f32_dot_rows compiled from dots.c (oracle/build.py
  * -> oracle/_ref/), and the generators / tie rules against the reference
  * tests' own restated brute force (tests/golden/).
  */

@@ -95,22 +95,45 @@ def test_ivf_single_query_api_and_errors(ctx):
     part.close()
 
 
+def _oracle_threads(fn, q, threads=16):
+    """The oracle over query chunks on host threads (its ctypes calls
+    release the GIL); results concatenated in query order."""
+    from concurrent.futures import ThreadPoolExecutor
+    parts = np.array_split(np.arange(len(q)), min(threads, len(q)))
+    with ThreadPoolExecutor(len(parts)) as ex:
+        outs = list(ex.map(lambda ix: fn(q[ix]), parts))
+    return tuple(np.concatenate([o[j] for o in outs]) for j in range(3))
+
+
 @pytest.mark.slow
 def test_ivf_full_size_1m_x_384(ctx):
-    """1M x 384 mixture of 1024, nlist 1024, nprobe 4/8/32."""
-    v, q = bench.make_mixture(1_000_000, 384, 1024, 8, seed=0)
-    cent, assign = bench.train_partition(v, 1024, O.COSINE)
-    part = mb.Partition.from_assignment(ctx, v, cent, assign)
-    order = np.argsort(assign, kind="stable").astype(np.uint32)
-    off = np.concatenate([[0], np.cumsum(np.bincount(assign, minlength=1024))]).astype(np.int64)
+    """BASELINE config C3 at its own size: 1M x 384 mixture of 1024, nlist
+    1024 (partition built on the device, as the bench builds it), nprobe
+    4/8/32, cosine, k = 10 -- 8 single queries and one 256-query batch (the
+    batch route: small-corpus centroid step and per-list query grouping),
+    every query against the oracle's scanProbedLists."""
+    v, q = bench.make_mixture(1_000_000, 384, 1024, 256 + 8, seed=0)
+    cent = bench.train_centroids(v, 1024)
+    buf = mb.VectorBuffer(ctx, v)
+    part = mb.Partition.build(ctx, buf, cent, mb.Metric.cosine)
+    off, order = part.layout()
     packed = v[order]
     pn = O.row_norms(packed)
+    singles, batch = q[256:], q[:256]
     for nprobe in (4, 8, 32):
-        got = mb.IVFFlatSearch.search_arrays(ctx, q, part, 10, nprobe, mb.Metric.cosine)
-        want = O.ivf_search(cent, packed, pn, order, off, q, 10, nprobe, O.COSINE)
+        want1 = O.ivf_search(cent, packed, pn, order, off, singles, 10, nprobe, O.COSINE)
+        for i in range(len(singles)):
+            got = mb.IVFFlatSearch.search_arrays(ctx, singles[i:i + 1], part, 10, nprobe,
+                                                 mb.Metric.cosine)
+            for a, b in zip(got, want1):
+                np.testing.assert_array_equal(a[0], b[i])
+        got = mb.IVFFlatSearch.search_arrays(ctx, batch, part, 10, nprobe, mb.Metric.cosine)
+        want = _oracle_threads(lambda qq: O.ivf_search(cent, packed, pn, order, off, qq, 10,
+                                                       nprobe, O.COSINE), batch)
         for a, b in zip(got, want):
             np.testing.assert_array_equal(a, b)
     part.close()
+    buf.close()
 
 
 @pytest.mark.parametrize("mg,mo", MET)

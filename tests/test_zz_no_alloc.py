@@ -63,6 +63,28 @@ def test_no_alloc_matches_workspace_search_twice(ctx):
     buf.close()
 
 
+def test_no_alloc_leaves_free_device_memory_unchanged(ctx):
+    """After the first call on the device, a call takes no device memory:
+    the free-memory figure is the same before and after it."""
+    import torch
+    rng = np.random.default_rng(5)
+    v = rng.standard_normal((30_000, 128), dtype=np.float32)
+    buf = mb.VectorBuffer(ctx, v)
+    nq, k = 4, 10
+    dq = torch.from_numpy(rng.standard_normal((nq, 128), dtype=np.float32)).cuda()
+    out = _outputs(nq, k)
+    mb.check(_noalloc(ctx, buf, dq.data_ptr(), nq, k, mb.Metric.l2, *(t.data_ptr() for t in out)))
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(3):
+        mb.check(_noalloc(ctx, buf, dq.data_ptr(), nq, k, mb.Metric.l2,
+                          *(t.data_ptr() for t in out)))
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
+    assert int(out[2].sum()) == nq * k
+    buf.close()
+
+
 def test_no_alloc_rejects_requests_beyond_its_scratch(ctx):
     import torch
     rng = np.random.default_rng(3)
