@@ -77,6 +77,25 @@ typedef struct mans_ivfpq mans_ivfpq;
 int32_t mans_ctx_create(int32_t device, mans_ctx **out_ctx);
 int32_t mans_ctx_destroy(mans_ctx *ctx);
 
+/* One context over several GPUs of this process (the reference's one
+ * MetalContext per index, ANNSIndex.swift:35, given all the GPUs of the
+ * machine).  A corpus created or loaded on it (mans_corpus_create,
+ * mans_corpus_load_mann) is split into contiguous row shards, one per device
+ * in `devices` order (the first n % n_devices shards hold one extra row), and
+ * mans_flat_search with host buffers searches every shard on its own GPU at
+ * once: each GPU stores its shard's top-k over NVLink into the first GPU's
+ * memory (peer access is enabled between the GPUs of the group), which merges
+ * them by (distance, id) -- ParallelFlatScan.mergeSorted
+ * (ParallelFlatScan.swift:288-315) over the shards.  Results equal the
+ * single-GPU search of the whole corpus.  The corpus calls and
+ * mans_flat_search accept such a context; the device-pointer calls, the
+ * workspaces and the IVF / IVF-PQ objects need a single-device context
+ * (MANS_ERR_INVALID).  Fails with MANS_ERR_DEVICE when a device is not an
+ * sm_100 GPU or cannot reach the first device over peer access. */
+int32_t mans_ctx_create_multi(const int32_t *devices, int32_t n_devices, mans_ctx **out_ctx);
+/* Number of GPUs of a context (1 for mans_ctx_create). */
+int32_t mans_ctx_device_count(const mans_ctx *ctx);
+
 /* Message of the last failed call on the calling thread (NUL-terminated,
  * truncated to buf_len).  Replaces the String payloads of ANNSError. */
 int32_t mans_last_error_message(char *buf, size_t buf_len);

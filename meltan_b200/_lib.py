@@ -22,6 +22,8 @@ _VP = C.c_void_p
 SIGNATURES = {
     "mans_ctx_create": (C.c_int32, [C.c_int32, C.POINTER(_VP)]),
     "mans_ctx_destroy": (C.c_int32, [_VP]),
+    "mans_ctx_create_multi": (C.c_int32, [_VP, C.c_int32, C.POINTER(_VP)]),
+    "mans_ctx_device_count": (C.c_int32, [_VP]),
     "mans_last_error_message": (C.c_int32, [C.c_char_p, C.c_size_t]),
     "mans_ctx_sm_count": (C.c_int32, [_VP]),
     "mans_ctx_set_tensor_core_batch": (C.c_int32, [_VP, C.c_int32]),

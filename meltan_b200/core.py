@@ -119,13 +119,30 @@ def _ptr(a: np.ndarray):
 
 
 class Context:
-    """One CUDA device; stands in for MetalContext."""
+    """One CUDA device; stands in for MetalContext.  ``Context.multi(devices)``
+    makes one context over several GPUs of this process: a VectorBuffer
+    created on it holds one row shard per GPU and FlatGPUSearch searches them
+    all, merging on the first GPU (mans_ctx_create_multi)."""
 
     def __init__(self, device: int = 0):
         h = C.c_void_p()
         check(lib().mans_ctx_create(device, C.byref(h)))
         self._h = h
         self.device = device
+
+    @classmethod
+    def multi(cls, devices):
+        devs = (C.c_int32 * len(devices))(*devices)
+        h = C.c_void_p()
+        check(lib().mans_ctx_create_multi(devs, len(devices), C.byref(h)))
+        self = cls.__new__(cls)
+        self._h = h
+        self.device = devices[0]
+        return self
+
+    @property
+    def device_count(self) -> int:
+        return lib().mans_ctx_device_count(self._h)
 
     @property
     def handle(self):

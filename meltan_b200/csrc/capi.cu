@@ -158,7 +158,9 @@ void destroy_workspace(mans_workspace* ws) {
   ws->tc_aux.release();
   ws->small_scores.release();
   ws->tc_bar.release();
+  ws->gather.release();
   ws->h_err.release();
+  if (ws->done) cudaEventDestroy(ws->done);
   for (auto& pr : ws->events) {
     cudaEventDestroy(pr.first);
     cudaEventDestroy(pr.second);
@@ -446,6 +448,11 @@ int32_t mans_ctx_create(int32_t device, mans_ctx** out_ctx) {
 
 int32_t mans_ctx_destroy(mans_ctx* ctx) {
   if (!ctx) return MANS_OK;
+  if (is_group(ctx)) {
+    for (mans_ctx* m : ctx->members) mans_ctx_destroy(m);
+    delete ctx;
+    return MANS_OK;
+  }
   DeviceGuard g(ctx->device);
   cudaDeviceSynchronize();
   for (mans_workspace* ws : ctx->pool) destroy_workspace(ws);
@@ -460,6 +467,7 @@ int32_t mans_ctx_set_tensor_core_batch(mans_ctx* ctx, int32_t min_batch) {
   if (!ctx) return fail(MANS_ERR_INVALID, "null context");
   if (min_batch < 0) return fail(MANS_ERR_INVALID, "negative batch size");
   ctx->tc_min_batch = min_batch;
+  for (mans_ctx* m : ctx->members) m->tc_min_batch = min_batch;
   return MANS_OK;
 }
 
@@ -468,11 +476,21 @@ int32_t mans_ctx_set_tensor_core_format(mans_ctx* ctx, int32_t format) {
   if (format < MANS_TC_AUTO || format > MANS_TC_INT8)
     return fail(MANS_ERR_INVALID, "unknown tensor-core operand format");
   ctx->tc_format = format;
+  for (mans_ctx* m : ctx->members) m->tc_format = format;
   return MANS_OK;
 }
 
 int32_t mans_corpus_int8_codes(mans_corpus* corpus, int8_t* codes, float* scales) {
   if (!corpus || (!codes && !scales)) return fail(MANS_ERR_INVALID, "null corpus or outputs");
+  if (is_group(corpus)) {  // the shards' codes in row order
+    for (size_t i = 0; i < corpus->shards.size(); ++i) {
+      const int64_t r0 = corpus->shard_row0[i];
+      int32_t rc = mans_corpus_int8_codes(corpus->shards[i], codes ? codes + r0 * corpus->dim : nullptr,
+                                          scales ? scales + r0 : nullptr);
+      if (rc != MANS_OK) return rc;
+    }
+    return MANS_OK;
+  }
   std::lock_guard<std::mutex> lk(corpus->tc_mu);
   return tc_export_int8(corpus, codes, scales);
 }
@@ -496,7 +514,7 @@ int32_t mans_corpus_create(mans_ctx* ctx, const float* rows, int64_t n, int64_t 
                            uint32_t id_offset, mans_corpus** out_corpus) {
   if (!ctx || !out_corpus) return fail(MANS_ERR_INVALID, "null context or output");
   *out_corpus = nullptr;
-  return corpus_upload(ctx, rows, n, dim, id_offset, out_corpus);
+  return corpus_create_any(ctx, rows, n, dim, id_offset, out_corpus);
 }
 
 int32_t mans_corpus_update_rows(mans_corpus* c, int64_t start, const float* rows, int64_t count) {
@@ -505,6 +523,17 @@ int32_t mans_corpus_update_rows(mans_corpus* c, int64_t start, const float* rows
     return fail(MANS_ERR_INVALID, "row range outside the corpus");
   if (count == 0) return MANS_OK;
   if (!rows) return fail(MANS_ERR_INVALID, "rows is null");
+  if (is_group(c)) {  // each shard overlapping the range takes its part
+    for (size_t i = 0; i < c->shards.size(); ++i) {
+      const int64_t s0 = std::max(start, c->shard_row0[i]);
+      const int64_t s1 = std::min(start + count, c->shard_row0[i + 1]);
+      if (s0 >= s1) continue;
+      int32_t rc = mans_corpus_update_rows(c->shards[i], s0 - c->shard_row0[i],
+                                           rows + (s0 - start) * c->dim, s1 - s0);
+      if (rc != MANS_OK) return rc;
+    }
+    return MANS_OK;
+  }
   DeviceGuard g(c->ctx->device);
   {
     std::lock_guard<std::mutex> lk(c->tc_mu);
@@ -523,6 +552,11 @@ int32_t mans_corpus_update_rows(mans_corpus* c, int64_t start, const float* rows
 
 int32_t mans_corpus_destroy(mans_corpus* c) {
   if (!c) return MANS_OK;
+  if (is_group(c)) {
+    for (mans_corpus* s : c->shards) mans_corpus_destroy(s);
+    delete c;
+    return MANS_OK;
+  }
   DeviceGuard g(c->ctx->device);
   cudaDeviceSynchronize();
   corpus_free(c);
@@ -534,6 +568,7 @@ int64_t mans_corpus_dim(const mans_corpus* c) { return c ? c->dim : 0; }
 
 int32_t mans_workspace_create(mans_ctx* ctx, mans_workspace** out_ws) {
   if (!ctx || !out_ws) return fail(MANS_ERR_INVALID, "null context or output");
+  if (int32_t rc = reject_group(ctx, nullptr, "a workspace")) return rc;
   mans_workspace* ws = new mans_workspace();
   ws->ctx = ctx;
   ws->stream = nullptr;
@@ -620,6 +655,11 @@ int32_t mans_flat_search(mans_ctx* ctx, const mans_corpus* corpus, const float* 
   }
   if (!queries || !out_dist || !out_ids || !out_counts)
     return fail(MANS_ERR_INVALID, "null buffer");
+  if (is_group(ctx) != is_group(corpus))
+    return fail(MANS_ERR_INVALID, "corpus and context disagree on the device group");
+  if (is_group(ctx))
+    return group_flat_search(ctx, corpus, queries, nq, dim, k, metric, out_dist, out_ids,
+                             out_counts);
   DeviceGuard g(ctx->device);
   mans_workspace* ws = acquire_workspace(ctx);
   if (!ws) return fail(MANS_ERR_OOM, "cannot create a workspace stream");
@@ -665,6 +705,7 @@ int32_t mans_flat_search_device(mans_ctx* ctx, const mans_corpus* corpus, mans_w
                                 void* cuda_stream) {
   int32_t rc = validate_flat(ctx, corpus, nq, metric);
   if (rc != MANS_OK) return rc;
+  if ((rc = reject_group(ctx, corpus, "mans_flat_search_device")) != MANS_OK) return rc;
   if (!ws || ws->ctx != ctx) return fail(MANS_ERR_INVALID, "workspace missing or foreign");
   DeviceGuard g(ctx->device);
   return run_flat_search(ctx, corpus, ws, d_queries, nq, k, metric, d_out_dist, d_out_ids,
@@ -677,6 +718,7 @@ int32_t mans_topk_merge_device(mans_ctx* ctx, mans_workspace* ws, const float* d
                                int32_t k, float* d_out_dist, uint32_t* d_out_ids,
                                int32_t* d_out_counts, void* cuda_stream) {
   if (!ctx || !ws) return fail(MANS_ERR_INVALID, "null context or workspace");
+  if (int32_t r = reject_group(ctx, nullptr, "mans_topk_merge_device")) return r;
   if (n_lists < 0 || nq < 0 || kin < 0 || list_stride < 0)
     return fail(MANS_ERR_INVALID, "negative size");
   if (nq == 0) return MANS_OK;

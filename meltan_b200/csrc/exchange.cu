@@ -78,6 +78,7 @@ int32_t mans_exchange_create(mans_ctx* ctx, int32_t world, int32_t rank, int64_t
   using namespace mans;
   if (!ctx || !out) return fail(MANS_ERR_INVALID, "null context or output");
   *out = nullptr;
+  if (int32_t r = reject_group(ctx, nullptr, "mans_exchange_create")) return r;
   if (world < 1 || rank < 0 || rank >= world || max_block_words <= 0)
     return fail(MANS_ERR_INVALID, "bad exchange shape");
   DeviceGuard g(ctx->device);

@@ -52,6 +52,9 @@ struct mans_ctx {
   int tc_min_batch = 16;
   // operand format of that path: MANS_TC_AUTO / MANS_TC_BF16 / MANS_TC_INT8
   int tc_format = 0;
+  // A context over several GPUs (mans_ctx_create_multi): one single-device
+  // context per GPU, members[0] on `device`; empty for a plain context.
+  std::vector<mans_ctx*> members;
 };
 
 // Row-major fp32 rows with a 16-byte pitch (ld = dim rounded up to 4), the
@@ -88,6 +91,11 @@ struct mans_corpus {
   mans::TcCorpusStats tc8_plain{};  // L2 / IP bound terms
   mans::TcCorpusStats tc8_cos{};    // cosine: terms relative to |r|
   CUtensorMap tc8_map;
+  // A corpus of a multi-GPU context: contiguous row shards, one per member
+  // device (shard i holds rows [shard_row0[i], shard_row0[i+1])); the fields
+  // above stay empty.  Empty for a single-device corpus.
+  std::vector<mans_corpus*> shards;
+  std::vector<int64_t> shard_row0;
 };
 
 struct mans_workspace {
@@ -123,6 +131,10 @@ struct mans_workspace {
   int64_t launches = 0;  // library kernels enqueued through this workspace
   int last_path = 0;     // path of the last flat search: 0 scan, 1 bf16 tensor, 2 int8 tensor
   int32_t* tc_fallbacks = nullptr;  // device counter of exact re-scans (last tc call)
+  // multi-GPU searches: the packed per-device result blocks land here (on the
+  // first device), and `done` marks the end of this workspace's part
+  mans::DeviceBuffer gather;
+  cudaEvent_t done = nullptr;
 };
 
 namespace mans {
@@ -145,6 +157,18 @@ void timing_end(cudaEvent_t stop, cudaStream_t stream);
 int32_t corpus_upload(mans_ctx* ctx, const float* rows, int64_t n, int64_t dim, uint32_t id_offset,
                       mans_corpus** out, int64_t src_ld = 0);
 void corpus_free(mans_corpus* c);
+// Multi-GPU contexts (group.cu).
+inline bool is_group(const mans_ctx* ctx) { return ctx && !ctx->members.empty(); }
+inline bool is_group(const mans_corpus* c) { return c && !c->shards.empty(); }
+// corpus_upload, or for a multi-GPU context one row shard per device.
+int32_t corpus_create_any(mans_ctx* ctx, const float* rows, int64_t n, int64_t dim,
+                          uint32_t id_offset, mans_corpus** out, int64_t src_ld = 0);
+int32_t group_flat_search(mans_ctx* ctx, const mans_corpus* corpus, const float* queries,
+                          int64_t nq, int64_t dim, int32_t k, int32_t metric, float* out_dist,
+                          uint32_t* out_ids, int32_t* out_counts);
+// MANS_ERR_INVALID for a multi-GPU context or corpus passed to an entry point
+// that runs on one device.
+int32_t reject_group(const mans_ctx* ctx, const mans_corpus* corpus, const char* what);
 // tensor-core batch path (tc_scan.cu)
 // i8: the int8 operand format (else bf16); tc_use_int8 picks it for a batch.
 bool tc_use_int8(const mans_ctx* ctx, int64_t nq);

@@ -405,6 +405,7 @@ int32_t mans_ivf_create(mans_ctx* ctx, const float* centroids, int32_t nlist, in
                         const int64_t* list_offsets, int64_t n, mans_ivf** out_ivf) {
   if (!ctx || !out_ivf) return fail(MANS_ERR_INVALID, "null context or output");
   *out_ivf = nullptr;
+  if (int32_t r = reject_group(ctx, nullptr, "an IVF-flat index")) return r;
   if (nlist <= 0 || dim <= 0 || n < 0) return fail(MANS_ERR_INVALID, "bad IVF shape");
   if (!centroids || !list_offsets || (n > 0 && (!packed_rows || !list_ids)))
     return fail(MANS_ERR_INVALID, "null IVF buffer");
@@ -656,6 +657,7 @@ int32_t mans_ivf_assign(mans_ctx* ctx, mans_corpus* corpus, const float* centroi
                         int32_t nlist, int32_t metric, int32_t* out_assign) {
   if (!ctx || !corpus || !centroids || !out_assign)
     return fail(MANS_ERR_INVALID, "null context, corpus or buffer");
+  if (int32_t r = reject_group(ctx, corpus, "mans_ivf_assign")) return r;
   if (nlist <= 0) return fail(MANS_ERR_INVALID, "nlist must be positive");
   if (metric < 0 || metric > 2) return fail(MANS_ERR_SEARCH, "IVF assignment needs cosine, l2 or ip");
   DeviceGuard g(ctx->device);
@@ -680,6 +682,7 @@ int32_t mans_ivf_build(mans_ctx* ctx, mans_corpus* corpus, const float* centroid
   if (!ctx || !corpus || !centroids || !out_ivf)
     return fail(MANS_ERR_INVALID, "null context, corpus or output");
   *out_ivf = nullptr;
+  if (int32_t r = reject_group(ctx, corpus, "mans_ivf_build")) return r;
   if (nlist <= 0) return fail(MANS_ERR_INVALID, "nlist must be positive");
   if (metric < 0 || metric > 2) return fail(MANS_ERR_SEARCH, "IVF build needs cosine, l2 or ip");
   DeviceGuard g(ctx->device);

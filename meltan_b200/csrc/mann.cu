@@ -205,8 +205,8 @@ int32_t mans_corpus_load_mann(mans_ctx* ctx, const char* path, int32_t shard_ind
   const uint8_t* vec = m.p + info.vector_offset;
   if (info.storage == 0) {
     // fp32 rows straight from the mapped pages
-    return corpus_upload(ctx, reinterpret_cast<const float*>(vec) + r0 * dim, rows, dim,
-                         static_cast<uint32_t>(r0), out_corpus);
+    return corpus_create_any(ctx, reinterpret_cast<const float*>(vec) + r0 * dim, rows, dim,
+                             static_cast<uint32_t>(r0), out_corpus);
   }
   std::vector<float> wide(static_cast<size_t>(std::max<int64_t>(rows, 1)) * dim);
   const uint8_t* src = vec + static_cast<size_t>(r0) * dim * 2;
@@ -215,7 +215,7 @@ int32_t mans_corpus_load_mann(mans_ctx* ctx, const char* path, int32_t shard_ind
     std::memcpy(&h, src + 2 * i, 2);
     wide[i] = half_to_float(h);
   }
-  return corpus_upload(ctx, wide.data(), rows, dim, static_cast<uint32_t>(r0), out_corpus);
+  return corpus_create_any(ctx, wide.data(), rows, dim, static_cast<uint32_t>(r0), out_corpus);
 }
 
 }  // extern "C"

@@ -79,6 +79,7 @@ extern "C" int32_t mans_flat_search_noalloc(mans_ctx* ctx, const mans_corpus* co
                                             void* cuda_stream) {
   if (!ctx || !corpus) return fail(MANS_ERR_INVALID, "null context or corpus");
   if (corpus->ctx != ctx) return fail(MANS_ERR_INVALID, "corpus belongs to another context");
+  if (int32_t r = reject_group(ctx, corpus, "mans_flat_search_noalloc")) return r;
   if (nq < 0) return fail(MANS_ERR_INVALID, "negative query count");
   if (metric == MANS_METRIC_HAMMING)
     return fail(MANS_ERR_SEARCH, "FlatGPUSearch does not support metric .hamming");

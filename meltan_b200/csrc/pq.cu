@@ -745,6 +745,7 @@ int32_t mans_ivfpq_create(mans_ctx* ctx, const float* coarse, int32_t nlist, int
                           const uint32_t* list_positions, int32_t metric, mans_ivfpq** out) {
   if (!ctx || !out) return fail(MANS_ERR_INVALID, "null context or output");
   *out = nullptr;
+  if (int32_t r = reject_group(ctx, nullptr, "an IVF-PQ index")) return r;
   if (nlist <= 0 || dim <= 0 || m <= 0 || n < 0) return fail(MANS_ERR_INVALID, "bad IVF-PQ shape");
   if (ks != 256)
     return fail(MANS_ERR_INVALID, "_IVFPQIndex requires numCentroids == 256 (UInt8 codes)");
@@ -983,6 +984,7 @@ int32_t mans_pq_adc_list(mans_ctx* ctx, const float* query, int64_t dim, const f
                          int32_t m, int32_t ks, const uint8_t* codes, int64_t count,
                          float* out_dist) {
   if (!ctx) return fail(MANS_ERR_INVALID, "null context");
+  if (int32_t r = reject_group(ctx, nullptr, "mans_pq_adc_list")) return r;
   if (count < 0) return fail(MANS_ERR_SEARCH, "Vector count must be non-negative");
   if (m <= 0 || dim <= 0 || dim % m != 0) return fail(MANS_ERR_DIM, "dimensionMismatch");
   if (count == 0) return MANS_OK;
@@ -1105,6 +1107,7 @@ extern "C" int32_t mans_pq_encode(mans_ctx* ctx, const float* vectors, int64_t n
   using namespace mans;
   if (!ctx || (n > 0 && (!vectors || !out_codes)) || !coarse || !codebooks)
     return fail(MANS_ERR_INVALID, "null context or buffer");
+  if (int32_t r = reject_group(ctx, nullptr, "mans_pq_encode")) return r;
   if (n < 0 || dim <= 0 || nlist <= 0 || m <= 0 || ks <= 0 || ks > 256 || dim % m != 0)
     return fail(MANS_ERR_INVALID, "bad PQ shape (dim must split into m subspaces, ks <= 256)");
   if (metric < 0 || metric > 2) return fail(MANS_ERR_SEARCH, "PQ encode needs cosine, l2 or ip");
