@@ -409,6 +409,39 @@ int32_t mans_ivfpq_resolve_device(mans_ctx *ctx, mans_workspace *ws, const int32
                                   float *d_out_dist, uint32_t *d_out_ids, int32_t *d_out_counts,
                                   void *cuda_stream);
 
+/* ---- index training (k-means) -------------------------------------------- */
+
+/* KMeans.cluster's Lloyd iterations (Sources/MetalANNSCore/KMeans.swift:
+ * 95-254) on the device, from the initial centroids the caller passes (the
+ * reference seeds them by k-means++ with Swift's random number API,
+ * KMeans.swift:256-328, which stays with the caller).  Row i's vector is
+ * vectors[i*row_stride + offset .. + dim) (host; offset/dim select a subspace,
+ * as KMeans.clusterSubspace does).  Each iteration assigns every row to the
+ * centroid of smallest SIMDDistance (`metric`, strict '<', first minimum
+ * wins), stops when no assignment changed, else sets every non-empty cluster
+ * to sum * (1 / count) in fp32.  `workers` is the reference's
+ * activeProcessorCount: with workers > 1, n >= 512 and k >= 8 the rows are
+ * summed in `workers` chunks of ceil(n / workers) rows, added in chunk order
+ * (useParallelLloyd), otherwise in one running sum -- the same fp32 order, so
+ * centroids and assignments are bit-equal to the reference's Lloyd loop run
+ * with that many cores.  centroids: host k x dim, read and overwritten;
+ * out_assignments (may be null): host n, the last assignment;
+ * out_iterations (may be null): centroid updates performed.  Validation
+ * follows KMeans.cluster: n = 0 or k outside [1, n] -> MANS_ERR_INVALID. */
+int32_t mans_kmeans_lloyd(mans_ctx *ctx, const float *vectors, int64_t n, int64_t row_stride,
+                          int64_t offset, int64_t dim, int32_t k, int32_t max_iterations,
+                          int32_t metric, int32_t workers, float *centroids,
+                          int32_t *out_assignments, int32_t *out_iterations);
+
+/* ProductQuantizer.train (Sources/MetalANNSCore/ProductQuantizer.swift:10-86)
+ * from initial codebooks: for each of the m subspaces of `vectors` (host,
+ * n x dim), mans_kmeans_lloyd with L2, k = ks = 256 and `max_iterations`.
+ * codebooks: host m x ks x (dim/m), read and overwritten (the
+ * GPUADCSearch.flattenCodebooks order, GPUADCSearch.swift:194-205).  Checks of
+ * the reference: ks must be 256, n >= 256, dim divisible by m. */
+int32_t mans_pq_train(mans_ctx *ctx, const float *vectors, int64_t n, int64_t dim, int32_t m,
+                      int32_t ks, int32_t max_iterations, int32_t workers, float *codebooks);
+
 /* GPUADCSearch.computeDistances(context:query:pq:packedCodes:vectorCount:
  * flatCodebooks:) (GPUADCSearch.swift:35-173): squared-L2 LUT of `query`
  * against the codebooks (pq_compute_distance_table) and the sequential sum

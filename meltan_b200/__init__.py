@@ -33,6 +33,7 @@ from .core import (  # noqa: F401
 from .ivf import IVFFlatSearch, Partition, assign_rows  # noqa: F401,E402
 from .pq import GPUADCSearch, IVFPQIndex  # noqa: F401,E402
 from .pq import encode as pq_encode  # noqa: F401,E402
+from . import train  # noqa: F401,E402
 from . import shard  # noqa: F401,E402
 from .shard import (ShardedFlatSearch, ShardedIVFPQSearch, ShardedIVFSearch,  # noqa: F401,E402
                     row_shard)

@@ -85,6 +85,11 @@ SIGNATURES = {
     "mans_pq_adc_list": (C.c_int32, [_VP, _VP, C.c_int64, _VP, C.c_int32, C.c_int32, _VP,
                                      C.c_int64, _VP]),
     "mans_build_info": (C.c_int32, [C.c_char_p, C.c_size_t]),
+    "mans_kmeans_lloyd": (C.c_int32, [_VP, _VP, C.c_int64, C.c_int64, C.c_int64, C.c_int64,
+                                      C.c_int32, C.c_int32, C.c_int32, C.c_int32, _VP, _VP,
+                                      _VP]),
+    "mans_pq_train": (C.c_int32, [_VP, _VP, C.c_int64, C.c_int64, C.c_int32, C.c_int32,
+                                  C.c_int32, C.c_int32, _VP]),
 }
 
 _lib = None

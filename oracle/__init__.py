@@ -67,6 +67,9 @@ def lib():
                                        _I64, _U32, _F, C.c_int64, C.c_int32, C.c_int32, C.c_int32,
                                        _F, _U32, _I32]
         L.orc_pq_adc.argtypes = [_F, C.c_int32, C.c_int32, _U8, C.c_int64, _F]
+        L.orc_kmeans_lloyd.argtypes = [_F, C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_int32,
+                                       C.c_int32, C.c_int32, C.c_int32, _F, _I32]
+        L.orc_kmeans_lloyd.restype = C.c_int32
         _I8 = C.POINTER(C.c_int8)
         L.orc_i8_dot_rows.argtypes = [_I8, _I8, C.c_int64, C.c_int64, _F]
         L.orc_dot_rows_gather.argtypes = [_F, _F, _U32, C.c_int64, C.c_int64, _F]
@@ -284,6 +287,33 @@ def nearest_coarse(v, coarse, metric):
     v, coarse = f32(v), f32(coarse)
     return int(lib().orc_nearest_coarse(_p(v, _F), _p(coarse, _F), coarse.shape[0],
                                         coarse.shape[1], metric))
+
+
+def kmeans_lloyd(vectors, centroids, max_iter, metric, workers, offset=0, dim=None):
+    """KMeans.cluster's Lloyd iterations (KMeans.swift:95-254) from the given
+    initial centroids; rows' sub-vectors [offset, offset + dim).  Returns
+    (centroids, assignments, updates)."""
+    v = f32(vectors)
+    n, stride = v.shape
+    dim = stride - offset if dim is None else dim
+    cent = np.array(f32(centroids), copy=True)
+    k = cent.shape[0]
+    assign = np.empty(n, np.int32)
+    it = lib().orc_kmeans_lloyd(_p(v, _F), n, stride, offset, dim, k, max_iter, metric, workers,
+                                _p(cent, _F), _p(assign, _I32))
+    return cent, assign, int(it)
+
+
+def pq_train_codebooks(vectors, codebooks, max_iter, workers):
+    """ProductQuantizer.train's per-subspace clustering (ProductQuantizer.swift
+    :10-86: KMeans.clusterSubspace, L2, k = 256) from given initial
+    codebooks (m x ks x sub); returns the trained codebooks."""
+    v = f32(vectors)
+    cb = np.array(f32(codebooks), copy=True)
+    m, ks, sub = cb.shape
+    for s in range(m):
+        cb[s], _, _ = kmeans_lloyd(v, cb[s], max_iter, L2, workers, offset=s * sub, dim=sub)
+    return cb
 
 
 def pq_adc(lut, codes):

@@ -726,6 +726,71 @@ int32_t orc_nearest_coarse(const float *v, const float *coarse, int32_t nlist, i
     return best;
 }
 
+/* KMeans.cluster's Lloyd iterations (Sources/MetalANNSCore/KMeans.swift:
+ * 95-254) from given initial centroids (the k-means++ seeding, :256-328,
+ * stays with the caller).  Row i's sub-vector is vectors[i*stride + offset ..
+ * + dim).  Per iteration: every row goes to the centroid of smallest
+ * SIMDDistance (strict `<` from FLT_MAX: the first minimum wins); the loop
+ * stops before the update when no assignment changed; otherwise each
+ * non-empty cluster becomes sum * (1 / count).  With workers > 1, n >= 512
+ * and k >= 8 the reference splits the rows into `workers` chunks of
+ * ceil(n / workers) (useParallelLloyd, :89-90,103-190): each chunk sums its
+ * rows per cluster in row order from 0, and the chunk sums are added to the
+ * cluster total in chunk order; otherwise one running sum per cluster in row
+ * order (:191-233) -- the same as a single chunk.  All sums are fp32.
+ * Returns the number of centroid updates; assign[i] is the last assignment. */
+int32_t orc_kmeans_lloyd(const float *vectors, int64_t n, int64_t stride, int64_t offset,
+                         int64_t dim, int32_t k, int32_t max_iter, int32_t metric,
+                         int32_t workers, float *centroids, int32_t *assign) {
+    int64_t W = workers < 1 ? 1 : workers;
+    if (W > n) W = n;
+    if (!(W > 1 && n >= 512 && k >= 8)) W = 1;
+    const int64_t chunk = (n + W - 1) / W;
+    float *sums = (float *)calloc((size_t)(W * k * dim), sizeof(float));
+    int64_t *counts = (int64_t *)calloc((size_t)(W * k), sizeof(int64_t));
+    int32_t updates = 0;
+    for (int64_t i = 0; i < n; ++i) assign[i] = -1;
+    for (int32_t it = 0; it < max_iter; ++it) {
+        memset(sums, 0, sizeof(float) * (size_t)(W * k * dim));
+        memset(counts, 0, sizeof(int64_t) * (size_t)(W * k));
+        int changed = 0;
+        for (int64_t i = 0; i < n; ++i) {
+            const float *v = vectors + i * stride + offset;
+            int32_t best = 0;
+            float best_d = FLT_MAX;
+            for (int32_t c = 0; c < k; ++c) {
+                float d = orc_simd_distance(v, centroids + (int64_t)c * dim, dim, metric);
+                if (d < best_d) {
+                    best_d = d;
+                    best = c;
+                }
+            }
+            if (assign[i] != best) changed = 1;
+            assign[i] = best;
+            const int64_t w = i / chunk;
+            counts[w * k + best] += 1;
+            float *acc = sums + (w * k + best) * dim;
+            for (int64_t d = 0; d < dim; ++d) acc[d] = acc[d] + v[d];
+        }
+        if (!changed) break;
+        for (int32_t c = 0; c < k; ++c) {
+            int64_t cnt = 0;
+            for (int64_t w = 0; w < W; ++w) cnt += counts[w * k + c];
+            if (cnt == 0) continue;
+            const float scale = 1.0f / (float)cnt;
+            for (int64_t d = 0; d < dim; ++d) {
+                float total = 0.0f;
+                for (int64_t w = 0; w < W; ++w) total = total + sums[(w * k + c) * dim + d];
+                centroids[(int64_t)c * dim + d] = total * scale;
+            }
+        }
+        ++updates;
+    }
+    free(sums);
+    free(counts);
+    return updates;
+}
+
 /* BoundedSortedList (BoundedSelection.swift:158-214) over (score, payload):
  * best-first by score; an equal-score newcomer is rejected when the list is
  * full and otherwise placed ahead of earlier equal scores (lowerBound). */
