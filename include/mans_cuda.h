@@ -357,7 +357,11 @@ int32_t mans_ivf_search_device(mans_ctx *ctx, mans_ivf *ivf, mans_workspace *ws,
  * order).  ks must be 256 (IVFPQIndex.swift:45-47); metric 0/1/2.
  * list_positions (may be NULL) gives each entry's position in its full list
  * when this index holds one row shard of a larger one, so that insertion
- * order survives the cross-shard merge.  Lists are limited to 2^20 entries. */
+ * order survives the cross-shard merge.  Candidates are ordered by a 32-bit
+ * insertion sequence (probe rank, then list position), so a search with
+ * nprobe p needs every list position below 2^(32 - ceil(log2 p)) (capped at
+ * 2^31): lists of up to 2^27 entries at nprobe 32; beyond that the search
+ * fails with MANS_ERR_SEARCH. */
 int32_t mans_ivfpq_create(mans_ctx *ctx, const float *coarse, int32_t nlist, int64_t dim,
                           const float *codebooks, int32_t m, int32_t ks, const uint8_t *codes,
                           int64_t n, const int64_t *list_offsets, const uint32_t *lists,

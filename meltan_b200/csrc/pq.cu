@@ -25,6 +25,7 @@
 //   and all of L u {K earliest E} lies within the 2K smallest (score, seq)
 //   keys.  Output order: score ascending, newest first among equal scores.
 #include <algorithm>
+#include <cstdio>
 #include <cstring>
 #include <vector>
 
@@ -45,6 +46,7 @@ struct mans_ivfpq {
   int32_t sub = 0;
   int32_t metric = 1;
   int64_t max_len = 0;
+  int64_t max_pos = 0;  // largest list position an entry reports
   mans_corpus* coarse = nullptr;  // coarse centroids (SIMDDistance scoring)
   float* codebooks = nullptr;     // m x ks x sub
   uint8_t* codes = nullptr;       // list-contiguous, n x m
@@ -56,7 +58,14 @@ struct mans_ivfpq {
 namespace mans {
 namespace {
 
-constexpr int kPosBits = 20;  // insertion sequence = probe rank << 20 | list position
+// Insertion sequence of a candidate: probe rank << pos_bits | list position,
+// with pos_bits = 32 - ceil(log2(nprobe)) capped at 31 (a search needs every
+// list position below 2^pos_bits: lists of up to 2^27 entries at nprobe 32).
+inline int32_t seq_pos_bits(int32_t probe) {
+  int rank_bits = 0;
+  while ((1 << rank_bits) < probe) ++rank_bits;
+  return std::min(31, 32 - rank_bits);
+}
 constexpr int kAdcThreads = 128;
 
 struct ResolveParams {
@@ -67,6 +76,7 @@ struct ResolveParams {
   int32_t kin;
   int64_t nq;
   int32_t cap;  // K
+  int32_t pos_bits;  // insertion sequence layout (see seq_pos_bits)
   // seq -> internal id mapping (IVF-PQ candidates); null: payload = seq
   const uint32_t* probe_lists;  // [nq][probe_stride]
   int32_t probe_stride;
@@ -82,8 +92,8 @@ __device__ __forceinline__ uint32_t resolve_payload(const ResolveParams& p, int6
   uint32_t seq = p.in_seq[q * p.kin + i];
   if (p.in_payload) return p.in_payload[q * p.kin + i];
   if (!p.probe_lists) return seq;
-  uint32_t rank = seq >> kPosBits;
-  uint32_t pos = seq & ((1u << kPosBits) - 1u);
+  uint32_t rank = seq >> p.pos_bits;
+  uint32_t pos = seq & ((1u << p.pos_bits) - 1u);
   uint32_t list = p.probe_lists[q * p.probe_stride + rank];
   return p.ids[p.offsets[list] + pos];
 }
@@ -172,6 +182,7 @@ struct AdcParams {
   const uint32_t* probe_lists;  // [nq][probe]
   const int32_t* probe_counts;
   int32_t probe;
+  int32_t pos_bits;         // insertion sequence layout (see seq_pos_bits)
   int64_t nq;
   int32_t dim, m, ks, sub, metric;
   int32_t k;   // candidates kept per (query, list)
@@ -353,7 +364,7 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
             total = adc_sum(lut, p.ks, p.codes + (off + e) * p.m, p.m);
             pos = p.pos ? p.pos[off + e] : static_cast<uint32_t>(e);
           }
-          key = make_key(total, (static_cast<uint32_t>(pr) << kPosBits) | pos);
+          key = make_key(total, (static_cast<uint32_t>(pr) << p.pos_bits) | pos);
         }
         w = wn;
         ps = psn;
@@ -395,7 +406,7 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
       if (valid) {
         const float total = adc_sum(lut, p.ks, p.codes + (off + e) * p.m, p.m);
         const uint32_t pos = p.pos ? p.pos[off + e] : static_cast<uint32_t>(e);
-        key = make_key(total, (static_cast<uint32_t>(pr) << kPosBits) | pos);
+        key = make_key(total, (static_cast<uint32_t>(pr) << p.pos_bits) | pos);
       }
       topk_offer(st, p.kp, key, valid);
       __syncthreads();
@@ -442,8 +453,8 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_list_kernel(
 namespace {
 
 // Shard output of the IVF-PQ search: the (score, seq) 2k-lists of the merge
-// step with each entry's internal id.  seq = probe rank << 20 | the entry's
-// position in its global list; a shard's list holds a subset of the global
+// step with each entry's internal id.  seq = probe rank << pos_bits | the
+// entry's position in its global list; a shard's list holds a subset of the global
 // entries with their global positions (`pos`, ascending), found by binary
 // search.
 __global__ void ivfpq_payload_kernel(int64_t nq, int32_t kin, const float* __restrict__ md,
@@ -452,15 +463,16 @@ __global__ void ivfpq_payload_kernel(int64_t nq, int32_t kin, const float* __res
                                      const uint32_t* __restrict__ probe_lists, int32_t probe,
                                      const int64_t* __restrict__ offsets,
                                      const uint32_t* __restrict__ ids,
-                                     const uint32_t* __restrict__ pos, float* out_score,
-                                     uint32_t* out_seq, uint32_t* out_id, int32_t* out_count) {
+                                     const uint32_t* __restrict__ pos, int32_t pos_bits,
+                                     float* out_score, uint32_t* out_seq, uint32_t* out_id,
+                                     int32_t* out_count) {
   const int64_t q = blockIdx.x;
   const int cnt = mc[q];
   for (int i = threadIdx.x; i < kin; i += blockDim.x) {
     const int64_t at = q * kin + i;
     if (i < cnt) {
       const uint32_t seq = mi[at];
-      const uint32_t rank = seq >> kPosBits, gpos = seq & ((1u << kPosBits) - 1u);
+      const uint32_t rank = seq >> pos_bits, gpos = seq & ((1u << pos_bits) - 1u);
       const uint32_t list = probe_lists[q * probe + rank];
       const int64_t off = offsets[list], len = offsets[list + 1] - off;
       int64_t idx = gpos;
@@ -576,6 +588,15 @@ static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* w
   const int32_t probe = std::max(1, std::min(nprobe, ix->nlist));
   const int32_t kc = std::min<int32_t>(2 * probe, ix->nlist);  // coarse candidates
   if (kc > 512) return fail(MANS_ERR_SEARCH, "nprobe above 256 is not supported on the GPU");
+  const int32_t pos_bits = seq_pos_bits(probe);
+  if (ix->max_pos >= (int64_t{1} << pos_bits)) {
+    char msg[160];
+    std::snprintf(msg, sizeof msg,
+                  "list position %lld does not fit the insertion sequence at nprobe %d "
+                  "(positions below 2^%d)",
+                  static_cast<long long>(ix->max_pos), probe, pos_bits);
+    return fail(MANS_ERR_SEARCH, msg);
+  }
   const int32_t k2 = 2 * kout;  // ADC candidates per list and after the merge
   const int32_t kp2 = pow2_at_least(k2);
 
@@ -646,6 +667,7 @@ static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* w
   a.probe_lists = pl;
   a.probe_counts = pc;
   a.probe = probe;
+  a.pos_bits = pos_bits;
   a.nq = nq;
   a.dim = static_cast<int32_t>(ix->dim);
   a.m = ix->m;
@@ -706,7 +728,8 @@ static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* w
     uint32_t* pi_ = reinterpret_cast<uint32_t*>(partial) + 2 * nq * k2;
     int32_t* pc_ = partial + 3 * nq * k2;
     ivfpq_payload_kernel<<<static_cast<unsigned>(nq), 128, 0, stream>>>(
-        nq, k2, md, mi, mc, pl, probe, ix->offsets, ix->ids, ix->pos, ps_, pq_, pi_, pc_);
+        nq, k2, md, mi, mc, pl, probe, ix->offsets, ix->ids, ix->pos, pos_bits, ps_, pq_, pi_,
+        pc_);
     e = cudaGetLastError();
     if (e != cudaSuccess) return fail_cuda(e, "payload launch");
     ws->launches += 4;
@@ -720,6 +743,7 @@ static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* w
   f.kin = k2;
   f.nq = nq;
   f.cap = kout;
+  f.pos_bits = pos_bits;
   f.probe_lists = pl;
   f.probe_stride = probe;
   f.offsets = ix->offsets;
@@ -763,13 +787,10 @@ int32_t mans_ivfpq_create(mans_ctx* ctx, const float* coarse, int32_t nlist, int
   }
   for (int64_t i = 0; i < total; ++i)
     if (lists[i] >= static_cast<uint64_t>(n)) return fail(MANS_ERR_INVALID, "list id out of range");
-  if (max_len >= (1 << kPosBits) ||
-      (list_positions && [&] {
-        for (int64_t i = 0; i < total; ++i)
-          if (list_positions[i] >= (1u << kPosBits)) return true;
-        return false;
-      }()))
-    return fail(MANS_ERR_INVALID, "inverted list longer than 2^20 entries");
+  int64_t max_pos = max_len - 1;
+  if (list_positions)
+    for (int64_t i = 0; i < total; ++i)
+      max_pos = std::max<int64_t>(max_pos, list_positions[i]);
   DeviceGuard g(ctx->device);
   mans_ivfpq* ix = new mans_ivfpq();
   ix->ctx = ctx;
@@ -781,6 +802,7 @@ int32_t mans_ivfpq_create(mans_ctx* ctx, const float* coarse, int32_t nlist, int
   ix->sub = static_cast<int32_t>(dim / m);
   ix->metric = metric;
   ix->max_len = max_len;
+  ix->max_pos = max_pos;
   // gather codes into list order on the host (codes are stored per internal id)
   std::vector<uint8_t> packed(static_cast<size_t>(std::max<int64_t>(total, 1)) * m);
   for (int64_t i = 0; i < total; ++i)

@@ -249,3 +249,35 @@ def test_list_sharded_ivfpq_equals_unsharded(ctx, shards):
         for ix in idx:
             ix.close()
     ws.close()
+
+
+def test_ivfpq_list_longer_than_2_pow_20(ctx):
+    """One inverted list of 1.1M entries (beyond 2^20), searched at nprobe 1
+    and 2 against the oracle; positions that cannot fit the 32-bit insertion
+    sequence at a given nprobe fail with searchFailed instead of merging
+    wrongly."""
+    rng = np.random.default_rng(31)
+    n, dim, m = 1_100_000, 8, 4
+    coarse = np.stack([np.zeros(dim, np.float32), np.full(dim, 100, np.float32)])
+    cb = (rng.standard_normal((m, 256, dim // m)) * 0.5).astype(np.float32)
+    codes = rng.integers(0, 256, (n, m)).astype(np.uint8)
+    codes[::7] = codes[3]  # many equal scores: the tie order spans the whole list
+    offsets = np.array([0, n - 3, n], np.int64)
+    lists = np.arange(n, dtype=np.uint32)
+    q = (rng.standard_normal((3, dim)) * 0.3).astype(np.float32)
+    ix = mb.IVFPQIndex(ctx, coarse, cb, codes, (offsets, lists))
+    for nprobe in (1, 2):
+        same(ix.search_arrays(q, 50, nprobe),
+             O.ivfpq_search(coarse, cb, codes, offsets, lists, q, 50, nprobe, O.L2))
+    ix.close()
+    # a shard whose entries report positions up to 2^29 + 2: fine at nprobe 4
+    # (positions below 2^30), rejected at nprobe 8 (below 2^29)
+    coarse8 = (rng.standard_normal((8, dim)) * 0.1).astype(np.float32)
+    small = np.array([0, 3, 6, 6, 6, 6, 6, 6, 6], np.int64)
+    pos = np.array([0, 1, (1 << 29) + 2, 0, 1, 2], np.uint32)
+    ixs = mb.IVFPQIndex(ctx, coarse8, cb, codes[:6], (small, np.arange(6, dtype=np.uint32)),
+                        list_positions=pos)
+    ixs.search_arrays(q, 5, 4)
+    with pytest.raises(mb.SearchFailed):
+        ixs.search_arrays(q, 5, 8)
+    ixs.close()
