@@ -72,41 +72,6 @@ __device__ __forceinline__ int list_chunks(const int64_t* off, int l, int chunk)
   return static_cast<int>((len + chunk - 1) / chunk);
 }
 
-// Exclusive prefix sum of in[0, n) into out[0, n] by the whole block.
-__device__ void block_exclusive_scan(const int32_t* in, int n, int32_t* out, int32_t* part) {
-  const int t = threadIdx.x, nt = blockDim.x;
-  const int per = (n + nt - 1) / nt;
-  const int b = t * per;
-  const int e = min(n, b + per);
-  int32_t sum = 0;
-  for (int i = b; i < e; ++i) sum += in[i];
-  // warp-level inclusive scan of the per-thread sums, then across warps
-  const int lane = t & 31, w = t >> 5;
-  int32_t v = sum;
-  for (int o = 1; o < 32; o <<= 1) {
-    int32_t u = __shfl_up_sync(0xFFFFFFFFu, v, o);
-    if (lane >= o) v += u;
-  }
-  if (lane == 31) part[w] = v;
-  __syncthreads();
-  if (w == 0) {
-    int32_t x = lane < (nt >> 5) ? part[lane] : 0;
-    for (int o = 1; o < 32; o <<= 1) {
-      int32_t u = __shfl_up_sync(0xFFFFFFFFu, x, o);
-      if (lane >= o) x += u;
-    }
-    part[32 + lane] = x;  // inclusive warp totals
-  }
-  __syncthreads();
-  int32_t acc = v - sum + (w > 0 ? part[32 + w - 1] : 0);
-  for (int i = b; i < e; ++i) {
-    out[i] = acc;
-    acc += in[i];
-  }
-  if (t == nt - 1) out[n] = acc;
-  __syncthreads();
-}
-
 __global__ void __launch_bounds__(kPlanThreads) ivf_plan_kernel(const PlanParams p) {
   __shared__ int32_t part[64];
   const int t = threadIdx.x, nt = blockDim.x;

@@ -419,6 +419,267 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
   }
 }
 
+// ---- grouped ADC: the queries that probe one list share its code reads -----
+//
+// For a batch, most lists are probed by several queries (C4: 32,768 (query,
+// list) pairs over 4,096 lists).  adc_group_plan_kernel groups the pairs by
+// list and cuts each group into tiles of up to kAdcGroup queries; a tile is
+// one item of pq_adc_group_kernel, which builds the tile's tables interleaved
+// (entry (s, c) of its W queries side by side, W = 1, 2 or 4 by the tile's
+// query count) and reads every code row once for all of them: one 16-byte
+// code load and one W-wide table load per subspace serve W queries, and a
+// W-wide load of random entries costs fewer shared-memory wavefronts per
+// entry than W single loads.  Each query keeps its own sequential fp32 sum
+// and its own warp-resident top-k, so every (query, list) slot gets exactly
+// the keys of pq_adc_kernel.
+
+constexpr int kAdcGroup = 4;
+constexpr int kAdcPlanThreads = 1024;
+constexpr int64_t kAdcGroupMinQueries = 16;  // smaller batches share few lists
+
+struct AdcGroupPlan {
+  const uint32_t* probe_lists;  // [nq][probe]
+  const int32_t* probe_counts;  // [nq]
+  int64_t nq;
+  int32_t probe;
+  int32_t nlist;
+  int32_t* list_cnt;    // [nlist] scratch
+  int32_t* list_off;    // [nlist + 1]: the pairs of list l at grouped[list_off[l] ..)
+  int32_t* tile_off;    // [nlist + 1]
+  int32_t* grouped;     // [nq * probe] pair (item) indices q * probe + rank, by list
+  int32_t* tile_list;   // [nq * probe]
+  int32_t* tile_first;  // [nq * probe]
+  int32_t* ntiles;      // [1]
+  int32_t* slot_counts; // pairs without a list (rank >= probe count) get 0 here
+};
+
+// One block: counting sort of the (query, rank) pairs by list (the order
+// inside a list does not matter: every pair owns its output slot) and the
+// tile table.
+__global__ void __launch_bounds__(kAdcPlanThreads) adc_group_plan_kernel(const AdcGroupPlan g) {
+  __shared__ int32_t part[64];
+  const int t = threadIdx.x, nt = blockDim.x;
+  const int64_t items = g.nq * g.probe;
+  for (int l = t; l < g.nlist; l += nt) g.list_cnt[l] = 0;
+  __syncthreads();
+  for (int64_t i = t; i < items; i += nt) {
+    const int64_t q = i / g.probe;
+    const int r = static_cast<int>(i - q * g.probe);
+    if (r < g.probe_counts[q])
+      atomicAdd(&g.list_cnt[g.probe_lists[i]], 1);
+    else
+      g.slot_counts[i] = 0;
+  }
+  __syncthreads();
+  block_exclusive_scan(g.list_cnt, g.nlist, g.list_off, part);
+  for (int l = t; l < g.nlist; l += nt) g.list_cnt[l] = (g.list_cnt[l] + kAdcGroup - 1) / kAdcGroup;
+  __syncthreads();
+  block_exclusive_scan(g.list_cnt, g.nlist, g.tile_off, part);
+  for (int l = t; l < g.nlist; l += nt) g.list_cnt[l] = 0;
+  __syncthreads();
+  for (int64_t i = t; i < items; i += nt) {
+    const int64_t q = i / g.probe;
+    const int r = static_cast<int>(i - q * g.probe);
+    if (r < g.probe_counts[q]) {
+      const uint32_t l = g.probe_lists[i];
+      const int at = atomicAdd(&g.list_cnt[l], 1);
+      g.grouped[g.list_off[l] + at] = static_cast<int32_t>(i);
+    }
+  }
+  for (int l = t; l < g.nlist; l += nt) {
+    const int t0 = g.tile_off[l], t1 = g.tile_off[l + 1];
+    for (int j = t0; j < t1; ++j) {
+      g.tile_list[j] = l;
+      g.tile_first[j] = g.list_off[l] + (j - t0) * kAdcGroup;
+    }
+  }
+  if (t == 0) *g.ntiles = g.tile_off[g.nlist];
+}
+
+// Offers one key per lane to the warp's ascending list of its k smallest keys
+// (lane i holds the (i+1)-th): a batch where more than six keys beat the k-th
+// is sorted by shuffles and merged in, fewer are inserted at their rank.
+__device__ __forceinline__ uint64_t warp_topk_offer(uint64_t best, uint64_t key, int k,
+                                                    int lane) {
+  const uint64_t kth = __shfl_sync(0xFFFFFFFFu, best, k - 1);
+  uint32_t pass = __ballot_sync(0xFFFFFFFFu, key < kth);
+  if (__popc(pass) > 6) return warp_merge32(best, warp_sort32(key < kth ? key : kKeyMax, lane), lane);
+  while (pass) {
+    const int src = __ffs(pass) - 1;
+    pass &= pass - 1;
+    const uint64_t x = __shfl_sync(0xFFFFFFFFu, key, src);
+    const int at = __popc(__ballot_sync(0xFFFFFFFFu, best < x));
+    const uint64_t up = __shfl_up_sync(0xFFFFFFFFu, best, 1);
+    best = lane < at ? best : (lane == at ? x : up);
+  }
+  return best;
+}
+
+template <int W>
+struct LutVec;
+template <>
+struct LutVec<1> {
+  using T = float;
+  __device__ static float get(const T& v, int j) { return v; }
+  __device__ static T make(const float* v) { return v[0]; }
+};
+template <>
+struct LutVec<2> {
+  using T = float2;
+  __device__ static float get(const T& v, int j) { return j == 0 ? v.x : v.y; }
+  __device__ static T make(const float* v) { return make_float2(v[0], v[1]); }
+};
+template <>
+struct LutVec<4> {
+  using T = float4;
+  __device__ static float get(const T& v, int j) {
+    return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
+  }
+  __device__ static T make(const float* v) { return make_float4(v[0], v[1], v[2], v[3]); }
+};
+
+// One tile: W-wide tables for its `cnt` queries (cnt <= W), then the scan of
+// the list's m = 16 code rows with W sequential sums per row.  The caller
+// has the residuals in shared memory and synchronises before and after.
+template <int W>
+__device__ __forceinline__ void adc_group_tile(const AdcParams& p, uint8_t* lut_raw,
+                                               const float* resid, const int32_t* s_item,
+                                               int cnt, int64_t off, int64_t len,
+                                               uint64_t (*wlist)[kAdcGroup][32]) {
+  using V = typename LutVec<W>::T;
+  V* lut = reinterpret_cast<V*>(lut_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float* cb = p.codebooks;
+  for (int e = tid; e < p.m * p.ks; e += kAdcThreads) {
+    const int s = e / p.ks;
+    float v[W];
+    if (p.metric == kL2 && p.sub == 8) {
+      const float4* c4 = reinterpret_cast<const float4*>(cb + static_cast<int64_t>(e) * 8);
+      const float4 a = __ldg(c4), b = __ldg(c4 + 1);
+      const float cw[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int j = 0; j < W; ++j) {
+        const float* r = resid + j * p.dim + s * 8;
+        float sum = 0.0f;
+#pragma unroll
+        for (int d = 0; d < 8; ++d) {
+          const float t = __fsub_rn(r[d], cw[d]);
+          sum = __fadd_rn(sum, __fmul_rn(t, t));
+        }
+        v[j] = sum;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < W; ++j)
+        v[j] = lut_entry(p.metric, resid + j * p.dim + s * p.sub,
+                         cb + static_cast<int64_t>(e) * p.sub, p.sub);
+    }
+    lut[e] = LutVec<W>::make(v);
+  }
+  __syncthreads();
+  uint32_t seqhi[W];
+#pragma unroll
+  for (int j = 0; j < W; ++j) {
+    const int32_t it = s_item[j < cnt ? j : 0];
+    seqhi[j] = static_cast<uint32_t>(it - (it / p.probe) * p.probe) << p.pos_bits;
+  }
+  uint64_t best[W];
+#pragma unroll
+  for (int j = 0; j < W; ++j) best[j] = kKeyMax;
+  const uint4* crow = reinterpret_cast<const uint4*>(p.codes + off * 16);
+  auto fetch = [&](int64_t e, uint4& w, uint32_t& ps) {
+    if (e < len) {
+      w = __ldg(crow + e);
+      ps = p.pos ? __ldg(p.pos + off + e) : static_cast<uint32_t>(e);
+    }
+  };
+  uint4 w = make_uint4(0u, 0u, 0u, 0u);
+  uint32_t ps = 0;
+  fetch(static_cast<int64_t>(warp) * 32 + lane, w, ps);
+  for (int64_t b = static_cast<int64_t>(warp) * 32; b < len; b += kAdcThreads) {
+    const int64_t e = b + lane;
+    uint4 wn = w;
+    uint32_t psn = ps;
+    fetch(e + kAdcThreads, wn, psn);
+    float acc[W];
+#pragma unroll
+    for (int j = 0; j < W; ++j) acc[j] = 0.0f;
+    if (e < len) {
+      const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) {
+        const V x = lut[jj * p.ks + ((words[jj >> 2] >> (8 * (jj & 3))) & 0xFFu)];
+#pragma unroll
+        for (int j = 0; j < W; ++j) acc[j] = __fadd_rn(acc[j], LutVec<W>::get(x, j));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+      if (j < cnt) {
+        const uint64_t key = e < len ? make_key(acc[j], seqhi[j] | ps) : kKeyMax;
+        best[j] = warp_topk_offer(best[j], key, p.k, lane);
+      }
+    }
+    w = wn;
+    ps = psn;
+  }
+#pragma unroll
+  for (int j = 0; j < W; ++j) wlist[warp][j][lane] = best[j];
+  __syncthreads();
+  for (int j = warp; j < cnt; j += kAdcThreads / 32) {
+    uint64_t bb = wlist[0][j][lane];
+#pragma unroll
+    for (int ow = 1; ow < kAdcThreads / 32; ++ow) bb = warp_merge32(bb, wlist[ow][j][lane], lane);
+    const int have = static_cast<int>(len < p.k ? len : p.k);
+    const int64_t it = s_item[j];
+    if (lane < have) p.slot_keys[it * p.kp + lane] = bb;
+    if (lane == 0) p.slot_counts[it] = have;
+  }
+}
+
+// Persistent over the tiles of adc_group_plan_kernel (m = 16, k <= 32 kept
+// per (query, list)).
+__global__ void __launch_bounds__(kAdcThreads) pq_adc_group_kernel(
+    const AdcParams p, const int32_t* __restrict__ grouped, const int32_t* __restrict__ list_off,
+    const int32_t* __restrict__ tile_list, const int32_t* __restrict__ tile_first,
+    const int32_t* __restrict__ ntiles_ptr) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* lut_raw =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<size_t>(smem_raw) + 15) / 16 * 16);
+  float* resid = reinterpret_cast<float*>(lut_raw + static_cast<size_t>(p.m) * p.ks * 16);
+  __shared__ uint64_t wlist[kAdcThreads / 32][kAdcGroup][32];
+  __shared__ int32_t s_item[kAdcGroup];
+  const int tid = threadIdx.x;
+  const int ntiles = *ntiles_ptr;
+  for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    __syncthreads();  // the previous tile is done with the shared buffers
+    const int list = tile_list[t];
+    const int first = tile_first[t];
+    const int cnt = min(kAdcGroup, list_off[list + 1] - first);
+    if (tid < kAdcGroup) s_item[tid] = grouped[first + min(tid, cnt - 1)];
+    const int64_t off = p.offsets[list];
+    const int64_t len = p.offsets[list + 1] - off;
+    __syncthreads();
+    if (len == 0) {  // an empty list (a shard holding other lists): no table to build
+      if (tid < cnt) p.slot_counts[s_item[tid]] = 0;
+      continue;
+    }
+    const int wq = cnt == 1 ? 1 : cnt == 2 ? 2 : 4;  // table width
+    for (int idx = tid; idx < wq * p.dim; idx += kAdcThreads) {
+      const int j = idx / p.dim, d = idx - j * p.dim;
+      const int64_t q = s_item[j < cnt ? j : 0] / p.probe;
+      resid[idx] = __fsub_rn(p.queries[q * p.dim + d], p.coarse[list * p.coarse_ld + d]);
+    }
+    __syncthreads();
+    if (wq == 1)
+      adc_group_tile<1>(p, lut_raw, resid, s_item, cnt, off, len, wlist);
+    else if (wq == 2)
+      adc_group_tile<2>(p, lut_raw, resid, s_item, cnt, off, len, wlist);
+    else
+      adc_group_tile<4>(p, lut_raw, resid, s_item, cnt, off, len, wlist);
+  }
+}
+
 // GPUADCSearch.computeDistances for one list (GPUADCSearch.swift:35-173 with
 // pq_compute_distance_table + pq_adc_scan, PQDistance.metal:4-66): a squared
 // L2 LUT over the query, then the sequential sum per code.  Every block
@@ -610,6 +871,21 @@ static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* w
   const size_t o_md = carve(o, nq * k2 * sizeof(float));
   const size_t o_mi = carve(o, nq * k2 * sizeof(uint32_t));
   const size_t o_mc = carve(o, nq * sizeof(int32_t));
+  // batches of m = 16 codes with at most 32 kept keys per list run the grouped
+  // ADC (the queries probing one list share its code reads)
+  const bool grouped = 2 * kout <= 32 && ix->m == 16 && nq >= kAdcGroupMinQueries &&
+                       16 + static_cast<size_t>(ix->m) * ix->ks * 16 +
+                               static_cast<size_t>(kAdcGroup) * ix->dim * 4 <=
+                           static_cast<size_t>(ctx->max_smem) - 5120;
+  const int64_t items_all = nq * probe;
+  if (items_all > INT32_MAX) return fail(MANS_ERR_SEARCH, "query batch too large");
+  const size_t o_gl = carve(o, grouped ? ix->nlist * sizeof(int32_t) : 0);
+  const size_t o_go = carve(o, grouped ? (ix->nlist + 1) * sizeof(int32_t) : 0);
+  const size_t o_gt = carve(o, grouped ? (ix->nlist + 1) * sizeof(int32_t) : 0);
+  const size_t o_gg = carve(o, grouped ? items_all * sizeof(int32_t) : 0);
+  const size_t o_gtl = carve(o, grouped ? items_all * sizeof(int32_t) : 0);
+  const size_t o_gtf = carve(o, grouped ? items_all * sizeof(int32_t) : 0);
+  const size_t o_gn = carve(o, grouped ? sizeof(int32_t) : 0);
   int32_t rc;
   if ((rc = ws->aux2.reserve(o)) != MANS_OK) return rc;
   // slot buffers: coarse search and ADC items, reserved once before any launch
@@ -679,6 +955,44 @@ static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* w
   a.slot_keys = static_cast<uint64_t*>(ws->slot_keys.ptr);
   a.slot_counts = static_cast<int32_t*>(ws->slot_counts.ptr);
   a.sortn = std::max(512, pow2_at_least(kp2 + kAdcThreads));
+  if (grouped) {
+    AdcGroupPlan gp{};
+    gp.probe_lists = pl;
+    gp.probe_counts = pc;
+    gp.nq = nq;
+    gp.probe = probe;
+    gp.nlist = ix->nlist;
+    gp.list_cnt = reinterpret_cast<int32_t*>(A + o_gl);
+    gp.list_off = reinterpret_cast<int32_t*>(A + o_go);
+    gp.tile_off = reinterpret_cast<int32_t*>(A + o_gt);
+    gp.grouped = reinterpret_cast<int32_t*>(A + o_gg);
+    gp.tile_list = reinterpret_cast<int32_t*>(A + o_gtl);
+    gp.tile_first = reinterpret_cast<int32_t*>(A + o_gtf);
+    gp.ntiles = reinterpret_cast<int32_t*>(A + o_gn);
+    gp.slot_counts = a.slot_counts;
+    adc_group_plan_kernel<<<1, kAdcPlanThreads, 0, stream>>>(gp);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_cuda(e, "adc plan launch");
+    const size_t gsmem = 16 + static_cast<size_t>(ix->m) * ix->ks * 16 +
+                         static_cast<size_t>(kAdcGroup) * ix->dim * 4;
+    e = cudaFuncSetAttribute(pq_adc_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(gsmem));
+    if (e != cudaSuccess) return fail_cuda(e, "grouped adc configure");
+    int per_sm = 1;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pq_adc_group_kernel, kAdcThreads,
+                                                      gsmem);
+    if (e != cudaSuccess) return fail_cuda(e, "grouped adc occupancy");
+    const int grid = static_cast<int>(std::min<int64_t>(
+        items_all, static_cast<int64_t>(ctx->num_sms) * std::max(1, per_sm)));
+    cudaEvent_t stop = timing_begin(ws, stream);
+    pq_adc_group_kernel<<<grid, kAdcThreads, gsmem, stream>>>(a, gp.grouped, gp.list_off,
+                                                              gp.tile_list, gp.tile_first,
+                                                              gp.ntiles);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_cuda(e, "grouped adc launch");
+    timing_end(stop, stream);
+    ws->launches += 1;
+  }
   // up to 32 kept keys per item: warp-resident lists, no shared top-k buffer
   const bool warp_topk = k2 <= 32;
   const void* kfn = warp_topk ? reinterpret_cast<const void*>(pq_adc_kernel<true>)
@@ -697,14 +1011,16 @@ static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* w
   const int64_t items = nq * probe;
   const int grid = static_cast<int>(
       std::min<int64_t>(items, static_cast<int64_t>(ctx->num_sms) * std::max(1, per_sm)));
-  cudaEvent_t stop = timing_begin(ws, stream);
-  if (warp_topk)
-    pq_adc_kernel<true><<<grid, kAdcThreads, smem, stream>>>(a);
-  else
-    pq_adc_kernel<false><<<grid, kAdcThreads, smem, stream>>>(a);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return fail_cuda(e, "adc launch");
-  timing_end(stop, stream);
+  if (!grouped) {
+    cudaEvent_t stop = timing_begin(ws, stream);
+    if (warp_topk)
+      pq_adc_kernel<true><<<grid, kAdcThreads, smem, stream>>>(a);
+    else
+      pq_adc_kernel<false><<<grid, kAdcThreads, smem, stream>>>(a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_cuda(e, "adc launch");
+    timing_end(stop, stream);
+  }
 
   // 3. 2k smallest (score, seq) per query over its probed lists
   MergeParams m{};

@@ -281,3 +281,71 @@ def test_ivfpq_list_longer_than_2_pow_20(ctx):
     with pytest.raises(mb.SearchFailed):
         ixs.search_arrays(q, 5, 8)
     ixs.close()
+
+
+@pytest.mark.parametrize("metric", [O.L2, O.COSINE, O.IP])
+@pytest.mark.parametrize("dim", [64, 128])
+def test_ivfpq_grouped_batches(ctx, metric, dim):
+    """Batches of >= 16 queries with m = 16 and k <= 16 run the grouped ADC
+    (the queries probing one list share its code reads, tables built 1, 2 or
+    4 wide by the tile's query count).  Queries drawn near a few centroids
+    make hot lists (many tiles per list), duplicate codes make ties; every
+    query equals the oracle, ids, scores and tie order."""
+    rng = np.random.default_rng(dim + metric)
+    n, m, nlist = 12000, 16, 40
+    v, _ = bench.make_mixture(n, dim, 30, 1, sigma=0.3, seed=dim)
+    coarse = v[rng.choice(n, nlist, replace=False)].copy()
+    cb = (rng.standard_normal((m, 256, dim // m)) * 0.2).astype(np.float32)
+    codes, offsets, flat = encode_all(v, coarse, cb, metric)
+    codes[flat[: len(flat) // 3: 5]] = codes[flat[0]]  # many equal scores
+    hot = coarse[:3][rng.integers(0, 3, 300)] + np.float32(0.05) * rng.standard_normal(
+        (300, dim), dtype=np.float32)
+    ix = mb.IVFPQIndex(ctx, coarse, cb, codes, (offsets, flat), metric=mb.Metric(metric))
+    for nq, q in ((16, hot[:16]), (41, hot[:41]), (300, hot)):
+        for k, nprobe in ((1, 1), (5, 3), (10, 8), (16, nlist)):
+            same(ix.search_arrays(q, k, nprobe),
+                 O.ivfpq_search(coarse, cb, codes, offsets, flat, q, k, nprobe, metric))
+    ix.close()
+
+
+@pytest.mark.parametrize("shards", [2, 3])
+def test_list_sharded_grouped_ivfpq(ctx, shards):
+    """List shards through the grouped ADC (m = 16, 64 queries): the shards'
+    blocks, merged and resolved, equal the oracle on the whole index."""
+    import torch
+    from meltan_b200 import pq as mpq
+    rng = np.random.default_rng(35)
+    n, dim, m, nlist = 8000, 64, 16, 30
+    v = rng.standard_normal((n, dim), dtype=np.float32)
+    coarse = v[rng.choice(n, nlist, replace=False)].copy()
+    cb = rng.standard_normal((m, 256, dim // m), dtype=np.float32)
+    codes, assign = mb.pq_encode(ctx, v, coarse, cb)
+    codes[5000:5200] = codes[10]
+    flat = np.argsort(assign, kind="stable").astype(np.uint32)
+    off = np.concatenate([[0], np.cumsum(np.bincount(assign, minlength=nlist))]).astype(np.int64)
+    owner = mpq.list_owners(np.diff(off), shards)
+    q = rng.standard_normal((64, dim), dtype=np.float32)
+    ws = mb.Workspace(ctx)
+    dq = torch.from_numpy(q).cuda()
+    for k, nprobe in ((10, 4), (16, 30)):
+        words = mpq.partial_words(len(q), k)
+        blocks = torch.empty((shards, words), dtype=torch.int32, device="cuda")
+        idx = []
+        for s_ in range(shards):
+            soff, sflat, spos = mb.IVFPQIndex.shard_lists_by_list(off, flat, owner == s_)
+            ix = mb.IVFPQIndex(ctx, coarse, cb, codes, (soff, sflat), list_positions=spos)
+            ix.search_partial_device(ws, dq.data_ptr(), len(q), k, nprobe, blocks[s_].data_ptr())
+            idx.append(ix)
+        od = torch.empty((len(q), k), dtype=torch.float32, device="cuda")
+        oi = torch.empty((len(q), k), dtype=torch.int32, device="cuda")
+        oc = torch.empty((len(q),), dtype=torch.int32, device="cuda")
+        mpq.resolve_device(ctx, ws, blocks.data_ptr(), shards, words, len(q), k, od.data_ptr(),
+                           oi.data_ptr(), oc.data_ptr())
+        ws.check()
+        want = O.ivfpq_search(coarse, cb, codes, off, flat, q, k, nprobe, O.L2)
+        np.testing.assert_array_equal(oc.cpu().numpy(), want[2])
+        np.testing.assert_array_equal(oi.cpu().numpy().view(np.uint32), want[1])
+        np.testing.assert_array_equal(od.cpu().numpy(), want[0])
+        for ix in idx:
+            ix.close()
+    ws.close()
