@@ -82,6 +82,7 @@ struct ResolveParams {
   int32_t probe_stride;
   const int64_t* offsets;
   const uint32_t* ids;
+  const uint32_t* pos;  // optional: each entry's position in its global list
   float* out_score;
   uint32_t* out_id;
   int32_t* out_count;
@@ -95,7 +96,19 @@ __device__ __forceinline__ uint32_t resolve_payload(const ResolveParams& p, int6
   uint32_t rank = seq >> p.pos_bits;
   uint32_t pos = seq & ((1u << p.pos_bits) - 1u);
   uint32_t list = p.probe_lists[q * p.probe_stride + rank];
-  return p.ids[p.offsets[list] + pos];
+  const int64_t off = p.offsets[list];
+  if (!p.pos) return p.ids[off + pos];
+  // entries that report positions in a larger (global) list: the entry with
+  // that position, found by binary search (positions ascend within a list)
+  int64_t lo = 0, hi = p.offsets[list + 1] - off;
+  while (lo < hi) {
+    const int64_t mid = (lo + hi) >> 1;
+    if (p.pos[off + mid] < pos)
+      lo = mid + 1;
+    else
+      hi = mid;
+  }
+  return p.ids[off + lo];
 }
 
 // One block per query.  Input rows are sorted by (score, seq) ascending.
@@ -433,7 +446,9 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
 // and its own warp-resident top-k, so every (query, list) slot gets exactly
 // the keys of pq_adc_kernel.
 
-constexpr int kAdcGroup = 4;
+constexpr int kAdcGroup = 4;          // queries per tile at most
+constexpr int kAdcGroupThreads = 128;  // threads of a grouped ADC block
+constexpr int kAdcLutBytes = kAdcGroup >= 4 ? 16 : 4 * kAdcGroup;  // one interleaved entry
 constexpr int kAdcPlanThreads = 1024;
 constexpr int64_t kAdcGroupMinQueries = 16;  // smaller batches share few lists
 
@@ -550,7 +565,7 @@ __device__ __forceinline__ void adc_group_tile(const AdcParams& p, uint8_t* lut_
   V* lut = reinterpret_cast<V*>(lut_raw);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float* cb = p.codebooks;
-  for (int e = tid; e < p.m * p.ks; e += kAdcThreads) {
+  for (int e = tid; e < p.m * p.ks; e += kAdcGroupThreads) {
     const int s = e / p.ks;
     float v[W];
     if (p.metric == kL2 && p.sub == 8) {
@@ -596,11 +611,11 @@ __device__ __forceinline__ void adc_group_tile(const AdcParams& p, uint8_t* lut_
   uint4 w = make_uint4(0u, 0u, 0u, 0u);
   uint32_t ps = 0;
   fetch(static_cast<int64_t>(warp) * 32 + lane, w, ps);
-  for (int64_t b = static_cast<int64_t>(warp) * 32; b < len; b += kAdcThreads) {
+  for (int64_t b = static_cast<int64_t>(warp) * 32; b < len; b += kAdcGroupThreads) {
     const int64_t e = b + lane;
     uint4 wn = w;
     uint32_t psn = ps;
-    fetch(e + kAdcThreads, wn, psn);
+    fetch(e + kAdcGroupThreads, wn, psn);
     float acc[W];
 #pragma unroll
     for (int j = 0; j < W; ++j) acc[j] = 0.0f;
@@ -626,10 +641,10 @@ __device__ __forceinline__ void adc_group_tile(const AdcParams& p, uint8_t* lut_
 #pragma unroll
   for (int j = 0; j < W; ++j) wlist[warp][j][lane] = best[j];
   __syncthreads();
-  for (int j = warp; j < cnt; j += kAdcThreads / 32) {
+  for (int j = warp; j < cnt; j += kAdcGroupThreads / 32) {
     uint64_t bb = wlist[0][j][lane];
 #pragma unroll
-    for (int ow = 1; ow < kAdcThreads / 32; ++ow) bb = warp_merge32(bb, wlist[ow][j][lane], lane);
+    for (int ow = 1; ow < kAdcGroupThreads / 32; ++ow) bb = warp_merge32(bb, wlist[ow][j][lane], lane);
     const int have = static_cast<int>(len < p.k ? len : p.k);
     const int64_t it = s_item[j];
     if (lane < have) p.slot_keys[it * p.kp + lane] = bb;
@@ -639,15 +654,15 @@ __device__ __forceinline__ void adc_group_tile(const AdcParams& p, uint8_t* lut_
 
 // Persistent over the tiles of adc_group_plan_kernel (m = 16, k <= 32 kept
 // per (query, list)).
-__global__ void __launch_bounds__(kAdcThreads) pq_adc_group_kernel(
+__global__ void __launch_bounds__(kAdcGroupThreads) pq_adc_group_kernel(
     const AdcParams p, const int32_t* __restrict__ grouped, const int32_t* __restrict__ list_off,
     const int32_t* __restrict__ tile_list, const int32_t* __restrict__ tile_first,
     const int32_t* __restrict__ ntiles_ptr) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* lut_raw =
       reinterpret_cast<uint8_t*>((reinterpret_cast<size_t>(smem_raw) + 15) / 16 * 16);
-  float* resid = reinterpret_cast<float*>(lut_raw + static_cast<size_t>(p.m) * p.ks * 16);
-  __shared__ uint64_t wlist[kAdcThreads / 32][kAdcGroup][32];
+  float* resid = reinterpret_cast<float*>(lut_raw + static_cast<size_t>(p.m) * p.ks * kAdcLutBytes);
+  __shared__ uint64_t wlist[kAdcGroupThreads / 32][kAdcGroup][32];
   __shared__ int32_t s_item[kAdcGroup];
   const int tid = threadIdx.x;
   const int ntiles = *ntiles_ptr;
@@ -664,19 +679,20 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_group_kernel(
       if (tid < cnt) p.slot_counts[s_item[tid]] = 0;
       continue;
     }
-    const int wq = cnt == 1 ? 1 : cnt == 2 ? 2 : 4;  // table width
-    for (int idx = tid; idx < wq * p.dim; idx += kAdcThreads) {
+    const int wq = cnt == 1 ? 1 : cnt == 2 ? 2 : 4;  // table width (<= kAdcGroup)
+    for (int idx = tid; idx < wq * p.dim; idx += kAdcGroupThreads) {
       const int j = idx / p.dim, d = idx - j * p.dim;
       const int64_t q = s_item[j < cnt ? j : 0] / p.probe;
       resid[idx] = __fsub_rn(p.queries[q * p.dim + d], p.coarse[list * p.coarse_ld + d]);
     }
     __syncthreads();
-    if (wq == 1)
+    if (wq == 1) {
       adc_group_tile<1>(p, lut_raw, resid, s_item, cnt, off, len, wlist);
-    else if (wq == 2)
+    } else if (wq == 2) {
       adc_group_tile<2>(p, lut_raw, resid, s_item, cnt, off, len, wlist);
-    else
-      adc_group_tile<4>(p, lut_raw, resid, s_item, cnt, off, len, wlist);
+    } else {
+      if constexpr (kAdcGroup >= 4) adc_group_tile<4>(p, lut_raw, resid, s_item, cnt, off, len, wlist);
+    }
   }
 }
 
@@ -874,7 +890,7 @@ static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* w
   // batches of m = 16 codes with at most 32 kept keys per list run the grouped
   // ADC (the queries probing one list share its code reads)
   const bool grouped = 2 * kout <= 32 && ix->m == 16 && nq >= kAdcGroupMinQueries &&
-                       16 + static_cast<size_t>(ix->m) * ix->ks * 16 +
+                       16 + static_cast<size_t>(ix->m) * ix->ks * kAdcLutBytes +
                                static_cast<size_t>(kAdcGroup) * ix->dim * 4 <=
                            static_cast<size_t>(ctx->max_smem) - 5120;
   const int64_t items_all = nq * probe;
@@ -973,19 +989,19 @@ static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* w
     adc_group_plan_kernel<<<1, kAdcPlanThreads, 0, stream>>>(gp);
     e = cudaGetLastError();
     if (e != cudaSuccess) return fail_cuda(e, "adc plan launch");
-    const size_t gsmem = 16 + static_cast<size_t>(ix->m) * ix->ks * 16 +
+    const size_t gsmem = 16 + static_cast<size_t>(ix->m) * ix->ks * kAdcLutBytes +
                          static_cast<size_t>(kAdcGroup) * ix->dim * 4;
     e = cudaFuncSetAttribute(pq_adc_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(gsmem));
     if (e != cudaSuccess) return fail_cuda(e, "grouped adc configure");
     int per_sm = 1;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pq_adc_group_kernel, kAdcThreads,
-                                                      gsmem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pq_adc_group_kernel,
+                                                      kAdcGroupThreads, gsmem);
     if (e != cudaSuccess) return fail_cuda(e, "grouped adc occupancy");
     const int grid = static_cast<int>(std::min<int64_t>(
         items_all, static_cast<int64_t>(ctx->num_sms) * std::max(1, per_sm)));
     cudaEvent_t stop = timing_begin(ws, stream);
-    pq_adc_group_kernel<<<grid, kAdcThreads, gsmem, stream>>>(a, gp.grouped, gp.list_off,
+    pq_adc_group_kernel<<<grid, kAdcGroupThreads, gsmem, stream>>>(a, gp.grouped, gp.list_off,
                                                               gp.tile_list, gp.tile_first,
                                                               gp.ntiles);
     e = cudaGetLastError();
@@ -1064,6 +1080,7 @@ static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* w
   f.probe_stride = probe;
   f.offsets = ix->offsets;
   f.ids = ix->ids;
+  f.pos = ix->pos;
   f.out_score = d_out_dist;
   f.out_id = d_out_ids;
   f.out_count = d_out_counts;
@@ -1104,9 +1121,15 @@ int32_t mans_ivfpq_create(mans_ctx* ctx, const float* coarse, int32_t nlist, int
   for (int64_t i = 0; i < total; ++i)
     if (lists[i] >= static_cast<uint64_t>(n)) return fail(MANS_ERR_INVALID, "list id out of range");
   int64_t max_pos = max_len - 1;
-  if (list_positions)
+  if (list_positions) {
+    // the searches find an entry from its position by binary search
+    for (int32_t l = 0; l < nlist; ++l)
+      for (int64_t i = list_offsets[l] + 1; i < list_offsets[l + 1]; ++i)
+        if (list_positions[i] <= list_positions[i - 1])
+          return fail(MANS_ERR_INVALID, "list positions must ascend within each list");
     for (int64_t i = 0; i < total; ++i)
       max_pos = std::max<int64_t>(max_pos, list_positions[i]);
+  }
   DeviceGuard g(ctx->device);
   mans_ivfpq* ix = new mans_ivfpq();
   ix->ctx = ctx;

@@ -277,10 +277,18 @@ def test_ivfpq_list_longer_than_2_pow_20(ctx):
     pos = np.array([0, 1, (1 << 29) + 2, 0, 1, 2], np.uint32)
     ixs = mb.IVFPQIndex(ctx, coarse8, cb, codes[:6], (small, np.arange(6, dtype=np.uint32)),
                         list_positions=pos)
-    ixs.search_arrays(q, 5, 4)
+    # a plain search of such a shard is the search of its own entries (the
+    # positions keep their relative order within each list)
+    lists6 = np.arange(6, dtype=np.uint32)
+    for nprobe in (1, 4):
+        same(ixs.search_arrays(q, 5, nprobe),
+             O.ivfpq_search(coarse8, cb, codes[:6], small, lists6, q, 5, nprobe, O.L2))
     with pytest.raises(mb.SearchFailed):
         ixs.search_arrays(q, 5, 8)
     ixs.close()
+    with pytest.raises(mb.ConstructionFailed):  # positions must ascend within a list
+        mb.IVFPQIndex(ctx, coarse8, cb, codes[:6], (small, lists6),
+                      list_positions=np.array([0, 5, 5, 0, 1, 2], np.uint32))
 
 
 @pytest.mark.parametrize("metric", [O.L2, O.COSINE, O.IP])
