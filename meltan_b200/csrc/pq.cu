@@ -56,6 +56,32 @@ struct mans_ivfpq {
 };
 
 namespace mans {
+
+// One distance-table entry of W queries side by side (the grouped ADC reads
+// all W with one shared-memory load).
+template <int W>
+struct LutVec;
+template <>
+struct LutVec<1> {
+  using T = float;
+  __device__ static float get(const T& v, int j) { return v; }
+  __device__ static T make(const float* v) { return v[0]; }
+};
+template <>
+struct LutVec<2> {
+  using T = float2;
+  __device__ static float get(const T& v, int j) { return j == 0 ? v.x : v.y; }
+  __device__ static T make(const float* v) { return make_float2(v[0], v[1]); }
+};
+template <>
+struct LutVec<4> {
+  using T = float4;
+  __device__ static float get(const T& v, int j) {
+    return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
+  }
+  __device__ static T make(const float* v) { return make_float4(v[0], v[1], v[2], v[3]); }
+};
+
 namespace {
 
 // Insertion sequence of a candidate: probe rank << pos_bits | list position,
@@ -225,6 +251,60 @@ __device__ __forceinline__ float lut_entry(int metric, const float* r, const flo
   return __fsub_rn(1.0f, __fdiv_rn(dot, denom));
 }
 
+// The distance tables of W queries for one list (the index has ks == 256):
+// entry (s, c) of query j at lut[s * 256 + c], component j.  Thread t of T
+// fills the columns c = t, t + T, ... of every subspace s, so a subspace's
+// residuals are loaded once per thread (broadcast reads) and no index is
+// divided; each entry is lut_entry's sequential sum, in the same order.
+template <int W, int T>
+__device__ __forceinline__ void build_tables(const AdcParams& p,
+                                             typename LutVec<W>::T* __restrict__ lut,
+                                             const float* __restrict__ resid) {
+  const int tid = threadIdx.x;
+  const float* cb = p.codebooks;
+  if (p.metric == kL2 && p.sub == 8) {
+    for (int s = 0; s < p.m; ++s) {
+      float r[W][8];
+#pragma unroll
+      for (int j = 0; j < W; ++j) {
+        const float4* r4 = reinterpret_cast<const float4*>(resid + j * p.dim + s * 8);
+        const float4 a = r4[0], b = r4[1];
+        r[j][0] = a.x; r[j][1] = a.y; r[j][2] = a.z; r[j][3] = a.w;
+        r[j][4] = b.x; r[j][5] = b.y; r[j][6] = b.z; r[j][7] = b.w;
+      }
+#pragma unroll 2
+      for (int c = tid; c < 256; c += T) {
+        const float4* c4 =
+            reinterpret_cast<const float4*>(cb + (static_cast<int64_t>(s) * 256 + c) * 8);
+        const float4 a = __ldg(c4), b = __ldg(c4 + 1);
+        const float cw[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        float v[W];
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+          float sum = 0.0f;
+#pragma unroll
+          for (int d = 0; d < 8; ++d) {
+            const float t = __fsub_rn(r[j][d], cw[d]);
+            sum = __fadd_rn(sum, __fmul_rn(t, t));
+          }
+          v[j] = sum;
+        }
+        lut[s * 256 + c] = LutVec<W>::make(v);
+      }
+    }
+  } else {
+    for (int s = 0; s < p.m; ++s)
+      for (int c = tid; c < 256; c += T) {
+        float v[W];
+#pragma unroll
+        for (int j = 0; j < W; ++j)
+          v[j] = lut_entry(p.metric, resid + j * p.dim + s * p.sub,
+                           cb + (static_cast<int64_t>(s) * 256 + c) * p.sub, p.sub);
+        lut[s * 256 + c] = LutVec<W>::make(v);
+      }
+  }
+}
+
 // Persistent: block b handles items b, b + grid, ... ; item = (query, probe rank).
 // One code row: its m bytes as 16-, 4- or 1-byte loads (the row stride is m
 // bytes, so the wide loads are aligned whenever m is a multiple of the width).
@@ -268,6 +348,31 @@ __device__ __forceinline__ uint64_t warp_merge32(uint64_t t, uint64_t x, int lan
   return y;
 }
 
+// Offers one key per lane to the warp's ascending list of its k smallest keys
+// (lane i holds the (i+1)-th; `kth` is the warp-uniform k-th key, kept
+// current): a batch where more than six keys beat the k-th is sorted by
+// shuffles and merged in, fewer are inserted one by one at their rank (keys
+// are distinct; a key that no longer beats the k-th after an earlier
+// insertion lands at rank k or drops out, which is harmless).
+__device__ __forceinline__ void warp_topk_offer(uint64_t& best, uint64_t& kth, uint64_t key,
+                                                int k, int lane) {
+  uint32_t pass = __ballot_sync(0xFFFFFFFFu, key < kth);
+  if (!pass) return;
+  if (__popc(pass) > 6) {
+    best = warp_merge32(best, warp_sort32(key < kth ? key : kKeyMax, lane), lane);
+  } else {
+    while (pass) {
+      const int src = __ffs(pass) - 1;
+      pass &= pass - 1;
+      const uint64_t x = __shfl_sync(0xFFFFFFFFu, key, src);
+      const int at = __popc(__ballot_sync(0xFFFFFFFFu, best < x));
+      const uint64_t up = __shfl_up_sync(0xFFFFFFFFu, best, 1);
+      best = lane < at ? best : (lane == at ? x : up);
+    }
+  }
+  kth = __shfl_sync(0xFFFFFFFFu, best, k - 1);
+}
+
 // Block b handles items b, b + grid, ... ; item = (query, probe rank).  Small
 // blocks (several resident per SM) hide the latency of the per-item steps:
 // residual, LUT in shared memory, sequential ADC per code, the item's k
@@ -289,7 +394,6 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const float* cb = p.codebooks;
   const int64_t items = p.nq * p.probe;
   for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
     const int64_t q = it / p.probe;
@@ -314,36 +418,11 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
       nb = 0;
     }
     __syncthreads();
-    if (p.metric == kL2 && p.sub == 8) {
-      // the common shape (d/m = 8): two 16-byte codebook loads per entry and
-      // the subspace's residual from shared memory (one subspace per warp
-      // step, so a broadcast); same operations in the same order as lut_entry.
-      // Unrolled so that several entries' codebook loads are in flight.
-#pragma unroll 4
-      for (int e = tid; e < p.m * p.ks; e += kAdcThreads) {
-        const int s = e / p.ks;
-        const float4* c4 = reinterpret_cast<const float4*>(cb + static_cast<int64_t>(e) * 8);
-        const float4 a = __ldg(c4), b = __ldg(c4 + 1);
-        const float* r = resid + s * 8;
-        const float cw[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        float sum = 0.0f;
-#pragma unroll
-        for (int d = 0; d < 8; ++d) {
-          const float t = __fsub_rn(r[d], cw[d]);
-          sum = __fadd_rn(sum, __fmul_rn(t, t));
-        }
-        lut[e] = sum;
-      }
-    } else {
-      for (int e = tid; e < p.m * p.ks; e += kAdcThreads) {
-        const int s = e / p.ks;
-        lut[e] = lut_entry(p.metric, resid + s * p.sub, cb + static_cast<int64_t>(e) * p.sub,
-                           p.sub);
-      }
-    }
+    build_tables<1, kAdcThreads>(p, lut, resid);
     __syncthreads();
     if (WARP_TOPK) {
       uint64_t best = kKeyMax;  // lane i: this warp's (i+1)-th smallest key
+      uint64_t kth = kKeyMax;   // this warp's k-th smallest key
       // m = 16: one 16-byte code row per lane, the next batch's row (and list
       // position) loaded before the current one is scored
       const bool wide = p.m == 16;
@@ -371,7 +450,7 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
             total = 0.0f;
 #pragma unroll
             for (int j = 0; j < 16; ++j)
-              total = __fadd_rn(total, lut[j * p.ks + ((words[j >> 2] >> (8 * (j & 3))) & 0xFFu)]);
+              total = __fadd_rn(total, lut[j * 256 + ((words[j >> 2] >> (8 * (j & 3))) & 0xFFu)]);
             pos = ps;
           } else {
             total = adc_sum(lut, p.ks, p.codes + (off + e) * p.m, p.m);
@@ -381,23 +460,7 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
         }
         w = wn;
         ps = psn;
-        const uint64_t kth = __shfl_sync(0xFFFFFFFFu, best, p.k - 1);
-        uint32_t pass = __ballot_sync(0xFFFFFFFFu, key < kth);
-        if (__popc(pass) > 6) {
-          best = warp_merge32(best, warp_sort32(key < kth ? key : kKeyMax, lane), lane);
-        } else {
-          // a few keys: insert each at its rank (keys are distinct); the
-          // last entry drops out.  A key that no longer beats the k-th after
-          // an earlier insertion lands at rank k or is dropped: harmless.
-          while (pass) {
-            const int src = __ffs(pass) - 1;
-            pass &= pass - 1;
-            const uint64_t x = __shfl_sync(0xFFFFFFFFu, key, src);
-            const int at = __popc(__ballot_sync(0xFFFFFFFFu, best < x));
-            const uint64_t up = __shfl_up_sync(0xFFFFFFFFu, best, 1);
-            best = lane < at ? best : (lane == at ? x : up);
-          }
-        }
+        warp_topk_offer(best, kth, key, p.k, lane);
       }
       wlist[warp][lane] = best;
       __syncthreads();
@@ -446,7 +509,7 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
 // and its own warp-resident top-k, so every (query, list) slot gets exactly
 // the keys of pq_adc_kernel.
 
-constexpr int kAdcGroup = 4;          // queries per tile at most
+constexpr int kAdcGroup = 2;          // queries per tile at most
 constexpr int kAdcGroupThreads = 128;  // threads of a grouped ADC block
 constexpr int kAdcLutBytes = kAdcGroup >= 4 ? 16 : 4 * kAdcGroup;  // one interleaved entry
 constexpr int kAdcPlanThreads = 1024;
@@ -511,48 +574,6 @@ __global__ void __launch_bounds__(kAdcPlanThreads) adc_group_plan_kernel(const A
   if (t == 0) *g.ntiles = g.tile_off[g.nlist];
 }
 
-// Offers one key per lane to the warp's ascending list of its k smallest keys
-// (lane i holds the (i+1)-th): a batch where more than six keys beat the k-th
-// is sorted by shuffles and merged in, fewer are inserted at their rank.
-__device__ __forceinline__ uint64_t warp_topk_offer(uint64_t best, uint64_t key, int k,
-                                                    int lane) {
-  const uint64_t kth = __shfl_sync(0xFFFFFFFFu, best, k - 1);
-  uint32_t pass = __ballot_sync(0xFFFFFFFFu, key < kth);
-  if (__popc(pass) > 6) return warp_merge32(best, warp_sort32(key < kth ? key : kKeyMax, lane), lane);
-  while (pass) {
-    const int src = __ffs(pass) - 1;
-    pass &= pass - 1;
-    const uint64_t x = __shfl_sync(0xFFFFFFFFu, key, src);
-    const int at = __popc(__ballot_sync(0xFFFFFFFFu, best < x));
-    const uint64_t up = __shfl_up_sync(0xFFFFFFFFu, best, 1);
-    best = lane < at ? best : (lane == at ? x : up);
-  }
-  return best;
-}
-
-template <int W>
-struct LutVec;
-template <>
-struct LutVec<1> {
-  using T = float;
-  __device__ static float get(const T& v, int j) { return v; }
-  __device__ static T make(const float* v) { return v[0]; }
-};
-template <>
-struct LutVec<2> {
-  using T = float2;
-  __device__ static float get(const T& v, int j) { return j == 0 ? v.x : v.y; }
-  __device__ static T make(const float* v) { return make_float2(v[0], v[1]); }
-};
-template <>
-struct LutVec<4> {
-  using T = float4;
-  __device__ static float get(const T& v, int j) {
-    return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
-  }
-  __device__ static T make(const float* v) { return make_float4(v[0], v[1], v[2], v[3]); }
-};
-
 // One tile: W-wide tables for its `cnt` queries (cnt <= W), then the scan of
 // the list's m = 16 code rows with W sequential sums per row.  The caller
 // has the residuals in shared memory and synchronises before and after.
@@ -564,33 +585,7 @@ __device__ __forceinline__ void adc_group_tile(const AdcParams& p, uint8_t* lut_
   using V = typename LutVec<W>::T;
   V* lut = reinterpret_cast<V*>(lut_raw);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const float* cb = p.codebooks;
-  for (int e = tid; e < p.m * p.ks; e += kAdcGroupThreads) {
-    const int s = e / p.ks;
-    float v[W];
-    if (p.metric == kL2 && p.sub == 8) {
-      const float4* c4 = reinterpret_cast<const float4*>(cb + static_cast<int64_t>(e) * 8);
-      const float4 a = __ldg(c4), b = __ldg(c4 + 1);
-      const float cw[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-      for (int j = 0; j < W; ++j) {
-        const float* r = resid + j * p.dim + s * 8;
-        float sum = 0.0f;
-#pragma unroll
-        for (int d = 0; d < 8; ++d) {
-          const float t = __fsub_rn(r[d], cw[d]);
-          sum = __fadd_rn(sum, __fmul_rn(t, t));
-        }
-        v[j] = sum;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < W; ++j)
-        v[j] = lut_entry(p.metric, resid + j * p.dim + s * p.sub,
-                         cb + static_cast<int64_t>(e) * p.sub, p.sub);
-    }
-    lut[e] = LutVec<W>::make(v);
-  }
+  build_tables<W, kAdcGroupThreads>(p, lut, resid);
   __syncthreads();
   uint32_t seqhi[W];
 #pragma unroll
@@ -598,9 +593,9 @@ __device__ __forceinline__ void adc_group_tile(const AdcParams& p, uint8_t* lut_
     const int32_t it = s_item[j < cnt ? j : 0];
     seqhi[j] = static_cast<uint32_t>(it - (it / p.probe) * p.probe) << p.pos_bits;
   }
-  uint64_t best[W];
+  uint64_t best[W], kth[W];
 #pragma unroll
-  for (int j = 0; j < W; ++j) best[j] = kKeyMax;
+  for (int j = 0; j < W; ++j) best[j] = kth[j] = kKeyMax;
   const uint4* crow = reinterpret_cast<const uint4*>(p.codes + off * 16);
   auto fetch = [&](int64_t e, uint4& w, uint32_t& ps) {
     if (e < len) {
@@ -623,7 +618,7 @@ __device__ __forceinline__ void adc_group_tile(const AdcParams& p, uint8_t* lut_
       const uint32_t words[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
       for (int jj = 0; jj < 16; ++jj) {
-        const V x = lut[jj * p.ks + ((words[jj >> 2] >> (8 * (jj & 3))) & 0xFFu)];
+        const V x = lut[jj * 256 + ((words[jj >> 2] >> (8 * (jj & 3))) & 0xFFu)];
 #pragma unroll
         for (int j = 0; j < W; ++j) acc[j] = __fadd_rn(acc[j], LutVec<W>::get(x, j));
       }
@@ -632,7 +627,7 @@ __device__ __forceinline__ void adc_group_tile(const AdcParams& p, uint8_t* lut_
     for (int j = 0; j < W; ++j) {
       if (j < cnt) {
         const uint64_t key = e < len ? make_key(acc[j], seqhi[j] | ps) : kKeyMax;
-        best[j] = warp_topk_offer(best[j], key, p.k, lane);
+        warp_topk_offer(best[j], kth[j], key, p.k, lane);
       }
     }
     w = wn;
