@@ -354,12 +354,19 @@ __device__ __forceinline__ uint64_t warp_merge32(uint64_t t, uint64_t x, int lan
 // shuffles and merged in, fewer are inserted one by one at their rank (keys
 // are distinct; a key that no longer beats the k-th after an earlier
 // insertion lands at rank k or drops out, which is harmless).
+// With `shared_thr` (shared memory, the warps of a block that split one list),
+// keys are filtered by the smaller of this warp's k-th key and the smallest
+// k-th key any of those warps has published: a key at or above another
+// warp's k-th has k smaller keys there and cannot reach the list's top k.
 __device__ __forceinline__ void warp_topk_offer(uint64_t& best, uint64_t& kth, uint64_t key,
-                                                int k, int lane) {
-  uint32_t pass = __ballot_sync(0xFFFFFFFFu, key < kth);
+                                                int k, int lane,
+                                                unsigned long long* shared_thr = nullptr) {
+  const uint64_t t =
+      shared_thr ? key_min(kth, *reinterpret_cast<volatile unsigned long long*>(shared_thr)) : kth;
+  uint32_t pass = __ballot_sync(0xFFFFFFFFu, key < t);
   if (!pass) return;
   if (__popc(pass) > 6) {
-    best = warp_merge32(best, warp_sort32(key < kth ? key : kKeyMax, lane), lane);
+    best = warp_merge32(best, warp_sort32(key < t ? key : kKeyMax, lane), lane);
   } else {
     while (pass) {
       const int src = __ffs(pass) - 1;
@@ -371,6 +378,7 @@ __device__ __forceinline__ void warp_topk_offer(uint64_t& best, uint64_t& kth, u
     }
   }
   kth = __shfl_sync(0xFFFFFFFFu, best, k - 1);
+  if (shared_thr && lane == 0 && kth < t) atomicMin(shared_thr, static_cast<unsigned long long>(kth));
 }
 
 // Block b handles items b, b + grid, ... ; item = (query, probe rank).  Small
@@ -391,6 +399,7 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
   __shared__ uint64_t thr;
   __shared__ int qc, nb;
   __shared__ uint64_t wlist[kAdcThreads / 32][32];
+  __shared__ unsigned long long s_thr1;  // smallest published k-th key (warp top-k)
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
@@ -417,6 +426,7 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
       qc = 0;
       nb = 0;
     }
+    if (WARP_TOPK && tid == 0) s_thr1 = kKeyMax;
     __syncthreads();
     build_tables<1, kAdcThreads>(p, lut, resid);
     __syncthreads();
@@ -450,7 +460,7 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
             total = 0.0f;
 #pragma unroll
             for (int j = 0; j < 16; ++j)
-              total = __fadd_rn(total, lut[j * 256 + ((words[j >> 2] >> (8 * (j & 3))) & 0xFFu)]);
+              total = __fadd_rn(total, lut[j * 256 + __byte_perm(words[j >> 2], 0u, 0x4440u + (j & 3))]);
             pos = ps;
           } else {
             total = adc_sum(lut, p.ks, p.codes + (off + e) * p.m, p.m);
@@ -460,7 +470,7 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
         }
         w = wn;
         ps = psn;
-        warp_topk_offer(best, kth, key, p.k, lane);
+        warp_topk_offer(best, kth, key, p.k, lane, &s_thr1);
       }
       wlist[warp][lane] = best;
       __syncthreads();
@@ -512,6 +522,9 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
 constexpr int kAdcGroup = 2;          // queries per tile at most
 constexpr int kAdcGroupThreads = 128;  // threads of a grouped ADC block
 constexpr int kAdcLutBytes = kAdcGroup >= 4 ? 16 : 4 * kAdcGroup;  // one interleaved entry
+// shared-memory share of the unified L1 / shared memory (percent; -1: the
+// driver's choice).  What is not shared memory caches the codebooks.
+constexpr int kAdcGroupCarveout = -1;
 constexpr int kAdcPlanThreads = 1024;
 constexpr int64_t kAdcGroupMinQueries = 16;  // smaller batches share few lists
 
@@ -581,7 +594,8 @@ template <int W>
 __device__ __forceinline__ void adc_group_tile(const AdcParams& p, uint8_t* lut_raw,
                                                const float* resid, const int32_t* s_item,
                                                int cnt, int64_t off, int64_t len,
-                                               uint64_t (*wlist)[kAdcGroup][32]) {
+                                               uint64_t (*wlist)[kAdcGroup][32],
+                                               unsigned long long* s_thr) {
   using V = typename LutVec<W>::T;
   V* lut = reinterpret_cast<V*>(lut_raw);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -618,7 +632,7 @@ __device__ __forceinline__ void adc_group_tile(const AdcParams& p, uint8_t* lut_
       const uint32_t words[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
       for (int jj = 0; jj < 16; ++jj) {
-        const V x = lut[jj * 256 + ((words[jj >> 2] >> (8 * (jj & 3))) & 0xFFu)];
+        const V x = lut[jj * 256 + __byte_perm(words[jj >> 2], 0u, 0x4440u + (jj & 3))];
 #pragma unroll
         for (int j = 0; j < W; ++j) acc[j] = __fadd_rn(acc[j], LutVec<W>::get(x, j));
       }
@@ -627,7 +641,7 @@ __device__ __forceinline__ void adc_group_tile(const AdcParams& p, uint8_t* lut_
     for (int j = 0; j < W; ++j) {
       if (j < cnt) {
         const uint64_t key = e < len ? make_key(acc[j], seqhi[j] | ps) : kKeyMax;
-        warp_topk_offer(best[j], kth[j], key, p.k, lane);
+        warp_topk_offer(best[j], kth[j], key, p.k, lane, s_thr + j);
       }
     }
     w = wn;
@@ -658,6 +672,7 @@ __global__ void __launch_bounds__(kAdcGroupThreads) pq_adc_group_kernel(
       reinterpret_cast<uint8_t*>((reinterpret_cast<size_t>(smem_raw) + 15) / 16 * 16);
   float* resid = reinterpret_cast<float*>(lut_raw + static_cast<size_t>(p.m) * p.ks * kAdcLutBytes);
   __shared__ uint64_t wlist[kAdcGroupThreads / 32][kAdcGroup][32];
+  __shared__ unsigned long long s_thr[kAdcGroup];  // smallest published k-th key per query
   __shared__ int32_t s_item[kAdcGroup];
   const int tid = threadIdx.x;
   const int ntiles = *ntiles_ptr;
@@ -666,7 +681,10 @@ __global__ void __launch_bounds__(kAdcGroupThreads) pq_adc_group_kernel(
     const int list = tile_list[t];
     const int first = tile_first[t];
     const int cnt = min(kAdcGroup, list_off[list + 1] - first);
-    if (tid < kAdcGroup) s_item[tid] = grouped[first + min(tid, cnt - 1)];
+    if (tid < kAdcGroup) {
+      s_item[tid] = grouped[first + min(tid, cnt - 1)];
+      s_thr[tid] = kKeyMax;
+    }
     const int64_t off = p.offsets[list];
     const int64_t len = p.offsets[list + 1] - off;
     __syncthreads();
@@ -682,11 +700,12 @@ __global__ void __launch_bounds__(kAdcGroupThreads) pq_adc_group_kernel(
     }
     __syncthreads();
     if (wq == 1) {
-      adc_group_tile<1>(p, lut_raw, resid, s_item, cnt, off, len, wlist);
+      adc_group_tile<1>(p, lut_raw, resid, s_item, cnt, off, len, wlist, s_thr);
     } else if (wq == 2) {
-      adc_group_tile<2>(p, lut_raw, resid, s_item, cnt, off, len, wlist);
+      adc_group_tile<2>(p, lut_raw, resid, s_item, cnt, off, len, wlist, s_thr);
     } else {
-      if constexpr (kAdcGroup >= 4) adc_group_tile<4>(p, lut_raw, resid, s_item, cnt, off, len, wlist);
+      if constexpr (kAdcGroup >= 4)
+        adc_group_tile<4>(p, lut_raw, resid, s_item, cnt, off, len, wlist, s_thr);
     }
   }
 }
@@ -988,6 +1007,9 @@ static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* w
                          static_cast<size_t>(kAdcGroup) * ix->dim * 4;
     e = cudaFuncSetAttribute(pq_adc_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(gsmem));
+    if (e == cudaSuccess && kAdcGroupCarveout >= 0)
+      e = cudaFuncSetAttribute(pq_adc_group_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               kAdcGroupCarveout);
     if (e != cudaSuccess) return fail_cuda(e, "grouped adc configure");
     int per_sm = 1;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pq_adc_group_kernel,
