@@ -522,6 +522,7 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
 constexpr int kAdcGroup = 2;          // queries per tile at most
 constexpr int kAdcGroupThreads = 128;  // threads of a grouped ADC block
 constexpr int kAdcLutBytes = kAdcGroup >= 4 ? 16 : 4 * kAdcGroup;  // one interleaved entry
+constexpr int kAdcRowsPerLane = 2;    // code rows a lane scores per step
 // shared-memory share of the unified L1 / shared memory (percent; -1: the
 // driver's choice).  What is not shared memory caches the codebooks.
 constexpr int kAdcGroupCarveout = -1;
@@ -610,6 +611,10 @@ __device__ __forceinline__ void adc_group_tile(const AdcParams& p, uint8_t* lut_
   uint64_t best[W], kth[W];
 #pragma unroll
   for (int j = 0; j < W; ++j) best[j] = kth[j] = kKeyMax;
+  // R code rows per lane per step (independent lookup chains in flight); the
+  // next step's rows are loaded while the current ones are scored
+  constexpr int R = kAdcRowsPerLane;
+  constexpr int64_t kStep = static_cast<int64_t>(kAdcGroupThreads) * R;
   const uint4* crow = reinterpret_cast<const uint4*>(p.codes + off * 16);
   auto fetch = [&](int64_t e, uint4& w, uint32_t& ps) {
     if (e < len) {
@@ -617,35 +622,61 @@ __device__ __forceinline__ void adc_group_tile(const AdcParams& p, uint8_t* lut_
       ps = p.pos ? __ldg(p.pos + off + e) : static_cast<uint32_t>(e);
     }
   };
-  uint4 w = make_uint4(0u, 0u, 0u, 0u);
-  uint32_t ps = 0;
-  fetch(static_cast<int64_t>(warp) * 32 + lane, w, ps);
-  for (int64_t b = static_cast<int64_t>(warp) * 32; b < len; b += kAdcGroupThreads) {
-    const int64_t e = b + lane;
-    uint4 wn = w;
-    uint32_t psn = ps;
-    fetch(e + kAdcGroupThreads, wn, psn);
-    float acc[W];
+  const int64_t b0 = static_cast<int64_t>(warp) * 32 * R;
+  uint4 w[R];
+  uint32_t ps[R];
 #pragma unroll
-    for (int j = 0; j < W; ++j) acc[j] = 0.0f;
-    if (e < len) {
-      const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+  for (int r = 0; r < R; ++r) {
+    w[r] = make_uint4(0u, 0u, 0u, 0u);
+    ps[r] = 0;
+    fetch(b0 + r * 32 + lane, w[r], ps[r]);
+  }
+  for (int64_t b = b0; b < len; b += kStep) {
+    uint4 wn[R];
+    uint32_t psn[R];
+    float acc[R][W];
 #pragma unroll
-      for (int jj = 0; jj < 16; ++jj) {
-        const V x = lut[jj * 256 + __byte_perm(words[jj >> 2], 0u, 0x4440u + (jj & 3))];
+    for (int r = 0; r < R; ++r) {
+      wn[r] = w[r];
+      psn[r] = ps[r];
+      fetch(b + kStep + r * 32 + lane, wn[r], psn[r]);
 #pragma unroll
-        for (int j = 0; j < W; ++j) acc[j] = __fadd_rn(acc[j], LutVec<W>::get(x, j));
+      for (int j = 0; j < W; ++j) acc[r][j] = 0.0f;
+    }
+#pragma unroll
+    for (int jj = 0; jj < 16; ++jj) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const uint32_t word = jj < 4 ? w[r].x : jj < 8 ? w[r].y : jj < 12 ? w[r].z : w[r].w;
+        const V x = lut[jj * 256 + __byte_perm(word, 0u, 0x4440u + (jj & 3))];
+#pragma unroll
+        for (int j = 0; j < W; ++j) acc[r][j] = __fadd_rn(acc[r][j], LutVec<W>::get(x, j));
       }
     }
 #pragma unroll
     for (int j = 0; j < W; ++j) {
       if (j < cnt) {
-        const uint64_t key = e < len ? make_key(acc[j], seqhi[j] | ps) : kKeyMax;
-        warp_topk_offer(best[j], kth[j], key, p.k, lane, s_thr + j);
+        // a float prefilter against the current bound (key order is score
+        // order first; a bound of kKeyMax reads as NaN and lets all through)
+        const uint64_t t =
+            key_min(kth[j], *reinterpret_cast<volatile unsigned long long*>(s_thr + j));
+        const float ts = key_distance(t);
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const int64_t e = b + r * 32 + lane;
+          const bool maybe = e < len && !(acc[r][j] > ts);
+          if (__any_sync(0xFFFFFFFFu, maybe)) {
+            const uint64_t key = maybe ? make_key(acc[r][j], seqhi[j] | ps[r]) : kKeyMax;
+            warp_topk_offer(best[j], kth[j], key, p.k, lane, s_thr + j);
+          }
+        }
       }
     }
-    w = wn;
-    ps = psn;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      w[r] = wn[r];
+      ps[r] = psn[r];
+    }
   }
 #pragma unroll
   for (int j = 0; j < W; ++j) wlist[warp][j][lane] = best[j];
