@@ -354,19 +354,12 @@ __device__ __forceinline__ uint64_t warp_merge32(uint64_t t, uint64_t x, int lan
 // shuffles and merged in, fewer are inserted one by one at their rank (keys
 // are distinct; a key that no longer beats the k-th after an earlier
 // insertion lands at rank k or drops out, which is harmless).
-// With `shared_thr` (shared memory, the warps of a block that split one list),
-// keys are filtered by the smaller of this warp's k-th key and the smallest
-// k-th key any of those warps has published: a key at or above another
-// warp's k-th has k smaller keys there and cannot reach the list's top k.
 __device__ __forceinline__ void warp_topk_offer(uint64_t& best, uint64_t& kth, uint64_t key,
-                                                int k, int lane,
-                                                unsigned long long* shared_thr = nullptr) {
-  const uint64_t t =
-      shared_thr ? key_min(kth, *reinterpret_cast<volatile unsigned long long*>(shared_thr)) : kth;
-  uint32_t pass = __ballot_sync(0xFFFFFFFFu, key < t);
+                                                int k, int lane) {
+  uint32_t pass = __ballot_sync(0xFFFFFFFFu, key < kth);
   if (!pass) return;
   if (__popc(pass) > 6) {
-    best = warp_merge32(best, warp_sort32(key < t ? key : kKeyMax, lane), lane);
+    best = warp_merge32(best, warp_sort32(key < kth ? key : kKeyMax, lane), lane);
   } else {
     while (pass) {
       const int src = __ffs(pass) - 1;
@@ -378,7 +371,6 @@ __device__ __forceinline__ void warp_topk_offer(uint64_t& best, uint64_t& kth, u
     }
   }
   kth = __shfl_sync(0xFFFFFFFFu, best, k - 1);
-  if (shared_thr && lane == 0 && kth < t) atomicMin(shared_thr, static_cast<unsigned long long>(kth));
 }
 
 // Block b handles items b, b + grid, ... ; item = (query, probe rank).  Small
@@ -399,7 +391,6 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
   __shared__ uint64_t thr;
   __shared__ int qc, nb;
   __shared__ uint64_t wlist[kAdcThreads / 32][32];
-  __shared__ unsigned long long s_thr1;  // smallest published k-th key (warp top-k)
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
@@ -426,7 +417,6 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
       qc = 0;
       nb = 0;
     }
-    if (WARP_TOPK && tid == 0) s_thr1 = kKeyMax;
     __syncthreads();
     build_tables<1, kAdcThreads>(p, lut, resid);
     __syncthreads();
@@ -460,7 +450,7 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
             total = 0.0f;
 #pragma unroll
             for (int j = 0; j < 16; ++j)
-              total = __fadd_rn(total, lut[j * 256 + __byte_perm(words[j >> 2], 0u, 0x4440u + (j & 3))]);
+              total = __fadd_rn(total, lut[j * 256 + ((words[j >> 2] >> (8 * (j & 3))) & 0xFFu)]);
             pos = ps;
           } else {
             total = adc_sum(lut, p.ks, p.codes + (off + e) * p.m, p.m);
@@ -470,7 +460,7 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
         }
         w = wn;
         ps = psn;
-        warp_topk_offer(best, kth, key, p.k, lane, &s_thr1);
+        warp_topk_offer(best, kth, key, p.k, lane);
       }
       wlist[warp][lane] = best;
       __syncthreads();
@@ -522,10 +512,6 @@ __global__ void __launch_bounds__(kAdcThreads) pq_adc_kernel(const AdcParams p) 
 constexpr int kAdcGroup = 2;          // queries per tile at most
 constexpr int kAdcGroupThreads = 128;  // threads of a grouped ADC block
 constexpr int kAdcLutBytes = kAdcGroup >= 4 ? 16 : 4 * kAdcGroup;  // one interleaved entry
-constexpr int kAdcRowsPerLane = 2;    // code rows a lane scores per step
-// shared-memory share of the unified L1 / shared memory (percent; -1: the
-// driver's choice).  What is not shared memory caches the codebooks.
-constexpr int kAdcGroupCarveout = -1;
 constexpr int kAdcPlanThreads = 1024;
 constexpr int64_t kAdcGroupMinQueries = 16;  // smaller batches share few lists
 
@@ -595,8 +581,7 @@ template <int W>
 __device__ __forceinline__ void adc_group_tile(const AdcParams& p, uint8_t* lut_raw,
                                                const float* resid, const int32_t* s_item,
                                                int cnt, int64_t off, int64_t len,
-                                               uint64_t (*wlist)[kAdcGroup][32],
-                                               unsigned long long* s_thr) {
+                                               uint64_t (*wlist)[kAdcGroup][32]) {
   using V = typename LutVec<W>::T;
   V* lut = reinterpret_cast<V*>(lut_raw);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -611,10 +596,6 @@ __device__ __forceinline__ void adc_group_tile(const AdcParams& p, uint8_t* lut_
   uint64_t best[W], kth[W];
 #pragma unroll
   for (int j = 0; j < W; ++j) best[j] = kth[j] = kKeyMax;
-  // R code rows per lane per step (independent lookup chains in flight); the
-  // next step's rows are loaded while the current ones are scored
-  constexpr int R = kAdcRowsPerLane;
-  constexpr int64_t kStep = static_cast<int64_t>(kAdcGroupThreads) * R;
   const uint4* crow = reinterpret_cast<const uint4*>(p.codes + off * 16);
   auto fetch = [&](int64_t e, uint4& w, uint32_t& ps) {
     if (e < len) {
@@ -622,61 +603,35 @@ __device__ __forceinline__ void adc_group_tile(const AdcParams& p, uint8_t* lut_
       ps = p.pos ? __ldg(p.pos + off + e) : static_cast<uint32_t>(e);
     }
   };
-  const int64_t b0 = static_cast<int64_t>(warp) * 32 * R;
-  uint4 w[R];
-  uint32_t ps[R];
+  uint4 w = make_uint4(0u, 0u, 0u, 0u);
+  uint32_t ps = 0;
+  fetch(static_cast<int64_t>(warp) * 32 + lane, w, ps);
+  for (int64_t b = static_cast<int64_t>(warp) * 32; b < len; b += kAdcGroupThreads) {
+    const int64_t e = b + lane;
+    uint4 wn = w;
+    uint32_t psn = ps;
+    fetch(e + kAdcGroupThreads, wn, psn);
+    float acc[W];
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
-    w[r] = make_uint4(0u, 0u, 0u, 0u);
-    ps[r] = 0;
-    fetch(b0 + r * 32 + lane, w[r], ps[r]);
-  }
-  for (int64_t b = b0; b < len; b += kStep) {
-    uint4 wn[R];
-    uint32_t psn[R];
-    float acc[R][W];
+    for (int j = 0; j < W; ++j) acc[j] = 0.0f;
+    if (e < len) {
+      const uint32_t words[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      wn[r] = w[r];
-      psn[r] = ps[r];
-      fetch(b + kStep + r * 32 + lane, wn[r], psn[r]);
+      for (int jj = 0; jj < 16; ++jj) {
+        const V x = lut[jj * 256 + ((words[jj >> 2] >> (8 * (jj & 3))) & 0xFFu)];
 #pragma unroll
-      for (int j = 0; j < W; ++j) acc[r][j] = 0.0f;
-    }
-#pragma unroll
-    for (int jj = 0; jj < 16; ++jj) {
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const uint32_t word = jj < 4 ? w[r].x : jj < 8 ? w[r].y : jj < 12 ? w[r].z : w[r].w;
-        const V x = lut[jj * 256 + __byte_perm(word, 0u, 0x4440u + (jj & 3))];
-#pragma unroll
-        for (int j = 0; j < W; ++j) acc[r][j] = __fadd_rn(acc[r][j], LutVec<W>::get(x, j));
+        for (int j = 0; j < W; ++j) acc[j] = __fadd_rn(acc[j], LutVec<W>::get(x, j));
       }
     }
 #pragma unroll
     for (int j = 0; j < W; ++j) {
       if (j < cnt) {
-        // a float prefilter against the current bound (key order is score
-        // order first; a bound of kKeyMax reads as NaN and lets all through)
-        const uint64_t t =
-            key_min(kth[j], *reinterpret_cast<volatile unsigned long long*>(s_thr + j));
-        const float ts = key_distance(t);
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const int64_t e = b + r * 32 + lane;
-          const bool maybe = e < len && !(acc[r][j] > ts);
-          if (__any_sync(0xFFFFFFFFu, maybe)) {
-            const uint64_t key = maybe ? make_key(acc[r][j], seqhi[j] | ps[r]) : kKeyMax;
-            warp_topk_offer(best[j], kth[j], key, p.k, lane, s_thr + j);
-          }
-        }
+        const uint64_t key = e < len ? make_key(acc[j], seqhi[j] | ps) : kKeyMax;
+        warp_topk_offer(best[j], kth[j], key, p.k, lane);
       }
     }
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      w[r] = wn[r];
-      ps[r] = psn[r];
-    }
+    w = wn;
+    ps = psn;
   }
 #pragma unroll
   for (int j = 0; j < W; ++j) wlist[warp][j][lane] = best[j];
@@ -703,7 +658,6 @@ __global__ void __launch_bounds__(kAdcGroupThreads) pq_adc_group_kernel(
       reinterpret_cast<uint8_t*>((reinterpret_cast<size_t>(smem_raw) + 15) / 16 * 16);
   float* resid = reinterpret_cast<float*>(lut_raw + static_cast<size_t>(p.m) * p.ks * kAdcLutBytes);
   __shared__ uint64_t wlist[kAdcGroupThreads / 32][kAdcGroup][32];
-  __shared__ unsigned long long s_thr[kAdcGroup];  // smallest published k-th key per query
   __shared__ int32_t s_item[kAdcGroup];
   const int tid = threadIdx.x;
   const int ntiles = *ntiles_ptr;
@@ -712,10 +666,7 @@ __global__ void __launch_bounds__(kAdcGroupThreads) pq_adc_group_kernel(
     const int list = tile_list[t];
     const int first = tile_first[t];
     const int cnt = min(kAdcGroup, list_off[list + 1] - first);
-    if (tid < kAdcGroup) {
-      s_item[tid] = grouped[first + min(tid, cnt - 1)];
-      s_thr[tid] = kKeyMax;
-    }
+    if (tid < kAdcGroup) s_item[tid] = grouped[first + min(tid, cnt - 1)];
     const int64_t off = p.offsets[list];
     const int64_t len = p.offsets[list + 1] - off;
     __syncthreads();
@@ -731,12 +682,11 @@ __global__ void __launch_bounds__(kAdcGroupThreads) pq_adc_group_kernel(
     }
     __syncthreads();
     if (wq == 1) {
-      adc_group_tile<1>(p, lut_raw, resid, s_item, cnt, off, len, wlist, s_thr);
+      adc_group_tile<1>(p, lut_raw, resid, s_item, cnt, off, len, wlist);
     } else if (wq == 2) {
-      adc_group_tile<2>(p, lut_raw, resid, s_item, cnt, off, len, wlist, s_thr);
+      adc_group_tile<2>(p, lut_raw, resid, s_item, cnt, off, len, wlist);
     } else {
-      if constexpr (kAdcGroup >= 4)
-        adc_group_tile<4>(p, lut_raw, resid, s_item, cnt, off, len, wlist, s_thr);
+      if constexpr (kAdcGroup >= 4) adc_group_tile<4>(p, lut_raw, resid, s_item, cnt, off, len, wlist);
     }
   }
 }
@@ -1038,9 +988,6 @@ static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* w
                          static_cast<size_t>(kAdcGroup) * ix->dim * 4;
     e = cudaFuncSetAttribute(pq_adc_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(gsmem));
-    if (e == cudaSuccess && kAdcGroupCarveout >= 0)
-      e = cudaFuncSetAttribute(pq_adc_group_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                               kAdcGroupCarveout);
     if (e != cudaSuccess) return fail_cuda(e, "grouped adc configure");
     int per_sm = 1;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pq_adc_group_kernel,
