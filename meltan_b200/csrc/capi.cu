@@ -158,8 +158,11 @@ void destroy_workspace(mans_workspace* ws) {
   ws->tc_aux.release();
   ws->small_scores.release();
   ws->tc_bar.release();
+  ws->probe_sync.release();
   ws->gather.release();
   ws->h_err.release();
+  ws->io.release();
+  ws->h_io.release();
   if (ws->done) cudaEventDestroy(ws->done);
   for (auto& pr : ws->events) {
     cudaEventDestroy(pr.first);
@@ -369,6 +372,7 @@ int32_t corpus_upload(mans_ctx* ctx, const float* rows, int64_t n, int64_t dim, 
   }
   int32_t rc = encode_row_map(&c->map, c->rows, n, dim, c->ld);
   if (rc == MANS_OK) rc = encode_row_map(&c->map_small, c->rows, n, dim, c->ld, kSmallTileRows);
+  if (rc == MANS_OK) rc = encode_row_map(&c->map_probe, c->rows, n, dim, c->ld, 32);
   if (rc != MANS_OK) {
     corpus_free(c);
     return rc;
@@ -396,15 +400,77 @@ int32_t check_device_error(mans_workspace* ws, cudaStream_t stream) {
   int h = 0;
   e = cudaMemcpy(&h, ws->err.ptr, sizeof(int), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return fail_cuda(e, "error word readback");
-  if (h != 0) {
-    ws->err_cleared = false;
-    if (ws->tc_bar.ptr) {  // a pass that gave up left the barrier count out of step
-      cudaMemset(ws->tc_bar.ptr, 0, sizeof(unsigned long long));
-      ws->tc_bar_base = 0;
-    }
-    return fail(MANS_ERR_EXEC, h == kErrTimeout ? "device wait timed out"
-                                                 : "device kernel reported an error");
+  return h != 0 ? device_error(ws, h) : MANS_OK;
+}
+
+// After a non-zero device error word `h` (stream idle): the next search
+// clears the word, and the grid-barrier counters a kernel that gave up may
+// have left out of step start again from zero.
+int32_t device_error(mans_workspace* ws, int h) {
+  ws->err_cleared = false;
+  if (ws->tc_bar.ptr) {
+    cudaMemset(ws->tc_bar.ptr, 0, sizeof(unsigned long long));
+    ws->tc_bar_base = 0;
   }
+  if (ws->probe_sync.ptr) {
+    cudaMemset(ws->probe_sync.ptr, 0, kProbeSyncBytes);
+    ws->probe_bar_base = 0;
+  }
+  return fail(MANS_ERR_EXEC, h == kErrTimeout ? "device wait timed out"
+                                               : "device kernel reported an error");
+}
+
+static size_t carve_io(size_t& o, size_t bytes) {
+  size_t at = (o + 255) / 256 * 256;
+  o = at + bytes;
+  return at;
+}
+
+int32_t host_buffer_search(mans_workspace* ws, const float* queries, int64_t nq, int64_t dim,
+                           int32_t kout, float* out_dist, uint32_t* out_ids, int32_t* out_counts,
+                           const DeviceSearch& search) {
+  cudaStream_t st = ws->stream;
+  const size_t qb = static_cast<size_t>(nq) * dim * sizeof(float);
+  const size_t rb = static_cast<size_t>(nq) * kout * sizeof(float);
+  const size_t cb = static_cast<size_t>(nq) * sizeof(int32_t);
+  size_t o = 0;
+  const size_t o_q = carve_io(o, qb);
+  const size_t o_d = carve_io(o, rb);
+  const size_t o_i = carve_io(o, rb);
+  const size_t o_c = carve_io(o, cb);
+  const size_t res_end = o;
+  const size_t o_e = carve_io(o, sizeof(int));
+  int32_t rc;
+  if ((rc = ws->io.reserve(o)) != MANS_OK) return rc;
+  if ((rc = ws->h_io.reserve(o)) != MANS_OK) return rc;
+  uint8_t* d = static_cast<uint8_t*>(ws->io.ptr);
+  uint8_t* h = static_cast<uint8_t*>(ws->h_io.ptr);
+  std::memcpy(h + o_q, queries, qb);
+  cudaError_t e = cudaMemcpyAsync(d + o_q, h + o_q, qb, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return fail_cuda(e, "query upload");
+  rc = search(reinterpret_cast<const float*>(d + o_q), reinterpret_cast<float*>(d + o_d),
+              reinterpret_cast<uint32_t*>(d + o_i), reinterpret_cast<int32_t*>(d + o_c), st);
+  if (rc != MANS_OK) {
+    cudaStreamSynchronize(st);
+    return rc;
+  }
+  e = cudaMemcpyAsync(h + o_d, d + o_d, res_end - o_d, cudaMemcpyDeviceToHost, st);
+  const bool word = ws->err.ptr && ws->err_cleared;
+  if (e == cudaSuccess && word)
+    e = cudaMemcpyAsync(h + o_e, ws->err.ptr, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e != cudaSuccess) {
+    cudaStreamSynchronize(st);
+    return fail_cuda(e, "result download");
+  }
+  e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return fail_cuda(e, "stream synchronize");
+  if (word) {
+    const int herr = *reinterpret_cast<const int*>(h + o_e);
+    if (herr != 0) return device_error(ws, herr);
+  }
+  std::memcpy(out_dist, h + o_d, rb);
+  std::memcpy(out_ids, h + o_i, rb);
+  std::memcpy(out_counts, h + o_c, cb);
   return MANS_OK;
 }
 
@@ -442,6 +508,7 @@ int32_t mans_ctx_create(int32_t device, mans_ctx** out_ctx) {
   ctx->device = device;
   ctx->num_sms = prop.multiProcessorCount;
   ctx->max_smem = static_cast<int>(prop.sharedMemPerBlockOptin);
+  ctx->coop_launch = prop.cooperativeLaunch != 0;
   *out_ctx = ctx;
   return MANS_OK;
 }
@@ -664,37 +731,12 @@ int32_t mans_flat_search(mans_ctx* ctx, const mans_corpus* corpus, const float* 
   mans_workspace* ws = acquire_workspace(ctx);
   if (!ws) return fail(MANS_ERR_OOM, "cannot create a workspace stream");
   const int32_t kout = std::min<int32_t>(k, MANS_MAX_TOPK);
-  cudaStream_t st = ws->stream;
-  do {
-    if ((rc = ws->queries.reserve(nq * dim * sizeof(float))) != MANS_OK) break;
-    if ((rc = ws->out_dist.reserve(nq * kout * sizeof(float))) != MANS_OK) break;
-    if ((rc = ws->out_ids.reserve(nq * kout * sizeof(uint32_t))) != MANS_OK) break;
-    if ((rc = ws->out_counts.reserve(nq * sizeof(int32_t))) != MANS_OK) break;
-    cudaError_t e = cudaMemcpyAsync(ws->queries.ptr, queries, nq * dim * sizeof(float),
-                                    cudaMemcpyHostToDevice, st);
-    if (e != cudaSuccess) {
-      rc = fail_cuda(e, "query upload");
-      break;
-    }
-    rc = run_flat_search(ctx, corpus, ws, static_cast<const float*>(ws->queries.ptr), nq, k, metric,
-                         static_cast<float*>(ws->out_dist.ptr),
-                         static_cast<uint32_t*>(ws->out_ids.ptr),
-                         static_cast<int32_t*>(ws->out_counts.ptr), st);
-    if (rc != MANS_OK) break;
-    e = cudaMemcpyAsync(out_dist, ws->out_dist.ptr, nq * kout * sizeof(float),
-                        cudaMemcpyDeviceToHost, st);
-    if (e == cudaSuccess)
-      e = cudaMemcpyAsync(out_ids, ws->out_ids.ptr, nq * kout * sizeof(uint32_t),
-                          cudaMemcpyDeviceToHost, st);
-    if (e == cudaSuccess)
-      e = cudaMemcpyAsync(out_counts, ws->out_counts.ptr, nq * sizeof(int32_t),
-                          cudaMemcpyDeviceToHost, st);
-    if (e != cudaSuccess) {
-      rc = fail_cuda(e, "result download");
-      break;
-    }
-    rc = check_device_error(ws, st);
-  } while (false);
+  rc = host_buffer_search(ws, queries, nq, dim, kout, out_dist, out_ids, out_counts,
+                          [&](const float* dq, float* dd, uint32_t* di, int32_t* dc,
+                              cudaStream_t st) {
+                            return run_flat_search(ctx, corpus, ws, dq, nq, k, metric, dd, di,
+                                                   dc, st);
+                          });
   release_workspace(ctx, ws);
   return rc;
 }

@@ -209,6 +209,46 @@ __device__ __forceinline__ uint64_t warp_sort32(uint64_t x, int lane) {
   return x;
 }
 
+// ---- warp-resident top-k of 64-bit keys (at most 32 kept) ----------------
+
+// The 32 smallest of two ascending lane-sorted lists, ascending: the lane-wise
+// minimum of t and x reversed is a bitonic sequence holding them, which a
+// half-cleaner cascade sorts.
+__device__ __forceinline__ uint64_t warp_merge32(uint64_t t, uint64_t x, int lane) {
+  uint64_t y = key_min(t, __shfl_sync(0xFFFFFFFFu, x, 31 - lane));
+#pragma unroll
+  for (int j = 16; j > 0; j >>= 1) {
+    const uint64_t z = __shfl_xor_sync(0xFFFFFFFFu, y, j);
+    y = (lane & j) == 0 ? key_min(y, z) : key_max(y, z);
+  }
+  return y;
+}
+
+// Offers one key per lane to the warp's ascending list of its k smallest keys
+// (lane i holds the (i+1)-th; `kth` is the warp-uniform k-th key, kept
+// current): a batch where more than six keys beat the k-th is sorted by
+// shuffles and merged in, fewer are inserted one by one at their rank (keys
+// are distinct; a key that no longer beats the k-th after an earlier
+// insertion lands at rank k or drops out, which is harmless).
+__device__ __forceinline__ void warp_topk_offer(uint64_t& best, uint64_t& kth, uint64_t key,
+                                                int k, int lane) {
+  uint32_t pass = __ballot_sync(0xFFFFFFFFu, key < kth);
+  if (!pass) return;
+  if (__popc(pass) > 6) {
+    best = warp_merge32(best, warp_sort32(key < kth ? key : kKeyMax, lane), lane);
+  } else {
+    while (pass) {
+      const int src = __ffs(pass) - 1;
+      pass &= pass - 1;
+      const uint64_t x = __shfl_sync(0xFFFFFFFFu, key, src);
+      const int at = __popc(__ballot_sync(0xFFFFFFFFu, best < x));
+      const uint64_t up = __shfl_up_sync(0xFFFFFFFFu, best, 1);
+      best = lane < at ? best : (lane == at ? x : up);
+    }
+  }
+  kth = __shfl_sync(0xFFFFFFFFu, best, k - 1);
+}
+
 // Running top-k of one query inside a thread block:
 //   buf[0, kp)      -- the current best keys (ascending, `nbest` of them valid)
 //   buf[kp, sortn)  -- an append queue of candidates below the threshold

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <functional>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -52,6 +53,9 @@ struct mans_ctx {
   int tc_min_batch = 16;
   // operand format of that path: MANS_TC_AUTO / MANS_TC_BF16 / MANS_TC_INT8
   int tc_format = 0;
+  // cooperative launches are available (the one-launch IVF-flat search)
+  bool coop_launch = false;
+  bool probe_configured = false;  // that kernel's shared-memory limit is set
   // A context over several GPUs (mans_ctx_create_multi): one single-device
   // context per GPU, members[0] on `device`; empty for a plain context.
   std::vector<mans_ctx*> members;
@@ -71,6 +75,7 @@ struct mans_corpus {
   bool owned = true;        // rows/norms/ids freed with the object
   CUtensorMap map;
   CUtensorMap map_small;  // the same rows in boxes of kSmallTileRows
+  CUtensorMap map_probe;  // the same rows in boxes of 32 (one-launch IVF-flat search)
   // bf16 copy and error-bound terms for the tensor-core batch path (built on
   // first use, dropped when rows change)
   std::mutex tc_mu;
@@ -122,7 +127,16 @@ struct mans_workspace {
   // keeps its expected value, both reset after a device error)
   mans::DeviceBuffer tc_bar;
   unsigned long long tc_bar_base = 0;
+  // one-launch IVF-flat search: its grid-barrier counter (monotonic, the host
+  // keeps the expected value) and per-query arrival counters (zero between
+  // launches); both reset after a device error
+  mans::DeviceBuffer probe_sync;
+  unsigned long long probe_bar_base = 0;
   mans::PinnedBuffer h_err;
+  // host-buffer searches: queries and packed results on the device, and their
+  // pinned staging copy on the host
+  mans::DeviceBuffer io;
+  mans::PinnedBuffer h_io;
   // optional CUDA-event timing of the dominant kernel (scan) launches
   bool timing = false;
   int timing_hold = 0;  // > 0 while an inner step (e.g. a centroid scan) runs untimed
@@ -142,6 +156,16 @@ mans_workspace* acquire_workspace(mans_ctx* ctx);
 void release_workspace(mans_ctx* ctx, mans_workspace* ws);
 void destroy_workspace(mans_workspace* ws);
 int32_t check_device_error(mans_workspace* ws, cudaStream_t stream);
+int32_t device_error(mans_workspace* ws, int h);
+// A search with host buffers: the queries are staged through pinned memory
+// and uploaded in one copy, `search` enqueues the device search on the
+// workspace stream, the packed results and the device error word come back
+// in one copy each, and the stream is synchronised once.
+using DeviceSearch = std::function<int32_t(const float* d_queries, float* d_dist, uint32_t* d_ids,
+                                           int32_t* d_counts, cudaStream_t stream)>;
+int32_t host_buffer_search(mans_workspace* ws, const float* queries, int64_t nq, int64_t dim,
+                           int32_t kout, float* out_dist, uint32_t* out_ids, int32_t* out_counts,
+                           const DeviceSearch& search);
 int pow2_at_least(int v);
 int choose_qb(int64_t nq);
 cudaEvent_t timing_begin(mans_workspace* ws, cudaStream_t stream);
@@ -169,6 +193,17 @@ int32_t group_flat_search(mans_ctx* ctx, const mans_corpus* corpus, const float*
 // MANS_ERR_INVALID for a multi-GPU context or corpus passed to an entry point
 // that runs on one device.
 int32_t reject_group(const mans_ctx* ctx, const mans_corpus* corpus, const char* what);
+// One-launch IVF-flat search of a few queries (ivf_probe.cu).
+constexpr int kProbeMaxQ = 4;            // queries per launch
+constexpr int kProbeMaxNlist = 8192;     // centroid keys of a query staged in shared memory
+constexpr size_t kProbeSyncBytes = 128;  // barrier counter at 0, arrival counters at 64
+bool ivf_probe_applies(const mans_ctx* ctx, const mans_corpus* packed, int32_t nlist, int64_t nq,
+                       int32_t kout, int32_t probe);
+int32_t run_ivf_probe(mans_ctx* ctx, const mans_corpus* cent, const mans_corpus* packed,
+                      const int64_t* d_offsets, mans_workspace* ws, const float* d_queries,
+                      int64_t nq, int32_t kout, int32_t keff, int32_t probe, int32_t metric,
+                      float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
+                      cudaStream_t stream);
 // tensor-core batch path (tc_scan.cu)
 // i8: the int8 operand format (else bf16); tc_use_int8 picks it for a batch.
 bool tc_use_int8(const mans_ctx* ctx, int64_t nq);

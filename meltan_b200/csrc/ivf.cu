@@ -209,6 +209,10 @@ static int32_t run_ivf_search(mans_ctx* ctx, mans_ivf* ivf, mans_workspace* ws,
   if (nq > INT32_MAX / std::max(probe, 1)) return fail(MANS_ERR_SEARCH, "query batch too large");
 
   const int32_t keff = static_cast<int32_t>(std::min<int64_t>(kout, ivf->n));
+  // a few queries: the whole search in one cooperative launch (ivf_probe.cu)
+  if (ivf_probe_applies(ctx, ivf->packed, ivf->nlist, nq, kout, probe))
+    return run_ivf_probe(ctx, ivf->cent, ivf->packed, ivf->offsets, ws, d_queries, nq, kout, keff,
+                         probe, metric, d_out_dist, d_out_ids, d_out_counts, stream);
   const int32_t kp = pow2_at_least(keff);
   const int64_t pairs = nq * probe;
   const int qb = choose_qb((pairs + ivf->nlist - 1) / ivf->nlist);
@@ -454,37 +458,12 @@ int32_t mans_ivf_search(mans_ctx* ctx, mans_ivf* ivf, const float* queries, int6
   DeviceGuard g(ctx->device);
   mans_workspace* ws = acquire_workspace(ctx);
   if (!ws) return fail(MANS_ERR_OOM, "cannot create a workspace stream");
-  cudaStream_t st = ws->stream;
-  do {
-    if ((rc = ws->queries.reserve(nq * dim * sizeof(float))) != MANS_OK) break;
-    if ((rc = ws->out_dist.reserve(nq * kout * sizeof(float))) != MANS_OK) break;
-    if ((rc = ws->out_ids.reserve(nq * kout * sizeof(uint32_t))) != MANS_OK) break;
-    if ((rc = ws->out_counts.reserve(nq * sizeof(int32_t))) != MANS_OK) break;
-    cudaError_t e = cudaMemcpyAsync(ws->queries.ptr, queries, nq * dim * sizeof(float),
-                                    cudaMemcpyHostToDevice, st);
-    if (e != cudaSuccess) {
-      rc = fail_cuda(e, "query upload");
-      break;
-    }
-    rc = run_ivf_search(ctx, ivf, ws, static_cast<const float*>(ws->queries.ptr), nq, k, nprobe,
-                        metric, static_cast<float*>(ws->out_dist.ptr),
-                        static_cast<uint32_t*>(ws->out_ids.ptr),
-                        static_cast<int32_t*>(ws->out_counts.ptr), st);
-    if (rc != MANS_OK) break;
-    e = cudaMemcpyAsync(out_dist, ws->out_dist.ptr, nq * kout * sizeof(float),
-                        cudaMemcpyDeviceToHost, st);
-    if (e == cudaSuccess)
-      e = cudaMemcpyAsync(out_ids, ws->out_ids.ptr, nq * kout * sizeof(uint32_t),
-                          cudaMemcpyDeviceToHost, st);
-    if (e == cudaSuccess)
-      e = cudaMemcpyAsync(out_counts, ws->out_counts.ptr, nq * sizeof(int32_t),
-                          cudaMemcpyDeviceToHost, st);
-    if (e != cudaSuccess) {
-      rc = fail_cuda(e, "result download");
-      break;
-    }
-    rc = check_device_error(ws, st);
-  } while (false);
+  rc = host_buffer_search(ws, queries, nq, dim, kout, out_dist, out_ids, out_counts,
+                          [&](const float* dq, float* dd, uint32_t* di, int32_t* dc,
+                              cudaStream_t st) {
+                            return run_ivf_search(ctx, ivf, ws, dq, nq, k, nprobe, metric, dd,
+                                                  di, dc, st);
+                          });
   release_workspace(ctx, ws);
   return rc;
 }

@@ -333,46 +333,6 @@ __device__ __forceinline__ float adc_sum(const float* lut, int ks, const uint8_t
   return total;
 }
 
-// ---- warp-resident top-k of (score, seq) keys (at most 32 kept) ----------------
-
-// The 32 smallest of two ascending lane-sorted lists, ascending: the lane-wise
-// minimum of t and x reversed is a bitonic sequence holding them, which a
-// half-cleaner cascade sorts.
-__device__ __forceinline__ uint64_t warp_merge32(uint64_t t, uint64_t x, int lane) {
-  uint64_t y = key_min(t, __shfl_sync(0xFFFFFFFFu, x, 31 - lane));
-#pragma unroll
-  for (int j = 16; j > 0; j >>= 1) {
-    const uint64_t z = __shfl_xor_sync(0xFFFFFFFFu, y, j);
-    y = (lane & j) == 0 ? key_min(y, z) : key_max(y, z);
-  }
-  return y;
-}
-
-// Offers one key per lane to the warp's ascending list of its k smallest keys
-// (lane i holds the (i+1)-th; `kth` is the warp-uniform k-th key, kept
-// current): a batch where more than six keys beat the k-th is sorted by
-// shuffles and merged in, fewer are inserted one by one at their rank (keys
-// are distinct; a key that no longer beats the k-th after an earlier
-// insertion lands at rank k or drops out, which is harmless).
-__device__ __forceinline__ void warp_topk_offer(uint64_t& best, uint64_t& kth, uint64_t key,
-                                                int k, int lane) {
-  uint32_t pass = __ballot_sync(0xFFFFFFFFu, key < kth);
-  if (!pass) return;
-  if (__popc(pass) > 6) {
-    best = warp_merge32(best, warp_sort32(key < kth ? key : kKeyMax, lane), lane);
-  } else {
-    while (pass) {
-      const int src = __ffs(pass) - 1;
-      pass &= pass - 1;
-      const uint64_t x = __shfl_sync(0xFFFFFFFFu, key, src);
-      const int at = __popc(__ballot_sync(0xFFFFFFFFu, best < x));
-      const uint64_t up = __shfl_up_sync(0xFFFFFFFFu, best, 1);
-      best = lane < at ? best : (lane == at ? x : up);
-    }
-  }
-  kth = __shfl_sync(0xFFFFFFFFu, best, k - 1);
-}
-
 // Block b handles items b, b + grid, ... ; item = (query, probe rank).  Small
 // blocks (several resident per SM) hide the latency of the per-item steps:
 // residual, LUT in shared memory, sequential ADC per code, the item's k
@@ -1297,41 +1257,12 @@ int32_t mans_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, const float* queries, i
   DeviceGuard g(ctx->device);
   mans_workspace* ws = acquire_workspace(ctx);
   if (!ws) return fail(MANS_ERR_OOM, "cannot create a workspace stream");
-  cudaStream_t st = ws->stream;
-  int32_t rc;
-  do {
-    if ((rc = ws->queries.reserve(nq * dim * sizeof(float))) != MANS_OK) break;
-    if ((rc = ws->out_dist.reserve(std::max<int64_t>(1, nq * kout) * sizeof(float))) != MANS_OK) break;
-    if ((rc = ws->out_ids.reserve(std::max<int64_t>(1, nq * kout) * sizeof(uint32_t))) != MANS_OK) break;
-    if ((rc = ws->out_counts.reserve(nq * sizeof(int32_t))) != MANS_OK) break;
-    if ((rc = ws->err.reserve(sizeof(int))) != MANS_OK) break;
-    cudaError_t e = cudaMemcpyAsync(ws->queries.ptr, queries, nq * dim * sizeof(float),
-                                    cudaMemcpyHostToDevice, st);
-    if (e != cudaSuccess) {
-      rc = fail_cuda(e, "query upload");
-      break;
-    }
-    rc = run_ivfpq_search(ctx, ix, ws, static_cast<const float*>(ws->queries.ptr), nq, k, nprobe,
-                          static_cast<float*>(ws->out_dist.ptr),
-                          static_cast<uint32_t*>(ws->out_ids.ptr),
-                          static_cast<int32_t*>(ws->out_counts.ptr), st);
-    if (rc != MANS_OK) break;
-    if (kout > 0) {
-      e = cudaMemcpyAsync(out_dist, ws->out_dist.ptr, nq * kout * sizeof(float),
-                          cudaMemcpyDeviceToHost, st);
-      if (e == cudaSuccess)
-        e = cudaMemcpyAsync(out_ids, ws->out_ids.ptr, nq * kout * sizeof(uint32_t),
-                            cudaMemcpyDeviceToHost, st);
-    }
-    if (e == cudaSuccess)
-      e = cudaMemcpyAsync(out_counts, ws->out_counts.ptr, nq * sizeof(int32_t),
-                          cudaMemcpyDeviceToHost, st);
-    if (e != cudaSuccess) {
-      rc = fail_cuda(e, "result download");
-      break;
-    }
-    rc = check_device_error(ws, st);
-  } while (false);
+  const int32_t rc =
+      host_buffer_search(ws, queries, nq, dim, kout, out_dist, out_ids, out_counts,
+                         [&](const float* dq, float* dd, uint32_t* di, int32_t* dc,
+                             cudaStream_t st) {
+                           return run_ivfpq_search(ctx, ix, ws, dq, nq, k, nprobe, dd, di, dc, st);
+                         });
   release_workspace(ctx, ws);
   return rc;
 }
