@@ -75,7 +75,6 @@ struct mans_corpus {
   bool owned = true;        // rows/norms/ids freed with the object
   CUtensorMap map;
   CUtensorMap map_small;  // the same rows in boxes of kSmallTileRows
-  CUtensorMap map_probe;  // the same rows in boxes of 32 (one-launch IVF-flat search)
   // bf16 copy and error-bound terms for the tensor-core batch path (built on
   // first use, dropped when rows change)
   std::mutex tc_mu;
