@@ -879,9 +879,11 @@ def build_index_data(args, nq_max, device=None, mb=None, ctx=None, shard=None, d
                   "lists": flat}
 
 
-def probed_list_rows(args, art, q):
+def probed_list_rows(args, art, q, distinct=False):
     """Rows of the lists each query probes (the per-query unit of the
-    roofline): top-nprobe centroids by the search's own key, with torch."""
+    roofline), or with `distinct` the rows of the union of the batch's probed
+    lists (what a batch that reads each probed list once must read):
+    top-nprobe centroids by the search's own key, with torch."""
     import torch
     dev = "cuda" if torch.cuda.is_available() else "cpu"
     qt = torch.from_numpy(q).to(dev)
@@ -900,6 +902,8 @@ def probed_list_rows(args, art, q):
         sizes = off[1:] - off[:-1]
         key = torch.cdist(qt, c)
     top = torch.topk(key, min(args.nprobe, key.shape[1]), dim=1, largest=False).indices
+    if distinct:
+        return int(sizes[torch.unique(top)].sum().item())
     return sizes[top].sum(1).cpu().numpy().astype(np.int64)
 
 
@@ -1028,13 +1032,20 @@ def measure_index(torch, ws, search_dev, search_host, q, kout, steps, warmup, wi
             "clocks": clock_info, "ok": ok, "kout": kout}
 
 
-def index_roofline(args, res, list_rows):
+def index_roofline(args, res, list_rows, distinct_rows=None):
     """HBM roofline of the timed kernel: the list scan (IVF-flat) or the ADC
-    scoring kernel (IVF-PQ), with the per-query bytes of the probed lists:
-    IVF-flat rows (d*4) + norm (4) + id (4); IVF-PQ code (m) + id (4)."""
+    scoring kernel (IVF-PQ), with the bytes of the probed lists: IVF-flat
+    rows (d*4) + norm (4) + id (4); IVF-PQ code (m) + id (4).  The IVF-flat
+    batch scan reads every probed list once for all the queries that probe
+    it, so its bytes are those of the distinct probed lists; the other
+    kernels count each query's lists."""
     peak, src = measured_peaks()
     per_row = args.dim * 4 + 8 if args.workload == "ivf" else args.pq_m + 4
     alg = float(list_rows.sum()) * per_row
+    batch_scan = args.workload == "ivf" and distinct_rows is not None and \
+        res["launches"] != res["steps"]
+    if batch_scan:
+        alg = float(distinct_rows) * per_row
     # One library launch per step: the one-launch IVF-flat search, whose
     # timed kernel also scores the centroids (rows + norms, once per launch).
     one_launch = args.workload == "ivf" and res["launches"] == res["steps"]
@@ -1042,7 +1053,9 @@ def index_roofline(args, res, list_rows):
         alg += float(args.nlist) * (args.dim * 4 + 4)
         kernel = "ivf_probe_kernel (centroid scan + top-nprobe + probed lists, one launch)"
     else:
-        kernel = "scan_topk_kernel (probed lists)" if args.workload == "ivf" else "pq_adc_kernel"
+        kernel = ("ivf_seg_scan_kernel (distinct probed lists, read once per batch)"
+                  if batch_scan and args.k <= 32 else
+                  "scan_topk_kernel (probed lists)" if args.workload == "ivf" else "pq_adc_kernel")
     kern_s = res["kern_avg_ms"] * 1e-3
     achieved = alg / kern_s / 1e9 if kern_s > 0 else 0.0
     wl = index_workload_config(args, res["nq"])["workload"]
@@ -1052,6 +1065,7 @@ def index_roofline(args, res, list_rows):
                                          "list_scan" if args.workload == "ivf" else "adc"),
             "kernel": kernel, "kernel_avg_us": 1e3 * res["kern_avg_ms"],
             "algorithmic_bytes_per_launch": alg,
+            "per_query_bytes_per_launch": float(list_rows.sum()) * per_row,
             "peak_source": f"{src} hbm_gbs (STREAM copy)"}
 
 
@@ -1171,7 +1185,9 @@ def index_session(args, torch, mb, lib, world, rank, dist, cases):
                 dist.all_reduce(t, op=dist.ReduceOp.MAX)
                 r["total_ms"], r["e2e_ms"] = t.tolist()
             r["nprobe"] = nprobe
-            r["roofline"] = index_roofline(args, r, probed_list_rows(args, art, q))
+            r["roofline"] = index_roofline(
+                args, r, probed_list_rows(args, art, q),
+                probed_list_rows(args, art, q, distinct=True) if args.workload == "ivf" else None)
             r["workload"] = index_workload_config(args, nq, nprobe)["workload"]
             r["config"] = index_workload_config(args, nq, nprobe)
             results.append(r)

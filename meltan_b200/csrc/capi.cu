@@ -372,6 +372,7 @@ int32_t corpus_upload(mans_ctx* ctx, const float* rows, int64_t n, int64_t dim, 
   }
   int32_t rc = encode_row_map(&c->map, c->rows, n, dim, c->ld);
   if (rc == MANS_OK) rc = encode_row_map(&c->map_small, c->rows, n, dim, c->ld, kSmallTileRows);
+  if (rc == MANS_OK) rc = encode_row_map(&c->map_seg, c->rows, n, dim, c->ld, 32);
   if (rc != MANS_OK) {
     corpus_free(c);
     return rc;

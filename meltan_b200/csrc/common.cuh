@@ -104,6 +104,59 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint3
       : "memory");
 }
 
+// ---- rows staged one per lane ---------------------------------------------------
+//
+// A warp stages up to 32 rows into shared memory with one bulk copy per lane
+// (a row pitch of ld + 4 floats puts the rows of a quarter-warp 4 banks apart,
+// so their 16-byte reads hit distinct banks), and each lane scores its row.
+
+// dot(q_i, row) for i < nq (independent chains), each in index order with
+// separately rounded multiply and add; the staged row and the queries are
+// zero past dim, and adding +0 leaves a sum that started at +0 unchanged.
+template <int NQ>
+__device__ __forceinline__ void row_dots(const float* srow, const float* q, int qw, int nq, int ld,
+                                         float (&acc)[NQ]) {
+#pragma unroll
+  for (int i = 0; i < NQ; ++i) acc[i] = 0.0f;
+  const float4* r4 = reinterpret_cast<const float4*>(srow);
+#pragma unroll 4
+  for (int c = 0; c < ld / 4; ++c) {
+    const float4 v = r4[c];
+#pragma unroll
+    for (int i = 0; i < NQ; ++i) {
+      if (i >= nq) break;
+      const float4 b = reinterpret_cast<const float4*>(q + i * qw)[c];
+      float a = acc[i];
+      a = __fadd_rn(a, __fmul_rn(v.x, b.x));
+      a = __fadd_rn(a, __fmul_rn(v.y, b.y));
+      a = __fadd_rn(a, __fmul_rn(v.z, b.z));
+      a = __fadd_rn(a, __fmul_rn(v.w, b.w));
+      acc[i] = a;
+    }
+  }
+}
+
+// Stages row src (ld floats, 16-byte aligned) into dst with one bulk copy
+// that completes on `bar` (one barrier per staged row).  The proxy fence orders this thread's earlier
+// reads of dst before the copy overwrites it.
+__device__ __forceinline__ void stage_row(float* dst, const float* src, int ld, uint64_t* bar) {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  const uint32_t bytes = static_cast<uint32_t>(ld) * 4;
+  mbar_arrive_expect_tx(bar, bytes);
+  bulk_load(dst, src, bytes, bar);
+}
+
+// Waits for this lane's staged row (lanes without a row pass); false for the
+// whole warp when a wait gave up, after one more bounded wait for the copy.
+__device__ __forceinline__ bool wait_row(uint64_t* bar, uint32_t ph, bool has_row, int* err) {
+  const bool ok = !has_row || mbar_wait_bounded(bar, ph, err);
+  if (__any_sync(0xFFFFFFFFu, !ok)) {
+    if (has_row && ok == false) mbar_wait_bounded(bar, ph, nullptr);
+    return false;
+  }
+  return true;
+}
+
 // ---- named barriers -----------------------------------------------------------
 
 __device__ __forceinline__ void named_sync(int id, int nthreads) {

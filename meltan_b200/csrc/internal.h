@@ -75,6 +75,7 @@ struct mans_corpus {
   bool owned = true;        // rows/norms/ids freed with the object
   CUtensorMap map;
   CUtensorMap map_small;  // the same rows in boxes of kSmallTileRows
+  CUtensorMap map_seg;    // the same rows in boxes of 32 (the IVF-flat batch list scan)
   // bf16 copy and error-bound terms for the tensor-core batch path (built on
   // first use, dropped when rows change)
   std::mutex tc_mu;

@@ -169,6 +169,180 @@ __global__ void query_norms_warp_kernel(const float* __restrict__ q, int64_t nq,
   out[w] = acc;
 }
 
+// List scan of query batches: one warp per block, as many blocks per SM as
+// the shared memory holds.  A block walks planned segments (a run of rows of
+// one probed list and up to kSegQ of the queries that probe it): 32-row
+// tiles arrive as TMA boxes of 32 rows x 32 fp32 (128-byte swizzle: 16-byte
+// chunk j of row r at chunk j ^ (r & 7), so the eight lanes of a
+// quarter-warp read distinct bank groups), lane i scores row i against every
+// query of the segment (independent chains, each the reference's summation
+// order) and keeps each query's 32 smallest (distance, id) keys in
+// registers; the next tile's boxes fly while the keys are ranked.  Each
+// query of the segment then writes its sorted keys to its slot.  Rows are
+// read once for all queries of the segment, and no block-wide barrier is
+// needed anywhere.
+constexpr int kSegQ = 4;
+constexpr int kSegBox = 32 * kTileCols * 4;  // one 32 x 32 fp32 box
+
+struct SegScanParams {
+  const ScanSegment* segs;
+  const int32_t* nseg;
+  const float* queries;  // nq x dim
+  const int32_t* qidx;
+  const float* qnorms;   // null for IP
+  const float* norms;    // null for IP
+  const uint32_t* ids;
+  int32_t dim;
+  int32_t nchunks;  // ceil(dim / 32)
+  int32_t metric;
+  int32_t k;   // <= 32
+  int32_t kp;  // slot width
+  uint64_t* slot_keys;
+  int32_t* slot_counts;
+  int* err;
+};
+
+__host__ __device__ inline size_t seg_scan_smem(int nchunks) {
+  return 1024 + static_cast<size_t>(nchunks) * kSegBox +
+         static_cast<size_t>(kSegQ) * nchunks * kTileCols * 4 + 16 + kSegQ * 4;
+}
+
+__device__ __forceinline__ void seg_load_tile(uint8_t* stage, const CUtensorMap* map, int64_t row,
+                                              int nchunks, uint64_t* bar) {
+  mbar_arrive_expect_tx(bar, static_cast<uint32_t>(nchunks) * kSegBox);
+  for (int cc = 0; cc < nchunks; ++cc)
+    tma_load_2d(stage + cc * kSegBox, map, cc * kTileCols, static_cast<int32_t>(row), bar);
+}
+
+__global__ void __launch_bounds__(32) ivf_seg_scan_kernel(const __grid_constant__ CUtensorMap map,
+                                                          const SegScanParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* stage =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<size_t>(smem_raw) + 1023) / 1024 * 1024);
+  const int nch = p.nchunks, qw = nch * kTileCols;
+  float* qs = reinterpret_cast<float*>(stage + nch * kSegBox);  // kSegQ x qw
+  uint64_t* bar = reinterpret_cast<uint64_t*>(qs + kSegQ * qw);
+  float* qn = reinterpret_cast<float*>(bar + 1);
+  const int lane = threadIdx.x;
+  if (lane == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&map);
+  }
+  __syncwarp();
+  uint32_t ph = 0;
+  const int nseg = *p.nseg;
+  for (int s = blockIdx.x; s < nseg; s += gridDim.x) {
+    const ScanSegment seg = p.segs[s];
+    const int nqs = seg.qcount;
+    // the first tile is in flight while the queries load
+    if (lane == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      seg_load_tile(stage, &map, seg.row_begin, nch, bar);
+    }
+    int qid[kSegQ];
+#pragma unroll
+    for (int j = 0; j < kSegQ; ++j) qid[j] = j < nqs ? __ldg(p.qidx + seg.qbase + j) : 0;
+    for (int i0 = lane; i0 < kSegQ * qw; i0 += 32 * 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * 32;
+        const int j = i / qw, c = i - j * qw;
+        int qj = qid[0];
+#pragma unroll
+        for (int jj = 1; jj < kSegQ; ++jj)
+          if (j == jj) qj = qid[jj];
+        v[u] = (i < kSegQ * qw && j < nqs && c < p.dim)
+                   ? __ldg(p.queries + static_cast<int64_t>(qj) * p.dim + c)
+                   : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (i0 + u * 32 < kSegQ * qw) qs[i0 + u * 32] = v[u];
+    }
+    if (lane < kSegQ) {
+      int qj = qid[0];
+#pragma unroll
+      for (int jj = 1; jj < kSegQ; ++jj)
+        if (lane == jj) qj = qid[jj];
+      qn[lane] = (p.qnorms && lane < nqs) ? __ldg(p.qnorms + qj) : 0.0f;
+    }
+    __syncwarp();
+    float qnj[kSegQ];
+#pragma unroll
+    for (int j = 0; j < kSegQ; ++j) qnj[j] = qn[j];
+    uint64_t best[kSegQ], kth[kSegQ];
+#pragma unroll
+    for (int j = 0; j < kSegQ; ++j) best[j] = kth[j] = kKeyMax;
+    bool aborted = false;
+    for (int t0 = 0; t0 < seg.row_count; t0 += 32) {
+      const int64_t row = seg.row_begin + t0 + lane;
+      const bool valid = t0 + lane < seg.row_count;
+      float vn = 0.0f;
+      uint32_t id = 0;
+      if (valid) {
+        if (p.norms) vn = __ldg(p.norms + row);
+        id = __ldg(p.ids + row);
+      }
+      const bool ok = mbar_wait_bounded(bar, ph, p.err);
+      if (__any_sync(0xFFFFFFFFu, !ok)) {
+        mbar_wait_bounded(bar, ph, nullptr);  // the copies in flight: once more, bounded
+        aborted = true;
+        break;
+      }
+      ph ^= 1u;
+      float acc[kSegQ];
+#pragma unroll
+      for (int j = 0; j < kSegQ; ++j) acc[j] = 0.0f;
+      for (int cc = 0; cc < nch; ++cc) {
+        const uint8_t* rowp = stage + cc * kSegBox + lane * 128;
+        float4 v[8];
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj)
+          v[jj] = *reinterpret_cast<const float4*>(rowp + ((jj ^ (lane & 7)) << 4));
+#pragma unroll
+        for (int j = 0; j < kSegQ; ++j) {
+          if (j >= nqs) break;
+          const float4* qv = reinterpret_cast<const float4*>(qs + j * qw + cc * kTileCols);
+          float a = acc[j];
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            const float4 b = qv[jj];
+            a = __fadd_rn(a, __fmul_rn(v[jj].x, b.x));
+            a = __fadd_rn(a, __fmul_rn(v[jj].y, b.y));
+            a = __fadd_rn(a, __fmul_rn(v[jj].z, b.z));
+            a = __fadd_rn(a, __fmul_rn(v[jj].w, b.w));
+          }
+          acc[j] = a;
+        }
+      }
+      __syncwarp();
+      if (t0 + 32 < seg.row_count && lane == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        seg_load_tile(stage, &map, seg.row_begin + t0 + 32, nch, bar);
+      }
+#pragma unroll
+      for (int j = 0; j < kSegQ; ++j) {
+        if (j >= nqs) break;
+        const float d = finalize_distance(p.metric, acc[j], qnj[j], vn);
+        warp_topk_offer(best[j], kth[j], valid ? make_key(d, id) : kKeyMax, p.k, lane);
+      }
+    }
+    if (aborted) break;
+#pragma unroll
+    for (int j = 0; j < kSegQ; ++j) {
+      if (j >= nqs) break;
+      const int slot = seg.slot_base + j * seg.slot_stride;
+      const bool ok = lane < p.k && best[j] != kKeyMax;
+      if (lane < p.kp) p.slot_keys[static_cast<size_t>(slot) * p.kp + lane] = ok ? best[j] : kKeyMax;
+      const unsigned vm = __ballot_sync(0xFFFFFFFFu, ok);
+      if (lane == 0) p.slot_counts[slot] = __popc(vm);
+    }
+    __syncwarp();
+  }
+}
+
 }  // namespace
 
 // Byte layout of the per-call scratch carved from one device buffer.
@@ -215,18 +389,41 @@ static int32_t run_ivf_search(mans_ctx* ctx, mans_ivf* ivf, mans_workspace* ws,
                          probe, metric, d_out_dist, d_out_ids, d_out_counts, stream);
   const int32_t kp = pow2_at_least(keff);
   const int64_t pairs = nq * probe;
-  const int qb = choose_qb((pairs + ivf->nlist - 1) / ivf->nlist);
-  // Work units: list chunks of 64 rows (64-row tiles) or 256 / 512 rows
-  // (256-row tiles) -- the smallest chunk whose unit count still fits in one
-  // wave of CTAs, so a short probe spreads over many SMs without giving one
-  // CTA several units in a row.
   const int64_t avg_len = (ivf->n + ivf->nlist - 1) / ivf->nlist;
+  // Batches with k <= 32 whose rows fit a warp's stage: the warp-per-segment
+  // scan (segments of up to kSegQ queries and 32..256 rows: the largest run
+  // that still gives every resident warp a few segments).
+  const int seg_nch = static_cast<int>((ivf->dim + kTileCols - 1) / kTileCols);
+  const size_t seg_smem = seg_scan_smem(seg_nch);
+  const void* seg_fn = reinterpret_cast<const void*>(ivf_seg_scan_kernel);
+  int seg_blocks = 0;
+  if (keff <= 32 && seg_smem <= static_cast<size_t>(ctx->max_smem)) {
+    static_cast<void>(cudaFuncSetAttribute(seg_fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(seg_smem)));
+    static_cast<void>(cudaFuncSetAttribute(seg_fn,
+                                           cudaFuncAttributePreferredSharedMemoryCarveout,
+                                           cudaSharedmemCarveoutMaxShared));
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&seg_blocks, seg_fn, 32, seg_smem) !=
+        cudaSuccess)
+      seg_blocks = 0;
+  }
+  const bool seg_scan = seg_blocks > 0;
+  const int qb = seg_scan ? kSegQ : choose_qb((pairs + ivf->nlist - 1) / ivf->nlist);
+  // Work units of the streaming scan: list chunks of 64 rows (64-row tiles)
+  // or 256 / 512 rows (256-row tiles) -- the smallest chunk whose unit count
+  // still fits in one wave of CTAs, so a short probe spreads over many SMs
+  // without giving one CTA several units in a row.
   auto units_for = [&](int64_t chunk) { return pairs * ((avg_len + chunk - 1) / chunk); };
   int chunk_rows = kChunkRows;
-  if (units_for(kSmallTileRows) <= ctx->num_sms)
+  if (seg_scan) {
+    const int64_t warps = static_cast<int64_t>(seg_blocks) * ctx->num_sms;
+    chunk_rows = 256;
+    while (chunk_rows > 32 && units_for(chunk_rows) < 4 * warps) chunk_rows /= 2;
+  } else if (units_for(kSmallTileRows) <= ctx->num_sms) {
     chunk_rows = kSmallTileRows;
-  else if (units_for(kTileRows) <= ctx->num_sms)
+  } else if (units_for(kTileRows) <= ctx->num_sms) {
     chunk_rows = kTileRows;
+  }
   const bool small = chunk_rows == kSmallTileRows;
   const int64_t max_chunks = std::max<int64_t>(1, (ivf->max_len + chunk_rows - 1) / chunk_rows);
   const int64_t max_refs = pairs * max_chunks;
@@ -234,7 +431,7 @@ static int32_t run_ivf_search(mans_ctx* ctx, mans_ivf* ivf, mans_workspace* ws,
   if (max_refs * qb > INT32_MAX / 2) return fail(MANS_ERR_SEARCH, "query batch too large");
   const int nchunks = static_cast<int>((ivf->dim + kTileCols - 1) / kTileCols);
   const int stages = scan_max_stages(qb, nchunks);
-  if (stages < 2) return fail(MANS_ERR_SEARCH, "dimension too large for the scan kernel");
+  if (!seg_scan && stages < 2) return fail(MANS_ERR_SEARCH, "dimension too large for the scan kernel");
 
   // scratch: centroid top-k + planner arrays + slots
   size_t o = 0;
@@ -317,6 +514,32 @@ static int32_t run_ivf_search(mans_ctx* ctx, mans_ivf* ivf, mans_workspace* ws,
   if (e != cudaSuccess) return fail_cuda(e, "ivf plan launch");
 
   // 3. scan the probed lists
+  if (seg_scan) {
+    SegScanParams sp{};
+    sp.segs = pp.segs;
+    sp.nseg = pp.nseg;
+    sp.queries = d_queries;
+    sp.qidx = pp.qidx;
+    sp.qnorms = metric != MANS_METRIC_IP ? qn : nullptr;
+    sp.norms = metric != MANS_METRIC_IP ? ivf->packed->norms : nullptr;
+    sp.ids = ivf->packed->ids;
+    sp.dim = static_cast<int32_t>(ivf->dim);
+    sp.nchunks = seg_nch;
+    sp.metric = metric;
+    sp.k = keff;
+    sp.kp = kp;
+    sp.slot_keys = static_cast<uint64_t*>(ws->slot_keys.ptr);
+    sp.slot_counts = static_cast<int32_t*>(ws->slot_counts.ptr);
+    sp.err = pp.err;
+    const int64_t grid = std::min<int64_t>(static_cast<int64_t>(seg_blocks) * ctx->num_sms,
+                                           std::max<int64_t>(1, max_segs));
+    cudaEvent_t stop = timing_begin(ws, stream);
+    ivf_seg_scan_kernel<<<static_cast<unsigned>(grid), 32, seg_smem, stream>>>(
+        ivf->packed->map_seg, sp);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_cuda(e, "ivf segment scan launch");
+    timing_end(stop, stream);
+  }
   ScanParams p{};
   p.segs = pp.segs;
   p.nseg = static_cast<int32_t>(max_segs);
@@ -339,10 +562,13 @@ static int32_t run_ivf_search(mans_ctx* ctx, mans_ivf* ivf, mans_workspace* ws,
   p.slot_keys = static_cast<uint64_t*>(ws->slot_keys.ptr);
   p.slot_counts = static_cast<int32_t*>(ws->slot_counts.ptr);
   p.err = pp.err;
-  cudaEvent_t stop = timing_begin(ws, stream);
-  e = launch_scan(qb, small ? ivf->packed->map_small : ivf->packed->map, p, ctx->num_sms, stream);
-  if (e != cudaSuccess) return fail_cuda(e, "ivf scan launch");
-  timing_end(stop, stream);
+  if (!seg_scan) {
+    cudaEvent_t stop = timing_begin(ws, stream);
+    e = launch_scan(qb, small ? ivf->packed->map_small : ivf->packed->map, p, ctx->num_sms,
+                    stream);
+    if (e != cudaSuccess) return fail_cuda(e, "ivf scan launch");
+    timing_end(stop, stream);
+  }
 
   // 4. merge per query
   MergeParams m{};

@@ -115,53 +115,6 @@ __host__ __device__ inline ProbeLayout probe_layout(int ld, int qw, int stages, 
   return L;
 }
 
-// dot(q_i, row) for i < nq (independent chains), each in index order with
-// separately rounded multiply and add; the staged row and the queries are
-// zero past dim, and adding +0 leaves a sum that started at +0 unchanged.
-template <int NQ>
-__device__ __forceinline__ void row_dots(const float* srow, const float* q, int qw, int nq, int ld,
-                                         float (&acc)[NQ]) {
-#pragma unroll
-  for (int i = 0; i < NQ; ++i) acc[i] = 0.0f;
-  const float4* r4 = reinterpret_cast<const float4*>(srow);
-#pragma unroll 4
-  for (int c = 0; c < ld / 4; ++c) {
-    const float4 v = r4[c];
-#pragma unroll
-    for (int i = 0; i < NQ; ++i) {
-      if (i >= nq) break;
-      const float4 b = reinterpret_cast<const float4*>(q + i * qw)[c];
-      float a = acc[i];
-      a = __fadd_rn(a, __fmul_rn(v.x, b.x));
-      a = __fadd_rn(a, __fmul_rn(v.y, b.y));
-      a = __fadd_rn(a, __fmul_rn(v.z, b.z));
-      a = __fadd_rn(a, __fmul_rn(v.w, b.w));
-      acc[i] = a;
-    }
-  }
-}
-
-// Stages row src into dst with one bulk copy that completes on `bar` (one
-// barrier per staged row).  The proxy fence orders this thread's earlier
-// reads of dst before the copy overwrites it.
-__device__ __forceinline__ void stage_row(float* dst, const float* src, int ld, uint64_t* bar) {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  const uint32_t bytes = static_cast<uint32_t>(ld) * 4;
-  mbar_arrive_expect_tx(bar, bytes);
-  bulk_load(dst, src, bytes, bar);
-}
-
-// Waits for this lane's staged row (lanes without a row pass); false for the
-// whole warp when a wait gave up, after one more bounded wait for the copy.
-__device__ __forceinline__ bool wait_row(uint64_t* bar, uint32_t ph, bool has_row, int* err) {
-  const bool ok = !has_row || mbar_wait_bounded(bar, ph, err);
-  if (__any_sync(0xFFFFFFFFu, !ok)) {
-    if (has_row && ok == false) mbar_wait_bounded(bar, ph, nullptr);
-    return false;
-  }
-  return true;
-}
-
 __global__ void __launch_bounds__(kProbeThreads, 1) ivf_probe_kernel(const ProbeParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>(probe_align(reinterpret_cast<size_t>(smem_raw), 128));

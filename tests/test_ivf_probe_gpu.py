@@ -167,3 +167,21 @@ def test_probe_repeated_calls_share_counters(ctx):
         np.testing.assert_array_equal(dd.cpu().numpy()[0], want[0][i])
     ws.close()
     part.close()
+
+
+@pytest.mark.parametrize("mg,mo", MET)
+def test_batch_segment_scan(ctx, mg, mo):
+    """Query batches (5 or more queries, k <= 32) take the warp-per-segment
+    list scan: segments of up to four queries of one list.  Many queries on
+    one list (the same query repeated), k at the edge of the path (32, and
+    33 on the streaming scan) and several dims."""
+    for dim in (3, 130, 384):
+        v, q = bench.make_mixture(12000, dim, 48, 40, seed=30 + dim)
+        cent = v[:: len(v) // 48][:48].copy()
+        lay = layout(v, cent, mo)
+        part = mb.Partition(ctx, cent, lay[2], lay[1], lay[0])
+        qq = np.concatenate([q, np.repeat(q[:1], 23, axis=0)])  # one list, 24 queries
+        for k in (1, 10, 32, 33):
+            for nprobe in (1, 5, 47):
+                check(ctx, part, lay, cent, qq, k, nprobe, mg, mo, fused=False)
+        part.close()
