@@ -383,8 +383,11 @@ int32_t mans_pq_encode(mans_ctx *ctx, const float *vectors, int64_t n, int64_t d
  * coarse SIMDDistance ranking with newest-first ties, residual LUT
  * (ProductQuantizer.distanceTableFlattened) and sequential ADC sums per
  * probed list, merged with the BoundedSortedList rule.  out_ids are internal
- * ids; results are min(k, 256) wide.  A query of the wrong width yields an
- * empty result, as the reference returns []. */
+ * ids; results are k wide (the reference's list has no cap beyond k): up to
+ * k = 256 the candidates stay in on-chip top-k lists, above it every probed
+ * entry's key is sorted per query in device memory (workspace scratch of
+ * 16 bytes per probed entry).  A query of the wrong width yields an empty
+ * result, as the reference returns []. */
 int32_t mans_ivfpq_search(mans_ctx *ctx, mans_ivfpq *ix, const float *queries, int64_t nq,
                           int64_t dim, int32_t k, int32_t nprobe, float *out_dist,
                           uint32_t *out_ids, int32_t *out_counts);

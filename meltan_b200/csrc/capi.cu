@@ -162,6 +162,7 @@ void destroy_workspace(mans_workspace* ws) {
   ws->gather.release();
   ws->h_err.release();
   ws->io.release();
+  ws->big.release();
   ws->h_io.release();
   if (ws->done) cudaEventDestroy(ws->done);
   for (auto& pr : ws->events) {

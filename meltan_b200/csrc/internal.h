@@ -133,6 +133,9 @@ struct mans_workspace {
   mans::DeviceBuffer probe_sync;
   unsigned long long probe_bar_base = 0;
   mans::PinnedBuffer h_err;
+  // IVF-PQ searches with k above 256: every probed entry's key, twice (sort
+  // input and output), and the sort's temporary storage
+  mans::DeviceBuffer big;
   // host-buffer searches: queries and packed results on the device, and their
   // pinned staging copy on the host
   mans::DeviceBuffer io;

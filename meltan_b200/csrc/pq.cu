@@ -34,6 +34,8 @@
 #include "kernels.h"
 #include "mans_cuda.h"
 
+#include <cub/cub.cuh>
+
 using namespace mans;
 
 struct mans_ivfpq {
@@ -115,9 +117,17 @@ struct ResolveParams {
   int32_t kout;
 };
 
+__device__ __forceinline__ uint32_t seq_payload(const ResolveParams& p, int64_t q, uint32_t seq);
+
 __device__ __forceinline__ uint32_t resolve_payload(const ResolveParams& p, int64_t q, int i) {
   uint32_t seq = p.in_seq[q * p.kin + i];
   if (p.in_payload) return p.in_payload[q * p.kin + i];
+  return seq_payload(p, q, seq);
+}
+
+// Internal id of the entry with insertion sequence `seq` (probe rank, list
+// position) among query q's probed lists.
+__device__ __forceinline__ uint32_t seq_payload(const ResolveParams& p, int64_t q, uint32_t seq) {
   if (!p.probe_lists) return seq;
   uint32_t rank = seq >> p.pos_bits;
   uint32_t pos = seq & ((1u << p.pos_bits) - 1u);
@@ -793,6 +803,235 @@ __global__ void __launch_bounds__(256) ivfpq_shard_merge_kernel(
   if (threadIdx.x == 0) m_count[q] = valid;
 }
 
+// ---- k above 256: every probed entry's key, sorted per query ------------------
+//
+// The shared-memory top-k lists of the batch kernels hold at most 512 keys,
+// while _IVFPQIndex.search keeps BoundedSortedList(capacity: k) for any k
+// (IVFPQIndex.swift:197).  For k > 256 every probed entry's (score, insertion
+// sequence) key is written out, the keys are sorted per query (CUB
+// segmented radix sort), and the list's outcome is read off the sorted keys.
+
+// Per query: the entries of each probed list (rank order) and their running
+// offsets within the query's key segment; counts[q] = the query's total.
+__global__ void __launch_bounds__(256) lk_offsets_kernel(const uint32_t* __restrict__ probe_lists,
+                                                         const int32_t* __restrict__ probe_counts,
+                                                         const int64_t* __restrict__ offsets,
+                                                         int32_t probe, int64_t* __restrict__ qoff,
+                                                         int64_t* __restrict__ counts) {
+  __shared__ int64_t wsum[8];
+  const int64_t q = blockIdx.x;
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  int64_t len = 0;
+  if (t < probe && t < probe_counts[q]) {
+    const uint32_t l = probe_lists[q * probe + t];
+    len = offsets[l + 1] - offsets[l];
+  }
+  int64_t incl = len;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t u = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += u;
+  }
+  if (lane == 31) wsum[w] = incl;
+  __syncthreads();
+  int64_t add = 0;
+  for (int i = 0; i < w; ++i) add += wsum[i];
+  if (t < probe) qoff[q * probe + t] = incl + add - len;
+  if (t == 255) counts[q] = incl + add;
+}
+
+// Exclusive running sum of counts[0, n) into seg[0, n] by one block.
+__global__ void __launch_bounds__(1024) lk_scan_kernel(const int64_t* __restrict__ counts, int64_t n,
+                                                       int64_t* __restrict__ seg) {
+  __shared__ int64_t part[32];
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int64_t per = (n + 1023) / 1024;
+  const int64_t b = t * per, e = b + per < n ? b + per : n;
+  int64_t sum = 0;
+  for (int64_t i = b; i < e; ++i) sum += counts[i];
+  int64_t incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t u = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += u;
+  }
+  if (lane == 31) part[w] = incl;
+  __syncthreads();
+  int64_t add = 0;
+  for (int i = 0; i < w; ++i) add += part[i];
+  int64_t acc = incl - sum + add;
+  for (int64_t i = b; i < e; ++i) {
+    seg[i] = acc;
+    acc += counts[i];
+  }
+  if (t == 1023) seg[n] = acc;
+}
+
+// One block per (query, probe rank) item: the residual, the distance table,
+// and the key of every entry of the list at its place in the query's segment.
+__global__ void __launch_bounds__(kAdcThreads) pq_adc_all_kernel(const AdcParams p,
+                                                                 const int64_t* __restrict__ seg,
+                                                                 const int64_t* __restrict__ qoff,
+                                                                 uint64_t* __restrict__ keys) {
+  extern __shared__ uint8_t smem_raw[];
+  float* lut = reinterpret_cast<float*>((reinterpret_cast<size_t>(smem_raw) + 15) / 16 * 16);
+  float* resid = lut + p.m * p.ks;
+  const int tid = threadIdx.x;
+  const int64_t items = p.nq * p.probe;
+  for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
+    const int64_t q = it / p.probe;
+    const int pr = static_cast<int>(it - q * p.probe);
+    __syncthreads();  // the previous item is done with the table
+    if (pr >= p.probe_counts[q]) continue;
+    const uint32_t list = p.probe_lists[q * p.probe + pr];
+    const int64_t off = p.offsets[list];
+    const int64_t len = p.offsets[list + 1] - off;
+    if (len == 0) continue;
+    for (int d = tid; d < p.dim; d += kAdcThreads)
+      resid[d] = __fsub_rn(p.queries[q * p.dim + d], p.coarse[list * p.coarse_ld + d]);
+    __syncthreads();
+    build_tables<1, kAdcThreads>(p, lut, resid);
+    __syncthreads();
+    uint64_t* out = keys + seg[q] + qoff[it];
+    for (int64_t e = tid; e < len; e += kAdcThreads) {
+      const float total = adc_sum(lut, p.ks, p.codes + (off + e) * p.m, p.m);
+      const uint32_t pos = p.pos ? __ldg(p.pos + off + e) : static_cast<uint32_t>(e);
+      out[e] = make_key(total, (static_cast<uint32_t>(pr) << p.pos_bits) | pos);
+    }
+  }
+}
+
+// The k-th smallest (1-based) of n 32-bit words by a block of 256 threads:
+// four 8-bit radix passes over get(i).
+template <typename Get>
+__device__ uint32_t block_kth_u32(Get get, int64_t n, int64_t k, int* hist, int* ctl) {
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  uint32_t prefix = 0, mask = 0;
+  int64_t rank = k;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    hist[t] = 0;
+    __syncthreads();
+    for (int64_t i = t; i < n; i += 256) {
+      const uint32_t v = get(i);
+      if ((v & mask) == prefix) atomicAdd(&hist[(v >> shift) & 255u], 1);
+    }
+    __syncthreads();
+    if (w == 0) {
+      int h[8];
+      int64_t s = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        h[i] = hist[lane * 8 + i];
+        s += h[i];
+      }
+      int64_t incl = s;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int64_t u = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += u;
+      }
+      const int64_t excl = incl - s;
+      if (excl < rank && rank <= incl) {
+        int64_t c = excl;
+        int bin = lane * 8 + 7;
+        for (int i = 0; i < 8; ++i) {
+          if (c + h[i] >= rank) {
+            bin = lane * 8 + i;
+            break;
+          }
+          c += h[i];
+        }
+        ctl[0] = bin;
+        ctl[1] = static_cast<int>(rank - c);
+      }
+    }
+    __syncthreads();
+    prefix |= static_cast<uint32_t>(ctl[0]) << shift;
+    mask |= 0xFFu << shift;
+    rank = ctl[1];
+  }
+  return prefix;
+}
+
+// BoundedSortedList(capacity K) over one query's keys sorted by (score, seq)
+// (the closed form of bsl_resolve_kernel, read off the full sorted segment).
+// Keys below the K-th key's score are all kept (runs of equal scores newest
+// first); of the keys equal to it, those among the first K arrivals (by
+// sequence) of the ones below and the K earliest equal ones were inserted,
+// and the newest K - l of them survive.
+__global__ void __launch_bounds__(256) bsl_resolve_large_kernel(const ResolveParams p,
+                                                                const uint64_t* __restrict__ sorted,
+                                                                const int64_t* __restrict__ seg) {
+  __shared__ int hist[256];
+  __shared__ int ctl[2];
+  __shared__ uint32_t skth;
+  const int64_t q = blockIdx.x;
+  const int tid = threadIdx.x;
+  const uint64_t* ks = sorted + seg[q];
+  const int64_t c = seg[q + 1] - seg[q];
+  const int64_t K = p.cap;
+  auto hi = [&](int64_t i) { return static_cast<uint32_t>(ks[i] >> 32); };
+  // first index in [a, b) whose score word is >= x (> x when `strict`)
+  auto bound = [&](int64_t a, int64_t b, uint32_t x, bool strict) {
+    while (a < b) {
+      const int64_t mid = (a + b) >> 1;
+      const uint32_t v = hi(mid);
+      if (strict ? v <= x : v < x)
+        a = mid + 1;
+      else
+        b = mid;
+    }
+    return a;
+  };
+  int64_t l, nout, e_keep = 0, e_first = 0;
+  if (c <= K) {
+    l = nout = c;
+  } else {
+    const uint32_t wv = hi(K - 1);
+    l = bound(0, K, wv, false);
+    const int64_t e_end = bound(K, c, wv, true);
+    const int64_t ecount = min(e_end - l, K);
+    const int64_t total = l + ecount;
+    const uint32_t sk =
+        block_kth_u32([&](int64_t i) { return static_cast<uint32_t>(ks[i]); }, total, K, hist, ctl);
+    if (tid == 0) skth = sk;
+    __syncthreads();
+    // inserted equal-score entries: the E' entries with sequence <= the K-th
+    // arrival (E' is sorted by sequence)
+    int64_t a = l, b = l + ecount;
+    while (a < b) {
+      const int64_t mid = (a + b) >> 1;
+      if (static_cast<uint32_t>(ks[mid]) <= skth)
+        a = mid + 1;
+      else
+        b = mid;
+    }
+    const int64_t ins = a - l;
+    e_keep = K - l;
+    e_first = l + ins - e_keep;
+    nout = K;
+  }
+  for (int64_t i = tid; i < l; i += 256) {
+    // the equal-score run [a, b) holding i, read back to front
+    const uint32_t v = hi(i);
+    const int64_t a = bound(0, i + 1, v, false), b = bound(i, l, v, true);
+    const int64_t src = a + (b - 1 - i);
+    p.out_score[q * p.kout + i] = key_distance(ks[src]);
+    p.out_id[q * p.kout + i] = seq_payload(p, q, static_cast<uint32_t>(ks[src]));
+  }
+  for (int64_t j = tid; j < e_keep; j += 256) {
+    const int64_t src = e_first + (e_keep - 1 - j);
+    p.out_score[q * p.kout + l + j] = key_distance(ks[src]);
+    p.out_id[q * p.kout + l + j] = seq_payload(p, q, static_cast<uint32_t>(ks[src]));
+  }
+  for (int64_t i = nout + tid; i < p.kout; i += 256) {
+    p.out_score[q * p.kout + i] = __int_as_float(0x7F800000);
+    p.out_id[q * p.kout + i] = kEmptyId;
+  }
+  if (tid == 0) p.out_count[q] = static_cast<int32_t>(nout);
+}
+
 }  // namespace
 
 static size_t carve(size_t& o, size_t bytes) {
@@ -803,11 +1042,113 @@ static size_t carve(size_t& o, size_t bytes) {
 
 // partial: null, or this shard's block [score | seq | id | count] (2k
 // entries per query) instead of the resolved top-k (the row-sharded search)
+// k above 256 (not for shard blocks): steps 2-4 over every probed entry.
+static int32_t run_ivfpq_large_k(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* ws,
+                                 const float* d_queries, int64_t nq, int32_t k, int32_t probe,
+                                 int32_t pos_bits, const uint32_t* pl, const int32_t* pc,
+                                 float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
+                                 cudaStream_t stream) {
+  int32_t rc;
+  // per-query offsets and segment starts (small; in `small_scores`, which the
+  // coarse step no longer needs)
+  const size_t o_qo = 0;
+  const size_t o_ct = (nq * probe * sizeof(int64_t) + 255) / 256 * 256;
+  const size_t o_sg = o_ct + (nq * sizeof(int64_t) + 255) / 256 * 256;
+  const size_t small_bytes = o_sg + (nq + 1) * sizeof(int64_t);
+  if ((rc = ws->small_scores.reserve(small_bytes)) != MANS_OK) return rc;
+  uint8_t* S = static_cast<uint8_t*>(ws->small_scores.ptr);
+  int64_t* qoff = reinterpret_cast<int64_t*>(S + o_qo);
+  int64_t* counts = reinterpret_cast<int64_t*>(S + o_ct);
+  int64_t* seg = reinterpret_cast<int64_t*>(S + o_sg);
+  lk_offsets_kernel<<<static_cast<unsigned>(nq), 256, 0, stream>>>(pl, pc, ix->offsets, probe, qoff,
+                                                                  counts);
+  lk_scan_kernel<<<1, 1024, 0, stream>>>(counts, nq, seg);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail_cuda(e, "large-k offsets launch");
+  // the total number of keys sizes the buffers: one host round trip
+  int64_t total = 0;
+  e = cudaMemcpyAsync(&total, seg + nq, sizeof(int64_t), cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return fail_cuda(e, "large-k total");
+  if (total > INT32_MAX) return fail(MANS_ERR_SEARCH, "too many probed entries for one batch");
+  size_t tmp_bytes = 0;
+  e = cub::DeviceSegmentedRadixSort::SortKeys(nullptr, tmp_bytes, static_cast<const uint64_t*>(nullptr),
+                                              static_cast<uint64_t*>(nullptr), static_cast<int>(total),
+                                              static_cast<int>(nq), seg, seg + 1, 0, 64, stream);
+  if (e != cudaSuccess) return fail_cuda(e, "large-k sort size");
+  const size_t keys_bytes = (static_cast<size_t>(std::max<int64_t>(total, 1)) * 8 + 255) / 256 * 256;
+  if ((rc = ws->big.reserve(2 * keys_bytes + tmp_bytes)) != MANS_OK) return rc;
+  uint64_t* kin = static_cast<uint64_t*>(ws->big.ptr);
+  uint64_t* kout_keys = reinterpret_cast<uint64_t*>(static_cast<uint8_t*>(ws->big.ptr) + keys_bytes);
+  void* tmp = static_cast<uint8_t*>(ws->big.ptr) + 2 * keys_bytes;
+  if (total > 0) {
+    AdcParams a{};
+    a.queries = d_queries;
+    a.coarse = ix->coarse->rows;
+    a.coarse_ld = ix->coarse->ld;
+    a.codebooks = ix->codebooks;
+    a.codes = ix->codes;
+    a.pos = ix->pos;
+    a.offsets = ix->offsets;
+    a.probe_lists = pl;
+    a.probe_counts = pc;
+    a.probe = probe;
+    a.pos_bits = pos_bits;
+    a.nq = nq;
+    a.dim = static_cast<int32_t>(ix->dim);
+    a.m = ix->m;
+    a.ks = ix->ks;
+    a.sub = ix->sub;
+    a.metric = ix->metric;
+    const size_t smem = 16 + static_cast<size_t>(ix->m) * ix->ks * 4 +
+                        static_cast<size_t>((ix->dim + 3) / 4 * 4) * 4;
+    if (smem > static_cast<size_t>(ctx->max_smem) - 64)
+      return fail(MANS_ERR_SEARCH, "PQ distance table exceeds shared memory");
+    e = cudaFuncSetAttribute(pq_adc_all_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+    if (e != cudaSuccess) return fail_cuda(e, "large-k adc configure");
+    int per_sm = 1;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pq_adc_all_kernel, kAdcThreads, smem);
+    if (e != cudaSuccess) return fail_cuda(e, "large-k adc occupancy");
+    const int grid = static_cast<int>(std::min<int64_t>(
+        nq * probe, static_cast<int64_t>(ctx->num_sms) * std::max(1, per_sm)));
+    cudaEvent_t stop = timing_begin(ws, stream);
+    pq_adc_all_kernel<<<grid, kAdcThreads, smem, stream>>>(a, seg, qoff, kin);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_cuda(e, "large-k adc launch");
+    timing_end(stop, stream);
+    e = cub::DeviceSegmentedRadixSort::SortKeys(tmp, tmp_bytes, kin, kout_keys,
+                                                static_cast<int>(total), static_cast<int>(nq), seg,
+                                                seg + 1, 0, 64, stream);
+    if (e != cudaSuccess) return fail_cuda(e, "large-k sort");
+  }
+  ResolveParams f{};
+  f.nq = nq;
+  f.cap = k;
+  f.pos_bits = pos_bits;
+  f.probe_lists = pl;
+  f.probe_stride = probe;
+  f.offsets = ix->offsets;
+  f.ids = ix->ids;
+  f.pos = ix->pos;
+  f.out_score = d_out_dist;
+  f.out_id = d_out_ids;
+  f.out_count = d_out_counts;
+  f.kout = k;
+  bsl_resolve_large_kernel<<<static_cast<unsigned>(nq), 256, 0, stream>>>(f, kout_keys, seg);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail_cuda(e, "large-k resolve launch");
+  ws->launches += 6;
+  return MANS_OK;
+}
+
 static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* ws,
                                 const float* d_queries, int64_t nq, int32_t k, int32_t nprobe,
                                 float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
                                 cudaStream_t stream, int32_t* partial = nullptr) {
-  const int32_t kout = std::min<int32_t>(k, MANS_MAX_TOPK);
+  // Results are k wide (BoundedSortedList(capacity: k), IVFPQIndex.swift:197);
+  // the shard blocks of the partial search keep at most 256.
+  const int32_t kout = partial ? std::min<int32_t>(k, MANS_MAX_TOPK) : k;
   if (nq <= 0) return MANS_OK;
   if (k <= 0 || ix->n <= 0 || ix->nlist <= 0) {
     if (kout <= 0) {
@@ -829,7 +1170,8 @@ static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* w
                   static_cast<long long>(ix->max_pos), probe, pos_bits);
     return fail(MANS_ERR_SEARCH, msg);
   }
-  const int32_t k2 = 2 * kout;  // ADC candidates per list and after the merge
+  const bool large_k = kout > MANS_MAX_TOPK;
+  const int32_t k2 = 2 * std::min<int32_t>(kout, MANS_MAX_TOPK);  // ADC candidates per list and after the merge
   const int32_t kp2 = pow2_at_least(k2);
 
   size_t o = 0;
@@ -901,6 +1243,9 @@ static int32_t run_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, mans_workspace* w
   bsl_resolve_kernel<<<static_cast<unsigned>(nq), 256, 0, stream>>>(r);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "coarse resolve launch");
+  if (large_k)
+    return run_ivfpq_large_k(ctx, ix, ws, d_queries, nq, kout, probe, pos_bits, pl, pc,
+                             d_out_dist, d_out_ids, d_out_counts, stream);
 
   // 2. per (query, probed list): residual LUT + ADC, 2k best per list
   AdcParams a{};
@@ -1243,7 +1588,7 @@ int32_t mans_ivfpq_search(mans_ctx* ctx, mans_ivfpq* ix, const float* queries, i
   if (!ctx || !ix || ix->ctx != ctx) return fail(MANS_ERR_INVALID, "null or foreign IVF-PQ index");
   if (nq < 0) return fail(MANS_ERR_INVALID, "negative query count");
   if (nq == 0) return MANS_OK;
-  const int32_t kout = std::max<int32_t>(0, std::min<int32_t>(k, MANS_MAX_TOPK));
+  const int32_t kout = std::max<int32_t>(0, k);  // k wide: the list has no cap beyond k
   if (dim != ix->dim) {
     // _IVFPQIndex.search returns [] for a query of the wrong width (:184-186)
     for (int64_t i = 0; i < nq * kout; ++i) {

@@ -65,7 +65,7 @@ class IVFPQIndex:
     def search_arrays(self, queries, k: int, nprobe: int):
         q = _f32(np.atleast_2d(queries))
         nq, dim = q.shape
-        kout = max(0, min(k, MAX_TOP_K))
+        kout = max(0, k)  # k wide: BoundedSortedList(capacity: k) has no cap beyond k
         od = np.empty((nq, kout), np.float32)
         oi = np.empty((nq, kout), np.uint32)
         oc = np.empty(nq, np.int32)

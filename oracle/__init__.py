@@ -333,9 +333,9 @@ def ivfpq_search(coarse, codebooks, codes, list_offsets, lists, queries, k, npro
     nlist, d = coarse.shape
     m, ks, sub = codebooks.shape
     nq = queries.shape[0]
-    kout = min(k, MAX_TOPK)
-    od = np.empty((nq, max(kout, 0)), np.float32)
-    oi = np.empty((nq, max(kout, 0)), np.uint32)
+    kout = max(k, 0)  # BoundedSortedList(capacity: k) has no cap beyond k
+    od = np.empty((nq, kout), np.float32)
+    oi = np.empty((nq, kout), np.uint32)
     oc = np.empty(nq, np.int32)
     lib().orc_ivfpq_search(_p(coarse, _F), nlist, d, _p(codebooks, _F), m, ks, _p(codes, _U8),
                            _p(list_offsets, _I64), _p(lists, _U32), _p(queries, _F), nq, k, nprobe,

@@ -823,13 +823,13 @@ static void bsl_insert(orc_scored *list, int *count, int cap, orc_scored x) {
  * (cpuADCDistances, :418-452), each candidate inserted in list order into a
  * BoundedSortedList of capacity k.  `lists`/`list_offsets` are the inverted
  * lists in insertion order (internal ids); `codes` is row-major [id][m].
- * Output rows are min(k, 256) wide (the C ABI's cap). */
+ * Output rows are k wide: the list has no cap beyond k (IVFPQIndex.swift:197). */
 void orc_ivfpq_search(const float *coarse, int32_t nlist, int64_t dim, const float *codebooks,
                       int32_t m, int32_t ks, const uint8_t *codes, const int64_t *list_offsets,
                       const uint32_t *lists, const float *queries, int64_t nq, int32_t k,
                       int32_t nprobe, int32_t metric, float *out_d, uint32_t *out_i,
                       int32_t *out_count) {
-    int kout = k < ORC_MAX_TOPK ? k : ORC_MAX_TOPK;
+    int kout = k > 0 ? k : 0;
     int32_t sub = (int32_t)(dim / m);
     int probe = nprobe < 1 ? 1 : (nprobe > nlist ? nlist : nprobe);
     orc_scored *closest = (orc_scored *)malloc(sizeof(orc_scored) * (size_t)probe);

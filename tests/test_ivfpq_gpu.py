@@ -357,3 +357,39 @@ def test_list_sharded_grouped_ivfpq(ctx, shards):
         for ix in idx:
             ix.close()
     ws.close()
+
+
+@pytest.mark.parametrize("metric", [O.L2, O.COSINE, O.IP])
+def test_ivfpq_k_above_256(ctx, metric):
+    """k above 256: BoundedSortedList(capacity: k) has no cap beyond k
+    (IVFPQIndex.swift:197), so results are k wide; every probed entry's key
+    is sorted per query on the device.  k below, at and above the candidate
+    count, ties from duplicated codes, and single queries."""
+    v, q, coarse, cb, codes, off, flat = make_index(6000, 32, 8, 16, metric, seed=41)
+    ix = mb.IVFPQIndex(ctx, coarse, cb, codes, (off, flat), metric=mb.Metric(metric))
+    for nprobe in (1, 4, 16):
+        for k in (257, 700, 6000, 9000):
+            same(ix.search_arrays(q, k, nprobe),
+                 O.ivfpq_search(coarse, cb, codes, off, flat, q, k, nprobe, metric))
+    same(ix.search_arrays(q[:1], 300, 3),
+         O.ivfpq_search(coarse, cb, codes, off, flat, q[:1], 300, 3, metric))
+    ix.close()
+
+
+def test_ivfpq_k_above_256_ties(ctx):
+    """Heavy ties with k above 256: duplicated vectors (newest first among
+    equal scores) and every code identical (pure insertion order, with the
+    equal-score entries past the k-th rejected)."""
+    v, q, coarse, cb, codes, off, flat = make_index(3000, 16, 4, 4, O.L2, seed=43, dup=True)
+    ix = mb.IVFPQIndex(ctx, coarse, cb, codes, (off, flat))
+    for k in (300, 1001, 2999):
+        same(ix.search_arrays(v[:4], k, 4),
+             O.ivfpq_search(coarse, cb, codes, off, flat, v[:4], k, 4, O.L2))
+    codes0 = np.zeros_like(codes)
+    ix0 = mb.IVFPQIndex(ctx, coarse, cb, codes0, (off, flat))
+    for k in (257, 512, 1500, 3000, 4000):
+        for nprobe in (1, 2, 4):
+            same(ix0.search_arrays(q[:3], k, nprobe),
+                 O.ivfpq_search(coarse, cb, codes0, off, flat, q[:3], k, nprobe, O.L2))
+    ix.close()
+    ix0.close()
