@@ -72,10 +72,34 @@ __device__ __forceinline__ int list_chunks(const int64_t* off, int l, int chunk)
   return static_cast<int>((len + chunk - 1) / chunk);
 }
 
-__global__ void __launch_bounds__(kPlanThreads) ivf_plan_kernel(const PlanParams p) {
+// Bytes of shared memory the planner needs to keep its counters and the list
+// offsets on chip (0: they do not fit, the global arrays of PlanParams are used).
+inline size_t plan_smem_bytes(int nlist, int64_t nq, int max_smem) {
+  const size_t b = (static_cast<size_t>(nlist) + 1) * 8 + 4 * (static_cast<size_t>(nlist) + 1) * 4 +
+                   2 * (static_cast<size_t>(nq) + 1) * 4 + 64;
+  return b <= static_cast<size_t>(max_smem) - 1024 ? b : 0;
+}
+
+__global__ void __launch_bounds__(kPlanThreads) ivf_plan_kernel(PlanParams p, int on_chip) {
   __shared__ int32_t part[64];
+  extern __shared__ __align__(16) uint8_t plan_smem[];
   const int t = threadIdx.x, nt = blockDim.x;
   const int64_t pairs = static_cast<int64_t>(p.nq) * p.pk;
+  int32_t* q_soff_out = p.q_soff;
+  if (on_chip) {
+    // counters, running sums and the list offsets in shared memory: the
+    // atomics and scans below stay on chip; q_soff is copied out at the end
+    int64_t* off_s = reinterpret_cast<int64_t*>(plan_smem);
+    int32_t* w = reinterpret_cast<int32_t*>(off_s + p.nlist + 1);
+    for (int i = t; i <= p.nlist; i += nt) off_s[i] = p.offsets[i];
+    p.offsets = off_s;
+    p.list_cnt = w;
+    p.list_tmp = w + (p.nlist + 1);
+    p.list_qoff = w + 2 * (p.nlist + 1);
+    p.list_soff = w + 3 * (p.nlist + 1);
+    p.q_cnt = w + 4 * (p.nlist + 1);
+    p.q_soff = p.q_cnt + (p.nq + 1);
+  }
   for (int i = t; i < p.nlist; i += nt) p.list_cnt[i] = 0;
   for (int i = t; i < p.nq; i += nt) p.q_cnt[i] = 0;
   __syncthreads();
@@ -146,27 +170,37 @@ __global__ void __launch_bounds__(kPlanThreads) ivf_plan_kernel(const PlanParams
       if (at < p.max_refs) p.q_slots[at] = s * p.qb + j;
     }
   }
+  if (on_chip)
+    for (int i = t; i <= p.nq; i += nt) q_soff_out[i] = p.q_soff[i];
 }
 
-// Squared query norms in index order, one warp per query: lanes load 32
-// consecutive elements, lane order is replayed through shuffles so every lane
-// accumulates the same sequential sum.
+// Squared query norms in index order, one warp per query: the lanes load 32
+// consecutive elements at a time (eight such loads in flight), and the chunk's
+// squares are added lane by lane through shuffles, so every lane carries the
+// same sequential sum (lanes past dim add +0, which leaves it unchanged).
 __global__ void query_norms_warp_kernel(const float* __restrict__ q, int64_t nq, int32_t dim,
                                         float* __restrict__ out) {
   int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
   if (w >= nq) return;
   const float* v = q + w * dim;
-  // lane 0 sums in index order; the unrolled loads run ahead of the
-  // dependent adds
-  if (lane != 0) return;
   float acc = 0.0f;
-#pragma unroll 8
-  for (int d = 0; d < dim; ++d) {
-    const float y = v[d];
-    acc = __fadd_rn(acc, __fmul_rn(y, y));
+  for (int c0 = 0; c0 < dim; c0 += 32 * 8) {
+    float x[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int c = c0 + u * 32 + lane;
+      x[u] = c < dim ? __ldg(v + c) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (c0 + u * 32 >= dim) break;
+      const float sq = __fmul_rn(x[u], x[u]);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc = __fadd_rn(acc, __shfl_sync(0xFFFFFFFFu, sq, j));
+    }
   }
-  out[w] = acc;
+  if (lane == 0) out[w] = acc;
 }
 
 // List scan of query batches: one warp per block, as many blocks per SM as
@@ -232,6 +266,7 @@ __global__ void __launch_bounds__(32) ivf_seg_scan_kernel(const __grid_constant_
   __syncwarp();
   uint32_t ph = 0;
   const int nseg = *p.nseg;
+  const bool q4 = (p.dim & 3) == 0;
   for (int s = blockIdx.x; s < nseg; s += gridDim.x) {
     const ScanSegment seg = p.segs[s];
     const int nqs = seg.qcount;
@@ -243,7 +278,23 @@ __global__ void __launch_bounds__(32) ivf_seg_scan_kernel(const __grid_constant_
     int qid[kSegQ];
 #pragma unroll
     for (int j = 0; j < kSegQ; ++j) qid[j] = j < nqs ? __ldg(p.qidx + seg.qbase + j) : 0;
-    for (int i0 = lane; i0 < kSegQ * qw; i0 += 32 * 8) {
+    if (q4) {
+      // 16-byte loads: query rows start 16-byte aligned when dim % 4 == 0
+      const int qw4 = qw / 4, d4 = p.dim / 4;
+      for (int i = lane; i < kSegQ * qw4; i += 32) {
+        const int j = i / qw4, c = i - j * qw4;
+        int qj = qid[0];
+#pragma unroll
+        for (int jj = 1; jj < kSegQ; ++jj)
+          if (j == jj) qj = qid[jj];
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (j < nqs && c < d4)
+          v = __ldg(reinterpret_cast<const float4*>(p.queries + static_cast<int64_t>(qj) * p.dim) +
+                    c);
+        reinterpret_cast<float4*>(qs)[i] = v;
+      }
+    }
+    for (int i0 = lane; !q4 && i0 < kSegQ * qw; i0 += 32 * 8) {
       float v[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
@@ -339,7 +390,7 @@ __global__ void __launch_bounds__(32) ivf_seg_scan_kernel(const __grid_constant_
       const unsigned vm = __ballot_sync(0xFFFFFFFFu, ok);
       if (lane == 0) p.slot_counts[slot] = __popc(vm);
     }
-    __syncwarp();
+    __syncwarp();  // every lane is done with this segment's queries
   }
 }
 
@@ -509,7 +560,14 @@ static int32_t run_ivf_search(mans_ctx* ctx, mans_ivf* ivf, mans_workspace* ws,
     query_norms_warp_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
         d_queries, nq, static_cast<int32_t>(ivf->dim), qn);
   }
-  ivf_plan_kernel<<<1, kPlanThreads, 0, stream>>>(pp);
+  const size_t plan_smem = plan_smem_bytes(ivf->nlist, nq, ctx->max_smem);
+  if (plan_smem > 48 * 1024) {
+    cudaError_t ea = cudaFuncSetAttribute(ivf_plan_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(plan_smem));
+    if (ea != cudaSuccess) return fail_cuda(ea, "ivf plan configure");
+  }
+  ivf_plan_kernel<<<1, kPlanThreads, plan_smem, stream>>>(pp, plan_smem > 0 ? 1 : 0);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "ivf plan launch");
 
