@@ -157,6 +157,18 @@ __device__ __forceinline__ bool wait_row(uint64_t* bar, uint32_t ph, bool has_ro
   return true;
 }
 
+// ---- programmatic dependent launch ----------------------------------------------
+//
+// A kernel launched with programmatic stream serialization may start while the
+// previous kernel on the stream still runs; pdl_wait() blocks until that kernel
+// has completed and its memory is visible (a no-op for a plain launch).
+// pdl_trigger() lets the next such kernel start once every block of this one
+// has issued it or exited.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- named barriers -----------------------------------------------------------
 
 __device__ __forceinline__ void named_sync(int id, int nthreads) {

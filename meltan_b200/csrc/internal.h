@@ -56,6 +56,9 @@ struct mans_ctx {
   // cooperative launches are available (the one-launch IVF-flat search)
   bool coop_launch = false;
   bool probe_configured = false;  // that kernel's shared-memory limit is set
+  // programmatic dependent launch between the tensor-core path's kernels
+  // (cleared if the runtime refuses it)
+  bool pdl = true;
   // A context over several GPUs (mans_ctx_create_multi): one single-device
   // context per GPU, members[0] on `device`; empty for a plain context.
   std::vector<mans_ctx*> members;

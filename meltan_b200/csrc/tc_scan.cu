@@ -578,6 +578,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // launched while the query prep (or the sample pass) may still run: the
+  // barriers and TMEM are set up; wait for its queries, bounds and counters
+  pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1095,6 +1098,7 @@ struct TcQueryParams {
 // of |d~ - d|.
 template <bool I8>
 __global__ void tc_query_prep_kernel(const TcQueryParams p) {
+  pdl_trigger();  // the pass may launch and set up while the queries are prepared
   const int64_t q = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (q >= p.nq_pad) return;
@@ -1183,6 +1187,8 @@ __global__ void __launch_bounds__(kThresholdThreads) tc_threshold_kernel(
     float* __restrict__ thr_out, float* __restrict__ c_out) {
   __shared__ KthSmem ks;
   extern __shared__ __align__(16) float stage[];  // the sample row, when staged
+  pdl_trigger();
+  pdl_wait();  // the sample pass's values
   const int64_t q = blockIdx.x;
   const float* row = dense + q * ld;
   const float inf = __int_as_float(0x7F800000);
@@ -1313,6 +1319,7 @@ __global__ void __launch_bounds__(kRerankThreads) tc_rerank_kernel(const RerankP
   __shared__ KthSmem ks;
   const int tid = threadIdx.x;
   const int64_t q = blockIdx.x;
+  pdl_wait();  // the pass's candidates
 #pragma unroll 2
   for (int c = tid; c < p.dim; c += kRerankThreads) qsm[c] = __ldg(p.queries + q * p.dim + c);
   const int total = p.cand_count[q];
@@ -1512,6 +1519,34 @@ static int32_t tc_prepare_bf16(mans_corpus* c, int metric) {
   c->tc_metric = norm_mode;
   c->tc_ready = true;
   return MANS_OK;
+}
+
+// Launches `fn` with programmatic stream serialization (it may start while
+// the previous kernel on `stream` runs and waits for it with pdl_wait), and
+// as a cooperative launch when `coop`.  If the runtime refuses the attribute
+// the kernel is launched plainly, and the context stops asking.
+static cudaError_t launch_pdl(mans_ctx* ctx, const void* fn, dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, void** args, bool coop) {
+  if (ctx->pdl) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    at[1].id = cudaLaunchAttributeCooperative;
+    at[1].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = coop ? 2 : 1;
+    const cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
+    if (e == cudaSuccess) return e;
+    cudaGetLastError();  // clear the refusal and fall back for good
+    ctx->pdl = false;
+  }
+  if (coop) return cudaLaunchCooperativeKernel(fn, grid, block, args, smem, stream);
+  return cudaLaunchKernel(fn, grid, block, args, smem, stream);
 }
 
 static size_t carve(size_t& o, size_t bytes) {
@@ -1796,11 +1831,11 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
     tp.groups = static_cast<int32_t>(std::min<int64_t>(tp.groups, (sample + kRN - 1) / kRN));
     grid_s = static_cast<int>(tp.groups * qblocks);
   }
-  if (i8)
-    tc_scan_kernel<kDense, true><<<grid_s, kTcThreads, smem, stream>>>(map_q, map_r, tp);
-  else
-    tc_scan_kernel<kDense, false><<<grid_s, kTcThreads, smem, stream>>>(map_q, map_r, tp);
-  if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc sample launch");
+  {
+    void* args[] = {const_cast<CUtensorMap*>(&map_q), const_cast<CUtensorMap*>(&map_r), &tp};
+    e = launch_pdl(ctx, kd, dim3(grid_s), dim3(kTcThreads), smem, stream, args, false);
+  }
+  if (e != cudaSuccess) return fail_cuda(e, "tc sample launch");
   // 3. thresholds
   // one wave of queries: wide blocks over a staged row (latency); larger
   // batches: narrow blocks reading global memory (occupancy)
@@ -1808,11 +1843,20 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   const int staged =
       one_wave && dld * sizeof(float) <= static_cast<size_t>(kThresholdStageMax) ? 1 : 0;
   const size_t th_smem = staged ? dld * sizeof(float) : 0;
-  tc_threshold_kernel<<<static_cast<unsigned>(nq), one_wave ? kThresholdThreads : 256, th_smem,
-                        stream>>>(
-      F(o_dn), dld, dvals, keff, staged, F(o_ep), F(o_al), F(o_ga), F(o_sc), metric, F(o_th),
-      F(o_cq));
-  if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc threshold launch");
+  {
+    float* a_dn = F(o_dn);
+    int64_t a_ld = dld, a_rows = dvals;
+    int32_t a_k = keff;
+    int a_staged = staged, a_metric = metric;
+    float *a_ep = F(o_ep), *a_al = F(o_al), *a_ga = F(o_ga), *a_sc = F(o_sc), *a_th = F(o_th),
+          *a_cq = F(o_cq);
+    void* args[] = {&a_dn, &a_ld, &a_rows, &a_k, &a_staged, &a_ep, &a_al, &a_ga, &a_sc, &a_metric,
+                    &a_th, &a_cq};
+    e = launch_pdl(ctx, reinterpret_cast<const void*>(tc_threshold_kernel),
+                   dim3(static_cast<unsigned>(nq)), dim3(one_wave ? kThresholdThreads : 256),
+                   th_smem, stream, args, false);
+  }
+  if (e != cudaSuccess) return fail_cuda(e, "tc threshold launch");
   }
   // 4. full filtered pass
   tp.rows = n;
@@ -1862,18 +1906,13 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
                              static_cast<int>(smem));
     if (e != cudaSuccess) return fail_cuda(e, "tc configure");
     void* args[] = {const_cast<CUtensorMap*>(&map_q), const_cast<CUtensorMap*>(&map_r), &tp};
-    e = cudaLaunchCooperativeKernel(fn, grid, kTcThreads, args, smem, stream);
+    e = launch_pdl(ctx, fn, dim3(grid), dim3(kTcThreads), smem, stream, args, true);
     if (e == cudaSuccess) ws->tc_bar_base += 2ull * static_cast<unsigned long long>(grid);
-  } else if (metric == kL2 && i8) {
-    tc_scan_kernel<kFilterBias, true><<<grid, kTcThreads, smem, stream>>>(map_q, map_r, tp);
-  } else if (metric == kL2) {
-    tc_scan_kernel<kFilterBias, false><<<grid, kTcThreads, smem, stream>>>(map_q, map_r, tp);
-  } else if (i8) {
-    tc_scan_kernel<kFilterPlain, true><<<grid, kTcThreads, smem, stream>>>(map_q, map_r, tp);
   } else {
-    tc_scan_kernel<kFilterPlain, false><<<grid, kTcThreads, smem, stream>>>(map_q, map_r, tp);
+    void* args[] = {const_cast<CUtensorMap*>(&map_q), const_cast<CUtensorMap*>(&map_r), &tp};
+    e = launch_pdl(ctx, metric == kL2 ? kb_ : kp_, dim3(grid), dim3(kTcThreads), smem, stream, args,
+                   false);
   }
-  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "tc scan launch");
   timing_end(stop, stream);
   // 5. certify + exact re-rank
@@ -1900,9 +1939,13 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   rp.out_counts = d_out_counts;
   rp.fallbacks = fallbacks;
   rp.region = rerank_region_bytes(nq, ctx->num_sms);
-  tc_rerank_kernel<<<static_cast<unsigned>(nq), kRerankThreads,
-                     rerank_smem_bytes(corpus->dim, rp.region), stream>>>(rp);
-  if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc rerank launch");
+  {
+    void* args[] = {&rp};
+    e = launch_pdl(ctx, reinterpret_cast<const void*>(tc_rerank_kernel),
+                   dim3(static_cast<unsigned>(nq)), dim3(kRerankThreads),
+                   rerank_smem_bytes(corpus->dim, rp.region), stream, args, false);
+  }
+  if (e != cudaSuccess) return fail_cuda(e, "tc rerank launch");
   ws->tc_fallbacks = fallbacks;
   ws->launches += fused ? 3 : 5;
   ws->last_path = i8 ? 2 : 1;
