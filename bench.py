@@ -611,6 +611,20 @@ class Runner:
                 h_out.copy_(r, non_blocking=True)
                 torch.cuda.current_stream().synchronize()
 
+        # per-stage breakdown (CUDA events around every kernel of a step,
+        # outside the timed region above; max over ranks per stage)
+        n_st = min(steps, 20)
+        ws.set_timing(False, stages=True)
+        self.barrier()
+        for i in range(n_st):
+            step(dq[i % pool])
+        self.barrier()
+        st = ws.stage_times()
+        ws.set_timing(False)
+        stage_t = torch.tensor([st[name][0] for name in ws.STAGES], dtype=torch.float64,
+                               device="cuda")
+        stage_n = [st[name][1] for name in ws.STAGES]
+
         for i in range(max(3, warmup)):
             e2e_step(i)
         self.barrier()
@@ -630,7 +644,10 @@ class Runner:
             self.dist.all_reduce(stats, op=self.dist.ReduceOp.MAX)
             self.dist.all_reduce(steps_t, op=self.dist.ReduceOp.MAX)
             self.dist.all_reduce(e2e_t, op=self.dist.ReduceOp.MAX)
+            self.dist.all_reduce(stage_t, op=self.dist.ReduceOp.MAX)
         total_ms, e2e_ms, kern_avg_ms = stats.tolist()
+        stages_us = {name: round(1e3 * ms / n_st, 2)
+                     for name, ms, c in zip(ws.STAGES, stage_t.tolist(), stage_n) if c > 0}
         # every rank is done with the peers' buffers before any is released
         self.barrier()
         sharded.close()
@@ -639,7 +656,7 @@ class Runner:
                 "launches": total_launches, "p50_ms": p50(steps_t.tolist()),
                 "e2e_p50_s": p50(e2e_t.tolist()), "clocks": clock_info, "ok": ok, "kout": kout,
                 "path": path, "fallbacks_last_step": fallbacks,
-                "distinct_batches": min(pool, steps)}
+                "distinct_batches": min(pool, steps), "stages_us": stages_us}
 
     def latency(self, qs):
         """Single-query latency over len(qs) distinct queries, each timed on
@@ -1423,6 +1440,7 @@ def main():
             "e2e_matches_device_path": res["ok"],
             "distinct_queries_timed": res["distinct_batches"] * args.nq,
             "exact_fallbacks_last_step": res["fallbacks_last_step"],
+            "stages_us": dict(res["stages_us"], note=STAGES_NOTE),
         }
         if latency:
             line["p50_steps_us"] = 1e3 * res["p50_ms"]
@@ -1456,6 +1474,9 @@ def main():
 
 
 LATENCY_QUERIES = 200
+STAGES_NOTE = ("per step, device time of each stage (CUDA events around its kernels on the "
+               "launching stream, 20 extra steps outside the timed region, max over ranks); "
+               "merge = slot merge, or shard exchange + merge")
 
 
 def flat_entry(args, r, shard_rows, metric, tc_min, wl):
@@ -1469,6 +1490,7 @@ def flat_entry(args, r, shard_rows, metric, tc_min, wl):
             "e2e_matches_device_path": r["ok"],
             "distinct_queries_timed": r["distinct_batches"] * r["nq"],
             "exact_fallbacks_last_step": r["fallbacks_last_step"],
+            "stages_us": r["stages_us"],
             "config": workload_config(args, r["nq"])}
 
 

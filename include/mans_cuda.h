@@ -205,14 +205,31 @@ int32_t mans_workspace_last_path(mans_workspace *ws, int32_t *out);
 
 /* Measurement hooks (no reference counterpart; the reference's benchmark CLI
  * times whole calls, Sources/MetalANNSBenchmarks/HotPathProfiler.swift:22-304).
- * With timing enabled every later search made with `ws` brackets its dominant
+ * `enable` bit 0: every later search made with `ws` brackets its dominant
  * kernel (the scan) with CUDA events on the launching stream;
  * mans_workspace_stats waits for them, returns the summed kernel time, the
  * number of timed launches and the number of library kernels enqueued, and
- * resets the counters. */
+ * resets the counters.
+ * `enable` bit 1: every stage of a flat search (MANS_STAGE_*: query prep,
+ * sample pass, thresholds, the full pass or exact scan, the re-rank, and the
+ * merges -- slot merge, shard merge, peer exchange) is bracketed the same
+ * way; mans_workspace_stage_times waits for them and returns, per stage, the
+ * summed time in ms and the number of timed launches, then resets.  Events
+ * between the kernels keep the next kernel from launching early
+ * (programmatic dependent launch), so the stages sum to a little more than
+ * an untimed search. */
+#define MANS_STAGE_QUERY_PREP 0
+#define MANS_STAGE_SAMPLE 1
+#define MANS_STAGE_THRESHOLD 2
+#define MANS_STAGE_PASS 3
+#define MANS_STAGE_RERANK 4
+#define MANS_STAGE_MERGE 5
+#define MANS_STAGES 6
 int32_t mans_workspace_set_timing(mans_workspace *ws, int32_t enable);
 int32_t mans_workspace_stats(mans_workspace *ws, double *kernel_ms, int64_t *kernel_launches,
                              int64_t *total_launches);
+int32_t mans_workspace_stage_times(mans_workspace *ws, double *stage_ms, int64_t *stage_counts,
+                                   int32_t n_stages);
 
 /* ---- exact flat search -------------------------------------------------- */
 

@@ -43,6 +43,7 @@ SIGNATURES = {
     "mans_workspace_check": (C.c_int32, [_VP, _VP]),
     "mans_workspace_set_timing": (C.c_int32, [_VP, C.c_int32]),
     "mans_workspace_stats": (C.c_int32, [_VP, C.POINTER(C.c_double), _I64, _I64]),
+    "mans_workspace_stage_times": (C.c_int32, [_VP, C.POINTER(C.c_double), _I64, C.c_int32]),
     "mans_flat_search": (C.c_int32, [_VP, _VP, _VP, C.c_int64, C.c_int64, C.c_int32, C.c_int32,
                                      _VP, _VP, _VP]),
     "mans_flat_search_device": (C.c_int32, [_VP, _VP, _VP, _VP, C.c_int64, C.c_int32, C.c_int32,

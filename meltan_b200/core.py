@@ -290,8 +290,21 @@ class Workspace:
         check(lib().mans_workspace_last_path(self._h, C.byref(out)))
         return out.value
 
-    def set_timing(self, enable: bool) -> None:
-        check(lib().mans_workspace_set_timing(self._h, 1 if enable else 0))
+    def set_timing(self, enable: bool, stages: bool = False) -> None:
+        """Dominant-kernel timing (`enable`) and per-stage timing (`stages`)
+        of the searches made with this workspace."""
+        check(lib().mans_workspace_set_timing(self._h, (1 if enable else 0) | (2 if stages else 0)))
+
+    STAGES = ("query_prep", "sample", "threshold", "pass", "rerank", "merge")
+
+    def stage_times(self):
+        """{stage: (summed ms, timed launches)} since per-stage timing was
+        enabled or last read (waits for the timed work)."""
+        n = len(self.STAGES)
+        ms = (C.c_double * n)()
+        cnt = (C.c_int64 * n)()
+        check(lib().mans_workspace_stage_times(self._h, ms, cnt, n))
+        return {name: (ms[i], cnt[i]) for i, name in enumerate(self.STAGES)}
 
     def stats(self):
         """(summed dominant-kernel ms, timed launches, all library launches)."""

@@ -169,6 +169,10 @@ void destroy_workspace(mans_workspace* ws) {
     cudaEventDestroy(pr.first);
     cudaEventDestroy(pr.second);
   }
+  for (auto& pr : ws->stage_events) {
+    cudaEventDestroy(pr.first);
+    cudaEventDestroy(pr.second);
+  }
   if (ws->own_stream && ws->stream) cudaStreamDestroy(ws->stream);
   delete ws;
 }
@@ -193,6 +197,24 @@ cudaEvent_t timing_begin(mans_workspace* ws, cudaStream_t stream) {
 
 void timing_end(cudaEvent_t stop, cudaStream_t stream) {
   if (stop) cudaEventRecord(stop, stream);
+}
+
+cudaEvent_t stage_begin(mans_workspace* ws, cudaStream_t stream, int stage) {
+  if (!ws || !ws->stage_timing || ws->timing_hold > 0) return nullptr;
+  if (ws->stage_used == ws->stage_events.size()) {
+    cudaEvent_t a, b;
+    if (cudaEventCreate(&a) != cudaSuccess) return nullptr;
+    if (cudaEventCreate(&b) != cudaSuccess) {
+      cudaEventDestroy(a);
+      return nullptr;
+    }
+    ws->stage_events.emplace_back(a, b);
+    ws->stage_of.push_back(0);
+  }
+  const size_t i = ws->stage_used++;
+  ws->stage_of[i] = stage;
+  cudaEventRecord(ws->stage_events[i].first, stream);
+  return ws->stage_events[i].second;
 }
 
 int pow2_at_least(int v) {
@@ -304,11 +326,13 @@ int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace
   p.slot_counts = static_cast<int32_t*>(ws->slot_counts.ptr);
   p.err = static_cast<int*>(ws->err.ptr);
   int grid = static_cast<int>(std::min<int64_t>(nseg, ctx->num_sms));
+  cudaEvent_t st_stop = stage_begin(ws, stream, MANS_STAGE_PASS);
   cudaEvent_t ev_stop = timing_begin(ws, stream);
   cudaError_t e =
       launch_scan(qb, tile_rows == kTileRows ? corpus->map : corpus->map_small, p, grid, stream);
   if (e != cudaSuccess) return fail_cuda(e, "scan launch");
   timing_end(ev_stop, stream);
+  timing_end(st_stop, stream);
   ws->launches += (qn ? 1 : 0) + 2;
 
   MergeParams m{};
@@ -325,8 +349,10 @@ int32_t run_flat_search(mans_ctx* ctx, const mans_corpus* corpus, mans_workspace
   m.out_ids = d_out_ids;
   m.out_counts = d_out_counts;
   m.err = p.err;
+  st_stop = stage_begin(ws, stream, MANS_STAGE_MERGE);
   e = launch_merge(m, stream);
   if (e != cudaSuccess) return fail_cuda(e, "merge launch");
+  timing_end(st_stop, stream);
   return MANS_OK;
 }
 
@@ -657,9 +683,37 @@ int32_t mans_workspace_destroy(mans_workspace* ws) {
 
 int32_t mans_workspace_set_timing(mans_workspace* ws, int32_t enable) {
   if (!ws) return fail(MANS_ERR_INVALID, "workspace is null");
-  ws->timing = enable != 0;
+  ws->timing = (enable & 1) != 0;
+  ws->stage_timing = (enable & 2) != 0;
   ws->events_used = 0;
+  ws->stage_used = 0;
   ws->launches = 0;
+  return MANS_OK;
+}
+
+int32_t mans_workspace_stage_times(mans_workspace* ws, double* stage_ms, int64_t* stage_counts,
+                                   int32_t n_stages) {
+  if (!ws) return fail(MANS_ERR_INVALID, "workspace is null");
+  if (n_stages < 0 || (n_stages > 0 && (!stage_ms || !stage_counts)))
+    return fail(MANS_ERR_INVALID, "bad stage arrays");
+  DeviceGuard g(ws->ctx->device);
+  for (int32_t s = 0; s < n_stages; ++s) {
+    stage_ms[s] = 0.0;
+    stage_counts[s] = 0;
+  }
+  for (size_t i = 0; i < ws->stage_used; ++i) {
+    float ms = 0.0f;
+    cudaError_t e = cudaEventSynchronize(ws->stage_events[i].second);
+    if (e == cudaSuccess)
+      e = cudaEventElapsedTime(&ms, ws->stage_events[i].first, ws->stage_events[i].second);
+    if (e != cudaSuccess) return fail_cuda(e, "stage timing");
+    const int s = ws->stage_of[i];
+    if (s >= 0 && s < n_stages) {
+      stage_ms[s] += ms;
+      ++stage_counts[s];
+    }
+  }
+  ws->stage_used = 0;
   return MANS_OK;
 }
 
@@ -793,8 +847,10 @@ int32_t mans_topk_merge_device(mans_ctx* ctx, mans_workspace* ws, const float* d
   m.out_ids = d_out_ids;
   m.out_counts = d_out_counts;
   m.err = static_cast<int*>(ws->err.ptr);
+  cudaEvent_t st_stop = stage_begin(ws, st, MANS_STAGE_MERGE);
   cudaError_t e = launch_merge(m, st);
   if (e != cudaSuccess) return fail_cuda(e, "merge launch");
+  timing_end(st_stop, st);
   ws->launches += 1;
   return MANS_OK;
 }

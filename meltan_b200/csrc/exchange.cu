@@ -153,6 +153,7 @@ int32_t mans_exchange_allgather(mans_exchange* ex, mans_workspace* ws, const int
   }
   const uint32_t epoch = ++ex->epoch;
   const int parity = static_cast<int>(epoch & 1u);
+  cudaEvent_t st_stop = stage_begin(ws, st, MANS_STAGE_MERGE);
   publish_kernel<<<ex->world, 256, 0, st>>>(ex->d_peer, ex->rank, ex->world, ex->stride, d_block,
                                            words, parity, epoch);
   cudaError_t e = cudaGetLastError();
@@ -181,6 +182,7 @@ int32_t mans_exchange_allgather(mans_exchange* ex, mans_workspace* ws, const int
   m.empty_on_error = true;  // a peer that never published: empty results, not a partial merge
   e = launch_merge(m, st);
   if (e != cudaSuccess) return fail_cuda(e, "exchange merge launch");
+  timing_end(st_stop, st);
   ws->launches += 2;
   return MANS_OK;
 }

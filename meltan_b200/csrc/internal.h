@@ -56,6 +56,8 @@ struct mans_ctx {
   // cooperative launches are available (the one-launch IVF-flat search)
   bool coop_launch = false;
   bool probe_configured = false;  // that kernel's shared-memory limit is set
+  bool tc_configured = false;     // the tensor-core path's kernel attributes are set
+  int tc_pairs = -1;              // CTA pairs of the pair pass resident at once (-1: not asked)
   // programmatic dependent launch between the tensor-core path's kernels
   // (cleared if the runtime refuses it)
   bool pdl = true;
@@ -89,6 +91,7 @@ struct mans_corpus {
   float* tc_stats = nullptr;  // n x 4: |r'|, |r' - bf16(r')|, |bf16(r')|, |r| rounded down
   mans::TcCorpusStats tc_stats_host{};
   CUtensorMap tc_map;
+  CUtensorMap tc_map_half;  // the same rows in 128-row boxes (one CTA of a pair)
   // signed 8-bit codes (Int8CodeBuffer quantisation), built on first use
   bool tc8_ready = false;
   void* tc8_rows = nullptr;  // n x tc8_ld int8
@@ -148,6 +151,12 @@ struct mans_workspace {
   int timing_hold = 0;  // > 0 while an inner step (e.g. a centroid scan) runs untimed
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> events;
   size_t events_used = 0;
+  // optional per-stage timing (mans_workspace_set_timing bit 1): CUDA events
+  // around each stage of a search, summed per stage by mans_workspace_stage_times
+  bool stage_timing = false;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> stage_events;
+  std::vector<int> stage_of;
+  size_t stage_used = 0;
   int64_t launches = 0;  // library kernels enqueued through this workspace
   int last_path = 0;     // path of the last flat search: 0 scan, 1 bf16 tensor, 2 int8 tensor
   int32_t* tc_fallbacks = nullptr;  // device counter of exact re-scans (last tc call)
@@ -182,6 +191,10 @@ struct TimingHold {
   ~TimingHold() { --ws->timing_hold; }
 };
 void timing_end(cudaEvent_t stop, cudaStream_t stream);
+// Records a start event before stage `stage` (MANS_STAGE_*) when per-stage
+// timing is on and no inner step holds the timing; returns the stop event to
+// record after the stage with timing_end (or null).
+cudaEvent_t stage_begin(mans_workspace* ws, cudaStream_t stream, int stage);
 // Copies rows (host or device, n x dim with a row pitch of src_ld elements,
 // 0 = dim) into a new corpus object (norms on the device).
 int32_t corpus_upload(mans_ctx* ctx, const float* rows, int64_t n, int64_t dim, uint32_t id_offset,

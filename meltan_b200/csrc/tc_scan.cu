@@ -60,8 +60,7 @@ constexpr int kEpiWarps = 16;
 constexpr int kTmemCols = 512;          // two 256-column accumulators
 constexpr size_t kResidentMax = 96 * 1024;
 constexpr size_t kPipeBudget = 196 * 1024;
-constexpr int kRerankThreads = 256;
-constexpr int kMaxRerank = 2048;  // exact re-score list per query
+constexpr int kRerankThreads = 128;
 constexpr int kRtSlots = 4;       // row-term ring depth (tiles)
 
 // Shared scratch of block_kth_smallest.
@@ -95,12 +94,14 @@ __host__ __device__ inline int tc_kblocks(int dim, bool i8) {
   return i8 ? (dim + 127) / 128 : (dim + kBK - 1) / kBK;
 }
 
-__host__ __device__ inline TcLayout tc_layout(int nk, int stream_queries) {
+// With `pair` (a CTA pair sharing M = 256 MMAs) a stage holds this CTA's
+// half of the row tile, 128 rows, so the same budget keeps twice the stages.
+__host__ __device__ inline TcLayout tc_layout(int nk, int stream_queries, bool pair = false) {
   TcLayout L;
   L.nk = nk;
   L.resident = !stream_queries && static_cast<size_t>(L.nk) * kQBytes <= kResidentMax;
   L.a_bytes = L.resident ? static_cast<size_t>(L.nk) * kQBytes : 0;
-  L.stage_bytes = kRBytes + (L.resident ? 0 : kQBytes);
+  L.stage_bytes = (pair ? kRBytes / 2 : kRBytes) + (L.resident ? 0 : kQBytes);
   size_t st = (kPipeBudget - L.a_bytes) / L.stage_bytes;
   L.stages = static_cast<int>(st > 8 ? 8 : st);
   L.rt_off = L.a_bytes + static_cast<size_t>(L.stages) * L.stage_bytes;  // 1 KiB aligned
@@ -174,6 +175,72 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ---- CTA pairs (cta_group::2): two CTAs of a cluster share one MMA --------
+// The leader (cluster rank 0) issues M = 256 MMAs whose A rows 0-127 and B
+// rows 0-127 come from its own shared memory and rows 128-255 from its
+// peer's, at the same offsets; each CTA's TMEM receives its own 128 A rows x
+// all N columns.  Every tcgen05 instruction of such a kernel uses
+// cta_group::2.  Loads carry no multicast: each CTA copies its own half.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+// shared::cluster address of the variable at `local`'s offset in CTA `rank`
+__device__ __forceinline__ uint32_t map_to_rank(const void* local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+  return r;
+}
+// arrive on an mbarrier given by its shared::cluster address (any CTA of the cluster)
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+// 2-D TMA load into this CTA's shared memory completing on an mbarrier of
+// either CTA of the pair (shared::cluster address)
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, int32_t x,
+                                                 int32_t y, uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, int ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols));
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::);
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, int ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+// D[tmem of both CTAs] (+)= A[smem, both] * B[smem, both]^T, kind::f16, M = 256
+__device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+// arrive on the mbarrier at `bar`'s offset in every CTA of `cta_mask` once
+// every pair MMA previously issued by this thread completed
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
 }
 
 // Shared-memory matrix descriptor of a K-major operand with 128-byte swizzle:
@@ -371,6 +438,187 @@ __device__ float block_kth_smallest(Get get, int64_t n, int k, KthSmem& S, int t
 }
 
 
+// 16-byte global -> shared copy without a register round trip (cp.async);
+// cp_async_wait_all waits for every copy the thread issued.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+}
+
+// Ascending sort of 32 floats, one per lane, by shuffles (bitonic network).
+__device__ __forceinline__ float warp_sort32_f(float x, int lane) {
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      const float y = __shfl_xor_sync(0xFFFFFFFFu, x, stride);
+      const bool up = (lane & size) == 0;
+      const bool lower = (lane & stride) == 0;
+      x = (lower == up) ? fminf(x, y) : fmaxf(x, y);
+    }
+  }
+  return x;
+}
+
+// k-th smallest of n finite values (counting repeats) by one warp, with the
+// levels of block_kth_smallest at warp scale: the values in play (finite, and
+// in the selected bin of every earlier level) are reduced to their min and
+// max, binned into 256 linear bins over [min, max] (distances of one search
+// spread over the bins, so the shared atomics rarely collide), and the bin of
+// the k-th value becomes the set in play of the next level.  At most 32
+// values in play are gathered and sorted by shuffles.  Equal min and max end
+// the search; after four levels without isolating 32 values (extreme dynamic
+// range only) the largest value in play bounds the k-th from above, which the
+// callers accept as block_kth_smallest's.  Non-finite values take no part;
+// with fewer than k finite values the result is +inf.  `hist` is the warp's
+// own 256 words of shared memory; no block barrier.
+template <typename Get>
+__device__ float warp_kth_smallest(Get get, int64_t n, int k, uint32_t* hist, int lane) {
+  const float inf = __int_as_float(0x7F800000);
+  float lo_at[4], sc_at[4];
+  int sel_at[4];
+  uint32_t kk = static_cast<uint32_t>(k);
+  auto member = [&](float v, int level) {
+    if (!(fabsf(v) < inf)) return false;
+#pragma unroll
+    for (int l = 0; l < 4; ++l)
+      if (l < level && min(255, max(0, static_cast<int>((v - lo_at[l]) * sc_at[l]))) != sel_at[l])
+        return false;
+    return true;
+  };
+#pragma unroll
+  for (int level = 0; level < 4; ++level) {
+    float lo = inf, hi = -inf;
+    uint32_t cnt = 0;
+    for (int64_t i = lane; i < n; i += 32) {
+      const float v = get(i);
+      if (member(v, level)) {
+        lo = fminf(lo, v);
+        hi = fmaxf(hi, v);
+        ++cnt;
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      lo = fminf(lo, __shfl_xor_sync(0xFFFFFFFFu, lo, o));
+      hi = fmaxf(hi, __shfl_xor_sync(0xFFFFFFFFu, hi, o));
+      cnt += __shfl_xor_sync(0xFFFFFFFFu, cnt, o);
+    }
+    if (cnt < kk) return inf;  // (level 0 only: deeper levels hold >= kk)
+    if (!(hi > lo)) return lo;  // every value in play is equal
+    if (cnt <= 32) {
+      // gather the values in play (ballot compaction) and sort them
+      float* list = reinterpret_cast<float*>(hist);
+      uint32_t at = 0;
+      for (int64_t i0 = 0; i0 < n; i0 += 32) {
+        const int64_t i = i0 + lane;
+        const float v = i < n ? get(i) : inf;
+        const bool m = i < n && member(v, level);
+        const unsigned bal = __ballot_sync(0xFFFFFFFFu, m);
+        if (m) list[at + __popc(bal & ((1u << lane) - 1u))] = v;
+        at += __popc(bal);
+      }
+      __syncwarp();
+      const float x = warp_sort32_f(lane < static_cast<int>(cnt) ? list[lane] : inf, lane);
+      __syncwarp();
+      return __shfl_sync(0xFFFFFFFFu, x, static_cast<int>(kk) - 1);
+    }
+    if (level == 3) return hi;
+    const float scale = 255.0f / (hi - lo);
+#pragma unroll
+    for (int j = lane; j < 256; j += 32) hist[j] = 0u;
+    __syncwarp();
+    for (int64_t i = lane; i < n; i += 32) {
+      const float v = get(i);
+      if (member(v, level))
+        atomicAdd(&hist[min(255, max(0, static_cast<int>((v - lo) * scale)))], 1u);
+    }
+    __syncwarp();
+    // bin of the kk-th value: lane l sums bins 8l..8l+7, an inclusive scan
+    // over the lanes finds the crossing, its owner walks its bins
+    uint32_t c[8], s = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      c[j] = hist[lane * 8 + j];
+      s += c[j];
+    }
+    uint32_t inc = s;
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+      if (lane >= o) inc += y;
+    }
+    const uint32_t excl = inc - s;
+    const bool mine = excl < kk && kk <= inc;
+    const int owner = __ffs(__ballot_sync(0xFFFFFFFFu, mine)) - 1;
+    int d = 0;
+    uint32_t before = excl;
+    if (mine) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (before + c[j] >= kk) {
+          d = lane * 8 + j;
+          break;
+        }
+        before += c[j];
+      }
+    }
+    d = __shfl_sync(0xFFFFFFFFu, d, owner);
+    before = __shfl_sync(0xFFFFFFFFu, before, owner);
+    lo_at[level] = lo;
+    sc_at[level] = scale;
+    sel_at[level] = d;
+    kk -= before;
+    __syncwarp();
+  }
+  return inf;  // not reached
+}
+
+// k-th smallest of n values (counting repeats) by one warp for k <= K:
+// every lane keeps the K smallest finite values of its strided share sorted
+// in registers (a value below the lane's largest kept one is inserted by a
+// compare-exchange chain), then k rounds of a warp-wide minimum over the
+// lanes' smallest kept values pop one value each (the lowest lane holding the
+// minimum pops); the k-th popped value is the answer.  A lane contributes at
+// most k of the k smallest, so K kept values per lane suffice.  Exact, with
+// no shared memory and no barrier; non-finite values take no part (+inf when
+// fewer than k are finite), as in warp_kth_smallest.
+constexpr int kSmallK = 16;  // k up to which the register selection is used
+
+template <int K, typename Get>
+__device__ float warp_kth_small(Get get, int64_t n, int k, int lane) {
+  const float inf = __int_as_float(0x7F800000);
+  float a[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) a[j] = inf;
+  for (int64_t i = lane; i < n; i += 32) {
+    float x = get(i);
+    if (!(fabsf(x) < inf) || !(x < a[K - 1])) continue;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      const float lo = fminf(a[j], x);
+      x = fmaxf(a[j], x);
+      a[j] = lo;
+    }
+  }
+  float res = inf;
+  for (int r = 0; r < k; ++r) {
+    float m = a[0];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fminf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    if (!(m < inf)) return inf;  // fewer than k finite values (warp-uniform)
+    const int w = __ffs(__ballot_sync(0xFFFFFFFFu, a[0] == m)) - 1;
+    if (lane == w) {
+#pragma unroll
+      for (int j = 0; j < K - 1; ++j) a[j] = a[j + 1];
+      a[K - 1] = inf;
+    }
+    res = m;
+  }
+  return res;
+}
+
 // Filter threshold of one query from the k-th smallest sampled value `kth`
 // (+inf when the sample holds fewer than k values): t = kth + 2 eps (rounded
 // up) and the score-domain constant c.  With d~ = alpha + beta - gamma v the
@@ -488,12 +736,19 @@ enum TcMode : int { kDense = 0, kFilterPlain = 1, kFilterBias = 2 };
 
 // I8: signed 8-bit codes with a per-row factor (TcParams::row_w) instead of
 // bf16 rows; the s32 accumulator is converted and scaled in the epilogue.
-template <int MODE, bool I8, bool FUSED = false>
+// PAIR: the filtered pass as CTA pairs (clusters of two): the pair holds two
+// query blocks (256 queries, one per CTA, resident), each CTA streams its
+// half of every 256-row tile (`map_r` with 128-row boxes), the leader issues
+// the M = 256 MMAs, and each CTA's epilogue reads its own queries' scores
+// for all 256 rows.  Each CTA then feeds half the row bytes per MMA, so its
+// stage ring covers twice the load latency.  Requires `groups` > 0.
+template <int MODE, bool I8, bool FUSED = false, bool PAIR = false>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_scan_kernel(const __grid_constant__ CUtensorMap map_q,
                    const __grid_constant__ CUtensorMap map_r, const TcParams p) {
+  static_assert(!PAIR || (!I8 && !FUSED && MODE != kDense), "pairs run the bf16 filtered pass");
   extern __shared__ uint8_t smem_raw[];
-  const TcLayout L = tc_layout(tc_kblocks(p.dim, I8), p.stream_queries);
+  const TcLayout L = tc_layout(tc_kblocks(p.dim, I8), p.stream_queries, PAIR);
   uint8_t* base =
       reinterpret_cast<uint8_t*>((reinterpret_cast<size_t>(smem_raw) + 1023) / 1024 * 1024);
   uint8_t* qres = base;                  // resident query block (nk x 16 KiB)
@@ -528,8 +783,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // the same rows in step, so each row tile comes from HBM once and from L2
   // for the others.  Otherwise blocks take contiguous query-block-major
   // ranges of (query block, row tile) units.
+  // Pairs: pair c / 2 owns query blocks 2 s and 2 s + 1 (s = pair % pair
+  // superblocks; CTA rank r takes block 2 s + r, which may lie past the last
+  // block: zero queries, no results) and the row tiles of group pair / s.
+  const uint32_t crank = PAIR ? cluster_rank() : 0u;
   int64_t u_begin, u_end;
-  if (p.groups > 0) {
+  if (PAIR) {
+    const int64_t qsb = (p.qblocks + 1) / 2;
+    const int64_t pr = blockIdx.x / 2;
+    const int64_t qb = 2 * (pr % qsb) + crank;
+    const int64_t g = pr / qsb;
+    u_begin = qb * rtiles + rtiles * g / p.groups;
+    u_end = qb * rtiles + rtiles * (g + 1) / p.groups;
+  } else if (p.groups > 0) {
     const int64_t qb = blockIdx.x % p.qblocks;
     const int64_t g = blockIdx.x / p.qblocks;
     u_begin = qb * rtiles + rtiles * g / p.groups;
@@ -554,7 +820,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], kEpiWarps);
+      // pairs: both CTAs' epilogue warps release the leader's accumulator
+      mbar_init(&acc_empty[b], PAIR ? 2 * kEpiWarps : kEpiWarps);
     }
     mbar_init(a_full, 1);
     mbar_init(a_empty, 1);
@@ -567,8 +834,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
   }
   if (tid == 64) {
     tma_prefetch_desc(&map_q);
@@ -576,6 +848,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  // pairs: the peer's barriers are initialised before any copy or arrival
+  // reaches them
+  if (PAIR) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   // launched while the query prep (or the sample pass) may still run: the
@@ -599,9 +874,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (L.resident && qb != cur_qb) {
           // refill the resident query block once the MMAs on the old one finished
           if (cur_qb >= 0 && !tc_wait(a_empty, (a_round - 1) & 1u, p.err, abort)) break;
-          mbar_arrive_expect_tx(a_full, static_cast<uint32_t>(nk * kQBytes));
-          for (int kb = 0; kb < nk; ++kb)
-            tma_load_2d(qres + kb * kQBytes, &map_q, kb * kKElems, static_cast<int32_t>(qb * kQM), a_full);
+          if (PAIR) {
+            // both halves complete on the leader's barrier (loaded once: pairs
+            // keep their query blocks for the whole pass)
+            if (crank == 0) mbar_arrive_expect_tx(a_full, static_cast<uint32_t>(2 * nk * kQBytes));
+            const uint32_t lead = map_to_rank(a_full, 0);
+            for (int kb = 0; kb < nk; ++kb)
+              tma_load_2d_pair(qres + kb * kQBytes, &map_q, kb * kKElems,
+                               static_cast<int32_t>(qb * kQM), lead);
+          } else {
+            mbar_arrive_expect_tx(a_full, static_cast<uint32_t>(nk * kQBytes));
+            for (int kb = 0; kb < nk; ++kb)
+              tma_load_2d(qres + kb * kQBytes, &map_q, kb * kKElems, static_cast<int32_t>(qb * kQM),
+                          a_full);
+          }
           a_pending = true;
           cur_qb = qb;
           ++a_round;
@@ -629,10 +915,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             break;
           }
           uint8_t* st = stages + stage * L.stage_bytes;
-          mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(L.stage_bytes));
-          tma_load_2d(st, &map_r, kb * kKElems, y, &full[stage]);
-          if (!L.resident)
-            tma_load_2d(st + kRBytes, &map_q, kb * kKElems, static_cast<int32_t>(qb * kQM), &full[stage]);
+          if (PAIR) {
+            // this CTA's 128 rows of the tile, completing on the leader's barrier
+            if (crank == 0)
+              mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(2 * L.stage_bytes));
+            tma_load_2d_pair(st, &map_r, kb * kKElems, y + static_cast<int32_t>(crank) * (kRN / 2),
+                             map_to_rank(&full[stage], 0));
+          } else {
+            mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(L.stage_bytes));
+            tma_load_2d(st, &map_r, kb * kKElems, y, &full[stage]);
+            if (!L.resident)
+              tma_load_2d(st + kRBytes, &map_q, kb * kKElems, static_cast<int32_t>(qb * kQM),
+                          &full[stage]);
+          }
           ++issued;
           if (++stage == L.stages) {
             stage = 0;
@@ -642,7 +937,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (!ok) break;
       }
       // after an abort, wait (bounded) for the copies still in flight
-      if (*abort) {
+      if (PAIR && *abort) {
+        // a pair's stage and query copies complete on the leader's barriers,
+        // which this CTA cannot wait on: give them a bounded moment to land
+        const unsigned long long t0 = global_ns();
+        while (global_ns() - t0 < 200000ull) {
+        }
+      } else if (*abort) {
         for (int64_t i = issued > L.stages ? issued - L.stages : 0; i < issued; ++i)
           mbar_wait_bounded(&full[i % L.stages], static_cast<uint32_t>((i / L.stages) & 1), nullptr);
         if (a_pending) mbar_wait_bounded(a_full, (a_round - 1) & 1u, nullptr);
@@ -652,9 +953,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
-      const uint32_t idesc = I8 ? idesc_i8(kQM, kRN) : idesc_bf16(kQM, kRN);
+    if (lane == 0 && crank == 0) {
+      // ---------------- MMA issuer (a pair's leader alone) ----------------
+      const uint32_t idesc =
+          I8 ? idesc_i8(kQM, kRN) : idesc_bf16(PAIR ? 2 * kQM : kQM, kRN);
       int stage = 0;
       uint32_t phase = 0;
       int64_t cur_qb = -1;
@@ -664,7 +966,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int64_t u = unit_of(v);
         const int64_t qb = u / rtiles;
         if (L.resident && qb != cur_qb) {
-          if (cur_qb >= 0) tc_commit(a_empty);  // old query block free once prior MMAs finish
+          // old query block free once prior MMAs finish (pairs keep theirs)
+          if constexpr (!PAIR) {
+            if (cur_qb >= 0) tc_commit(a_empty);
+          }
           if (!tc_wait(a_full, a_round & 1u, p.err, abort)) break;
           cur_qb = qb;
           ++a_round;
@@ -688,22 +993,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           // four MMAs of 32 bytes of K per 128-byte stage (16 bf16 / 32 int8)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            if (I8)
+            if constexpr (PAIR)
+              tc_mma_pair(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+            else if constexpr (I8)
               tc_mma_i8(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
             else
               tc_mma(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
           }
-          tc_commit(&empty[stage]);  // frees the smem stage once these MMAs finish
+          // frees the smem stage (of both CTAs of a pair) once these MMAs finish
+          if constexpr (PAIR)
+            tc_commit_pair(&empty[stage], 3);
+          else
+            tc_commit(&empty[stage]);
           if (++stage == L.stages) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit(&acc_full[b]);  // accumulator ready for the epilogue
+        // accumulator ready for the epilogue (of both CTAs of a pair)
+        if constexpr (PAIR)
+          tc_commit_pair(&acc_full[b], 3);
+        else
+          tc_commit(&acc_full[b]);
       }
       // every MMA issued by this thread has completed once `drain` flips
-      tc_commit(drain);
+      if constexpr (PAIR)
+        tc_commit_pair(drain, 1);
+      else
+        tc_commit(drain);
       mbar_wait_bounded(drain, 0, nullptr);
     }
   } else if (warp >= 4) {
@@ -960,7 +1278,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&acc_empty[b]);
+        if (PAIR)
+          mbar_arrive_cluster(map_to_rank(&acc_empty[b], 0));  // the leader issues the MMAs
+        else
+          mbar_arrive(&acc_empty[b]);
         if (row_terms) mbar_arrive(&rt_empty[rslot]);
       }
     }
@@ -975,8 +1296,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  // pairs: neither CTA leaves (or frees TMEM) while the other may still
+  // signal its barriers or the leader's MMAs read its shared memory
+  if (PAIR) cluster_sync_all();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+  if (warp == 1) {
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem, kTmemCols);
+    else
+      tmem_dealloc(tmem, kTmemCols);
+  }
 }
 
 // fp32 rows -> bf16 rows (round to nearest even), one warp per row.  With
@@ -1096,8 +1425,11 @@ struct TcQueryParams {
 // s_q, quantised in double as BoundedExactScan.swift:52-64 does), the exact
 // squared norm in index order, the affine terms and the certified bound eps_q
 // of |d~ - d|.
+constexpr int kPrepWarps = 8;   // queries per block
+constexpr int kPrepSq = 512;    // squares per warp buffered before lane 0 sums them
+
 template <bool I8>
-__global__ void tc_query_prep_kernel(const TcQueryParams p) {
+__global__ void __launch_bounds__(kPrepWarps * 32) tc_query_prep_kernel(const TcQueryParams p) {
   pdl_trigger();  // the pass may launch and set up while the queries are prepared
   const int64_t q = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -1124,21 +1456,50 @@ __global__ void tc_query_prep_kernel(const TcQueryParams p) {
     qs = mx > 0.0f ? static_cast<double>(mx) / 127.0 : 1.0;
   }
   double nq2 = 0.0, nres = 0.0, nt = 0.0;
-  // |q|^2 of the exact path: sequential fp32 sum in index order.  Each lane
-  // squares its element of the 32-wide chunk and the warp adds the chunk's
-  // squares lane by lane through shuffles, so every lane carries the same
-  // running sum without a serial pass over memory.  Lanes past `dim` add
-  // +0, which leaves a sum of non-negative squares (never -0) unchanged.
+  // |q|^2 of the exact path: sequential fp32 sum in index order.  The lanes
+  // square their elements into the warp's shared slice (up to 512 at a time)
+  // and lane 0 adds them in index order: a short loop instead of a long
+  // unrolled shuffle chain, which matters for a kernel whose run time is its
+  // latency.  Lanes past `dim` store +0, which leaves a sum of non-negative
+  // squares (never -0) unchanged.
+  __shared__ __align__(16) float sqbuf[kPrepWarps][kPrepSq];
+  float* sb = sqbuf[threadIdx.x >> 5];
+  int filled = 0;
   float acc = 0.0f;
-  // read-only loads (no aliasing with the stores below), four in flight
+  auto drain = [&]() {
+    __syncwarp();
+    if (lane == 0) {
 #pragma unroll 4
-  for (int c0 = 0; c0 < p.ld16; c0 += 32) {
-    const int c = c0 + lane;
-    const float x = c < p.dim ? __ldg(v + c) : 0.0f;
-    if (c0 < p.dim) {
-      const float sq = __fmul_rn(x, x);
+      for (int j = 0; j < filled; j += 4) {
+        const float4 t = *reinterpret_cast<const float4*>(sb + j);
+        acc = __fadd_rn(acc, t.x);
+        acc = __fadd_rn(acc, t.y);
+        acc = __fadd_rn(acc, t.z);
+        acc = __fadd_rn(acc, t.w);
+      }
+    }
+    __syncwarp();
+    filled = 0;
+  };
+  // Up to 384 columns (the usual widths) the query's elements are loaded in
+  // one round trip and held in registers; wider queries load 32 at a time.
+  constexpr int kHeld = 12;
+  float held[kHeld];
+  const bool in_regs = p.ld16 <= 32 * kHeld;
+  if (in_regs) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) acc = __fadd_rn(acc, __shfl_sync(0xFFFFFFFFu, sq, j));
+    for (int j = 0; j < kHeld; ++j) {
+      const int c = 32 * j + lane;
+      held[j] = c < p.dim ? __ldg(v + c) : 0.0f;
+    }
+  }
+  // one 32-column chunk: the exact |q|^2 steps, the rounded copy, the sums
+  auto column = [&](int c0, float x) {
+    const int c = c0 + lane;
+    if (c0 < p.dim) {
+      sb[filled + lane] = __fmul_rn(x, x);  // x = 0 past dim
+      filled += 32;
+      if (filled == kPrepSq) drain();
     }
     if (c < p.ld16) {
       double xb;
@@ -1158,7 +1519,18 @@ __global__ void tc_query_prep_kernel(const TcQueryParams p) {
       nres += (xx - xb) * (xx - xb);
       nt += xb * xb;
     }
+  };
+  if (in_regs) {
+#pragma unroll
+    for (int j = 0; j < kHeld; ++j)
+      if (32 * j < p.ld16) column(32 * j, held[j]);
+  } else {
+    // read-only loads (no aliasing with the stores), four in flight
+#pragma unroll 4
+    for (int c0 = 0; c0 < p.ld16; c0 += 32)
+      column(c0, c0 + lane < p.dim ? __ldg(v + c0 + lane) : 0.0f);
   }
+  if (filled > 0) drain();
   for (int o = 16; o > 0; o >>= 1) {
     nq2 += __shfl_xor_sync(0xFFFFFFFFu, nq2, o);
     nres += __shfl_xor_sync(0xFFFFFFFFu, nres, o);
@@ -1211,6 +1583,42 @@ __global__ void __launch_bounds__(kThresholdThreads) tc_threshold_kernel(
     threshold_from_kth(kth, eps[q], alpha[q], gamma[q], scale[q], thr_out + q, c_out + q);
 }
 
+// The same thresholds for batches of more queries than SMs, one warp per
+// query: the query's sample values (at most kThrWarpMax) are staged in the
+// warp's shared slice and its k-th smallest taken by warp_kth_smallest, so
+// the whole batch fits in one wave of small blocks with no block barrier.
+constexpr int kThrWarps = 4;
+constexpr int kThrWarpMax = 2048;
+
+__global__ void __launch_bounds__(kThrWarps * 32) tc_threshold_warp_kernel(
+    const float* __restrict__ dense, int64_t ld, int64_t rows, int32_t k, int64_t nq,
+    const float* __restrict__ eps, const float* __restrict__ alpha,
+    const float* __restrict__ gamma, const float* __restrict__ scale,
+    float* __restrict__ thr_out, float* __restrict__ c_out) {
+  __shared__ uint32_t hist[kThrWarps][256];
+  __shared__ __align__(16) float vals[kThrWarps][kThrWarpMax];
+  pdl_trigger();
+  pdl_wait();  // the sample pass's values
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * kThrWarps + w;
+  if (q >= nq) return;
+  // `ld` is a multiple of 4 and the sample block 256-byte aligned: 16-byte
+  // asynchronous copies, all in flight at once (one memory round trip)
+  const float* row = dense + q * ld;
+  float* sv = vals[w];
+  for (int64_t i = lane; i < (rows + 3) / 4; i += 32) cp_async16(sv + 4 * i, row + 4 * i);
+  cp_async_wait_all();
+  __syncwarp();
+  float kth = __int_as_float(0x7F800000);
+  if (rows >= k) {
+    auto get = [&](int64_t i) { return sv[i]; };
+    kth = k <= kSmallK ? warp_kth_small<kSmallK>(get, rows, k, lane)
+                       : warp_kth_smallest(get, rows, k, hist[w], lane);
+  }
+  if (lane == 0)
+    threshold_from_kth(kth, eps[q], alpha[q], gamma[q], scale[q], thr_out + q, c_out + q);
+}
+
 struct RerankParams {
   const uint64_t* cand;
   const int32_t* cand_count;
@@ -1234,6 +1642,7 @@ struct RerankParams {
   int32_t* out_counts;
   int32_t* fallbacks;  // count of queries re-scanned exactly
   int32_t region;      // bytes of the shared staging region
+  int32_t max_band;    // entries of the band buffer (>= kSortN, a power of two)
 };
 
 // Exact distance of one corpus row in the reference order.
@@ -1260,24 +1669,23 @@ __device__ __forceinline__ float exact_distance(const RerankParams& p, const flo
   return finalize_distance(p.metric, acc, qn, p.metric == kIP ? 0.0f : __ldg(p.norms + row));
 }
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst)), "l"(src)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
-}
 
 // Dynamic shared memory of tc_rerank_kernel: the query (dim floats, 16-byte
-// rounded), then one region that first holds the candidate keys and later the
-// staged corpus rows of the exact re-score.
-// The region is large (64 KB) while the query blocks fit on the SMs in one
-// wave, small (16 KB, more blocks per SM) for large batches.
+// rounded), the band buffer (max_band 64-bit entries: first the band's row
+// ids, then their exact keys; the exact fallback's running top-k), then one
+// region that first holds the candidate keys and later the staged corpus rows
+// of the exact re-score.
+// The region is large (64 KB) and the band buffer 2048 entries while the
+// queries fit on the SMs in one wave; for large batches both shrink (16 KB,
+// 1024 entries) so that eight blocks share an SM and the batch runs in one
+// wave too.  A band wider than the buffer takes the exact re-scan.
 inline int rerank_region_bytes(int64_t nq, int num_sms) {
   return nq <= num_sms ? 64 * 1024 : 16 * 1024;
 }
-inline size_t rerank_smem_bytes(int64_t dim, int region) {
-  return static_cast<size_t>((dim + 3) / 4 * 4) * sizeof(float) + region;
+inline int rerank_max_band(int64_t nq, int num_sms) { return nq <= num_sms ? 2048 : 1024; }
+inline size_t rerank_smem_bytes(int64_t dim, int max_band, int region) {
+  return static_cast<size_t>((dim + 3) / 4 * 4) * sizeof(float) +
+         static_cast<size_t>(max_band) * sizeof(uint64_t) + region;
 }
 
 // Exact distance of a row staged in shared memory, in the reference order;
@@ -1305,18 +1713,19 @@ __device__ __forceinline__ float exact_distance_smem(const RerankParams& p, cons
 //          is the exact top-k of the corpus, provided the filter kept every
 //          row up to band (band <= thr) and the list did not overflow.
 // Otherwise the query is re-scanned exactly over all rows by this block.
-__global__ void __launch_bounds__(kRerankThreads) tc_rerank_kernel(const RerankParams p) {
+__global__ void __launch_bounds__(kRerankThreads, 8) tc_rerank_kernel(const RerankParams p) {
   extern __shared__ __align__(16) unsigned char rsm[];
   float* qsm = reinterpret_cast<float*>(rsm);
-  unsigned char* region = rsm + static_cast<size_t>((p.dim + 3) / 4 * 4) * sizeof(float);
+  // band row ids (phase 1), then the band's exact keys (phase 2)
+  uint64_t* ekeys = reinterpret_cast<uint64_t*>(rsm + static_cast<size_t>((p.dim + 3) / 4 * 4) *
+                                                          sizeof(float));
+  unsigned char* region = reinterpret_cast<unsigned char*>(ekeys + p.max_band);
   uint64_t* skeys = reinterpret_cast<uint64_t*>(region);  // candidate keys (phase 1)
   float* srows = reinterpret_cast<float*>(region);         // staged rows (phase 2)
-  __shared__ uint64_t ekeys[kMaxRerank];                    // exact keys of the band
+  __shared__ uint32_t hist[256];                            // k-th selection (warp 0)
   __shared__ uint64_t thr;
   __shared__ int qc, nb, fail_flag, nlist;
   __shared__ float band_sh;
-  __shared__ uint32_t list[kMaxRerank];
-  __shared__ KthSmem ks;
   const int tid = threadIdx.x;
   const int64_t q = blockIdx.x;
   pdl_wait();  // the pass's candidates
@@ -1334,19 +1743,25 @@ __global__ void __launch_bounds__(kRerankThreads) tc_rerank_kernel(const RerankP
   const uint64_t* cq = p.cand + q * p.cand_cap;
   const bool stage_keys = cnt * 8 <= p.region;
   if (stage_keys) {
-#pragma unroll 4
-    for (int i = tid; i < cnt; i += kRerankThreads) skeys[i] = __ldg(cq + i);
+    // pairs of keys by 16-byte asynchronous copies, all in flight at once
+    // (the list capacity is even and each list 16-byte aligned)
+    for (int i = tid; i < (cnt + 1) / 2; i += kRerankThreads) cp_async16(skeys + 2 * i, cq + 2 * i);
+    cp_async_wait_all();
   }
   const uint64_t* keys = stage_keys ? skeys : cq;
   __syncthreads();
   if (!fail_flag) {
-    const float tk = block_kth_smallest([&](int64_t i) { return key_distance(keys[i]); }, cnt,
-                                        p.k, ks, tid, kRerankThreads, [] { __syncthreads(); });
-    if (tid == 0) {
-      float band = tk + 2.0f * e;
-      band = band + fabsf(band) * 1e-6f;
-      if (!(band <= thr_q)) fail_flag = 1;  // the filter did not cover the band
-      band_sh = band;
+    if (tid < 32) {
+      // the k-th smallest candidate distance, by warp 0 alone
+      auto get = [&](int64_t i) { return key_distance(keys[i]); };
+      const float tk = p.k <= kSmallK ? warp_kth_small<kSmallK>(get, cnt, p.k, tid)
+                                      : warp_kth_smallest(get, cnt, p.k, hist, tid);
+      if (tid == 0) {
+        float band = tk + 2.0f * e;
+        band = band + fabsf(band) * 1e-6f;
+        if (!(band <= thr_q)) fail_flag = 1;  // the filter did not cover the band
+        band_sh = band;
+      }
     }
     __syncthreads();
     if (!fail_flag) {
@@ -1355,41 +1770,47 @@ __global__ void __launch_bounds__(kRerankThreads) tc_rerank_kernel(const RerankP
         const uint64_t key = keys[i];
         if (key_distance(key) <= band) {
           const int pos = atomicAdd(&nlist, 1);
-          if (pos < kMaxRerank) list[pos] = key_id(key);
+          if (pos < p.max_band) ekeys[pos] = key_id(key);
         }
       }
       __syncthreads();
-      if (tid == 0 && nlist > kMaxRerank) fail_flag = 1;
+      if (tid == 0 && nlist > p.max_band) fail_flag = 1;
       __syncthreads();
     }
   }
   if (!fail_flag) {
     // exact re-score of the band: rows staged in shared memory by cp.async
-    // (all loads of a round in flight), one thread per row
+    // (all loads of a round in flight), one thread per row.  Entry i of the
+    // band buffer holds row id i until thread i - b of its round replaces it
+    // by the exact key, after every read of the round's ids.
     const int m = nlist;
     const int pitch = (p.dim + 3) / 4 * 4 + 4;  // floats; +4 spreads rows over the banks
     const int per_round = max(1, min(kRerankThreads, p.region / (pitch * 4)));
     const int chunks = (p.dim + 3) / 4;  // 16-byte pieces of one row
     for (int b = 0; b < m; b += per_round) {
       const int rn = min(per_round, m - b);
+      const int64_t my_row = tid < rn ? static_cast<int64_t>(ekeys[b + tid]) : 0;
       // the row's |r|^2, loaded while its row is in flight
-      const float vn = (tid < rn && p.metric != kIP) ? __ldg(p.norms + list[b + tid]) : 0.0f;
+      const float vn = (tid < rn && p.metric != kIP) ? __ldg(p.norms + my_row) : 0.0f;
       for (int t = tid; t < rn * chunks; t += kRerankThreads) {
         const int r = t / chunks, c = t - r * chunks;
-        cp_async16(srows + r * pitch + 4 * c, p.rows + static_cast<int64_t>(list[b + r]) * p.ld + 4 * c);
+        cp_async16(srows + r * pitch + 4 * c,
+                   p.rows + static_cast<int64_t>(ekeys[b + r]) * p.ld + 4 * c);
       }
       cp_async_wait_all();
       __syncthreads();
-      if (tid < rn) {
-        const int64_t row = list[b + tid];
+      if (tid < rn)
         ekeys[b + tid] = make_key(exact_distance_smem(p, qsm, qn, srows + tid * pitch, vn),
-                                  static_cast<uint32_t>(row + p.id_offset));
-      }
+                                  static_cast<uint32_t>(my_row + p.id_offset));
       __syncthreads();
     }
     if (m <= 32) {
       // the usual band (about k rows): one warp sorts it by shuffles
-      if (tid < 32) ekeys[tid] = warp_sort32(tid < m ? ekeys[tid] : kKeyMax, tid);
+      if (tid < 32) {
+        const uint64_t x = warp_sort32(tid < m ? ekeys[tid] : kKeyMax, tid);
+        __syncwarp();
+        ekeys[tid] = x;
+      }
       __syncthreads();
     } else {
       int mp = 1;
@@ -1484,6 +1905,8 @@ static int32_t tc_prepare_bf16(mans_corpus* c, int metric) {
     if (e != cudaSuccess) return fail_cuda(e, "cudaMalloc(bf16 corpus)");
     c->tc_ld16 = ld16;
     int32_t rc = encode_tc_map(&c->tc_map, c->tc_rows, n, c->dim, ld16, kRN, false);
+    if (rc == MANS_OK)
+      rc = encode_tc_map(&c->tc_map_half, c->tc_rows, n, c->dim, ld16, kRN / 2, false);
     if (rc != MANS_OK) return rc;
   }
   if (n > 0) {
@@ -1547,6 +1970,63 @@ static cudaError_t launch_pdl(mans_ctx* ctx, const void* fn, dim3 grid, dim3 blo
   }
   if (coop) return cudaLaunchCooperativeKernel(fn, grid, block, args, smem, stream);
   return cudaLaunchKernel(fn, grid, block, args, smem, stream);
+}
+
+// Clusters of two CTAs (one per SM) of the pair pass, launched with the
+// programmatic-dependent-launch attribute like the other kernels.
+static cudaError_t launch_pair(mans_ctx* ctx, const void* fn, dim3 grid, dim3 block, size_t smem,
+                               cudaStream_t stream, void** args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = ctx->pdl ? 2 : 1;
+  return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+// How many CTA pairs of the pair pass the device runs at once (0: the
+// one-CTA pass runs).  The pair pass is opt-in (MANS_TC_PAIRS=1 when the
+// context first runs a multi-block batch): measured on B200 it is correct but
+// slower than the one-CTA pass (1M x 384, 1024 queries: 672.6 against
+// 640.6 us; 125k rows: 119.6 against 107.2 us).  Asked once per context.
+static int tc_pair_capacity(mans_ctx* ctx, size_t smem) {
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (ctx->tc_pairs < 0) {
+    const char* env = getenv("MANS_TC_PAIRS");
+    int n = 0;
+    if (env && env[0] == '1') {
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = dim3(2 * (ctx->num_sms / 2));
+      cfg.blockDim = dim3(kTcThreads);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = 2;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      const void* fn = reinterpret_cast<const void*>(tc_scan_kernel<kFilterPlain, false, false, true>);
+      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           ctx->max_smem);
+      if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n, fn, &cfg);
+      if (e != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+      }
+    }
+    ctx->tc_pairs = std::min(n, ctx->num_sms / 2);
+  }
+  return ctx->tc_pairs;
 }
 
 static size_t carve(size_t& o, size_t bytes) {
@@ -1654,6 +2134,49 @@ int32_t tc_export_int8(mans_corpus* c, int8_t* codes, float* scales) {
   return e == cudaSuccess ? MANS_OK : fail_cuda(e, "int8 code download");
 }
 
+// Kernel attributes of the tensor-core path, set once per context (they are
+// per device and outlive the call): every pass variant may use the device's
+// whole opt-in shared memory, and the small per-query kernels prefer the
+// whole carve-out as shared memory, so that eight re-rank or six threshold
+// blocks share an SM.
+static int32_t tc_configure(mans_ctx* ctx) {
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (ctx->tc_configured) return MANS_OK;
+  const void* pass[] = {
+      reinterpret_cast<const void*>(tc_scan_kernel<kDense, false>),
+      reinterpret_cast<const void*>(tc_scan_kernel<kDense, true>),
+      reinterpret_cast<const void*>(tc_scan_kernel<kFilterPlain, false>),
+      reinterpret_cast<const void*>(tc_scan_kernel<kFilterPlain, true>),
+      reinterpret_cast<const void*>(tc_scan_kernel<kFilterBias, false>),
+      reinterpret_cast<const void*>(tc_scan_kernel<kFilterBias, true>),
+      reinterpret_cast<const void*>(tc_scan_kernel<kFilterPlain, false, true>),
+      reinterpret_cast<const void*>(tc_scan_kernel<kFilterPlain, true, true>),
+      reinterpret_cast<const void*>(tc_scan_kernel<kFilterBias, false, true>),
+      reinterpret_cast<const void*>(tc_scan_kernel<kFilterBias, true, true>),
+      reinterpret_cast<const void*>(tc_scan_kernel<kFilterPlain, false, false, true>),
+      reinterpret_cast<const void*>(tc_scan_kernel<kFilterBias, false, false, true>)};
+  cudaError_t e = cudaSuccess;
+  for (const void* fn : pass)
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, ctx->max_smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tc_threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kThresholdStageMax);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tc_rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(rerank_smem_bytes(12 * 1024, 2048, 64 * 1024)));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tc_rerank_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tc_threshold_warp_kernel,
+                             cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return fail_cuda(e, "tc configure");
+  ctx->tc_configured = true;
+  return MANS_OK;
+}
+
 int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* ws,
                            const float* d_queries, int64_t nq, int32_t k, int32_t metric,
                            float* d_out_dist, uint32_t* d_out_ids, int32_t* d_out_counts,
@@ -1683,8 +2206,10 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   int64_t sample = std::max<int64_t>(smin, static_cast<int64_t>(keff) * n / 2048);
   if (qblocks > 1) sample = std::max<int64_t>(sample, n / 16);
   sample = std::min<int64_t>(n, (sample + kRN - 1) / kRN * kRN);
+  // candidate list capacity per query, even: the re-rank stages a list by
+  // 16-byte copies of key pairs, so every list must start 16-byte aligned
   const int32_t cap = static_cast<int32_t>(
-      std::min<int64_t>(std::max<int64_t>(i8 ? 32768 : 8192, 64ll * keff), n));
+      (std::min<int64_t>(std::max<int64_t>(i8 ? 32768 : 8192, 64ll * keff), n) + 1) / 2 * 2);
 
   static const int stream_q = [] {
     const char* e = getenv("MANS_TC_STREAM_QUERIES");
@@ -1767,38 +2292,30 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   qp.scale = F(o_sc);
   qp.nq_pad = nq_pad;
   qp.ccount = ccount;
+  cudaEvent_t st_stop = stage_begin(ws, stream, MANS_STAGE_QUERY_PREP);
   if (i8)
-    tc_query_prep_kernel<true><<<static_cast<unsigned>((nq_pad + 7) / 8), 256, 0, stream>>>(qp);
+    tc_query_prep_kernel<true><<<static_cast<unsigned>((nq_pad + kPrepWarps - 1) / kPrepWarps),
+                                   kPrepWarps * 32, 0, stream>>>(qp);
   else
-    tc_query_prep_kernel<false><<<static_cast<unsigned>((nq_pad + 7) / 8), 256, 0, stream>>>(qp);
+    tc_query_prep_kernel<false><<<static_cast<unsigned>((nq_pad + kPrepWarps - 1) / kPrepWarps),
+                                    kPrepWarps * 32, 0, stream>>>(qp);
   if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "tc query prep launch");
+  timing_end(st_stop, stream);
 
   CUtensorMap map_q;
   if ((rc = encode_tc_map(&map_q, qbf, nq_pad, corpus->dim, ld16, kQM, i8)) != MANS_OK) return rc;
   const CUtensorMap& map_r = i8 ? corpus->tc8_map : corpus->tc_map;
   const size_t smem = lay.total;
   if (lay.stages < 2) return fail(MANS_ERR_SEARCH, "dimension too large for the tensor-core pass");
-  // the attribute is per device; set it on every call (cheap, no allocation)
   const void* kd = i8 ? reinterpret_cast<const void*>(tc_scan_kernel<kDense, true>)
                      : reinterpret_cast<const void*>(tc_scan_kernel<kDense, false>);
   const void* kp_ = i8 ? reinterpret_cast<const void*>(tc_scan_kernel<kFilterPlain, true>)
                        : reinterpret_cast<const void*>(tc_scan_kernel<kFilterPlain, false>);
   const void* kb_ = i8 ? reinterpret_cast<const void*>(tc_scan_kernel<kFilterBias, true>)
                        : reinterpret_cast<const void*>(tc_scan_kernel<kFilterBias, false>);
-  e = cudaFuncSetAttribute(kd, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(kp_, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem));
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(kb_, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem));
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(tc_threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kThresholdStageMax);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(tc_rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(rerank_smem_bytes(corpus->dim, 64 * 1024)));
-  if (e != cudaSuccess) return fail_cuda(e, "tc configure");
+  if (smem > static_cast<size_t>(ctx->max_smem))
+    return fail(MANS_ERR_SEARCH, "tensor-core pass needs more shared memory than the device has");
+  if ((rc = tc_configure(ctx)) != MANS_OK) return rc;
   if (corpus->dim * sizeof(float) > 48 * 1024)
     return fail(MANS_ERR_SEARCH, "dimension too large for the tensor-core re-rank");
 
@@ -1831,11 +2348,13 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
     tp.groups = static_cast<int32_t>(std::min<int64_t>(tp.groups, (sample + kRN - 1) / kRN));
     grid_s = static_cast<int>(tp.groups * qblocks);
   }
+  st_stop = stage_begin(ws, stream, MANS_STAGE_SAMPLE);
   {
     void* args[] = {const_cast<CUtensorMap*>(&map_q), const_cast<CUtensorMap*>(&map_r), &tp};
     e = launch_pdl(ctx, kd, dim3(grid_s), dim3(kTcThreads), smem, stream, args, false);
   }
   if (e != cudaSuccess) return fail_cuda(e, "tc sample launch");
+  timing_end(st_stop, stream);
   // 3. thresholds
   // one wave of queries: wide blocks over a staged row (latency); larger
   // batches: narrow blocks reading global memory (occupancy)
@@ -1843,20 +2362,30 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   const int staged =
       one_wave && dld * sizeof(float) <= static_cast<size_t>(kThresholdStageMax) ? 1 : 0;
   const size_t th_smem = staged ? dld * sizeof(float) : 0;
+  st_stop = stage_begin(ws, stream, MANS_STAGE_THRESHOLD);
   {
     float* a_dn = F(o_dn);
-    int64_t a_ld = dld, a_rows = dvals;
+    int64_t a_ld = dld, a_rows = dvals, a_nq = nq;
     int32_t a_k = keff;
     int a_staged = staged, a_metric = metric;
     float *a_ep = F(o_ep), *a_al = F(o_al), *a_ga = F(o_ga), *a_sc = F(o_sc), *a_th = F(o_th),
           *a_cq = F(o_cq);
-    void* args[] = {&a_dn, &a_ld, &a_rows, &a_k, &a_staged, &a_ep, &a_al, &a_ga, &a_sc, &a_metric,
-                    &a_th, &a_cq};
-    e = launch_pdl(ctx, reinterpret_cast<const void*>(tc_threshold_kernel),
-                   dim3(static_cast<unsigned>(nq)), dim3(one_wave ? kThresholdThreads : 256),
-                   th_smem, stream, args, false);
+    if (!one_wave && dld <= kThrWarpMax) {
+      // many queries, short samples: one warp per query
+      void* args[] = {&a_dn, &a_ld, &a_rows, &a_k, &a_nq, &a_ep, &a_al, &a_ga, &a_sc, &a_th, &a_cq};
+      e = launch_pdl(ctx, reinterpret_cast<const void*>(tc_threshold_warp_kernel),
+                     dim3(static_cast<unsigned>((nq + kThrWarps - 1) / kThrWarps)),
+                     dim3(kThrWarps * 32), 0, stream, args, false);
+    } else {
+      void* args[] = {&a_dn, &a_ld, &a_rows, &a_k, &a_staged, &a_ep, &a_al, &a_ga, &a_sc,
+                      &a_metric, &a_th, &a_cq};
+      e = launch_pdl(ctx, reinterpret_cast<const void*>(tc_threshold_kernel),
+                     dim3(static_cast<unsigned>(nq)), dim3(one_wave ? kThresholdThreads : 256),
+                     th_smem, stream, args, false);
+    }
   }
   if (e != cudaSuccess) return fail_cuda(e, "tc threshold launch");
+  timing_end(st_stop, stream);
   }
   // 4. full filtered pass
   tp.rows = n;
@@ -1870,6 +2399,19 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   if (tp.groups > 0) {
     tp.groups = static_cast<int32_t>(std::min<int64_t>(tp.groups, (n + kRN - 1) / kRN));
     grid = static_cast<int>(tp.groups * qblocks);
+  }
+  // CTA pairs (bf16, two or more query blocks, the query block resident):
+  // pairs of query blocks walk row groups in step, `groups` pairs per pair
+  // of query blocks, as many pairs as fit on the device at once.
+  const TcLayout lay2 = tc_layout(lay.nk, stream_q, true);
+  const int64_t qsb = (qblocks + 1) / 2;
+  const int max_pairs = (!i8 && !fused && qblocks >= 2 && lay2.resident && !stream_q)
+                            ? tc_pair_capacity(ctx, lay2.total)
+                            : 0;
+  const bool pair = max_pairs > 0 && qsb <= max_pairs;
+  if (pair) {
+    tp.groups = static_cast<int32_t>(std::min<int64_t>(max_pairs / qsb, (n + kRN - 1) / kRN));
+    grid = static_cast<int>(2 * tp.groups * qsb);
   }
   tp.row0 = 0;
   {
@@ -1894,6 +2436,7 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
     tp.thr_out = F(o_th);
     tp.c_out = F(o_cq);
   }
+  st_stop = stage_begin(ws, stream, MANS_STAGE_PASS);
   cudaEvent_t stop = timing_begin(ws, stream);
   if (fused) {
     // co-resident blocks (one per SM) meet at two grid barriers
@@ -1902,12 +2445,15 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
                             : reinterpret_cast<const void*>(tc_scan_kernel<kFilterBias, false, true>))
                       : (i8 ? reinterpret_cast<const void*>(tc_scan_kernel<kFilterPlain, true, true>)
                             : reinterpret_cast<const void*>(tc_scan_kernel<kFilterPlain, false, true>));
-    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem));
-    if (e != cudaSuccess) return fail_cuda(e, "tc configure");
     void* args[] = {const_cast<CUtensorMap*>(&map_q), const_cast<CUtensorMap*>(&map_r), &tp};
     e = launch_pdl(ctx, fn, dim3(grid), dim3(kTcThreads), smem, stream, args, true);
     if (e == cudaSuccess) ws->tc_bar_base += 2ull * static_cast<unsigned long long>(grid);
+  } else if (pair) {
+    const void* fn = metric == kL2
+                         ? reinterpret_cast<const void*>(tc_scan_kernel<kFilterBias, false, false, true>)
+                         : reinterpret_cast<const void*>(tc_scan_kernel<kFilterPlain, false, false, true>);
+    void* args[] = {const_cast<CUtensorMap*>(&map_q), &corpus->tc_map_half, &tp};
+    e = launch_pair(ctx, fn, dim3(grid), dim3(kTcThreads), lay2.total, stream, args);
   } else {
     void* args[] = {const_cast<CUtensorMap*>(&map_q), const_cast<CUtensorMap*>(&map_r), &tp};
     e = launch_pdl(ctx, metric == kL2 ? kb_ : kp_, dim3(grid), dim3(kTcThreads), smem, stream, args,
@@ -1915,6 +2461,7 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   }
   if (e != cudaSuccess) return fail_cuda(e, "tc scan launch");
   timing_end(stop, stream);
+  timing_end(st_stop, stream);
   // 5. certify + exact re-rank
   RerankParams rp{};
   rp.cand = cand;
@@ -1939,13 +2486,16 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   rp.out_counts = d_out_counts;
   rp.fallbacks = fallbacks;
   rp.region = rerank_region_bytes(nq, ctx->num_sms);
+  rp.max_band = rerank_max_band(nq, ctx->num_sms);
+  st_stop = stage_begin(ws, stream, MANS_STAGE_RERANK);
   {
     void* args[] = {&rp};
     e = launch_pdl(ctx, reinterpret_cast<const void*>(tc_rerank_kernel),
                    dim3(static_cast<unsigned>(nq)), dim3(kRerankThreads),
-                   rerank_smem_bytes(corpus->dim, rp.region), stream, args, false);
+                   rerank_smem_bytes(corpus->dim, rp.max_band, rp.region), stream, args, false);
   }
   if (e != cudaSuccess) return fail_cuda(e, "tc rerank launch");
+  timing_end(st_stop, stream);
   ws->tc_fallbacks = fallbacks;
   ws->launches += fused ? 3 : 5;
   ws->last_path = i8 ? 2 : 1;

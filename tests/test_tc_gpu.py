@@ -110,6 +110,74 @@ def test_tc_duplicates_force_exact_fallback(tctx):
     buf.close()
 
 
+@pytest.fixture(scope="module")
+def pair_ctx():
+    """A context whose multi-block batches run the opt-in pair pass: the
+    MANS_TC_PAIRS switch is read at the context's first multi-block batch,
+    which runs here while it is set."""
+    import os
+    old = os.environ.get("MANS_TC_PAIRS")
+    os.environ["MANS_TC_PAIRS"] = "1"
+    c = mb.Context(0)
+    c.set_tensor_core_batch(1)
+    try:
+        rng = np.random.default_rng(3)
+        v = unit_rows(rng, 5000, 64)
+        q = unit_rows(rng, 256, 64)
+        same(run(c, v, q, 10, mb.Metric.cosine), O.flat_search(v, q, 10, O.COSINE))
+    finally:
+        if old is None:
+            del os.environ["MANS_TC_PAIRS"]
+        else:
+            os.environ["MANS_TC_PAIRS"] = old
+    yield c
+    c.close()
+
+
+@pytest.mark.parametrize("mg,mo", MET)
+@pytest.mark.parametrize("nq,d", [(256, 384), (300, 128), (1000, 384)])
+def test_tc_pair_pass(pair_ctx, mg, mo, nq, d):
+    """Two or more query blocks with resident queries run the filtered pass
+    as CTA pairs (M = 256 MMAs over two CTAs, each streaming half of every
+    row tile); an odd number of query blocks leaves the last pair's second
+    CTA without queries."""
+    rng = np.random.default_rng(nq + d)
+    v = unit_rows(rng, 30001, d)
+    q = unit_rows(rng, nq, d)
+    for k in (10, 100):
+        same(run(pair_ctx, v, q, k, mg), O.flat_search(v, q, k, mo))
+
+
+@pytest.mark.parametrize("mg,mo", MET[:2])
+def test_tc_large_batch_wide_bands(tctx, mg, mo):
+    """More queries than SMs (the one-wave re-rank with a 1024-entry band
+    buffer and the warp-per-query thresholds): 1,500 copies of one query's
+    row make a band wider than the buffer (exact re-scan), 600 copies of
+    another a band sorted in shared memory, duplicates of a third straddle
+    the k-th rank (ties by id)."""
+    import torch
+    rng = np.random.default_rng(17)
+    v = unit_rows(rng, 40000, 64)
+    q = unit_rows(rng, 200, 64)
+    v[2000:3500] = q[0]
+    v[9000:9600] = q[1]
+    v[30000:30007] = q[2]
+    buf = mb.VectorBuffer(tctx, v)
+    ws = mb.Workspace(tctx)
+    dq = torch.from_numpy(q).cuda()
+    od = torch.empty((200, 10), dtype=torch.float32, device="cuda")
+    oi = torch.empty((200, 10), dtype=torch.int32, device="cuda")
+    oc = torch.empty((200,), dtype=torch.int32, device="cuda")
+    mb.FlatGPUSearch.search_device(tctx, buf, ws, dq.data_ptr(), 200, 10, mg,
+                                   od.data_ptr(), oi.data_ptr(), oc.data_ptr())
+    ws.check()
+    assert ws.fallbacks() >= 1
+    want = O.flat_search(v, q, 10, mo)
+    same((od.cpu().numpy(), oi.cpu().numpy().view(np.uint32), oc.cpu().numpy()), want)
+    ws.close()
+    buf.close()
+
+
 def test_tc_zero_rows_take_the_exact_scan(tctx):
     rng = np.random.default_rng(5)
     v = unit_rows(rng, 3000, 48)
