@@ -68,6 +68,10 @@ def parse():
     ap.add_argument("--pq-shard", default="list", choices=["list", "row"],
                     help="IVF-PQ over N > 1 GPUs: whole inverted lists per rank (each rank "
                          "builds tables only for the probed lists it holds) or row ranges")
+    ap.add_argument("--ivf-layout", default="replica", choices=["replica", "shard"],
+                    help="IVF-flat at N > 1: a full replica of the index per GPU, each GPU "
+                         "serving its own queries (default; the 1M-row index fits one GPU), "
+                         "or row shards with a merge of every query's per-shard blocks")
     ap.add_argument("--transport", default="p2p", choices=["p2p", "nccl"],
                     help="how row shards exchange their top-k blocks (N > 1)")
     a = ap.parse_args()
@@ -779,7 +783,9 @@ def index_workload_config(args, nq=None, nprobe=None):
            "metric": args.metric, "nlist": args.nlist, "nprobe": nprobe,
            "components": args.components,
            "parallelism": (f"listshard{args.gpus}" if args.workload == "ivfpq" and args.gpus > 1
-                           and args.pq_shard == "list" else f"rowshard{args.gpus}"),
+                           and args.pq_shard == "list" else
+                           f"replica{args.gpus}" if index_replicas(args, args.gpus) else
+                           f"rowshard{args.gpus}"),
            "l2": "probed lists differ per query; each step streams its lists once "
                  "(no flush; lists of one batch may hit L2)"}
     if args.workload == "ivfpq":
@@ -966,8 +972,11 @@ def measure_index(torch, ws, search_dev, search_host, q, kout, steps, warmup, wi
     Row shards (``search_host`` None): ``search_dev`` returns the merged
     packed block and the end-to-end step copies the queries in and the block
     out around it; ``barrier`` lines the ranks up around the timed loops."""
-    nq = q.shape[0]
-    dq = torch.from_numpy(q).cuda()
+    if q.ndim == 2:
+        q = q[None]
+    pool, nq = q.shape[0], q.shape[1]
+    dq_pool = torch.from_numpy(np.ascontiguousarray(q)).cuda()
+    dq = dq_pool[0]
     sync = barrier or torch.cuda.synchronize
     od = torch.empty((nq, kout), dtype=torch.float32, device="cuda")
     oi = torch.empty((nq, kout), dtype=torch.int32, device="cuda")
@@ -996,7 +1005,7 @@ def measure_index(torch, ws, search_dev, search_host, q, kout, steps, warmup, wi
     t0.record(stream)
     for i in range(steps):
         ev[i][0].record(stream)
-        last = step()
+        last = step(dq_pool[i % pool])
         ev[i][1].record(stream)
     t1.record(stream)
     torch.cuda.synchronize()
@@ -1007,7 +1016,9 @@ def measure_index(torch, ws, search_dev, search_host, q, kout, steps, warmup, wi
     ws.set_timing(False)
     total_ms = t0.elapsed_time(t1)
     step_ms = [x.elapsed_time(y) for x, y in ev]
-    hq = torch.from_numpy(q).pin_memory()
+    # the device outputs above are those of batch (steps - 1) % pool, which
+    # the last end-to-end step searches too
+    hq_pool = torch.from_numpy(np.ascontiguousarray(q)).pin_memory()
     hd = torch.empty((nq, kout), dtype=torch.float32).pin_memory()
     hi = torch.empty((nq, kout), dtype=torch.int32).pin_memory()
     hc = torch.empty((nq,), dtype=torch.int32).pin_memory()
@@ -1018,8 +1029,8 @@ def measure_index(torch, ws, search_dev, search_host, q, kout, steps, warmup, wi
         dq2 = torch.empty_like(dq)
         hblk = torch.empty_like(last, device="cpu").pin_memory()
 
-        def e2e():
-            dq2.copy_(hq, non_blocking=True)
+        def e2e(j):
+            dq2.copy_(hq_pool[j % pool], non_blocking=True)
             r = step(dq2)
             hblk.copy_(r, non_blocking=True)
             stream.synchronize()
@@ -1030,20 +1041,22 @@ def measure_index(torch, ws, search_dev, search_host, q, kout, steps, warmup, wi
     else:
         dev_out = (od.cpu().numpy(), oi.cpu().numpy(), oc.cpu().numpy())
 
-        def e2e():
-            search_host(hq.data_ptr(), nq, hd.data_ptr(), hi.data_ptr(), hc.data_ptr())
+        def e2e(j):
+            search_host(hq_pool[j % pool].data_ptr(), nq, hd.data_ptr(), hi.data_ptr(),
+                        hc.data_ptr())
 
-    for _ in range(max(3, warmup)):
-        e2e()
+    for j in range(max(3, warmup)):
+        e2e(j)
     sync()
     e2e_times = []
-    for _ in range(steps):
+    for j in range(steps):
         t = time.perf_counter()
-        e2e()
+        e2e(j)
         e2e_times.append(time.perf_counter() - t)
     ok = bool(np.array_equal(dev_out[2], hc.numpy()) and np.array_equal(dev_out[1], hi.numpy())
               and np.array_equal(dev_out[0], hd.numpy()))
-    return {"nq": nq, "steps": steps, "total_ms": total_ms, "e2e_ms": 1e3 * sum(e2e_times),
+    return {"nq": nq, "steps": steps, "pool": pool, "total_ms": total_ms,
+            "e2e_ms": 1e3 * sum(e2e_times),
             "kern_avg_ms": kern_ms / max(kern_launches, 1), "kern_launches": kern_launches,
             "launches": total_launches, "p50_ms": p50(step_ms), "e2e_p50_s": p50(e2e_times),
             "clocks": clock_info, "ok": ok, "kout": kout}
@@ -1108,15 +1121,21 @@ def index_session(args, torch, mb, lib, world, rank, dist, cases):
     (results, build seconds, host data for the CPU baselines); the device
     objects are released before returning."""
     metric = METRIC_NAMES[args.metric]
-    nq_max = max(c[0] for c in cases)
     t_build = time.perf_counter()
     ctx = mb.Context(torch.cuda.current_device())
-    # N > 1: both index kinds shard their rows over the ranks (shared
-    # centroids / codebooks, global ids or list positions, per-rank blocks
-    # gathered and merged into the unsharded result)
-    ivf_sharded = world > 1
+    # N > 1: IVF-PQ shards its rows or lists over the ranks (shared centroids
+    # and codebooks, list positions, per-rank blocks gathered and resolved into
+    # the unsharded result); IVF-flat does the same with --ivf-layout shard,
+    # and by default keeps a full replica per rank, each rank searching its
+    # own queries.
+    replicas = index_replicas(args, world)
+    ivf_sharded = world > 1 and not replicas
+    # each case cycles through a pool of distinct query batches (per rank for
+    # replicas); queries are drawn after the database, so their number leaves
+    # the database unchanged
+    q_need = max(c[0] * query_pool(c[0]) * (world if replicas else 1) for c in cases)
     shard = mb.row_shard(args.n, world, rank) if ivf_sharded else None
-    v, q_all, art = build_index_data(args, nq_max, mb=mb, ctx=ctx, shard=shard,
+    v, q_all, art = build_index_data(args, q_need, mb=mb, ctx=ctx, shard=shard,
                                      dist=dist if ivf_sharded else None)
     ws = mb.Workspace(ctx)
     L = lib
@@ -1193,18 +1212,24 @@ def index_session(args, torch, mb, lib, world, rank, dist, cases):
         saved = args.nprobe
         args.nprobe = nprobe
         try:
-            q = q_all[:nq]
+            pool = query_pool(nq)
+            off = rank * nq * pool if replicas else 0
+            q = q_all[off:off + nq * pool].reshape(pool, nq, args.dim)
             r = measure_index(torch, ws, dev_fn(nprobe), host_fn(nprobe), q, kout, steps, warmup,
-                              with_clocks, barrier=barrier)
+                              with_clocks, barrier=barrier if not replicas else
+                              (lambda: (dist.barrier(), torch.cuda.synchronize())))
             if world > 1:
                 t = torch.tensor([r["total_ms"], r["e2e_ms"]], dtype=torch.float64,
                                  device="cuda")
                 dist.all_reduce(t, op=dist.ReduceOp.MAX)
                 r["total_ms"], r["e2e_ms"] = t.tolist()
             r["nprobe"] = nprobe
-            r["roofline"] = index_roofline(
-                args, r, probed_list_rows(args, art, q),
-                probed_list_rows(args, art, q, distinct=True) if args.workload == "ivf" else None)
+            # bytes per launch: the mean over the pool's batches
+            rows = np.float64(np.mean([np.sum(probed_list_rows(args, art, qb)) for qb in q]))
+            drows = (np.float64(np.mean([np.sum(probed_list_rows(args, art, qb, distinct=True))
+                                         for qb in q]))
+                     if args.workload == "ivf" else None)
+            r["roofline"] = index_roofline(args, r, rows, drows)
             r["workload"] = index_workload_config(args, nq, nprobe)["workload"]
             r["config"] = index_workload_config(args, nq, nprobe)
             results.append(r)
@@ -1226,6 +1251,17 @@ def index_session(args, torch, mb, lib, world, rank, dist, cases):
     return results, build_s, host
 
 
+def index_replicas(args, world):
+    """IVF-flat at N > 1 runs as replicas unless --ivf-layout shard."""
+    return world > 1 and args.workload == "ivf" and args.ivf_layout == "replica"
+
+
+def query_pool(nq):
+    """Distinct query batches a timed case cycles through: 64 single queries,
+    4 batches up to 256 queries, 2 larger batches."""
+    return 64 if nq == 1 else (4 if nq <= 256 else 2)
+
+
 def index_entry(args, r, world, ivf_sharded):
     """One measured case as a JSON object (the main line's keys)."""
     return {"workload": r["workload"], "nq": r["nq"], "nprobe": r["nprobe"],
@@ -1233,11 +1269,14 @@ def index_entry(args, r, world, ivf_sharded):
             "value": (1 if ivf_sharded else world) * r["nq"] * r["steps"] / (r["total_ms"] * 1e-3),
             "unit": "queries/s", "ms_per_step": r["total_ms"] / r["steps"],
             "p50_us": 1e3 * r["p50_ms"],
-            "e2e": {"value": r["nq"] * r["steps"] / (r["e2e_ms"] * 1e-3), "unit": "queries/s",
+            "e2e": {"value": (1 if ivf_sharded else world) * r["nq"] * r["steps"] /
+                             (r["e2e_ms"] * 1e-3), "unit": "queries/s",
                     "p50_us": 1e6 * r["e2e_p50_s"],
                     "h2d_bytes_per_step": r["nq"] * args.dim * 4,
                     "d2h_bytes_per_step": r["nq"] * r["kout"] * 8 + r["nq"] * 4},
             "gpu_launches": int(r["launches"]), "roofline": r["roofline"],
+            "scaling": "strong" if ivf_sharded or world == 1 else "weak",
+            "distinct_batches_timed": r["pool"],
             "config": r["config"], "e2e_matches_device_path": r["ok"],
             "dtype": "f32" if args.workload == "ivf" else "f32 (u8 codes)"}
 
@@ -1291,7 +1330,7 @@ def index_cases(args):
 
 
 def run_index(args, torch, mb, lib, world, rank, dist):
-    ivf_sharded = world > 1
+    ivf_sharded = world > 1 and not index_replicas(args, world)
     results, build_s, host = index_session(args, torch, mb, lib, world, rank, dist,
                                            index_cases(args))
     if rank == 0:
@@ -1301,13 +1340,16 @@ def run_index(args, torch, mb, lib, world, rank, dist):
             "value": (1 if ivf_sharded else world) * args.nq * args.steps / (res["total_ms"] * 1e-3),
             "unit": "queries/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": res["total_ms"] / args.steps, "p50_us": 1e3 * res["p50_ms"],
-            "higher_is_better": True, "scaling": "strong" if ivf_sharded else "weak",
+            "higher_is_better": True,
+            "scaling": "strong" if ivf_sharded or world == 1 else "weak",
             "vs_baseline": None,
+            "distinct_batches_timed": res["pool"],
             "dtype": "f32" if args.workload == "ivf" else "f32 (u8 codes)",
             "data": index_data_note(args, build_s),
             "config": index_workload_config(args),
             "roofline": res["roofline"],
-            "e2e": {"value": args.nq * args.steps / (res["e2e_ms"] * 1e-3), "unit": "queries/s",
+            "e2e": {"value": (1 if ivf_sharded else world) * args.nq * args.steps /
+                             (res["e2e_ms"] * 1e-3), "unit": "queries/s",
                     "p50_us": 1e6 * res["e2e_p50_s"],
                     "h2d_bytes_per_step": args.nq * args.dim * 4,
                     "d2h_bytes_per_step": args.nq * res["kout"] * 8 + args.nq * 4},
@@ -1458,7 +1500,7 @@ def main():
             line["also"].append(entry)
         for ia, results, build_s, host in index_results:
             for i, r in enumerate(results):
-                e = index_entry(ia, r, world, world > 1)
+                e = index_entry(ia, r, world, world > 1 and not index_replicas(ia, world))
                 e["data"] = index_data_note(ia, build_s)
                 if i == 0:
                     e["build"] = {"device_s": host["build_gpu_s"], "what": host["build_gpu"],

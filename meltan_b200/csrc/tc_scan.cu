@@ -1676,13 +1676,17 @@ __device__ __forceinline__ float exact_distance(const RerankParams& p, const flo
 // region that first holds the candidate keys and later the staged corpus rows
 // of the exact re-score.
 // The region is large (64 KB) and the band buffer 2048 entries while the
-// queries fit on the SMs in one wave; for large batches both shrink (16 KB,
-// 1024 entries) so that eight blocks share an SM and the batch runs in one
-// wave too.  A band wider than the buffer takes the exact re-scan.
-inline int rerank_region_bytes(int64_t nq, int num_sms) {
-  return nq <= num_sms ? 64 * 1024 : 16 * 1024;
+// queries fit on the SMs in one wave.  For larger batches the region holds
+// 16 staged rows (at least 16 KB, at most 32 KB) and the band buffer 512
+// entries: the usual band (k plus a few rows) is re-scored in one round, and
+// at d = 384 seven blocks share an SM, so 1,024 queries still run in one
+// wave.  A band wider than the buffer takes the exact re-scan.
+inline int rerank_region_bytes(int64_t nq, int num_sms, int64_t dim) {
+  if (nq <= num_sms) return 64 * 1024;
+  const int64_t r16 = 16 * ((dim + 3) / 4 * 4 + 4) * 4;
+  return static_cast<int>(std::max<int64_t>(16 * 1024, std::min<int64_t>(r16, 32 * 1024)));
 }
-inline int rerank_max_band(int64_t nq, int num_sms) { return nq <= num_sms ? 2048 : 1024; }
+inline int rerank_max_band(int64_t nq, int num_sms) { return nq <= num_sms ? 2048 : 512; }
 inline size_t rerank_smem_bytes(int64_t dim, int max_band, int region) {
   return static_cast<size_t>((dim + 3) / 4 * 4) * sizeof(float) +
          static_cast<size_t>(max_band) * sizeof(uint64_t) + region;
@@ -2137,7 +2141,7 @@ int32_t tc_export_int8(mans_corpus* c, int8_t* codes, float* scales) {
 // Kernel attributes of the tensor-core path, set once per context (they are
 // per device and outlive the call): every pass variant may use the device's
 // whole opt-in shared memory, and the small per-query kernels prefer the
-// whole carve-out as shared memory, so that eight re-rank or six threshold
+// whole carve-out as shared memory, so that seven re-rank or six threshold
 // blocks share an SM.
 static int32_t tc_configure(mans_ctx* ctx) {
   std::lock_guard<std::mutex> lk(ctx->mu);
@@ -2485,7 +2489,7 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   rp.out_ids = d_out_ids;
   rp.out_counts = d_out_counts;
   rp.fallbacks = fallbacks;
-  rp.region = rerank_region_bytes(nq, ctx->num_sms);
+  rp.region = rerank_region_bytes(nq, ctx->num_sms, corpus->dim);
   rp.max_band = rerank_max_band(nq, ctx->num_sms);
   st_stop = stage_begin(ws, stream, MANS_STAGE_RERANK);
   {

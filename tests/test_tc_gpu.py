@@ -150,9 +150,9 @@ def test_tc_pair_pass(pair_ctx, mg, mo, nq, d):
 
 @pytest.mark.parametrize("mg,mo", MET[:2])
 def test_tc_large_batch_wide_bands(tctx, mg, mo):
-    """More queries than SMs (the one-wave re-rank with a 1024-entry band
+    """More queries than SMs (the one-wave re-rank with a 512-entry band
     buffer and the warp-per-query thresholds): 1,500 copies of one query's
-    row make a band wider than the buffer (exact re-scan), 600 copies of
+    row make a band wider than the buffer (exact re-scan), 300 copies of
     another a band sorted in shared memory, duplicates of a third straddle
     the k-th rank (ties by id)."""
     import torch
@@ -160,7 +160,7 @@ def test_tc_large_batch_wide_bands(tctx, mg, mo):
     v = unit_rows(rng, 40000, 64)
     q = unit_rows(rng, 200, 64)
     v[2000:3500] = q[0]
-    v[9000:9600] = q[1]
+    v[9000:9300] = q[1]
     v[30000:30007] = q[2]
     buf = mb.VectorBuffer(tctx, v)
     ws = mb.Workspace(tctx)
