@@ -96,22 +96,30 @@ __host__ __device__ inline int tc_kblocks(int dim, bool i8) {
 
 // With `pair` (a CTA pair sharing M = 256 MMAs) a stage holds this CTA's
 // half of the row tile, 128 rows, so the same budget keeps twice the stages.
-__host__ __device__ inline TcLayout tc_layout(int nk, int stream_queries, bool pair = false) {
+// `lean` (the bf16 filtered pass without per-row terms or fused sampling:
+// cosine and inner product) has neither the row-term ring nor the k-th
+// selection scratch, and gives the freed shared memory to the stage ring:
+// every stage that fits in kLeanBudget (one more 32 KiB stage at d = 384).
+constexpr size_t kLeanBudget = 227 * 1024;
+__host__ __device__ inline TcLayout tc_layout(int nk, int stream_queries, bool pair = false,
+                                              bool lean = false) {
   TcLayout L;
   L.nk = nk;
   L.resident = !stream_queries && static_cast<size_t>(L.nk) * kQBytes <= kResidentMax;
   L.a_bytes = L.resident ? static_cast<size_t>(L.nk) * kQBytes : 0;
   L.stage_bytes = (pair ? kRBytes / 2 : kRBytes) + (L.resident ? 0 : kQBytes);
-  size_t st = (kPipeBudget - L.a_bytes) / L.stage_bytes;
+  // barriers: full/empty per stage, acc_full/acc_empty x2, a_full, a_empty,
+  // drain, rt_full/rt_empty per row-term slot (at most 8 stages)
+  const size_t bars_max = 8 * (2 * 8 + 7 + 2 * kRtSlots);
+  const size_t budget = lean ? kLeanBudget - 1024 - bars_max - 16 : kPipeBudget;
+  size_t st = budget > L.a_bytes ? (budget - L.a_bytes) / L.stage_bytes : 0;
   L.stages = static_cast<int>(st > 8 ? 8 : st);
   L.rt_off = L.a_bytes + static_cast<size_t>(L.stages) * L.stage_bytes;  // 1 KiB aligned
-  L.bar_off = L.rt_off + static_cast<size_t>(kRtSlots) * 2 * kRN * sizeof(float);
-  // barriers: full/empty per stage, acc_full/acc_empty x2, a_full, a_empty,
-  // drain, rt_full/rt_empty per row-term slot
+  L.bar_off = L.rt_off + (lean ? 0 : static_cast<size_t>(kRtSlots) * 2 * kRN * sizeof(float));
   const size_t bars = 8 * (2 * static_cast<size_t>(L.stages) + 7 + 2 * kRtSlots);
   // + tmem slot / abort (16 B) + the k-th selection scratch of the fused sampling
   L.kth_off = L.bar_off + bars + 16;
-  L.total = 1024 + L.kth_off + sizeof(KthSmem);
+  L.total = 1024 + L.kth_off + (lean ? 0 : sizeof(KthSmem));
   return L;
 }
 
@@ -747,8 +755,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_scan_kernel(const __grid_constant__ CUtensorMap map_q,
                    const __grid_constant__ CUtensorMap map_r, const TcParams p) {
   static_assert(!PAIR || (!I8 && !FUSED && MODE != kDense), "pairs run the bf16 filtered pass");
+  // no per-row terms and no fused sampling: the lean layout (more stages)
+  constexpr bool kLean = MODE == kFilterPlain && !I8 && !FUSED && !PAIR;
   extern __shared__ uint8_t smem_raw[];
-  const TcLayout L = tc_layout(tc_kblocks(p.dim, I8), p.stream_queries, PAIR);
+  const TcLayout L = tc_layout(tc_kblocks(p.dim, I8), p.stream_queries, PAIR, kLean);
   uint8_t* base =
       reinterpret_cast<uint8_t*>((reinterpret_cast<size_t>(smem_raw) + 1023) / 1024 * 1024);
   uint8_t* qres = base;                  // resident query block (nk x 16 KiB)
@@ -2459,9 +2469,12 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
     void* args[] = {const_cast<CUtensorMap*>(&map_q), &corpus->tc_map_half, &tp};
     e = launch_pair(ctx, fn, dim3(grid), dim3(kTcThreads), lay2.total, stream, args);
   } else {
+    // the bf16 plain filter (cosine, inner product) runs the lean layout
+    const size_t smem_pass =
+        (metric != kL2 && !i8) ? tc_layout(lay.nk, stream_q, false, true).total : smem;
     void* args[] = {const_cast<CUtensorMap*>(&map_q), const_cast<CUtensorMap*>(&map_r), &tp};
-    e = launch_pdl(ctx, metric == kL2 ? kb_ : kp_, dim3(grid), dim3(kTcThreads), smem, stream, args,
-                   false);
+    e = launch_pdl(ctx, metric == kL2 ? kb_ : kp_, dim3(grid), dim3(kTcThreads), smem_pass, stream,
+                   args, false);
   }
   if (e != cudaSuccess) return fail_cuda(e, "tc scan launch");
   timing_end(stop, stream);
