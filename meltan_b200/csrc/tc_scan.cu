@@ -1093,11 +1093,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // after the sample tiles: thresholds of this block's share of its query
     // block's queries (query qb*128 + l for l = grp, grp + groups, ...), then
     // every block reads its queries' constants
+    // A single query: every block derives its threshold from the sample
+    // itself (the same inputs and steps in every block, so the same value,
+    // which every block also stores for the re-rank), and the second barrier
+    // is only arrived at, keeping the counter's per-call advance.
     auto fused_sync = [&](int64_t qb) -> bool {
       if (!grid_barrier(1)) return false;
-      fused_thresholds(p.samp_out, p.samp_ld, p.k, p.nq, p.groups > 0 ? p.groups : 1, p.q_eps,
-                       p.q_alpha, p.q_gamma, p.q_scale, p.thr_out, p.c_out, ks, et, qb, grp);
-      if (!grid_barrier(2)) return false;
+      if (p.nq == 1) {
+        fused_thresholds(p.samp_out, p.samp_ld, p.k, p.nq, 1, p.q_eps, p.q_alpha, p.q_gamma,
+                         p.q_scale, p.thr_out, p.c_out, ks, et, qb, 0);
+        named_sync(1, kEpiWarps * 32);  // thread 0's stores of thr / c are seen by the block
+        if (et == 0) atomicAdd(p.bar, 1ull);
+      } else {
+        fused_thresholds(p.samp_out, p.samp_ld, p.k, p.nq, p.groups > 0 ? p.groups : 1, p.q_eps,
+                         p.q_alpha, p.q_gamma, p.q_scale, p.thr_out, p.c_out, ks, et, qb, grp);
+        if (!grid_barrier(2)) return false;
+      }
       cq = qvalid ? __ldcg(p.c_out + q) : __int_as_float(0x7F800000);
       return true;
     };
