@@ -45,6 +45,15 @@ struct TcParams {
   const float* q_scale;
   float* thr_out;               // per query: sample k-th + 2 eps
   float* c_out;                 // per query: score-domain constant (also read as q_c)
+  // Dynamic tail of a fused pass (pool != null): block c streams the static
+  // tiles [c * static_tiles, (c + 1) * static_tiles), then claims tiles
+  // pool_first + t, t = atomicAdd(pool, 1), while t < pool_tiles, so blocks
+  // whose stream runs faster take more of the tail.  *pool is zeroed by the
+  // query prep of the same search.
+  unsigned long long* pool;
+  int64_t static_tiles;
+  int64_t pool_first;
+  int64_t pool_tiles;
 };
 
 // Corpus-wide terms of the error bound (maxima over rows, rounded up).

@@ -72,6 +72,10 @@ struct KthSmem {
   float lo[4], scale[4];
   int sel[4];
   uint32_t sh[4];
+  // dynamic tail of the fused pass: the producer's claimed tiles (-1: none
+  // left), each published to the MMA issuer and the epilogue by ufull[slot]
+  uint64_t ufull[16];
+  int64_t uq[16];
 };
 
 // Shared-memory plan of tc_scan_kernel for a given width: the query block is
@@ -805,6 +809,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int64_t g = pr / qsb;
     u_begin = qb * rtiles + rtiles * g / p.groups;
     u_end = qb * rtiles + rtiles * (g + 1) / p.groups;
+  } else if (FUSED && p.pool) {
+    u_begin = blockIdx.x * p.static_tiles;
+    u_end = u_begin + p.static_tiles;
   } else if (p.groups > 0) {
     const int64_t qb = blockIdx.x % p.qblocks;
     const int64_t g = blockIdx.x / p.qblocks;
@@ -821,6 +828,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       FUSED ? (nown < p.sample_tiles ? nown : static_cast<int64_t>(p.sample_tiles)) : 0;
   const int64_t nvirt = s_c + nown;
   auto unit_of = [&](int64_t v) { return u_begin + (v < s_c ? v : v - s_c); };
+  // Dynamic tail: virtual units from nvirt on come from the pool, in the
+  // order this block's producer claimed them (slot (v - nvirt) % 16 of the
+  // ring, phase ((v - nvirt) / 16) & 1).  The producer runs at most a few
+  // units ahead of the epilogue (two accumulators and a ring of less than two
+  // tiles), so a slot is read by both consumers before it is written again.
+  const bool dyn = FUSED && p.pool != nullptr;
+  KthSmem* kss = reinterpret_cast<KthSmem*>(base + L.kth_off);
 
 
   if (tid == 0) {
@@ -828,6 +842,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
+    if (dyn)
+      for (int s = 0; s < 16; ++s) mbar_init(&kss->ufull[s], 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       // pairs: both CTAs' epilogue warps release the leader's accumulator
@@ -877,8 +893,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int64_t issued = 0;
       int64_t rt_issued = 0;
       bool a_pending = false;
-      for (int64_t v = 0; v < nvirt && !*abort; ++v) {
-        const int64_t u = unit_of(v);
+      // the claim of the next pool tile is issued one unit ahead, so its
+      // round trip overlaps the current unit's copies
+      unsigned long long claim = dyn ? atomicAdd(p.pool, 1ull) : 0ull;
+      for (int64_t v = 0; (v < nvirt || dyn) && !*abort; ++v) {
+        int64_t u;
+        if (v < nvirt) {
+          u = unit_of(v);
+        } else {
+          const int64_t t = static_cast<int64_t>(claim);
+          u = t < p.pool_tiles ? p.pool_first + t : -1;
+          const int slot = static_cast<int>((v - nvirt) % 16);
+          kss->uq[slot] = u;
+          mbar_arrive(&kss->ufull[slot]);
+          if (u < 0) break;
+          claim = atomicAdd(p.pool, 1ull);
+        }
         const int64_t qb = u / rtiles;
         const int64_t rt = u - qb * rtiles;
         if (L.resident && qb != cur_qb) {
@@ -972,8 +1002,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int64_t cur_qb = -1;
       uint32_t a_round = 0;
       int local = 0;
-      for (int64_t v = 0; v < nvirt && !*abort; ++v, ++local) {
-        const int64_t u = unit_of(v);
+      for (int64_t v = 0; (v < nvirt || dyn) && !*abort; ++v, ++local) {
+        int64_t u;
+        if (v < nvirt) {
+          u = unit_of(v);
+        } else {
+          const int slot = static_cast<int>((v - nvirt) % 16);
+          if (!tc_wait(&kss->ufull[slot], static_cast<uint32_t>(((v - nvirt) / 16) & 1), p.err,
+                       abort))
+            break;
+          u = kss->uq[slot];
+          if (u < 0) break;
+        }
         const int64_t qb = u / rtiles;
         if (L.resident && qb != cur_qb) {
           // old query block free once prior MMAs finish (pairs keep theirs)
@@ -1112,8 +1152,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       cq = qvalid ? __ldcg(p.c_out + q) : __int_as_float(0x7F800000);
       return true;
     };
-    for (int64_t vu = 0; vu < nvirt; ++vu, ++local) {
-      const int64_t u = unit_of(vu);
+    for (int64_t vu = 0; vu < nvirt || dyn; ++vu, ++local) {
+      int64_t u;
+      if (vu < nvirt) {
+        u = unit_of(vu);
+      } else {
+        const int slot = static_cast<int>((vu - nvirt) % 16);
+        if (!mbar_wait_bounded(&kss->ufull[slot], static_cast<uint32_t>(((vu - nvirt) / 16) & 1),
+                               p.err)) {
+          *abort = 1;
+          break;
+        }
+        u = kss->uq[slot];
+        if (u < 0) break;
+      }
       const int64_t qb = u / rtiles;
       const int64_t rt = u - qb * rtiles;
       if (qb != cur_qb) {
@@ -1440,6 +1492,7 @@ struct TcQueryParams {
   float* scale;  // magnitude bound of the score-domain value x
   int64_t nq_pad;      // query rows of the bf16 block (multiple of 128); rows >= nq are zeroed
   int32_t* ccount;     // candidate counters (nq + 1, the last one counts fallbacks), zeroed
+  unsigned long long* pool;  // tile counter of the fused pass's dynamic tail (or null), zeroed
 };
 
 // One warp per query: the bf16 copy (or the int8 codes with their scale
@@ -1466,7 +1519,10 @@ __global__ void __launch_bounds__(kPrepWarps * 32) tc_query_prep_kernel(const Tc
   }
   if (lane == 0) {
     p.ccount[q] = 0;
-    if (q == 0) p.ccount[p.nq] = 0;
+    if (q == 0) {
+      p.ccount[p.nq] = 0;
+      if (p.pool) *p.pool = 0;
+    }
   }
   const float* v = p.queries + q * p.dim;
   double qs = 1.0;  // query scale (int8)
@@ -2280,6 +2336,7 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   const size_t o_dn = carve(o, nq * (fused ? samp_ld : dld) * sizeof(float));
   const size_t o_cc = carve(o, nq * sizeof(int32_t) + sizeof(int32_t));
   const size_t o_cd = carve(o, nq * static_cast<size_t>(cap) * sizeof(uint64_t));
+  const size_t o_pl = carve(o, sizeof(unsigned long long));
   if ((rc = ws->tc_aux.reserve(o)) != MANS_OK) return rc;
   if (fused && !ws->tc_bar.ptr) {
     if ((rc = ws->tc_bar.reserve(sizeof(unsigned long long))) != MANS_OK) return rc;
@@ -2317,6 +2374,17 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
   qp.scale = F(o_sc);
   qp.nq_pad = nq_pad;
   qp.ccount = ccount;
+  // Fused pass: each block streams a static share of about 85 % of the
+  // tiles (its sample tiles first), and the tail is claimed tile by tile, so
+  // that blocks whose stream runs faster take more of it: the blocks' rates
+  // differ by several percent, which a static split leaves as idle SMs at
+  // the end of the pass.
+  int64_t static_tiles = 0;
+  if (fused) {
+    static_tiles = std::max<int64_t>(samp_tiles, rtiles_all * 17 / (20 * groups_full));
+    if (static_tiles * groups_full > rtiles_all) static_tiles = 0;
+  }
+  qp.pool = static_tiles > 0 ? reinterpret_cast<unsigned long long*>(A + o_pl) : nullptr;
   cudaEvent_t st_stop = stage_begin(ws, stream, MANS_STAGE_QUERY_PREP);
   if (i8)
     tc_query_prep_kernel<true><<<static_cast<unsigned>((nq_pad + kPrepWarps - 1) / kPrepWarps),
@@ -2455,6 +2523,10 @@ int32_t run_flat_search_tc(mans_ctx* ctx, mans_corpus* corpus, mans_workspace* w
     tp.samp_ld = samp_ld;
     tp.bar = static_cast<unsigned long long*>(ws->tc_bar.ptr);
     tp.bar_base = ws->tc_bar_base;
+    tp.pool = qp.pool;
+    tp.static_tiles = static_tiles;
+    tp.pool_first = static_tiles * grid;
+    tp.pool_tiles = rtiles_all - static_tiles * grid;
     tp.k = keff;
     tp.q_eps = F(o_ep);
     tp.q_scale = F(o_sc);
